@@ -1,0 +1,464 @@
+"""Benchmark of the GDN hot path on B200 (one JSON line on rank 0).
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference] [--workload prefill|long]
+
+Workload "prefill" (default) is BASELINE config 1 per GPU: chunked prefill,
+B=4, T=4096, H=16, dk=dv=128, bf16 q/k/v (L2-normalised q/k), fp32 gates,
+N(0, 0.02) initial state; with N GPUs every rank runs its own config-1 batch
+(batch sharding, no collective: weak scaling).  The line also carries the
+decode half of the metric (config 2: B=256, H=32, 128x128 state updated in
+place, 64 consecutive steps) under "decode".
+
+Workload "long" is config 4 (B=8, T=32768, H=32): heads split evenly over
+the N ranks, each rank runs the prefill kernel on its heads, then an NCCL
+all-gather assembles o (strong scaling).
+
+``--impl reference`` times the reference's CPU path (the numpy restatement in
+oracle/, all host threads) on bounded samples of the same workload.
+
+Timing: W untimed warm-up steps, then exactly K steps between CUDA events on
+the launching stream, bracketed by barrier + synchronize, max over ranks.
+Inputs exceed the 126 MB L2 (config 1 moves ~279 MB per step), so no flush.
+SM clocks and throttle reasons are sampled through NVML during the timed region.
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import math
+import os
+import statistics
+import sys
+import threading
+import time
+
+REPO = os.path.dirname(os.path.abspath(__file__))
+sys.path.insert(0, REPO)
+
+C1 = dict(B=4, T=4096, H=16, dk=128, dv=128)
+C2 = dict(B=256, H=32, dk=128, dv=128, steps=64)
+C4 = dict(B=8, T=32768, H=32, dk=128, dv=128)
+FLOP_PER_TOKEN_HEAD = lambda dk, dv, C=64: 4 * C * (dk + dv) + 6 * dk * dv   # 163,840 at 128/128
+
+
+def measured_peaks():
+    path = os.path.join(REPO, "MEASURED_PEAKS.json")
+    if os.path.exists(path):
+        with open(path) as f:
+            p = json.load(f)
+        return float(p["hbm_gbs"]), float(p["bf16_tflops"]), "measured"
+    return 6650.0, 1590.0, "fallback"
+
+
+def prefill_alg_bytes(B, T, H, dk, dv, gate_bytes=4):
+    """Algorithmic HBM bytes of one prefill: q,k,v in + o out (bf16), a,b gates,
+    fp32 state in + out."""
+    th = B * T * H
+    return th * (2 * dk * 2 + dv * 2 + dv * 2) + th * 2 * gate_bytes + 2 * B * H * dk * dv * 4
+
+
+def decode_state_bytes(B, H, dk, dv):
+    return 2 * B * H * dk * dv * 4
+
+
+# ---------------------------------------------------------------------------
+# clocks (NVML, sampled in a thread during the timed region)
+# ---------------------------------------------------------------------------
+class ClockSampler:
+    REASONS = {
+        0x0000000000000001: "gpu_idle", 0x0000000000000002: "applications_clocks_setting",
+        0x0000000000000004: "sw_power_cap", 0x0000000000000008: "hw_slowdown",
+        0x0000000000000010: "sync_boost", 0x0000000000000020: "sw_thermal_slowdown",
+        0x0000000000000040: "hw_thermal_slowdown", 0x0000000000000080: "hw_power_brake_slowdown",
+        0x0000000000000100: "display_clock_setting",
+    }
+
+    def __init__(self, device_index: int, period_s: float = 0.005):
+        self.samples, self.reasons = [], set()
+        self.max_mhz = None
+        self._stop = threading.Event()
+        self._period = period_s
+        try:
+            import pynvml
+            pynvml.nvmlInit()
+            self._nv = pynvml
+            self._h = pynvml.nvmlDeviceGetHandleByIndex(device_index)
+            self.max_mhz = pynvml.nvmlDeviceGetMaxClockInfo(self._h, pynvml.NVML_CLOCK_SM)
+        except Exception:   # NVML unavailable: report no samples
+            self._nv = None
+        self._t = threading.Thread(target=self._run, daemon=True)
+
+    def _run(self):
+        while not self._stop.is_set():
+            try:
+                self.samples.append(self._nv.nvmlDeviceGetClockInfo(self._h, self._nv.NVML_CLOCK_SM))
+                mask = self._nv.nvmlDeviceGetCurrentClocksEventReasons(self._h)
+                for bit, name in self.REASONS.items():
+                    if mask & bit and bit != 0x1:
+                        self.reasons.add(name)
+            except Exception:
+                pass
+            time.sleep(self._period)
+
+    def __enter__(self):
+        if self._nv is not None:
+            self._t.start()
+        return self
+
+    def __exit__(self, *a):
+        self._stop.set()
+        if self._nv is not None:
+            self._t.join()
+
+    def summary(self):
+        return {"sm_mhz": statistics.median(self.samples) if self.samples else None,
+                "sm_max_mhz": self.max_mhz, "reasons": sorted(self.reasons), "samples": len(self.samples)}
+
+
+# ---------------------------------------------------------------------------
+# distributed plumbing
+# ---------------------------------------------------------------------------
+def dist_init(n_gpus):
+    import torch
+    rank = int(os.environ.get("RANK", "0"))
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    torch.cuda.set_device(local)
+    if world > 1:
+        import datetime
+        import torch.distributed as dist
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=300),
+                                device_id=torch.device("cuda", local))
+    if n_gpus != world and rank == 0:
+        print(f"warning: --gpus {n_gpus} but WORLD_SIZE={world}", file=sys.stderr)
+    return rank, world, local
+
+
+def barrier(world):
+    if world > 1:
+        import torch.distributed as dist
+        dist.barrier()
+
+
+def max_over_ranks(x, world):
+    if world == 1:
+        return x
+    import torch
+    import torch.distributed as dist
+    t = torch.tensor([x], dtype=torch.float64, device="cuda")
+    dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    return float(t.item())
+
+
+def timed(fn, steps, warmup, world, stream, clocks=None):
+    """W warm-up calls, then K calls between CUDA events; returns max-over-ranks ms total."""
+    import torch
+    for _ in range(warmup):
+        fn()
+    torch.cuda.synchronize()
+    barrier(world)
+    torch.cuda.synchronize()
+    t0 = torch.cuda.Event(enable_timing=True)
+    t1 = torch.cuda.Event(enable_timing=True)
+    ctx = clocks if clocks is not None else _Null()
+    with ctx:
+        t0.record(stream)
+        for _ in range(steps):
+            fn()
+        t1.record(stream)
+        torch.cuda.synchronize()
+    barrier(world)
+    return max_over_ranks(t0.elapsed_time(t1), world)
+
+
+class _Null:
+    def __enter__(self):
+        return self
+
+    def __exit__(self, *a):
+        return False
+
+
+# ---------------------------------------------------------------------------
+# synthetic inputs (seeded, on device) with the BASELINE distributions
+# ---------------------------------------------------------------------------
+def gen_prefill(B, T, H, dk, dv, seed, device, layout="bhtd", Hs=None, state=True):
+    import torch
+    g = torch.Generator(device=device).manual_seed(seed)
+    Hs = Hs or H
+    shape_qk = (B, Hs, T, dk) if layout == "bhtd" else (B, T, Hs, dk)
+    shape_v = (B, Hs, T, dv) if layout == "bhtd" else (B, T, Hs, dv)
+    q = torch.nn.functional.normalize(torch.randn(shape_qk, generator=g, device=device), dim=-1).bfloat16()
+    k = torch.nn.functional.normalize(torch.randn(shape_qk, generator=g, device=device), dim=-1).bfloat16()
+    v = torch.randn(shape_v, generator=g, device=device).bfloat16()
+    a = torch.randn(B, Hs, T, generator=g, device=device)                 # fp32 gates (config 1)
+    b = torch.randn(B, Hs, T, generator=g, device=device)
+    A_log = torch.full((Hs,), math.log(0.1), device=device)
+    s0 = torch.randn(B, Hs, dk, dv, generator=g, device=device) * 0.02 if state else None
+    return dict(q=q, k=k, v=v, a=a, b=b, A_log=A_log, state_in=s0)
+
+
+# ---------------------------------------------------------------------------
+# our arm
+# ---------------------------------------------------------------------------
+def run_ours(args):
+    import torch
+    import gdn_18646_b200 as G
+    from gdn_18646_b200 import ops
+
+    rank, world, local = dist_init(args.gpus)
+    dev = torch.device("cuda", local)
+    stream = torch.cuda.current_stream()
+    hbm_peak, tf_peak, peak_kind = measured_peaks()
+    G._lib.lib()
+
+    if args.workload == "long":
+        return run_long(args, rank, world, dev, stream, hbm_peak, tf_peak, peak_kind)
+
+    c = C1
+    inp = gen_prefill(c["B"], c["T"], c["H"], c["dk"], c["dv"], 1234 + rank, dev)
+    out = torch.empty_like(inp["v"])
+    s_out = torch.empty_like(inp["state_in"])
+    scale = 1.0 / math.sqrt(c["dk"])
+
+    def step():
+        ops.prefill(inp["q"], inp["k"], inp["v"], inp["A_log"], inp["a"], inp["b"], state_in=inp["state_in"],
+                    scale=scale, out=out, state_out=s_out)
+
+    clocks = ClockSampler(local)
+    ms = timed(step, args.steps, args.warmup, world, stream, clocks)
+    ms_step = ms / args.steps
+    tokens = c["B"] * c["T"]
+    value = world * tokens / (ms_step * 1e-3)
+    alg_bytes = prefill_alg_bytes(**c)
+    flops = FLOP_PER_TOKEN_HEAD(c["dk"], c["dv"]) * c["B"] * c["T"] * c["H"]
+    achieved_gbs = alg_bytes / (ms_step * 1e-3) / 1e9
+    achieved_tf = flops / (ms_step * 1e-3) / 1e12
+
+    # end-to-end through the public API with host buffers (pinned), copies inside the timed region
+    host_in = {k_: v_.cpu().pin_memory() for k_, v_ in inp.items() if v_ is not None}
+    dev_in = {k_: torch.empty_like(v_) for k_, v_ in inp.items() if v_ is not None}
+    host_o = torch.empty(out.shape, dtype=out.dtype, pin_memory=True)
+    host_s = torch.empty(s_out.shape, dtype=s_out.dtype, pin_memory=True)
+    h2d = sum(t.numel() * t.element_size() for t in host_in.values())
+    d2h = host_o.numel() * 2 + host_s.numel() * 4
+
+    def e2e_step():
+        for k_, t in host_in.items():
+            dev_in[k_].copy_(t, non_blocking=True)
+        ops.prefill(dev_in["q"], dev_in["k"], dev_in["v"], dev_in["A_log"], dev_in["a"], dev_in["b"],
+                    state_in=dev_in["state_in"], scale=scale, out=out, state_out=s_out)
+        host_o.copy_(out, non_blocking=True)
+        host_s.copy_(s_out, non_blocking=True)
+
+    e2e_steps = max(3, min(args.steps, 20))
+    ms_e2e = timed(e2e_step, e2e_steps, max(1, min(args.warmup, 3)), world, stream) / e2e_steps
+    e2e_value = world * tokens / (ms_e2e * 1e-3)
+
+    dec = run_decode(args, rank, world, dev, stream, hbm_peak)
+    cpu = cpu_baseline_prefill() if (rank == 0 and world == 1 and not args.no_cpu_baseline) else None
+
+    if rank == 0:
+        line = {
+            "metric": "prefill tokens/s (config 1: B=4 T=4096 H=16 dk=dv=128, per GPU)",
+            "value": value, "unit": "tokens/s", "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
+            "ms_per_step": ms_step, "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
+            "dtype": "bf16", "data": "synthetic (seeded; BASELINE config-1 distributions)",
+            "config": {"workload": "config1_chunked_prefill", "B": c["B"], "T": c["T"], "H": c["H"],
+                       "dk": c["dk"], "dv": c["dv"], "chunk": 64, "gates": "fp32", "global_batch": world * c["B"],
+                       "seq_len": c["T"], "parallelism": f"batch-sharded x{world} (no collective)",
+                       "l2": "inputs larger than L2 (279 MB per step), no flush"},
+            "e2e": {"value": e2e_value, "unit": "tokens/s", "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h,
+                    "ms_per_step": ms_e2e},
+            "gpu_launches": args.steps,
+            "roofline": {"bound": "hbm", "achieved": achieved_gbs, "peak": hbm_peak, "unit": "GB/s",
+                         "frac": achieved_gbs / hbm_peak, "traffic": PREFILL_TRAFFIC_PER_LAUNCH,
+                         "peak_kind": peak_kind, "alg_bytes_per_launch": alg_bytes,
+                         "tensor_tflops": achieved_tf, "tensor_frac_of_measured": achieved_tf / tf_peak,
+                         "tensor_frac_of_2250": achieved_tf / 2250.0},
+            "clocks": clocks.summary(),
+            "decode": dec,
+            "cpu_baseline": cpu,
+        }
+        print(json.dumps(line), flush=True)
+    finish(world)
+
+
+# ncu-measured DRAM bytes (read + write) of one prefill launch at config 1;
+# None until a capture exists (see profiles/).
+PREFILL_TRAFFIC_PER_LAUNCH = None
+DECODE_TRAFFIC_PER_LAUNCH = None
+
+
+def run_decode(args, rank, world, dev, stream, hbm_peak):
+    """Config 2: 64 consecutive in-place decode steps, fresh q/k/v/a/b per step."""
+    import torch
+    from gdn_18646_b200 import ops
+    c = C2
+    g = torch.Generator(device=dev).manual_seed(777 + rank)
+    B, H, dk, dv, n = c["B"], c["H"], c["dk"], c["dv"], c["steps"]
+    qs = torch.nn.functional.normalize(torch.randn(n, B, H, dk, generator=g, device=dev), dim=-1).bfloat16()
+    ks = torch.nn.functional.normalize(torch.randn(n, B, H, dk, generator=g, device=dev), dim=-1).bfloat16()
+    vs = torch.randn(n, B, H, dv, generator=g, device=dev).bfloat16()
+    as_ = torch.randn(n, B, H, generator=g, device=dev).bfloat16()
+    bs = torch.randn(n, B, H, generator=g, device=dev).bfloat16()
+    A_log = torch.full((H,), math.log(0.1), device=dev)
+    dtb = torch.zeros(H, device=dev)
+    S = torch.randn(B, H, dk, dv, generator=g, device=dev) * 0.02
+    o = torch.empty(B, H, dv, device=dev)
+    state = {"i": 0}
+
+    def step():
+        i = state["i"] % n
+        state["i"] += 1
+        ops.decode_step(qs[i], ks[i], vs[i], as_[i], bs[i], A_log, dtb, S, out=o)
+
+    ms = timed(step, n, 8, world, stream)
+    ms_step = ms / n
+    sb = decode_state_bytes(B, H, dk, dv)
+    gbs = sb / (ms_step * 1e-3) / 1e9
+    return {"config": "config2_decode B=256 H=32 dk=dv=128, 64 in-place steps", "tokens_per_s": world * B / (ms_step * 1e-3),
+            "ms_per_step": ms_step, "state_gbs": gbs, "frac_of_measured_hbm": gbs / hbm_peak,
+            "frac_of_8000": gbs / 8000.0, "state_bytes_per_step": sb, "traffic": DECODE_TRAFFIC_PER_LAUNCH}
+
+
+def run_long(args, rank, world, dev, stream, hbm_peak, tf_peak, peak_kind):
+    """Config 4: head-sharded long-context prefill + NCCL all-gather of o."""
+    import torch
+    from gdn_18646_b200 import ops
+    c = C4
+    H = c["H"]
+    assert H % world == 0, "heads must split evenly"
+    Hs = H // world
+    inp = gen_prefill(c["B"], c["T"], H, c["dk"], c["dv"], 4321 + rank, dev, layout="bhtd", Hs=Hs, state=False)
+    out = torch.empty_like(inp["v"])
+    s_out = torch.empty(c["B"], Hs, c["dk"], c["dv"], device=dev)
+    gathered = torch.empty((world,) + tuple(out.shape), dtype=out.dtype, device=dev) if world > 1 else None
+    scale = 1.0 / math.sqrt(c["dk"])
+
+    def kernel_only():
+        ops.prefill(inp["q"], inp["k"], inp["v"], inp["A_log"], inp["a"], inp["b"], scale=scale, out=out,
+                    state_out=s_out)
+
+    def with_gather():
+        kernel_only()
+        if world > 1:
+            import torch.distributed as dist
+            dist.all_gather_into_tensor(gathered, out)
+
+    ms_k = timed(kernel_only, args.steps, args.warmup, world, stream) / args.steps
+    clocks = ClockSampler(int(os.environ.get("LOCAL_RANK", "0")))
+    ms = timed(with_gather, args.steps, args.warmup, world, stream, clocks) / args.steps
+    tokens = c["B"] * c["T"]
+    alg = prefill_alg_bytes(c["B"], c["T"], Hs, c["dk"], c["dv"])
+    flops = FLOP_PER_TOKEN_HEAD(c["dk"], c["dv"]) * c["B"] * c["T"] * Hs
+    if rank == 0:
+        line = {
+            "metric": "prefill tokens/s (config 4: B=8 T=32768 H=32, heads split over GPUs, o all-gathered)",
+            "value": tokens / (ms * 1e-3), "unit": "tokens/s", "n_gpus": world, "steps": args.steps,
+            "warmup": args.warmup, "ms_per_step": ms, "higher_is_better": True, "scaling": "strong",
+            "vs_baseline": None, "dtype": "bf16", "data": "synthetic (seeded; BASELINE config-4 distributions)",
+            "config": {"workload": "config4_long_context_head_sharded", "B": c["B"], "T": c["T"], "H": H,
+                       "heads_per_gpu": Hs, "parallelism": f"heads x{world} + NCCL all_gather(o)",
+                       "l2": "inputs larger than L2, no flush"},
+            "kernel_only": {"value": tokens / (ms_k * 1e-3), "ms_per_step": ms_k},
+            "gpu_launches": args.steps,
+            "roofline": {"bound": "hbm", "achieved": alg / (ms_k * 1e-3) / 1e9, "peak": hbm_peak, "unit": "GB/s",
+                         "frac": alg / (ms_k * 1e-3) / 1e9 / hbm_peak, "traffic": None, "peak_kind": peak_kind,
+                         "tensor_tflops": flops / (ms_k * 1e-3) / 1e12,
+                         "tensor_frac_of_measured": flops / (ms_k * 1e-3) / 1e12 / tf_peak},
+            "clocks": clocks.summary(),
+        }
+        print(json.dumps(line), flush=True)
+    finish(world)
+
+
+def finish(world):
+    if world > 1:
+        import torch.distributed as dist
+        dist.barrier()
+        dist.destroy_process_group()
+
+
+# ---------------------------------------------------------------------------
+# CPU baseline / reference arm: the reference algorithm restated in numpy
+# ---------------------------------------------------------------------------
+def _cpu_sample(seed, Hs):
+    from oracle import gdn_oracle as O
+    c = C1
+    return O.make_prefill_inputs(seed, 1, c["T"], Hs, c["dk"], c["dv"], gate_dtype="f32", state_std=0.02)
+
+
+def _cpu_run(inp):
+    from oracle import gdn_oracle as O
+    return O.prefill(inp["q"], inp["k"], inp["v"], inp["A_log"], inp["a"], inp["dt_bias"], inp["b"], inp["mask"],
+                     state_in=inp["state_in"], scale=inp["scale"], chunk_size=64)
+
+
+def cpu_baseline_prefill(Hs=4, reps=3):
+    """Best of `reps` oracle runs on a sample of Hs of the 64 config-1 sequences
+    (B=1, T=4096, Hs heads); tokens/s scaled to whole config-1 tokens."""
+    inp = _cpu_sample(99, Hs)
+    best = float("inf")
+    for _ in range(reps):
+        t0 = time.perf_counter()
+        _cpu_run(inp)
+        best = min(best, time.perf_counter() - t0)
+    c = C1
+    frac = Hs / (c["B"] * c["H"])
+    return {"value": frac * c["B"] * c["T"] / best, "unit": "tokens/s", "cores": os.cpu_count(),
+            "kind": "port", "sample": f"oracle/gdn_oracle.prefill (numpy fp32) on {Hs} of the 64 config-1 "
+                                      f"sequences (B=1, T=4096, {Hs} heads), best of {reps}: {best:.2f} s"}
+
+
+def run_reference(args):
+    """The reference arm: the reference's CPU algorithm (numpy restatement of
+    reference/prefill_ref.py), all host threads, bounded sample per step."""
+    rank = int(os.environ.get("RANK", "0"))
+    if rank != 0:
+        return
+    Hs = 2
+    inp = _cpu_sample(7, Hs)
+    for _ in range(args.warmup):
+        _cpu_run(inp)
+    t0 = time.perf_counter()
+    for _ in range(args.steps):
+        _cpu_run(inp)
+    dt = (time.perf_counter() - t0) / args.steps
+    c = C1
+    frac = Hs / (c["B"] * c["H"])
+    value = frac * c["B"] * c["T"] / dt
+    sample = (f"oracle/gdn_oracle.prefill (numpy fp32, {os.cpu_count()} host cores) per step on {Hs} of the 64 "
+              f"config-1 sequences (B=1, T=4096), scaled to config-1 tokens")
+    line = {"impl": "reference", "metric": "prefill tokens/s (config 1: B=4 T=4096 H=16 dk=dv=128, per GPU)",
+            "value": value, "unit": "tokens/s", "n_gpus": int(os.environ.get("WORLD_SIZE", "1")), "steps": args.steps,
+            "warmup": args.warmup, "ms_per_step": dt * 1e3, "higher_is_better": True, "scaling": "weak",
+            "vs_baseline": None, "dtype": "f32", "data": "synthetic (seeded; BASELINE config-1 distributions)",
+            "config": {"workload": "config1_chunked_prefill", "B": c["B"], "T": c["T"], "H": c["H"], "dk": c["dk"],
+                       "dv": c["dv"], "chunk": 64, "sample_heads": Hs},
+            "cpu_baseline": {"value": value, "unit": "tokens/s", "cores": os.cpu_count(), "kind": "port",
+                             "sample": sample},
+            "e2e": {"value": value, "unit": "tokens/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+            "gpu_launches": 0}
+    print(json.dumps(line), flush=True)
+
+
+def main(argv=None):
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=200)
+    ap.add_argument("--warmup", type=int, default=10)
+    ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
+    ap.add_argument("--workload", choices=["prefill", "long"], default="prefill")
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    args = ap.parse_args(argv)
+    if args.warmup < 3:
+        args.warmup = 3
+    if args.impl == "reference":
+        run_reference(args)
+    else:
+        run_ours(args)
+
+
+if __name__ == "__main__":
+    main()

@@ -1,0 +1,91 @@
+"""ctypes binding of libgdn_b200.so (the C ABI declared in include/gdn_b200.h).
+
+The library is the product: there is no CPU or PyTorch fallback.  If the
+shared object is missing, importing an op raises immediately.
+"""
+from __future__ import annotations
+
+import ctypes
+import os
+import threading
+
+LIB_PATH = os.path.join(os.path.dirname(os.path.abspath(__file__)), "lib", "libgdn_b200.so")
+
+# status codes (include/gdn_b200.h)
+GDN_OK = 0
+GDN_ERR_NULL = 1
+GDN_ERR_SHAPE = 2
+GDN_ERR_DTYPE = 3
+GDN_ERR_ALIGN = 4
+GDN_ERR_UNSUPPORTED = 5
+GDN_ERR_CUDA = 6
+GDN_ERR_DEVICE = 7
+GDN_ERR_DEVICE_TIMEOUT = 8
+
+GDN_DTYPE_BF16 = 0
+GDN_DTYPE_F32 = 1
+GDN_LAYOUT_BHTD = 0
+GDN_LAYOUT_BTHD = 1
+
+_P = ctypes.c_void_p
+_I = ctypes.c_int
+_F = ctypes.c_float
+
+# name -> argtypes (every entry returns int unless listed in _STR_FUNCS)
+SIGNATURES = {
+    "gdn_prefill_fwd": [_P, _P, _P, _P, _P, _P, _I, _F, _P, _P, _P, _P, _P,
+                        _I, _I, _I, _I, _I, _I, _I, _F, _P],
+    "gdn_decode_step": [_P, _P, _P, _P, _P, _I, _P, _P, _P, _P, _P, _I, _I, _I, _I, _I, _F, _P],
+    "gdn_rmsnorm_fwd": [_P, _P, _P, _I, _I, _F, _P],
+    "gdn_gated_rmsnorm_fwd": [_P, _I, _P, _P, _P, _I, _I, _F, _P],
+    "gdn_proj_conv_silu_fwd": [_P, _P, _P, _P, _I, _I, _I, _I, _P, _P, _I, _P],
+    "gdn_check_device_error": [],
+    "gdn_last_error": [],
+    "gdn_version": [],
+}
+_STR_FUNCS = {"gdn_last_error", "gdn_version"}
+
+_lock = threading.Lock()
+_lib = None
+
+
+class GdnError(RuntimeError):
+    """A libgdn_b200 entry point returned a non-zero status."""
+
+    def __init__(self, func: str, status: int, message: str):
+        super().__init__(f"{func}: {message} (status {status})")
+        self.status = status
+
+
+def lib() -> ctypes.CDLL:
+    """Load libgdn_b200.so once; raise if it has not been built."""
+    global _lib
+    if _lib is None:
+        with _lock:
+            if _lib is None:
+                if not os.path.exists(LIB_PATH):
+                    raise RuntimeError(
+                        f"{LIB_PATH} is missing: build it with `python -m gdn_18646_b200.build` "
+                        "(there is no fallback implementation)")
+                handle = ctypes.CDLL(LIB_PATH)
+                for name, args in SIGNATURES.items():
+                    fn = getattr(handle, name)
+                    fn.argtypes = args
+                    fn.restype = ctypes.c_char_p if name in _STR_FUNCS else ctypes.c_int
+                _lib = handle
+    return _lib
+
+
+def last_error() -> str:
+    return lib().gdn_last_error().decode()
+
+
+def call(name: str, *args) -> None:
+    status = getattr(lib(), name)(*args)
+    if status != GDN_OK:
+        raise GdnError(name, status, last_error())
+
+
+def call_status(name: str, *args) -> int:
+    """Call without raising; returns the status code."""
+    return getattr(lib(), name)(*args)

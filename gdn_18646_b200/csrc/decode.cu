@@ -1,0 +1,180 @@
+// decode.cu -- single-token gated delta rule step (the recurrence of
+// reference/decode_ref.py:11-61; replaces kernels/decode.cu of the reference).
+//
+// One CTA per (batch, value head).  The fp32 state S[dk][dv] of the head is
+// streamed exactly once in and once out with 16-byte accesses:
+//   thread (cg, rg) owns 4 consecutive value columns 4cg..4cg+3 and the rows
+//   i = r*RG + rg, r < RPT, held in registers as float4.
+// Both reductions over the key dimension (k.S and q.S) are taken from the
+// OLD state in a single pass, using
+//   o_j = scale * (g * (q.S)_j + delta_j * (q.k)),   delta_j = beta*(v_j - g*(k.S)_j),
+// so the update S' = g*S + k delta^T is written straight from registers.
+// Every element is read before any is written by the same thread, so
+// state_out may alias state_in (in-place update).
+#include "common.cuh"
+
+namespace gdn {
+namespace {
+
+template <int DK, int DV>
+struct DecodeCfg {
+    static constexpr int CG = DV / 4;                                   // column groups (float4 each)
+    static constexpr int RPT = DK * DV >= 65536 ? 16 : (DK / 4 < 32 ? DK / 4 : 32);  // rows per thread
+    static constexpr int RG = DK / RPT;                                 // row groups
+    static constexpr int NT = CG * RG;                                  // threads per CTA
+    static_assert(RPT <= 32 && NT <= 1024, "state slice too large for registers");
+};
+
+template <int DK, int DV>
+__global__ void __launch_bounds__(DecodeCfg<DK, DV>::NT)
+decode_step_kernel(const uint16_t* __restrict__ q, const uint16_t* __restrict__ k,
+                   const uint16_t* __restrict__ v, const void* __restrict__ a,
+                   const void* __restrict__ b, int gate_dtype, const float* __restrict__ A_log,
+                   const float* __restrict__ dt_bias, const float* state_in, float* state_out,
+                   float* __restrict__ out, int Hqk, int Hv, float scale) {
+    using C = DecodeCfg<DK, DV>;
+    __shared__ float q_s[DK];
+    __shared__ float k_s[DK];
+    __shared__ float red_a[C::RG][DV];
+    __shared__ float red_b[C::RG][DV];
+    __shared__ float qk_s;
+
+    const int tid = threadIdx.x;
+    const int cg = tid % C::CG;
+    const int rg = tid / C::CG;
+    const int bh = blockIdx.x;                 // b * Hv + h
+    const int h = bh % Hv;
+    const int bidx = bh / Hv;
+    const int hq = h / (Hv / Hqk);
+    const long qk_off = (static_cast<long>(bidx) * Hqk + hq) * DK;
+    const long s_off = static_cast<long>(bh) * DK * DV;
+
+    // issue the state loads first: they dominate the step
+    float4 s[C::RPT];
+#pragma unroll
+    for (int r = 0; r < C::RPT; ++r)
+        s[r] = ld_stream_f4(state_in + s_off + static_cast<long>(r * C::RG + rg) * DV + 4 * cg);
+
+    for (int i = tid; i < DK; i += C::NT) {
+        q_s[i] = bf16_bits_to_f32(q[qk_off + i]);
+        k_s[i] = bf16_bits_to_f32(k[qk_off + i]);
+    }
+    // gates (reference/decode_ref.py:36-38)
+    const float av = load_gate(a, bh, gate_dtype);
+    const float bv = load_gate(b, bh, gate_dtype);
+    const float dtb = dt_bias ? dt_bias[h] : 0.f;
+    const float g = expf(-expf(A_log[h]) * softplus_f(av + dtb));
+    const float beta = sigmoid_f(bv);
+    const uint2 vraw = *reinterpret_cast<const uint2*>(v + static_cast<long>(bh) * DV + 4 * cg);
+    __syncthreads();
+
+    if (tid < 32) {
+        float acc = 0.f;
+        for (int i = tid; i < DK; i += 32) acc += q_s[i] * k_s[i];
+#pragma unroll
+        for (int o = 16; o > 0; o >>= 1) acc += __shfl_xor_sync(0xffffffffu, acc, o);
+        if (tid == 0) qk_s = acc;
+    }
+
+    float pa[4] = {0.f, 0.f, 0.f, 0.f}, pb[4] = {0.f, 0.f, 0.f, 0.f};
+#pragma unroll
+    for (int r = 0; r < C::RPT; ++r) {
+        const int i = r * C::RG + rg;
+        const float ki = k_s[i], qi = q_s[i];
+        pa[0] += ki * s[r].x; pa[1] += ki * s[r].y; pa[2] += ki * s[r].z; pa[3] += ki * s[r].w;
+        pb[0] += qi * s[r].x; pb[1] += qi * s[r].y; pb[2] += qi * s[r].z; pb[3] += qi * s[r].w;
+    }
+    *reinterpret_cast<float4*>(&red_a[rg][4 * cg]) = make_float4(pa[0], pa[1], pa[2], pa[3]);
+    *reinterpret_cast<float4*>(&red_b[rg][4 * cg]) = make_float4(pb[0], pb[1], pb[2], pb[3]);
+    __syncthreads();
+
+    float ka[4] = {0.f, 0.f, 0.f, 0.f}, qa[4] = {0.f, 0.f, 0.f, 0.f};
+#pragma unroll
+    for (int x = 0; x < C::RG; ++x) {
+        const float4 ra = *reinterpret_cast<const float4*>(&red_a[x][4 * cg]);
+        const float4 rb = *reinterpret_cast<const float4*>(&red_b[x][4 * cg]);
+        ka[0] += ra.x; ka[1] += ra.y; ka[2] += ra.z; ka[3] += ra.w;
+        qa[0] += rb.x; qa[1] += rb.y; qa[2] += rb.z; qa[3] += rb.w;
+    }
+    const float vj[4] = {bf16_bits_to_f32(vraw.x & 0xffffu), bf16_bits_to_f32(vraw.x >> 16),
+                         bf16_bits_to_f32(vraw.y & 0xffffu), bf16_bits_to_f32(vraw.y >> 16)};
+    const float qk = qk_s;
+    float delta[4], oj[4];
+#pragma unroll
+    for (int c = 0; c < 4; ++c) {
+        delta[c] = beta * (vj[c] - g * ka[c]);             // decode_ref.py:49-52
+        oj[c] = scale * (g * qa[c] + delta[c] * qk);       // decode_ref.py:56
+    }
+    if (rg == 0)
+        *reinterpret_cast<float4*>(out + static_cast<long>(bh) * DV + 4 * cg) =
+            make_float4(oj[0], oj[1], oj[2], oj[3]);
+
+#pragma unroll
+    for (int r = 0; r < C::RPT; ++r) {
+        const int i = r * C::RG + rg;
+        const float ki = k_s[i];
+        float4 n;
+        n.x = g * s[r].x + ki * delta[0];                  // decode_ref.py:46,53
+        n.y = g * s[r].y + ki * delta[1];
+        n.z = g * s[r].z + ki * delta[2];
+        n.w = g * s[r].w + ki * delta[3];
+        st_stream_f4(state_out + s_off + static_cast<long>(i) * DV + 4 * cg, n);
+    }
+}
+
+template <int DK, int DV>
+void launch_decode(const void* q, const void* k, const void* v, const void* a, const void* b,
+                   int gate_dtype, const float* A_log, const float* dt_bias, const float* s_in,
+                   float* s_out, float* out, int B, int Hqk, int Hv, float scale, cudaStream_t st) {
+    using C = DecodeCfg<DK, DV>;
+    decode_step_kernel<DK, DV><<<B * Hv, C::NT, 0, st>>>(
+        static_cast<const uint16_t*>(q), static_cast<const uint16_t*>(k),
+        static_cast<const uint16_t*>(v), a, b, gate_dtype, A_log, dt_bias, s_in, s_out, out, Hqk, Hv,
+        scale);
+}
+
+}  // namespace
+}  // namespace gdn
+
+extern "C" int gdn_decode_step(const void* q, const void* k, const void* v, const void* a,
+                               const void* b, int gate_dtype, const float* A_log,
+                               const float* dt_bias, const float* state_in, float* state_out,
+                               float* out, int B, int Hqk, int Hv, int dk, int dv, float scale,
+                               void* stream) {
+    using namespace gdn;
+    if (!q || !k || !v || !a || !b || !A_log || !state_in || !state_out || !out)
+        return fail(GDN_ERR_NULL, "gdn_decode_step: q, k, v, a, b, A_log, state_in, state_out and out are required");
+    if (B <= 0 || Hqk <= 0 || Hv <= 0 || Hv % Hqk != 0)
+        return fail(GDN_ERR_SHAPE, "gdn_decode_step: bad B=%d Hqk=%d Hv=%d (need B,H > 0 and Hv %% Hqk == 0)", B, Hqk, Hv);
+    if (static_cast<long>(B) * Hv > 0x7fffffffL)
+        return fail(GDN_ERR_SHAPE, "gdn_decode_step: B*Hv too large");
+    if (gate_dtype != GDN_DTYPE_BF16 && gate_dtype != GDN_DTYPE_F32)
+        return fail(GDN_ERR_DTYPE, "gdn_decode_step: gate_dtype must be GDN_DTYPE_BF16 or GDN_DTYPE_F32");
+    const bool ok_dims = (dk == 64 || dk == 128 || dk == 256) && (dv == 64 || dv == 128 || dv == 256);
+    if (!ok_dims)
+        return fail(GDN_ERR_UNSUPPORTED, "gdn_decode_step: dk=%d dv=%d not supported (each must be 64, 128 or 256)", dk, dv);
+    if (!aligned16(state_in) || !aligned16(state_out) || !aligned16(out) || !aligned16(q) || !aligned16(k) ||
+        (reinterpret_cast<uintptr_t>(v) & 7u))
+        return fail(GDN_ERR_ALIGN, "gdn_decode_step: state/out/q/k must be 16-byte aligned and v 8-byte aligned");
+    int st = check_sm100();
+    if (st != GDN_OK) return st;
+    if (scale == 0.f) scale = 1.f / sqrtf(static_cast<float>(dk));
+    cudaStream_t s = static_cast<cudaStream_t>(stream);
+#define GDN_DEC(DKV, DVV)                                                                     \
+    if (dk == DKV && dv == DVV) {                                                             \
+        launch_decode<DKV, DVV>(q, k, v, a, b, gate_dtype, A_log, dt_bias, state_in, state_out, \
+                                out, B, Hqk, Hv, scale, s);                                     \
+        return launch_status("gdn_decode_step");                                              \
+    }
+    GDN_DEC(64, 64)
+    GDN_DEC(64, 128)
+    GDN_DEC(64, 256)
+    GDN_DEC(128, 64)
+    GDN_DEC(128, 128)
+    GDN_DEC(128, 256)
+    GDN_DEC(256, 64)
+    GDN_DEC(256, 128)
+    GDN_DEC(256, 256)
+#undef GDN_DEC
+    return fail(GDN_ERR_UNSUPPORTED, "gdn_decode_step: unreachable dims");
+}

@@ -1,0 +1,250 @@
+"""Torch-facing operators over the C ABI (libgdn_b200.so).
+
+Two surfaces:
+
+* functional ops (``prefill``, ``decode_step``, ``rmsnorm``, ``gated_rmsnorm``,
+  ``proj_conv_silu``) taking torch CUDA tensors, shape-generic, launching on
+  ``torch.cuda.current_stream()``;
+* drop-in module objects with the reference's operator surface -- the
+  ``exts`` dict consumed by ``gdn_layer.GDNLayerCustom`` (gdn_layer.py:206-217):
+  ``exts()['prefill'].prefill(...)`` (kernels/prefill_chunked.cu:512-526),
+  ``['decode'].forward(...)`` (kernels/decode.cu:172-218),
+  ``['proj'].forward(...)`` (kernels/fused_proj_conv_silu.cu:298-360),
+  ``['rmsnorm'].forward(...)`` (kernels/rmsnorm.cu:280-298).
+
+torch is only the allocator / stream provider here; all arithmetic runs in
+the sm_100a kernels of the library.
+"""
+from __future__ import annotations
+
+import math
+
+import torch
+
+from . import _lib
+from ._lib import (GDN_DTYPE_BF16, GDN_DTYPE_F32, GDN_LAYOUT_BHTD, GDN_LAYOUT_BTHD)
+
+CHUNK = 64
+
+
+def _stream() -> int:
+    return torch.cuda.current_stream().cuda_stream
+
+
+def _ptr(t):
+    return None if t is None else t.data_ptr()
+
+
+def _gate_dtype(t: torch.Tensor, name: str) -> int:
+    if t.dtype == torch.bfloat16:
+        return GDN_DTYPE_BF16
+    if t.dtype == torch.float32:
+        return GDN_DTYPE_F32
+    raise RuntimeError(f"{name}: gate tensors must be bfloat16 or float32, got {t.dtype}")
+
+
+def _need(cond: bool, msg: str) -> None:
+    if not cond:
+        raise RuntimeError(msg)
+
+
+def _cuda_contig(t: torch.Tensor, name: str, dtype=None) -> None:
+    _need(t.is_cuda, f"{name} must be a CUDA tensor")
+    _need(t.is_contiguous(), f"{name} must be contiguous")
+    if dtype is not None:
+        _need(t.dtype == dtype, f"{name} must be {dtype}, got {t.dtype}")
+
+
+# ---------------------------------------------------------------------------
+# functional ops
+# ---------------------------------------------------------------------------
+
+
+def prefill(q, k, v, A_log, a, b_logits, *, dt_bias=0.0, mask=None, state_in=None,
+            scale=0.0, layout="bhtd", out=None, state_out=None, return_state=True):
+    """Chunked gated-delta-rule prefill (reference/prefill_ref.py semantics).
+
+    layout "bhtd": q,k [B,Hqk,T,dk], v [B,Hv,T,dv]; "bthd": q,k [B,T,Hqk,dk], v [B,T,Hv,dv].
+    a, b_logits [B,Hv,T] (bf16 or f32); A_log [Hv] f32; dt_bias float or f32 [Hv];
+    mask [B,T] f32 or None; state_in [B,Hv,dk,dv] f32 or None.
+    Returns (out bf16 in v's layout, state_out f32 [B,Hv,dk,dv] or None).
+    """
+    lay = GDN_LAYOUT_BHTD if layout == "bhtd" else GDN_LAYOUT_BTHD
+    for name, t in (("q", q), ("k", k), ("v", v)):
+        _cuda_contig(t, name, torch.bfloat16)
+    if lay == GDN_LAYOUT_BHTD:
+        B, Hqk, T, dk = q.shape
+        Hv, dv = v.shape[1], v.shape[3]
+    else:
+        B, T, Hqk, dk = q.shape
+        Hv, dv = v.shape[2], v.shape[3]
+    _need(tuple(k.shape) == tuple(q.shape), "k must have q's shape")
+    gdt = _gate_dtype(a, "a")
+    _need(b_logits.dtype == a.dtype, "a and b_logits must share a dtype")
+    _cuda_contig(a, "a")
+    _cuda_contig(b_logits, "b_logits")
+    _need(tuple(a.shape) == (B, Hv, T) and tuple(b_logits.shape) == (B, Hv, T), "a, b_logits must be [B, Hv, T]")
+    _cuda_contig(A_log, "A_log", torch.float32)
+    dt_vec = None
+    dt_scalar = 0.0
+    if isinstance(dt_bias, torch.Tensor) and dt_bias.numel() > 1:
+        _cuda_contig(dt_bias, "dt_bias", torch.float32)
+        dt_vec = dt_bias
+    else:
+        dt_scalar = float(dt_bias)
+    if mask is not None:
+        _cuda_contig(mask, "mask", torch.float32)
+    if state_in is not None:
+        _cuda_contig(state_in, "state_in", torch.float32)
+    if out is None:
+        out = torch.empty_like(v)
+    if state_out is None and return_state:
+        state_out = torch.empty(B, Hv, dk, dv, dtype=torch.float32, device=q.device)
+    _lib.call("gdn_prefill_fwd", _ptr(q), _ptr(k), _ptr(v), _ptr(A_log), _ptr(a), _ptr(b_logits), gdt,
+              dt_scalar, _ptr(dt_vec), _ptr(mask), _ptr(state_in), _ptr(out), _ptr(state_out),
+              B, T, Hqk, Hv, dk, dv, lay, float(scale), _stream())
+    return out, state_out
+
+
+def decode_step(q, k, v, a, b, A_log, dt_bias, state, *, scale=0.0, out=None, state_out=None):
+    """One decode step; updates ``state`` in place unless ``state_out`` is given.
+    q,k [B,Hqk,dk] bf16; v [B,Hv,dv] bf16; a,b [B,Hv]; state [B,Hv,dk,dv] f32.
+    Returns out f32 [B,Hv,dv]."""
+    B, Hqk, dk = q.shape
+    Hv, dv = v.shape[1], v.shape[2]
+    for name, t in (("q", q), ("k", k), ("v", v)):
+        _cuda_contig(t, name, torch.bfloat16)
+    _cuda_contig(state, "state", torch.float32)
+    gdt = _gate_dtype(a, "a")
+    if out is None:
+        out = torch.empty(B, Hv, dv, dtype=torch.float32, device=q.device)
+    if state_out is None:
+        state_out = state
+    _lib.call("gdn_decode_step", _ptr(q), _ptr(k), _ptr(v), _ptr(a), _ptr(b), gdt, _ptr(A_log),
+              _ptr(dt_bias), _ptr(state), _ptr(state_out), _ptr(out), B, Hqk, Hv, dk, dv, float(scale),
+              _stream())
+    return out
+
+
+def rmsnorm(x, gamma, eps=1e-6, out=None):
+    """y = x * rsqrt(mean(x^2) + eps) * gamma over the last dim; bf16 in/out."""
+    _cuda_contig(x, "x", torch.bfloat16)
+    _cuda_contig(gamma, "gamma", torch.bfloat16)
+    D = x.shape[-1]
+    R = x.numel() // D
+    if out is None:
+        out = torch.empty_like(x)
+    _lib.call("gdn_rmsnorm_fwd", _ptr(x), _ptr(gamma), _ptr(out), R, D, float(eps), _stream())
+    return out
+
+
+def gated_rmsnorm(x, z, gamma, eps=1e-6, out=None):
+    """y = rmsnorm(x) * gamma * silu(z) over the last dim (x bf16 or f32, z bf16)."""
+    _cuda_contig(x, "x")
+    _cuda_contig(z, "z", torch.bfloat16)
+    _cuda_contig(gamma, "gamma", torch.bfloat16)
+    xdt = _gate_dtype(x, "x")
+    D = x.shape[-1]
+    R = x.numel() // D
+    if out is None:
+        out = torch.empty(x.shape, dtype=torch.bfloat16, device=x.device)
+    _lib.call("gdn_gated_rmsnorm_fwd", _ptr(x), xdt, _ptr(z), _ptr(gamma), _ptr(out), R, D, float(eps),
+              _stream())
+    return out
+
+
+def proj_conv_silu(x, W, conv_w, *, conv_state_in=None, conv_state_out=None, l2norm_group=0, out=None):
+    """SiLU(causal_conv4(x @ W^T)) with optional conv history and per-group L2 norm.
+    x [B,T,D] bf16; W [Dout,D] bf16; conv_w [Dout,4] bf16 -> [B,T,Dout] bf16."""
+    _cuda_contig(x, "x", torch.bfloat16)
+    _cuda_contig(W, "W", torch.bfloat16)
+    _cuda_contig(conv_w, "conv_w", torch.bfloat16)
+    B, T, D = x.shape
+    Dout = W.shape[0]
+    if out is None:
+        out = torch.empty(B, T, Dout, dtype=torch.bfloat16, device=x.device)
+    _lib.call("gdn_proj_conv_silu_fwd", _ptr(x), _ptr(W), _ptr(conv_w), _ptr(out), B, T, D, Dout,
+              _ptr(conv_state_in), _ptr(conv_state_out), int(l2norm_group), _stream())
+    return out
+
+
+# ---------------------------------------------------------------------------
+# reference-surface modules (drop-in for GDNLayerCustom's ``exts`` dict)
+# ---------------------------------------------------------------------------
+
+
+class PrefillModule:
+    """``prefill(q,k,v,A_log,a,dt_bias,b_logits,mask,state_in,scale) -> (out, state_out)``
+    with the argument meaning of kernels/prefill_chunked.cu:422-433 (q,k,v [B,H,T,*]
+    bf16; a,b_logits [B,H,T] bf16; dt_bias float; mask [B,T] f32; state_in empty =
+    zeros).  Shape-generic: H, dk in {64,128}, dv in {64,128,256}, any T."""
+
+    # the reference layer's shapes (gdn_layer.py:24-28); C_DIM is the chunk length
+    H_DIM = 16
+    K_DIM = 128
+    V_DIM = 256
+    C_DIM = CHUNK
+
+    def prefill(self, q, k, v, A_log, a, dt_bias, b_logits, mask, state_in, scale):
+        for name, t in (("q", q), ("k", k), ("v", v), ("a", a), ("b_logits", b_logits)):
+            _need(t.is_cuda and t.is_contiguous() and t.dtype == torch.bfloat16,
+                  f"{name}: contiguous bfloat16 CUDA required")
+        s_in = state_in if (state_in is not None and state_in.numel() > 0) else None
+        return prefill(q, k, v, A_log, a, b_logits, dt_bias=float(dt_bias), mask=mask, state_in=s_in,
+                       scale=float(scale), layout="bhtd")
+
+
+class DecodeModule:
+    """``forward(q,k,v,a_sc,b_sc,A_log,dt_bias,S_in,scale,o_out,S_out) -> None``
+    (kernels/decode.cu:172-214): q,k [B,H,K], v [B,H,V] bf16, a,b [B,H] bf16,
+    A_log, dt_bias [H] f32, S_in/S_out [B,H,K,V] f32 (may alias), o_out [B,H,V] f32."""
+
+    def forward(self, q, k, v, a_sc, b_sc, A_log, dt_bias, S_in, scale, o_out, S_out):
+        for name, t in (("q", q), ("k", k), ("v", v), ("a_sc", a_sc), ("b_sc", b_sc), ("A_log", A_log),
+                        ("dt_bias", dt_bias), ("S_in", S_in), ("o_out", o_out), ("S_out", S_out)):
+            _need(t.is_cuda, f"{name} must be a CUDA tensor")
+            _need(t.is_contiguous(), f"{name} must be contiguous")
+        decode_step(q, k, v, a_sc, b_sc, A_log, dt_bias, S_in, scale=float(scale), out=o_out, state_out=S_out)
+
+
+class ProjModule:
+    """``forward(input [B,T,D], weight [D_out,D], conv_w [D_out,4]) -> [B,T,D_out]``
+    bf16 (kernels/fused_proj_conv_silu.cu:298-355)."""
+
+    def forward(self, input, weight, conv_w):
+        _need(input.is_cuda and weight.is_cuda and conv_w.is_cuda, "all tensors must be on CUDA")
+        _need(input.is_contiguous() and weight.is_contiguous() and conv_w.is_contiguous(),
+              "all tensors must be contiguous")
+        _need(input.dtype == torch.bfloat16 and weight.dtype == torch.bfloat16 and conv_w.dtype == torch.bfloat16,
+              "all tensors must be bfloat16")
+        _need(weight.shape[1] == input.shape[2], "weight dim-1 must equal D")
+        _need(conv_w.shape[0] == weight.shape[0], "conv_w dim-0 must equal D_out")
+        _need(conv_w.shape[1] == 4, "conv_w dim-1 must equal CONV_K")
+        return proj_conv_silu(input, weight, conv_w)
+
+
+class RMSNormModule:
+    """``forward(x [R,D] bf16, gamma [D] bf16, eps, block_threads, rows_per_block)``
+    (kernels/rmsnorm.cu:280-293).  The launch-shape arguments are validated like the
+    reference's (:133-144) and otherwise unused; any D % 8 == 0 up to 8192 works."""
+
+    def forward(self, x, gamma, eps, block_threads, rows_per_block):
+        _need(x.is_cuda, "x must be CUDA")
+        _need(gamma.is_cuda, "gamma must be CUDA")
+        _need(x.dtype == torch.bfloat16, "x must be BF16")
+        _need(gamma.dtype == torch.bfloat16, "gamma must be BF16")
+        _need(x.dim() == 2, "x must be [R, D]")
+        _need(gamma.dim() == 1 and gamma.shape[0] == x.shape[1], "gamma must be [D]")
+        _need(x.is_contiguous() and gamma.is_contiguous(), "inputs must be contiguous")
+        _need(rows_per_block >= 1, "rows_per_block must be >= 1")
+        _need(32 <= block_threads <= 1024, "block_threads must be in [32, 1024]")
+        _need(block_threads % rows_per_block == 0, "block_threads must be divisible by rows_per_block")
+        tpr = block_threads // rows_per_block
+        _need(tpr >= 32 and tpr % 32 == 0, "threads_per_row must be a multiple of 32")
+        return rmsnorm(x, gamma, float(eps))
+
+
+def exts() -> dict:
+    """The ``exts`` dict of gdn_layer.GDNLayerCustom (gdn_layer.py:209-217)."""
+    _lib.lib()  # fail loudly now if the library is missing
+    return dict(rmsnorm=RMSNormModule(), proj=ProjModule(), prefill=PrefillModule(), decode=DecodeModule())

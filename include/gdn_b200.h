@@ -1,0 +1,143 @@
+/*
+ * gdn_b200.h -- C ABI of the B200 (sm_100a) Gated DeltaNet hot path.
+ *
+ * Every entry point takes raw DEVICE pointers, explicit shapes, a CUDA
+ * stream (passed as void*, a cudaStream_t; NULL = legacy default stream) and
+ * returns an int status (GDN_OK == 0).  Launches are asynchronous on that
+ * stream; no entry point allocates device memory or synchronises.  On error
+ * nothing is launched and gdn_last_error() describes the problem (the message
+ * is per calling thread).
+ *
+ * bf16 tensors are raw 16-bit buffers (__nv_bfloat16 / torch.bfloat16).
+ * Each declaration names the reference interface it replaces
+ * (diacccc/GDN_18646, file:line).
+ */
+#ifndef GDN_B200_H
+#define GDN_B200_H
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+/* status codes */
+enum {
+    GDN_OK = 0,
+    GDN_ERR_NULL = 1,        /* a required pointer is NULL                     */
+    GDN_ERR_SHAPE = 2,       /* a size is out of range or inconsistent         */
+    GDN_ERR_DTYPE = 3,       /* unknown dtype / layout code                    */
+    GDN_ERR_ALIGN = 4,       /* a pointer is not 16-byte aligned               */
+    GDN_ERR_UNSUPPORTED = 5, /* head dims or widths this build does not cover  */
+    GDN_ERR_CUDA = 6,        /* a CUDA runtime/driver call or launch failed    */
+    GDN_ERR_DEVICE = 7,      /* the current device is not an sm_100 part       */
+    GDN_ERR_DEVICE_TIMEOUT = 8 /* a kernel gave up on a bounded wait           */
+};
+
+/* dtype codes for gate / activation inputs */
+enum { GDN_DTYPE_BF16 = 0, GDN_DTYPE_F32 = 1 };
+
+/* activation layouts: [B, H, T, D] (the reference's) or [B, T, H, D] */
+enum { GDN_LAYOUT_BHTD = 0, GDN_LAYOUT_BTHD = 1 };
+
+/* Chunk length of the prefill kernel (the reference's C_DIM,
+ * kernels/prefill_chunked.cu:18). */
+#define GDN_CHUNK 64
+
+/*
+ * Chunked gated-delta-rule prefill.
+ * Replaces gdn_prefill() / the "prefill" pybind op,
+ * kernels/prefill_chunked.cu:422-504 and :512-521 (math: reference/prefill_ref.py:11-132).
+ *
+ *   q, k       bf16 [B, Hqk, T, dk] (layout BHTD) or [B, T, Hqk, dk] (BTHD)
+ *   v          bf16 [B, Hv, T, dv]  or [B, T, Hv, dv]
+ *   A_log      f32  [Hv]
+ *   a, b_logits [B, Hv, T] in gate_dtype (bf16 or f32)
+ *   dt_bias    scalar, used when dt_bias_vec == NULL; else dt_bias_vec f32 [Hv]
+ *   mask       f32 [B, T] or NULL (all ones)
+ *   state_in   f32 [B, Hv, dk, dv] or NULL (zeros)     (the reference's empty tensor)
+ *   out        bf16, same layout as v
+ *   state_out  f32 [B, Hv, dk, dv] (may be NULL: final state not written)
+ *   scale      0.0f -> 1/sqrt(dk)  (reference/prefill_ref.py:45-46)
+ * Value head h reads q/k head h / (Hv / Hqk) (grouped value heads; Hqk == Hv
+ * is the reference's case).  Supported: dk in {64, 128}, dv in {64, 128, 256},
+ * any T >= 1 (a ragged last chunk is handled like the reference's padding),
+ * Hv % Hqk == 0.  Pointers must be 16-byte aligned.
+ */
+int gdn_prefill_fwd(const void* q, const void* k, const void* v,
+                    const float* A_log, const void* a, const void* b_logits, int gate_dtype,
+                    float dt_bias, const float* dt_bias_vec,
+                    const float* mask, const float* state_in,
+                    void* out, float* state_out,
+                    int B, int T, int Hqk, int Hv, int dk, int dv, int layout,
+                    float scale, void* stream);
+
+/*
+ * Single-token decode step, state updated in place if state_out == state_in.
+ * Replaces gdn_decode_cuda(), kernels/decode.cu:131-162, and its torch wrapper
+ * gdn_decode_forward(), kernels/decode.cu:172-214 (math: reference/decode_ref.py:11-61).
+ *
+ *   q, k       bf16 [B, Hqk, dk];  v bf16 [B, Hv, dv]
+ *   a, b       [B, Hv] in gate_dtype
+ *   A_log, dt_bias  f32 [Hv] (dt_bias may be NULL = 0)
+ *   state_in   f32 [B, Hv, dk, dv];  state_out f32 [B, Hv, dk, dv] (may alias state_in)
+ *   out        f32 [B, Hv, dv]
+ *   scale      0.0f -> 1/sqrt(dk)
+ * Supported: dk, dv in {64, 128, 256}.
+ */
+int gdn_decode_step(const void* q, const void* k, const void* v,
+                    const void* a, const void* b, int gate_dtype,
+                    const float* A_log, const float* dt_bias,
+                    const float* state_in, float* state_out, float* out,
+                    int B, int Hqk, int Hv, int dk, int dv, float scale, void* stream);
+
+/*
+ * RMSNorm, bf16 in/out, fp32 math: y = x * rsqrt(mean(x^2) + eps) * gamma.
+ * Replaces rmsnorm_forward(), kernels/rmsnorm.cu:280-293 (math: reference/rmsnorm_ref.py:9-28).
+ * x, y bf16 [R, D]; gamma bf16 [D].  D % 8 == 0, D <= 8192 (D <= 4096 when x is f32).
+ */
+int gdn_rmsnorm_fwd(const void* x, const void* gamma, void* y, int R, int D, float eps,
+                    void* stream);
+
+/*
+ * Gated output RMSNorm: y = RMSNorm(x) * gamma * SiLU(z) (per row of D).
+ * No counterpart in the reference (the BASELINE layer's gated norm; the
+ * RMSNorm part follows reference/rmsnorm_ref.py:24-28).
+ * x [R, D] in x_dtype (bf16 or f32); z bf16 [R, D]; gamma bf16 [D]; y bf16 [R, D].
+ * D % 8 == 0, D <= 8192 (D <= 4096 when x is f32).
+ */
+int gdn_gated_rmsnorm_fwd(const void* x, int x_dtype, const void* z, const void* gamma, void* y,
+                          int R, int D, float eps, void* stream);
+
+/*
+ * Fused input projection + causal depthwise conv1d (kernel 4) + SiLU.
+ * Replaces fused_proj_conv_silu(), kernels/fused_proj_conv_silu.cu:298-355
+ * (math: reference/fused_proj_conv_silu_ref.py:33-67).
+ *   x bf16 [B, T, D]; W bf16 [Dout, D]; conv_w bf16 [Dout, 4]; y bf16 [B, T, Dout]
+ *   conv_state_in  bf16 [B, Dout, 3] or NULL: the 3 projected tokens preceding x
+ *                  (oldest first; NULL = zeros, the reference's causal padding)
+ *   conv_state_out bf16 [B, Dout, 3] or NULL: receives the last 3 projected tokens
+ *   l2norm_group   0, or a head size g (Dout % g == 0): each g-wide group of the
+ *                  output is L2-normalised (fp32, eps 1e-6) before the bf16 store.
+ * D % 64 == 0, Dout % 128 == 0.
+ */
+int gdn_proj_conv_silu_fwd(const void* x, const void* W, const void* conv_w, void* y,
+                           int B, int T, int D, int Dout,
+                           const void* conv_state_in, void* conv_state_out,
+                           int l2norm_group, void* stream);
+
+/* Human-readable description of the calling thread's last error. */
+const char* gdn_last_error(void);
+
+/* Library version string. */
+const char* gdn_version(void);
+
+/*
+ * Reads and clears the device-side error word of the current device (set by a
+ * kernel that gave up on a bounded wait).  Synchronises the device.  Returns
+ * GDN_OK, GDN_ERR_DEVICE_TIMEOUT or GDN_ERR_CUDA.
+ */
+int gdn_check_device_error(void);
+
+#ifdef __cplusplus
+}
+#endif
+#endif /* GDN_B200_H */

