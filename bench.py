@@ -443,6 +443,53 @@ def run_reference(args):
     print(json.dumps(line), flush=True)
 
 
+def run_only(args):
+    """One kernel, ``--warmup`` + ``--steps`` launches, no extras: the command
+    the ncu captures under profiles/ were taken with."""
+    import torch
+    from gdn_18646_b200 import ops
+    dev = torch.device("cuda", 0)
+    torch.cuda.set_device(dev)
+    if args.only == "prefill":
+        c = C1
+        inp = gen_prefill(c["B"], c["T"], c["H"], c["dk"], c["dv"], 1234, dev)
+        out = torch.empty_like(inp["v"])
+        s_out = torch.empty_like(inp["state_in"])
+
+        def step():
+            ops.prefill(inp["q"], inp["k"], inp["v"], inp["A_log"], inp["a"], inp["b"], state_in=inp["state_in"],
+                        scale=c["dk"] ** -0.5, out=out, state_out=s_out)
+    elif args.only == "decode":
+        c = C2
+        g = torch.Generator(device=dev).manual_seed(5)
+        B, H, dk, dv = c["B"], c["H"], c["dk"], c["dv"]
+        q = torch.nn.functional.normalize(torch.randn(B, H, dk, generator=g, device=dev), dim=-1).bfloat16()
+        k = torch.nn.functional.normalize(torch.randn(B, H, dk, generator=g, device=dev), dim=-1).bfloat16()
+        v = torch.randn(B, H, dv, generator=g, device=dev).bfloat16()
+        a = torch.randn(B, H, generator=g, device=dev).bfloat16()
+        b = torch.randn(B, H, generator=g, device=dev).bfloat16()
+        A_log = torch.full((H,), math.log(0.1), device=dev)
+        dtb = torch.zeros(H, device=dev)
+        S = torch.randn(B, H, dk, dv, generator=g, device=dev) * 0.02
+        o = torch.empty(B, H, dv, device=dev)
+
+        def step():
+            ops.decode_step(q, k, v, a, b, A_log, dtb, S, out=o)
+    else:
+        # config 3 fused q|k|v projection: x [2, 8192, 2048] -> 8192 conv channels
+        g = torch.Generator(device=dev).manual_seed(6)
+        x = torch.randn(2, 8192, 2048, generator=g, device=dev).bfloat16()
+        W = (torch.randn(8192, 2048, generator=g, device=dev) * 0.02).bfloat16()
+        cw = (torch.randn(8192, 4, generator=g, device=dev) * 0.5).bfloat16()
+        y = torch.empty(2, 8192, 8192, dtype=torch.bfloat16, device=dev)
+
+        def step():
+            ops.proj_conv_silu(x, W, cw, out=y)
+    stream = torch.cuda.current_stream()
+    ms = timed(step, max(1, args.steps), max(0, args.warmup), 1, stream)
+    print(json.dumps({"only": args.only, "steps": args.steps, "ms_per_step": ms / max(1, args.steps)}), flush=True)
+
+
 def main(argv=None):
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
@@ -451,7 +498,11 @@ def main(argv=None):
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--workload", choices=["prefill", "long"], default="prefill")
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--only", choices=["prefill", "decode", "proj"], default=None,
+                    help="run just one kernel's workload (for profiling); prints a short JSON line")
     args = ap.parse_args(argv)
+    if args.only:
+        return run_only(args)
     if args.warmup < 3:
         args.warmup = 3
     if args.impl == "reference":

@@ -47,18 +47,47 @@ __device__ __forceinline__ float bf16_bits_to_f32(uint16_t b) {
     return __uint_as_float(static_cast<uint32_t>(b) << 16);
 }
 __device__ __forceinline__ uint16_t f32_to_bf16_bits(float x) {
-    __nv_bfloat16 h = __float2bfloat16_rn(x);
-    return *reinterpret_cast<uint16_t*>(&h);
+    uint16_t r;
+    asm("cvt.rn.bf16.f32 %0, %1;" : "=h"(r) : "f"(x));
+    return r;
 }
-// pack two floats into a bf16x2 word (lo in the low half)
+// pack two floats into a bf16x2 word (lo in the low half), round to nearest even
 __device__ __forceinline__ uint32_t pack_bf16x2(float lo, float hi) {
-    return static_cast<uint32_t>(f32_to_bf16_bits(lo)) |
-           (static_cast<uint32_t>(f32_to_bf16_bits(hi)) << 16);
+    uint32_t r;
+    asm("cvt.rn.bf16x2.f32 %0, %1, %2;" : "=r"(r) : "f"(hi), "f"(lo));
+    return r;
 }
 // split x into bf16 hi + bf16 lo with x ~= hi + lo (relative error ~2^-16)
 __device__ __forceinline__ void split_bf16(float x, uint16_t& hi, uint16_t& lo) {
     hi = f32_to_bf16_bits(x);
     lo = f32_to_bf16_bits(x - bf16_bits_to_f32(hi));
+}
+
+// Two floats -> packed bf16x2 (round to nearest even), x0 in the low half.
+__device__ __forceinline__ uint32_t cvt_bf16x2(float x0, float x1) {
+    uint32_t r;
+    asm("cvt.rn.bf16x2.f32 %0, %1, %2;" : "=r"(r) : "f"(x1), "f"(x0));
+    return r;
+}
+// Split two floats into bf16x2 hi and lo words with x ~= hi + lo.
+__device__ __forceinline__ void split2_bf16(float x0, float x1, uint32_t& hi, uint32_t& lo) {
+    hi = cvt_bf16x2(x0, x1);
+    lo = cvt_bf16x2(x0 - __uint_as_float(hi << 16), x1 - __uint_as_float(hi & 0xffff0000u));
+}
+// 2^x on the MUFU (relative error ~2^-22; inputs here are <= 0 or bounded).
+__device__ __forceinline__ float ex2_approx(float x) {
+    float y;
+    asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
+    return y;
+}
+
+// warp-level bf16 MMA, m16n8k16, fp32 accumulate (used for small 16x16 blocks)
+__device__ __forceinline__ void mma_bf16_16816(float (&d)[4], const uint32_t (&a)[4], uint32_t b0, uint32_t b1) {
+    asm volatile(
+        "mma.sync.aligned.m16n8k16.row.col.f32.bf16.bf16.f32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, "
+        "{%0,%1,%2,%3};"
+        : "+f"(d[0]), "+f"(d[1]), "+f"(d[2]), "+f"(d[3])
+        : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b0), "r"(b1));
 }
 
 // Load a gate value stored as bf16 or f32.
@@ -140,6 +169,48 @@ __device__ __forceinline__ void tma_load_3d(void* dst, const CUtensorMap* map, u
         " [%0], [%1, {%3, %4, %5}], [%2];" ::"r"(smem_u32(dst)),
         "l"(reinterpret_cast<uint64_t>(map)), "r"(smem_u32(bar)), "r"(c0), "r"(c1), "r"(c2)
         : "memory");
+}
+
+// TMA tiled store smem -> global (bulk group), its commit and read-completion wait
+__device__ __forceinline__ void tma_store_3d(const CUtensorMap* map, const void* src, int c0, int c1, int c2) {
+    asm volatile("cp.async.bulk.tensor.3d.global.shared::cta.bulk_group [%0, {%2, %3, %4}], [%1];" ::"l"(
+                     reinterpret_cast<uint64_t>(map)),
+                 "r"(smem_u32(src)), "r"(c0), "r"(c1), "r"(c2)
+                 : "memory");
+}
+__device__ __forceinline__ void tma_store_4d(const CUtensorMap* map, const void* src, int c0, int c1, int c2,
+                                             int c3) {
+    asm volatile("cp.async.bulk.tensor.4d.global.shared::cta.bulk_group [%0, {%2, %3, %4, %5}], [%1];" ::"l"(
+                     reinterpret_cast<uint64_t>(map)),
+                 "r"(smem_u32(src)), "r"(c0), "r"(c1), "r"(c2), "r"(c3)
+                 : "memory");
+}
+__device__ __forceinline__ void bulk_commit() { asm volatile("cp.async.bulk.commit_group;" ::: "memory"); }
+__device__ __forceinline__ void bulk_wait_read0() {
+    asm volatile("cp.async.bulk.wait_group.read 0;" ::: "memory");
+}
+__device__ __forceinline__ void bulk_wait_all0() { asm volatile("cp.async.bulk.wait_group 0;" ::: "memory"); }
+
+// named barrier over a subset of warps
+__device__ __forceinline__ void named_bar(int id, int nthreads) {
+    asm volatile("bar.sync %0, %1;" ::"r"(id), "r"(nthreads) : "memory");
+}
+
+// Wait that also gives up as soon as another thread of the CTA raised *abort
+// (so every role of a warp-specialised kernel drains after one timeout).
+__device__ __forceinline__ bool mbar_wait_or_abort(uint64_t* bar, uint32_t parity, unsigned int* err,
+                                                   volatile int* abort) {
+    if (mbar_try_wait(bar, parity)) return true;
+    const long long t0 = clock64();
+    while (!mbar_try_wait(bar, parity)) {
+        if (*abort) return false;
+        if (clock64() - t0 > (1ll << 31)) {
+            if (err) atomicOr(err, DERR_TIMEOUT);
+            *abort = 1;
+            return false;
+        }
+    }
+    return true;
 }
 
 // generic-proxy smem writes -> visible to the async proxy (MMA / TMA store)

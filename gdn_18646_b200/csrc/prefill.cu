@@ -2,34 +2,47 @@
 //
 // Math: reference/prefill_ref.py:11-132 (chunk C = 64, WY / UT form).  Replaces
 // the reference's gdn_prefill_v2_kernel (kernels/prefill_chunked.cu:41-417),
-// which runs fp32 CUDA-core loops and hard-codes H=16, K=128, V=256.
+// which runs fp32 CUDA-core loops with one thread per value column and
+// hard-codes H=16, K=128, V=256.
 //
 // One CTA per (batch, value head, 128-wide value tile).  Per 64-token chunk,
-// with Lambda the in-chunk cumulative log decay, beta' = beta * mask and
-//   N[t,s] = -beta'_t (k_t . k_s) exp(Lambda_t - Lambda_s)   (t > s)
-//   A'     = (I - N)^-1 diag(beta')                          (prefill_ref.py:96-101)
-// the chunk update is computed in the "R form"
-//   R   = V - diag(e^Lambda) K S                 (K S on tensor cores)
-//   dV  = A' R                                   (= U - W S of prefill_ref.py:103-118)
-//   O   = diag(m) [ scale diag(e^Lambda) Q S + P dV ],
-//         P[t,s] = scale (q_t . k_s) exp(Lambda_t - Lambda_s), s <= t    (:120-122)
-//   S  <- e^{Lambda_last} S + K^T diag(e^{Lambda_last - Lambda}) dV       (:124-126)
-// Every product is one tcgen05.mma.kind::f16 chain with M = 128 rows in TMEM:
-// the state is kept TRANSPOSED (S^T, value index = TMEM lane) so the value
-// tile is the M dimension of every product:
-//   QKK = [Q;K] K^T                      M=128 (64 q rows + 64 k rows), N=64
-//   SQK = S^T [Q;K]^T  (S_hi, + S_lo K)  M=128, N=128  -> (QS)^T | (KS)^T
-//   DV  = R^T A'^T     (3 split terms)   M=128, N=64   -> dV^T
-//   ST += dV'^T K      (2 split terms)   M=128, N=dk   (K operand MN-major)
-//   PDV = dV^T P^T                       M=128, N=64
-// fp32 intermediates that feed the state path (S, R, A', dV') are split into
-// bf16 hi + lo pairs, so those products carry ~16 mantissa bits; q/k/v are
-// exact bf16 inputs.  The output path (Q S_hi, P dV) uses single bf16.
-// The 64x64 unit-lower-triangular inverse runs on CUDA cores in fp32
-// (16x16 diagonal blocks by forward substitution in registers, then the
-// off-diagonal blocks), the decay ratios are exp(Lambda_t - Lambda_s), never
-// gamma_t / gamma_s.  q/k/v chunks arrive by TMA (128B swizzle), double
-// buffered; the fp32 state lives in TMEM for the whole sequence.
+// with Lambda the in-chunk cumulative log decay, beta' = beta * mask,
+//   N[t,s] = -beta'_t (k_t . k_s) exp(Lambda_t - Lambda_s)  (t > s)
+//   A      = (I - N)^-1                                      (prefill_ref.py:96-101)
+//   U      = A diag(beta') V,  W = A diag(beta' e^Lambda) K  (prefill_ref.py:103-104)
+//   dV     = U - W S                                         (:117-118)
+//   O      = diag(m) [ scale diag(e^Lambda) Q S + P dV ],
+//            P[t,s] = scale (q_t.k_s) exp(Lambda_t - Lambda_s), s <= t   (:120-122)
+//   S     <- e^{Lambda_last} S + K^T diag(e^{Lambda_last - Lambda}) dV   (:124-126)
+//
+// The state is held TRANSPOSED in TMEM (S^T: value index = TMEM lane), so the
+// value tile is the M = 128 dimension of every state-path product.
+//
+// Warp roles (288 threads):
+//   warp 0      TMA producer: q/k chunk tiles (2-slot ring) and v tiles.
+//   warps 1-4   PREP warpgroup, one chunk ahead of the chain: gates and the
+//               in-chunk cumulative decay; [Q;K] K^T on tensor cores; P and N
+//               (TMEM -> registers); the 64x64 unit-lower-triangular inverse
+//               (16x16 diagonal blocks by substitution in registers, the
+//               off-diagonal blocks with warp-level bf16 MMAs on hi/lo-split
+//               operands); U^T = V^T (A diag beta')^T and
+//               W^T = K^T (A diag(beta' e^Lambda))^T on tensor cores; W^T to
+//               shared memory as a bf16 hi/lo pair.
+//   warps 5-8   CHAIN warpgroup, the sequential state recurrence:
+//               S^T -> bf16 hi/lo; dV^T = U^T - S^T W^T accumulated straight into
+//               U^T's TMEM (negated B operand) and (Q S)^T; then
+//               S^T = e^{Lambda_last} S^T + dV'^T K and (P dV)^T; the output
+//               tile is staged in shared memory and written by a TMA store.
+// Each warpgroup issues its own tcgen05.mma from one elected thread and
+// tracks completion with tcgen05.commit -> mbarrier.  fp32 values feeding the
+// state path (S, W, A diag beta', A diag beta' e^Lambda, dV') are split into
+// bf16 hi + lo pairs (~16 mantissa bits per product); q/k/v are exact bf16
+// inputs; the output path (Q S_hi, P dV) uses single bf16.
+// Decay ratios exp(Lambda_t - Lambda_s) are formed as u_t * w_s with
+// u_t = 2^(l_t - m), w_s = 2^(m - l_s) around the chunk's mid decay m (never
+// gamma_t / gamma_s); chunks whose total decay could overflow that product
+// fall back to one exp2 per element.  Every mbarrier wait is bounded; a
+// timeout raises a CTA-wide abort and all roles drain through their barriers.
 #include <mutex>
 
 #include "common.cuh"
@@ -38,43 +51,60 @@
 namespace gdn {
 namespace {
 
-constexpr int kC = 64;          // chunk length
-constexpr int kThreads = 128;   // 4 warps; warp w owns TMEM lanes 32w..32w+31
+constexpr int kC = 64;                 // chunk length
+constexpr int kThreads = 288;          // 9 warps
 constexpr int kTmemCols = 512;
 
-// TMEM column map (fp32 accumulators, 128 lanes)
-constexpr uint32_t COL_QKK = 0;    // 64 cols: lanes 0-63 Q K^T, lanes 64-127 K K^T
-constexpr uint32_t COL_SQK = 64;   // 128 cols: [0,64) (Q S)^T, [64,128) (K S)^T
-constexpr uint32_t COL_DV = 192;   // 64 cols: dV^T
-constexpr uint32_t COL_PDV = 256;  // 64 cols: (P dV)^T
-constexpr uint32_t COL_ST = 320;   // dk cols: S^T (fp32 state)
+// TMEM column map (fp32, 128 lanes)
+constexpr uint32_t COL_QKK = 0;        // prep: [Q;K] K^T (lanes 0-63 QK^T, 64-127 KK^T), then W^T
+constexpr uint32_t COL_UT = 64;        // 2 x 64: U^T for chunk parity 0/1, becomes dV^T in place
+constexpr uint32_t COL_QS = 192;       // (Q S_hi)^T
+constexpr uint32_t COL_PDV = 256;      // (P dV)^T
+constexpr uint32_t COL_ST = 320;       // S^T (fp32 state, dk columns)
+
+// named barriers
+constexpr int BAR_PREP = 1, BAR_CHAIN = 2;
 
 template <int DK>
 struct PrefillSmem {
     static constexpr int CB = DK / 64;                    // 64-wide column blocks of q/k
-    static constexpr int QK_BYTES = CB * 16384;           // [Q;K]: per block 128 rows x 128 B
-    static constexpr int V_BYTES = 2 * 8192;              // V: 2 blocks of 64 rows x 128 B
+    static constexpr int QK_BYTES = CB * 16384;           // slot: per block [Q 64 rows | K 64 rows] x 128 B
+    static constexpr int V_BYTES = 2 * 8192;              // 2 blocks of 64 rows x 128 B
     static constexpr int SR_BYTES = (2 * CB * 16384 > 49152) ? 2 * CB * 16384 : 49152;
-    // offsets (bytes from the 1024-aligned base)
     static constexpr int OFF_QK0 = 0;
     static constexpr int OFF_QK1 = OFF_QK0 + QK_BYTES;
-    static constexpr int OFF_V0 = OFF_QK1 + QK_BYTES;
-    static constexpr int OFF_V1 = OFF_V0 + V_BYTES;
-    static constexpr int OFF_SR = OFF_V1 + V_BYTES;       // S_hi | S_lo, later R / dV' / dVb
-    static constexpr int S_LO = CB * 16384;               // within SR
-    static constexpr int R_HI = 0, R_LO = 16384, DVB = 32768;  // within SR
-    static constexpr int OFF_P = OFF_SR + SR_BYTES;       // P [t][s] bf16, 8 KB
-    static constexpr int OFF_AH = OFF_P + 8192;           // A' hi [t][s]
-    static constexpr int OFF_AL = OFF_AH + 8192;          // A' lo
-    static constexpr int NLD = 65;                        // fp32 row stride of N / A
-    static constexpr int OFF_N = OFF_AL + 8192;           // N fp32 [64][65]
-    static constexpr int OFF_A = OFF_N + 64 * NLD * 4;    // A fp32 [64][65]
-    static constexpr int OFF_X = OFF_A + 64 * NLD * 4;    // X fp32 [16][48]
-    static constexpr int OFF_G = OFF_X + 16 * 48 * 4;     // gates: 5 x 64 fp32 + 2 totals
-    static constexpr int OFF_BAR = OFF_G + 6 * 64 * 4;    // 3 mbarriers + tmem base + flag
-    static constexpr int BYTES = OFF_BAR + 64;
-    static constexpr int ALLOC = BYTES + 1024;            // slack for 1024-B alignment
+    static constexpr int OFF_V = OFF_QK1 + QK_BYTES;
+    static constexpr int OFF_SR = OFF_V + V_BYTES;        // chain: S hi|lo; dV' hi|lo|dV bf16; o staging
+    static constexpr int S_LO = CB * 16384;
+    static constexpr int DVH = 0, DVL = 16384, DVB = 32768, OST = 0;
+    static constexpr int OFF_X = OFF_SR + SR_BYTES;       // prep A1 hi/lo, A2 hi/lo; then W^T hi/lo
+    static constexpr int X_A1H = 0, X_A1L = 8192, X_A2H = 16384, X_A2L = 24576;
+    static constexpr int X_WTH = 0, X_WTL = 16384;
+    static constexpr int OFF_P = OFF_X + 32768;           // P [2] x 8 KB
+    static constexpr int NLD = 68;                        // fp32 row stride of N (16 B aligned rows)
+    static constexpr int OFF_N = OFF_P + 16384;           // N; diagonal blocks replaced by D_i
+    static constexpr int AOLD = 20;                       // fp32 row stride of 16x16 scratch blocks
+    static constexpr int OFF_AO = OFF_N + 64 * NLD * 4;   // 6 off-diagonal blocks of A
+    static constexpr int OFF_XS = OFF_AO + 6 * 16 * AOLD * 4;   // 3 per-warp 16x16 scratch blocks
+    static constexpr int GSTRIDE = 9 * 64;                      // gate floats per parity slot
+    static constexpr int OFF_G = OFF_XS + 3 * 16 * AOLD * 4;    // gates [2] x 9 x 64 floats
+    static constexpr int OFF_BAR = OFF_G + 2 * GSTRIDE * 4;
+    static constexpr int BYTES = OFF_BAR + 256;
+    static constexpr int ALLOC = BYTES + 1024;
     static_assert(ALLOC <= 232448, "prefill shared memory exceeds 227 KB");
+};
+
+// per-chunk gate vectors (floats), 9 x 64 per parity slot
+enum {
+    G_LAM2 = 0,   // Lambda_t * log2(e)
+    G_U = 1,      // 2^(l_t - m)
+    G_W = 2,      // 2^(m - l_t)
+    G_EDEC = 3,   // exp(Lambda_last - Lambda_t)
+    G_BM = 4,     // beta_t * mask_t
+    G_BME = 5,    // beta_t * mask_t * exp(Lambda_t)
+    G_OC = 6,     // mask_t * scale * exp(Lambda_t)   (output coefficient of Q S)
+    G_MK = 7,     // mask_t (0 for padding)
+    G_TOT = 8     // [0,1] per-warp scan totals, [2] gamma_c, [3] direct-exp fallback flag
 };
 
 struct PrefillArgs {
@@ -87,10 +117,15 @@ struct PrefillArgs {
     const float* mask;
     const float* state_in;
     float* state_out;
-    uint16_t* out;
     unsigned int* err;
     int B, T, Hqk, Hv, dv, ntiles, layout;
     float scale;
+};
+
+struct Bars {
+    uint64_t qk_full[2], qk_free[2], v_full, v_free;
+    uint64_t qkk_done, uw_done, prep_done[2], chain_done[2];
+    uint64_t ws_done, st_done;
 };
 
 __device__ __forceinline__ void tmem_ld64(uint32_t taddr, float (&v)[64]) {
@@ -105,57 +140,147 @@ __device__ __forceinline__ void tmem_ld64(uint32_t taddr, float (&v)[64]) {
     }
 }
 
-// Write 64 fp32 values as one 128-byte row (64 bf16) of a 128B-swizzled
-// K-major tile, split into hi and lo tiles.
-__device__ __forceinline__ void store_row_split(uint8_t* hi_tile, uint8_t* lo_tile, int row,
-                                                const float (&v)[64]) {
+// 8 fp32 -> one 16-byte chunk of hi and of lo bf16
+__device__ __forceinline__ void split8(const float* v, uint4& h, uint4& l) {
+    split2_bf16(v[0], v[1], h.x, l.x);
+    split2_bf16(v[2], v[3], h.y, l.y);
+    split2_bf16(v[4], v[5], h.z, l.z);
+    split2_bf16(v[6], v[7], h.w, l.w);
+}
+__device__ __forceinline__ uint4 pack8(const float* v) {
+    return make_uint4(cvt_bf16x2(v[0], v[1]), cvt_bf16x2(v[2], v[3]), cvt_bf16x2(v[4], v[5]),
+                      cvt_bf16x2(v[6], v[7]));
+}
+// 64 fp32 -> one 128-byte row of a 128B-swizzled tile, bf16 hi and lo parts
+__device__ __forceinline__ void store_row_split(uint8_t* hi_tile, uint8_t* lo_tile, int row, const float (&v)[64]) {
 #pragma unroll
     for (int ch = 0; ch < 8; ++ch) {
-        uint32_t h[4], l[4];
-#pragma unroll
-        for (int p = 0; p < 4; ++p) {
-            uint16_t h0, l0, h1, l1;
-            split_bf16(v[8 * ch + 2 * p], h0, l0);
-            split_bf16(v[8 * ch + 2 * p + 1], h1, l1);
-            h[p] = static_cast<uint32_t>(h0) | (static_cast<uint32_t>(h1) << 16);
-            l[p] = static_cast<uint32_t>(l0) | (static_cast<uint32_t>(l1) << 16);
-        }
+        uint4 h, l;
+        split8(&v[8 * ch], h, l);
         const uint32_t off = sw128_chunk(row, ch);
-        *reinterpret_cast<uint4*>(hi_tile + off) = make_uint4(h[0], h[1], h[2], h[3]);
-        *reinterpret_cast<uint4*>(lo_tile + off) = make_uint4(l[0], l[1], l[2], l[3]);
+        *reinterpret_cast<uint4*>(hi_tile + off) = h;
+        *reinterpret_cast<uint4*>(lo_tile + off) = l;
     }
 }
-__device__ __forceinline__ void store_row_bf16(uint8_t* tile, int row, const float (&v)[64]) {
+
+// ---------------------------------------------------------------------------
+// 16x16 block product on one warp: acc (two 16x8 halves, C fragments) +=
+// L (16x16 fp32, row stride ldl) * R (16x16 fp32, row stride ldr), with both
+// operands split into bf16 hi + lo (3 MMAs per half: hi*hi + hi*lo + lo*hi).
+// ---------------------------------------------------------------------------
+__device__ __forceinline__ void blk_mma_acc(float (&acc)[2][4], const float* L, int ldl, const float* R, int ldr,
+                                            int lane) {
+    const int g = lane >> 2, t4 = lane & 3;
+    uint32_t ah[4], al[4];
+    {
+        const float2 v00 = *reinterpret_cast<const float2*>(L + g * ldl + 2 * t4);
+        const float2 v10 = *reinterpret_cast<const float2*>(L + (g + 8) * ldl + 2 * t4);
+        const float2 v01 = *reinterpret_cast<const float2*>(L + g * ldl + 2 * t4 + 8);
+        const float2 v11 = *reinterpret_cast<const float2*>(L + (g + 8) * ldl + 2 * t4 + 8);
+        split2_bf16(v00.x, v00.y, ah[0], al[0]);
+        split2_bf16(v10.x, v10.y, ah[1], al[1]);
+        split2_bf16(v01.x, v01.y, ah[2], al[2]);
+        split2_bf16(v11.x, v11.y, ah[3], al[3]);
+    }
 #pragma unroll
-    for (int ch = 0; ch < 8; ++ch) {
-        const uint32_t off = sw128_chunk(row, ch);
-        *reinterpret_cast<uint4*>(tile + off) =
-            make_uint4(pack_bf16x2(v[8 * ch], v[8 * ch + 1]), pack_bf16x2(v[8 * ch + 2], v[8 * ch + 3]),
-                       pack_bf16x2(v[8 * ch + 4], v[8 * ch + 5]), pack_bf16x2(v[8 * ch + 6], v[8 * ch + 7]));
+    for (int hn = 0; hn < 2; ++hn) {
+        const int n = 8 * hn + g;
+        uint32_t bh0, bl0, bh1, bl1;
+        split2_bf16(R[(2 * t4) * ldr + n], R[(2 * t4 + 1) * ldr + n], bh0, bl0);
+        split2_bf16(R[(2 * t4 + 8) * ldr + n], R[(2 * t4 + 9) * ldr + n], bh1, bl1);
+        mma_bf16_16816(acc[hn], ah, bh0, bh1);
+        mma_bf16_16816(acc[hn], ah, bl0, bl1);
+        mma_bf16_16816(acc[hn], al, bh0, bh1);
+    }
+}
+__device__ __forceinline__ void blk_store(float* dst, int ld, const float (&acc)[2][4], int lane) {
+    const int g = lane >> 2, t4 = lane & 3;
+#pragma unroll
+    for (int hn = 0; hn < 2; ++hn) {
+        *reinterpret_cast<float2*>(dst + g * ld + 8 * hn + 2 * t4) = make_float2(acc[hn][0], acc[hn][1]);
+        *reinterpret_cast<float2*>(dst + (g + 8) * ld + 8 * hn + 2 * t4) = make_float2(acc[hn][2], acc[hn][3]);
+    }
+}
+
+// slot of off-diagonal block (i, j), i > j, in the A scratch
+__device__ __forceinline__ int ao_slot(int i, int j) {
+    return (i - j == 1) ? j : (i - j == 2 ? 3 + j : 5);
+}
+
+// ---------------------------------------------------------------------------
+// A = (I - N)^-1 for the 64x64 strictly-lower N held in Nsm (row stride NLD),
+// by the 128 prep threads:
+//   1. warp w inverts the 16x16 diagonal block w by forward substitution in
+//      registers (row i of the block becomes final at step i and is broadcast
+//      by shuffles); D_w overwrites the diagonal block of Nsm;
+//   2. off-diagonal blocks by distance i - j = 1, 2, 3:
+//      A_ij = D_i * sum_{k=j}^{i-1} N_ik A_kj  (A_jj = D_j), warp-level MMAs.
+// ---------------------------------------------------------------------------
+template <int NLD, int AOLD>
+__device__ __forceinline__ void invert_unit_lower(float* Nsm, float* Ao, float* Xs, int pw, int lane) {
+    {
+        const int r = lane >> 1, hf = lane & 1;
+        const int row0 = 16 * pw;
+        float n[16], x[8];
+        const float4* nr = reinterpret_cast<const float4*>(Nsm + (row0 + r) * NLD + row0);
+#pragma unroll
+        for (int q = 0; q < 4; ++q) {
+            const float4 t4 = nr[q];
+            n[4 * q] = t4.x; n[4 * q + 1] = t4.y; n[4 * q + 2] = t4.z; n[4 * q + 3] = t4.w;
+        }
+#pragma unroll
+        for (int cc = 0; cc < 8; ++cc) x[cc] = (8 * hf + cc == r) ? 1.f : 0.f;
+#pragma unroll
+        for (int i = 0; i < 15; ++i) {
+            float bi[8];
+#pragma unroll
+            for (int cc = 0; cc < 8; ++cc) bi[cc] = __shfl_sync(0xffffffffu, x[cc], 2 * i + hf);
+            if (r > i) {
+#pragma unroll
+                for (int cc = 0; cc < 8; ++cc) x[cc] = fmaf(n[i], bi[cc], x[cc]);
+            }
+        }
+        __syncwarp();
+        float4* dst = reinterpret_cast<float4*>(Nsm + (row0 + r) * NLD + row0 + 8 * hf);
+        dst[0] = make_float4(x[0], x[1], x[2], x[3]);
+        dst[1] = make_float4(x[4], x[5], x[6], x[7]);
+    }
+    named_bar(BAR_PREP, 128);
+    float* xs = Xs + pw * 16 * AOLD;
+#pragma unroll 1
+    for (int dist = 1; dist < 4; ++dist) {
+        if (pw < 4 - dist) {
+            const int j = pw, i = pw + dist;
+            float acc[2][4] = {{0.f, 0.f, 0.f, 0.f}, {0.f, 0.f, 0.f, 0.f}};
+            // X = N_ij D_j + sum_{k=j+1}^{i-1} N_ik A_kj
+            blk_mma_acc(acc, Nsm + (16 * i) * NLD + 16 * j, NLD, Nsm + (16 * j) * NLD + 16 * j, NLD, lane);
+            for (int k = j + 1; k < i; ++k)
+                blk_mma_acc(acc, Nsm + (16 * i) * NLD + 16 * k, NLD, Ao + ao_slot(k, j) * 16 * AOLD, AOLD, lane);
+            blk_store(xs, AOLD, acc, lane);
+            __syncwarp();
+            float acc2[2][4] = {{0.f, 0.f, 0.f, 0.f}, {0.f, 0.f, 0.f, 0.f}};
+            blk_mma_acc(acc2, Nsm + (16 * i) * NLD + 16 * i, NLD, xs, AOLD, lane);
+            blk_store(Ao + ao_slot(i, j) * 16 * AOLD, AOLD, acc2, lane);
+        }
+        named_bar(BAR_PREP, 128);
     }
 }
 
 template <int DK>
 __global__ void __launch_bounds__(kThreads, 1)
 prefill_chunk_kernel(const __grid_constant__ CUtensorMap map_q, const __grid_constant__ CUtensorMap map_k,
-                     const __grid_constant__ CUtensorMap map_v, const PrefillArgs args) {
+                     const __grid_constant__ CUtensorMap map_v, const __grid_constant__ CUtensorMap map_o,
+                     const PrefillArgs args) {
     using L = PrefillSmem<DK>;
     extern __shared__ uint8_t smem_raw[];
     uint8_t* sm = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
-
-    float* g_lam = reinterpret_cast<float*>(sm + L::OFF_G);   // Lambda_t
-    float* g_elam = g_lam + 64;                               // exp(Lambda_t)
-    float* g_edec = g_lam + 128;                              // exp(Lambda_last - Lambda_t)
-    float* g_bm = g_lam + 192;                                // beta_t * mask_t
-    float* g_mk = g_lam + 256;                                // mask_t (0 for padding)
-    float* g_tot = g_lam + 320;                               // per-warp scan totals
-    uint64_t* bar_tma = reinterpret_cast<uint64_t*>(sm + L::OFF_BAR);   // [2]
-    uint64_t* bar_mma = bar_tma + 2;
-    uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bar_tma + 3);
+    Bars* bars = reinterpret_cast<Bars*>(sm + L::OFF_BAR);
+    uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(sm + L::OFF_BAR + sizeof(Bars));
     volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
     float* Nsm = reinterpret_cast<float*>(sm + L::OFF_N);
-    float* Asm = reinterpret_cast<float*>(sm + L::OFF_A);
-    float* Xsm = reinterpret_cast<float*>(sm + L::OFF_X);
+    float* Ao = reinterpret_cast<float*>(sm + L::OFF_AO);
+    float* Xs = reinterpret_cast<float*>(sm + L::OFF_XS);
+    float* gates = reinterpret_cast<float*>(sm + L::OFF_G);
 
     const int tid = threadIdx.x;
     const int warp = tid >> 5;
@@ -169,18 +294,18 @@ prefill_chunk_kernel(const __grid_constant__ CUtensorMap map_q, const __grid_con
     const int nchunks = (T + kC - 1) / kC;
     const int v0 = tile * 128;
     const int dv_valid = min(128, args.dv - v0);
-    const int nvb = (dv_valid + 63) / 64;          // 64-wide V column blocks in this tile
-    const uint32_t tma_bytes = static_cast<uint32_t>((2 * L::CB + nvb) * 8192);
+    const int nvb = (dv_valid + 63) / 64;
+    unsigned int* err = args.err;
 
     if (tid == 0) {
-        mbar_init(&bar_tma[0], 1);
-        mbar_init(&bar_tma[1], 1);
-        mbar_init(bar_mma, 1);
+        uint64_t* all = reinterpret_cast<uint64_t*>(bars);
+        for (int i = 0; i < static_cast<int>(sizeof(Bars) / 8); ++i) mbar_init(&all[i], 1);
         *abort_flag = 0;
         fence_mbar_init();
         tma_prefetch_desc(&map_q);
         tma_prefetch_desc(&map_k);
         tma_prefetch_desc(&map_v);
+        tma_prefetch_desc(&map_o);
     }
     if (warp == 0) {
         tmem_alloc(tmem_slot, kTmemCols);
@@ -190,360 +315,433 @@ prefill_chunk_kernel(const __grid_constant__ CUtensorMap map_q, const __grid_con
     __syncthreads();
     tc_fence_after();
     const uint32_t tmem = *tmem_slot;
-    const uint32_t lane_base = static_cast<uint32_t>(warp * 32) << 16;
-    auto taddr = [&](uint32_t col) { return tmem + lane_base + col; };
 
-    // ---- initial state -> TMEM (S^T: lane j = value column, column d = key index)
-    const long s_base = static_cast<long>(bh) * DK * args.dv + v0;
-    {
-        const int j = tid;
+    if (warp == 0) {
+        // ======================= TMA producer (lane 0: q/k ring, lane 1: v)
+        if (lane == 0) {
+            for (int c = 0; c < nchunks; ++c) {
+                const int slot = c & 1;
+                if (c >= 2 && !mbar_wait_or_abort(&bars->qk_free[slot], ((c >> 1) - 1) & 1, err, abort_flag)) break;
+                uint8_t* dst = sm + (slot ? L::OFF_QK1 : L::OFF_QK0);
+                mbar_arrive_expect_tx(&bars->qk_full[slot], 2 * L::CB * 8192);
+#pragma unroll
+                for (int cb = 0; cb < L::CB; ++cb) {
+                    tma_load_4d(dst + cb * 16384, &map_q, &bars->qk_full[slot], cb * 64, c * kC, hq, bidx);
+                    tma_load_4d(dst + cb * 16384 + 8192, &map_k, &bars->qk_full[slot], cb * 64, c * kC, hq, bidx);
+                }
+            }
+        } else if (lane == 1) {
+            for (int c = 0; c < nchunks; ++c) {
+                if (c >= 1 && !mbar_wait_or_abort(&bars->v_free, (c - 1) & 1, err, abort_flag)) break;
+                mbar_arrive_expect_tx(&bars->v_full, nvb * 8192);
+                for (int vb = 0; vb < nvb; ++vb)
+                    tma_load_4d(sm + L::OFF_V + vb * 8192, &map_v, &bars->v_full, v0 + vb * 64, c * kC, h, bidx);
+            }
+        }
+    } else if (warp <= 4) {
+        // ======================= PREP warpgroup
+        const int pt = tid - 32;                           // 0..127
+        const int pw = pt >> 5;                            // 0..3
+        const int tl = ((warp & 3) << 5) | lane;           // TMEM lane of this thread
+        const uint32_t lane_off = static_cast<uint32_t>(warp & 3) << 21;   // (32*(warp%4)) << 16
+        const bool leader = (pt == 0);
+        const float A_neg = -expf(args.A_log[h]);
+        const float dtb = args.dt_bias_vec ? args.dt_bias_vec[h] : args.dt_bias;
+        const float scale = args.scale;
+        const long gate_base = static_cast<long>(bh) * T;
+        constexpr float kLog2e = 1.4426950408889634f;
+        // gate inputs of the chunk being prepared, loaded one chunk ahead
+        float pa = 0.f, pb = 0.f, pm = 0.f;
+        auto load_gates = [&](int cc) {
+            const int tok = cc * kC + pt;
+            if (pt < kC && cc < nchunks && tok < T) {
+                pa = load_gate(args.a, gate_base + tok, args.gate_dtype);
+                pb = load_gate(args.b, gate_base + tok, args.gate_dtype);
+                pm = args.mask ? args.mask[static_cast<long>(bidx) * T + tok] : 1.f;
+            } else {
+                pa = 0.f;
+                pb = 0.f;
+                pm = 0.f;
+            }
+        };
+        load_gates(0);
+#pragma unroll 1
+        for (int c = 0; c < nchunks; ++c) {
+            const int par = c & 1;
+            float* g = gates + par * L::GSTRIDE;
+            if (c >= 2) mbar_wait_or_abort(&bars->chain_done[par], ((c >> 1) - 1) & 1, err, abort_flag);
+
+            // ---- gates (prefill_ref.py:49-64, 79-91): log decay, beta * mask, in-chunk cumsum
+            float lg = 0.f;
+            if (pt < kC) {
+                const int tok = c * kC + pt;
+                float bm = 0.f, mk = 0.f;
+                if (tok < T) {
+                    mk = pm;
+                    lg = A_neg * softplus_f(pa + dtb);
+                    bm = sigmoid_f(pb) * mk;
+                }
+                g[G_BM * 64 + pt] = bm;
+                g[G_MK * 64 + pt] = mk;
+#pragma unroll
+                for (int o = 1; o < 32; o <<= 1) {
+                    const float y = __shfl_up_sync(0xffffffffu, lg, o);
+                    if (lane >= o) lg += y;
+                }
+                if (lane == 31) g[G_TOT * 64 + pw] = lg;
+            }
+            load_gates(c + 1);                             // prefetch the next chunk's gate inputs
+            named_bar(BAR_PREP, 128);
+            const float lam_last = g[G_TOT * 64 + 0] + g[G_TOT * 64 + 1];
+            const float ll2 = lam_last * kLog2e;
+            const bool direct = ll2 < -240.f;              // u_t * w_s could overflow
+            if (pt < kC) {
+                const float lam = lg + (pw == 1 ? g[G_TOT * 64 + 0] : 0.f);
+                const float l2 = lam * kLog2e;
+                const float m2 = 0.5f * ll2;
+                const float el = ex2_approx(l2);
+                g[G_LAM2 * 64 + pt] = l2;
+                g[G_U * 64 + pt] = ex2_approx(l2 - m2);
+                g[G_W * 64 + pt] = ex2_approx(m2 - l2);
+                g[G_EDEC * 64 + pt] = ex2_approx(ll2 - l2);
+                g[G_BME * 64 + pt] = g[G_BM * 64 + pt] * el;
+                g[G_OC * 64 + pt] = g[G_MK * 64 + pt] * scale * el;
+                if (pt == 0) g[G_TOT * 64 + 2] = ex2_approx(ll2);
+            }
+
+            // ---- [Q;K] K^T on tensor cores
+            mbar_wait_or_abort(&bars->qk_full[par], (c >> 1) & 1, err, abort_flag);
+            uint8_t* qk_s = sm + (par ? L::OFF_QK1 : L::OFF_QK0);
+            if (leader && !*abort_flag) {
+                tc_fence_after();
+                const uint32_t sqk = smem_u32(qk_s);
+                constexpr uint32_t id64 = idesc_bf16(128, 64, false, false);
+#pragma unroll
+                for (int kk = 0; kk < DK / 16; ++kk) {
+                    const uint32_t o = (kk >> 2) * 16384 + (kk & 3) * 32;
+                    umma_bf16_ss(tmem + COL_QKK, sdesc_sw128(sqk + o, 16, 1024),
+                                 sdesc_sw128(sqk + o + 8192, 16, 1024), id64, kk > 0);
+                }
+                umma_commit(&bars->qkk_done);
+            }
+            named_bar(BAR_PREP, 128);      // gate vectors complete
+            mbar_wait_or_abort(&bars->qkk_done, c & 1, err, abort_flag);
+            tc_fence_after();
+
+            // ---- P (lanes 0-63) and N (lanes 64-127): only the lower triangle is computed
+            {
+                float row[64];
+                tmem_ld64(tmem + lane_off + COL_QKK, row);
+                const float* gw = g + G_W * 64;
+                const float* gl2 = g + G_LAM2 * 64;
+                if (tl < kC) {
+                    const int t = tl;
+                    const float coef = scale * g[G_MK * 64 + t];
+                    const float cu = coef * g[G_U * 64 + t];
+                    const float lt = gl2[t];
+                    uint8_t* prow = sm + L::OFF_P + par * 8192;
+#pragma unroll
+                    for (int ch = 0; ch < 8; ++ch) {
+                        uint4 w4 = make_uint4(0u, 0u, 0u, 0u);
+                        if (8 * ch <= t) {
+                            float e[8];
+#pragma unroll
+                            for (int u = 0; u < 8; ++u) {
+                                const int s = 8 * ch + u;
+                                const float dec = direct ? coef * ex2_approx(lt - gl2[s]) : cu * gw[s];
+                                e[u] = (s <= t) ? row[s] * dec : 0.f;
+                            }
+                            w4 = pack8(e);
+                        }
+                        *reinterpret_cast<uint4*>(prow + sw128_chunk(t, ch)) = w4;
+                    }
+                } else {
+                    const int t = tl - kC;
+                    const float coef = -g[G_BM * 64 + t];
+                    const float cu = coef * g[G_U * 64 + t];
+                    const float lt = gl2[t];
+                    float* nrow = Nsm + t * L::NLD;
+                    const int send = (t | 15) + 1;         // through the end of t's diagonal block
+#pragma unroll
+                    for (int s4 = 0; s4 < 16; ++s4) {
+                        if (4 * s4 < send) {
+                            float o4[4];
+#pragma unroll
+                            for (int u = 0; u < 4; ++u) {
+                                const int s = 4 * s4 + u;
+                                const float dec = direct ? coef * ex2_approx(lt - gl2[s]) : cu * gw[s];
+                                o4[u] = (s < t) ? row[s] * dec : 0.f;
+                            }
+                            *reinterpret_cast<float4*>(nrow + 4 * s4) = make_float4(o4[0], o4[1], o4[2], o4[3]);
+                        }
+                    }
+                }
+            }
+            tc_fence_before();
+            named_bar(BAR_PREP, 128);
+
+            // ---- A = (I - N)^-1
+            invert_unit_lower<L::NLD, L::AOLD>(Nsm, Ao, Xs, pw, lane);
+
+            // ---- A1 = A diag(beta'), A2 = A diag(beta' e^Lambda) -> X (hi/lo rows [t][s])
+            if (c >= 1) mbar_wait_or_abort(&bars->ws_done, (c - 1) & 1, err, abort_flag);
+            {
+                const int t = pt >> 1, hf = pt & 1;
+                const int ib = t >> 4, r = t & 15;
+                const float* bm = g + G_BM * 64;
+                const float* bme = g + G_BME * 64;
+                uint8_t* X = sm + L::OFF_X;
+#pragma unroll
+                for (int ch = 0; ch < 4; ++ch) {
+                    const int s0 = 32 * hf + 8 * ch;
+                    const uint32_t off = sw128_chunk(t, 4 * hf + ch);
+                    uint4 h1 = make_uint4(0u, 0u, 0u, 0u), l1 = h1, h2 = h1, l2 = h1;
+                    if (s0 <= t) {
+                        const int jb = s0 >> 4;
+                        const float* src = (jb == ib) ? Nsm + t * L::NLD + s0
+                                                      : Ao + ao_slot(ib, jb) * 16 * L::AOLD + r * L::AOLD + (s0 & 15);
+                        const float4 x0 = *reinterpret_cast<const float4*>(src);
+                        const float4 x1 = *reinterpret_cast<const float4*>(src + 4);
+                        const float xv[8] = {x0.x, x0.y, x0.z, x0.w, x1.x, x1.y, x1.z, x1.w};
+                        float e1[8], e2[8];
+#pragma unroll
+                        for (int u = 0; u < 8; ++u) {
+                            const float xa = (s0 + u <= t) ? xv[u] : 0.f;
+                            e1[u] = xa * bm[s0 + u];
+                            e2[u] = xa * bme[s0 + u];
+                        }
+                        split8(e1, h1, l1);
+                        split8(e2, h2, l2);
+                    }
+                    *reinterpret_cast<uint4*>(X + L::X_A1H + off) = h1;
+                    *reinterpret_cast<uint4*>(X + L::X_A1L + off) = l1;
+                    *reinterpret_cast<uint4*>(X + L::X_A2H + off) = h2;
+                    *reinterpret_cast<uint4*>(X + L::X_A2L + off) = l2;
+                }
+            }
+            fence_async_smem();
+            tc_fence_before();
+            named_bar(BAR_PREP, 128);
+
+            // ---- U^T = V^T A1^T  (into UT[par]),  W^T = K^T A2^T  (into COL_QKK)
+            if (leader) {
+                const bool okv = mbar_wait_or_abort(&bars->v_full, c & 1, err, abort_flag);
+                tc_fence_after();
+                if (okv && !*abort_flag) {
+                    const uint32_t sv = smem_u32(sm + L::OFF_V);
+                    const uint32_t sk = smem_u32(qk_s) + 8192;
+                    const uint32_t sx = smem_u32(sm + L::OFF_X);
+                    constexpr uint32_t id_mn = idesc_bf16(128, 64, true, false);
+#pragma unroll
+                    for (int p = 0; p < 2; ++p) {
+                        const uint32_t b1 = sx + (p ? L::X_A1L : L::X_A1H);
+#pragma unroll
+                        for (int kk = 0; kk < 4; ++kk)
+                            umma_bf16_ss(tmem + COL_UT + par * 64, sdesc_sw128(sv + kk * 2048, 8192, 1024),
+                                         sdesc_sw128(b1 + kk * 32, 16, 1024), id_mn, (p > 0 || kk > 0) ? 1u : 0u);
+                    }
+#pragma unroll
+                    for (int p = 0; p < 2; ++p) {
+                        const uint32_t b2 = sx + (p ? L::X_A2L : L::X_A2H);
+#pragma unroll
+                        for (int kk = 0; kk < 4; ++kk)
+                            umma_bf16_ss(tmem + COL_QKK, sdesc_sw128(sk + kk * 2048, 16384, 1024),
+                                         sdesc_sw128(b2 + kk * 32, 16, 1024), id_mn, (p > 0 || kk > 0) ? 1u : 0u);
+                    }
+                    umma_commit(&bars->uw_done);
+                    umma_commit(&bars->v_free);
+                }
+            }
+            mbar_wait_or_abort(&bars->uw_done, c & 1, err, abort_flag);
+            tc_fence_after();
+
+            // ---- W^T (lane d) -> X as MN-major B operand rows [d][t], hi/lo
+            {
+                float row[64];
+                tmem_ld64(tmem + lane_off + COL_QKK, row);
+                store_row_split(sm + L::OFF_X + L::X_WTH, sm + L::OFF_X + L::X_WTL, tl, row);
+            }
+            fence_async_smem();
+            tc_fence_before();
+            named_bar(BAR_PREP, 128);
+            if (leader) mbar_arrive(&bars->prep_done[par]);
+        }
+    } else {
+        // ======================= CHAIN warpgroup
+        const int ct = tid - 160;                          // 0..127
+        const int j = ((warp & 3) << 5) | lane;            // TMEM lane = value row j
+        const uint32_t lane_off = static_cast<uint32_t>(warp & 3) << 21;
+        const bool leader = (ct == 0);
+        const long s_base = static_cast<long>(bh) * DK * args.dv + v0;
+        uint8_t* sr = sm + L::OFF_SR;
+
+        // initial state -> TMEM (S^T: lane j = value column, column d = key index)
 #pragma unroll
         for (int blk = 0; blk < DK / 32; ++blk) {
             float vals[32];
 #pragma unroll
             for (int i = 0; i < 32; ++i) {
                 const int d = blk * 32 + i;
-                vals[i] = (args.state_in && j < dv_valid) ? args.state_in[s_base + static_cast<long>(d) * args.dv + j] : 0.f;
+                vals[i] = (args.state_in && j < dv_valid) ? args.state_in[s_base + static_cast<long>(d) * args.dv + j]
+                                                          : 0.f;
             }
-            tmem_st32(taddr(COL_ST + 32 * blk), vals);
+            tmem_st32(tmem + lane_off + COL_ST + 32 * blk, vals);
         }
         tmem_st_wait();
-    }
 
-    auto issue_tma = [&](int c, int buf) {
-        uint8_t* qk = sm + (buf ? L::OFF_QK1 : L::OFF_QK0);
-        uint8_t* vv = sm + (buf ? L::OFF_V1 : L::OFF_V0);
-        mbar_arrive_expect_tx(&bar_tma[buf], tma_bytes);
-#pragma unroll
-        for (int cb = 0; cb < L::CB; ++cb) {
-            tma_load_4d(qk + cb * 16384, &map_q, &bar_tma[buf], cb * 64, c * kC, hq, bidx);
-            tma_load_4d(qk + cb * 16384 + 8192, &map_k, &bar_tma[buf], cb * 64, c * kC, hq, bidx);
-        }
-        for (int vb = 0; vb < nvb; ++vb)
-            tma_load_4d(vv + vb * 8192, &map_v, &bar_tma[buf], v0 + vb * 64, c * kC, h, bidx);
-    };
-    if (tid == 0) issue_tma(0, 0);
+#pragma unroll 1
+        for (int c = 0; c < nchunks; ++c) {
+            const int par = c & 1;
+            const float* g = gates + par * L::GSTRIDE;
+            uint8_t* qk_s = sm + (par ? L::OFF_QK1 : L::OFF_QK0);
+            mbar_wait_or_abort(&bars->prep_done[par], (c >> 1) & 1, err, abort_flag);
+            const float gamma_c = g[G_TOT * 64 + 2];
+            if (leader) bulk_wait_read0();                 // previous output tile has left shared memory
+            named_bar(BAR_CHAIN, 128);
 
-    uint32_t tma_phase[2] = {0u, 0u};
-    uint32_t mma_phase = 0u;
-    const float A_neg = -expf(args.A_log[h]);
-    const float dtb = args.dt_bias_vec ? args.dt_bias_vec[h] : args.dt_bias;
-    const float scale = args.scale;
-    const long gate_base = static_cast<long>(bh) * T;
-
-    auto wait_mma = [&]() {
-        if (!mbar_wait(bar_mma, mma_phase, args.err)) *abort_flag = 1;
-        mma_phase ^= 1u;
-        tc_fence_after();
-    };
-
-    for (int c = 0; c < nchunks; ++c) {
-        const int buf = c & 1;
-        uint8_t* qk_s = sm + (buf ? L::OFF_QK1 : L::OFF_QK0);
-        uint8_t* v_s = sm + (buf ? L::OFF_V1 : L::OFF_V0);
-        uint8_t* sr = sm + L::OFF_SR;
-        if (tid == 0 && c + 1 < nchunks) issue_tma(c + 1, buf ^ 1);
-
-        // ---- (1) gates: log decay, beta * mask, in-chunk cumulative sum (prefill_ref.py:49-64,79-91)
-        float lg = 0.f;
-        if (tid < kC) {
-            const int tok = c * kC + tid;
-            float bm = 0.f, mk = 0.f;
-            if (tok < T) {
-                const float av = load_gate(args.a, gate_base + tok, args.gate_dtype);
-                const float bv = load_gate(args.b, gate_base + tok, args.gate_dtype);
-                mk = args.mask ? args.mask[static_cast<long>(bidx) * T + tok] : 1.f;
-                lg = A_neg * softplus_f(av + dtb);
-                bm = sigmoid_f(bv) * mk;
-            }
-            g_bm[tid] = bm;
-            g_mk[tid] = mk;
-#pragma unroll
-            for (int o = 1; o < 32; o <<= 1) {
-                const float y = __shfl_up_sync(0xffffffffu, lg, o);
-                if (lane >= o) lg += y;
-            }
-            if (lane == 31) g_tot[warp] = lg;
-        }
-        __syncthreads();
-        const float lam_last = g_tot[0] + g_tot[1];
-        if (tid < kC) {
-            const float lam = lg + (warp == 1 ? g_tot[0] : 0.f);
-            g_lam[tid] = lam;
-            g_elam[tid] = expf(lam);
-            g_edec[tid] = expf(lam_last - lam);
-        }
-        const float gamma_c = expf(lam_last);
-
-        // ---- (2) state S^T -> smem (bf16 hi/lo, K-major rows) and S^T *= gamma_c in TMEM
-        {
-            const int j = tid;
+            // ---- S^T -> bf16 hi/lo rows [j][d]; S^T *= gamma_c in TMEM
 #pragma unroll
             for (int blk = 0; blk < DK / 32; ++blk) {
                 float vals[32];
-                tmem_ld32(taddr(COL_ST + 32 * blk), vals);
+                tmem_ld32(tmem + lane_off + COL_ST + 32 * blk, vals);
                 tmem_ld_wait();
                 const int cb = blk >> 1;
 #pragma unroll
                 for (int ch4 = 0; ch4 < 4; ++ch4) {
-                    uint32_t hw[4], lw[4];
-#pragma unroll
-                    for (int p = 0; p < 4; ++p) {
-                        uint16_t h0, l0, h1, l1;
-                        split_bf16(vals[8 * ch4 + 2 * p], h0, l0);
-                        split_bf16(vals[8 * ch4 + 2 * p + 1], h1, l1);
-                        hw[p] = static_cast<uint32_t>(h0) | (static_cast<uint32_t>(h1) << 16);
-                        lw[p] = static_cast<uint32_t>(l0) | (static_cast<uint32_t>(l1) << 16);
-                    }
+                    uint4 hw, lw;
+                    split8(&vals[8 * ch4], hw, lw);
                     const uint32_t off = cb * 16384 + sw128_chunk(j, (blk & 1) * 4 + ch4);
-                    *reinterpret_cast<uint4*>(sr + off) = make_uint4(hw[0], hw[1], hw[2], hw[3]);
-                    *reinterpret_cast<uint4*>(sr + L::S_LO + off) = make_uint4(lw[0], lw[1], lw[2], lw[3]);
+                    *reinterpret_cast<uint4*>(sr + off) = hw;
+                    *reinterpret_cast<uint4*>(sr + L::S_LO + off) = lw;
                 }
 #pragma unroll
                 for (int i = 0; i < 32; ++i) vals[i] *= gamma_c;
-                tmem_st32(taddr(COL_ST + 32 * blk), vals);
+                tmem_st32(tmem + lane_off + COL_ST + 32 * blk, vals);
             }
             tmem_st_wait();
-        }
-        if (!mbar_wait(&bar_tma[buf], tma_phase[buf], args.err)) *abort_flag = 1;
-        tma_phase[buf] ^= 1u;
-        fence_async_smem();
-        tc_fence_before();
-        __syncthreads();
-        if (*abort_flag) break;
+            fence_async_smem();
+            tc_fence_before();
+            named_bar(BAR_CHAIN, 128);
 
-        // ---- (3) MMA: QKK = [Q;K] K^T ; SQK = S_hi^T [Q;K]^T ; SQK[:,64:] += S_lo^T K^T
-        if (tid == 0) {
+            // ---- dV^T = U^T - S^T W^T (3 split terms, negated B, in place in UT[par]); (Q S_hi)^T
+            if (leader && !*abort_flag) {
+                tc_fence_after();
+                const uint32_t ssr = smem_u32(sr);
+                const uint32_t swt = smem_u32(sm + L::OFF_X);
+                const uint32_t sqk = smem_u32(qk_s);
+                constexpr uint32_t id_ws = idesc_bf16(128, 64, false, true) | (1u << 14);   // negate B
+                constexpr uint32_t id64 = idesc_bf16(128, 64, false, false);
+#pragma unroll
+                for (int p = 0; p < 3; ++p) {
+                    const uint32_t sa = ssr + (p == 1 ? L::S_LO : 0);
+                    const uint32_t sb = swt + (p == 2 ? L::X_WTL : L::X_WTH);
+#pragma unroll
+                    for (int kk = 0; kk < DK / 16; ++kk)
+                        umma_bf16_ss(tmem + COL_UT + par * 64,
+                                     sdesc_sw128(sa + (kk >> 2) * 16384 + (kk & 3) * 32, 16, 1024),
+                                     sdesc_sw128(sb + kk * 2048, 16, 1024), id_ws, 1u);
+                }
+#pragma unroll
+                for (int kk = 0; kk < DK / 16; ++kk) {
+                    const uint32_t o = (kk >> 2) * 16384 + (kk & 3) * 32;
+                    umma_bf16_ss(tmem + COL_QS, sdesc_sw128(ssr + o, 16, 1024), sdesc_sw128(sqk + o, 16, 1024),
+                                 id64, kk > 0);
+                }
+                umma_commit(&bars->ws_done);
+            }
+            mbar_wait_or_abort(&bars->ws_done, c & 1, err, abort_flag);
             tc_fence_after();
-            const uint32_t sqk = smem_u32(qk_s);
-            const uint32_t ssr = smem_u32(sr);
-            constexpr uint32_t id64 = idesc_bf16(128, 64, false, false);
-            constexpr uint32_t id128 = idesc_bf16(128, 128, false, false);
-#pragma unroll
-            for (int kk = 0; kk < DK / 16; ++kk) {
-                const uint32_t o = (kk >> 2) * 16384 + (kk & 3) * 32;
-                umma_bf16_ss(tmem + COL_QKK, sdesc_sw128(sqk + o, 16, 1024), sdesc_sw128(sqk + o + 8192, 16, 1024),
-                             id64, kk > 0);
-            }
-#pragma unroll
-            for (int kk = 0; kk < DK / 16; ++kk) {
-                const uint32_t o = (kk >> 2) * 16384 + (kk & 3) * 32;
-                umma_bf16_ss(tmem + COL_SQK, sdesc_sw128(ssr + o, 16, 1024), sdesc_sw128(sqk + o, 16, 1024),
-                             id128, kk > 0);
-            }
-#pragma unroll
-            for (int kk = 0; kk < DK / 16; ++kk) {
-                const uint32_t o = (kk >> 2) * 16384 + (kk & 3) * 32;
-                umma_bf16_ss(tmem + COL_SQK + 64, sdesc_sw128(ssr + L::S_LO + o, 16, 1024),
-                             sdesc_sw128(sqk + o + 8192, 16, 1024), id64, 1u);
-            }
-            umma_commit(bar_mma);
-        }
-        wait_mma();
 
-        // ---- (4) epilogue: P (warps 0-1), N (warps 2-3), R = V - e^Lambda (K S) (all)
-        {
-            float row[64];
-            tmem_ld64(taddr(COL_QKK), row);
-            if (tid < kC) {
-                const int t = tid;
-                const float lt = g_lam[t];
+            // ---- dV (bf16) and dV' = dV * exp(Lambda_last - Lambda) (hi/lo) -> rows [j][t]
+            {
+                float row[64];
+                tmem_ld64(tmem + lane_off + COL_UT + par * 64, row);
+                const float* edec = g + G_EDEC * 64;
 #pragma unroll
-                for (int s = 0; s < 64; ++s) row[s] = (s <= t) ? scale * row[s] * expf(lt - g_lam[s]) : 0.f;
-                store_row_bf16(sm + L::OFF_P, t, row);
-            } else {
-                const int t = tid - kC;
-                const float lt = g_lam[t];
-                const float bt = -g_bm[t];
+                for (int ch = 0; ch < 8; ++ch) {
+                    const uint32_t off = sw128_chunk(j, ch);
+                    *reinterpret_cast<uint4*>(sr + L::DVB + off) = pack8(&row[8 * ch]);
+                    float e[8];
 #pragma unroll
-                for (int s = 0; s < 64; ++s) Nsm[t * L::NLD + s] = (s < t) ? bt * row[s] * expf(lt - g_lam[s]) : 0.f;
+                    for (int u = 0; u < 8; ++u) e[u] = row[8 * ch + u] * edec[8 * ch + u];
+                    uint4 hw, lw;
+                    split8(e, hw, lw);
+                    *reinterpret_cast<uint4*>(sr + L::DVH + off) = hw;
+                    *reinterpret_cast<uint4*>(sr + L::DVL + off) = lw;
+                }
             }
-            tmem_ld64(taddr(COL_SQK + 64), row);   // (K S)^T[j][t]
-            const int j = tid;
-            if (j < dv_valid) {
-                const uint8_t* vb = v_s + (j >> 6) * 8192;
+            fence_async_smem();
+            tc_fence_before();
+            named_bar(BAR_CHAIN, 128);
+
+            // ---- S^T += dV'^T K (K as MN-major B);  (P dV)^T = dV^T P^T
+            if (leader && !*abort_flag) {
+                tc_fence_after();
+                const uint32_t ssr = smem_u32(sr);
+                const uint32_t sk = smem_u32(qk_s) + 8192;
+                const uint32_t sp = smem_u32(sm + L::OFF_P + par * 8192);
+                constexpr uint32_t idst = idesc_bf16(128, DK, false, true);
+                constexpr uint32_t id64 = idesc_bf16(128, 64, false, false);
+#pragma unroll
+                for (int p = 0; p < 2; ++p) {
+                    const uint32_t ra = ssr + (p ? L::DVL : L::DVH);
+#pragma unroll
+                    for (int kk = 0; kk < 4; ++kk)
+                        umma_bf16_ss(tmem + COL_ST, sdesc_sw128(ra + kk * 32, 16, 1024),
+                                     sdesc_sw128(sk + kk * 2048, 16384, 1024), idst, 1u);
+                }
+#pragma unroll
+                for (int kk = 0; kk < 4; ++kk)
+                    umma_bf16_ss(tmem + COL_PDV, sdesc_sw128(ssr + L::DVB + kk * 32, 16, 1024),
+                                 sdesc_sw128(sp + kk * 32, 16, 1024), id64, kk > 0);
+                umma_commit(&bars->st_done);
+                umma_commit(&bars->qk_free[par]);
+            }
+            mbar_wait_or_abort(&bars->st_done, c & 1, err, abort_flag);
+            tc_fence_after();
+
+            // ---- output tile o[t, j] = oc_t (Q S)[t,j] + (P dV)[t,j] -> smem [t][j] -> TMA store
+            {
+                float qs[64], pd[64];
+                tmem_ld64(tmem + lane_off + COL_QS, qs);
+                tmem_ld64(tmem + lane_off + COL_PDV, pd);
+                const float* oc = g + G_OC * 64;
+                uint8_t* ob = sr + L::OST + (j >> 6) * 8192;
                 const uint32_t jj = j & 63;
 #pragma unroll
-                for (int t = 0; t < 64; ++t) {
-                    const float vt = bf16_bits_to_f32(*reinterpret_cast<const uint16_t*>(vb + sw128_off(t, jj)));
-                    row[t] = vt - g_elam[t] * row[t];
+                for (int t = 0; t < kC; ++t)
+                    *reinterpret_cast<uint16_t*>(ob + sw128_off(t, jj)) = f32_to_bf16_bits(fmaf(oc[t], qs[t], pd[t]));
+            }
+            fence_async_smem();
+            tc_fence_before();
+            named_bar(BAR_CHAIN, 128);
+            if (leader) {
+                if (!*abort_flag) {
+                    for (int vb = 0; vb < nvb; ++vb)
+                        tma_store_4d(&map_o, sr + L::OST + vb * 8192, v0 + vb * 64, c * kC, h, bidx);
+                    bulk_commit();
                 }
-            } else {
-#pragma unroll
-                for (int t = 0; t < 64; ++t) row[t] = 0.f;
+                mbar_arrive(&bars->chain_done[par]);
             }
-            store_row_split(sr + L::R_HI, sr + L::R_LO, j, row);
         }
-        __syncthreads();
-        if (*abort_flag) break;
+        if (leader) bulk_wait_all0();
 
-        // ---- (5) A = (I - N)^-1: 16x16 diagonal blocks by forward substitution (warp w -> block w)
-        {
-            const int r = lane >> 1, hf = lane & 1;
-            const int row0 = 16 * warp;
-            float n[16], x[8];
+        // ---- final state S^T -> state_out [dk][dv]
+        if (!*abort_flag && args.state_out) {
 #pragma unroll
-            for (int s = 0; s < 16; ++s) n[s] = Nsm[(row0 + r) * L::NLD + row0 + s];
+            for (int blk = 0; blk < DK / 32; ++blk) {
+                float vals[32];
+                tmem_ld32(tmem + lane_off + COL_ST + 32 * blk, vals);
+                tmem_ld_wait();
+                if (j < dv_valid) {
 #pragma unroll
-            for (int cc = 0; cc < 8; ++cc) x[cc] = (8 * hf + cc == r) ? 1.f : 0.f;
-#pragma unroll
-            for (int i = 0; i < 15; ++i) {
-                float bi[8];
-#pragma unroll
-                for (int cc = 0; cc < 8; ++cc) bi[cc] = __shfl_sync(0xffffffffu, x[cc], 2 * i + hf);
-                if (r > i) {
-#pragma unroll
-                    for (int cc = 0; cc < 8; ++cc) x[cc] += n[i] * bi[cc];
+                    for (int i = 0; i < 32; ++i)
+                        args.state_out[s_base + static_cast<long>(blk * 32 + i) * args.dv + j] = vals[i];
                 }
-            }
-#pragma unroll
-            for (int cc = 0; cc < 8; ++cc) Asm[(row0 + r) * L::NLD + row0 + 8 * hf + cc] = x[cc];
-        }
-        __syncthreads();
-        // off-diagonal blocks, row block by row block: A_ij = D_i sum_{k=j}^{i-1} N_ik A_kj
-        for (int ib = 1; ib < 4; ++ib) {
-            const int ncol = 16 * ib;
-            for (int e = tid; e < 16 * ncol; e += kThreads) {
-                const int rr = e / ncol, cc = e % ncol;
-                const float* nrow = Nsm + (16 * ib + rr) * L::NLD;
-                float acc = 0.f;
-                for (int s = cc; s < ncol; ++s) acc += nrow[s] * Asm[s * L::NLD + cc];
-                Xsm[rr * 48 + cc] = acc;
-            }
-            __syncthreads();
-            for (int e = tid; e < 16 * ncol; e += kThreads) {
-                const int rr = e / ncol, cc = e % ncol;
-                const float* drow = Asm + (16 * ib + rr) * L::NLD + 16 * ib;
-                float acc = 0.f;
-                for (int u = 0; u <= rr; ++u) acc += drow[u] * Xsm[u * 48 + cc];
-                Asm[(16 * ib + rr) * L::NLD + cc] = acc;
-            }
-            __syncthreads();
-        }
-        // A' = A diag(beta') -> split bf16 rows [t][s] (B operand of dV^T = R^T A'^T)
-        {
-            const int t = tid >> 1, hf = tid & 1;
-            const float* arow = Asm + t * L::NLD;
-#pragma unroll
-            for (int ch = 0; ch < 4; ++ch) {
-                uint32_t hw[4], lw[4];
-#pragma unroll
-                for (int p = 0; p < 4; ++p) {
-                    const int s0 = 32 * hf + 8 * ch + 2 * p;
-                    const float a0 = (s0 <= t) ? arow[s0] * g_bm[s0] : 0.f;
-                    const float a1 = (s0 + 1 <= t) ? arow[s0 + 1] * g_bm[s0 + 1] : 0.f;
-                    uint16_t h0, l0, h1, l1;
-                    split_bf16(a0, h0, l0);
-                    split_bf16(a1, h1, l1);
-                    hw[p] = static_cast<uint32_t>(h0) | (static_cast<uint32_t>(h1) << 16);
-                    lw[p] = static_cast<uint32_t>(l0) | (static_cast<uint32_t>(l1) << 16);
-                }
-                const uint32_t off = sw128_chunk(t, 4 * hf + ch);
-                *reinterpret_cast<uint4*>(sm + L::OFF_AH + off) = make_uint4(hw[0], hw[1], hw[2], hw[3]);
-                *reinterpret_cast<uint4*>(sm + L::OFF_AL + off) = make_uint4(lw[0], lw[1], lw[2], lw[3]);
-            }
-        }
-        fence_async_smem();
-        tc_fence_before();
-        __syncthreads();
-
-        // ---- (6) MMA: DV = R_hi A'_hi + R_lo A'_hi + R_hi A'_lo   (dV^T, M=128 N=64 K=64)
-        if (tid == 0) {
-            tc_fence_after();
-            const uint32_t ssr = smem_u32(sr);
-            const uint32_t sah = smem_u32(sm + L::OFF_AH), sal = smem_u32(sm + L::OFF_AL);
-            constexpr uint32_t id64 = idesc_bf16(128, 64, false, false);
-#pragma unroll
-            for (int p = 0; p < 3; ++p) {
-                const uint32_t ra = ssr + (p == 1 ? L::R_LO : L::R_HI);
-                const uint32_t rb = (p == 2) ? sal : sah;
-#pragma unroll
-                for (int kk = 0; kk < 4; ++kk)
-                    umma_bf16_ss(tmem + COL_DV, sdesc_sw128(ra + kk * 32, 16, 1024), sdesc_sw128(rb + kk * 32, 16, 1024),
-                                 id64, (p > 0 || kk > 0) ? 1u : 0u);
-            }
-            umma_commit(bar_mma);
-        }
-        wait_mma();
-
-        // ---- (7) dV' = dV * exp(Lambda_last - Lambda) (split) and dV (bf16) -> smem rows [j][t]
-        {
-            float row[64];
-            tmem_ld64(taddr(COL_DV), row);
-            store_row_bf16(sr + L::DVB, tid, row);
-#pragma unroll
-            for (int t = 0; t < 64; ++t) row[t] *= g_edec[t];
-            store_row_split(sr + L::R_HI, sr + L::R_LO, tid, row);
-        }
-        fence_async_smem();
-        tc_fence_before();
-        __syncthreads();
-        if (*abort_flag) break;
-
-        // ---- (8) MMA: ST += dV'_hi K + dV'_lo K (K as MN-major B) ; PDV = dV^T P^T
-        if (tid == 0) {
-            tc_fence_after();
-            const uint32_t ssr = smem_u32(sr);
-            const uint32_t sk = smem_u32(qk_s) + 8192;
-            constexpr uint32_t idst = idesc_bf16(128, DK, false, true);
-            constexpr uint32_t id64 = idesc_bf16(128, 64, false, false);
-#pragma unroll
-            for (int p = 0; p < 2; ++p) {
-                const uint32_t ra = ssr + (p ? L::R_LO : L::R_HI);
-#pragma unroll
-                for (int kk = 0; kk < 4; ++kk)
-                    umma_bf16_ss(tmem + COL_ST, sdesc_sw128(ra + kk * 32, 16, 1024),
-                                 sdesc_sw128(sk + kk * 2048, 16384, 1024), idst, 1u);
-            }
-            const uint32_t sp = smem_u32(sm + L::OFF_P);
-#pragma unroll
-            for (int kk = 0; kk < 4; ++kk)
-                umma_bf16_ss(tmem + COL_PDV, sdesc_sw128(ssr + L::DVB + kk * 32, 16, 1024),
-                             sdesc_sw128(sp + kk * 32, 16, 1024), id64, kk > 0);
-            umma_commit(bar_mma);
-        }
-        wait_mma();
-
-        // ---- (9) output o[t, j] = mask_t (scale e^Lambda_t (Q S)[t,j] + (P dV)[t,j])
-        {
-            float qs[64], pd[64];
-            tmem_ld64(taddr(COL_SQK), qs);
-            tmem_ld64(taddr(COL_PDV), pd);
-            const int j = tid;
-            if (j < dv_valid) {
-                const int tmax = min(kC, T - c * kC);
-                const long tok0 = static_cast<long>(c) * kC;
-                const long ostep = (args.layout == GDN_LAYOUT_BHTD) ? args.dv : static_cast<long>(args.Hv) * args.dv;
-                uint16_t* obase = args.out + ((args.layout == GDN_LAYOUT_BHTD)
-                                                  ? (static_cast<long>(bh) * T + tok0) * args.dv
-                                                  : ((static_cast<long>(bidx) * T + tok0) * args.Hv + h) * args.dv) +
-                                  v0 + j;
-#pragma unroll
-                for (int t = 0; t < kC; ++t) {
-                    if (t < tmax) obase[t * ostep] = f32_to_bf16_bits(g_mk[t] * (scale * g_elam[t] * qs[t] + pd[t]));
-                }
-            }
-        }
-        tc_fence_before();
-        __syncthreads();
-        if (*abort_flag) break;
-    }
-
-    // ---- final state S^T (TMEM) -> state_out [dk][dv]
-    if (!*abort_flag && args.state_out) {
-        const int j = tid;
-#pragma unroll
-        for (int blk = 0; blk < DK / 32; ++blk) {
-            float vals[32];
-            tmem_ld32(taddr(COL_ST + 32 * blk), vals);
-            tmem_ld_wait();
-            if (j < dv_valid) {
-#pragma unroll
-                for (int i = 0; i < 32; ++i)
-                    args.state_out[s_base + static_cast<long>(blk * 32 + i) * args.dv + j] = vals[i];
             }
         }
     }
+
     tc_fence_before();
     __syncthreads();
     if (warp == 0) tmem_dealloc(tmem, kTmemCols);
@@ -553,8 +751,8 @@ std::once_flag g_attr_once[2][64];
 int g_attr_status[2][64];
 
 template <int DK>
-int launch_prefill(const CUtensorMap& mq, const CUtensorMap& mk, const CUtensorMap& mv, const PrefillArgs& args,
-                   int grid, cudaStream_t st) {
+int launch_prefill(const CUtensorMap& mq, const CUtensorMap& mk, const CUtensorMap& mv, const CUtensorMap& mo,
+                   const PrefillArgs& args, int grid, cudaStream_t st) {
     using L = PrefillSmem<DK>;
     int dev = 0;
     cudaGetDevice(&dev);
@@ -566,11 +764,11 @@ int launch_prefill(const CUtensorMap& mq, const CUtensorMap& mk, const CUtensorM
     });
     if (g_attr_status[which][dev & 63] != GDN_OK)
         return fail(GDN_ERR_CUDA, "gdn_prefill_fwd: cannot grant %d B of shared memory", L::ALLOC);
-    prefill_chunk_kernel<DK><<<grid, kThreads, L::ALLOC, st>>>(mq, mk, mv, args);
+    prefill_chunk_kernel<DK><<<grid, kThreads, L::ALLOC, st>>>(mq, mk, mv, mo, args);
     return launch_status("gdn_prefill_fwd");
 }
 
-// q/k/v map: dims (D, T, H, B) innermost first, box (64, 64, 1, 1), 128B swizzle.
+// q/k/v/o map: dims (D, T, H, B) innermost first, box (64, 64, 1, 1), 128B swizzle.
 int make_act_map(CUtensorMap* m, const void* base, int D, int T, int H, int B, int layout) {
     uint64_t dims[4] = {static_cast<uint64_t>(D), static_cast<uint64_t>(T), static_cast<uint64_t>(H),
                         static_cast<uint64_t>(B)};
@@ -619,10 +817,11 @@ extern "C" int gdn_prefill_fwd(const void* q, const void* k, const void* v, cons
     if (st != GDN_OK) return st;
     if (scale == 0.f) scale = 1.f / sqrtf(static_cast<float>(dk));
 
-    CUtensorMap mq, mk, mv;
+    CUtensorMap mq, mk, mv, mo;
     if ((st = make_act_map(&mq, q, dk, T, Hqk, B, layout)) != GDN_OK) return st;
     if ((st = make_act_map(&mk, k, dk, T, Hqk, B, layout)) != GDN_OK) return st;
     if ((st = make_act_map(&mv, v, dv, T, Hv, B, layout)) != GDN_OK) return st;
+    if ((st = make_act_map(&mo, out, dv, T, Hv, B, layout)) != GDN_OK) return st;
 
     PrefillArgs args;
     args.a = a;
@@ -634,7 +833,6 @@ extern "C" int gdn_prefill_fwd(const void* q, const void* k, const void* v, cons
     args.mask = mask;
     args.state_in = state_in;
     args.state_out = state_out;
-    args.out = static_cast<uint16_t*>(out);
     args.err = device_error_word();
     args.B = B;
     args.T = T;
@@ -646,6 +844,6 @@ extern "C" int gdn_prefill_fwd(const void* q, const void* k, const void* v, cons
     args.scale = scale;
     const int grid = static_cast<int>(B * Hv * ntiles);
     cudaStream_t s = static_cast<cudaStream_t>(stream);
-    if (dk == 128) return launch_prefill<128>(mq, mk, mv, args, grid, s);
-    return launch_prefill<64>(mq, mk, mv, args, grid, s);
+    if (dk == 128) return launch_prefill<128>(mq, mk, mv, mo, args, grid, s);
+    return launch_prefill<64>(mq, mk, mv, mo, args, grid, s);
 }

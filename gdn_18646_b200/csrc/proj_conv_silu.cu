@@ -1,28 +1,334 @@
-// proj_conv_silu.cu -- fused input projection + causal depthwise conv1d + SiLU.
+// proj_conv_silu.cu -- fused input projection + causal depthwise conv1d (k=4) + SiLU
+// (+ optional per-head L2 norm), on tcgen05 tensor cores.
+//
+// Math: reference/fused_proj_conv_silu_ref.py:33-67 with its bf16 rounding
+// points (projection rounded to bf16, conv over bf16 values in fp32 rounded
+// to bf16, SiLU rounded to bf16).  Replaces fused_proj_conv_silu_kernel
+// (kernels/fused_proj_conv_silu.cu:105-295, WMMA + cp.async).
+//
+// The GEMM is computed TRANSPOSED: D[c, t] = sum_d W[c, d] x[t, d], with
+// 128 output channels on the TMEM lanes (MMA M = 128) and 256 consecutive
+// tokens on the TMEM columns (MMA N = 256).  Each epilogue thread therefore
+// owns one channel across 256 tokens and the causal conv along tokens is a
+// register-local sliding window.  A tile's GEMM rows start 3 tokens before
+// its first output token (TMA zero-fills negative token coordinates, which is
+// exactly the reference's causal zero padding), so each tile emits 253 tokens.
+//
+// Persistent, warp-specialised: warp 0 = TMA producer (W and x tiles, 128B
+// swizzle, 3-stage ring), warp 1 = MMA issuer (tcgen05.mma kind::f16, both
+// operands K-major), warps 2-5 = epilogue (TMEM -> conv/SiLU/L2 -> smem ->
+// TMA store).  Two TMEM accumulators (2 x 256 columns) let the epilogue of
+// tile i overlap the MMAs of tile i+1.
+#include <mutex>
+
 #include "common.cuh"
+#include "tensormap.h"
 
 namespace gdn {
+namespace {
+
+constexpr int PM = 128;               // channels per tile (MMA M)
+constexpr int PN = 256;               // token rows per tile (MMA N)
+constexpr int POUT = PN - 3;          // output tokens per tile
+constexpr int PK = 64;                // K per stage (one 128-byte swizzle atom of bf16)
+constexpr int PSTAGES = 3;
+constexpr int A_BYTES = PM * PK * 2;  // 16 KB
+constexpr int B_BYTES = PN * PK * 2;  // 32 KB
+constexpr int STAGE_BYTES = A_BYTES + B_BYTES;
+constexpr int Y_SUB_BYTES = PN * 128; // one 64-channel output sub-tile: 256 rows x 128 B
+constexpr int OFF_Y = PSTAGES * STAGE_BYTES;
+constexpr int OFF_BAR = OFF_Y + 2 * Y_SUB_BYTES;
+constexpr int PROJ_SMEM = OFF_BAR + 128 + 1024;
+static_assert(PROJ_SMEM <= 232448, "proj shared memory exceeds 227 KB");
+constexpr int kProjThreads = 192;     // 6 warps
+
+struct ProjArgs {
+    const uint16_t* conv_w;      // [Dout, 4]
+    const uint16_t* state_in;    // [B, Dout, 3] or null
+    uint16_t* state_out;         // [B, Dout, 3] or null
+    unsigned int* err;
+    int B, T, D, Dout;
+    int n_ct, n_tt, ntiles;
+    int l2;                      // 0 or group size
+};
+
+__device__ __forceinline__ float bf16r(float x) { return bf16_bits_to_f32(f32_to_bf16_bits(x)); }
+
+__global__ void __launch_bounds__(kProjThreads, 1)
+proj_conv_silu_kernel(const __grid_constant__ CUtensorMap map_w, const __grid_constant__ CUtensorMap map_x,
+                      const __grid_constant__ CUtensorMap map_y, const ProjArgs args) {
+    extern __shared__ uint8_t smem_raw[];
+    uint8_t* sm = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+    uint64_t* full = reinterpret_cast<uint64_t*>(sm + OFF_BAR);   // [PSTAGES]
+    uint64_t* empty = full + PSTAGES;                               // [PSTAGES]
+    uint64_t* acc_full = empty + PSTAGES;                           // [2]
+    uint64_t* acc_empty = acc_full + 2;                             // [2]
+    uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(acc_empty + 2);
+    volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
+    uint8_t* ysm = sm + OFF_Y;
+
+    const int tid = threadIdx.x;
+    const int warp = tid >> 5;
+    const int lane = tid & 31;
+    const int nk = args.D / PK;
+
+    if (tid == 0) {
+        for (int s = 0; s < PSTAGES; ++s) {
+            mbar_init(&full[s], 1);
+            mbar_init(&empty[s], 1);
+        }
+        for (int s = 0; s < 2; ++s) {
+            mbar_init(&acc_full[s], 1);
+            mbar_init(&acc_empty[s], 4);
+        }
+        *abort_flag = 0;
+        fence_mbar_init();
+        tma_prefetch_desc(&map_w);
+        tma_prefetch_desc(&map_x);
+        tma_prefetch_desc(&map_y);
+    }
+    if (warp == 1) {
+        tmem_alloc(tmem_slot, 512);
+        tmem_relinquish();
+    }
+    tc_fence_before();
+    __syncthreads();
+    tc_fence_after();
+    const uint32_t tmem = *tmem_slot;
+
+    if (warp == 0) {
+        // ---------------- TMA producer
+        if (lane == 0) {
+            int stage = 0;
+            uint32_t phase = 0;
+            for (int tile = blockIdx.x; tile < args.ntiles; tile += gridDim.x) {
+                const int ct = tile % args.n_ct;
+                const int rest = tile / args.n_ct;
+                const int tt = rest % args.n_tt;
+                const int b = rest / args.n_tt;
+                const int ts = tt * POUT - 3;
+                for (int kb = 0; kb < nk; ++kb) {
+                    if (!mbar_wait_or_abort(&empty[stage], phase ^ 1u, args.err, abort_flag)) break;
+                    uint8_t* st = sm + stage * STAGE_BYTES;
+                    mbar_arrive_expect_tx(&full[stage], STAGE_BYTES);
+                    tma_load_2d(st, &map_w, &full[stage], kb * PK, ct * PM);
+                    tma_load_3d(st + A_BYTES, &map_x, &full[stage], kb * PK, ts, b);
+                    if (++stage == PSTAGES) {
+                        stage = 0;
+                        phase ^= 1u;
+                    }
+                }
+                if (*abort_flag) break;
+            }
+        }
+    } else if (warp == 1) {
+        // ---------------- MMA issuer
+        if (lane == 0) {
+            int stage = 0;
+            uint32_t phase = 0;
+            int local = 0;
+            constexpr uint32_t idesc = idesc_bf16(PM, PN, false, false);
+            for (int tile = blockIdx.x; tile < args.ntiles; tile += gridDim.x, ++local) {
+                const int abuf = local & 1;
+                const uint32_t aphase = static_cast<uint32_t>(local >> 1) & 1u;
+                if (!mbar_wait_or_abort(&acc_empty[abuf], aphase ^ 1u, args.err, abort_flag)) break;
+                tc_fence_after();
+                const uint32_t d_tmem = tmem + abuf * PN;
+                for (int kb = 0; kb < nk; ++kb) {
+                    if (!mbar_wait_or_abort(&full[stage], phase, args.err, abort_flag)) break;
+                    tc_fence_after();
+                    const uint32_t sa = smem_u32(sm + stage * STAGE_BYTES);
+                    const uint32_t sb = sa + A_BYTES;
+#pragma unroll
+                    for (int k = 0; k < PK / 16; ++k)
+                        umma_bf16_ss(d_tmem, sdesc_sw128(sa + k * 32, 16, 1024), sdesc_sw128(sb + k * 32, 16, 1024),
+                                     idesc, (kb > 0 || k > 0) ? 1u : 0u);
+                    umma_commit(&empty[stage]);
+                    if (++stage == PSTAGES) {
+                        stage = 0;
+                        phase ^= 1u;
+                    }
+                }
+                if (*abort_flag) break;
+                umma_commit(&acc_full[abuf]);
+            }
+        }
+    } else {
+        // ---------------- epilogue: 4 warps, TMEM lanes 32*(warp%4) .. +31
+        const int quad = warp & 3;
+        const int cl = quad * 32 + lane;            // channel within the tile (= TMEM lane)
+        const int et = tid - 64;                    // 0..127
+        const uint32_t lane_off = static_cast<uint32_t>(quad * 32) << 16;
+        int local = 0;
+        for (int tile = blockIdx.x; tile < args.ntiles; tile += gridDim.x, ++local) {
+            const int ct = tile % args.n_ct;
+            const int rest = tile / args.n_ct;
+            const int tt = rest % args.n_tt;
+            const int b = rest / args.n_tt;
+            const int t0 = tt * POUT;
+            const int ts = t0 - 3;
+            const int c = ct * PM + cl;
+            const int abuf = local & 1;
+            const uint32_t aphase = static_cast<uint32_t>(local >> 1) & 1u;
+
+            // previous tile's TMA store must have finished reading the staging buffer
+            if (et == 0) bulk_wait_read0();
+            named_bar(1, 128);
+
+            const uint2 wraw = *reinterpret_cast<const uint2*>(args.conv_w + static_cast<long>(c) * 4);
+            const float w0 = bf16_bits_to_f32(wraw.x & 0xffffu), w1 = bf16_bits_to_f32(wraw.x >> 16);
+            const float w2 = bf16_bits_to_f32(wraw.y & 0xffffu), w3 = bf16_bits_to_f32(wraw.y >> 16);
+            const long sbase = (static_cast<long>(b) * args.Dout + c) * 3;
+
+            const bool ok = mbar_wait_or_abort(&acc_full[abuf], aphase, args.err, abort_flag);
+            tc_fence_after();
+            float p1 = 0.f, p2 = 0.f, p3 = 0.f;     // projections of tokens i-3, i-2, i-1
+            uint8_t* ysub = ysm + (cl >> 6) * Y_SUB_BYTES;
+            const uint32_t ccol = cl & 63;
+#pragma unroll 1
+            for (int blk = 0; blk < PN / 32; ++blk) {
+                float acc[32];
+                tmem_ld32(tmem + lane_off + abuf * PN + blk * 32, acc);
+                tmem_ld_wait();
+#pragma unroll
+                for (int u = 0; u < 32; ++u) {
+                    const int i = blk * 32 + u;
+                    const int tok = ts + i;
+                    float p = bf16r(acc[u]);
+                    if (tok < 0) p = args.state_in ? bf16_bits_to_f32(args.state_in[sbase + (tok + 3)]) : 0.f;
+                    if (args.state_out && tok < args.T && tok >= args.T - 3 && (i >= 3 || tt == 0))
+                        args.state_out[sbase + (tok - (args.T - 3))] = f32_to_bf16_bits(p);
+                    if (i >= 3) {
+                        float conv = p1 * w0;
+                        conv = fmaf(p2, w1, conv);
+                        conv = fmaf(p3, w2, conv);
+                        conv = fmaf(p, w3, conv);
+                        const float y = bf16r(silu_f(bf16r(conv)));
+                        *reinterpret_cast<uint16_t*>(ysub + sw128_off(i - 3, ccol)) = f32_to_bf16_bits(y);
+                    }
+                    p1 = p2;
+                    p2 = p3;
+                    p3 = p;
+                }
+            }
+            // accumulator buffer free for the MMA warp
+            tc_fence_before();
+            __syncwarp();
+            if (lane == 0) mbar_arrive(&acc_empty[abuf]);
+
+            if (args.l2) {
+                named_bar(1, 128);
+                const int g = args.l2;
+                for (int r = et; r < POUT; r += 128) {
+                    for (int g0 = 0; g0 < PM; g0 += g) {
+                        float ss = 0.f;
+                        for (int cc = g0; cc < g0 + g; ++cc) {
+                            const float y = bf16_bits_to_f32(*reinterpret_cast<const uint16_t*>(
+                                ysm + (cc >> 6) * Y_SUB_BYTES + sw128_off(r, cc & 63)));
+                            ss += y * y;
+                        }
+                        const float inv = 1.f / sqrtf(ss + 1e-6f);
+                        for (int cc = g0; cc < g0 + g; ++cc) {
+                            uint16_t* py = reinterpret_cast<uint16_t*>(ysm + (cc >> 6) * Y_SUB_BYTES + sw128_off(r, cc & 63));
+                            *py = f32_to_bf16_bits(bf16_bits_to_f32(*py) * inv);
+                        }
+                    }
+                }
+            }
+            fence_async_smem();
+            named_bar(1, 128);
+            if (et == 0 && ok && !*abort_flag) {
+                tma_store_3d(&map_y, ysm, ct * PM, t0, b);
+                tma_store_3d(&map_y, ysm + Y_SUB_BYTES, ct * PM + 64, t0, b);
+                bulk_commit();
+            }
+        }
+        if (et == 0) bulk_wait_all0();
+    }
+
+    tc_fence_before();
+    __syncthreads();
+    if (warp == 1) tmem_dealloc(tmem, 512);
+}
+
+std::once_flag g_proj_attr_once[64];
+int g_proj_attr_status[64];
+int g_sm_count[64];
+
+}  // namespace
+
 int check_proj_args(const void* x, const void* W, const void* conv_w, void* y, int B, int T, int D, int Dout,
                     const void* csi, const void* cso, int l2) {
     if (!x || !W || !conv_w || !y) return fail(GDN_ERR_NULL, "gdn_proj_conv_silu_fwd: x, W, conv_w and y are required");
     if (B <= 0 || T <= 0 || D <= 0 || Dout <= 0 || D % 64 != 0 || Dout % 128 != 0)
-        return fail(GDN_ERR_SHAPE, "gdn_proj_conv_silu_fwd: need B, T > 0, D %% 64 == 0 and Dout %% 128 == 0 (got B=%d T=%d D=%d Dout=%d)",
+        return fail(GDN_ERR_SHAPE,
+                    "gdn_proj_conv_silu_fwd: need B, T > 0, D %% 64 == 0 and Dout %% 128 == 0 (got B=%d T=%d D=%d Dout=%d)",
                     B, T, D, Dout);
-    if (l2 != 0 && (l2 < 8 || l2 > 256 || Dout % l2 != 0 || 128 % l2 != 0))
+    if (l2 != 0 && (l2 < 8 || l2 > 128 || Dout % l2 != 0 || 128 % l2 != 0))
         return fail(GDN_ERR_SHAPE, "gdn_proj_conv_silu_fwd: l2norm_group %d must divide 128 and Dout", l2);
     if (!aligned16(x) || !aligned16(W) || !aligned16(y) || (reinterpret_cast<uintptr_t>(conv_w) & 7u) ||
         (csi && (reinterpret_cast<uintptr_t>(csi) & 1u)) || (cso && (reinterpret_cast<uintptr_t>(cso) & 1u)))
         return fail(GDN_ERR_ALIGN, "gdn_proj_conv_silu_fwd: x, W, y must be 16-byte and conv_w 8-byte aligned");
     return GDN_OK;
 }
+
 }  // namespace gdn
 
 extern "C" int gdn_proj_conv_silu_fwd(const void* x, const void* W, const void* conv_w, void* y, int B, int T,
                                       int D, int Dout, const void* conv_state_in, void* conv_state_out,
                                       int l2norm_group, void* stream) {
     using namespace gdn;
-    (void)stream;
     int st = check_proj_args(x, W, conv_w, y, B, T, D, Dout, conv_state_in, conv_state_out, l2norm_group);
     if (st != GDN_OK) return st;
-    return fail(GDN_ERR_UNSUPPORTED, "gdn_proj_conv_silu_fwd: not built yet");
+    if ((st = check_sm100()) != GDN_OK) return st;
+    int dev = 0;
+    cudaGetDevice(&dev);
+    std::call_once(g_proj_attr_once[dev & 63], [dev]() {
+        g_proj_attr_status[dev & 63] =
+            cudaFuncSetAttribute(proj_conv_silu_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, PROJ_SMEM) ==
+                    cudaSuccess ? GDN_OK : GDN_ERR_CUDA;
+        int sms = 0;
+        cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+        g_sm_count[dev & 63] = sms > 0 ? sms : 148;
+    });
+    if (g_proj_attr_status[dev & 63] != GDN_OK)
+        return fail(GDN_ERR_CUDA, "gdn_proj_conv_silu_fwd: cannot grant %d B of shared memory", PROJ_SMEM);
+
+    CUtensorMap mw, mx, my;
+    {
+        uint64_t dims[2] = {static_cast<uint64_t>(D), static_cast<uint64_t>(Dout)};
+        uint64_t strides[1] = {static_cast<uint64_t>(D) * 2};
+        uint32_t box[2] = {PK, PM};
+        if ((st = make_map_bf16(&mw, W, 2, dims, strides, box, true)) != GDN_OK) return st;
+    }
+    {
+        uint64_t dims[3] = {static_cast<uint64_t>(D), static_cast<uint64_t>(T), static_cast<uint64_t>(B)};
+        uint64_t strides[2] = {static_cast<uint64_t>(D) * 2, static_cast<uint64_t>(D) * 2 * T};
+        uint32_t box[3] = {PK, PN, 1};
+        if ((st = make_map_bf16(&mx, x, 3, dims, strides, box, true)) != GDN_OK) return st;
+    }
+    {
+        uint64_t dims[3] = {static_cast<uint64_t>(Dout), static_cast<uint64_t>(T), static_cast<uint64_t>(B)};
+        uint64_t strides[2] = {static_cast<uint64_t>(Dout) * 2, static_cast<uint64_t>(Dout) * 2 * T};
+        uint32_t box[3] = {64, POUT, 1};
+        if ((st = make_map_bf16(&my, y, 3, dims, strides, box, true)) != GDN_OK) return st;
+    }
+    ProjArgs a;
+    a.conv_w = static_cast<const uint16_t*>(conv_w);
+    a.state_in = static_cast<const uint16_t*>(conv_state_in);
+    a.state_out = static_cast<uint16_t*>(conv_state_out);
+    a.err = device_error_word();
+    a.B = B;
+    a.T = T;
+    a.D = D;
+    a.Dout = Dout;
+    a.n_ct = Dout / PM;
+    a.n_tt = (T + POUT - 1) / POUT;
+    const long ntiles = static_cast<long>(a.n_ct) * a.n_tt * B;
+    if (ntiles > 0x7fffffffL) return fail(GDN_ERR_SHAPE, "gdn_proj_conv_silu_fwd: too many tiles");
+    a.ntiles = static_cast<int>(ntiles);
+    a.l2 = l2norm_group;
+    const int grid = static_cast<int>(ntiles < g_sm_count[dev & 63] ? ntiles : g_sm_count[dev & 63]);
+    proj_conv_silu_kernel<<<grid, kProjThreads, PROJ_SMEM, static_cast<cudaStream_t>(stream)>>>(mw, mx, my, a);
+    return launch_status("gdn_proj_conv_silu_fwd");
 }
