@@ -42,6 +42,9 @@ __device__ __forceinline__ float softplus_f(float x) {
 }
 __device__ __forceinline__ float sigmoid_f(float x) { return 1.f / (1.f + expf(-x)); }
 __device__ __forceinline__ float silu_f(float x) { return x / (1.f + expf(-x)); }
+// MUFU-based variants for per-token gate math (relative error ~1e-7)
+__device__ __forceinline__ float softplus_fast(float x) { return x > 20.f ? x : log1pf(__expf(x)); }
+__device__ __forceinline__ float sigmoid_fast(float x) { return __frcp_rn(1.f + __expf(-x)); }
 
 __device__ __forceinline__ float bf16_bits_to_f32(uint16_t b) {
     return __uint_as_float(static_cast<uint32_t>(b) << 16);

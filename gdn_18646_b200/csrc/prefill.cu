@@ -31,8 +31,10 @@
 //   warps 5-8   CHAIN warpgroup, the sequential state recurrence:
 //               S^T -> bf16 hi/lo; dV^T = U^T - S^T W^T accumulated straight into
 //               U^T's TMEM (negated B operand) and (Q S)^T; then
-//               S^T = e^{Lambda_last} S^T + dV'^T K and (P dV)^T; the output
-//               tile is staged in shared memory and written by a TMA store.
+//               S^T = e^{Lambda_last} S^T + dV'^T K and (P dV)^T.  W^T is
+//               split to shared memory by the chain (prep never waits on its
+//               U/W MMA), and chunk c's output tile is staged in shared memory
+//               and TMA-stored at the top of chunk c+1, while prep still runs.
 // Each warpgroup issues its own tcgen05.mma from one elected thread and
 // tracks completion with tcgen05.commit -> mbarrier.  fp32 values feeding the
 // state path (S, W, A diag beta', A diag beta' e^Lambda, dV') are split into
@@ -56,11 +58,12 @@ constexpr int kThreads = 288;          // 9 warps
 constexpr int kTmemCols = 512;
 
 // TMEM column map (fp32, 128 lanes)
-constexpr uint32_t COL_QKK = 0;        // prep: [Q;K] K^T (lanes 0-63 QK^T, 64-127 KK^T), then W^T
+constexpr uint32_t COL_QKK = 0;        // prep: [Q;K] K^T (lanes 0-63 QK^T, 64-127 KK^T)
 constexpr uint32_t COL_UT = 64;        // 2 x 64: U^T for chunk parity 0/1, becomes dV^T in place
 constexpr uint32_t COL_QS = 192;       // (Q S_hi)^T
 constexpr uint32_t COL_PDV = 256;      // (P dV)^T
 constexpr uint32_t COL_ST = 320;       // S^T (fp32 state, dk columns)
+constexpr uint32_t COL_WT = 448;       // W^T (lanes = key index d)
 
 // named barriers
 constexpr int BAR_PREP = 1, BAR_CHAIN = 2;
@@ -88,7 +91,8 @@ struct PrefillSmem {
     static constexpr int OFF_XS = OFF_AO + 6 * 16 * AOLD * 4;   // 3 per-warp 16x16 scratch blocks
     static constexpr int GSTRIDE = 9 * 64;                      // gate floats per parity slot
     static constexpr int OFF_G = OFF_XS + 3 * 16 * AOLD * 4;    // gates [2] x 9 x 64 floats
-    static constexpr int OFF_BAR = OFF_G + 2 * GSTRIDE * 4;
+    static constexpr int OFF_OC = OFF_G + 2 * GSTRIDE * 4;      // chain copy of G_OC [2] x 64
+    static constexpr int OFF_BAR = OFF_OC + 2 * 64 * 4;
     static constexpr int BYTES = OFF_BAR + 256;
     static constexpr int ALLOC = BYTES + 1024;
     static_assert(ALLOC <= 232448, "prefill shared memory exceeds 227 KB");
@@ -125,7 +129,7 @@ struct PrefillArgs {
 struct Bars {
     uint64_t qk_full[2], qk_free[2], v_full, v_free;
     uint64_t qkk_done, uw_done, prep_done[2], chain_done[2];
-    uint64_t ws_done, st_done;
+    uint64_t ws_done, st_done, wt_read;
 };
 
 __device__ __forceinline__ void tmem_ld64(uint32_t taddr, float (&v)[64]) {
@@ -206,15 +210,31 @@ __device__ __forceinline__ void blk_store(float* dst, int ld, const float (&acc)
 __device__ __forceinline__ int ao_slot(int i, int j) {
     return (i - j == 1) ? j : (i - j == 2 ? 3 + j : 5);
 }
+__device__ __forceinline__ void blk_load(float (&acc)[2][4], const float* src, int ld, int lane) {
+    const int g = lane >> 2, t4 = lane & 3;
+#pragma unroll
+    for (int hn = 0; hn < 2; ++hn) {
+        const float2 a = *reinterpret_cast<const float2*>(src + g * ld + 8 * hn + 2 * t4);
+        const float2 b = *reinterpret_cast<const float2*>(src + (g + 8) * ld + 8 * hn + 2 * t4);
+        acc[hn][0] = a.x;
+        acc[hn][1] = a.y;
+        acc[hn][2] = b.x;
+        acc[hn][3] = b.y;
+    }
+}
 
 // ---------------------------------------------------------------------------
 // A = (I - N)^-1 for the 64x64 strictly-lower N held in Nsm (row stride NLD),
-// by the 128 prep threads:
+// by the 128 prep threads (4 warps):
 //   1. warp w inverts the 16x16 diagonal block w by forward substitution in
 //      registers (row i of the block becomes final at step i and is broadcast
 //      by shuffles); D_w overwrites the diagonal block of Nsm;
-//   2. off-diagonal blocks by distance i - j = 1, 2, 3:
-//      A_ij = D_i * sum_{k=j}^{i-1} N_ik A_kj  (A_jj = D_j), warp-level MMAs.
+//   2. off-diagonal blocks, A_ij = D_i sum_{k=j}^{i-1} N_ik A_kj (A_jj = D_j),
+//      as warp-level MMAs on 16x16 blocks, with the D-only terms issued first:
+//        a) Y_{i,i-1} = N_{i,i-1} D_{i-1};  Z20 = N20 D0, Z31 = N31 D1, Z30 = N30 D0
+//        b) A_{i,i-1} = D_i Y_{i,i-1}
+//        c) A20 = D2 (Z20 + N21 A10);  A31 = D3 (Z31 + N32 A21);  W30 = Z30 + N31 A10
+//        d) A30 = D3 (W30 + N32 A20)
 // ---------------------------------------------------------------------------
 template <int NLD, int AOLD>
 __device__ __forceinline__ void invert_unit_lower(float* Nsm, float* Ao, float* Xs, int pw, int lane) {
@@ -246,24 +266,56 @@ __device__ __forceinline__ void invert_unit_lower(float* Nsm, float* Ao, float* 
         dst[1] = make_float4(x[4], x[5], x[6], x[7]);
     }
     named_bar(BAR_PREP, 128);
-    float* xs = Xs + pw * 16 * AOLD;
-#pragma unroll 1
-    for (int dist = 1; dist < 4; ++dist) {
-        if (pw < 4 - dist) {
-            const int j = pw, i = pw + dist;
-            float acc[2][4] = {{0.f, 0.f, 0.f, 0.f}, {0.f, 0.f, 0.f, 0.f}};
-            // X = N_ij D_j + sum_{k=j+1}^{i-1} N_ik A_kj
-            blk_mma_acc(acc, Nsm + (16 * i) * NLD + 16 * j, NLD, Nsm + (16 * j) * NLD + 16 * j, NLD, lane);
-            for (int k = j + 1; k < i; ++k)
-                blk_mma_acc(acc, Nsm + (16 * i) * NLD + 16 * k, NLD, Ao + ao_slot(k, j) * 16 * AOLD, AOLD, lane);
+    auto Nb = [&](int i, int j) { return Nsm + (16 * i) * NLD + 16 * j; };   // N_ij (i > j) or D_i (i == j)
+    auto Ab = [&](int i, int j) { return Ao + ao_slot(i, j) * 16 * AOLD; };
+    float* xs = Xs + (pw < 3 ? pw : 0) * 16 * AOLD;
+    // a) Y_{pw+1,pw} -> xs;  Z -> final slot of its block
+    if (pw < 3) {
+        float acc[2][4] = {{0.f, 0.f, 0.f, 0.f}, {0.f, 0.f, 0.f, 0.f}};
+        blk_mma_acc(acc, Nb(pw + 1, pw), NLD, Nb(pw, pw), NLD, lane);
+        blk_store(xs, AOLD, acc, lane);
+        const int zi = (pw == 2) ? 3 : pw + 2, zj = (pw == 2) ? 0 : pw;
+        float acz[2][4] = {{0.f, 0.f, 0.f, 0.f}, {0.f, 0.f, 0.f, 0.f}};
+        blk_mma_acc(acz, Nb(zi, zj), NLD, Nb(zj, zj), NLD, lane);
+        blk_store(Ab(zi, zj), AOLD, acz, lane);
+    }
+    __syncwarp();
+    // b) A_{pw+1,pw} = D_{pw+1} Y
+    if (pw < 3) {
+        float acc[2][4] = {{0.f, 0.f, 0.f, 0.f}, {0.f, 0.f, 0.f, 0.f}};
+        blk_mma_acc(acc, Nb(pw + 1, pw + 1), NLD, xs, AOLD, lane);
+        blk_store(Ab(pw + 1, pw), AOLD, acc, lane);
+    }
+    named_bar(BAR_PREP, 128);
+    // c) warp 0: A20, warp 1: A31, warp 2: W30 (partial sum of A30's X)
+    if (pw < 3) {
+        const int i = (pw == 2) ? 3 : pw + 2, j = (pw == 2) ? 0 : pw, k = (pw == 2) ? 1 : pw + 1;
+        float acc[2][4];
+        blk_load(acc, Ab(i, j), AOLD, lane);
+        blk_mma_acc(acc, Nb(i, k), NLD, Ab(k, j), AOLD, lane);
+        if (pw < 2) {
             blk_store(xs, AOLD, acc, lane);
             __syncwarp();
             float acc2[2][4] = {{0.f, 0.f, 0.f, 0.f}, {0.f, 0.f, 0.f, 0.f}};
-            blk_mma_acc(acc2, Nsm + (16 * i) * NLD + 16 * i, NLD, xs, AOLD, lane);
-            blk_store(Ao + ao_slot(i, j) * 16 * AOLD, AOLD, acc2, lane);
+            blk_mma_acc(acc2, Nb(i, i), NLD, xs, AOLD, lane);
+            blk_store(Ab(i, j), AOLD, acc2, lane);
+        } else {
+            blk_store(Ab(i, j), AOLD, acc, lane);
         }
-        named_bar(BAR_PREP, 128);
     }
+    named_bar(BAR_PREP, 128);
+    // d) A30 = D3 (W30 + N32 A20)
+    if (pw == 0) {
+        float acc[2][4];
+        blk_load(acc, Ab(3, 0), AOLD, lane);
+        blk_mma_acc(acc, Nb(3, 2), NLD, Ab(2, 0), AOLD, lane);
+        blk_store(xs, AOLD, acc, lane);
+        __syncwarp();
+        float acc2[2][4] = {{0.f, 0.f, 0.f, 0.f}, {0.f, 0.f, 0.f, 0.f}};
+        blk_mma_acc(acc2, Nb(3, 3), NLD, xs, AOLD, lane);
+        blk_store(Ab(3, 0), AOLD, acc2, lane);
+    }
+    named_bar(BAR_PREP, 128);
 }
 
 template <int DK>
@@ -281,6 +333,7 @@ prefill_chunk_kernel(const __grid_constant__ CUtensorMap map_q, const __grid_con
     float* Ao = reinterpret_cast<float*>(sm + L::OFF_AO);
     float* Xs = reinterpret_cast<float*>(sm + L::OFF_XS);
     float* gates = reinterpret_cast<float*>(sm + L::OFF_G);
+    float* ocbuf = reinterpret_cast<float*>(sm + L::OFF_OC);
 
     const int tid = threadIdx.x;
     const int warp = tid >> 5;
@@ -344,24 +397,28 @@ prefill_chunk_kernel(const __grid_constant__ CUtensorMap map_q, const __grid_con
         const int pw = pt >> 5;                            // 0..3
         const int tl = ((warp & 3) << 5) | lane;           // TMEM lane of this thread
         const uint32_t lane_off = static_cast<uint32_t>(warp & 3) << 21;   // (32*(warp%4)) << 16
-        const bool leader = (pt == 0);
+        const bool leader = (pt == 32);                    // MMA issuer: not on the gate warp (pw == 0)
         const float A_neg = -expf(args.A_log[h]);
         const float dtb = args.dt_bias_vec ? args.dt_bias_vec[h] : args.dt_bias;
         const float scale = args.scale;
         const long gate_base = static_cast<long>(bh) * T;
         constexpr float kLog2e = 1.4426950408889634f;
-        // gate inputs of the chunk being prepared, loaded one chunk ahead
-        float pa = 0.f, pb = 0.f, pm = 0.f;
+        // gate inputs (two tokens per lane of warp pw == 0), loaded one chunk ahead
+        float pa0 = 0.f, pa1 = 0.f, pb0 = 0.f, pb1 = 0.f, pm0 = 0.f, pm1 = 0.f;
         auto load_gates = [&](int cc) {
-            const int tok = cc * kC + pt;
-            if (pt < kC && cc < nchunks && tok < T) {
-                pa = load_gate(args.a, gate_base + tok, args.gate_dtype);
-                pb = load_gate(args.b, gate_base + tok, args.gate_dtype);
-                pm = args.mask ? args.mask[static_cast<long>(bidx) * T + tok] : 1.f;
-            } else {
-                pa = 0.f;
-                pb = 0.f;
-                pm = 0.f;
+            const int tok = cc * kC + 2 * lane;
+            pa0 = pa1 = pb0 = pb1 = pm0 = pm1 = 0.f;
+            if (pw == 0 && cc < nchunks) {
+                if (tok < T) {
+                    pa0 = load_gate(args.a, gate_base + tok, args.gate_dtype);
+                    pb0 = load_gate(args.b, gate_base + tok, args.gate_dtype);
+                    pm0 = args.mask ? args.mask[static_cast<long>(bidx) * T + tok] : 1.f;
+                }
+                if (tok + 1 < T) {
+                    pa1 = load_gate(args.a, gate_base + tok + 1, args.gate_dtype);
+                    pb1 = load_gate(args.b, gate_base + tok + 1, args.gate_dtype);
+                    pm1 = args.mask ? args.mask[static_cast<long>(bidx) * T + tok + 1] : 1.f;
+                }
             }
         };
         load_gates(0);
@@ -371,45 +428,7 @@ prefill_chunk_kernel(const __grid_constant__ CUtensorMap map_q, const __grid_con
             float* g = gates + par * L::GSTRIDE;
             if (c >= 2) mbar_wait_or_abort(&bars->chain_done[par], ((c >> 1) - 1) & 1, err, abort_flag);
 
-            // ---- gates (prefill_ref.py:49-64, 79-91): log decay, beta * mask, in-chunk cumsum
-            float lg = 0.f;
-            if (pt < kC) {
-                const int tok = c * kC + pt;
-                float bm = 0.f, mk = 0.f;
-                if (tok < T) {
-                    mk = pm;
-                    lg = A_neg * softplus_f(pa + dtb);
-                    bm = sigmoid_f(pb) * mk;
-                }
-                g[G_BM * 64 + pt] = bm;
-                g[G_MK * 64 + pt] = mk;
-#pragma unroll
-                for (int o = 1; o < 32; o <<= 1) {
-                    const float y = __shfl_up_sync(0xffffffffu, lg, o);
-                    if (lane >= o) lg += y;
-                }
-                if (lane == 31) g[G_TOT * 64 + pw] = lg;
-            }
-            load_gates(c + 1);                             // prefetch the next chunk's gate inputs
-            named_bar(BAR_PREP, 128);
-            const float lam_last = g[G_TOT * 64 + 0] + g[G_TOT * 64 + 1];
-            const float ll2 = lam_last * kLog2e;
-            const bool direct = ll2 < -240.f;              // u_t * w_s could overflow
-            if (pt < kC) {
-                const float lam = lg + (pw == 1 ? g[G_TOT * 64 + 0] : 0.f);
-                const float l2 = lam * kLog2e;
-                const float m2 = 0.5f * ll2;
-                const float el = ex2_approx(l2);
-                g[G_LAM2 * 64 + pt] = l2;
-                g[G_U * 64 + pt] = ex2_approx(l2 - m2);
-                g[G_W * 64 + pt] = ex2_approx(m2 - l2);
-                g[G_EDEC * 64 + pt] = ex2_approx(ll2 - l2);
-                g[G_BME * 64 + pt] = g[G_BM * 64 + pt] * el;
-                g[G_OC * 64 + pt] = g[G_MK * 64 + pt] * scale * el;
-                if (pt == 0) g[G_TOT * 64 + 2] = ex2_approx(ll2);
-            }
-
-            // ---- [Q;K] K^T on tensor cores
+            // ---- [Q;K] K^T on tensor cores (overlaps the gate computation below)
             mbar_wait_or_abort(&bars->qk_full[par], (c >> 1) & 1, err, abort_flag);
             uint8_t* qk_s = sm + (par ? L::OFF_QK1 : L::OFF_QK0);
             if (leader && !*abort_flag) {
@@ -424,7 +443,47 @@ prefill_chunk_kernel(const __grid_constant__ CUtensorMap map_q, const __grid_con
                 }
                 umma_commit(&bars->qkk_done);
             }
+
+            // ---- gates (prefill_ref.py:49-64, 79-91) on one warp, two tokens per lane
+            if (pw == 0) {
+                const int t0 = 2 * lane;
+                const int tok = c * kC + t0;
+                float lg0 = 0.f, lg1 = 0.f, bm0 = 0.f, bm1 = 0.f;
+                if (tok < T) {
+                    lg0 = A_neg * softplus_fast(pa0 + dtb);
+                    bm0 = sigmoid_fast(pb0) * pm0;
+                }
+                if (tok + 1 < T) {
+                    lg1 = A_neg * softplus_fast(pa1 + dtb);
+                    bm1 = sigmoid_fast(pb1) * pm1;
+                }
+                float sc = lg0 + lg1;
+#pragma unroll
+                for (int o = 1; o < 32; o <<= 1) {
+                    const float y = __shfl_up_sync(0xffffffffu, sc, o);
+                    if (lane >= o) sc += y;
+                }
+                const float ll2 = __shfl_sync(0xffffffffu, sc, 31) * kLog2e;
+                const float m2 = 0.5f * ll2;
+                const float l21 = sc * kLog2e, l20 = (sc - lg1) * kLog2e;
+                const float el0 = ex2_approx(l20), el1 = ex2_approx(l21);
+                *reinterpret_cast<float2*>(g + G_LAM2 * 64 + t0) = make_float2(l20, l21);
+                *reinterpret_cast<float2*>(g + G_U * 64 + t0) = make_float2(ex2_approx(l20 - m2), ex2_approx(l21 - m2));
+                *reinterpret_cast<float2*>(g + G_W * 64 + t0) = make_float2(ex2_approx(m2 - l20), ex2_approx(m2 - l21));
+                *reinterpret_cast<float2*>(g + G_EDEC * 64 + t0) =
+                    make_float2(ex2_approx(ll2 - l20), ex2_approx(ll2 - l21));
+                *reinterpret_cast<float2*>(g + G_BM * 64 + t0) = make_float2(bm0, bm1);
+                *reinterpret_cast<float2*>(g + G_BME * 64 + t0) = make_float2(bm0 * el0, bm1 * el1);
+                *reinterpret_cast<float2*>(g + G_OC * 64 + t0) = make_float2(pm0 * scale * el0, pm1 * scale * el1);
+                *reinterpret_cast<float2*>(g + G_MK * 64 + t0) = make_float2(pm0, pm1);
+                if (lane == 0) {
+                    g[G_TOT * 64 + 2] = ex2_approx(ll2);                  // gamma_c
+                    g[G_TOT * 64 + 3] = (ll2 < -240.f) ? 1.f : 0.f;        // u_t * w_s could overflow
+                }
+                load_gates(c + 1);                         // prefetch the next chunk's gate inputs
+            }
             named_bar(BAR_PREP, 128);      // gate vectors complete
+            const bool direct = g[G_TOT * 64 + 3] != 0.f;
             mbar_wait_or_abort(&bars->qkk_done, c & 1, err, abort_flag);
             tc_fence_after();
 
@@ -445,11 +504,13 @@ prefill_chunk_kernel(const __grid_constant__ CUtensorMap map_q, const __grid_con
                         uint4 w4 = make_uint4(0u, 0u, 0u, 0u);
                         if (8 * ch <= t) {
                             float e[8];
+                            if (!direct) {
 #pragma unroll
-                            for (int u = 0; u < 8; ++u) {
-                                const int s = 8 * ch + u;
-                                const float dec = direct ? coef * ex2_approx(lt - gl2[s]) : cu * gw[s];
-                                e[u] = (s <= t) ? row[s] * dec : 0.f;
+                                for (int u = 0; u < 8; ++u) e[u] = (8 * ch + u <= t) ? row[8 * ch + u] * (cu * gw[8 * ch + u]) : 0.f;
+                            } else {
+#pragma unroll
+                                for (int u = 0; u < 8; ++u)
+                                    e[u] = (8 * ch + u <= t) ? row[8 * ch + u] * (coef * ex2_approx(lt - gl2[8 * ch + u])) : 0.f;
                             }
                             w4 = pack8(e);
                         }
@@ -466,11 +527,13 @@ prefill_chunk_kernel(const __grid_constant__ CUtensorMap map_q, const __grid_con
                     for (int s4 = 0; s4 < 16; ++s4) {
                         if (4 * s4 < send) {
                             float o4[4];
+                            if (!direct) {
 #pragma unroll
-                            for (int u = 0; u < 4; ++u) {
-                                const int s = 4 * s4 + u;
-                                const float dec = direct ? coef * ex2_approx(lt - gl2[s]) : cu * gw[s];
-                                o4[u] = (s < t) ? row[s] * dec : 0.f;
+                                for (int u = 0; u < 4; ++u) o4[u] = (4 * s4 + u < t) ? row[4 * s4 + u] * (cu * gw[4 * s4 + u]) : 0.f;
+                            } else {
+#pragma unroll
+                                for (int u = 0; u < 4; ++u)
+                                    o4[u] = (4 * s4 + u < t) ? row[4 * s4 + u] * (coef * ex2_approx(lt - gl2[4 * s4 + u])) : 0.f;
                             }
                             *reinterpret_cast<float4*>(nrow + 4 * s4) = make_float4(o4[0], o4[1], o4[2], o4[3]);
                         }
@@ -523,8 +586,10 @@ prefill_chunk_kernel(const __grid_constant__ CUtensorMap map_q, const __grid_con
             tc_fence_before();
             named_bar(BAR_PREP, 128);
 
-            // ---- U^T = V^T A1^T  (into UT[par]),  W^T = K^T A2^T  (into COL_QKK)
+            // ---- U^T = V^T A1^T (into UT[par]), W^T = K^T A2^T (into COL_WT); the chain waits for them
             if (leader) {
+                mbar_arrive(&bars->prep_done[par]);       // P, gates, A1/A2 are in shared memory
+                if (c >= 1) mbar_wait_or_abort(&bars->wt_read, (c - 1) & 1, err, abort_flag);
                 const bool okv = mbar_wait_or_abort(&bars->v_full, c & 1, err, abort_flag);
                 tc_fence_after();
                 if (okv && !*abort_flag) {
@@ -545,35 +610,43 @@ prefill_chunk_kernel(const __grid_constant__ CUtensorMap map_q, const __grid_con
                         const uint32_t b2 = sx + (p ? L::X_A2L : L::X_A2H);
 #pragma unroll
                         for (int kk = 0; kk < 4; ++kk)
-                            umma_bf16_ss(tmem + COL_QKK, sdesc_sw128(sk + kk * 2048, 16384, 1024),
+                            umma_bf16_ss(tmem + COL_WT, sdesc_sw128(sk + kk * 2048, 16384, 1024),
                                          sdesc_sw128(b2 + kk * 32, 16, 1024), id_mn, (p > 0 || kk > 0) ? 1u : 0u);
                     }
                     umma_commit(&bars->uw_done);
                     umma_commit(&bars->v_free);
                 }
             }
-            mbar_wait_or_abort(&bars->uw_done, c & 1, err, abort_flag);
-            tc_fence_after();
-
-            // ---- W^T (lane d) -> X as MN-major B operand rows [d][t], hi/lo
-            {
-                float row[64];
-                tmem_ld64(tmem + lane_off + COL_QKK, row);
-                store_row_split(sm + L::OFF_X + L::X_WTH, sm + L::OFF_X + L::X_WTL, tl, row);
-            }
-            fence_async_smem();
-            tc_fence_before();
-            named_bar(BAR_PREP, 128);
-            if (leader) mbar_arrive(&bars->prep_done[par]);
         }
     } else {
         // ======================= CHAIN warpgroup
         const int ct = tid - 160;                          // 0..127
-        const int j = ((warp & 3) << 5) | lane;            // TMEM lane = value row j
+        const int j = ((warp & 3) << 5) | lane;            // TMEM lane = value row j (or key row d for W^T)
         const uint32_t lane_off = static_cast<uint32_t>(warp & 3) << 21;
         const bool leader = (ct == 0);
         const long s_base = static_cast<long>(bh) * DK * args.dv + v0;
         uint8_t* sr = sm + L::OFF_SR;
+
+        // output tile of chunk cc from (Q S)^T and (P dV)^T in TMEM:
+        //   o[t, j] = oc_t (Q S)[t,j] + (P dV)[t,j]  -> smem [t][j] (128B swizzle) -> TMA store
+        auto write_output = [&](int cc) {
+            float qs[64], pd[64];
+            tmem_ld64(tmem + lane_off + COL_QS, qs);
+            tmem_ld64(tmem + lane_off + COL_PDV, pd);
+            const float* oc = ocbuf + (cc & 1) * 64;
+            uint8_t* ob = sr + L::OST + (j >> 6) * 8192;
+            const uint32_t jj = j & 63;
+#pragma unroll
+            for (int t = 0; t < kC; ++t)
+                *reinterpret_cast<uint16_t*>(ob + sw128_off(t, jj)) = f32_to_bf16_bits(fmaf(oc[t], qs[t], pd[t]));
+            fence_async_smem();
+            tc_fence_before();
+            named_bar(BAR_CHAIN, 128);
+            if (leader && !*abort_flag) {
+                for (int vb = 0; vb < nvb; ++vb) tma_store_4d(&map_o, sr + L::OST + vb * 8192, v0 + vb * 64, cc * kC, h, bidx);
+                bulk_commit();
+            }
+        };
 
         // initial state -> TMEM (S^T: lane j = value column, column d = key index)
 #pragma unroll
@@ -594,12 +667,21 @@ prefill_chunk_kernel(const __grid_constant__ CUtensorMap map_q, const __grid_con
             const int par = c & 1;
             const float* g = gates + par * L::GSTRIDE;
             uint8_t* qk_s = sm + (par ? L::OFF_QK1 : L::OFF_QK0);
+            if (c >= 1) write_output(c - 1);               // previous chunk's output, while prep runs
             mbar_wait_or_abort(&bars->prep_done[par], (c >> 1) & 1, err, abort_flag);
-            const float gamma_c = g[G_TOT * 64 + 2];
-            if (leader) bulk_wait_read0();                 // previous output tile has left shared memory
-            named_bar(BAR_CHAIN, 128);
+            mbar_wait_or_abort(&bars->uw_done, c & 1, err, abort_flag);
+            tc_fence_after();
 
+            // ---- W^T (lane d) -> X as MN-major B operand rows [d][t], hi/lo
+            {
+                float row[64];
+                tmem_ld64(tmem + lane_off + COL_WT, row);
+                store_row_split(sm + L::OFF_X + L::X_WTH, sm + L::OFF_X + L::X_WTL, j, row);
+            }
+            if (leader) bulk_wait_read0();                 // the output tile has left shared memory
+            named_bar(BAR_CHAIN, 128);
             // ---- S^T -> bf16 hi/lo rows [j][d]; S^T *= gamma_c in TMEM
+            const float gamma_c = g[G_TOT * 64 + 2];
 #pragma unroll
             for (int blk = 0; blk < DK / 32; ++blk) {
                 float vals[32];
@@ -622,15 +704,14 @@ prefill_chunk_kernel(const __grid_constant__ CUtensorMap map_q, const __grid_con
             fence_async_smem();
             tc_fence_before();
             named_bar(BAR_CHAIN, 128);
+            if (leader) mbar_arrive(&bars->wt_read);
 
             // ---- dV^T = U^T - S^T W^T (3 split terms, negated B, in place in UT[par]); (Q S_hi)^T
             if (leader && !*abort_flag) {
                 tc_fence_after();
                 const uint32_t ssr = smem_u32(sr);
                 const uint32_t swt = smem_u32(sm + L::OFF_X);
-                const uint32_t sqk = smem_u32(qk_s);
                 constexpr uint32_t id_ws = idesc_bf16(128, 64, false, true) | (1u << 14);   // negate B
-                constexpr uint32_t id64 = idesc_bf16(128, 64, false, false);
 #pragma unroll
                 for (int p = 0; p < 3; ++p) {
                     const uint32_t sa = ssr + (p == 1 ? L::S_LO : 0);
@@ -644,8 +725,8 @@ prefill_chunk_kernel(const __grid_constant__ CUtensorMap map_q, const __grid_con
 #pragma unroll
                 for (int kk = 0; kk < DK / 16; ++kk) {
                     const uint32_t o = (kk >> 2) * 16384 + (kk & 3) * 32;
-                    umma_bf16_ss(tmem + COL_QS, sdesc_sw128(ssr + o, 16, 1024), sdesc_sw128(sqk + o, 16, 1024),
-                                 id64, kk > 0);
+                    umma_bf16_ss(tmem + COL_QS, sdesc_sw128(ssr + o, 16, 1024), sdesc_sw128(smem_u32(qk_s) + o, 16, 1024),
+                                 idesc_bf16(128, 64, false, false), kk > 0);
                 }
                 umma_commit(&bars->ws_done);
             }
@@ -699,31 +780,11 @@ prefill_chunk_kernel(const __grid_constant__ CUtensorMap map_q, const __grid_con
             }
             mbar_wait_or_abort(&bars->st_done, c & 1, err, abort_flag);
             tc_fence_after();
-
-            // ---- output tile o[t, j] = oc_t (Q S)[t,j] + (P dV)[t,j] -> smem [t][j] -> TMA store
-            {
-                float qs[64], pd[64];
-                tmem_ld64(tmem + lane_off + COL_QS, qs);
-                tmem_ld64(tmem + lane_off + COL_PDV, pd);
-                const float* oc = g + G_OC * 64;
-                uint8_t* ob = sr + L::OST + (j >> 6) * 8192;
-                const uint32_t jj = j & 63;
-#pragma unroll
-                for (int t = 0; t < kC; ++t)
-                    *reinterpret_cast<uint16_t*>(ob + sw128_off(t, jj)) = f32_to_bf16_bits(fmaf(oc[t], qs[t], pd[t]));
-            }
-            fence_async_smem();
-            tc_fence_before();
+            if (ct < kC) ocbuf[par * 64 + ct] = g[G_OC * 64 + ct];
             named_bar(BAR_CHAIN, 128);
-            if (leader) {
-                if (!*abort_flag) {
-                    for (int vb = 0; vb < nvb; ++vb)
-                        tma_store_4d(&map_o, sr + L::OST + vb * 8192, v0 + vb * 64, c * kC, h, bidx);
-                    bulk_commit();
-                }
-                mbar_arrive(&bars->chain_done[par]);
-            }
+            if (leader) mbar_arrive(&bars->chain_done[par]);
         }
+        if (nchunks >= 1) write_output(nchunks - 1);
         if (leader) bulk_wait_all0();
 
         // ---- final state S^T -> state_out [dk][dv]
