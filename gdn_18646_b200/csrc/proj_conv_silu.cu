@@ -52,7 +52,7 @@ struct ProjArgs {
     int l2;                      // 0 or group size
 };
 
-__device__ __forceinline__ float bf16r(float x) { return bf16_bits_to_f32(f32_to_bf16_bits(x)); }
+__device__ __forceinline__ float bf16r(float x) { return __uint_as_float(static_cast<uint32_t>(f32_to_bf16_bits(x)) << 16); }
 
 __global__ void __launch_bounds__(kProjThreads, 1)
 proj_conv_silu_kernel(const __grid_constant__ CUtensorMap map_w, const __grid_constant__ CUtensorMap map_x,
@@ -185,30 +185,53 @@ proj_conv_silu_kernel(const __grid_constant__ CUtensorMap map_w, const __grid_co
             float p1 = 0.f, p2 = 0.f, p3 = 0.f;     // projections of tokens i-3, i-2, i-1
             uint8_t* ysub = ysm + (cl >> 6) * Y_SUB_BYTES;
             const uint32_t ccol = cl & 63;
+            // tiles that touch the conv history (first tile with state_in, last tile with state_out)
+            const bool special = (tt == 0 && args.state_in) || (args.state_out && ts + PN > args.T - 3);
 #pragma unroll 1
             for (int blk = 0; blk < PN / 32; ++blk) {
                 float acc[32];
                 tmem_ld32(tmem + lane_off + abuf * PN + blk * 32, acc);
                 tmem_ld_wait();
+                if (!special) {
 #pragma unroll
-                for (int u = 0; u < 32; ++u) {
-                    const int i = blk * 32 + u;
-                    const int tok = ts + i;
-                    float p = bf16r(acc[u]);
-                    if (tok < 0) p = args.state_in ? bf16_bits_to_f32(args.state_in[sbase + (tok + 3)]) : 0.f;
-                    if (args.state_out && tok < args.T && tok >= args.T - 3 && (i >= 3 || tt == 0))
-                        args.state_out[sbase + (tok - (args.T - 3))] = f32_to_bf16_bits(p);
-                    if (i >= 3) {
-                        float conv = p1 * w0;
-                        conv = fmaf(p2, w1, conv);
-                        conv = fmaf(p3, w2, conv);
-                        conv = fmaf(p, w3, conv);
-                        const float y = bf16r(silu_f(bf16r(conv)));
-                        *reinterpret_cast<uint16_t*>(ysub + sw128_off(i - 3, ccol)) = f32_to_bf16_bits(y);
+                    for (int u = 0; u < 32; ++u) {
+                        const int i = blk * 32 + u;
+                        const float p = bf16r(acc[u]);
+                        if (i >= 3) {
+                            float conv = p1 * w0;
+                            conv = fmaf(p2, w1, conv);
+                            conv = fmaf(p3, w2, conv);
+                            conv = fmaf(p, w3, conv);
+                            const float cr = bf16r(conv);
+                            const float y = __fdividef(cr, 1.f + __expf(-cr));   // SiLU
+                            *reinterpret_cast<uint16_t*>(ysub + sw128_off(i - 3, ccol)) = f32_to_bf16_bits(y);
+                        }
+                        p1 = p2;
+                        p2 = p3;
+                        p3 = p;
                     }
-                    p1 = p2;
-                    p2 = p3;
-                    p3 = p;
+                } else {
+#pragma unroll
+                    for (int u = 0; u < 32; ++u) {
+                        const int i = blk * 32 + u;
+                        const int tok = ts + i;
+                        float p = bf16r(acc[u]);
+                        if (tok < 0) p = args.state_in ? bf16_bits_to_f32(args.state_in[sbase + (tok + 3)]) : 0.f;
+                        if (args.state_out && tok < args.T && tok >= args.T - 3 && (i >= 3 || tt == 0))
+                            args.state_out[sbase + (tok - (args.T - 3))] = f32_to_bf16_bits(p);
+                        if (i >= 3) {
+                            float conv = p1 * w0;
+                            conv = fmaf(p2, w1, conv);
+                            conv = fmaf(p3, w2, conv);
+                            conv = fmaf(p, w3, conv);
+                            const float cr = bf16r(conv);
+                            const float y = __fdividef(cr, 1.f + __expf(-cr));   // SiLU
+                            *reinterpret_cast<uint16_t*>(ysub + sw128_off(i - 3, ccol)) = f32_to_bf16_bits(y);
+                        }
+                        p1 = p2;
+                        p2 = p3;
+                        p3 = p;
+                    }
                 }
             }
             // accumulator buffer free for the MMA warp
