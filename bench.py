@@ -256,6 +256,7 @@ def run_ours(args):
     e2e_value = world * tokens / (ms_e2e * 1e-3)
 
     dec = run_decode(args, rank, world, dev, stream, hbm_peak)
+    prj = run_proj(args, world, dev, stream, tf_peak)
     cpu = cpu_baseline_prefill() if (rank == 0 and world == 1 and not args.no_cpu_baseline) else None
 
     if rank == 0:
@@ -278,16 +279,18 @@ def run_ours(args):
                          "tensor_frac_of_2250": achieved_tf / 2250.0},
             "clocks": clocks.summary(),
             "decode": dec,
+            "proj": prj,
             "cpu_baseline": cpu,
         }
         print(json.dumps(line), flush=True)
     finish(world)
 
 
-# ncu-measured DRAM bytes (read + write) of one prefill launch at config 1;
-# None until a capture exists (see profiles/).
-PREFILL_TRAFFIC_PER_LAUNCH = None
-DECODE_TRAFFIC_PER_LAUNCH = None
+# ncu-measured DRAM bytes (dram__bytes_read.sum + dram__bytes_write.sum) of one
+# launch, from the launch lists in profiles/prefill_chunk_kernel_config1.md
+# (208.0 + 45.2 MB) and profiles/decode_step_kernel_config2.md (543.2 + 479.7 MB).
+PREFILL_TRAFFIC_PER_LAUNCH = 253.2e6
+DECODE_TRAFFIC_PER_LAUNCH = 1022.9e6
 
 
 def run_decode(args, rank, world, dev, stream, hbm_peak):
@@ -320,6 +323,24 @@ def run_decode(args, rank, world, dev, stream, hbm_peak):
     return {"config": "config2_decode B=256 H=32 dk=dv=128, 64 in-place steps", "tokens_per_s": world * B / (ms_step * 1e-3),
             "ms_per_step": ms_step, "state_gbs": gbs, "frac_of_measured_hbm": gbs / hbm_peak,
             "frac_of_8000": gbs / 8000.0, "state_bytes_per_step": sb, "traffic": DECODE_TRAFFIC_PER_LAUNCH}
+
+
+def run_proj(args, world, dev, stream, tf_peak):
+    """Config 3's fused q|k|v input projection + conv4 + SiLU (x [2, 8192, 2048],
+    8192 output channels), GEMM-bound."""
+    import torch
+    from gdn_18646_b200 import ops
+    g = torch.Generator(device=dev).manual_seed(6)
+    x = torch.randn(2, 8192, 2048, generator=g, device=dev).bfloat16()
+    W = (torch.randn(8192, 2048, generator=g, device=dev) * 0.02).bfloat16()
+    cw = (torch.randn(8192, 4, generator=g, device=dev) * 0.5).bfloat16()
+    y = torch.empty(2, 8192, 8192, dtype=torch.bfloat16, device=dev)
+    steps = 10
+    ms = timed(lambda: ops.proj_conv_silu(x, W, cw, out=y), steps, 3, world, stream) / steps
+    flops = 2.0 * 2 * 8192 * 2048 * 8192
+    tf = flops / (ms * 1e-3) / 1e12
+    return {"config": "config3 fused q|k|v projection+conv4+SiLU, x [2,8192,2048] -> 8192 channels",
+            "ms_per_launch": ms, "tflops": tf, "frac_of_measured_bf16": tf / tf_peak, "frac_of_2250": tf / 2250.0}
 
 
 def run_long(args, rank, world, dev, stream, hbm_peak, tf_peak, peak_kind):
@@ -395,20 +416,21 @@ def _cpu_run(inp):
                      state_in=inp["state_in"], scale=inp["scale"], chunk_size=64)
 
 
-def cpu_baseline_prefill(Hs=4, reps=3):
-    """Best of `reps` oracle runs on a sample of Hs of the 64 config-1 sequences
-    (B=1, T=4096, Hs heads); tokens/s scaled to whole config-1 tokens."""
-    inp = _cpu_sample(99, Hs)
-    best = float("inf")
-    for _ in range(reps):
+def cpu_baseline_prefill(min_seconds=10.0, max_reps=8):
+    """The oracle (numpy fp32, all host threads) on the whole config-1 workload
+    (B=4, T=4096, H=16), repeated until ~10 s of CPU time; best run reported."""
+    from oracle import gdn_oracle as O
+    c = C1
+    inp = O.make_prefill_inputs(99, c["B"], c["T"], c["H"], c["dk"], c["dv"], gate_dtype="f32", state_std=0.02)
+    best, total, reps = float("inf"), 0.0, 0
+    while reps < max_reps and (total < min_seconds or reps < 2):
         t0 = time.perf_counter()
         _cpu_run(inp)
-        best = min(best, time.perf_counter() - t0)
-    c = C1
-    frac = Hs / (c["B"] * c["H"])
-    return {"value": frac * c["B"] * c["T"] / best, "unit": "tokens/s", "cores": os.cpu_count(),
-            "kind": "port", "sample": f"oracle/gdn_oracle.prefill (numpy fp32) on {Hs} of the 64 config-1 "
-                                      f"sequences (B=1, T=4096, {Hs} heads), best of {reps}: {best:.2f} s"}
+        dt = time.perf_counter() - t0
+        best, total, reps = min(best, dt), total + dt, reps + 1
+    return {"value": c["B"] * c["T"] / best, "unit": "tokens/s", "cores": os.cpu_count(), "kind": "port",
+            "sample": f"oracle/gdn_oracle.prefill (numpy fp32, {os.cpu_count()} host threads) on the whole "
+                      f"config-1 workload (B=4, T=4096, H=16), best of {reps} runs ({total:.1f} s total)"}
 
 
 def run_reference(args):
@@ -417,7 +439,7 @@ def run_reference(args):
     rank = int(os.environ.get("RANK", "0"))
     if rank != 0:
         return
-    Hs = 2
+    Hs = 8
     inp = _cpu_sample(7, Hs)
     for _ in range(args.warmup):
         _cpu_run(inp)

@@ -1,0 +1,171 @@
+"""Gated DeltaNet layer on the libgdn_b200 kernels.
+
+Prefill (T tokens):
+    x [B,T,D] -> RMSNorm -> q,k = L2norm(SiLU(conv4(x Wq^T))), v = SiLU(conv4(x Wv^T))
+              -> z = x Wz^T, a = x Wa^T, b = x Wb^T  (cuBLAS, plain GEMMs)
+              -> chunked gated delta rule (grouped value heads, [B,T,H,D] layout)
+              -> gated RMSNorm(o) * SiLU(z) -> x Wo^T
+Decode (1 token) runs the same blocks with the carried recurrent state
+[B,Hv,dk,dv] fp32 and the three conv histories [B,C,3] bf16; ``prefill``
+returns both so decode continues a prefilled sequence.
+
+Composition follows the reference layer (gdn_layer.py:120-199) with the
+additions of the BASELINE layer (L2-normalised q/k, 16 q/k heads shared by 32
+value heads, z-gated output norm, per-head A_log/dt_bias); weights are
+synthetic N(0, 0.02) (config 3).  No transposes are materialised between
+kernels: projections write [B,T,H*D], which the prefill reads as [B,T,H,D].
+"""
+from __future__ import annotations
+
+import math
+from dataclasses import dataclass
+
+import torch
+
+from . import ops
+
+
+@dataclass
+class GDNConfig:
+    hidden: int = 2048
+    n_qk: int = 16          # q/k heads
+    n_v: int = 32           # value heads
+    dk: int = 128
+    dv: int = 128
+    conv: int = 4
+    eps: float = 1e-6
+
+    @property
+    def qk_dim(self):
+        return self.n_qk * self.dk
+
+    @property
+    def v_dim(self):
+        return self.n_v * self.dv
+
+
+def make_weights(cfg: GDNConfig, device="cuda", seed=0, std=0.02):
+    """Random weights of config 3 (bf16 ~N(0, std)); A_log / dt_bias follow the
+    BASELINE gate distribution (log-decay = -0.1 * softplus(a))."""
+    g = torch.Generator(device=device).manual_seed(seed)
+
+    def w(*shape, s=std):
+        return (torch.randn(*shape, generator=g, device=device) * s).bfloat16()
+
+    D = cfg.hidden
+    return dict(
+        norm_gamma=torch.ones(D, dtype=torch.bfloat16, device=device),
+        W_q=w(cfg.qk_dim, D), conv_q=w(cfg.qk_dim, cfg.conv, s=0.5),
+        W_k=w(cfg.qk_dim, D), conv_k=w(cfg.qk_dim, cfg.conv, s=0.5),
+        W_v=w(cfg.v_dim, D), conv_v=w(cfg.v_dim, cfg.conv, s=0.5),
+        W_z=w(cfg.v_dim, D),
+        W_ab=w(2 * cfg.n_v, D),
+        A_log=torch.full((cfg.n_v,), math.log(0.1), device=device),
+        dt_bias=torch.zeros(cfg.n_v, device=device),
+        onorm_gamma=torch.ones(cfg.dv, dtype=torch.bfloat16, device=device),
+        W_o=w(D, cfg.v_dim),
+    )
+
+
+class GDNLayer:
+    """B200 Gated DeltaNet layer; every op is a libgdn_b200 kernel except the
+    plain z / a,b / output GEMMs (cuBLAS through torch)."""
+
+    def __init__(self, weights: dict, cfg: GDNConfig | None = None):
+        self.w = weights
+        self.cfg = cfg or GDNConfig()
+        self.scale = self.cfg.dk ** -0.5
+
+    def init_state(self, B: int, device="cuda"):
+        c = self.cfg
+        return dict(
+            recurrent=torch.zeros(B, c.n_v, c.dk, c.dv, dtype=torch.float32, device=device),
+            conv_q=torch.zeros(B, c.qk_dim, c.conv - 1, dtype=torch.bfloat16, device=device),
+            conv_k=torch.zeros(B, c.qk_dim, c.conv - 1, dtype=torch.bfloat16, device=device),
+            conv_v=torch.zeros(B, c.v_dim, c.conv - 1, dtype=torch.bfloat16, device=device),
+        )
+
+    def _project(self, xn, state_in, state_out):
+        """q, k (L2-normalised per head), v, z and the a/b gate logits for xn [B,T,D]."""
+        c, w = self.cfg, self.w
+        B, T, D = xn.shape
+        si = state_in or {}
+        q = ops.proj_conv_silu(xn, w["W_q"], w["conv_q"], l2norm_group=c.dk, conv_state_in=si.get("conv_q"),
+                               conv_state_out=state_out["conv_q"])
+        k = ops.proj_conv_silu(xn, w["W_k"], w["conv_k"], l2norm_group=c.dk, conv_state_in=si.get("conv_k"),
+                               conv_state_out=state_out["conv_k"])
+        v = ops.proj_conv_silu(xn, w["W_v"], w["conv_v"], conv_state_in=si.get("conv_v"),
+                               conv_state_out=state_out["conv_v"])
+        z = xn @ w["W_z"].T
+        ab = xn @ w["W_ab"].T                                    # [B, T, 2*Hv]
+        return q, k, v, z, ab
+
+    @torch.no_grad()
+    def prefill(self, x: torch.Tensor, state: dict | None = None):
+        """x [B,T,D] bf16 -> (y [B,T,D] bf16, state after the last token)."""
+        c, w = self.cfg, self.w
+        B, T, D = x.shape
+        xn = ops.rmsnorm(x.reshape(B * T, D), w["norm_gamma"], c.eps).reshape(B, T, D)
+        new_state = self.init_state(B, x.device)
+        q, k, v, z, ab = self._project(xn, state, new_state)
+        a = ab[..., :c.n_v].transpose(1, 2).contiguous()        # [B, Hv, T]
+        b = ab[..., c.n_v:].transpose(1, 2).contiguous()
+        o, S = ops.prefill(q.view(B, T, c.n_qk, c.dk), k.view(B, T, c.n_qk, c.dk), v.view(B, T, c.n_v, c.dv),
+                           w["A_log"], a, b, dt_bias=w["dt_bias"],
+                           state_in=None if state is None else state["recurrent"],
+                           scale=self.scale, layout="bthd", state_out=new_state["recurrent"])
+        y = ops.gated_rmsnorm(o.view(B * T * c.n_v, c.dv), z.view(B * T * c.n_v, c.dv), w["onorm_gamma"], c.eps)
+        return y.view(B, T, c.v_dim) @ w["W_o"].T, new_state
+
+    @torch.no_grad()
+    def decode(self, x: torch.Tensor, state: dict, out_state: dict | None = None):
+        """One token: x [B,1,D] bf16 -> (y [B,1,D] bf16, state).  The recurrent
+        state is updated in place; conv histories go to ``out_state`` (fresh
+        buffers by default).  All shapes are static, so the call can be
+        captured in a CUDA graph."""
+        c, w = self.cfg, self.w
+        B = x.shape[0]
+        D = c.hidden
+        xn = ops.rmsnorm(x.reshape(B, D), w["norm_gamma"], c.eps).reshape(B, 1, D)
+        if out_state is None:
+            out_state = dict(recurrent=state["recurrent"],
+                             conv_q=torch.empty_like(state["conv_q"]), conv_k=torch.empty_like(state["conv_k"]),
+                             conv_v=torch.empty_like(state["conv_v"]))
+        q, k, v, z, ab = self._project(xn, state, out_state)
+        a = ab[:, 0, :c.n_v].contiguous()
+        b = ab[:, 0, c.n_v:].contiguous()
+        o = ops.decode_step(q.view(B, c.n_qk, c.dk), k.view(B, c.n_qk, c.dk), v.view(B, c.n_v, c.dv), a, b,
+                            w["A_log"], w["dt_bias"], state["recurrent"], scale=self.scale,
+                            state_out=out_state["recurrent"])
+        y = ops.gated_rmsnorm(o.view(B * c.n_v, c.dv), z.view(B * c.n_v, c.dv), w["onorm_gamma"], c.eps)
+        return (y.view(B, 1, c.v_dim) @ w["W_o"].T), out_state
+
+
+class DecodeGraph:
+    """A CUDA graph of one ``GDNLayer.decode`` step over static buffers, so a
+    decode loop costs one graph launch per token."""
+
+    def __init__(self, layer: GDNLayer, state: dict, B: int):
+        self.layer = layer
+        dev = state["recurrent"].device
+        self.x = torch.zeros(B, 1, layer.cfg.hidden, dtype=torch.bfloat16, device=dev)
+        self.state = state
+        self.next_conv = {k_: torch.empty_like(v_) for k_, v_ in state.items() if k_ != "recurrent"}
+        # warm up once outside the graph (first-call set-up of the kernels)
+        s = torch.cuda.Stream()
+        s.wait_stream(torch.cuda.current_stream())
+        with torch.cuda.stream(s):
+            scratch = {k_: v_.clone() for k_, v_ in state.items()}
+            layer.decode(self.x, scratch, dict(scratch))
+        torch.cuda.current_stream().wait_stream(s)
+        self.graph = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(self.graph):
+            out_state = dict(recurrent=state["recurrent"], **self.next_conv)
+            self.y, _ = layer.decode(self.x, state, out_state)
+
+    def step(self, x: torch.Tensor) -> torch.Tensor:
+        self.x.copy_(x)
+        self.graph.replay()
+        for k_, buf in self.next_conv.items():       # carry the conv histories
+            self.state[k_].copy_(buf)
+        return self.y

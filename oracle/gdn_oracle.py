@@ -400,3 +400,40 @@ def rel_fro(a, b) -> float:
     a = np.asarray(a, dtype=np.float64)
     b = np.asarray(b, dtype=np.float64)
     return float(np.linalg.norm(a - b) / max(np.linalg.norm(b), 1e-30))
+
+
+# --------------------------------------------------------------------------
+# Layer composition -- restatement-pinned
+# --------------------------------------------------------------------------
+
+
+def _bf16_matmul(x_bits, W_bits):
+    """bf16 x @ W^T with fp32 accumulation rounded to bf16 (a torch bf16 matmul)."""
+    return f32_to_bf16(np.einsum("...d,od->...o", bf16_to_f32(x_bits), bf16_to_f32(W_bits), dtype=np.float32))
+
+
+def layer_prefill(x, w, n_qk=16, n_v=32, dk=128, dv=128, eps=1e-6):
+    """The config-3 layer on the restated reference functions, composed as
+    gdn_layer.py:120-159 with the BASELINE additions (L2-normalised q/k,
+    grouped value heads, z-gated output RMSNorm).  x [B,T,D] bf16 bits;
+    w: dict of numpy weights (bf16 bits / f32).  Returns y [B,T,D] bf16 bits
+    and the final recurrent state [B,n_v,dk,dv]."""
+    B, T, D = x.shape
+    xn = rmsnorm(x.reshape(B * T, D), w["norm_gamma"], eps).reshape(B, T, D)
+    q = l2norm_heads(proj_conv_silu(xn, w["W_q"], w["conv_q"])[0], dk)
+    k = l2norm_heads(proj_conv_silu(xn, w["W_k"], w["conv_k"])[0], dk)
+    v = proj_conv_silu(xn, w["W_v"], w["conv_v"])[0]
+    z = _bf16_matmul(xn, w["W_z"])
+    ab = _bf16_matmul(xn, w["W_ab"])
+    a = np.ascontiguousarray(np.swapaxes(ab[..., :n_v], 1, 2))
+    b = np.ascontiguousarray(np.swapaxes(ab[..., n_v:], 1, 2))
+    qh = np.swapaxes(q.reshape(B, T, n_qk, dk), 1, 2)
+    kh = np.swapaxes(k.reshape(B, T, n_qk, dk), 1, 2)
+    vh = np.swapaxes(v.reshape(B, T, n_v, dv), 1, 2)
+    qh, kh = expand_qk_heads(qh, n_v), expand_qk_heads(kh, n_v)
+    dtb = float(np.asarray(w["dt_bias"]).reshape(-1)[0])
+    o, S = prefill(qh, kh, vh, w["A_log"], a, dtb, b, np.ones((B, T), np.float32), scale=dk ** -0.5,
+                   chunk_size=64)
+    o_bits = f32_to_bf16(np.swapaxes(o, 1, 2))            # [B,T,n_v,dv] bf16, as the kernel writes it
+    y = gated_rmsnorm(o_bits.reshape(-1, dv), z.reshape(-1, dv), w["onorm_gamma"], eps)
+    return _bf16_matmul(y.reshape(B, T, n_v * dv), w["W_o"]), S
