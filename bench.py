@@ -38,7 +38,9 @@ sys.path.insert(0, REPO)
 C1 = dict(B=4, T=4096, H=16, dk=128, dv=128)
 C2 = dict(B=256, H=32, dk=128, dv=128, steps=64)
 C4 = dict(B=8, T=32768, H=32, dk=128, dv=128)
-FLOP_PER_TOKEN_HEAD = lambda dk, dv, C=64: 4 * C * (dk + dv) + 6 * dk * dv   # 163,840 at 128/128
+# Algorithmic flops per (token, head) of the chunked form (inverse excluded):
+# QK^T, KK^T, A.K (2C dk each), A.V, P.dV (2C dv each), W.S, Q.S, K^T.dV (2 dk dv each).
+FLOP_PER_TOKEN_HEAD = lambda dk, dv, C=64: 2 * C * (3 * dk + 2 * dv) + 6 * dk * dv   # 180,224 at 128/128
 
 
 def measured_peaks():
@@ -271,9 +273,10 @@ def run_ours(args):
                        "l2": "inputs larger than L2 (279 MB per step), no flush"},
             "e2e": {"value": e2e_value, "unit": "tokens/s", "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h,
                     "ms_per_step": ms_e2e},
-            "gpu_launches": args.steps,
+            "gpu_launches": args.steps * G._lib.lib().gdn_prefill_launch_count(c["B"], c["T"], c["H"], c["dk"], c["dv"]),
             "roofline": {"bound": "hbm", "achieved": achieved_gbs, "peak": hbm_peak, "unit": "GB/s",
-                         "frac": achieved_gbs / hbm_peak, "traffic": PREFILL_TRAFFIC_PER_LAUNCH,
+                         "frac": achieved_gbs / hbm_peak, "traffic": PREFILL_TRAFFIC_PER_STEP,
+                         "kernel": "prefill step: gates + prep + chain launches (chain ~60% of the time)",
                          "peak_kind": peak_kind, "alg_bytes_per_launch": alg_bytes,
                          "tensor_tflops": achieved_tf, "tensor_frac_of_measured": achieved_tf / tf_peak,
                          "tensor_frac_of_2250": achieved_tf / 2250.0},
@@ -286,10 +289,11 @@ def run_ours(args):
     finish(world)
 
 
-# ncu-measured DRAM bytes (dram__bytes_read.sum + dram__bytes_write.sum) of one
-# launch, from the launch lists in profiles/prefill_chunk_kernel_config1.md
-# (208.0 + 45.2 MB) and profiles/decode_step_kernel_config2.md (543.2 + 479.7 MB).
-PREFILL_TRAFFIC_PER_LAUNCH = 253.2e6
+# ncu-measured DRAM bytes (dram__bytes_read.sum + dram__bytes_write.sum): one
+# config-1 prefill step (its gates, prep and chain launches, summed) from
+# profiles/prefill_config1.md, and one decode launch from
+# profiles/decode_step_kernel_config2.md (543.2 + 479.7 MB).
+PREFILL_TRAFFIC_PER_STEP = 821.6e6
 DECODE_TRAFFIC_PER_LAUNCH = 1022.9e6
 
 
@@ -346,7 +350,7 @@ def run_proj(args, world, dev, stream, tf_peak):
 def run_long(args, rank, world, dev, stream, hbm_peak, tf_peak, peak_kind):
     """Config 4: head-sharded long-context prefill + NCCL all-gather of o."""
     import torch
-    from gdn_18646_b200 import ops
+    from gdn_18646_b200 import _lib, ops
     c = C4
     H = c["H"]
     assert H % world == 0, "heads must split evenly"
@@ -383,7 +387,7 @@ def run_long(args, rank, world, dev, stream, hbm_peak, tf_peak, peak_kind):
                        "heads_per_gpu": Hs, "parallelism": f"heads x{world} + NCCL all_gather(o)",
                        "l2": "inputs larger than L2, no flush"},
             "kernel_only": {"value": tokens / (ms_k * 1e-3), "ms_per_step": ms_k},
-            "gpu_launches": args.steps,
+            "gpu_launches": args.steps * _lib.lib().gdn_prefill_launch_count(c["B"], c["T"], Hs, c["dk"], c["dv"]),
             "roofline": {"bound": "hbm", "achieved": alg / (ms_k * 1e-3) / 1e9, "peak": hbm_peak, "unit": "GB/s",
                          "frac": alg / (ms_k * 1e-3) / 1e9 / hbm_peak, "traffic": None, "peak_kind": peak_kind,
                          "tensor_tflops": flops / (ms_k * 1e-3) / 1e12,

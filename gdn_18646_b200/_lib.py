@@ -26,15 +26,24 @@ GDN_DTYPE_BF16 = 0
 GDN_DTYPE_F32 = 1
 GDN_LAYOUT_BHTD = 0
 GDN_LAYOUT_BTHD = 1
+GDN_SCHEDULE_AUTO = 0
+GDN_SCHEDULE_SINGLE = 1
+GDN_SCHEDULE_PIECED = 2
 
 _P = ctypes.c_void_p
 _I = ctypes.c_int
 _F = ctypes.c_float
+_Z = ctypes.c_size_t
 
 # name -> argtypes (every entry returns int unless listed in _STR_FUNCS)
 SIGNATURES = {
     "gdn_prefill_fwd": [_P, _P, _P, _P, _P, _P, _I, _F, _P, _P, _P, _P, _P,
                         _I, _I, _I, _I, _I, _I, _I, _F, _P],
+    "gdn_prefill_fwd_ws": [_P, _P, _P, _P, _P, _P, _I, _F, _P, _P, _P, _P, _P,
+                           _I, _I, _I, _I, _I, _I, _I, _F, _P, _Z, _P],
+    "gdn_prefill_workspace_bytes": [_I, _I, _I, _I, _I],
+    "gdn_prefill_set_schedule": [_I],
+    "gdn_prefill_launch_count": [_I, _I, _I, _I, _I],
     "gdn_decode_step": [_P, _P, _P, _P, _P, _I, _P, _P, _P, _P, _P, _I, _I, _I, _I, _I, _F, _P],
     "gdn_rmsnorm_fwd": [_P, _P, _P, _I, _I, _F, _P],
     "gdn_gated_rmsnorm_fwd": [_P, _I, _P, _P, _P, _I, _I, _F, _P],
@@ -44,6 +53,7 @@ SIGNATURES = {
     "gdn_version": [],
 }
 _STR_FUNCS = {"gdn_last_error", "gdn_version"}
+_SIZE_FUNCS = {"gdn_prefill_workspace_bytes"}
 
 _lock = threading.Lock()
 _lib = None
@@ -71,7 +81,8 @@ def lib() -> ctypes.CDLL:
                 for name, args in SIGNATURES.items():
                     fn = getattr(handle, name)
                     fn.argtypes = args
-                    fn.restype = ctypes.c_char_p if name in _STR_FUNCS else ctypes.c_int
+                    fn.restype = (ctypes.c_char_p if name in _STR_FUNCS else
+                                  ctypes.c_size_t if name in _SIZE_FUNCS else ctypes.c_int)
                 _lib = handle
     return _lib
 

@@ -5,8 +5,8 @@
 // which runs fp32 CUDA-core loops with one thread per value column and
 // hard-codes H=16, K=128, V=256.
 //
-// One CTA per (batch, value head, 128-wide value tile).  Per 64-token chunk,
-// with Lambda the in-chunk cumulative log decay, beta' = beta * mask,
+// Per 64-token chunk, with Lambda the in-chunk cumulative log decay and
+// beta' = beta * mask:
 //   N[t,s] = -beta'_t (k_t . k_s) exp(Lambda_t - Lambda_s)  (t > s)
 //   A      = (I - N)^-1                                      (prefill_ref.py:96-101)
 //   U      = A diag(beta') V,  W = A diag(beta' e^Lambda) K  (prefill_ref.py:103-104)
@@ -15,36 +15,44 @@
 //            P[t,s] = scale (q_t.k_s) exp(Lambda_t - Lambda_s), s <= t   (:120-122)
 //   S     <- e^{Lambda_last} S + K^T diag(e^{Lambda_last - Lambda}) dV   (:124-126)
 //
-// The state is held TRANSPOSED in TMEM (S^T: value index = TMEM lane), so the
-// value tile is the M = 128 dimension of every state-path product.
+// Everything that does not involve S is independent per chunk, so the work is
+// split into two launches:
 //
-// Warp roles (288 threads):
-//   warp 0      TMA producer: q/k chunk tiles (2-slot ring) and v tiles.
-//   warps 1-4   PREP warpgroup, one chunk ahead of the chain: gates and the
-//               in-chunk cumulative decay; [Q;K] K^T on tensor cores; P and N
-//               (TMEM -> registers); the 64x64 unit-lower-triangular inverse
-//               (16x16 diagonal blocks by substitution in registers, the
-//               off-diagonal blocks with warp-level bf16 MMAs on hi/lo-split
-//               operands); U^T = V^T (A diag beta')^T and
-//               W^T = K^T (A diag(beta' e^Lambda))^T on tensor cores; W^T to
-//               shared memory as a bf16 hi/lo pair.
-//   warps 5-8   CHAIN warpgroup, the sequential state recurrence:
-//               S^T -> bf16 hi/lo; dV^T = U^T - S^T W^T accumulated straight into
-//               U^T's TMEM (negated B operand) and (Q S)^T; then
-//               S^T = e^{Lambda_last} S^T + dV'^T K and (P dV)^T.  W^T is
-//               split to shared memory by the chain (prep never waits on its
-//               U/W MMA), and chunk c's output tile is staged in shared memory
-//               and TMA-stored at the top of chunk c+1, while prep still runs.
-// Each warpgroup issues its own tcgen05.mma from one elected thread and
-// tracks completion with tcgen05.commit -> mbarrier.  fp32 values feeding the
-// state path (S, W, A diag beta', A diag beta' e^Lambda, dV') are split into
+// 1. prefill_prep_kernel: one task per (batch, value head, chunk), all in
+//    parallel (persistent CTAs, 3 per SM).  Gates, [Q;K] K^T on tensor cores,
+//    P and N, the 64x64 inverse, A1 = A diag(beta'), A2 = A diag(beta' e^Lambda),
+//    W^T = K^T A2^T on tensor cores.  It writes one chunk record to a workspace:
+//    A1 and W^T as bf16 hi/lo pairs, P in bf16, and the gate vectors the
+//    recurrence needs -- each operand already in the 128-byte-swizzled shared
+//    memory image the second kernel's MMAs read, so it is fetched with one
+//    bulk copy.
+// 2. prefill_chain_kernel: one CTA per (batch, value head, 128-wide value
+//    tile) walks the chunks in order.  The fp32 state lives in TMEM,
+//    TRANSPOSED (S^T: value index = TMEM lane, so the value tile is the
+//    M = 128 dimension of every product), for the whole sequence.  Per chunk:
+//      U^T   = V^T A1^T                          (A, B from shared memory; hi|lo as one N=128 MMA)
+//      S^T  -> bf16 hi/lo, kept in TMEM          (CUDA cores, TMEM -> TMEM)
+//      dV^T  = U^T - S^T W^T                     (A = S^T hi/lo from TMEM: S_hi [W_hi|W_lo] as one
+//                                                 N=128 MMA, then S_lo W_hi; halves summed on CUDA cores)
+//      (Q S_hi)^T                                (A from TMEM)
+//      dV^T -> bf16 and dV'^T = dV^T diag(e^{Lambda_last - Lambda}) hi/lo, in TMEM
+//      S^T   = gamma S^T + dV'^T K               (A from TMEM, K as MN-major B)
+//      (P dV)^T                                  (A from TMEM)
+//      o     = oc * (Q S) + P dV -> bf16 tile -> TMA store
+//    with warp roles: warp 0 TMA/bulk producer, warp 1 MMA issuer, warps 2-9
+//    the state path (each TMEM lane quadrant twice, one half of the columns
+//    each), warps 10-13 the output tile.  Only the state path's CUDA-core work
+//    and its MMAs sit on the sequential critical path.
+//
+// fp32 values feeding the state path (S, W, A diag beta', dV') are split into
 // bf16 hi + lo pairs (~16 mantissa bits per product); q/k/v are exact bf16
-// inputs; the output path (Q S_hi, P dV) uses single bf16.
-// Decay ratios exp(Lambda_t - Lambda_s) are formed as u_t * w_s with
-// u_t = 2^(l_t - m), w_s = 2^(m - l_s) around the chunk's mid decay m (never
-// gamma_t / gamma_s); chunks whose total decay could overflow that product
-// fall back to one exp2 per element.  Every mbarrier wait is bounded; a
-// timeout raises a CTA-wide abort and all roles drain through their barriers.
+// inputs; the output path (Q S_hi, P dV) uses single bf16.  Decay ratios
+// exp(Lambda_t - Lambda_s) are formed as u_t * w_s with u_t = 2^(l_t - m),
+// w_s = 2^(m - l_s) around the chunk's mid decay m (never gamma_t / gamma_s);
+// chunks whose total decay could overflow that product fall back to one exp2
+// per element.  Every mbarrier wait is bounded; a timeout raises a CTA-wide
+// abort and all roles drain through their barriers.
+#include <atomic>
 #include <mutex>
 
 #include "common.cuh"
@@ -54,64 +62,77 @@ namespace gdn {
 namespace {
 
 constexpr int kC = 64;                 // chunk length
-constexpr int kThreads = 288;          // 9 warps
-constexpr int kTmemCols = 512;
+constexpr int BAR_PREP = 1;            // named barrier of the prep kernel's 128 threads
+constexpr int BAR_OUT = 2;             // named barrier of the chain kernel's output warps
 
-// TMEM column map (fp32, 128 lanes)
-constexpr uint32_t COL_QKK = 0;        // prep: [Q;K] K^T (lanes 0-63 QK^T, 64-127 KK^T)
-constexpr uint32_t COL_UT = 64;        // 2 x 64: U^T for chunk parity 0/1, becomes dV^T in place
-constexpr uint32_t COL_QS = 192;       // (Q S_hi)^T
-constexpr uint32_t COL_PDV = 256;      // (P dV)^T
-constexpr uint32_t COL_ST = 320;       // S^T (fp32 state, dk columns)
-constexpr uint32_t COL_WT = 448;       // W^T (lanes = key index d)
+// ---------------------------------------------------------------------------
+// Chunk record (bytes, 1024-aligned images), written by the gate and prep kernels:
+//   GB        gate vectors of the chunk for the prep kernel (PrepGate layout)
+//   A1H, A1L  A diag(beta'), rows t, cols s        (K-major B of U^T = V^T A1^T)
+//   WTH, WTL  W^T, rows d, cols t                  (MN-major B of S^T W^T)
+//   P         rows t, cols s                       (K-major B of dV^T P^T)
+//   G         floats: [0,64) oc_t = m_t scale e^Lambda_t, [64,128) e^{Lambda_last - Lambda_t},
+//             [128] gamma = e^{Lambda_last}
+// The part from WTH to the end is fetched per chunk as one bulk copy, A1 as another.
+// ---------------------------------------------------------------------------
+template <int DK>
+struct Rec {
+    static constexpr int GB = 0;                      // gate vectors for the prep kernel (PrepGate)
+    static constexpr int A1H = 2048, A1L = A1H + 8192;
+    static constexpr int WTH = A1L + 8192;
+    static constexpr int WTL = WTH + DK * 128;
+    static constexpr int P = WTL + DK * 128;
+    static constexpr int G = P + 8192;
+    static constexpr int BYTES = G + 1024;
+    static constexpr int SLOT_BYTES = BYTES - WTH;   // WTH .. end
+    static_assert(BYTES % 1024 == 0 && SLOT_BYTES % 1024 == 0, "record images must stay 1024-aligned");
+};
 
-// named barriers
-constexpr int BAR_PREP = 1, BAR_CHAIN = 2;
+// ---------------------------------------------------------------------------
+// prep kernel layout
+// ---------------------------------------------------------------------------
+constexpr int kPrepThreads = 128;
+constexpr int kPrepCtasPerSm = 3;
+constexpr int kPrepTmemCols = 128;
+constexpr int kPrepPerCta = 3;         // prep workers per CTA of the overlap kernel
+constexpr uint32_t P_COL_QKK = 0;      // [Q;K] K^T (lanes 0-63 QK^T, 64-127 KK^T)
+constexpr uint32_t P_COL_WT = 64;      // W^T (lanes = key index d)
 
 template <int DK>
-struct PrefillSmem {
+struct PrepSmem {
     static constexpr int CB = DK / 64;                    // 64-wide column blocks of q/k
-    static constexpr int QK_BYTES = CB * 16384;           // slot: per block [Q 64 rows | K 64 rows] x 128 B
-    static constexpr int V_BYTES = 2 * 8192;              // 2 blocks of 64 rows x 128 B
-    static constexpr int SR_BYTES = (2 * CB * 16384 > 49152) ? 2 * CB * 16384 : 49152;
-    static constexpr int OFF_QK0 = 0;
-    static constexpr int OFF_QK1 = OFF_QK0 + QK_BYTES;
-    static constexpr int OFF_V = OFF_QK1 + QK_BYTES;
-    static constexpr int OFF_SR = OFF_V + V_BYTES;        // chain: S hi|lo; dV' hi|lo|dV bf16; o staging
-    static constexpr int S_LO = CB * 16384;
-    static constexpr int DVH = 0, DVL = 16384, DVB = 32768, OST = 0;
-    static constexpr int OFF_X = OFF_SR + SR_BYTES;       // prep A1 hi/lo, A2 hi/lo; then W^T hi/lo
-    static constexpr int X_A1H = 0, X_A1L = 8192, X_A2H = 16384, X_A2L = 24576;
-    static constexpr int X_WTH = 0, X_WTL = 16384;
-    static constexpr int OFF_P = OFF_X + 32768;           // P [2] x 8 KB
+    static constexpr int QK_BYTES = CB * 16384;           // per block [Q 64 rows | K 64 rows] x 128 B
+    static constexpr int OFF_A2H = 0;                     // A2 hi over the dead Q block 0
+    static constexpr int OFF_A2L = (DK == 128) ? 16384 : QK_BYTES;   // over Q block 1, or its own 8 KB
+    static constexpr int END_A = (DK == 128) ? QK_BYTES : QK_BYTES + 8192;
     static constexpr int NLD = 68;                        // fp32 row stride of N (16 B aligned rows)
-    static constexpr int OFF_N = OFF_P + 16384;           // N; diagonal blocks replaced by D_i
+    static constexpr int OFF_N = END_A;                   // N; diagonal blocks replaced by D_i
     static constexpr int AOLD = 20;                       // fp32 row stride of 16x16 scratch blocks
     static constexpr int OFF_AO = OFF_N + 64 * NLD * 4;   // 6 off-diagonal blocks of A
     static constexpr int OFF_XS = OFF_AO + 6 * 16 * AOLD * 4;   // 3 per-warp 16x16 scratch blocks
-    static constexpr int GSTRIDE = 9 * 64;                      // gate floats per parity slot
-    static constexpr int OFF_G = OFF_XS + 3 * 16 * AOLD * 4;    // gates [2] x 9 x 64 floats
-    static constexpr int OFF_OC = OFF_G + 2 * GSTRIDE * 4;      // chain copy of G_OC [2] x 64
-    static constexpr int OFF_BAR = OFF_OC + 2 * 64 * 4;
-    static constexpr int BYTES = OFF_BAR + 256;
+    static constexpr int OFF_G = OFF_XS + 3 * 16 * AOLD * 4;    // gate vectors (record part GB)
+    static constexpr int OFF_BAR = OFF_G + 2048;
+    static constexpr int BYTES = OFF_BAR + 64;
     static constexpr int ALLOC = BYTES + 1024;
-    static_assert(ALLOC <= 232448, "prefill shared memory exceeds 227 KB");
+    // the M=128 W^T MMA reads a second 64-row block of K^T at +16384 (unused lanes when DK = 64)
+    static_assert(DK == 128 || 8192 + 16384 + 8192 <= BYTES, "W^T operand window leaves shared memory");
+    static_assert(kPrepCtasPerSm * (ALLOC + 1024) <= 233472, "prep kernel does not fit 3 CTAs per SM");
 };
 
-// per-chunk gate vectors (floats), 9 x 64 per parity slot
-enum {
+// per-chunk gate vectors for the prep kernel (floats, 64 per entry), record part GB
+enum PrepGate {
     G_LAM2 = 0,   // Lambda_t * log2(e)
-    G_U = 1,      // 2^(l_t - m)
+    G_U = 1,      // 2^(l_t - m), m = Lambda_last * log2(e) / 2
     G_W = 2,      // 2^(m - l_t)
-    G_EDEC = 3,   // exp(Lambda_last - Lambda_t)
-    G_BM = 4,     // beta_t * mask_t
-    G_BME = 5,    // beta_t * mask_t * exp(Lambda_t)
-    G_OC = 6,     // mask_t * scale * exp(Lambda_t)   (output coefficient of Q S)
-    G_MK = 7,     // mask_t (0 for padding)
-    G_TOT = 8     // [0,1] per-warp scan totals, [2] gamma_c, [3] direct-exp fallback flag
+    G_BM = 3,     // beta_t * mask_t
+    G_BME = 4,    // beta_t * mask_t * exp(Lambda_t)
+    G_MK = 5,     // mask_t (0 for padding)
+    G_FLAG = 6,   // [0]: 1 when u_t * w_s could overflow (direct exp2 per element instead)
+    G_COUNT = 7
 };
+constexpr int kGateBytes = G_COUNT * 64 * 4;     // 1792, bulk-copied with the q/k tiles
 
-struct PrefillArgs {
+struct GateArgs {
     const void* a;
     const void* b;
     int gate_dtype;
@@ -119,17 +140,73 @@ struct PrefillArgs {
     float dt_bias;
     const float* dt_bias_vec;
     const float* mask;
-    const float* state_in;
-    float* state_out;
-    unsigned int* err;
-    int B, T, Hqk, Hv, dv, ntiles, layout;
+    uint8_t* rec;
+    int ntasks, T, Hv, nchunks;
     float scale;
 };
 
-struct Bars {
-    uint64_t qk_full[2], qk_free[2], v_full, v_free;
-    uint64_t qkk_done, uw_done, prep_done[2], chain_done[2];
-    uint64_t ws_done, st_done, wt_read;
+struct PrepArgs {
+    uint8_t* rec;
+    unsigned int* err;
+    int ntasks;          // B * Hv * ncp: the chunks [c0, c0 + ncp) of every sequence
+    int Hqk, Hv, nchunks, c0, ncp;
+    float scale;
+};
+
+// ---------------------------------------------------------------------------
+// chain kernel layout
+// ---------------------------------------------------------------------------
+constexpr int kChainThreads = 448;     // 14 warps
+constexpr int kChainTmemCols = 512;
+constexpr uint32_t C_ST = 0;           // S^T fp32 (DK columns)
+constexpr uint32_t C_SHI = 128;        // S^T bf16 hi, packed pairs (DK/2 columns)
+constexpr uint32_t C_SLO = 192;        // S^T bf16 lo
+// C_UT: 192 columns, one N=192 accumulator.
+//   [0, 64)    U^T from A1 hi, minus S_hi^T W_hi^T and S_lo^T W_hi^T
+//   [64, 128)  U^T from A1 lo, minus S_hi^T W_lo^T            (dV^T = [0,64) + [64,128))
+//   [128, 192) O^T: + S_hi^T Q~^T, then + dV^T P^T; read and reset to 0 by the output warps
+// After dV is formed, per 32-token group g, in place: dV'^T hi at 32g, lo at 32g + 16.
+constexpr uint32_t C_UT = 256;
+constexpr uint32_t C_O = C_UT + 128;
+constexpr uint32_t C_DVB = 448;        // dV^T bf16 (32 columns), A operand of dV^T P^T
+
+template <int DK>
+struct ChainSmem {
+    static constexpr int CB = DK / 64;
+    // one slot per chunk: K tile (TMA), W^T hi | W^T lo (record), q tile (TMA; rebuilt in place
+    // as Q~^T, so the three 64-column B blocks of the N=192 MMA are DK*128 bytes apart), P, gates
+    static constexpr int K_OFF = 0;
+    static constexpr int R_WTH = CB * 8192;
+    static constexpr int R_WTL = R_WTH + DK * 128;
+    static constexpr int Q_OFF = R_WTL + DK * 128;
+    static constexpr int R_P = Q_OFF + CB * 8192;
+    static constexpr int R_G = R_P + 8192;
+    static constexpr int SLOT_BYTES = R_G + 1024;
+    static constexpr int OFF_V = 2 * SLOT_BYTES;           // v tile, 2 blocks of 64 columns
+    static constexpr int OFF_A1 = OFF_V + 16384;           // A1 hi | lo
+    static constexpr int OFF_O = OFF_A1 + 16384;           // output staging, 2 x (2 blocks x 8 KB)
+    static constexpr int OFF_BAR = OFF_O + 32768;
+    static constexpr int BYTES = OFF_BAR + 256;
+    static constexpr int ALLOC = BYTES + 1024;
+    static_assert(R_WTL - R_WTH == DK * 128 && Q_OFF - R_WTL == DK * 128 && CB * 8192 == DK * 128,
+                  "the N=192 B operand needs equally spaced blocks");
+    static_assert(SLOT_BYTES % 1024 == 0, "slot images must stay 1024-aligned");
+    static_assert(ALLOC <= 232448, "chain kernel shared memory exceeds 227 KB");
+};
+
+struct ChainBars {
+    uint64_t slot_full[2], slot_free[2], va_full, va_free;
+    uint64_t split_half[2], qt_ready[2], ws_done, dv_done, st_done, pdv_done, o_free;
+};
+
+struct ChainArgs {
+    const uint8_t* rec;
+    const float* state_in;
+    float* state_out;
+    unsigned int* err;
+    int T, Hqk, Hv, dv, ntiles;
+    int nchunks_total;   // chunks of the whole sequence (record indexing)
+    int c0, nchunks;     // this launch walks chunks [c0, c0 + nchunks)
 };
 
 __device__ __forceinline__ void tmem_ld64(uint32_t taddr, float (&v)[64]) {
@@ -237,7 +314,7 @@ __device__ __forceinline__ void blk_load(float (&acc)[2][4], const float* src, i
 //        d) A30 = D3 (W30 + N32 A20)
 // ---------------------------------------------------------------------------
 template <int NLD, int AOLD>
-__device__ __forceinline__ void invert_unit_lower(float* Nsm, float* Ao, float* Xs, int pw, int lane) {
+__device__ __forceinline__ void invert_unit_lower(float* Nsm, float* Ao, float* Xs, int pw, int lane, int bar_id) {
     {
         const int r = lane >> 1, hf = lane & 1;
         const int row0 = 16 * pw;
@@ -265,7 +342,7 @@ __device__ __forceinline__ void invert_unit_lower(float* Nsm, float* Ao, float* 
         dst[0] = make_float4(x[0], x[1], x[2], x[3]);
         dst[1] = make_float4(x[4], x[5], x[6], x[7]);
     }
-    named_bar(BAR_PREP, 128);
+    named_bar(bar_id, 128);
     auto Nb = [&](int i, int j) { return Nsm + (16 * i) * NLD + 16 * j; };   // N_ij (i > j) or D_i (i == j)
     auto Ab = [&](int i, int j) { return Ao + ao_slot(i, j) * 16 * AOLD; };
     float* xs = Xs + (pw < 3 ? pw : 0) * 16 * AOLD;
@@ -286,7 +363,7 @@ __device__ __forceinline__ void invert_unit_lower(float* Nsm, float* Ao, float* 
         blk_mma_acc(acc, Nb(pw + 1, pw + 1), NLD, xs, AOLD, lane);
         blk_store(Ab(pw + 1, pw), AOLD, acc, lane);
     }
-    named_bar(BAR_PREP, 128);
+    named_bar(bar_id, 128);
     // c) warp 0: A20, warp 1: A31, warp 2: W30 (partial sum of A30's X)
     if (pw < 3) {
         const int i = (pw == 2) ? 3 : pw + 2, j = (pw == 2) ? 0 : pw, k = (pw == 2) ? 1 : pw + 1;
@@ -303,7 +380,7 @@ __device__ __forceinline__ void invert_unit_lower(float* Nsm, float* Ao, float* 
             blk_store(Ab(i, j), AOLD, acc, lane);
         }
     }
-    named_bar(BAR_PREP, 128);
+    named_bar(bar_id, 128);
     // d) A30 = D3 (W30 + N32 A20)
     if (pw == 0) {
         float acc[2][4];
@@ -315,53 +392,404 @@ __device__ __forceinline__ void invert_unit_lower(float* Nsm, float* Ao, float* 
         blk_mma_acc(acc2, Nb(3, 3), NLD, xs, AOLD, lane);
         blk_store(Ab(3, 0), AOLD, acc2, lane);
     }
-    named_bar(BAR_PREP, 128);
+    named_bar(bar_id, 128);
 }
 
+__device__ __forceinline__ uint8_t* align1024(uint8_t* p) {
+    return reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(p) + 1023) & ~uintptr_t(1023));
+}
+
+// ===========================================================================
+// Kernel 0: gate vectors of every chunk, one warp per (batch, value head, chunk)
+// (prefill_ref.py:49-64, 79-91): g_t = -exp(A_log) softplus(a_t + dt_bias),
+// beta_t = sigmoid(b_t) * mask_t, Lambda = in-chunk cumulative sum of g.
+// ===========================================================================
 template <int DK>
-__global__ void __launch_bounds__(kThreads, 1)
-prefill_chunk_kernel(const __grid_constant__ CUtensorMap map_q, const __grid_constant__ CUtensorMap map_k,
-                     const __grid_constant__ CUtensorMap map_v, const __grid_constant__ CUtensorMap map_o,
-                     const PrefillArgs args) {
-    using L = PrefillSmem<DK>;
-    extern __shared__ uint8_t smem_raw[];
-    uint8_t* sm = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
-    Bars* bars = reinterpret_cast<Bars*>(sm + L::OFF_BAR);
-    uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(sm + L::OFF_BAR + sizeof(Bars));
+__global__ void __launch_bounds__(128)
+prefill_gates_kernel(const GateArgs args) {
+    using R = Rec<DK>;
+    constexpr float kLog2e = 1.4426950408889634f;
+    const int lane = threadIdx.x & 31;
+    const int task = blockIdx.x * 4 + (threadIdx.x >> 5);
+    if (task >= args.ntasks) return;
+    const int T = args.T;
+    const int bh = task / args.nchunks, c = task - bh * args.nchunks;
+    const int h = bh % args.Hv, bidx = bh / args.Hv;
+    const long base = static_cast<long>(bh) * T;
+    const int t0 = 2 * lane;
+    const int tok = c * kC + t0;
+    float a0 = 0.f, a1 = 0.f, b0 = 0.f, b1 = 0.f, m0 = 0.f, m1 = 0.f;
+    if (tok < T) {
+        a0 = load_gate(args.a, base + tok, args.gate_dtype);
+        b0 = load_gate(args.b, base + tok, args.gate_dtype);
+        m0 = args.mask ? args.mask[static_cast<long>(bidx) * T + tok] : 1.f;
+    }
+    if (tok + 1 < T) {
+        a1 = load_gate(args.a, base + tok + 1, args.gate_dtype);
+        b1 = load_gate(args.b, base + tok + 1, args.gate_dtype);
+        m1 = args.mask ? args.mask[static_cast<long>(bidx) * T + tok + 1] : 1.f;
+    }
+    const float A_neg = -expf(args.A_log[h]);
+    const float dtb = args.dt_bias_vec ? args.dt_bias_vec[h] : args.dt_bias;
+    float lg0 = 0.f, lg1 = 0.f, bm0 = 0.f, bm1 = 0.f;
+    if (tok < T) {
+        lg0 = A_neg * softplus_f(a0 + dtb);
+        bm0 = sigmoid_f(b0) * m0;
+    }
+    if (tok + 1 < T) {
+        lg1 = A_neg * softplus_f(a1 + dtb);
+        bm1 = sigmoid_f(b1) * m1;
+    }
+    float sc = lg0 + lg1;
+#pragma unroll
+    for (int o = 1; o < 32; o <<= 1) {
+        const float y = __shfl_up_sync(0xffffffffu, sc, o);
+        if (lane >= o) sc += y;
+    }
+    const float ll2 = __shfl_sync(0xffffffffu, sc, 31) * kLog2e;
+    const float m2 = 0.5f * ll2;
+    const float l21 = sc * kLog2e, l20 = (sc - lg1) * kLog2e;
+    const float el0 = ex2_approx(l20), el1 = ex2_approx(l21);
+    uint8_t* rec = args.rec + static_cast<long>(task) * R::BYTES;
+    float* g = reinterpret_cast<float*>(rec + R::GB);
+    *reinterpret_cast<float2*>(g + G_LAM2 * 64 + t0) = make_float2(l20, l21);
+    *reinterpret_cast<float2*>(g + G_U * 64 + t0) = make_float2(ex2_approx(l20 - m2), ex2_approx(l21 - m2));
+    *reinterpret_cast<float2*>(g + G_W * 64 + t0) = make_float2(ex2_approx(m2 - l20), ex2_approx(m2 - l21));
+    *reinterpret_cast<float2*>(g + G_BM * 64 + t0) = make_float2(bm0, bm1);
+    *reinterpret_cast<float2*>(g + G_BME * 64 + t0) = make_float2(bm0 * el0, bm1 * el1);
+    *reinterpret_cast<float2*>(g + G_MK * 64 + t0) = make_float2(m0, m1);
+    *reinterpret_cast<float2*>(g + G_FLAG * 64 + t0) =
+        make_float2(lane == 0 && ll2 < -240.f ? 1.f : 0.f, 0.f);          // u_t * w_s could overflow
+    float* G = reinterpret_cast<float*>(rec + R::G);
+    *reinterpret_cast<float2*>(G + t0) = make_float2(m0 * args.scale * el0, m1 * args.scale * el1);
+    *reinterpret_cast<float2*>(G + 64 + t0) = make_float2(ex2_approx(ll2 - l20), ex2_approx(ll2 - l21));
+    if (lane == 0) G[128] = ex2_approx(ll2);                              // gamma_c
+}
+
+// ===========================================================================
+// Kernel 1: per-chunk preparation, all chunks in parallel
+// ===========================================================================
+// One prep worker: 128 threads (tid 0..127) with their own shared memory
+// (PrepSmem at `sm`, 1024-aligned), 128 TMEM columns and named barrier
+// `bar_id`; it takes tasks vblock, vblock + vgrid, ...
+template <int DK>
+__device__ __forceinline__ void prep_body(const CUtensorMap* map_q, const CUtensorMap* map_k, const PrepArgs& args,
+                                          uint8_t* sm, const int tid, const int vblock, const int vgrid,
+                                          const int bar_id, const bool relinquish) {
+    using L = PrepSmem<DK>;
+    using R = Rec<DK>;
+    uint64_t* bar_qk = reinterpret_cast<uint64_t*>(sm + L::OFF_BAR);      // q/k tiles landed
+    uint64_t* bar_qkk = bar_qk + 1;                                        // [Q;K] K^T done
+    uint64_t* bar_w = bar_qk + 2;                                          // W^T done
+    uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bar_qk + 3);
     volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
     float* Nsm = reinterpret_cast<float*>(sm + L::OFF_N);
     float* Ao = reinterpret_cast<float*>(sm + L::OFF_AO);
     float* Xs = reinterpret_cast<float*>(sm + L::OFF_XS);
-    float* gates = reinterpret_cast<float*>(sm + L::OFF_G);
-    float* ocbuf = reinterpret_cast<float*>(sm + L::OFF_OC);
+    const float* gates = reinterpret_cast<const float*>(sm + L::OFF_G);
+
+    const int warp = tid >> 5;
+    const int lane = tid & 31;
+    const int pw = warp;
+    const uint32_t lane_off = static_cast<uint32_t>(warp) << 21;
+    const bool leader = (tid == 32);                    // MMA/TMA issuer: not on the gate warp
+    const int nchunks = args.nchunks;
+    const int group = args.Hv / args.Hqk;
+    const float scale = args.scale;
+    unsigned int* err = args.err;
+
+    if (tid == 0) {
+        mbar_init(bar_qk, 1);
+        mbar_init(bar_qkk, 1);
+        mbar_init(bar_w, 1);
+        *abort_flag = 0;
+        fence_mbar_init();
+        tma_prefetch_desc(map_q);
+        tma_prefetch_desc(map_k);
+    }
+    if (warp == 0) {
+        tmem_alloc(tmem_slot, kPrepTmemCols);
+        if (relinquish) tmem_relinquish();
+    }
+    tc_fence_before();
+    named_bar(bar_id, kPrepThreads);
+    tc_fence_after();
+    const uint32_t tmem = *tmem_slot;
+
+    // q/k tiles and the gate vectors of `task` -> shared memory, completing on bar_qk
+    auto issue_qk = [&](int task) {
+        const int bh = task / args.ncp, c = args.c0 + (task - bh * args.ncp);
+        const int hq = (bh % args.Hv) / group, bidx = bh / args.Hv;
+        mbar_arrive_expect_tx(bar_qk, 2 * L::CB * 8192 + kGateBytes);
+#pragma unroll
+        for (int cb = 0; cb < L::CB; ++cb) {
+            tma_load_4d(sm + cb * 16384, map_q, bar_qk, cb * 64, c * kC, hq, bidx);
+            tma_load_4d(sm + cb * 16384 + 8192, map_k, bar_qk, cb * 64, c * kC, hq, bidx);
+        }
+        bulk_load(sm + L::OFF_G, args.rec + (static_cast<long>(bh) * nchunks + c) * R::BYTES + R::GB, kGateBytes,
+                  bar_qk);
+    };
+    if (leader && vblock < args.ntasks) issue_qk(vblock);
+
+    int it = 0;
+#pragma unroll 1
+    for (int task = vblock; task < args.ntasks; task += vgrid, ++it) {
+        const uint32_t ph = it & 1;
+        const int tbh = task / args.ncp;
+        uint8_t* rec = args.rec + (static_cast<long>(tbh) * nchunks + args.c0 + (task - tbh * args.ncp)) * R::BYTES;
+        const float* g = gates;                           // this task's gate vectors (landed with q/k)
+
+        // ---- [Q;K] K^T on tensor cores
+        mbar_wait_or_abort(bar_qk, ph, err, abort_flag);
+        if (leader && !*abort_flag) {
+            tc_fence_after();
+            const uint32_t sqk = smem_u32(sm);
+            constexpr uint32_t id64 = idesc_bf16(128, 64, false, false);
+#pragma unroll
+            for (int kk = 0; kk < DK / 16; ++kk) {
+                const uint32_t o = (kk >> 2) * 16384 + (kk & 3) * 32;
+                umma_bf16_ss(tmem + P_COL_QKK, sdesc_sw128(sqk + o, 16, 1024),
+                             sdesc_sw128(sqk + o + 8192, 16, 1024), id64, kk > 0);
+            }
+            umma_commit(bar_qkk);
+        }
+
+        const bool direct = g[G_FLAG * 64] != 0.f;
+        mbar_wait_or_abort(bar_qkk, ph, err, abort_flag);
+        tc_fence_after();
+
+        // ---- P (lanes 0-63) -> image over the dead q block 0 (bulk-stored to the record),
+        //      N (lanes 64-127) -> shared; lower triangle only
+        {
+            float row[64];
+            tmem_ld64(tmem + lane_off + P_COL_QKK, row);
+            const float* gw = g + G_W * 64;
+            const float* gl2 = g + G_LAM2 * 64;
+            if (tid < kC) {
+                const int t = tid;
+                const float coef = scale * g[G_MK * 64 + t];
+                const float cu = coef * g[G_U * 64 + t];
+                const float lt = gl2[t];
+                uint8_t* prow = sm + L::OFF_A2H;
+#pragma unroll
+                for (int ch = 0; ch < 8; ++ch) {
+                    uint4 w4 = make_uint4(0u, 0u, 0u, 0u);
+                    if (8 * ch <= t) {
+                        float e[8];
+                        if (!direct) {
+#pragma unroll
+                            for (int u = 0; u < 8; ++u) e[u] = (8 * ch + u <= t) ? row[8 * ch + u] * (cu * gw[8 * ch + u]) : 0.f;
+                        } else {
+#pragma unroll
+                            for (int u = 0; u < 8; ++u)
+                                e[u] = (8 * ch + u <= t) ? row[8 * ch + u] * (coef * ex2_approx(lt - gl2[8 * ch + u])) : 0.f;
+                        }
+                        w4 = pack8(e);
+                    }
+                    *reinterpret_cast<uint4*>(prow + sw128_chunk(t, ch)) = w4;
+                }
+            } else {
+                const int t = tid - kC;
+                const float coef = -g[G_BM * 64 + t];
+                const float cu = coef * g[G_U * 64 + t];
+                const float lt = gl2[t];
+                float* nrow = Nsm + t * L::NLD;
+                const int send = (t | 15) + 1;             // through the end of t's diagonal block
+#pragma unroll
+                for (int s4 = 0; s4 < 16; ++s4) {
+                    if (4 * s4 < send) {
+                        float o4[4];
+                        if (!direct) {
+#pragma unroll
+                            for (int u = 0; u < 4; ++u) o4[u] = (4 * s4 + u < t) ? row[4 * s4 + u] * (cu * gw[4 * s4 + u]) : 0.f;
+                        } else {
+#pragma unroll
+                            for (int u = 0; u < 4; ++u)
+                                o4[u] = (4 * s4 + u < t) ? row[4 * s4 + u] * (coef * ex2_approx(lt - gl2[4 * s4 + u])) : 0.f;
+                        }
+                        *reinterpret_cast<float4*>(nrow + 4 * s4) = make_float4(o4[0], o4[1], o4[2], o4[3]);
+                    }
+                }
+            }
+        }
+        fence_async_smem();
+        tc_fence_before();
+        named_bar(bar_id, kPrepThreads);
+        if (leader) {
+            bulk_store(rec + R::P, sm + L::OFF_A2H, 8192);
+            bulk_commit();
+        }
+
+        // ---- A = (I - N)^-1
+        invert_unit_lower<L::NLD, L::AOLD>(Nsm, Ao, Xs, pw, lane, bar_id);
+
+        // ---- A1 = A diag(beta'), A2 = A diag(beta' e^Lambda), bf16 hi/lo images (rows [t][s]):
+        //      computed into registers, then A2 over the q blocks (W MMA operand) and A1 over
+        //      N (bulk-stored to the record) once every thread has read N and the off-diagonal blocks
+        {
+            const int t = tid >> 1, hf = tid & 1;
+            const int ib = t >> 4, r = t & 15;
+            const float* bm = g + G_BM * 64;
+            const float* bme = g + G_BME * 64;
+            uint4 h1[4], l1[4], h2[4], l2[4];
+#pragma unroll
+            for (int ch = 0; ch < 4; ++ch) {
+                const int s0 = 32 * hf + 8 * ch;
+                h1[ch] = l1[ch] = h2[ch] = l2[ch] = make_uint4(0u, 0u, 0u, 0u);
+                if (s0 <= t) {
+                    const int jb = s0 >> 4;
+                    const float* src = (jb == ib) ? Nsm + t * L::NLD + s0
+                                                  : Ao + ao_slot(ib, jb) * 16 * L::AOLD + r * L::AOLD + (s0 & 15);
+                    const float4 x0 = *reinterpret_cast<const float4*>(src);
+                    const float4 x1 = *reinterpret_cast<const float4*>(src + 4);
+                    const float xv[8] = {x0.x, x0.y, x0.z, x0.w, x1.x, x1.y, x1.z, x1.w};
+                    float e1[8], e2[8];
+#pragma unroll
+                    for (int u = 0; u < 8; ++u) {
+                        const float xa = (s0 + u <= t) ? xv[u] : 0.f;
+                        e1[u] = xa * bm[s0 + u];
+                        e2[u] = xa * bme[s0 + u];
+                    }
+                    split8(e1, h1[ch], l1[ch]);
+                    split8(e2, h2[ch], l2[ch]);
+                }
+            }
+            if (leader) bulk_wait_read0();                // the P image has left the q block
+            named_bar(bar_id, kPrepThreads);              // N and the A blocks are no longer read
+            uint8_t* a1 = reinterpret_cast<uint8_t*>(Nsm);
+#pragma unroll
+            for (int ch = 0; ch < 4; ++ch) {
+                const uint32_t off = sw128_chunk(t, 4 * hf + ch);
+                *reinterpret_cast<uint4*>(a1 + off) = h1[ch];
+                *reinterpret_cast<uint4*>(a1 + 8192 + off) = l1[ch];
+                *reinterpret_cast<uint4*>(sm + L::OFF_A2H + off) = h2[ch];
+                *reinterpret_cast<uint4*>(sm + L::OFF_A2L + off) = l2[ch];
+            }
+        }
+        fence_async_smem();
+        tc_fence_before();
+        named_bar(bar_id, kPrepThreads);
+        if (leader) {
+            bulk_store(rec + R::A1H, Nsm, 16384);
+            bulk_commit();
+        }
+
+        // ---- W^T = K^T A2^T (K as MN-major A, A2 as K-major B), 2 split terms
+        if (leader && !*abort_flag) {
+            tc_fence_after();
+            const uint32_t sk = smem_u32(sm) + 8192;
+            constexpr uint32_t id_mn = idesc_bf16(128, 64, true, false);
+#pragma unroll
+            for (int p = 0; p < 2; ++p) {
+                const uint32_t b2 = smem_u32(sm + (p ? L::OFF_A2L : L::OFF_A2H));
+#pragma unroll
+                for (int kk = 0; kk < 4; ++kk)
+                    umma_bf16_ss(tmem + P_COL_WT, sdesc_sw128(sk + kk * 2048, 16384, 1024),
+                                 sdesc_sw128(b2 + kk * 32, 16, 1024), id_mn, (p > 0 || kk > 0) ? 1u : 0u);
+            }
+            umma_commit(bar_w);
+        }
+        mbar_wait_or_abort(bar_w, ph, err, abort_flag);
+        tc_fence_after();
+
+        // ---- W^T rows (lane d) -> bf16 hi/lo images over the dead q/k tiles -> record
+        if (tid < DK) {
+            float row[64];
+            tmem_ld64(tmem + lane_off + P_COL_WT, row);
+            store_row_split(sm, sm + DK * 128, tid, row);
+        }
+        fence_async_smem();
+        tc_fence_before();
+        named_bar(bar_id, kPrepThreads);
+        bool pending = false;
+        if (leader) {
+            bulk_store(rec + R::WTH, sm, 2 * DK * 128);
+            bulk_commit();
+            bulk_wait_read0();                        // the images (and A1 over N) have been read out
+            // q/k shared memory is free: fetch the next task's tiles
+            if (!*abort_flag && task + vgrid < args.ntasks) {
+                issue_qk(task + vgrid);
+                pending = true;
+            }
+        }
+        named_bar(bar_id, kPrepThreads);
+        if (*abort_flag) {
+            if (pending) mbar_wait(bar_qk, ph ^ 1u, err);   // let the issued copy land before exiting
+            break;
+        }
+    }
+
+    if (leader) bulk_wait_all0();                      // record stores complete before the worker ends
+    tc_fence_before();
+    named_bar(bar_id, kPrepThreads);
+    if (warp == 0) tmem_dealloc(tmem, kPrepTmemCols);
+}
+
+template <int DK>
+__global__ void __launch_bounds__(kPrepThreads, kPrepCtasPerSm)
+prefill_prep_kernel(const __grid_constant__ CUtensorMap map_q, const __grid_constant__ CUtensorMap map_k,
+                    const PrepArgs args) {
+    extern __shared__ uint8_t smem_raw[];
+    prep_body<DK>(&map_q, &map_k, args, align1024(smem_raw), threadIdx.x, blockIdx.x, gridDim.x, BAR_PREP, true);
+}
+
+// ===========================================================================
+// Kernel 2: the sequential state recurrence, one CTA per (b, h, value tile)
+// ===========================================================================
+// One chain CTA (all 448 threads), working on (b, h, value tile) number `cta`.
+template <int DK>
+__device__ __forceinline__ void chain_body(const CUtensorMap* map_q, const CUtensorMap* map_k,
+                                           const CUtensorMap* map_v, const CUtensorMap* map_o, const ChainArgs& args,
+                                           uint8_t* sm, const int cta) {
+    using L = ChainSmem<DK>;
+    using R = Rec<DK>;
+    constexpr int HALF = DK / 2;                   // key columns per state-path thread group
+    constexpr int NBLK = HALF / 32;                // 32-column split blocks per group
+    ChainBars* bars = reinterpret_cast<ChainBars*>(sm + L::OFF_BAR);
+    uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(sm + L::OFF_BAR + sizeof(ChainBars));
+    volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
 
     const int tid = threadIdx.x;
     const int warp = tid >> 5;
     const int lane = tid & 31;
-    const int tile = blockIdx.x % args.ntiles;
-    const int bh = blockIdx.x / args.ntiles;       // b * Hv + h
+    const int tile = cta % args.ntiles;
+    const int bh = cta / args.ntiles;              // b * Hv + h
     const int h = bh % args.Hv;
     const int bidx = bh / args.Hv;
     const int hq = h / (args.Hv / args.Hqk);
-    const int T = args.T;
-    const int nchunks = (T + kC - 1) / kC;
+    const int nchunks = args.nchunks;
     const int v0 = tile * 128;
     const int dv_valid = min(128, args.dv - v0);
     const int nvb = (dv_valid + 63) / 64;
     unsigned int* err = args.err;
+    const int c0 = args.c0;
+    const uint8_t* rec0 = args.rec + (static_cast<long>(bh) * args.nchunks_total + c0) * R::BYTES;
 
     if (tid == 0) {
-        uint64_t* all = reinterpret_cast<uint64_t*>(bars);
-        for (int i = 0; i < static_cast<int>(sizeof(Bars) / 8); ++i) mbar_init(&all[i], 1);
+        mbar_init(&bars->slot_full[0], 1);
+        mbar_init(&bars->slot_full[1], 1);
+        mbar_init(&bars->slot_free[0], 2);         // MMA commit + output warps (Q~^T built)
+        mbar_init(&bars->slot_free[1], 2);
+        mbar_init(&bars->va_full, 1);
+        mbar_init(&bars->va_free, 1);
+        mbar_init(&bars->split_half[0], 256);
+        mbar_init(&bars->split_half[1], 256);
+        mbar_init(&bars->qt_ready[0], 1);          // per slot: the output warps run a chunk ahead
+        mbar_init(&bars->qt_ready[1], 1);
+        mbar_init(&bars->ws_done, 1);
+        mbar_init(&bars->dv_done, 256);
+        mbar_init(&bars->st_done, 1);
+        mbar_init(&bars->pdv_done, 1);
+        mbar_init(&bars->o_free, 128);
         *abort_flag = 0;
         fence_mbar_init();
-        tma_prefetch_desc(&map_q);
-        tma_prefetch_desc(&map_k);
-        tma_prefetch_desc(&map_v);
-        tma_prefetch_desc(&map_o);
+        tma_prefetch_desc(map_q);
+        tma_prefetch_desc(map_k);
+        tma_prefetch_desc(map_v);
+        tma_prefetch_desc(map_o);
     }
     if (warp == 0) {
-        tmem_alloc(tmem_slot, kTmemCols);
+        tmem_alloc(tmem_slot, kChainTmemCols);
         tmem_relinquish();
     }
     tc_fence_before();
@@ -370,463 +798,472 @@ prefill_chunk_kernel(const __grid_constant__ CUtensorMap map_q, const __grid_con
     const uint32_t tmem = *tmem_slot;
 
     if (warp == 0) {
-        // ======================= TMA producer (lane 0: q/k ring, lane 1: v)
+        // ======================= producer: lane 0 the per-chunk slot, lane 1 V and A1
         if (lane == 0) {
             for (int c = 0; c < nchunks; ++c) {
                 const int slot = c & 1;
-                if (c >= 2 && !mbar_wait_or_abort(&bars->qk_free[slot], ((c >> 1) - 1) & 1, err, abort_flag)) break;
-                uint8_t* dst = sm + (slot ? L::OFF_QK1 : L::OFF_QK0);
-                mbar_arrive_expect_tx(&bars->qk_full[slot], 2 * L::CB * 8192);
+                if (c >= 2 && !mbar_wait_or_abort(&bars->slot_free[slot], ((c >> 1) - 1) & 1, err, abort_flag)) break;
+                uint8_t* dst = sm + slot * L::SLOT_BYTES;
+                const uint8_t* rec = rec0 + static_cast<long>(c) * R::BYTES;
+                mbar_arrive_expect_tx(&bars->slot_full[slot], 2 * L::CB * 8192 + 2 * DK * 128 + 8192 + 1024);
 #pragma unroll
                 for (int cb = 0; cb < L::CB; ++cb) {
-                    tma_load_4d(dst + cb * 16384, &map_q, &bars->qk_full[slot], cb * 64, c * kC, hq, bidx);
-                    tma_load_4d(dst + cb * 16384 + 8192, &map_k, &bars->qk_full[slot], cb * 64, c * kC, hq, bidx);
+                    tma_load_4d(dst + L::Q_OFF + cb * 8192, map_q, &bars->slot_full[slot], cb * 64, (c0 + c) * kC, hq,
+                                bidx);
+                    tma_load_4d(dst + L::K_OFF + cb * 8192, map_k, &bars->slot_full[slot], cb * 64, (c0 + c) * kC, hq,
+                                bidx);
                 }
+                bulk_load(dst + L::R_WTH, rec + R::WTH, 2 * DK * 128, &bars->slot_full[slot]);
+                bulk_load(dst + L::R_P, rec + R::P, 8192 + 1024, &bars->slot_full[slot]);
             }
         } else if (lane == 1) {
             for (int c = 0; c < nchunks; ++c) {
-                if (c >= 1 && !mbar_wait_or_abort(&bars->v_free, (c - 1) & 1, err, abort_flag)) break;
-                mbar_arrive_expect_tx(&bars->v_full, nvb * 8192);
+                if (c >= 1 && !mbar_wait_or_abort(&bars->va_free, (c - 1) & 1, err, abort_flag)) break;
+                mbar_arrive_expect_tx(&bars->va_full, nvb * 8192 + 16384);
                 for (int vb = 0; vb < nvb; ++vb)
-                    tma_load_4d(sm + L::OFF_V + vb * 8192, &map_v, &bars->v_full, v0 + vb * 64, c * kC, h, bidx);
+                    tma_load_4d(sm + L::OFF_V + vb * 8192, map_v, &bars->va_full, v0 + vb * 64, (c0 + c) * kC, h, bidx);
+                bulk_load(sm + L::OFF_A1, rec0 + static_cast<long>(c) * R::BYTES + R::A1H, 16384, &bars->va_full);
             }
         }
-    } else if (warp <= 4) {
-        // ======================= PREP warpgroup
-        const int pt = tid - 32;                           // 0..127
-        const int pw = pt >> 5;                            // 0..3
-        const int tl = ((warp & 3) << 5) | lane;           // TMEM lane of this thread
-        const uint32_t lane_off = static_cast<uint32_t>(warp & 3) << 21;   // (32*(warp%4)) << 16
-        const bool leader = (pt == 32);                    // MMA issuer: not on the gate warp (pw == 0)
-        const float A_neg = -expf(args.A_log[h]);
-        const float dtb = args.dt_bias_vec ? args.dt_bias_vec[h] : args.dt_bias;
-        const float scale = args.scale;
-        const long gate_base = static_cast<long>(bh) * T;
-        constexpr float kLog2e = 1.4426950408889634f;
-        // gate inputs (two tokens per lane of warp pw == 0), loaded one chunk ahead
-        float pa0 = 0.f, pa1 = 0.f, pb0 = 0.f, pb1 = 0.f, pm0 = 0.f, pm1 = 0.f;
-        auto load_gates = [&](int cc) {
-            const int tok = cc * kC + 2 * lane;
-            pa0 = pa1 = pb0 = pb1 = pm0 = pm1 = 0.f;
-            if (pw == 0 && cc < nchunks) {
-                if (tok < T) {
-                    pa0 = load_gate(args.a, gate_base + tok, args.gate_dtype);
-                    pb0 = load_gate(args.b, gate_base + tok, args.gate_dtype);
-                    pm0 = args.mask ? args.mask[static_cast<long>(bidx) * T + tok] : 1.f;
-                }
-                if (tok + 1 < T) {
-                    pa1 = load_gate(args.a, gate_base + tok + 1, args.gate_dtype);
-                    pb1 = load_gate(args.b, gate_base + tok + 1, args.gate_dtype);
-                    pm1 = args.mask ? args.mask[static_cast<long>(bidx) * T + tok + 1] : 1.f;
-                }
+    } else if (warp == 1) {
+        // ======================= MMA issuer (one thread)
+        if (lane == 0) {
+            const uint32_t sv = smem_u32(sm + L::OFF_V);
+            const uint32_t sa1 = smem_u32(sm + L::OFF_A1);
+            // [U_h^T | U_l^T] = V^T [A1_hi^T | A1_lo^T] into C_UT: V as MN-major A, the
+            // two A1 parts as one K-major B of 128 rows (N = 128)
+            auto issue_u = [&]() {
+                constexpr uint32_t id_u = idesc_bf16(128, 128, true, false);
+#pragma unroll
+                for (int kk = 0; kk < 4; ++kk)
+                    umma_bf16_ss(tmem + C_UT, sdesc_sw128(sv + kk * 2048, 8192, 1024),
+                                 sdesc_sw128(sa1 + kk * 32, 16, 1024), id_u, kk > 0 ? 1u : 0u);
+                umma_commit(&bars->va_free);
+            };
+            if (mbar_spin_or_abort(&bars->va_full, 0, err, abort_flag) && !*abort_flag) {
+                tc_fence_after();
+                issue_u();
             }
-        };
-        load_gates(0);
 #pragma unroll 1
-        for (int c = 0; c < nchunks; ++c) {
-            const int par = c & 1;
-            float* g = gates + par * L::GSTRIDE;
-            if (c >= 2) mbar_wait_or_abort(&bars->chain_done[par], ((c >> 1) - 1) & 1, err, abort_flag);
-
-            // ---- [Q;K] K^T on tensor cores (overlaps the gate computation below)
-            mbar_wait_or_abort(&bars->qk_full[par], (c >> 1) & 1, err, abort_flag);
-            uint8_t* qk_s = sm + (par ? L::OFF_QK1 : L::OFF_QK0);
-            if (leader && !*abort_flag) {
-                tc_fence_after();
-                const uint32_t sqk = smem_u32(qk_s);
-                constexpr uint32_t id64 = idesc_bf16(128, 64, false, false);
+            for (int c = 0; c < nchunks; ++c) {
+                const int slot = c & 1;
+                const uint32_t sbase = smem_u32(sm + slot * L::SLOT_BYTES);
+                const uint32_t sk = sbase + L::K_OFF, swt = sbase + L::R_WTH;
+                mbar_spin_or_abort(&bars->slot_full[slot], (c >> 1) & 1, err, abort_flag);
+                mbar_spin_or_abort(&bars->qt_ready[slot], (c >> 1) & 1, err, abort_flag);
+                if (c >= 1) mbar_spin_or_abort(&bars->o_free, (c - 1) & 1, err, abort_flag);
+                // [U_h^T - S^T W_hi^T | U_l^T - S_hi^T W_lo^T | O^T + S_hi^T Q~^T], B negated:
+                // S_hi^T [W_hi^T | W_lo^T | -Q~^T] is one N=192 MMA (three MN-major 64-column
+                // blocks LBO apart, Q~ = -diag(oc) Q built in place by the output warps), then
+                // S_lo^T W_hi^T into the first 64 columns.  Issued per split block as S^T
+                // hi/lo arrive from the state-path threads.
+                constexpr uint32_t id_w3 = idesc_bf16(128, 192, false, true) | (1u << 14);
+                constexpr uint32_t id_w1 = idesc_bf16(128, 64, false, true) | (1u << 14);
 #pragma unroll
-                for (int kk = 0; kk < DK / 16; ++kk) {
-                    const uint32_t o = (kk >> 2) * 16384 + (kk & 3) * 32;
-                    umma_bf16_ss(tmem + COL_QKK, sdesc_sw128(sqk + o, 16, 1024),
-                                 sdesc_sw128(sqk + o + 8192, 16, 1024), id64, kk > 0);
-                }
-                umma_commit(&bars->qkk_done);
-            }
-
-            // ---- gates (prefill_ref.py:49-64, 79-91) on one warp, two tokens per lane
-            if (pw == 0) {
-                const int t0 = 2 * lane;
-                const int tok = c * kC + t0;
-                float lg0 = 0.f, lg1 = 0.f, bm0 = 0.f, bm1 = 0.f;
-                if (tok < T) {
-                    lg0 = A_neg * softplus_fast(pa0 + dtb);
-                    bm0 = sigmoid_fast(pb0) * pm0;
-                }
-                if (tok + 1 < T) {
-                    lg1 = A_neg * softplus_fast(pa1 + dtb);
-                    bm1 = sigmoid_fast(pb1) * pm1;
-                }
-                float sc = lg0 + lg1;
+                for (int blk = 0; blk < NBLK; ++blk) {
+                    mbar_spin_or_abort(&bars->split_half[blk], c & 1, err, abort_flag);
+                    tc_fence_after();
+                    if (!*abort_flag) {
 #pragma unroll
-                for (int o = 1; o < 32; o <<= 1) {
-                    const float y = __shfl_up_sync(0xffffffffu, sc, o);
-                    if (lane >= o) sc += y;
-                }
-                const float ll2 = __shfl_sync(0xffffffffu, sc, 31) * kLog2e;
-                const float m2 = 0.5f * ll2;
-                const float l21 = sc * kLog2e, l20 = (sc - lg1) * kLog2e;
-                const float el0 = ex2_approx(l20), el1 = ex2_approx(l21);
-                *reinterpret_cast<float2*>(g + G_LAM2 * 64 + t0) = make_float2(l20, l21);
-                *reinterpret_cast<float2*>(g + G_U * 64 + t0) = make_float2(ex2_approx(l20 - m2), ex2_approx(l21 - m2));
-                *reinterpret_cast<float2*>(g + G_W * 64 + t0) = make_float2(ex2_approx(m2 - l20), ex2_approx(m2 - l21));
-                *reinterpret_cast<float2*>(g + G_EDEC * 64 + t0) =
-                    make_float2(ex2_approx(ll2 - l20), ex2_approx(ll2 - l21));
-                *reinterpret_cast<float2*>(g + G_BM * 64 + t0) = make_float2(bm0, bm1);
-                *reinterpret_cast<float2*>(g + G_BME * 64 + t0) = make_float2(bm0 * el0, bm1 * el1);
-                *reinterpret_cast<float2*>(g + G_OC * 64 + t0) = make_float2(pm0 * scale * el0, pm1 * scale * el1);
-                *reinterpret_cast<float2*>(g + G_MK * 64 + t0) = make_float2(pm0, pm1);
-                if (lane == 0) {
-                    g[G_TOT * 64 + 2] = ex2_approx(ll2);                  // gamma_c
-                    g[G_TOT * 64 + 3] = (ll2 < -240.f) ? 1.f : 0.f;        // u_t * w_s could overflow
-                }
-                load_gates(c + 1);                         // prefetch the next chunk's gate inputs
-            }
-            named_bar(BAR_PREP, 128);      // gate vectors complete
-            const bool direct = g[G_TOT * 64 + 3] != 0.f;
-            mbar_wait_or_abort(&bars->qkk_done, c & 1, err, abort_flag);
-            tc_fence_after();
-
-            // ---- P (lanes 0-63) and N (lanes 64-127): only the lower triangle is computed
-            {
-                float row[64];
-                tmem_ld64(tmem + lane_off + COL_QKK, row);
-                const float* gw = g + G_W * 64;
-                const float* gl2 = g + G_LAM2 * 64;
-                if (tl < kC) {
-                    const int t = tl;
-                    const float coef = scale * g[G_MK * 64 + t];
-                    const float cu = coef * g[G_U * 64 + t];
-                    const float lt = gl2[t];
-                    uint8_t* prow = sm + L::OFF_P + par * 8192;
+                        for (int g2 = 0; g2 < 2; ++g2) {
 #pragma unroll
-                    for (int ch = 0; ch < 8; ++ch) {
-                        uint4 w4 = make_uint4(0u, 0u, 0u, 0u);
-                        if (8 * ch <= t) {
-                            float e[8];
-                            if (!direct) {
-#pragma unroll
-                                for (int u = 0; u < 8; ++u) e[u] = (8 * ch + u <= t) ? row[8 * ch + u] * (cu * gw[8 * ch + u]) : 0.f;
-                            } else {
-#pragma unroll
-                                for (int u = 0; u < 8; ++u)
-                                    e[u] = (8 * ch + u <= t) ? row[8 * ch + u] * (coef * ex2_approx(lt - gl2[8 * ch + u])) : 0.f;
+                            for (int k2 = 0; k2 < 2; ++k2) {
+                                const int kk = (g2 * HALF + blk * 32) / 16 + k2;
+                                umma_bf16_ts(tmem + C_UT, tmem + C_SHI + kk * 8,
+                                             sdesc_sw128(swt + kk * 2048, DK * 128, 1024), id_w3, 1u);
                             }
-                            w4 = pack8(e);
                         }
-                        *reinterpret_cast<uint4*>(prow + sw128_chunk(t, ch)) = w4;
-                    }
-                } else {
-                    const int t = tl - kC;
-                    const float coef = -g[G_BM * 64 + t];
-                    const float cu = coef * g[G_U * 64 + t];
-                    const float lt = gl2[t];
-                    float* nrow = Nsm + t * L::NLD;
-                    const int send = (t | 15) + 1;         // through the end of t's diagonal block
 #pragma unroll
-                    for (int s4 = 0; s4 < 16; ++s4) {
-                        if (4 * s4 < send) {
-                            float o4[4];
-                            if (!direct) {
+                        for (int g2 = 0; g2 < 2; ++g2) {
 #pragma unroll
-                                for (int u = 0; u < 4; ++u) o4[u] = (4 * s4 + u < t) ? row[4 * s4 + u] * (cu * gw[4 * s4 + u]) : 0.f;
-                            } else {
-#pragma unroll
-                                for (int u = 0; u < 4; ++u)
-                                    o4[u] = (4 * s4 + u < t) ? row[4 * s4 + u] * (coef * ex2_approx(lt - gl2[4 * s4 + u])) : 0.f;
+                            for (int k2 = 0; k2 < 2; ++k2) {
+                                const int kk = (g2 * HALF + blk * 32) / 16 + k2;
+                                umma_bf16_ts(tmem + C_UT, tmem + C_SLO + kk * 8, sdesc_sw128(swt + kk * 2048, 16, 1024),
+                                             id_w1, 1u);
                             }
-                            *reinterpret_cast<float4*>(nrow + 4 * s4) = make_float4(o4[0], o4[1], o4[2], o4[3]);
                         }
                     }
                 }
-            }
-            tc_fence_before();
-            named_bar(BAR_PREP, 128);
-
-            // ---- A = (I - N)^-1
-            invert_unit_lower<L::NLD, L::AOLD>(Nsm, Ao, Xs, pw, lane);
-
-            // ---- A1 = A diag(beta'), A2 = A diag(beta' e^Lambda) -> X (hi/lo rows [t][s])
-            if (c >= 1) mbar_wait_or_abort(&bars->ws_done, (c - 1) & 1, err, abort_flag);
-            {
-                const int t = pt >> 1, hf = pt & 1;
-                const int ib = t >> 4, r = t & 15;
-                const float* bm = g + G_BM * 64;
-                const float* bme = g + G_BME * 64;
-                uint8_t* X = sm + L::OFF_X;
-#pragma unroll
-                for (int ch = 0; ch < 4; ++ch) {
-                    const int s0 = 32 * hf + 8 * ch;
-                    const uint32_t off = sw128_chunk(t, 4 * hf + ch);
-                    uint4 h1 = make_uint4(0u, 0u, 0u, 0u), l1 = h1, h2 = h1, l2 = h1;
-                    if (s0 <= t) {
-                        const int jb = s0 >> 4;
-                        const float* src = (jb == ib) ? Nsm + t * L::NLD + s0
-                                                      : Ao + ao_slot(ib, jb) * 16 * L::AOLD + r * L::AOLD + (s0 & 15);
-                        const float4 x0 = *reinterpret_cast<const float4*>(src);
-                        const float4 x1 = *reinterpret_cast<const float4*>(src + 4);
-                        const float xv[8] = {x0.x, x0.y, x0.z, x0.w, x1.x, x1.y, x1.z, x1.w};
-                        float e1[8], e2[8];
-#pragma unroll
-                        for (int u = 0; u < 8; ++u) {
-                            const float xa = (s0 + u <= t) ? xv[u] : 0.f;
-                            e1[u] = xa * bm[s0 + u];
-                            e2[u] = xa * bme[s0 + u];
-                        }
-                        split8(e1, h1, l1);
-                        split8(e2, h2, l2);
-                    }
-                    *reinterpret_cast<uint4*>(X + L::X_A1H + off) = h1;
-                    *reinterpret_cast<uint4*>(X + L::X_A1L + off) = l1;
-                    *reinterpret_cast<uint4*>(X + L::X_A2H + off) = h2;
-                    *reinterpret_cast<uint4*>(X + L::X_A2L + off) = l2;
-                }
-            }
-            fence_async_smem();
-            tc_fence_before();
-            named_bar(BAR_PREP, 128);
-
-            // ---- U^T = V^T A1^T (into UT[par]), W^T = K^T A2^T (into COL_WT); the chain waits for them
-            if (leader) {
-                mbar_arrive(&bars->prep_done[par]);       // P, gates, A1/A2 are in shared memory
-                if (c >= 1) mbar_wait_or_abort(&bars->wt_read, (c - 1) & 1, err, abort_flag);
-                const bool okv = mbar_wait_or_abort(&bars->v_full, c & 1, err, abort_flag);
+                if (!*abort_flag) umma_commit(&bars->ws_done);
+                mbar_spin_or_abort(&bars->dv_done, c & 1, err, abort_flag);
                 tc_fence_after();
-                if (okv && !*abort_flag) {
-                    const uint32_t sv = smem_u32(sm + L::OFF_V);
-                    const uint32_t sk = smem_u32(qk_s) + 8192;
-                    const uint32_t sx = smem_u32(sm + L::OFF_X);
-                    constexpr uint32_t id_mn = idesc_bf16(128, 64, true, false);
+                if (!*abort_flag) {
+                    // S^T += dV'^T K (K as MN-major B); dV' hi/lo sit in C_UT per 32-token half
+                    constexpr uint32_t idst = idesc_bf16(128, DK, false, true);
 #pragma unroll
                     for (int p = 0; p < 2; ++p) {
-                        const uint32_t b1 = sx + (p ? L::X_A1L : L::X_A1H);
 #pragma unroll
                         for (int kk = 0; kk < 4; ++kk)
-                            umma_bf16_ss(tmem + COL_UT + par * 64, sdesc_sw128(sv + kk * 2048, 8192, 1024),
-                                         sdesc_sw128(b1 + kk * 32, 16, 1024), id_mn, (p > 0 || kk > 0) ? 1u : 0u);
+                            umma_bf16_ts(tmem + C_ST, tmem + C_UT + (kk >> 1) * 32 + p * 16 + (kk & 1) * 8,
+                                         sdesc_sw128(sk + kk * 2048, 8192, 1024), idst, 1u);
                     }
+                    umma_commit(&bars->st_done);
+                    // O^T += dV^T P^T
+                    constexpr uint32_t id64 = idesc_bf16(128, 64, false, false);
 #pragma unroll
-                    for (int p = 0; p < 2; ++p) {
-                        const uint32_t b2 = sx + (p ? L::X_A2L : L::X_A2H);
-#pragma unroll
-                        for (int kk = 0; kk < 4; ++kk)
-                            umma_bf16_ss(tmem + COL_WT, sdesc_sw128(sk + kk * 2048, 16384, 1024),
-                                         sdesc_sw128(b2 + kk * 32, 16, 1024), id_mn, (p > 0 || kk > 0) ? 1u : 0u);
-                    }
-                    umma_commit(&bars->uw_done);
-                    umma_commit(&bars->v_free);
+                    for (int kk = 0; kk < 4; ++kk)
+                        umma_bf16_ts(tmem + C_O, tmem + C_DVB + kk * 8, sdesc_sw128(sbase + L::R_P + kk * 32, 16, 1024),
+                                     id64, 1u);
+                    umma_commit(&bars->pdv_done);
+                    umma_commit(&bars->slot_free[slot]);
+                }
+                if (c + 1 < nchunks) {
+                    // U^T of the next chunk overwrites C_UT once the state update has read dV'
+                    mbar_spin_or_abort(&bars->st_done, c & 1, err, abort_flag);
+                    const bool ok = mbar_spin_or_abort(&bars->va_full, (c + 1) & 1, err, abort_flag);
+                    tc_fence_after();
+                    if (ok && !*abort_flag) issue_u();
                 }
             }
         }
-    } else {
-        // ======================= CHAIN warpgroup
-        const int ct = tid - 160;                          // 0..127
-        const int j = ((warp & 3) << 5) | lane;            // TMEM lane = value row j (or key row d for W^T)
+    } else if (warp < 10) {
+        // ======================= state path: 256 threads, lane j twice (one half of the key columns each)
+        const int ct = tid - 64;
+        const int grp = ct >> 7;
+        const int j = ((warp & 3) << 5) | lane;
         const uint32_t lane_off = static_cast<uint32_t>(warp & 3) << 21;
-        const bool leader = (ct == 0);
         const long s_base = static_cast<long>(bh) * DK * args.dv + v0;
-        uint8_t* sr = sm + L::OFF_SR;
 
-        // output tile of chunk cc from (Q S)^T and (P dV)^T in TMEM:
-        //   o[t, j] = oc_t (Q S)[t,j] + (P dV)[t,j]  -> smem [t][j] (128B swizzle) -> TMA store
-        auto write_output = [&](int cc) {
-            float qs[64], pd[64];
-            tmem_ld64(tmem + lane_off + COL_QS, qs);
-            tmem_ld64(tmem + lane_off + COL_PDV, pd);
-            const float* oc = ocbuf + (cc & 1) * 64;
-            uint8_t* ob = sr + L::OST + (j >> 6) * 8192;
-            const uint32_t jj = j & 63;
+        // initial state -> TMEM (S^T: lane j = value column, column d = key index); O^T = 0
 #pragma unroll
-            for (int t = 0; t < kC; ++t)
-                *reinterpret_cast<uint16_t*>(ob + sw128_off(t, jj)) = f32_to_bf16_bits(fmaf(oc[t], qs[t], pd[t]));
-            fence_async_smem();
-            tc_fence_before();
-            named_bar(BAR_CHAIN, 128);
-            if (leader && !*abort_flag) {
-                for (int vb = 0; vb < nvb; ++vb) tma_store_4d(&map_o, sr + L::OST + vb * 8192, v0 + vb * 64, cc * kC, h, bidx);
-                bulk_commit();
-            }
-        };
-
-        // initial state -> TMEM (S^T: lane j = value column, column d = key index)
-#pragma unroll
-        for (int blk = 0; blk < DK / 32; ++blk) {
+        for (int blk = 0; blk < NBLK; ++blk) {
             float vals[32];
 #pragma unroll
             for (int i = 0; i < 32; ++i) {
-                const int d = blk * 32 + i;
+                const int d = grp * HALF + blk * 32 + i;
                 vals[i] = (args.state_in && j < dv_valid) ? args.state_in[s_base + static_cast<long>(d) * args.dv + j]
                                                           : 0.f;
             }
-            tmem_st32(tmem + lane_off + COL_ST + 32 * blk, vals);
+            tmem_st32(tmem + lane_off + C_ST + grp * HALF + blk * 32, vals);
+        }
+        {
+            float z[32];
+#pragma unroll
+            for (int i = 0; i < 32; ++i) z[i] = 0.f;
+            tmem_st32(tmem + lane_off + C_O + grp * 32, z);
         }
         tmem_st_wait();
 
 #pragma unroll 1
         for (int c = 0; c < nchunks; ++c) {
-            const int par = c & 1;
-            const float* g = gates + par * L::GSTRIDE;
-            uint8_t* qk_s = sm + (par ? L::OFF_QK1 : L::OFF_QK0);
-            if (c >= 1) write_output(c - 1);               // previous chunk's output, while prep runs
-            mbar_wait_or_abort(&bars->prep_done[par], (c >> 1) & 1, err, abort_flag);
-            mbar_wait_or_abort(&bars->uw_done, c & 1, err, abort_flag);
+            const int slot = c & 1;
+            const float* G = reinterpret_cast<const float*>(sm + slot * L::SLOT_BYTES + L::R_G);
+            mbar_wait_or_abort(&bars->slot_full[slot], (c >> 1) & 1, err, abort_flag);
+            if (c >= 1) mbar_wait_or_abort(&bars->st_done, (c - 1) & 1, err, abort_flag);
             tc_fence_after();
-
-            // ---- W^T (lane d) -> X as MN-major B operand rows [d][t], hi/lo
-            {
-                float row[64];
-                tmem_ld64(tmem + lane_off + COL_WT, row);
-                store_row_split(sm + L::OFF_X + L::X_WTH, sm + L::OFF_X + L::X_WTL, j, row);
-            }
-            if (leader) bulk_wait_read0();                 // the output tile has left shared memory
-            named_bar(BAR_CHAIN, 128);
-            // ---- S^T -> bf16 hi/lo rows [j][d]; S^T *= gamma_c in TMEM
-            const float gamma_c = g[G_TOT * 64 + 2];
+            // ---- S^T -> bf16 hi/lo (TMEM), S^T *= gamma_c; one arrive per 32-column block
+            const float gamma_c = G[128];
 #pragma unroll
-            for (int blk = 0; blk < DK / 32; ++blk) {
-                float vals[32];
-                tmem_ld32(tmem + lane_off + COL_ST + 32 * blk, vals);
+            for (int blk = 0; blk < NBLK; ++blk) {
+                const uint32_t col = grp * HALF + blk * 32;
+                float v[32];
+                tmem_ld32(tmem + lane_off + C_ST + col, v);
                 tmem_ld_wait();
-                const int cb = blk >> 1;
+                uint32_t hi[16], lo[16];
 #pragma unroll
-                for (int ch4 = 0; ch4 < 4; ++ch4) {
-                    uint4 hw, lw;
-                    split8(&vals[8 * ch4], hw, lw);
-                    const uint32_t off = cb * 16384 + sw128_chunk(j, (blk & 1) * 4 + ch4);
-                    *reinterpret_cast<uint4*>(sr + off) = hw;
-                    *reinterpret_cast<uint4*>(sr + L::S_LO + off) = lw;
-                }
+                for (int i = 0; i < 16; ++i) split2_bf16(v[2 * i], v[2 * i + 1], hi[i], lo[i]);
+                tmem_st16(tmem + lane_off + C_SHI + col / 2, hi);
+                tmem_st16(tmem + lane_off + C_SLO + col / 2, lo);
 #pragma unroll
-                for (int i = 0; i < 32; ++i) vals[i] *= gamma_c;
-                tmem_st32(tmem + lane_off + COL_ST + 32 * blk, vals);
+                for (int i = 0; i < 32; ++i) v[i] *= gamma_c;
+                tmem_st32(tmem + lane_off + C_ST + col, v);
+                tmem_st_wait();
+                tc_fence_before();
+                mbar_arrive(&bars->split_half[blk]);
             }
-            tmem_st_wait();
-            fence_async_smem();
-            tc_fence_before();
-            named_bar(BAR_CHAIN, 128);
-            if (leader) mbar_arrive(&bars->wt_read);
 
-            // ---- dV^T = U^T - S^T W^T (3 split terms, negated B, in place in UT[par]); (Q S_hi)^T
-            if (leader && !*abort_flag) {
-                tc_fence_after();
-                const uint32_t ssr = smem_u32(sr);
-                const uint32_t swt = smem_u32(sm + L::OFF_X);
-                constexpr uint32_t id_ws = idesc_bf16(128, 64, false, true) | (1u << 14);   // negate B
-#pragma unroll
-                for (int p = 0; p < 3; ++p) {
-                    const uint32_t sa = ssr + (p == 1 ? L::S_LO : 0);
-                    const uint32_t sb = swt + (p == 2 ? L::X_WTL : L::X_WTH);
-#pragma unroll
-                    for (int kk = 0; kk < DK / 16; ++kk)
-                        umma_bf16_ss(tmem + COL_UT + par * 64,
-                                     sdesc_sw128(sa + (kk >> 2) * 16384 + (kk & 3) * 32, 16, 1024),
-                                     sdesc_sw128(sb + kk * 2048, 16, 1024), id_ws, 1u);
-                }
-#pragma unroll
-                for (int kk = 0; kk < DK / 16; ++kk) {
-                    const uint32_t o = (kk >> 2) * 16384 + (kk & 3) * 32;
-                    umma_bf16_ss(tmem + COL_QS, sdesc_sw128(ssr + o, 16, 1024), sdesc_sw128(smem_u32(qk_s) + o, 16, 1024),
-                                 idesc_bf16(128, 64, false, false), kk > 0);
-                }
-                umma_commit(&bars->ws_done);
-            }
+            // ---- dV (bf16) and dV' = dV * exp(Lambda_last - Lambda) (hi/lo), tokens [32 grp, 32 grp + 32)
             mbar_wait_or_abort(&bars->ws_done, c & 1, err, abort_flag);
             tc_fence_after();
-
-            // ---- dV (bf16) and dV' = dV * exp(Lambda_last - Lambda) (hi/lo) -> rows [j][t]
             {
-                float row[64];
-                tmem_ld64(tmem + lane_off + COL_UT + par * 64, row);
-                const float* edec = g + G_EDEC * 64;
+                float v[32], w[32];
+                tmem_ld32(tmem + lane_off + C_UT + grp * 32, v);
+                tmem_ld32(tmem + lane_off + C_UT + 64 + grp * 32, w);
+                tmem_ld_wait();
+                const float* edec = G + 64 + grp * 32;
+                uint32_t bw[16], hi[16], lo[16];
 #pragma unroll
-                for (int ch = 0; ch < 8; ++ch) {
-                    const uint32_t off = sw128_chunk(j, ch);
-                    *reinterpret_cast<uint4*>(sr + L::DVB + off) = pack8(&row[8 * ch]);
-                    float e[8];
-#pragma unroll
-                    for (int u = 0; u < 8; ++u) e[u] = row[8 * ch + u] * edec[8 * ch + u];
-                    uint4 hw, lw;
-                    split8(e, hw, lw);
-                    *reinterpret_cast<uint4*>(sr + L::DVH + off) = hw;
-                    *reinterpret_cast<uint4*>(sr + L::DVL + off) = lw;
+                for (int i = 0; i < 16; ++i) {
+                    const float d0 = v[2 * i] + w[2 * i], d1 = v[2 * i + 1] + w[2 * i + 1];
+                    bw[i] = cvt_bf16x2(d0, d1);
+                    split2_bf16(d0 * edec[2 * i], d1 * edec[2 * i + 1], hi[i], lo[i]);
                 }
+                tmem_st16(tmem + lane_off + C_UT + grp * 32, hi);
+                tmem_st16(tmem + lane_off + C_UT + grp * 32 + 16, lo);
+                tmem_st16(tmem + lane_off + C_DVB + grp * 16, bw);
             }
-            fence_async_smem();
+            tmem_st_wait();
             tc_fence_before();
-            named_bar(BAR_CHAIN, 128);
-
-            // ---- S^T += dV'^T K (K as MN-major B);  (P dV)^T = dV^T P^T
-            if (leader && !*abort_flag) {
-                tc_fence_after();
-                const uint32_t ssr = smem_u32(sr);
-                const uint32_t sk = smem_u32(qk_s) + 8192;
-                const uint32_t sp = smem_u32(sm + L::OFF_P + par * 8192);
-                constexpr uint32_t idst = idesc_bf16(128, DK, false, true);
-                constexpr uint32_t id64 = idesc_bf16(128, 64, false, false);
-#pragma unroll
-                for (int p = 0; p < 2; ++p) {
-                    const uint32_t ra = ssr + (p ? L::DVL : L::DVH);
-#pragma unroll
-                    for (int kk = 0; kk < 4; ++kk)
-                        umma_bf16_ss(tmem + COL_ST, sdesc_sw128(ra + kk * 32, 16, 1024),
-                                     sdesc_sw128(sk + kk * 2048, 16384, 1024), idst, 1u);
-                }
-#pragma unroll
-                for (int kk = 0; kk < 4; ++kk)
-                    umma_bf16_ss(tmem + COL_PDV, sdesc_sw128(ssr + L::DVB + kk * 32, 16, 1024),
-                                 sdesc_sw128(sp + kk * 32, 16, 1024), id64, kk > 0);
-                umma_commit(&bars->st_done);
-                umma_commit(&bars->qk_free[par]);
-            }
-            mbar_wait_or_abort(&bars->st_done, c & 1, err, abort_flag);
-            tc_fence_after();
-            if (ct < kC) ocbuf[par * 64 + ct] = g[G_OC * 64 + ct];
-            named_bar(BAR_CHAIN, 128);
-            if (leader) mbar_arrive(&bars->chain_done[par]);
+            mbar_arrive(&bars->dv_done);
         }
-        if (nchunks >= 1) write_output(nchunks - 1);
-        if (leader) bulk_wait_all0();
 
         // ---- final state S^T -> state_out [dk][dv]
+        mbar_wait_or_abort(&bars->st_done, (nchunks - 1) & 1, err, abort_flag);
+        tc_fence_after();
         if (!*abort_flag && args.state_out) {
 #pragma unroll
-            for (int blk = 0; blk < DK / 32; ++blk) {
+            for (int blk = 0; blk < NBLK; ++blk) {
                 float vals[32];
-                tmem_ld32(tmem + lane_off + COL_ST + 32 * blk, vals);
+                tmem_ld32(tmem + lane_off + C_ST + grp * HALF + blk * 32, vals);
                 tmem_ld_wait();
                 if (j < dv_valid) {
 #pragma unroll
                     for (int i = 0; i < 32; ++i)
-                        args.state_out[s_base + static_cast<long>(blk * 32 + i) * args.dv + j] = vals[i];
+                        args.state_out[s_base + static_cast<long>(grp * HALF + blk * 32 + i) * args.dv + j] = vals[i];
                 }
             }
         }
+    } else {
+        // ======================= output warps
+        const int ot = tid - 320;
+        const int j = ((warp & 3) << 5) | lane;
+        const uint32_t lane_off = static_cast<uint32_t>(warp & 3) << 21;
+        const bool oleader = (ot == 0);
+        // Q~^T = -diag(oc) Q, transposed in place over chunk cc's q tile: row d of the
+        // MN-major image holds the 64 tokens (B operand of the N=192 MMA, third block)
+        auto build_qt = [&](int cc) {
+            const int slot = cc & 1;
+            uint8_t* qt = sm + slot * L::SLOT_BYTES + L::Q_OFF;
+            const float* oc = reinterpret_cast<const float*>(sm + slot * L::SLOT_BYTES + L::R_G);
+            mbar_wait_or_abort(&bars->slot_full[slot], (cc >> 1) & 1, err, abort_flag);
+            uint32_t pk[32];
+            const int d = ot;
+            if (d < DK) {
+                const uint8_t* src = qt + (d >> 6) * 8192;
+#pragma unroll
+                for (int i = 0; i < 32; ++i) {
+                    const float x0 = bf16_bits_to_f32(*reinterpret_cast<const uint16_t*>(src + sw128_off(2 * i, d & 63)));
+                    const float x1 =
+                        bf16_bits_to_f32(*reinterpret_cast<const uint16_t*>(src + sw128_off(2 * i + 1, d & 63)));
+                    pk[i] = cvt_bf16x2(-oc[2 * i] * x0, -oc[2 * i + 1] * x1);
+                }
+            }
+            named_bar(BAR_OUT, 128);                   // every q element has been read
+            if (d < DK) {
+#pragma unroll
+                for (int ch = 0; ch < 8; ++ch)
+                    *reinterpret_cast<uint4*>(qt + sw128_chunk(d, ch)) =
+                        make_uint4(pk[4 * ch], pk[4 * ch + 1], pk[4 * ch + 2], pk[4 * ch + 3]);
+            }
+            fence_async_smem();
+            named_bar(BAR_OUT, 128);
+            if (oleader) {
+                mbar_arrive(&bars->qt_ready[slot]);
+                mbar_arrive(&bars->slot_free[slot]);      // the output warps are done with this slot
+            }
+        };
+        build_qt(0);
+#pragma unroll 1
+        for (int c = 0; c < nchunks; ++c) {
+            if (c + 1 < nchunks) build_qt(c + 1);
+            // ---- o[t, j] = O^T[j, t]; the accumulator is reset for the next chunk
+            mbar_wait_or_abort(&bars->pdv_done, c & 1, err, abort_flag);
+            tc_fence_after();
+            uint32_t ob2[32];                              // bf16 results, tokens (2i, 2i+1)
+            {
+                float o[32];
+                float z[32];
+#pragma unroll
+                for (int i = 0; i < 32; ++i) z[i] = 0.f;
+#pragma unroll
+                for (int half = 0; half < 2; ++half) {
+                    tmem_ld32(tmem + lane_off + C_O + 32 * half, o);
+                    tmem_ld_wait();
+                    tmem_st32(tmem + lane_off + C_O + 32 * half, z);
+#pragma unroll
+                    for (int i = 0; i < 16; ++i) ob2[16 * half + i] = cvt_bf16x2(o[2 * i], o[2 * i + 1]);
+                }
+                tmem_st_wait();
+            }
+            tc_fence_before();
+            mbar_arrive(&bars->o_free);
+            if (oleader) bulk_wait_read1();                // the store of two chunks ago left this buffer
+            named_bar(BAR_OUT, 128);
+            uint8_t* ob = sm + L::OFF_O + (c & 1) * 16384 + (j >> 6) * 8192;
+            const uint32_t jj = j & 63;
+#pragma unroll
+            for (int i = 0; i < 32; ++i) {
+                *reinterpret_cast<uint16_t*>(ob + sw128_off(2 * i, jj)) = static_cast<uint16_t>(ob2[i] & 0xffffu);
+                *reinterpret_cast<uint16_t*>(ob + sw128_off(2 * i + 1, jj)) = static_cast<uint16_t>(ob2[i] >> 16);
+            }
+            fence_async_smem();
+            named_bar(BAR_OUT, 128);
+            if (oleader) {
+                if (!*abort_flag)
+                    for (int vb = 0; vb < nvb; ++vb)
+                        tma_store_4d(map_o, sm + L::OFF_O + (c & 1) * 16384 + vb * 8192, v0 + vb * 64, (c0 + c) * kC, h,
+                                     bidx);
+                bulk_commit();
+            }
+        }
+        if (oleader) bulk_wait_all0();
     }
 
     tc_fence_before();
     __syncthreads();
-    if (warp == 0) tmem_dealloc(tmem, kTmemCols);
+    if (warp == 0) tmem_dealloc(tmem, kChainTmemCols);
 }
+
+template <int DK>
+__global__ void __launch_bounds__(kChainThreads, 1)
+prefill_chain_kernel(const __grid_constant__ CUtensorMap map_q, const __grid_constant__ CUtensorMap map_k,
+                     const __grid_constant__ CUtensorMap map_v, const __grid_constant__ CUtensorMap map_o,
+                     const ChainArgs args) {
+    extern __shared__ uint8_t smem_raw[];
+    chain_body<DK>(&map_q, &map_k, &map_v, &map_o, args, align1024(smem_raw), blockIdx.x);
+}
+
+// Shared memory of one overlap CTA: a chain CTA, or kPrepPerCta prep workers.
+template <int DK>
+struct OverlapSmem {
+    static constexpr int PREP_STRIDE = (PrepSmem<DK>::BYTES + 1023) / 1024 * 1024;
+    static constexpr int PREP_BYTES = kPrepPerCta * PREP_STRIDE + 1024;
+    static constexpr int ALLOC = ChainSmem<DK>::ALLOC > PREP_BYTES ? ChainSmem<DK>::ALLOC : PREP_BYTES;
+    static_assert(ALLOC <= 232448, "overlap kernel shared memory exceeds 227 KB");
+};
+
+// Chain piece k and prep piece k+1 in one launch: CTAs [0, nchain) run the
+// recurrence over the chunks prepared by the previous launch; every other CTA
+// hosts kPrepPerCta independent prep workers (128 threads each) preparing the
+// next piece.  No CTA waits on another, so residency does not matter for
+// correctness; with one CTA per SM the two roles run side by side.
+template <int DK>
+__global__ void __launch_bounds__(kChainThreads, 1)
+prefill_overlap_kernel(const __grid_constant__ CUtensorMap map_q, const __grid_constant__ CUtensorMap map_k,
+                       const __grid_constant__ CUtensorMap map_v, const __grid_constant__ CUtensorMap map_o,
+                       const ChainArgs ca, const PrepArgs pa, const int nchain) {
+    extern __shared__ uint8_t smem_raw[];
+    uint8_t* sm = align1024(smem_raw);
+    if (static_cast<int>(blockIdx.x) < nchain) {
+        chain_body<DK>(&map_q, &map_k, &map_v, &map_o, ca, sm, blockIdx.x);
+    } else {
+        const int wg = threadIdx.x >> 7;
+        if (wg < kPrepPerCta) {
+            const int vblock = (blockIdx.x - nchain) * kPrepPerCta + wg;
+            const int vgrid = (gridDim.x - nchain) * kPrepPerCta;
+            prep_body<DK>(&map_q, &map_k, pa, sm + wg * OverlapSmem<DK>::PREP_STRIDE, threadIdx.x & 127, vblock, vgrid,
+                          BAR_PREP + wg, false);
+        }
+    }
+}
+
 
 std::once_flag g_attr_once[2][64];
 int g_attr_status[2][64];
+int g_sm_count[64];
 
+constexpr int kMaxPieces = 4;
+std::atomic<int> g_schedule{GDN_SCHEDULE_AUTO};
+
+// Predicted time (us) of the two schedules, from per-unit costs measured on
+// B200 (config-1 shapes): a round of prep tasks takes ~10 us in the prep
+// kernel (3 workers per SM) and ~13 us in the overlap kernel, a worker's first
+// task ~4 us more; a chain chunk ~2.8 us, a chain launch ~7 us of state
+// load/store and pipeline fill.  The pieced schedule wins when the chain is
+// long and the sequences few (e.g. a head-sharded long-context prefill), not
+// at config 1 where prep rounds, not the chain, would bound each overlap launch.
+bool use_pieces(int nbh, int nchunks, int chain_grid, int sms) {
+    if (2 * chain_grid > sms || nchunks < 4 * kMaxPieces) return false;
+    auto rounds = [](long tasks, long workers) { return static_cast<double>((tasks + workers - 1) / workers); };
+    const double prep_round = 10.0, ovl_round = 13.0, first = 4.0, chunk = 2.8, launch = 7.0;
+    const long w_all = static_cast<long>(sms) * kPrepCtasPerSm;
+    const long w_free = static_cast<long>(sms - chain_grid) * kPrepPerCta;
+    const double unpieced = rounds(static_cast<long>(nbh) * nchunks, w_all) * prep_round + first + nchunks * chunk + launch;
+    const int per = (nchunks + kMaxPieces - 1) / kMaxPieces;
+    double pieced = rounds(static_cast<long>(nbh) * per, w_all) * prep_round + first;
+    for (int c0 = 0; c0 < nchunks; c0 += per) {
+        const int nc = nchunks - c0 < per ? nchunks - c0 : per;
+        const int nn = nchunks - (c0 + nc) < per ? nchunks - (c0 + nc) : per;
+        const double ch = nc * chunk + launch;
+        const double pr = nn > 0 ? rounds(static_cast<long>(nbh) * nn, w_free) * ovl_round + first : 0.0;
+        pieced += ch > pr ? ch : pr;
+    }
+    return pieced < 0.95 * unpieced;
+}
+
+// The schedule, all on the caller's stream.  Gates (one launch), then prep and
+// chain.  When the chain kernel leaves at least half of the SMs idle (few
+// sequences), the sequence is cut into up to 4 pieces of chunks:
+//   prep(piece 0) -> overlap(chain piece 0 | prep piece 1) -> ... -> chain(last piece)
+// with the state carried between chain pieces through `state_tmp`; otherwise
+// one prep and one chain launch over all chunks.
 template <int DK>
 int launch_prefill(const CUtensorMap& mq, const CUtensorMap& mk, const CUtensorMap& mv, const CUtensorMap& mo,
-                   const PrefillArgs& args, int grid, cudaStream_t st) {
-    using L = PrefillSmem<DK>;
+                   const GateArgs& ga, PrepArgs pa, ChainArgs ca, int chain_grid, float* state_tmp,
+                   cudaStream_t st) {
     int dev = 0;
     cudaGetDevice(&dev);
     const int which = DK == 128 ? 1 : 0;
     std::call_once(g_attr_once[which][dev & 63], [&]() {
-        g_attr_status[which][dev & 63] =
-            cudaFuncSetAttribute(prefill_chunk_kernel<DK>, cudaFuncAttributeMaxDynamicSharedMemorySize, L::ALLOC) ==
-                    cudaSuccess ? GDN_OK : GDN_ERR_CUDA;
+        int sms = 0;
+        const bool ok =
+            cudaFuncSetAttribute(prefill_prep_kernel<DK>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                 PrepSmem<DK>::ALLOC) == cudaSuccess &&
+            cudaFuncSetAttribute(prefill_chain_kernel<DK>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                 ChainSmem<DK>::ALLOC) == cudaSuccess &&
+            cudaFuncSetAttribute(prefill_overlap_kernel<DK>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                 OverlapSmem<DK>::ALLOC) == cudaSuccess &&
+            cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev) == cudaSuccess && sms > 0;
+        g_sm_count[dev & 63] = sms;
+        g_attr_status[which][dev & 63] = ok ? GDN_OK : GDN_ERR_CUDA;
     });
     if (g_attr_status[which][dev & 63] != GDN_OK)
-        return fail(GDN_ERR_CUDA, "gdn_prefill_fwd: cannot grant %d B of shared memory", L::ALLOC);
-    prefill_chunk_kernel<DK><<<grid, kThreads, L::ALLOC, st>>>(mq, mk, mv, mo, args);
-    return launch_status("gdn_prefill_fwd");
+        return fail(GDN_ERR_CUDA, "gdn_prefill_fwd: cannot configure the prefill kernels (%d / %d / %d B shared memory)",
+                    PrepSmem<DK>::ALLOC, ChainSmem<DK>::ALLOC, OverlapSmem<DK>::ALLOC);
+    const int sms = g_sm_count[dev & 63];
+    const int nchunks = ca.nchunks_total;
+    const int nbh = ga.ntasks / nchunks;                     // B * Hv
+
+    prefill_gates_kernel<DK><<<(ga.ntasks + 3) / 4, 128, 0, st>>>(ga);
+    int s = launch_status("gdn_prefill_fwd (gates)");
+    if (s != GDN_OK) return s;
+
+    auto set_piece = [&](int c0, int nc, const float* sin, float* sout, int pc0, int pnc) {
+        ca.c0 = c0;
+        ca.nchunks = nc;
+        ca.state_in = sin;
+        ca.state_out = sout;
+        pa.c0 = pc0;
+        pa.ncp = pnc;
+        pa.ntasks = nbh * pnc;
+    };
+    auto prep_only = [&](int ctas) {
+        const int grid = pa.ntasks < ctas ? pa.ntasks : ctas;
+        prefill_prep_kernel<DK><<<grid, kPrepThreads, PrepSmem<DK>::ALLOC, st>>>(mq, mk, pa);
+        return launch_status("gdn_prefill_fwd (prep)");
+    };
+    auto chain_only = [&]() {
+        prefill_chain_kernel<DK><<<chain_grid, kChainThreads, ChainSmem<DK>::ALLOC, st>>>(mq, mk, mv, mo, ca);
+        return launch_status("gdn_prefill_fwd (chain)");
+    };
+    const float* user_in = ca.state_in;
+    float* user_out = ca.state_out;
+
+    const int mode = g_schedule.load(std::memory_order_relaxed);
+    const bool pieced = mode == GDN_SCHEDULE_PIECED   ? (nchunks >= 2)
+                        : mode == GDN_SCHEDULE_SINGLE ? false
+                                                      : use_pieces(nbh, nchunks, chain_grid, sms);
+    if (!pieced) {
+        set_piece(0, nchunks, user_in, user_out, 0, nchunks);
+        if ((s = prep_only(sms * kPrepCtasPerSm)) != GDN_OK) return s;
+        return chain_only();
+    }
+    const int per = (nchunks + kMaxPieces - 1) / kMaxPieces;
+    const int pieces = (nchunks + per - 1) / per;
+    auto piece_len = [&](int k) { return (nchunks - k * per) < per ? (nchunks - k * per) : per; };
+    set_piece(0, 0, nullptr, nullptr, 0, piece_len(0));
+    if ((s = prep_only(sms * kPrepCtasPerSm)) != GDN_OK) return s;
+    for (int k = 0; k + 1 < pieces; ++k) {
+        set_piece(k * per, piece_len(k), k == 0 ? user_in : state_tmp, state_tmp, (k + 1) * per, piece_len(k + 1));
+        // chain CTAs first, prep workers on the remaining SMs (at least one CTA of them)
+        const int grid = chain_grid + (sms - chain_grid > 1 ? sms - chain_grid : 1);
+        prefill_overlap_kernel<DK><<<grid, kChainThreads, OverlapSmem<DK>::ALLOC, st>>>(mq, mk, mv, mo, ca, pa,
+                                                                                       chain_grid);
+        if ((s = launch_status("gdn_prefill_fwd (overlap)")) != GDN_OK) return s;
+    }
+    const int kl = pieces - 1;
+    set_piece(kl * per, piece_len(kl), kl == 0 ? user_in : state_tmp, user_out, 0, 0);
+    return chain_only();
 }
 
 // q/k/v/o map: dims (D, T, H, B) innermost first, box (64, 64, 1, 1), 128B swizzle.
@@ -848,14 +1285,47 @@ int make_act_map(CUtensorMap* m, const void* base, int D, int T, int H, int B, i
     return make_map_bf16(m, base, 4, dims, strides, box, true);
 }
 
+size_t record_bytes(int dk) { return dk == 128 ? Rec<128>::BYTES : Rec<64>::BYTES; }
+
 }  // namespace
 }  // namespace gdn
 
-extern "C" int gdn_prefill_fwd(const void* q, const void* k, const void* v, const float* A_log, const void* a,
-                               const void* b_logits, int gate_dtype, float dt_bias, const float* dt_bias_vec,
-                               const float* mask, const float* state_in, void* out, float* state_out, int B, int T,
-                               int Hqk, int Hv, int dk, int dv, int layout, float scale, void* stream) {
-    using namespace gdn;
+extern "C" int gdn_prefill_launch_count(int B, int T, int Hv, int dk, int dv) {
+    if (B <= 0 || T <= 0 || Hv <= 0 || !(dk == 64 || dk == 128) || !(dv == 64 || dv == 128 || dv == 256)) return -1;
+    int dev = 0, sms = 0;
+    if (cudaGetDevice(&dev) != cudaSuccess || cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess)
+        return -1;
+    const int nchunks = (T + gdn::kC - 1) / gdn::kC;
+    const int nbh = B * Hv, chain_grid = nbh * ((dv + 127) / 128);
+    const int mode = gdn::g_schedule.load(std::memory_order_relaxed);
+    const bool pieced = mode == GDN_SCHEDULE_PIECED   ? (nchunks >= 2)
+                        : mode == GDN_SCHEDULE_SINGLE ? false
+                                                      : gdn::use_pieces(nbh, nchunks, chain_grid, sms);
+    if (!pieced) return 3;
+    const int per = (nchunks + gdn::kMaxPieces - 1) / gdn::kMaxPieces;
+    return 2 + (nchunks + per - 1) / per;                // gates, prep(piece 0), overlaps, last chain
+}
+
+extern "C" int gdn_prefill_set_schedule(int mode) {
+    if (mode != GDN_SCHEDULE_AUTO && mode != GDN_SCHEDULE_SINGLE && mode != GDN_SCHEDULE_PIECED)
+        return gdn::fail(GDN_ERR_DTYPE, "gdn_prefill_set_schedule: unknown mode %d", mode);
+    gdn::g_schedule.store(mode);
+    return GDN_OK;
+}
+
+extern "C" size_t gdn_prefill_workspace_bytes(int B, int T, int Hv, int dk, int dv) {
+    if (B <= 0 || T <= 0 || Hv <= 0 || !(dk == 64 || dk == 128) || !(dv == 64 || dv == 128 || dv == 256)) return 0;
+    const size_t nchunks = (static_cast<size_t>(T) + gdn::kC - 1) / gdn::kC;
+    // chunk records, then an fp32 state buffer [B, Hv, dk, dv] for the pieced schedule
+    return static_cast<size_t>(B) * Hv * nchunks * gdn::record_bytes(dk) + static_cast<size_t>(B) * Hv * dk * dv * 4;
+}
+
+namespace gdn {
+namespace {
+// Argument checks shared by both prefill entry points (no device access).
+int validate_prefill(const void* q, const void* k, const void* v, const float* A_log, const void* a,
+                     const void* b_logits, int gate_dtype, const float* state_in, const void* out,
+                     const float* state_out, int B, int T, int Hqk, int Hv, int dk, int dv, int layout) {
     if (!q || !k || !v || !A_log || !a || !b_logits || !out)
         return fail(GDN_ERR_NULL, "gdn_prefill_fwd: q, k, v, A_log, a, b_logits and out are required");
     if (B <= 0 || T <= 0 || Hqk <= 0 || Hv <= 0 || Hv % Hqk != 0)
@@ -872,9 +1342,32 @@ extern "C" int gdn_prefill_fwd(const void* q, const void* k, const void* v, cons
         (state_out && !aligned16(state_out)))
         return fail(GDN_ERR_ALIGN, "gdn_prefill_fwd: q, k, v, out and states must be 16-byte aligned");
     const long ntiles = (dv + 127) / 128;
-    if (static_cast<long>(B) * Hv * ntiles > 0x7fffffffL)
-        return fail(GDN_ERR_SHAPE, "gdn_prefill_fwd: B*Hv too large");
-    int st = check_sm100();
+    const long nchunks = (static_cast<long>(T) + kC - 1) / kC;
+    if (static_cast<long>(B) * Hv * ntiles > 0x7fffffffL || static_cast<long>(B) * Hv * nchunks > 0x7fffffffL)
+        return fail(GDN_ERR_SHAPE, "gdn_prefill_fwd: B*Hv*chunks too large");
+    return GDN_OK;
+}
+}  // namespace
+}  // namespace gdn
+
+extern "C" int gdn_prefill_fwd_ws(const void* q, const void* k, const void* v, const float* A_log, const void* a,
+                                  const void* b_logits, int gate_dtype, float dt_bias, const float* dt_bias_vec,
+                                  const float* mask, const float* state_in, void* out, float* state_out, int B,
+                                  int T, int Hqk, int Hv, int dk, int dv, int layout, float scale, void* workspace,
+                                  size_t workspace_bytes, void* stream) {
+    using namespace gdn;
+    int st = validate_prefill(q, k, v, A_log, a, b_logits, gate_dtype, state_in, out, state_out, B, T, Hqk, Hv, dk,
+                              dv, layout);
+    if (st != GDN_OK) return st;
+    const long ntiles = (dv + 127) / 128;
+    const long nchunks = (static_cast<long>(T) + kC - 1) / kC;
+    const size_t need = gdn_prefill_workspace_bytes(B, T, Hv, dk, dv);
+    if (!workspace || workspace_bytes < need)
+        return fail(GDN_ERR_SHAPE, "gdn_prefill_fwd: workspace of %zu B required, %zu B given", need,
+                    workspace ? workspace_bytes : static_cast<size_t>(0));
+    if ((reinterpret_cast<uintptr_t>(workspace) & 127u) != 0)
+        return fail(GDN_ERR_ALIGN, "gdn_prefill_fwd: workspace must be 128-byte aligned");
+    st = check_sm100();
     if (st != GDN_OK) return st;
     if (scale == 0.f) scale = 1.f / sqrtf(static_cast<float>(dk));
 
@@ -884,27 +1377,76 @@ extern "C" int gdn_prefill_fwd(const void* q, const void* k, const void* v, cons
     if ((st = make_act_map(&mv, v, dv, T, Hv, B, layout)) != GDN_OK) return st;
     if ((st = make_act_map(&mo, out, dv, T, Hv, B, layout)) != GDN_OK) return st;
 
-    PrefillArgs args;
-    args.a = a;
-    args.b = b_logits;
-    args.gate_dtype = gate_dtype;
-    args.A_log = A_log;
-    args.dt_bias = dt_bias;
-    args.dt_bias_vec = dt_bias_vec;
-    args.mask = mask;
-    args.state_in = state_in;
-    args.state_out = state_out;
-    args.err = device_error_word();
-    args.B = B;
-    args.T = T;
-    args.Hqk = Hqk;
-    args.Hv = Hv;
-    args.dv = dv;
-    args.ntiles = static_cast<int>(ntiles);
-    args.layout = layout;
-    args.scale = scale;
+    GateArgs ga;
+    ga.a = a;
+    ga.b = b_logits;
+    ga.gate_dtype = gate_dtype;
+    ga.A_log = A_log;
+    ga.dt_bias = dt_bias;
+    ga.dt_bias_vec = dt_bias_vec;
+    ga.mask = mask;
+    ga.rec = static_cast<uint8_t*>(workspace);
+    ga.ntasks = static_cast<int>(static_cast<long>(B) * Hv * nchunks);
+    ga.T = T;
+    ga.Hv = Hv;
+    ga.nchunks = static_cast<int>(nchunks);
+    ga.scale = scale;
+
+    PrepArgs pa;
+    pa.rec = static_cast<uint8_t*>(workspace);
+    pa.err = device_error_word();
+    pa.ntasks = ga.ntasks;
+    pa.Hqk = Hqk;
+    pa.Hv = Hv;
+    pa.nchunks = ga.nchunks;
+    pa.c0 = 0;
+    pa.ncp = ga.nchunks;
+    pa.scale = scale;
+
+    ChainArgs ca;
+    ca.rec = static_cast<const uint8_t*>(workspace);
+    ca.state_in = state_in;
+    ca.state_out = state_out;
+    ca.err = pa.err;
+    ca.T = T;
+    ca.Hqk = Hqk;
+    ca.Hv = Hv;
+    ca.dv = dv;
+    ca.ntiles = static_cast<int>(ntiles);
+    ca.nchunks_total = static_cast<int>(nchunks);
+    ca.c0 = 0;
+    ca.nchunks = ca.nchunks_total;
+    float* state_tmp = reinterpret_cast<float*>(static_cast<uint8_t*>(workspace) +
+                                                static_cast<size_t>(ga.ntasks) * record_bytes(dk));
+
     const int grid = static_cast<int>(B * Hv * ntiles);
     cudaStream_t s = static_cast<cudaStream_t>(stream);
-    if (dk == 128) return launch_prefill<128>(mq, mk, mv, mo, args, grid, s);
-    return launch_prefill<64>(mq, mk, mv, mo, args, grid, s);
+    if (dk == 128) return launch_prefill<128>(mq, mk, mv, mo, ga, pa, ca, grid, state_tmp, s);
+    return launch_prefill<64>(mq, mk, mv, mo, ga, pa, ca, grid, state_tmp, s);
+}
+
+// Same call with the workspace taken from the stream-ordered allocator for the
+// duration of the call.
+extern "C" int gdn_prefill_fwd(const void* q, const void* k, const void* v, const float* A_log, const void* a,
+                               const void* b_logits, int gate_dtype, float dt_bias, const float* dt_bias_vec,
+                               const float* mask, const float* state_in, void* out, float* state_out, int B, int T,
+                               int Hqk, int Hv, int dk, int dv, int layout, float scale, void* stream) {
+    using namespace gdn;
+    int st0 = validate_prefill(q, k, v, A_log, a, b_logits, gate_dtype, state_in, out, state_out, B, T, Hqk, Hv, dk,
+                               dv, layout);
+    if (st0 != GDN_OK) return st0;
+    const size_t need = gdn_prefill_workspace_bytes(B, T, Hv, dk, dv);
+    void* ws = nullptr;
+    cudaStream_t s = static_cast<cudaStream_t>(stream);
+    if (need > 0) {
+        const int st = check_sm100();
+        if (st != GDN_OK) return st;
+        const cudaError_t e = cudaMallocAsync(&ws, need, s);
+        if (e != cudaSuccess)
+            return fail(GDN_ERR_CUDA, "gdn_prefill_fwd: workspace of %zu B: %s", need, cudaGetErrorString(e));
+    }
+    const int st = gdn_prefill_fwd_ws(q, k, v, A_log, a, b_logits, gate_dtype, dt_bias, dt_bias_vec, mask, state_in,
+                                      out, state_out, B, T, Hqk, Hv, dk, dv, layout, scale, ws, need, stream);
+    if (ws) cudaFreeAsync(ws, s);
+    return st;
 }

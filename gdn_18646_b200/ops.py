@@ -100,9 +100,11 @@ def prefill(q, k, v, A_log, a, b_logits, *, dt_bias=0.0, mask=None, state_in=Non
         out = torch.empty_like(v)
     if state_out is None and return_state:
         state_out = torch.empty(B, Hv, dk, dv, dtype=torch.float32, device=q.device)
-    _lib.call("gdn_prefill_fwd", _ptr(q), _ptr(k), _ptr(v), _ptr(A_log), _ptr(a), _ptr(b_logits), gdt,
+    ws_bytes = _lib.lib().gdn_prefill_workspace_bytes(B, T, Hv, dk, dv)
+    ws = torch.empty(max(int(ws_bytes), 1), dtype=torch.uint8, device=q.device)
+    _lib.call("gdn_prefill_fwd_ws", _ptr(q), _ptr(k), _ptr(v), _ptr(A_log), _ptr(a), _ptr(b_logits), gdt,
               dt_scalar, _ptr(dt_vec), _ptr(mask), _ptr(state_in), _ptr(out), _ptr(state_out),
-              B, T, Hqk, Hv, dk, dv, lay, float(scale), _stream())
+              B, T, Hqk, Hv, dk, dv, lay, float(scale), _ptr(ws), int(ws_bytes), _stream())
     return out, state_out
 
 

@@ -4,7 +4,9 @@
  * Every entry point takes raw DEVICE pointers, explicit shapes, a CUDA
  * stream (passed as void*, a cudaStream_t; NULL = legacy default stream) and
  * returns an int status (GDN_OK == 0).  Launches are asynchronous on that
- * stream; no entry point allocates device memory or synchronises.  On error
+ * stream; no entry point synchronises, and only gdn_prefill_fwd allocates
+ * (its workspace, stream-ordered; gdn_prefill_fwd_ws takes it from the
+ * caller instead).  On error
  * nothing is launched and gdn_last_error() describes the problem (the message
  * is per calling thread).
  *
@@ -14,6 +16,8 @@
  */
 #ifndef GDN_B200_H
 #define GDN_B200_H
+
+#include <stddef.h>
 
 #ifdef __cplusplus
 extern "C" {
@@ -69,6 +73,46 @@ int gdn_prefill_fwd(const void* q, const void* k, const void* v,
                     void* out, float* state_out,
                     int B, int T, int Hqk, int Hv, int dk, int dv, int layout,
                     float scale, void* stream);
+
+/*
+ * Bytes of device workspace gdn_prefill_fwd_ws needs (0 for invalid shapes):
+ * one chunk record per (batch, value head, 64-token chunk), 59 KB at dk=128,
+ * 43 KB at dk=64, plus one fp32 state [B, Hv, dk, dv].  No counterpart in the
+ * reference, whose kernel keeps everything in shared memory.
+ */
+size_t gdn_prefill_workspace_bytes(int B, int T, int Hv, int dk, int dv);
+
+/*
+ * Prefill launch schedule (process-wide; default GDN_SCHEDULE_AUTO):
+ *   SINGLE  one prep launch over all chunks, then one chain launch;
+ *   PIECED  the chunks cut into up to 4 pieces, the chain of piece k running
+ *           in the same launch as the prep of piece k+1;
+ *   AUTO    PIECED when a cost model predicts it faster (few sequences,
+ *           many chunks), else SINGLE.
+ * Results are identical up to fp32 summation order.  No counterpart in the
+ * reference (single kernel).
+ */
+enum { GDN_SCHEDULE_AUTO = 0, GDN_SCHEDULE_SINGLE = 1, GDN_SCHEDULE_PIECED = 2 };
+int gdn_prefill_set_schedule(int mode);
+
+/* Kernel launches one gdn_prefill_fwd call makes on the current device under
+ * the current schedule (3 for SINGLE), or -1 for invalid shapes / no device. */
+int gdn_prefill_launch_count(int B, int T, int Hv, int dk, int dv);
+
+/*
+ * gdn_prefill_fwd with a caller-provided workspace (device memory,
+ * 128-byte aligned, at least gdn_prefill_workspace_bytes(B, T, Hv, dk, dv)
+ * bytes, not used by other work on the stream while the call runs).
+ * gdn_prefill_fwd itself takes the workspace from the stream-ordered
+ * allocator (cudaMallocAsync / cudaFreeAsync on `stream`).
+ */
+int gdn_prefill_fwd_ws(const void* q, const void* k, const void* v,
+                       const float* A_log, const void* a, const void* b_logits, int gate_dtype,
+                       float dt_bias, const float* dt_bias_vec,
+                       const float* mask, const float* state_in,
+                       void* out, float* state_out,
+                       int B, int T, int Hqk, int Hv, int dk, int dv, int layout,
+                       float scale, void* workspace, size_t workspace_bytes, void* stream);
 
 /*
  * Single-token decode step, state updated in place if state_out == state_in.

@@ -129,3 +129,22 @@ def test_python_surface_raises_runtime_error(lib):
         _lib.call("gdn_prefill_fwd", *prefill_args(dk=96))
     assert ei.value.status == _lib.GDN_ERR_UNSUPPORTED
     assert isinstance(ei.value, RuntimeError)
+
+
+def test_prefill_workspace_and_schedule_entry_points(lib):
+    rec = 2048 + 16384 + 2 * 128 * 128 + 8192 + 1024           # gate block, A1 hi/lo, W^T hi/lo, P, gates
+    assert lib.gdn_prefill_workspace_bytes(4, 4096, 16, 128, 128) == 4 * 16 * 64 * rec + 4 * 16 * 128 * 128 * 4
+    assert lib.gdn_prefill_workspace_bytes(1, 65, 2, 64, 64) == 2 * 2 * (2048 + 16384 + 2 * 64 * 128 + 9216) + \
+        2 * 64 * 64 * 4
+    assert lib.gdn_prefill_workspace_bytes(1, 64, 2, 96, 64) == 0
+    assert lib.gdn_prefill_workspace_bytes(0, 64, 2, 128, 128) == 0
+    assert _lib.call_status("gdn_prefill_set_schedule", 7) == _lib.GDN_ERR_DTYPE
+    assert _lib.call_status("gdn_prefill_set_schedule", _lib.GDN_SCHEDULE_AUTO) == _lib.GDN_OK
+    assert lib.gdn_prefill_launch_count(1, 64, 2, 96, 64) == -1
+
+
+def test_prefill_ws_rejects_small_workspace(lib):
+    args = prefill_args()
+    args = args[:-1] + [FAKE, 1024, None]                          # workspace, workspace_bytes, stream
+    assert _lib.call_status("gdn_prefill_fwd_ws", *args) == _lib.GDN_ERR_SHAPE
+    assert "workspace" in _lib.last_error()
