@@ -42,6 +42,8 @@ SIGNATURES = {
     "gdn_prefill_fwd_ws": [_P, _P, _P, _P, _P, _P, _I, _F, _P, _P, _P, _P, _P,
                            _I, _I, _I, _I, _I, _I, _I, _F, _P, _Z, _P],
     "gdn_prefill_workspace_bytes": [_I, _I, _I, _I, _I],
+    "gdn_prefill_fwd_noalloc": [_P, _P, _P, _P, _P, _P, _I, _F, _P, _P, _P, _P, _P,
+                                _I, _I, _I, _I, _I, _I, _I, _F, _P],
     "gdn_prefill_set_schedule": [_I],
     "gdn_prefill_launch_count": [_I, _I, _I, _I, _I],
     "gdn_decode_step": [_P, _P, _P, _P, _P, _I, _P, _P, _P, _P, _P, _I, _I, _I, _I, _I, _F, _P],

@@ -1450,3 +1450,52 @@ extern "C" int gdn_prefill_fwd(const void* q, const void* k, const void* v, cons
     if (ws) cudaFreeAsync(ws, s);
     return st;
 }
+
+// ---------------------------------------------------------------------------
+// Allocation-free prefill for callers that cannot allocate device memory: the
+// workspace is a static device array of kStaticScratchBytes (32 MiB), enough
+// for ~540 chunk records at dk=128 (e.g. B*Hv = 8 sequences of 4096 tokens).
+// Calls on one device share it, so they must be ordered (one stream, or
+// externally serialised).
+// ---------------------------------------------------------------------------
+namespace gdn {
+constexpr size_t kStaticScratchBytes = size_t(32) << 20;
+static __device__ __align__(256) uint8_t g_prefill_scratch[kStaticScratchBytes];
+namespace {
+std::once_flag g_scratch_once[64];
+void* g_scratch_ptr[64];
+int g_scratch_status[64];
+}  // namespace
+}  // namespace gdn
+
+extern "C" int gdn_prefill_fwd_noalloc(const void* q, const void* k, const void* v, const float* A_log, const void* a,
+                                       const void* b_logits, int gate_dtype, float dt_bias, const float* dt_bias_vec,
+                                       const float* mask, const float* state_in, void* out, float* state_out, int B,
+                                       int T, int Hqk, int Hv, int dk, int dv, int layout, float scale, void* stream) {
+    using namespace gdn;
+    int st = validate_prefill(q, k, v, A_log, a, b_logits, gate_dtype, state_in, out, state_out, B, T, Hqk, Hv, dk,
+                              dv, layout);
+    if (st != GDN_OK) return st;
+    const size_t need = gdn_prefill_workspace_bytes(B, T, Hv, dk, dv);
+    if (need > kStaticScratchBytes)
+        return fail(GDN_ERR_UNSUPPORTED,
+                    "gdn_prefill_fwd_noalloc: this problem needs %zu B of workspace, the static scratch holds %zu B "
+                    "(use gdn_prefill_fwd or gdn_prefill_fwd_ws)",
+                    need, kStaticScratchBytes);
+    if ((st = check_sm100()) != GDN_OK) return st;
+    int dev = 0;
+    if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64)
+        return fail(GDN_ERR_CUDA, "gdn_prefill_fwd_noalloc: no current device");
+    // once per device, with that device current: the address of the static scratch
+    std::call_once(g_scratch_once[dev], [dev]() {
+        void* p = nullptr;
+        const cudaError_t e = cudaGetSymbolAddress(&p, g_prefill_scratch);
+        g_scratch_ptr[dev] = p;
+        g_scratch_status[dev] = (e == cudaSuccess && p != nullptr) ? GDN_OK : GDN_ERR_CUDA;
+    });
+    if (g_scratch_status[dev] != GDN_OK)
+        return fail(GDN_ERR_CUDA, "gdn_prefill_fwd_noalloc: cudaGetSymbolAddress of the static scratch failed");
+    return gdn_prefill_fwd_ws(q, k, v, A_log, a, b_logits, gate_dtype, dt_bias, dt_bias_vec, mask, state_in, out,
+                              state_out, B, T, Hqk, Hv, dk, dv, layout, scale, g_scratch_ptr[dev], kStaticScratchBytes,
+                              stream);
+}

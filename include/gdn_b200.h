@@ -115,6 +115,21 @@ int gdn_prefill_fwd_ws(const void* q, const void* k, const void* v,
                        float scale, void* workspace, size_t workspace_bytes, void* stream);
 
 /*
+ * gdn_prefill_fwd without any device allocation: the workspace is a static
+ * 32 MiB device array inside the library, so problems whose
+ * gdn_prefill_workspace_bytes exceeds 32 MiB return GDN_ERR_UNSUPPORTED.
+ * Calls on one device share that array and must be ordered (one stream or
+ * externally serialised).  Same arguments and results as gdn_prefill_fwd.
+ */
+int gdn_prefill_fwd_noalloc(const void* q, const void* k, const void* v,
+                            const float* A_log, const void* a, const void* b_logits, int gate_dtype,
+                            float dt_bias, const float* dt_bias_vec,
+                            const float* mask, const float* state_in,
+                            void* out, float* state_out,
+                            int B, int T, int Hqk, int Hv, int dk, int dv, int layout,
+                            float scale, void* stream);
+
+/*
  * Single-token decode step, state updated in place if state_out == state_in.
  * Replaces gdn_decode_cuda(), kernels/decode.cu:131-162, and its torch wrapper
  * gdn_decode_forward(), kernels/decode.cu:172-214 (math: reference/decode_ref.py:11-61).
