@@ -1452,11 +1452,15 @@ extern "C" int gdn_prefill_fwd(const void* q, const void* k, const void* v, cons
 }
 
 // ---------------------------------------------------------------------------
-// Allocation-free prefill for callers that cannot allocate device memory: the
-// workspace is a static device array of kStaticScratchBytes (32 MiB), enough
-// for ~540 chunk records at dk=128 (e.g. B*Hv = 8 sequences of 4096 tokens).
-// Calls on one device share it, so they must be ordered (one stream, or
-// externally serialised).
+// Allocation-free prefill, for callers that cannot allocate device memory at
+// call time (an engine that reserved the GPU's memory for its own pools, a
+// plugin whose host forbids allocation in its execute callback).  The
+// workspace is a static device array of kStaticScratchBytes (32 MiB, held on
+// every GPU that loads the library), enough for ~540 chunk records at dk=128
+// (e.g. B*Hv = 8 sequences of 4096 tokens).  Every record value and the carried
+// state are written by a call before that call uses them, so the array's
+// contents from the previous call need no clearing; calls that overlap on the
+// GPU race on it.
 // ---------------------------------------------------------------------------
 namespace gdn {
 constexpr size_t kStaticScratchBytes = size_t(32) << 20;
@@ -1486,7 +1490,9 @@ extern "C" int gdn_prefill_fwd_noalloc(const void* q, const void* k, const void*
     int dev = 0;
     if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64)
         return fail(GDN_ERR_CUDA, "gdn_prefill_fwd_noalloc: no current device");
-    // once per device, with that device current: the address of the static scratch
+    // once per device, with that device current: the device address of the static
+    // scratch (the symbol itself is only a host-side stand-in); this first call
+    // should come before any stream capture
     std::call_once(g_scratch_once[dev], [dev]() {
         void* p = nullptr;
         const cudaError_t e = cudaGetSymbolAddress(&p, g_prefill_scratch);

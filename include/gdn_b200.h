@@ -115,11 +115,29 @@ int gdn_prefill_fwd_ws(const void* q, const void* k, const void* v,
                        float scale, void* workspace, size_t workspace_bytes, void* stream);
 
 /*
- * gdn_prefill_fwd without any device allocation: the workspace is a static
- * 32 MiB device array inside the library, so problems whose
- * gdn_prefill_workspace_bytes exceeds 32 MiB return GDN_ERR_UNSUPPORTED.
- * Calls on one device share that array and must be ordered (one stream or
- * externally serialised).  Same arguments and results as gdn_prefill_fwd.
+ * gdn_prefill_fwd for callers that cannot allocate device memory.  No
+ * counterpart in the reference, whose kernel needs no workspace.
+ *
+ * The prefill needs a workspace (one record per 64-token chunk, see
+ * gdn_prefill_workspace_bytes).  Some callers cannot get one at call time:
+ * an engine that reserved the GPU's memory up front for its own pools (a
+ * cudaMalloc would fail or fragment that reservation), or a plugin whose
+ * host forbids allocation inside its execute callback.  This entry point
+ * takes the workspace from a 32 MiB array compiled into the library (held on
+ * every GPU that loads the library until the process exits) and makes no
+ * cudaMalloc, cudaMallocAsync or other allocating call.
+ *
+ *   - Limit: problems with gdn_prefill_workspace_bytes(B, T, Hv, dk, dv) > 32 MiB
+ *     return GDN_ERR_UNSUPPORTED (about 540 chunk records at dk = 128, e.g.
+ *     8 sequences of 4096 tokens); use gdn_prefill_fwd_ws for larger ones.
+ *   - The first call on a device looks up the array's device address
+ *     (cudaGetSymbolAddress, once per device); make that first call before
+ *     any stream capture.
+ *   - Every call uses the same array, which keeps the previous call's
+ *     contents; each call writes every value it uses before using it, so
+ *     nothing needs clearing.  Calls that overlap on the GPU (different
+ *     streams, different host threads) race on it: order them.
+ * Same arguments, status codes and results as gdn_prefill_fwd.
  */
 int gdn_prefill_fwd_noalloc(const void* q, const void* k, const void* v,
                             const float* A_log, const void* a, const void* b_logits, int gate_dtype,
