@@ -259,6 +259,7 @@ def run_ours(args):
 
     dec = run_decode(args, rank, world, dev, stream, hbm_peak)
     prj = run_proj(args, world, dev, stream, tf_peak)
+    lay = run_layer(world, dev, stream, hbm_peak)
     cpu = cpu_baseline_prefill() if (rank == 0 and world == 1 and not args.no_cpu_baseline) else None
 
     if rank == 0:
@@ -283,6 +284,7 @@ def run_ours(args):
             "clocks": clocks.summary(),
             "decode": dec,
             "proj": prj,
+            "layer": lay,
             "cpu_baseline": cpu,
         }
         print(json.dumps(line), flush=True)
@@ -345,6 +347,38 @@ def run_proj(args, world, dev, stream, tf_peak):
     tf = flops / (ms * 1e-3) / 1e12
     return {"config": "config3 fused q|k|v projection+conv4+SiLU, x [2,8192,2048] -> 8192 channels",
             "ms_per_launch": ms, "tflops": tf, "frac_of_measured_bf16": tf / tf_peak, "frac_of_2250": tf / 2250.0}
+
+
+def run_layer(world, dev, stream, hbm_peak):
+    """Config 3: the whole layer (RMSNorm, q|k|v projection + conv4 + SiLU with
+    q/k L2 norm, z/a/b projections, chunked prefill over 16 q/k and 32 value
+    heads, gated output norm, output projection) over x [2, 8192, 2048], then
+    128 decode steps carrying the state, each step one CUDA-graph replay."""
+    import torch
+    from gdn_18646_b200.layer import DecodeGraph, GDNConfig, GDNLayer, make_weights
+    cfg = GDNConfig()
+    layer = GDNLayer(make_weights(cfg, device=dev, seed=3), cfg)
+    g = torch.Generator(device=dev).manual_seed(7)
+    B, T, n_dec = 2, 8192, 128
+    x = torch.randn(B, T, cfg.hidden, generator=g, device=dev).bfloat16()
+    xd = torch.randn(n_dec, B, 1, cfg.hidden, generator=g, device=dev).bfloat16()
+    ms_pf = timed(lambda: layer.prefill(x), 5, 2, world, stream) / 5
+    _, st = layer.prefill(x)
+    graph = DecodeGraph(layer, st, B)
+
+    def decode_all():
+        for t in range(n_dec):
+            graph.step(xd[t])
+
+    ms_dec = timed(decode_all, 3, 1, world, stream) / (3 * n_dec)
+    w_bytes = sum(v.numel() * v.element_size() for k_, v in layer.w.items() if k_.startswith("W_"))
+    state_bytes = 2 * B * cfg.n_v * cfg.dk * cfg.dv * 4
+    return {"config": "config3 layer: prefill x [2, 8192, 2048] then 128 decode steps (CUDA graph per step)",
+            "prefill_ms": ms_pf, "prefill_tokens_per_s": B * T / (ms_pf * 1e-3),
+            "decode_ms_per_step": ms_dec, "decode_tokens_per_s": B / (ms_dec * 1e-3),
+            "decode_bytes_per_step": w_bytes + state_bytes,
+            "decode_gbs": (w_bytes + state_bytes) / (ms_dec * 1e-3) / 1e9,
+            "decode_frac_of_measured_hbm": (w_bytes + state_bytes) / (ms_dec * 1e-3) / 1e9 / hbm_peak}
 
 
 def run_long(args, rank, world, dev, stream, hbm_peak, tf_peak, peak_kind):
@@ -485,6 +519,18 @@ def run_only(args):
         def step():
             ops.prefill(inp["q"], inp["k"], inp["v"], inp["A_log"], inp["a"], inp["b"], state_in=inp["state_in"],
                         scale=c["dk"] ** -0.5, out=out, state_out=s_out)
+    elif args.only == "layer_decode":
+        from gdn_18646_b200.layer import DecodeGraph, GDNConfig, GDNLayer, make_weights
+        cfg = GDNConfig()
+        layer = GDNLayer(make_weights(cfg, device=dev, seed=3), cfg)
+        g = torch.Generator(device=dev).manual_seed(7)
+        B = 2
+        _, st = layer.prefill(torch.randn(B, 256, cfg.hidden, generator=g, device=dev).bfloat16())
+        graph = DecodeGraph(layer, st, B)
+        xd = torch.randn(B, 1, cfg.hidden, generator=g, device=dev).bfloat16()
+
+        def step():
+            graph.step(xd)
     elif args.only == "decode":
         c = C2
         g = torch.Generator(device=dev).manual_seed(5)
@@ -524,7 +570,7 @@ def main(argv=None):
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--workload", choices=["prefill", "long"], default="prefill")
     ap.add_argument("--no-cpu-baseline", action="store_true")
-    ap.add_argument("--only", choices=["prefill", "decode", "proj"], default=None,
+    ap.add_argument("--only", choices=["prefill", "decode", "proj", "layer_decode"], default=None,
                     help="run just one kernel's workload (for profiling); prints a short JSON line")
     args = ap.parse_args(argv)
     if args.only:

@@ -5,8 +5,8 @@ this package is the torch-facing host side: the functional ops and the
 reference-surface ``exts()`` modules.
 """
 from . import _lib
-from .ops import (CHUNK, DecodeModule, PrefillModule, ProjModule, RMSNormModule, decode_step, exts,
+from .ops import (CHUNK, DecodeModule, PrefillModule, ProjModule, RMSNormModule, decode_proj, decode_step, exts,
                   gated_rmsnorm, prefill, proj_conv_silu, rmsnorm)
 
-__all__ = ["CHUNK", "DecodeModule", "PrefillModule", "ProjModule", "RMSNormModule", "decode_step", "exts",
+__all__ = ["CHUNK", "DecodeModule", "PrefillModule", "ProjModule", "RMSNormModule", "decode_proj", "decode_step", "exts",
            "gated_rmsnorm", "prefill", "proj_conv_silu", "rmsnorm", "_lib"]

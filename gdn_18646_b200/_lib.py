@@ -35,6 +35,12 @@ _I = ctypes.c_int
 _F = ctypes.c_float
 _Z = ctypes.c_size_t
 
+class ProjSegment(ctypes.Structure):
+    """gdn_proj_segment (include/gdn_b200.h): one channel segment of gdn_decode_proj_fwd."""
+    _fields_ = [("W", _P), ("y", _P), ("conv_w", _P), ("conv_state_in", _P), ("conv_state_out", _P),
+                ("C", _I), ("ldy", _I), ("l2_group", _I)]
+
+
 # name -> argtypes (every entry returns int unless listed in _STR_FUNCS)
 SIGNATURES = {
     "gdn_prefill_fwd": [_P, _P, _P, _P, _P, _P, _I, _F, _P, _P, _P, _P, _P,
@@ -49,6 +55,7 @@ SIGNATURES = {
     "gdn_decode_step": [_P, _P, _P, _P, _P, _I, _P, _P, _P, _P, _P, _I, _I, _I, _I, _I, _F, _P],
     "gdn_rmsnorm_fwd": [_P, _P, _P, _I, _I, _F, _P],
     "gdn_gated_rmsnorm_fwd": [_P, _I, _P, _P, _P, _I, _I, _F, _P],
+    "gdn_decode_proj_fwd": [_P, _P, _F, _I, _I, ctypes.POINTER(ProjSegment), _I, _P],
     "gdn_proj_conv_silu_fwd": [_P, _P, _P, _P, _I, _I, _I, _I, _P, _P, _I, _P],
     "gdn_check_device_error": [],
     "gdn_last_error": [],

@@ -6,8 +6,10 @@ Prefill (T tokens):
               -> chunked gated delta rule (grouped value heads, [B,T,H,D] layout)
               -> gated RMSNorm(o) * SiLU(z) -> x Wo^T
 Decode (1 token) runs the same blocks with the carried recurrent state
-[B,Hv,dk,dv] fp32 and the three conv histories [B,C,3] bf16; ``prefill``
-returns both so decode continues a prefilled sequence.
+[B,Hv,dk,dv] fp32 and the three conv histories [B,C,3] bf16 (the last three
+projected values per channel); ``prefill`` returns both so decode continues a
+prefilled sequence.  The decode projections are one weight-streaming GEMV
+launch over that history (no recompute of the last four tokens).
 
 Composition follows the reference layer (gdn_layer.py:120-199) with the
 additions of the BASELINE layer (L2-normalised q/k, 16 q/k heads shared by 32
@@ -121,51 +123,60 @@ class GDNLayer:
     def decode(self, x: torch.Tensor, state: dict, out_state: dict | None = None):
         """One token: x [B,1,D] bf16 -> (y [B,1,D] bf16, state).  The recurrent
         state is updated in place; conv histories go to ``out_state`` (fresh
-        buffers by default).  All shapes are static, so the call can be
-        captured in a CUDA graph."""
+        buffers by default; ``out_state=state`` updates them in place too).
+
+        Four launches: RMSNorm + q|k|v (conv4, SiLU, q/k L2 norm) + z + a + b as
+        one weight-streaming GEMV over the cached conv history
+        (gdn_decode_proj_fwd), the recurrence step, the gated output norm, and
+        the output projection (the same GEMV kernel).  All shapes are static, so
+        the call can be captured in a CUDA graph."""
         c, w = self.cfg, self.w
         B = x.shape[0]
         D = c.hidden
-        xn = ops.rmsnorm(x.reshape(B, D), w["norm_gamma"], c.eps).reshape(B, 1, D)
         if out_state is None:
             out_state = dict(recurrent=state["recurrent"],
                              conv_q=torch.empty_like(state["conv_q"]), conv_k=torch.empty_like(state["conv_k"]),
                              conv_v=torch.empty_like(state["conv_v"]))
-        q, k, v, z, ab = self._project(xn, state, out_state)
-        a = ab[:, 0, :c.n_v].contiguous()
-        b = ab[:, 0, c.n_v:].contiguous()
+        q, k, v, z, a, b = ops.decode_proj(x.reshape(B, D), [
+            dict(W=w["W_q"], conv_w=w["conv_q"], conv_state_in=state["conv_q"], conv_state_out=out_state["conv_q"],
+                 l2_group=c.dk),
+            dict(W=w["W_k"], conv_w=w["conv_k"], conv_state_in=state["conv_k"], conv_state_out=out_state["conv_k"],
+                 l2_group=c.dk),
+            dict(W=w["W_v"], conv_w=w["conv_v"], conv_state_in=state["conv_v"], conv_state_out=out_state["conv_v"]),
+            dict(W=w["W_z"]),
+            dict(W=w["W_ab"][:c.n_v]),
+            dict(W=w["W_ab"][c.n_v:]),
+        ], norm_gamma=w["norm_gamma"], eps=c.eps)
         o = ops.decode_step(q.view(B, c.n_qk, c.dk), k.view(B, c.n_qk, c.dk), v.view(B, c.n_v, c.dv), a, b,
                             w["A_log"], w["dt_bias"], state["recurrent"], scale=self.scale,
                             state_out=out_state["recurrent"])
         y = ops.gated_rmsnorm(o.view(B * c.n_v, c.dv), z.view(B * c.n_v, c.dv), w["onorm_gamma"], c.eps)
-        return (y.view(B, 1, c.v_dim) @ w["W_o"].T), out_state
+        (out,) = ops.decode_proj(y.view(B, c.v_dim), [dict(W=w["W_o"])])
+        return out.view(B, 1, D), out_state
 
 
 class DecodeGraph:
     """A CUDA graph of one ``GDNLayer.decode`` step over static buffers, so a
-    decode loop costs one graph launch per token."""
+    decode loop costs one graph launch per token.  The recurrent state and the
+    conv histories of ``state`` are updated in place by every step."""
 
     def __init__(self, layer: GDNLayer, state: dict, B: int):
         self.layer = layer
         dev = state["recurrent"].device
         self.x = torch.zeros(B, 1, layer.cfg.hidden, dtype=torch.bfloat16, device=dev)
         self.state = state
-        self.next_conv = {k_: torch.empty_like(v_) for k_, v_ in state.items() if k_ != "recurrent"}
-        # warm up once outside the graph (first-call set-up of the kernels)
+        # warm up once outside the graph (first-call set-up of the kernels) on scratch copies
         s = torch.cuda.Stream()
         s.wait_stream(torch.cuda.current_stream())
         with torch.cuda.stream(s):
             scratch = {k_: v_.clone() for k_, v_ in state.items()}
-            layer.decode(self.x, scratch, dict(scratch))
+            layer.decode(self.x, scratch, scratch)
         torch.cuda.current_stream().wait_stream(s)
         self.graph = torch.cuda.CUDAGraph()
         with torch.cuda.graph(self.graph):
-            out_state = dict(recurrent=state["recurrent"], **self.next_conv)
-            self.y, _ = layer.decode(self.x, state, out_state)
+            self.y, _ = layer.decode(self.x, state, state)
 
     def step(self, x: torch.Tensor) -> torch.Tensor:
         self.x.copy_(x)
         self.graph.replay()
-        for k_, buf in self.next_conv.items():       # carry the conv histories
-            self.state[k_].copy_(buf)
         return self.y

@@ -170,6 +170,43 @@ def proj_conv_silu(x, W, conv_w, *, conv_state_in=None, conv_state_out=None, l2n
     return out
 
 
+def decode_proj(x, segments, *, norm_gamma=None, eps=1e-6):
+    """Input projections of one decode step in one launch (gdn_decode_proj_fwd).
+
+    x [B, D] bf16 (B <= 8); ``segments``: list of dicts with ``W`` [C, D] bf16 and
+    optionally ``conv_w`` [C, 4], ``conv_state_in`` / ``conv_state_out`` [B, C, 3]
+    (may be the same tensor: updated in place), ``l2_group`` and ``out`` [B, C].
+    With ``norm_gamma`` x is RMS-normalised first.  Returns the list of outputs,
+    each [B, C] bf16: SiLU(conv4) (L2-normalised per group when asked) for the
+    segments with ``conv_w``, plain bf16(x W^T) rows for the others."""
+    _cuda_contig(x, "x", torch.bfloat16)
+    _need(x.dim() == 2, "x must be [B, D]")
+    B, D = x.shape
+    if norm_gamma is not None:
+        _cuda_contig(norm_gamma, "norm_gamma", torch.bfloat16)
+    segs = (_lib.ProjSegment * len(segments))()
+    outs = []
+    for i, sg in enumerate(segments):
+        W = sg["W"]
+        _cuda_contig(W, f"segments[{i}].W", torch.bfloat16)
+        _need(W.shape[1] == D, f"segments[{i}].W must be [C, {D}]")
+        C = W.shape[0]
+        out = sg.get("out")
+        if out is None:
+            out = torch.empty(B, C, dtype=torch.bfloat16, device=x.device)
+        _need(out.dtype == torch.bfloat16 and out.is_cuda and out.shape[-1] == C and out.stride(-1) == 1,
+              f"segments[{i}].out must be bf16 [B, {C}] with unit inner stride")
+        for name in ("conv_w", "conv_state_in", "conv_state_out"):
+            if sg.get(name) is not None:
+                _cuda_contig(sg[name], f"segments[{i}].{name}", torch.bfloat16)
+        segs[i] = _lib.ProjSegment(_ptr(W), _ptr(out), _ptr(sg.get("conv_w")), _ptr(sg.get("conv_state_in")),
+                                   _ptr(sg.get("conv_state_out")), C, out.stride(0) if B > 1 else C,
+                                   int(sg.get("l2_group", 0)))
+        outs.append(out)
+    _lib.call("gdn_decode_proj_fwd", _ptr(x), _ptr(norm_gamma), float(eps), B, D, segs, len(segments), _stream())
+    return outs
+
+
 # ---------------------------------------------------------------------------
 # reference-surface modules (drop-in for GDNLayerCustom's ``exts`` dict)
 # ---------------------------------------------------------------------------

@@ -185,6 +185,44 @@ int gdn_gated_rmsnorm_fwd(const void* x, int x_dtype, const void* z, const void*
                           int R, int D, float eps, void* stream);
 
 /*
+ * One channel segment of gdn_decode_proj_fwd: output channels c in [0, C) of
+ * weight W [C, D] bf16, written to y[b * ldy + c] (bf16).
+ *   conv_w         bf16 [C, 4] or NULL.  With it: y = SiLU(conv4(history, x.W[c]))
+ *                  with the rounding points of gdn_proj_conv_silu_fwd; without it:
+ *                  y = bf16(x . W[c]) (a plain GEMV row, e.g. z, a, b, W_o).
+ *   conv_state_in  bf16 [B, C, 3] or NULL (zeros): the last 3 projected values
+ *                  per channel, oldest first (what gdn_proj_conv_silu_fwd and the
+ *                  prefill leave in conv_state_out).
+ *   conv_state_out bf16 [B, C, 3] or NULL; receives (h1, h2, this step's value);
+ *                  may be the same buffer as conv_state_in.
+ *   l2_group       0, or g dividing 128 (C % 128 == 0): each g-wide group of y
+ *                  is L2-normalised (fp32, eps 1e-6) before the store.
+ * C % 16 == 0; W 16-byte and conv_w 8-byte aligned.
+ */
+typedef struct {
+    const void* W;
+    void* y;
+    const void* conv_w;
+    const void* conv_state_in;
+    void* conv_state_out;
+    int C;
+    int ldy;
+    int l2_group;
+} gdn_proj_segment;
+
+/*
+ * Input projections of one decode step (one token per sequence) in a single
+ * launch: up to 8 segments (e.g. q | k | v with conv + SiLU, q/k L2-normalised
+ * per head, then z, a, b as plain rows) over the same x [B, D] bf16, with an
+ * optional fused RMSNorm of x (norm_gamma bf16 [D] or NULL, eps).  Replaces the
+ * reference's per-step 4-token recompute, gdn_layer.py:58-69
+ * (_decode_fused_proj_step), with a 1-token GEMV over the cached conv history.
+ * 1 <= B <= 8, D % 256 == 0, (16 + B) * D * 2 bytes within ~200 KB (D <= 4096 at B = 8).
+ */
+int gdn_decode_proj_fwd(const void* x, const void* norm_gamma, float eps, int B, int D,
+                        const gdn_proj_segment* segs, int nseg, void* stream);
+
+/*
  * Fused input projection + causal depthwise conv1d (kernel 4) + SiLU.
  * Replaces fused_proj_conv_silu(), kernels/fused_proj_conv_silu.cu:298-355
  * (math: reference/fused_proj_conv_silu_ref.py:33-67).

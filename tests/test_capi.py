@@ -148,3 +148,26 @@ def test_prefill_ws_rejects_small_workspace(lib):
     args = args[:-1] + [FAKE, 1024, None]                          # workspace, workspace_bytes, stream
     assert _lib.call_status("gdn_prefill_fwd_ws", *args) == _lib.GDN_ERR_SHAPE
     assert "workspace" in _lib.last_error()
+
+
+def test_decode_proj_rejects(lib):
+    def seg(**over):
+        d = dict(W=FAKE, y=FAKE, conv_w=None, conv_state_in=None, conv_state_out=None, C=256, ldy=256, l2_group=0)
+        d.update(over)
+        return _lib.ProjSegment(**d)
+
+    def call(segs, B=2, D=2048, x=FAKE):
+        arr = (_lib.ProjSegment * max(1, len(segs)))(*segs)
+        return _lib.call_status("gdn_decode_proj_fwd", x, None, 1e-6, B, D, arr, len(segs), None)
+
+    assert call([seg()], x=None) == _lib.GDN_ERR_NULL
+    assert call([seg()], B=9) == _lib.GDN_ERR_SHAPE
+    assert call([seg()], D=2000) == _lib.GDN_ERR_SHAPE
+    assert call([]) == _lib.GDN_ERR_SHAPE
+    assert call([seg(C=40, ldy=40)]) == _lib.GDN_ERR_SHAPE
+    assert call([seg()], D=1000) == _lib.GDN_ERR_SHAPE
+    assert call([seg()], B=8, D=8192) == _lib.GDN_ERR_SHAPE
+    assert call([seg(l2_group=128, C=192, ldy=192)]) == _lib.GDN_ERR_SHAPE
+    assert call([seg(conv_state_in=FAKE)]) == _lib.GDN_ERR_NULL
+    assert call([seg(W=ODD)]) == _lib.GDN_ERR_ALIGN
+    assert "gdn_decode_proj_fwd" in _lib.last_error()

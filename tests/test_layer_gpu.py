@@ -53,7 +53,11 @@ def test_layer_prefill_then_decode_matches_full_prefill(cuda_device):
     _close(y_cat, to_np(y_full))
     assert O.rel_fro(to_np(st["recurrent"]), to_np(st_full["recurrent"])) < 1e-3
     for key in ("conv_q", "conv_k", "conv_v"):
-        assert torch.equal(st[key], st_full[key])
+        # the decode projection is a GEMV, the prefill's a tensor-core GEMM: the
+        # fp32 summation orders differ, so a cached bf16 value may differ by an ulp
+        g, w = O.bf16_to_f32(to_np(st[key])), O.bf16_to_f32(to_np(st_full[key]))
+        assert np.all(np.abs(g - w) <= np.abs(w) * 2.0 ** -6 + 1e-2)
+        assert np.mean(g != w) <= 0.05
 
 
 def test_layer_decode_cuda_graph_matches_eager(cuda_device):
