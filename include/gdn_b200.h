@@ -195,9 +195,9 @@ int gdn_gated_rmsnorm_fwd(const void* x, int x_dtype, const void* z, const void*
  *                  prefill leave in conv_state_out).
  *   conv_state_out bf16 [B, C, 3] or NULL; receives (h1, h2, this step's value);
  *                  may be the same buffer as conv_state_in.
- *   l2_group       0, or g dividing 128 (C % 128 == 0): each g-wide group of y
+ *   l2_group       0, or g >= 8 dividing 128 and C: each g-wide group of y
  *                  is L2-normalised (fp32, eps 1e-6) before the store.
- * C % 16 == 0; W 16-byte and conv_w 8-byte aligned.
+ * C % 16 == 0; W, conv_w and conv_state_in 16-byte aligned.
  */
 typedef struct {
     const void* W;
@@ -217,7 +217,8 @@ typedef struct {
  * optional fused RMSNorm of x (norm_gamma bf16 [D] or NULL, eps).  Replaces the
  * reference's per-step 4-token recompute, gdn_layer.py:58-69
  * (_decode_fused_proj_step), with a 1-token GEMV over the cached conv history.
- * 1 <= B <= 8, D % 256 == 0, (16 + B) * D * 2 bytes within ~200 KB (D <= 4096 at B = 8).
+ * 1 <= B <= 8, D % 256 == 0, and the B token rows must leave room for two weight
+ * stages in shared memory: any D <= 5888 at B = 8, D <= 8192 at B <= 4.
  */
 int gdn_decode_proj_fwd(const void* x, const void* norm_gamma, float eps, int B, int D,
                         const gdn_proj_segment* segs, int nseg, void* stream);

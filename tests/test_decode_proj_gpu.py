@@ -37,7 +37,8 @@ def _oracle_seg(xn, W, cw=None, hist=None, l2=0):
     return y, np.concatenate([h[:, :, 1:], proj[:, 0][:, :, None]], axis=2)
 
 
-@pytest.mark.parametrize("B,D,norm", [(2, 2048, True), (1, 1024, False), (8, 1024, True), (5, 4096, False)])
+@pytest.mark.parametrize("B,D,norm", [(2, 2048, True), (1, 1024, False), (8, 1024, True), (5, 4096, False),
+                                      (3, 4352, True)])   # 4352: 256-column stages
 def test_decode_proj_segments_vs_oracle(cuda_device, B, D, norm):
     import torch
     from gdn_18646_b200 import ops
@@ -45,8 +46,10 @@ def test_decode_proj_segments_vs_oracle(cuda_device, B, D, norm):
     x = _bf16(rng, (B, D))
     gamma = O.f32_to_bf16(1.0 + 0.1 * rng.standard_normal(D, dtype=np.float32))
     xn = O.rmsnorm(x, gamma, 1e-6) if norm else x
-    segs = [  # (C, conv, l2): q-like (groups wider than a CTA: cluster), small groups, v-like, z-like, a-like
-        (256, True, 128), (64, True, 16), (384, True, 0), (512, False, 0), (32, False, 0), (48, False, 0)]
+    segs = [  # (C, conv, l2): q-like (groups wider than a tile: cluster), small groups, 64-wide groups whose
+        # last cluster group is half empty, v-like, z-like, a-like
+        (256, True, 128), (64, True, 16), (192, True, 64), (384, True, 0), (512, False, 0), (32, False, 0),
+        (48, False, 0)]
     W = [_bf16(rng, (C, D), D ** -0.5) for C, _, _ in segs]
     cw = [_bf16(rng, (C, 4), 0.5) if conv else None for C, conv, _ in segs]
     hist = [_bf16(rng, (B, C, 3)) if conv else None for C, conv, _ in segs]
