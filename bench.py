@@ -260,6 +260,7 @@ def run_ours(args):
     dec = run_decode(args, rank, world, dev, stream, hbm_peak)
     prj = run_proj(args, world, dev, stream, tf_peak)
     lay = run_layer(world, dev, stream, hbm_peak)
+    vl = run_varlen(world, dev, stream)
     cpu = cpu_baseline_prefill() if (rank == 0 and world == 1 and not args.no_cpu_baseline) else None
 
     if rank == 0:
@@ -285,6 +286,7 @@ def run_ours(args):
             "decode": dec,
             "proj": prj,
             "layer": lay,
+            "varlen": vl,
             "cpu_baseline": cpu,
         }
         print(json.dumps(line), flush=True)
@@ -387,6 +389,57 @@ def run_layer(world, dev, stream, hbm_peak):
             "decode_bytes_per_layer_step": w_bytes + state_bytes,
             "decode_gbs": (w_bytes + state_bytes) / (ms_dec * 1e-3) / 1e9,
             "decode_frac_of_measured_hbm": (w_bytes + state_bytes) / (ms_dec * 1e-3) / 1e9 / hbm_peak}
+
+
+def run_varlen(world, dev, stream):
+    """Packed variable-length prefill against the same sequences padded to the
+    longest one: 16 sequences of seeded lengths in [64, 4096] (H=16, dk=dv=128,
+    config-1 distributions); tokens/s counts real tokens only."""
+    import numpy as np
+    import torch
+    from gdn_18646_b200 import ops
+    rng = np.random.default_rng(11)
+    lens = rng.integers(64, 4097, size=16)
+    N, H, dk, dv = len(lens), 16, 128, 128
+    Ttot, Tmax = int(lens.sum()), int(lens.max())
+    g = torch.Generator(device=dev).manual_seed(12)
+    q = torch.nn.functional.normalize(torch.randn(Ttot, H, dk, generator=g, device=dev), dim=-1).bfloat16()
+    k = torch.nn.functional.normalize(torch.randn(Ttot, H, dk, generator=g, device=dev), dim=-1).bfloat16()
+    v = torch.randn(Ttot, H, dv, generator=g, device=dev).bfloat16()
+    a = torch.randn(H, Ttot, generator=g, device=dev).bfloat16()
+    b = torch.randn(H, Ttot, generator=g, device=dev).bfloat16()
+    A_log = torch.full((H,), math.log(0.1), device=dev)
+    s0 = torch.randn(N, H, dk, dv, generator=g, device=dev) * 0.02
+    cu = torch.tensor(np.concatenate([[0], np.cumsum(lens)]), dtype=torch.int32, device=dev)
+    out = torch.empty_like(v)
+    s_out = torch.empty_like(s0)
+    # the same sequences padded to Tmax (mask 0 on the padding), layout [N, T, H, D]
+    qp = torch.zeros(N, Tmax, H, dk, dtype=torch.bfloat16, device=dev)
+    kp, vp = torch.zeros_like(qp), torch.zeros(N, Tmax, H, dv, dtype=torch.bfloat16, device=dev)
+    ap = torch.zeros(N, H, Tmax, dtype=torch.bfloat16, device=dev)
+    bp = torch.zeros_like(ap)
+    mask = torch.zeros(N, Tmax, device=dev)
+    for i, L in enumerate(lens):
+        t0 = int(cu[i])
+        qp[i, :L], kp[i, :L], vp[i, :L] = q[t0:t0 + L], k[t0:t0 + L], v[t0:t0 + L]
+        ap[i, :, :L], bp[i, :, :L] = a[:, t0:t0 + L], b[:, t0:t0 + L]
+        mask[i, :L] = 1.0
+    outp = torch.empty_like(vp)
+
+    def packed():
+        ops.prefill_varlen(q, k, v, A_log, a, b, cu, max_len=Tmax, state_in=s0, scale=dk ** -0.5, out=out,
+                           state_out=s_out)
+
+    def padded():
+        ops.prefill(qp, kp, vp, A_log, ap, bp, mask=mask, state_in=s0, scale=dk ** -0.5, layout="bthd", out=outp,
+                    state_out=s_out)
+
+    ms_v = timed(packed, 10, 3, world, stream) / 10
+    ms_p = timed(padded, 10, 3, world, stream) / 10
+    return {"config": f"{N} sequences, lengths {int(lens.min())}..{Tmax} (sum {Ttot}), H=16 dk=dv=128",
+            "varlen_ms": ms_v, "varlen_tokens_per_s": Ttot / (ms_v * 1e-3),
+            "padded_ms": ms_p, "padded_tokens_per_s": Ttot / (ms_p * 1e-3),
+            "launches": 3}
 
 
 def run_long(args, rank, world, dev, stream, hbm_peak, tf_peak, peak_kind):

@@ -6,7 +6,7 @@ reference-surface ``exts()`` modules.
 """
 from . import _lib
 from .ops import (CHUNK, DecodeModule, PrefillModule, ProjModule, RMSNormModule, decode_proj, decode_step, exts,
-                  gated_rmsnorm, prefill, proj_conv_silu, rmsnorm)
+                  gated_rmsnorm, prefill, prefill_varlen, proj_conv_silu, rmsnorm)
 
 __all__ = ["CHUNK", "DecodeModule", "PrefillModule", "ProjModule", "RMSNormModule", "decode_proj", "decode_step", "exts",
-           "gated_rmsnorm", "prefill", "proj_conv_silu", "rmsnorm", "_lib"]
+           "gated_rmsnorm", "prefill", "prefill_varlen", "proj_conv_silu", "rmsnorm", "_lib"]

@@ -27,7 +27,7 @@ unsigned int* device_error_word();         // per-device error flag (device poin
 inline bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
 
 // Device-side error flag bits.
-enum : unsigned int { DERR_TIMEOUT = 1u };
+enum : unsigned int { DERR_TIMEOUT = 1u, DERR_VARLEN = 2u };
 
 // ---------------------------------------------------------------------------
 // device helpers

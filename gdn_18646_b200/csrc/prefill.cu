@@ -143,6 +143,9 @@ struct GateArgs {
     uint8_t* rec;
     int ntasks, T, Hv, nchunks;
     float scale;
+    const int* cu;       // varlen: sequence b is packed tokens [cu[b], cu[b+1]); a, b_logits [Hv, Ttot]
+    int Ttot;
+    unsigned int* err;
 };
 
 struct PrepArgs {
@@ -151,6 +154,8 @@ struct PrepArgs {
     int ntasks;          // B * Hv * ncp: the chunks [c0, c0 + ncp) of every sequence
     int Hqk, Hv, nchunks, c0, ncp;
     float scale;
+    const int* cu;       // varlen sequence offsets or null
+    int Ttot;
 };
 
 // ---------------------------------------------------------------------------
@@ -207,7 +212,30 @@ struct ChainArgs {
     int T, Hqk, Hv, dv, ntiles;
     int nchunks_total;   // chunks of the whole sequence (record indexing)
     int c0, nchunks;     // this launch walks chunks [c0, c0 + nchunks)
+    const int* cu;       // varlen sequence offsets or null
+    uint16_t* out;       // varlen: o [Ttot, Hv, dv], written directly for each sequence's last chunk
+    int Ttot;
 };
+
+// Varlen: first token and length of sequence b.  Offsets that are negative,
+// decreasing or past Ttot make the sequence empty (nothing read or written for
+// it beyond its state) and raise DERR_VARLEN in the device error word.
+__device__ __forceinline__ int varlen_seq(const int* cu, int b, int Ttot, int& start, unsigned int* err) {
+    start = cu[b];
+    const int end = cu[b + 1];
+    if (start < 0 || end < start || end > Ttot) {
+        if (err) atomicOr(err, DERR_VARLEN);
+        start = 0;
+        return 0;
+    }
+    return end - start;
+}
+// chunks of a sequence of `len` tokens (at least one, so an empty sequence still
+// passes its state on), at most the launch's chunk count
+__device__ __forceinline__ int varlen_chunks(int len, int nchunks_total) {
+    const int n = len > 0 ? (len + kC - 1) / kC : 1;
+    return n < nchunks_total ? n : nchunks_total;
+}
 
 __device__ __forceinline__ void tmem_ld64(uint32_t taddr, float (&v)[64]) {
     float a[32], b[32];
@@ -412,10 +440,12 @@ prefill_gates_kernel(const GateArgs args) {
     const int lane = threadIdx.x & 31;
     const int task = blockIdx.x * 4 + (threadIdx.x >> 5);
     if (task >= args.ntasks) return;
-    const int T = args.T;
     const int bh = task / args.nchunks, c = task - bh * args.nchunks;
     const int h = bh % args.Hv, bidx = bh / args.Hv;
-    const long base = static_cast<long>(bh) * T;
+    // valid tokens of this sequence and the offset of its gates (varlen: [Hv, Ttot], packed)
+    int start = 0;
+    const int T = args.cu ? varlen_seq(args.cu, bidx, args.Ttot, start, args.err) : args.T;
+    const long base = args.cu ? static_cast<long>(h) * args.Ttot + start : static_cast<long>(bh) * T;
     const int t0 = 2 * lane;
     const int tok = c * kC + t0;
     float a0 = 0.f, a1 = 0.f, b0 = 0.f, b1 = 0.f, m0 = 0.f, m1 = 0.f;
@@ -516,24 +546,39 @@ __device__ __forceinline__ void prep_body(const CUtensorMap* map_q, const CUtens
     tc_fence_after();
     const uint32_t tmem = *tmem_slot;
 
+    // varlen: the next task at or after `task` (stride vgrid) inside its sequence's chunks
+    auto next_task = [&](int task) {
+        if (args.cu)
+            for (; task < args.ntasks; task += vgrid) {
+                const int bh = task / args.ncp, c = args.c0 + (task - bh * args.ncp);
+                int st0;
+                if (c < varlen_chunks(varlen_seq(args.cu, bh / args.Hv, args.Ttot, st0, nullptr), nchunks)) break;
+            }
+        return task;
+    };
     // q/k tiles and the gate vectors of `task` -> shared memory, completing on bar_qk
     auto issue_qk = [&](int task) {
         const int bh = task / args.ncp, c = args.c0 + (task - bh * args.ncp);
         const int hq = (bh % args.Hv) / group, bidx = bh / args.Hv;
+        // token row and batch coordinates (varlen: packed tokens, one batch)
+        int st0 = 0;
+        if (args.cu) varlen_seq(args.cu, bidx, args.Ttot, st0, nullptr);
+        const int trow = st0 + c * kC, bco = args.cu ? 0 : bidx;
         mbar_arrive_expect_tx(bar_qk, 2 * L::CB * 8192 + kGateBytes);
 #pragma unroll
         for (int cb = 0; cb < L::CB; ++cb) {
-            tma_load_4d(sm + cb * 16384, map_q, bar_qk, cb * 64, c * kC, hq, bidx);
-            tma_load_4d(sm + cb * 16384 + 8192, map_k, bar_qk, cb * 64, c * kC, hq, bidx);
+            tma_load_4d(sm + cb * 16384, map_q, bar_qk, cb * 64, trow, hq, bco);
+            tma_load_4d(sm + cb * 16384 + 8192, map_k, bar_qk, cb * 64, trow, hq, bco);
         }
         bulk_load(sm + L::OFF_G, args.rec + (static_cast<long>(bh) * nchunks + c) * R::BYTES + R::GB, kGateBytes,
                   bar_qk);
     };
-    if (leader && vblock < args.ntasks) issue_qk(vblock);
+    const int first = next_task(vblock);
+    if (leader && first < args.ntasks) issue_qk(first);
 
     int it = 0;
 #pragma unroll 1
-    for (int task = vblock; task < args.ntasks; task += vgrid, ++it) {
+    for (int task = first; task < args.ntasks; task = next_task(task + vgrid), ++it) {
         const uint32_t ph = it & 1;
         const int tbh = task / args.ncp;
         uint8_t* rec = args.rec + (static_cast<long>(tbh) * nchunks + args.c0 + (task - tbh * args.ncp)) * R::BYTES;
@@ -707,8 +752,9 @@ __device__ __forceinline__ void prep_body(const CUtensorMap* map_q, const CUtens
             bulk_commit();
             bulk_wait_read0();                        // the images (and A1 over N) have been read out
             // q/k shared memory is free: fetch the next task's tiles
-            if (!*abort_flag && task + vgrid < args.ntasks) {
-                issue_qk(task + vgrid);
+            const int nt = next_task(task + vgrid);
+            if (!*abort_flag && nt < args.ntasks) {
+                issue_qk(nt);
                 pending = true;
             }
         }
@@ -757,7 +803,12 @@ __device__ __forceinline__ void chain_body(const CUtensorMap* map_q, const CUten
     const int h = bh % args.Hv;
     const int bidx = bh / args.Hv;
     const int hq = h / (args.Hv / args.Hqk);
-    const int nchunks = args.nchunks;
+    // varlen: this sequence's first token row and length, its own chunk count
+    // (single-piece schedule), batch coordinate 0 of the packed tensors
+    int trow0 = 0;
+    const int seq_len = args.cu ? varlen_seq(args.cu, bidx, args.Ttot, trow0, nullptr) : args.T;
+    const int bco = args.cu ? 0 : bidx;
+    const int nchunks = args.cu ? varlen_chunks(seq_len, args.nchunks_total) : args.nchunks;
     const int v0 = tile * 128;
     const int dv_valid = min(128, args.dv - v0);
     const int nvb = (dv_valid + 63) / 64;
@@ -808,10 +859,10 @@ __device__ __forceinline__ void chain_body(const CUtensorMap* map_q, const CUten
                 mbar_arrive_expect_tx(&bars->slot_full[slot], 2 * L::CB * 8192 + 2 * DK * 128 + 8192 + 1024);
 #pragma unroll
                 for (int cb = 0; cb < L::CB; ++cb) {
-                    tma_load_4d(dst + L::Q_OFF + cb * 8192, map_q, &bars->slot_full[slot], cb * 64, (c0 + c) * kC, hq,
-                                bidx);
-                    tma_load_4d(dst + L::K_OFF + cb * 8192, map_k, &bars->slot_full[slot], cb * 64, (c0 + c) * kC, hq,
-                                bidx);
+                    tma_load_4d(dst + L::Q_OFF + cb * 8192, map_q, &bars->slot_full[slot], cb * 64,
+                                trow0 + (c0 + c) * kC, hq, bco);
+                    tma_load_4d(dst + L::K_OFF + cb * 8192, map_k, &bars->slot_full[slot], cb * 64,
+                                trow0 + (c0 + c) * kC, hq, bco);
                 }
                 bulk_load(dst + L::R_WTH, rec + R::WTH, 2 * DK * 128, &bars->slot_full[slot]);
                 bulk_load(dst + L::R_P, rec + R::P, 8192 + 1024, &bars->slot_full[slot]);
@@ -821,7 +872,8 @@ __device__ __forceinline__ void chain_body(const CUtensorMap* map_q, const CUten
                 if (c >= 1 && !mbar_wait_or_abort(&bars->va_free, (c - 1) & 1, err, abort_flag)) break;
                 mbar_arrive_expect_tx(&bars->va_full, nvb * 8192 + 16384);
                 for (int vb = 0; vb < nvb; ++vb)
-                    tma_load_4d(sm + L::OFF_V + vb * 8192, map_v, &bars->va_full, v0 + vb * 64, (c0 + c) * kC, h, bidx);
+                    tma_load_4d(sm + L::OFF_V + vb * 8192, map_v, &bars->va_full, v0 + vb * 64, trow0 + (c0 + c) * kC, h,
+                                bco);
                 bulk_load(sm + L::OFF_A1, rec0 + static_cast<long>(c) * R::BYTES + R::A1H, 16384, &bars->va_full);
             }
         }
@@ -1077,6 +1129,20 @@ __device__ __forceinline__ void chain_body(const CUtensorMap* map_q, const CUten
             }
             tc_fence_before();
             mbar_arrive(&bars->o_free);
+            // varlen: a sequence's last chunk is stored row by row, only its own tokens (the
+            // rows past its end belong to the next sequence); coalesced over the 128 columns
+            const int cabs = c0 + c;
+            const bool tail = args.cu && (cabs + 1) * kC > seq_len;
+            if (tail && j < dv_valid && !*abort_flag) {
+                const int nvalid = seq_len - cabs * kC;
+                uint16_t* orow = args.out + (static_cast<long>(trow0 + cabs * kC) * args.Hv + h) * args.dv + v0 + j;
+                const long ostride = static_cast<long>(args.Hv) * args.dv;
+#pragma unroll
+                for (int i = 0; i < 32; ++i) {
+                    if (2 * i < nvalid) orow[(2 * i) * ostride] = static_cast<uint16_t>(ob2[i] & 0xffffu);
+                    if (2 * i + 1 < nvalid) orow[(2 * i + 1) * ostride] = static_cast<uint16_t>(ob2[i] >> 16);
+                }
+            }
             if (oleader) bulk_wait_read1();                // the store of two chunks ago left this buffer
             named_bar(BAR_OUT, 128);
             uint8_t* ob = sm + L::OFF_O + (c & 1) * 16384 + (j >> 6) * 8192;
@@ -1089,10 +1155,10 @@ __device__ __forceinline__ void chain_body(const CUtensorMap* map_q, const CUten
             fence_async_smem();
             named_bar(BAR_OUT, 128);
             if (oleader) {
-                if (!*abort_flag)
+                if (!*abort_flag && !tail)
                     for (int vb = 0; vb < nvb; ++vb)
-                        tma_store_4d(map_o, sm + L::OFF_O + (c & 1) * 16384 + vb * 8192, v0 + vb * 64, (c0 + c) * kC, h,
-                                     bidx);
+                        tma_store_4d(map_o, sm + L::OFF_O + (c & 1) * 16384 + vb * 8192, v0 + vb * 64,
+                                     trow0 + cabs * kC, h, bco);
                 bulk_commit();
             }
         }
@@ -1240,7 +1306,9 @@ int launch_prefill(const CUtensorMap& mq, const CUtensorMap& mk, const CUtensorM
     float* user_out = ca.state_out;
 
     const int mode = g_schedule.load(std::memory_order_relaxed);
-    const bool pieced = mode == GDN_SCHEDULE_PIECED   ? (nchunks >= 2)
+    // varlen sequences have their own chunk counts: one prep and one chain launch
+    const bool pieced = ca.cu                          ? false
+                        : mode == GDN_SCHEDULE_PIECED ? (nchunks >= 2)
                         : mode == GDN_SCHEDULE_SINGLE ? false
                                                       : use_pieces(nbh, nchunks, chain_grid, sms);
     if (!pieced) {
@@ -1350,15 +1418,16 @@ int validate_prefill(const void* q, const void* k, const void* v, const float* A
 }  // namespace
 }  // namespace gdn
 
-extern "C" int gdn_prefill_fwd_ws(const void* q, const void* k, const void* v, const float* A_log, const void* a,
-                                  const void* b_logits, int gate_dtype, float dt_bias, const float* dt_bias_vec,
-                                  const float* mask, const float* state_in, void* out, float* state_out, int B,
-                                  int T, int Hqk, int Hv, int dk, int dv, int layout, float scale, void* workspace,
-                                  size_t workspace_bytes, void* stream) {
-    using namespace gdn;
-    int st = validate_prefill(q, k, v, A_log, a, b_logits, gate_dtype, state_in, out, state_out, B, T, Hqk, Hv, dk,
-                              dv, layout);
-    if (st != GDN_OK) return st;
+namespace gdn {
+namespace {
+// One prefill over B sequences of T tokens, or (cu != null) over B packed
+// sequences of at most T tokens each in tensors of Ttot tokens (layout BTHD,
+// batch 1), already validated.
+int run_prefill(const void* q, const void* k, const void* v, const float* A_log, const void* a, const void* b_logits,
+                int gate_dtype, float dt_bias, const float* dt_bias_vec, const float* mask, const float* state_in,
+                void* out, float* state_out, int B, int T, int Hqk, int Hv, int dk, int dv, int layout, float scale,
+                void* workspace, size_t workspace_bytes, void* stream, const int* cu, int Ttot) {
+    int st = GDN_OK;
     const long ntiles = (dv + 127) / 128;
     const long nchunks = (static_cast<long>(T) + kC - 1) / kC;
     const size_t need = gdn_prefill_workspace_bytes(B, T, Hv, dk, dv);
@@ -1371,11 +1440,13 @@ extern "C" int gdn_prefill_fwd_ws(const void* q, const void* k, const void* v, c
     if (st != GDN_OK) return st;
     if (scale == 0.f) scale = 1.f / sqrtf(static_cast<float>(dk));
 
+    // varlen: the packed tensors are one batch of Ttot tokens
+    const int mT = cu ? Ttot : T, mB = cu ? 1 : B;
     CUtensorMap mq, mk, mv, mo;
-    if ((st = make_act_map(&mq, q, dk, T, Hqk, B, layout)) != GDN_OK) return st;
-    if ((st = make_act_map(&mk, k, dk, T, Hqk, B, layout)) != GDN_OK) return st;
-    if ((st = make_act_map(&mv, v, dv, T, Hv, B, layout)) != GDN_OK) return st;
-    if ((st = make_act_map(&mo, out, dv, T, Hv, B, layout)) != GDN_OK) return st;
+    if ((st = make_act_map(&mq, q, dk, mT, Hqk, mB, layout)) != GDN_OK) return st;
+    if ((st = make_act_map(&mk, k, dk, mT, Hqk, mB, layout)) != GDN_OK) return st;
+    if ((st = make_act_map(&mv, v, dv, mT, Hv, mB, layout)) != GDN_OK) return st;
+    if ((st = make_act_map(&mo, out, dv, mT, Hv, mB, layout)) != GDN_OK) return st;
 
     GateArgs ga;
     ga.a = a;
@@ -1391,6 +1462,9 @@ extern "C" int gdn_prefill_fwd_ws(const void* q, const void* k, const void* v, c
     ga.Hv = Hv;
     ga.nchunks = static_cast<int>(nchunks);
     ga.scale = scale;
+    ga.cu = cu;
+    ga.Ttot = mT;
+    ga.err = device_error_word();
 
     PrepArgs pa;
     pa.rec = static_cast<uint8_t*>(workspace);
@@ -1402,6 +1476,8 @@ extern "C" int gdn_prefill_fwd_ws(const void* q, const void* k, const void* v, c
     pa.c0 = 0;
     pa.ncp = ga.nchunks;
     pa.scale = scale;
+    pa.cu = cu;
+    pa.Ttot = mT;
 
     ChainArgs ca;
     ca.rec = static_cast<const uint8_t*>(workspace);
@@ -1416,6 +1492,9 @@ extern "C" int gdn_prefill_fwd_ws(const void* q, const void* k, const void* v, c
     ca.nchunks_total = static_cast<int>(nchunks);
     ca.c0 = 0;
     ca.nchunks = ca.nchunks_total;
+    ca.cu = cu;
+    ca.out = static_cast<uint16_t*>(out);
+    ca.Ttot = mT;
     float* state_tmp = reinterpret_cast<float*>(static_cast<uint8_t*>(workspace) +
                                                 static_cast<size_t>(ga.ntasks) * record_bytes(dk));
 
@@ -1423,6 +1502,21 @@ extern "C" int gdn_prefill_fwd_ws(const void* q, const void* k, const void* v, c
     cudaStream_t s = static_cast<cudaStream_t>(stream);
     if (dk == 128) return launch_prefill<128>(mq, mk, mv, mo, ga, pa, ca, grid, state_tmp, s);
     return launch_prefill<64>(mq, mk, mv, mo, ga, pa, ca, grid, state_tmp, s);
+}
+}  // namespace
+}  // namespace gdn
+
+extern "C" int gdn_prefill_fwd_ws(const void* q, const void* k, const void* v, const float* A_log, const void* a,
+                                  const void* b_logits, int gate_dtype, float dt_bias, const float* dt_bias_vec,
+                                  const float* mask, const float* state_in, void* out, float* state_out, int B,
+                                  int T, int Hqk, int Hv, int dk, int dv, int layout, float scale, void* workspace,
+                                  size_t workspace_bytes, void* stream) {
+    using namespace gdn;
+    const int st = validate_prefill(q, k, v, A_log, a, b_logits, gate_dtype, state_in, out, state_out, B, T, Hqk, Hv,
+                                    dk, dv, layout);
+    if (st != GDN_OK) return st;
+    return run_prefill(q, k, v, A_log, a, b_logits, gate_dtype, dt_bias, dt_bias_vec, mask, state_in, out, state_out,
+                       B, T, Hqk, Hv, dk, dv, layout, scale, workspace, workspace_bytes, stream, nullptr, 0);
 }
 
 // Same call with the workspace taken from the stream-ordered allocator for the
@@ -1448,6 +1542,77 @@ extern "C" int gdn_prefill_fwd(const void* q, const void* k, const void* v, cons
     const int st = gdn_prefill_fwd_ws(q, k, v, A_log, a, b_logits, gate_dtype, dt_bias, dt_bias_vec, mask, state_in,
                                       out, state_out, B, T, Hqk, Hv, dk, dv, layout, scale, ws, need, stream);
     if (ws) cudaFreeAsync(ws, s);
+    return st;
+}
+
+// ---------------------------------------------------------------------------
+// Variable-length prefill: N sequences packed along the token axis, sequence i
+// being tokens [cu_seqlens[i], cu_seqlens[i+1]) of q/k/v/out and of the gate
+// rows, with its own initial and final state.  Chunks restart at every
+// sequence start; a sequence's last chunk is stored row by row so that the
+// next sequence's rows are never written.
+// ---------------------------------------------------------------------------
+extern "C" size_t gdn_prefill_varlen_workspace_bytes(int N, int max_len, int Hv, int dk, int dv) {
+    return gdn_prefill_workspace_bytes(N, max_len, Hv, dk, dv);
+}
+
+namespace gdn {
+namespace {
+int validate_varlen(const void* q, const void* k, const void* v, const float* A_log, const void* a,
+                    const void* b_logits, int gate_dtype, const int* cu_seqlens, int N, int Ttot, int max_len,
+                    const float* state_in, const void* out, const float* state_out, int Hqk, int Hv, int dk, int dv) {
+    if (!cu_seqlens) return fail(GDN_ERR_NULL, "gdn_prefill_varlen_fwd: cu_seqlens is required");
+    if ((reinterpret_cast<uintptr_t>(cu_seqlens) & 3u) != 0)
+        return fail(GDN_ERR_ALIGN, "gdn_prefill_varlen_fwd: cu_seqlens must be 4-byte aligned int32");
+    if (N < 1 || Ttot < 1 || max_len < 1 || max_len > Ttot)
+        return fail(GDN_ERR_SHAPE, "gdn_prefill_varlen_fwd: need N >= 1 and 1 <= max_len <= Ttot (got N=%d Ttot=%d max_len=%d)",
+                    N, Ttot, max_len);
+    // tensors: [Ttot, H, D] = layout BTHD with one batch; states [N, Hv, dk, dv]
+    const int st = validate_prefill(q, k, v, A_log, a, b_logits, gate_dtype, state_in, out, state_out, 1, Ttot, Hqk,
+                                    Hv, dk, dv, GDN_LAYOUT_BTHD);
+    if (st != GDN_OK) return st;
+    const long nchunks = (static_cast<long>(max_len) + kC - 1) / kC;
+    if (static_cast<long>(N) * Hv * nchunks > 0x7fffffffL || static_cast<long>(N) * Hv * ((dv + 127) / 128) > 0x7fffffffL)
+        return fail(GDN_ERR_SHAPE, "gdn_prefill_varlen_fwd: N * Hv * chunks exceeds the launch limits");
+    return GDN_OK;
+}
+}  // namespace
+}  // namespace gdn
+
+extern "C" int gdn_prefill_varlen_fwd_ws(const void* q, const void* k, const void* v, const float* A_log,
+                                         const void* a, const void* b_logits, int gate_dtype, float dt_bias,
+                                         const float* dt_bias_vec, const int* cu_seqlens, int N, int Ttot, int max_len,
+                                         const float* state_in, void* out, float* state_out, int Hqk, int Hv, int dk,
+                                         int dv, float scale, void* workspace, size_t workspace_bytes, void* stream) {
+    using namespace gdn;
+    const int st = validate_varlen(q, k, v, A_log, a, b_logits, gate_dtype, cu_seqlens, N, Ttot, max_len, state_in,
+                                   out, state_out, Hqk, Hv, dk, dv);
+    if (st != GDN_OK) return st;
+    return run_prefill(q, k, v, A_log, a, b_logits, gate_dtype, dt_bias, dt_bias_vec, nullptr, state_in, out,
+                       state_out, N, max_len, Hqk, Hv, dk, dv, GDN_LAYOUT_BTHD, scale, workspace, workspace_bytes,
+                       stream, cu_seqlens, Ttot);
+}
+
+extern "C" int gdn_prefill_varlen_fwd(const void* q, const void* k, const void* v, const float* A_log, const void* a,
+                                      const void* b_logits, int gate_dtype, float dt_bias, const float* dt_bias_vec,
+                                      const int* cu_seqlens, int N, int Ttot, int max_len, const float* state_in,
+                                      void* out, float* state_out, int Hqk, int Hv, int dk, int dv, float scale,
+                                      void* stream) {
+    using namespace gdn;
+    const int st0 = validate_varlen(q, k, v, A_log, a, b_logits, gate_dtype, cu_seqlens, N, Ttot, max_len, state_in,
+                                    out, state_out, Hqk, Hv, dk, dv);
+    if (st0 != GDN_OK) return st0;
+    const size_t need = gdn_prefill_varlen_workspace_bytes(N, max_len, Hv, dk, dv);
+    cudaStream_t s = static_cast<cudaStream_t>(stream);
+    int st = check_sm100();
+    if (st != GDN_OK) return st;
+    void* ws = nullptr;
+    const cudaError_t e = cudaMallocAsync(&ws, need, s);
+    if (e != cudaSuccess)
+        return fail(GDN_ERR_CUDA, "gdn_prefill_varlen_fwd: workspace of %zu B: %s", need, cudaGetErrorString(e));
+    st = gdn_prefill_varlen_fwd_ws(q, k, v, A_log, a, b_logits, gate_dtype, dt_bias, dt_bias_vec, cu_seqlens, N, Ttot,
+                                   max_len, state_in, out, state_out, Hqk, Hv, dk, dv, scale, ws, need, stream);
+    cudaFreeAsync(ws, s);
     return st;
 }
 

@@ -135,7 +135,12 @@ extern "C" int gdn_check_device_error(void) {
     if (word != 0) {
         unsigned int zero = 0;
         cudaMemcpy(gdn::device_error_word(), &zero, sizeof(zero), cudaMemcpyHostToDevice);
-        return gdn::fail(GDN_ERR_DEVICE_TIMEOUT, "a kernel gave up on a bounded wait (device error word 0x%x)", word);
+        if (word & gdn::DERR_TIMEOUT)
+            return gdn::fail(GDN_ERR_DEVICE_TIMEOUT, "a kernel gave up on a bounded wait (device error word 0x%x)", word);
+        return gdn::fail(GDN_ERR_SHAPE,
+                         "gdn_prefill_varlen_fwd: cu_seqlens held offsets that are negative, decreasing or past Ttot; "
+                         "those sequences were skipped (device error word 0x%x)",
+                         word);
     }
     return GDN_OK;
 }

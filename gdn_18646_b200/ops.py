@@ -108,6 +108,53 @@ def prefill(q, k, v, A_log, a, b_logits, *, dt_bias=0.0, mask=None, state_in=Non
     return out, state_out
 
 
+def prefill_varlen(q, k, v, A_log, a, b_logits, cu_seqlens, *, max_len=None, dt_bias=0.0, state_in=None,
+                   scale=0.0, out=None, state_out=None, return_state=True):
+    """Prefill of N sequences packed along the token axis (gdn_prefill_varlen_fwd_ws).
+
+    q,k [Ttot,Hqk,dk], v [Ttot,Hv,dv] bf16; a, b_logits [Hv,Ttot]; cu_seqlens int32 [N+1]
+    on the device (sequence i = tokens cu_seqlens[i]:cu_seqlens[i+1]); max_len = the
+    longest sequence (read from cu_seqlens with a device->host copy when not given);
+    state_in [N,Hv,dk,dv] f32 or None.  Returns (out [Ttot,Hv,dv] bf16, state_out
+    [N,Hv,dk,dv] f32 or None); per sequence the result of ``prefill`` on it alone."""
+    for name, t in (("q", q), ("k", k), ("v", v)):
+        _cuda_contig(t, name, torch.bfloat16)
+    _need(q.dim() == 3 and v.dim() == 3, "q, k, v must be [Ttot, H, D]")
+    Ttot, Hqk, dk = q.shape
+    Hv, dv = v.shape[1], v.shape[2]
+    _need(tuple(k.shape) == tuple(q.shape) and v.shape[0] == Ttot, "k must have q's shape, v Ttot rows")
+    gdt = _gate_dtype(a, "a")
+    _need(b_logits.dtype == a.dtype, "a and b_logits must share a dtype")
+    _cuda_contig(a, "a")
+    _cuda_contig(b_logits, "b_logits")
+    _need(tuple(a.shape) == (Hv, Ttot) and tuple(b_logits.shape) == (Hv, Ttot), "a, b_logits must be [Hv, Ttot]")
+    _cuda_contig(cu_seqlens, "cu_seqlens", torch.int32)
+    N = cu_seqlens.numel() - 1
+    _need(N >= 1, "cu_seqlens needs at least two entries")
+    if max_len is None:
+        max_len = int((cu_seqlens[1:] - cu_seqlens[:-1]).max())
+    max_len = max(int(max_len), 1)
+    _cuda_contig(A_log, "A_log", torch.float32)
+    dt_vec, dt_scalar = None, 0.0
+    if isinstance(dt_bias, torch.Tensor) and dt_bias.numel() > 1:
+        _cuda_contig(dt_bias, "dt_bias", torch.float32)
+        dt_vec = dt_bias
+    else:
+        dt_scalar = float(dt_bias)
+    if state_in is not None:
+        _cuda_contig(state_in, "state_in", torch.float32)
+    if out is None:
+        out = torch.empty_like(v)
+    if state_out is None and return_state:
+        state_out = torch.empty(N, Hv, dk, dv, dtype=torch.float32, device=q.device)
+    ws_bytes = _lib.lib().gdn_prefill_varlen_workspace_bytes(N, max_len, Hv, dk, dv)
+    ws = torch.empty(max(int(ws_bytes), 1), dtype=torch.uint8, device=q.device)
+    _lib.call("gdn_prefill_varlen_fwd_ws", _ptr(q), _ptr(k), _ptr(v), _ptr(A_log), _ptr(a), _ptr(b_logits), gdt,
+              dt_scalar, _ptr(dt_vec), _ptr(cu_seqlens), N, Ttot, max_len, _ptr(state_in), _ptr(out),
+              _ptr(state_out), Hqk, Hv, dk, dv, float(scale), _ptr(ws), int(ws_bytes), _stream())
+    return out, state_out
+
+
 def decode_step(q, k, v, a, b, A_log, dt_bias, state, *, scale=0.0, out=None, state_out=None):
     """One decode step; updates ``state`` in place unless ``state_out`` is given.
     q,k [B,Hqk,dk] bf16; v [B,Hv,dv] bf16; a,b [B,Hv]; state [B,Hv,dk,dv] f32.

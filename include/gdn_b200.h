@@ -148,6 +148,43 @@ int gdn_prefill_fwd_noalloc(const void* q, const void* k, const void* v,
                             float scale, void* stream);
 
 /*
+ * Variable-length prefill: N sequences packed along the token axis (no padding).
+ * No reference counterpart (the reference kernel takes equal-length batches,
+ * kernels/prefill_chunked.cu:422-504); per sequence the result is that of
+ * gdn_prefill_fwd on that sequence alone.
+ *
+ *   q, k        bf16 [Ttot, Hqk, dk];  v, out bf16 [Ttot, Hv, dv]
+ *   a, b_logits [Hv, Ttot] in gate_dtype
+ *   cu_seqlens  int32 [N + 1], DEVICE memory: sequence i is tokens
+ *               [cu_seqlens[i], cu_seqlens[i+1]); cu_seqlens[0] = 0,
+ *               non-decreasing, cu_seqlens[N] = Ttot.  Empty sequences pass
+ *               their state through.
+ *   max_len     host int, at least the longest sequence (sizes the workspace
+ *               and the launch; a longer sequence is processed only up to
+ *               max_len rounded up to 64 tokens).
+ *   state_in    f32 [N, Hv, dk, dv] or NULL (zeros);  state_out f32 [N, Hv, dk, dv] or NULL
+ * Offsets that are negative, decreasing or past Ttot cannot be seen on the host
+ * (the array is on the device): such a sequence is skipped and
+ * gdn_check_device_error() reports GDN_ERR_SHAPE.  Always one prep and one
+ * chain launch after the gates (3 launches).  Mask is not supported here.
+ * Workspace: gdn_prefill_varlen_workspace_bytes(N, max_len, Hv, dk, dv).
+ */
+size_t gdn_prefill_varlen_workspace_bytes(int N, int max_len, int Hv, int dk, int dv);
+int gdn_prefill_varlen_fwd_ws(const void* q, const void* k, const void* v,
+                              const float* A_log, const void* a, const void* b_logits, int gate_dtype,
+                              float dt_bias, const float* dt_bias_vec,
+                              const int* cu_seqlens, int N, int Ttot, int max_len,
+                              const float* state_in, void* out, float* state_out,
+                              int Hqk, int Hv, int dk, int dv, float scale,
+                              void* workspace, size_t workspace_bytes, void* stream);
+int gdn_prefill_varlen_fwd(const void* q, const void* k, const void* v,
+                           const float* A_log, const void* a, const void* b_logits, int gate_dtype,
+                           float dt_bias, const float* dt_bias_vec,
+                           const int* cu_seqlens, int N, int Ttot, int max_len,
+                           const float* state_in, void* out, float* state_out,
+                           int Hqk, int Hv, int dk, int dv, float scale, void* stream);
+
+/*
  * Single-token decode step, state updated in place if state_out == state_in.
  * Replaces gdn_decode_cuda(), kernels/decode.cu:131-162, and its torch wrapper
  * gdn_decode_forward(), kernels/decode.cu:172-214 (math: reference/decode_ref.py:11-61).
@@ -248,8 +285,9 @@ const char* gdn_version(void);
 
 /*
  * Reads and clears the device-side error word of the current device (set by a
- * kernel that gave up on a bounded wait).  Synchronises the device.  Returns
- * GDN_OK, GDN_ERR_DEVICE_TIMEOUT or GDN_ERR_CUDA.
+ * kernel that gave up on a bounded wait, or by a varlen prefill that met
+ * invalid offsets).  Synchronises the device.  Returns GDN_OK,
+ * GDN_ERR_DEVICE_TIMEOUT, GDN_ERR_SHAPE (invalid varlen offsets) or GDN_ERR_CUDA.
  */
 int gdn_check_device_error(void);
 

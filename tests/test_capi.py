@@ -171,3 +171,31 @@ def test_decode_proj_rejects(lib):
     assert call([seg(conv_state_in=FAKE)]) == _lib.GDN_ERR_NULL
     assert call([seg(W=ODD)]) == _lib.GDN_ERR_ALIGN
     assert "gdn_decode_proj_fwd" in _lib.last_error()
+
+
+def varlen_args(**over):
+    a = dict(q=FAKE, k=FAKE, v=FAKE, A_log=FAKE, a=FAKE, b=FAKE, gate=0, dtb=0.0, dtv=None, cu=FAKE, N=2,
+             Ttot=100, max_len=64, s_in=None, out=FAKE, s_out=FAKE, Hqk=2, Hv=2, dk=128, dv=128, scale=0.0,
+             ws=FAKE, ws_bytes=1 << 30, stream=None)
+    a.update(over)
+    return list(a.values())
+
+
+@pytest.mark.parametrize("over,code", [
+    (dict(cu=None), _lib.GDN_ERR_NULL),
+    (dict(cu=ODD), _lib.GDN_ERR_ALIGN),
+    (dict(N=0), _lib.GDN_ERR_SHAPE),
+    (dict(max_len=101), _lib.GDN_ERR_SHAPE),
+    (dict(max_len=0), _lib.GDN_ERR_SHAPE),
+    (dict(q=None), _lib.GDN_ERR_NULL),
+    (dict(dk=96), _lib.GDN_ERR_UNSUPPORTED),
+    (dict(Hqk=3, Hv=4), _lib.GDN_ERR_SHAPE),
+])
+def test_prefill_varlen_rejects(lib, over, code):
+    assert _lib.call_status("gdn_prefill_varlen_fwd_ws", *varlen_args(**over)) == code
+    assert "gdn_prefill" in _lib.last_error()
+
+
+def test_prefill_varlen_workspace_matches_fixed_length(lib):
+    assert lib.gdn_prefill_varlen_workspace_bytes(3, 1000, 4, 128, 128) == \
+        lib.gdn_prefill_workspace_bytes(3, 1000, 4, 128, 128)
