@@ -581,17 +581,16 @@ def run_only(args):
             ops.prefill(inp["q"], inp["k"], inp["v"], inp["A_log"], inp["a"], inp["b"], state_in=inp["state_in"],
                         scale=c["dk"] ** -0.5, out=out, state_out=s_out)
     elif args.only == "layer_decode":
-        from gdn_18646_b200.layer import DecodeGraph, GDNConfig, GDNLayer, make_weights
+        from gdn_18646_b200.layer import GDNConfig, GDNLayer, make_weights
         cfg = GDNConfig()
         layer = GDNLayer(make_weights(cfg, device=dev, seed=3), cfg)
         g = torch.Generator(device=dev).manual_seed(7)
         B = 2
         _, st = layer.prefill(torch.randn(B, 256, cfg.hidden, generator=g, device=dev).bfloat16())
-        graph = DecodeGraph(layer, st, B)
         xd = torch.randn(B, 1, cfg.hidden, generator=g, device=dev).bfloat16()
 
-        def step():
-            graph.step(xd)
+        def step():                                    # eager launches, so a profiler sees each kernel
+            layer.decode(xd, st, st)
     elif args.only == "decode":
         c = C2
         g = torch.Generator(device=dev).manual_seed(5)
