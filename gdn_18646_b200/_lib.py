@@ -29,6 +29,7 @@ GDN_LAYOUT_BTHD = 1
 GDN_SCHEDULE_AUTO = 0
 GDN_SCHEDULE_SINGLE = 1
 GDN_SCHEDULE_PIECED = 2
+GDN_SCHEDULE_STREAM = 3
 
 _P = ctypes.c_void_p
 _I = ctypes.c_int

@@ -146,6 +146,7 @@ struct GateArgs {
     const int* cu;       // varlen: sequence b is packed tokens [cu[b], cu[b+1]); a, b_logits [Hv, Ttot]
     int Ttot;
     unsigned int* err;
+    unsigned int* ready; // streamed schedule: per-record ready flags, cleared here
 };
 
 struct PrepArgs {
@@ -156,6 +157,8 @@ struct PrepArgs {
     float scale;
     const int* cu;       // varlen sequence offsets or null
     int Ttot;
+    unsigned int* ready; // streamed schedule: set once a record is complete in global memory
+    int chunk_major;     // task order: chunk-major (all sequences' chunk 0 first) for the streamed schedule
 };
 
 // ---------------------------------------------------------------------------
@@ -215,7 +218,38 @@ struct ChainArgs {
     const int* cu;       // varlen sequence offsets or null
     uint16_t* out;       // varlen: o [Ttot, Hv, dv], written directly for each sequence's last chunk
     int Ttot;
+    const unsigned int* ready;   // streamed schedule: wait for a record's flag before loading it
 };
+
+// ---------------------------------------------------------------------------
+// Streamed schedule: prep workers and chain CTAs in one cooperative launch; a
+// prep worker publishes each finished record with a release flag, a chain CTA
+// acquires it before its bulk loads.  The record bytes are written by the
+// async proxy (bulk stores), so both sides fence the async proxy around the flag.
+// ---------------------------------------------------------------------------
+__device__ __forceinline__ void publish_record(unsigned int* flag) {
+    asm volatile("fence.proxy.async.global;" ::: "memory");
+    asm volatile("st.release.gpu.global.u32 [%0], %1;" ::"l"(flag), "r"(1u) : "memory");
+}
+// Bounded wait for a record flag (~2^31 cycles, then DERR_TIMEOUT and the CTA's abort flag).
+__device__ __forceinline__ bool wait_record(const unsigned int* flag, unsigned int* err, volatile int* abort) {
+    const long long t0 = clock64();
+    for (;;) {
+        uint32_t v;
+        asm volatile("ld.acquire.gpu.global.u32 %0, [%1];" : "=r"(v) : "l"(flag) : "memory");
+        if (v != 0) break;
+        if (*abort) return false;
+        if (clock64() - t0 > (1ll << 31)) {
+            if (err) atomicOr(err, DERR_TIMEOUT);
+            *abort = 1;
+            return false;
+        }
+        __nanosleep(100);
+    }
+    asm volatile("fence.proxy.async.global;" ::: "memory");
+    return true;
+}
+__device__ __forceinline__ void bulk_wait_group3() { asm volatile("cp.async.bulk.wait_group 3;" ::: "memory"); }
 
 // Varlen: first token and length of sequence b.  Offsets that are negative,
 // decreasing or past Ttot make the sequence empty (nothing read or written for
@@ -494,6 +528,7 @@ prefill_gates_kernel(const GateArgs args) {
     *reinterpret_cast<float2*>(G + t0) = make_float2(m0 * args.scale * el0, m1 * args.scale * el1);
     *reinterpret_cast<float2*>(G + 64 + t0) = make_float2(ex2_approx(ll2 - l20), ex2_approx(ll2 - l21));
     if (lane == 0) G[128] = ex2_approx(ll2);                              // gamma_c
+    if (args.ready && lane == 0) args.ready[task] = 0;                    // record not prepared yet
 }
 
 // ===========================================================================
@@ -546,11 +581,24 @@ __device__ __forceinline__ void prep_body(const CUtensorMap* map_q, const CUtens
     tc_fence_after();
     const uint32_t tmem = *tmem_slot;
 
+    // task -> (sequence-head bh, chunk c); chunk-major order for the streamed schedule
+    auto coords = [&](int task, int& bh, int& c) {
+        if (args.chunk_major) {
+            const int nbh = args.ntasks / args.ncp;
+            const int cc = task / nbh;
+            bh = task - cc * nbh;
+            c = args.c0 + cc;
+        } else {
+            bh = task / args.ncp;
+            c = args.c0 + (task - bh * args.ncp);
+        }
+    };
     // varlen: the next task at or after `task` (stride vgrid) inside its sequence's chunks
     auto next_task = [&](int task) {
         if (args.cu)
             for (; task < args.ntasks; task += vgrid) {
-                const int bh = task / args.ncp, c = args.c0 + (task - bh * args.ncp);
+                int bh, c;
+                coords(task, bh, c);
                 int st0;
                 if (c < varlen_chunks(varlen_seq(args.cu, bh / args.Hv, args.Ttot, st0, nullptr), nchunks)) break;
             }
@@ -558,7 +606,8 @@ __device__ __forceinline__ void prep_body(const CUtensorMap* map_q, const CUtens
     };
     // q/k tiles and the gate vectors of `task` -> shared memory, completing on bar_qk
     auto issue_qk = [&](int task) {
-        const int bh = task / args.ncp, c = args.c0 + (task - bh * args.ncp);
+        int bh, c;
+        coords(task, bh, c);
         const int hq = (bh % args.Hv) / group, bidx = bh / args.Hv;
         // token row and batch coordinates (varlen: packed tokens, one batch)
         int st0 = 0;
@@ -577,11 +626,14 @@ __device__ __forceinline__ void prep_body(const CUtensorMap* map_q, const CUtens
     if (leader && first < args.ntasks) issue_qk(first);
 
     int it = 0;
+    long published = -1;                               // streamed: record whose flag is still to be set
 #pragma unroll 1
     for (int task = first; task < args.ntasks; task = next_task(task + vgrid), ++it) {
         const uint32_t ph = it & 1;
-        const int tbh = task / args.ncp;
-        uint8_t* rec = args.rec + (static_cast<long>(tbh) * nchunks + args.c0 + (task - tbh * args.ncp)) * R::BYTES;
+        int tbh, tc;
+        coords(task, tbh, tc);
+        const long rec_idx = static_cast<long>(tbh) * nchunks + tc;
+        uint8_t* rec = args.rec + rec_idx * R::BYTES;
         const float* g = gates;                           // this task's gate vectors (landed with q/k)
 
         // ---- [Q;K] K^T on tensor cores
@@ -751,6 +803,14 @@ __device__ __forceinline__ void prep_body(const CUtensorMap* map_q, const CUtens
             bulk_store(rec + R::WTH, sm, 2 * DK * 128);
             bulk_commit();
             bulk_wait_read0();                        // the images (and A1 over N) have been read out
+            if (args.ready) {
+                // the previous task's three store groups have completed: publish it
+                if (published >= 0) {
+                    bulk_wait_group3();
+                    publish_record(args.ready + published);
+                }
+                published = rec_idx;
+            }
             // q/k shared memory is free: fetch the next task's tiles
             const int nt = next_task(task + vgrid);
             if (!*abort_flag && nt < args.ntasks) {
@@ -765,7 +825,10 @@ __device__ __forceinline__ void prep_body(const CUtensorMap* map_q, const CUtens
         }
     }
 
-    if (leader) bulk_wait_all0();                      // record stores complete before the worker ends
+    if (leader) {
+        bulk_wait_all0();                              // record stores complete before the worker ends
+        if (args.ready && published >= 0) publish_record(args.ready + published);
+    }
     tc_fence_before();
     named_bar(bar_id, kPrepThreads);
     if (warp == 0) tmem_dealloc(tmem, kPrepTmemCols);
@@ -856,6 +919,9 @@ __device__ __forceinline__ void chain_body(const CUtensorMap* map_q, const CUten
                 if (c >= 2 && !mbar_wait_or_abort(&bars->slot_free[slot], ((c >> 1) - 1) & 1, err, abort_flag)) break;
                 uint8_t* dst = sm + slot * L::SLOT_BYTES;
                 const uint8_t* rec = rec0 + static_cast<long>(c) * R::BYTES;
+                if (args.ready &&
+                    !wait_record(args.ready + static_cast<long>(bh) * args.nchunks_total + c0 + c, err, abort_flag))
+                    break;
                 mbar_arrive_expect_tx(&bars->slot_full[slot], 2 * L::CB * 8192 + 2 * DK * 128 + 8192 + 1024);
 #pragma unroll
                 for (int cb = 0; cb < L::CB; ++cb) {
@@ -870,6 +936,9 @@ __device__ __forceinline__ void chain_body(const CUtensorMap* map_q, const CUten
         } else if (lane == 1) {
             for (int c = 0; c < nchunks; ++c) {
                 if (c >= 1 && !mbar_wait_or_abort(&bars->va_free, (c - 1) & 1, err, abort_flag)) break;
+                if (args.ready &&
+                    !wait_record(args.ready + static_cast<long>(bh) * args.nchunks_total + c0 + c, err, abort_flag))
+                    break;
                 mbar_arrive_expect_tx(&bars->va_full, nvb * 8192 + 16384);
                 for (int vb = 0; vb < nvb; ++vb)
                     tma_load_4d(sm + L::OFF_V + vb * 8192, map_v, &bars->va_full, v0 + vb * 64, trow0 + (c0 + c) * kC, h,
@@ -1247,6 +1316,57 @@ bool use_pieces(int nbh, int nchunks, int chain_grid, int sms) {
     return pieced < 0.95 * unpieced;
 }
 
+// Predicted time (us) of the streamed schedule when the first `lead` chunks of
+// every sequence are prepared by a prep launch on all SMs (~12 us a round of 3
+// workers per SM) and the rest by the free SMs' workers inside the cooperative
+// launch (~15 us a round) while the chain CTAs consume them (~3.3 us a chunk):
+// the lead, then the slower of the two streams.  Per-unit costs from traces of
+// config 1 on B200 (globaltimer stamps per record and per chain chunk).
+double streamed_time(int nbh, int nchunks, int chain_grid, int sms, int lead) {
+    const long w_all = static_cast<long>(sms) * kPrepCtasPerSm;
+    const long w_free = static_cast<long>(sms - chain_grid) * kPrepPerCta;
+    const double prep_round = 12.0, ovl_round = 15.0, first = 4.0, chunk = 3.3, launch = 7.0;
+    const long t_lead = static_cast<long>(nbh) * lead, t_rest = static_cast<long>(nbh) * (nchunks - lead);
+    const double head = lead > 0 ? static_cast<double>((t_lead + w_all - 1) / w_all) * prep_round + first + launch : 0.0;
+    const double prep = static_cast<double>((t_rest + w_free - 1) / w_free) * ovl_round + chunk;
+    const double chain = first + (lead > 0 ? 0.0 : ovl_round) + nchunks * chunk;
+    return head + (prep > chain ? prep : chain) + launch;
+}
+// The lead (chunks prepared before the cooperative launch) the model likes best.
+int stream_lead(int nbh, int nchunks, int chain_grid, int sms) {
+    int best = 0;
+    double tbest = streamed_time(nbh, nchunks, chain_grid, sms, 0);
+    for (int lead = 1; lead < nchunks; ++lead) {
+        const double t = streamed_time(nbh, nchunks, chain_grid, sms, lead);
+        if (t < tbest) {
+            tbest = t;
+            best = lead;
+        }
+    }
+    return best;
+}
+double unpieced_time(int nbh, int nchunks, int sms) {
+    const long w_all = static_cast<long>(sms) * kPrepCtasPerSm;
+    return static_cast<double>((static_cast<long>(nbh) * nchunks + w_all - 1) / w_all) * 12.0 + 4.0 + nchunks * 3.2 +
+           7.0;
+}
+
+// The schedule a call runs under the process-wide mode.  The streamed schedule
+// needs one free SM besides the chain CTAs (all CTAs co-resident, one per SM);
+// the pieced one equal-length sequences.
+int pick_schedule(int mode, int nbh, int nchunks, int chain_grid, int sms, bool varlen) {
+    const bool can_stream = chain_grid < sms && nchunks >= 2;
+    if (mode == GDN_SCHEDULE_STREAM) return can_stream ? GDN_SCHEDULE_STREAM : GDN_SCHEDULE_SINGLE;
+    if (mode == GDN_SCHEDULE_PIECED) return (!varlen && nchunks >= 2) ? GDN_SCHEDULE_PIECED : GDN_SCHEDULE_SINGLE;
+    if (mode == GDN_SCHEDULE_SINGLE) return GDN_SCHEDULE_SINGLE;
+    if (can_stream &&
+        streamed_time(nbh, nchunks, chain_grid, sms, stream_lead(nbh, nchunks, chain_grid, sms)) <
+            0.95 * unpieced_time(nbh, nchunks, sms))
+        return GDN_SCHEDULE_STREAM;
+    if (!varlen && use_pieces(nbh, nchunks, chain_grid, sms)) return GDN_SCHEDULE_PIECED;
+    return GDN_SCHEDULE_SINGLE;
+}
+
 // The schedule, all on the caller's stream.  Gates (one launch), then prep and
 // chain.  When the chain kernel leaves at least half of the SMs idle (few
 // sequences), the sequence is cut into up to 4 pieces of chunks:
@@ -1255,7 +1375,7 @@ bool use_pieces(int nbh, int nchunks, int chain_grid, int sms) {
 // one prep and one chain launch over all chunks.
 template <int DK>
 int launch_prefill(const CUtensorMap& mq, const CUtensorMap& mk, const CUtensorMap& mv, const CUtensorMap& mo,
-                   const GateArgs& ga, PrepArgs pa, ChainArgs ca, int chain_grid, float* state_tmp,
+                   GateArgs ga, PrepArgs pa, ChainArgs ca, int chain_grid, float* state_tmp, unsigned int* ready,
                    cudaStream_t st) {
     int dev = 0;
     cudaGetDevice(&dev);
@@ -1279,6 +1399,9 @@ int launch_prefill(const CUtensorMap& mq, const CUtensorMap& mk, const CUtensorM
     const int sms = g_sm_count[dev & 63];
     const int nchunks = ca.nchunks_total;
     const int nbh = ga.ntasks / nchunks;                     // B * Hv
+    const int sched = pick_schedule(g_schedule.load(std::memory_order_relaxed), nbh, nchunks, chain_grid, sms,
+                                    ca.cu != nullptr);
+    if (sched == GDN_SCHEDULE_STREAM) ga.ready = ready;
 
     prefill_gates_kernel<DK><<<(ga.ntasks + 3) / 4, 128, 0, st>>>(ga);
     int s = launch_status("gdn_prefill_fwd (gates)");
@@ -1305,13 +1428,36 @@ int launch_prefill(const CUtensorMap& mq, const CUtensorMap& mk, const CUtensorM
     const float* user_in = ca.state_in;
     float* user_out = ca.state_out;
 
-    const int mode = g_schedule.load(std::memory_order_relaxed);
-    // varlen sequences have their own chunk counts: one prep and one chain launch
-    const bool pieced = ca.cu                          ? false
-                        : mode == GDN_SCHEDULE_PIECED ? (nchunks >= 2)
-                        : mode == GDN_SCHEDULE_SINGLE ? false
-                                                      : use_pieces(nbh, nchunks, chain_grid, sms);
-    if (!pieced) {
+    if (sched == GDN_SCHEDULE_STREAM) {
+        // the first `lead` chunks of every sequence on all SMs (their records published too),
+        // then one cooperative launch (all CTAs co-resident: chain CTAs wait on prep workers):
+        // chain CTAs over all chunks, prep workers on every other SM for the rest, chunk-major
+        const int lead = stream_lead(nbh, nchunks, chain_grid, sms);
+        pa.ready = ready;
+        if (lead > 0) {
+            set_piece(0, 0, nullptr, nullptr, 0, lead);
+            if ((s = prep_only(sms * kPrepCtasPerSm)) != GDN_OK) return s;
+        }
+        set_piece(0, nchunks, user_in, user_out, lead, nchunks - lead);
+        pa.chunk_major = 1;
+        ca.ready = ready;
+        cudaLaunchConfig_t cfg = {};
+        cfg.gridDim = dim3(sms);
+        cfg.blockDim = dim3(kChainThreads);
+        cfg.dynamicSmemBytes = OverlapSmem<DK>::ALLOC;
+        cfg.stream = st;
+        cudaLaunchAttribute attr[1];
+        attr[0].id = cudaLaunchAttributeCooperative;
+        attr[0].val.cooperative = 1;
+        cfg.attrs = attr;
+        cfg.numAttrs = 1;
+        const cudaError_t e = cudaLaunchKernelEx(&cfg, prefill_overlap_kernel<DK>, mq, mk, mv, mo, ca, pa, chain_grid);
+        if (e != cudaSuccess)
+            return fail(GDN_ERR_CUDA, "gdn_prefill_fwd (streamed): cooperative launch of %d CTAs failed: %s", sms,
+                        cudaGetErrorString(e));
+        return launch_status("gdn_prefill_fwd (streamed)");
+    }
+    if (sched == GDN_SCHEDULE_SINGLE) {
         set_piece(0, nchunks, user_in, user_out, 0, nchunks);
         if ((s = prep_only(sms * kPrepCtasPerSm)) != GDN_OK) return s;
         return chain_only();
@@ -1365,17 +1511,18 @@ extern "C" int gdn_prefill_launch_count(int B, int T, int Hv, int dk, int dv) {
         return -1;
     const int nchunks = (T + gdn::kC - 1) / gdn::kC;
     const int nbh = B * Hv, chain_grid = nbh * ((dv + 127) / 128);
-    const int mode = gdn::g_schedule.load(std::memory_order_relaxed);
-    const bool pieced = mode == GDN_SCHEDULE_PIECED   ? (nchunks >= 2)
-                        : mode == GDN_SCHEDULE_SINGLE ? false
-                                                      : gdn::use_pieces(nbh, nchunks, chain_grid, sms);
-    if (!pieced) return 3;
+    const int sched = gdn::pick_schedule(gdn::g_schedule.load(std::memory_order_relaxed), nbh, nchunks, chain_grid,
+                                         sms, false);
+    if (sched == GDN_SCHEDULE_STREAM)                     // gates, (lead prep), the cooperative prep + chain launch
+        return gdn::stream_lead(nbh, nchunks, chain_grid, sms) > 0 ? 3 : 2;
+    if (sched == GDN_SCHEDULE_SINGLE) return 3;
     const int per = (nchunks + gdn::kMaxPieces - 1) / gdn::kMaxPieces;
     return 2 + (nchunks + per - 1) / per;                // gates, prep(piece 0), overlaps, last chain
 }
 
 extern "C" int gdn_prefill_set_schedule(int mode) {
-    if (mode != GDN_SCHEDULE_AUTO && mode != GDN_SCHEDULE_SINGLE && mode != GDN_SCHEDULE_PIECED)
+    if (mode != GDN_SCHEDULE_AUTO && mode != GDN_SCHEDULE_SINGLE && mode != GDN_SCHEDULE_PIECED &&
+        mode != GDN_SCHEDULE_STREAM)
         return gdn::fail(GDN_ERR_DTYPE, "gdn_prefill_set_schedule: unknown mode %d", mode);
     gdn::g_schedule.store(mode);
     return GDN_OK;
@@ -1384,8 +1531,10 @@ extern "C" int gdn_prefill_set_schedule(int mode) {
 extern "C" size_t gdn_prefill_workspace_bytes(int B, int T, int Hv, int dk, int dv) {
     if (B <= 0 || T <= 0 || Hv <= 0 || !(dk == 64 || dk == 128) || !(dv == 64 || dv == 128 || dv == 256)) return 0;
     const size_t nchunks = (static_cast<size_t>(T) + gdn::kC - 1) / gdn::kC;
-    // chunk records, then an fp32 state buffer [B, Hv, dk, dv] for the pieced schedule
-    return static_cast<size_t>(B) * Hv * nchunks * gdn::record_bytes(dk) + static_cast<size_t>(B) * Hv * dk * dv * 4;
+    // chunk records, an fp32 state buffer [B, Hv, dk, dv] for the pieced schedule, and one
+    // ready flag per record for the streamed schedule
+    return static_cast<size_t>(B) * Hv * nchunks * gdn::record_bytes(dk) + static_cast<size_t>(B) * Hv * dk * dv * 4 +
+           (static_cast<size_t>(B) * Hv * nchunks * 4 + 127) / 128 * 128;
 }
 
 namespace gdn {
@@ -1465,6 +1614,7 @@ int run_prefill(const void* q, const void* k, const void* v, const float* A_log,
     ga.cu = cu;
     ga.Ttot = mT;
     ga.err = device_error_word();
+    ga.ready = nullptr;
 
     PrepArgs pa;
     pa.rec = static_cast<uint8_t*>(workspace);
@@ -1478,6 +1628,8 @@ int run_prefill(const void* q, const void* k, const void* v, const float* A_log,
     pa.scale = scale;
     pa.cu = cu;
     pa.Ttot = mT;
+    pa.ready = nullptr;
+    pa.chunk_major = 0;
 
     ChainArgs ca;
     ca.rec = static_cast<const uint8_t*>(workspace);
@@ -1495,13 +1647,16 @@ int run_prefill(const void* q, const void* k, const void* v, const float* A_log,
     ca.cu = cu;
     ca.out = static_cast<uint16_t*>(out);
     ca.Ttot = mT;
+    ca.ready = nullptr;
     float* state_tmp = reinterpret_cast<float*>(static_cast<uint8_t*>(workspace) +
                                                 static_cast<size_t>(ga.ntasks) * record_bytes(dk));
 
     const int grid = static_cast<int>(B * Hv * ntiles);
     cudaStream_t s = static_cast<cudaStream_t>(stream);
-    if (dk == 128) return launch_prefill<128>(mq, mk, mv, mo, ga, pa, ca, grid, state_tmp, s);
-    return launch_prefill<64>(mq, mk, mv, mo, ga, pa, ca, grid, state_tmp, s);
+    unsigned int* ready = reinterpret_cast<unsigned int*>(reinterpret_cast<uint8_t*>(state_tmp) +
+                                                          static_cast<size_t>(B) * Hv * dk * dv * 4);
+    if (dk == 128) return launch_prefill<128>(mq, mk, mv, mo, ga, pa, ca, grid, state_tmp, ready, s);
+    return launch_prefill<64>(mq, mk, mv, mo, ga, pa, ca, grid, state_tmp, ready, s);
 }
 }  // namespace
 }  // namespace gdn

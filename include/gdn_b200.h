@@ -77,7 +77,8 @@ int gdn_prefill_fwd(const void* q, const void* k, const void* v,
 /*
  * Bytes of device workspace gdn_prefill_fwd_ws needs (0 for invalid shapes):
  * one chunk record per (batch, value head, 64-token chunk), 59 KB at dk=128,
- * 43 KB at dk=64, plus one fp32 state [B, Hv, dk, dv].  No counterpart in the
+ * 43 KB at dk=64, plus one fp32 state [B, Hv, dk, dv] and a 4-byte ready flag
+ * per record (rounded up to 128 B).  No counterpart in the
  * reference, whose kernel keeps everything in shared memory.
  */
 size_t gdn_prefill_workspace_bytes(int B, int T, int Hv, int dk, int dv);
@@ -87,16 +88,21 @@ size_t gdn_prefill_workspace_bytes(int B, int T, int Hv, int dk, int dv);
  *   SINGLE  one prep launch over all chunks, then one chain launch;
  *   PIECED  the chunks cut into up to 4 pieces, the chain of piece k running
  *           in the same launch as the prep of piece k+1;
- *   AUTO    PIECED when a cost model predicts it faster (few sequences,
- *           many chunks), else SINGLE.
+ *   STREAM  after the gates, a prep launch over the first chunks of every
+ *           sequence (as many as a cost model finds best, possibly none),
+ *           then one cooperative launch: the chain CTAs and, on every other
+ *           SM, prep workers producing the remaining chunk records
+ *           chunk-major; a chain CTA waits (bounded) for each record's ready
+ *           flag.  Needs fewer chain CTAs (B * Hv * ceil(dv/128)) than SMs;
+ *   AUTO    the one a cost model predicts fastest.
  * Results are identical up to fp32 summation order.  No counterpart in the
  * reference (single kernel).
  */
-enum { GDN_SCHEDULE_AUTO = 0, GDN_SCHEDULE_SINGLE = 1, GDN_SCHEDULE_PIECED = 2 };
+enum { GDN_SCHEDULE_AUTO = 0, GDN_SCHEDULE_SINGLE = 1, GDN_SCHEDULE_PIECED = 2, GDN_SCHEDULE_STREAM = 3 };
 int gdn_prefill_set_schedule(int mode);
 
 /* Kernel launches one gdn_prefill_fwd call makes on the current device under
- * the current schedule (3 for SINGLE), or -1 for invalid shapes / no device. */
+ * the current schedule (3 for SINGLE, 2 or 3 for STREAM), or -1 for invalid shapes / no device. */
 int gdn_prefill_launch_count(int B, int T, int Hv, int dk, int dv);
 
 /*

@@ -133,9 +133,13 @@ def test_python_surface_raises_runtime_error(lib):
 
 def test_prefill_workspace_and_schedule_entry_points(lib):
     rec = 2048 + 16384 + 2 * 128 * 128 + 8192 + 1024           # gate block, A1 hi/lo, W^T hi/lo, P, gates
-    assert lib.gdn_prefill_workspace_bytes(4, 4096, 16, 128, 128) == 4 * 16 * 64 * rec + 4 * 16 * 128 * 128 * 4
+
+    def flags(n):                                               # one 4-byte ready flag per record, 128 B granules
+        return (4 * n + 127) // 128 * 128
+    assert lib.gdn_prefill_workspace_bytes(4, 4096, 16, 128, 128) == \
+        4 * 16 * 64 * rec + 4 * 16 * 128 * 128 * 4 + flags(4 * 16 * 64)
     assert lib.gdn_prefill_workspace_bytes(1, 65, 2, 64, 64) == 2 * 2 * (2048 + 16384 + 2 * 64 * 128 + 9216) + \
-        2 * 64 * 64 * 4
+        2 * 64 * 64 * 4 + flags(2 * 2)
     assert lib.gdn_prefill_workspace_bytes(1, 64, 2, 96, 64) == 0
     assert lib.gdn_prefill_workspace_bytes(0, 64, 2, 128, 128) == 0
     assert _lib.call_status("gdn_prefill_set_schedule", 7) == _lib.GDN_ERR_DTYPE

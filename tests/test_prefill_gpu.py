@@ -116,29 +116,40 @@ def test_prefill_slow_decay_long_sequence_precision(cuda_device):
     assert O.rel_fro(S, S_r) < 1e-4
 
 
-@pytest.mark.parametrize("schedule", ["pieced", "single"])
+_MODES = {"pieced": 2, "single": 1, "stream": 3}     # GDN_SCHEDULE_*
+
+
+@pytest.mark.parametrize("schedule", ["pieced", "single", "stream"])
 @pytest.mark.parametrize("B,T,H,Hqk,dk,dv", [(1, 1000, 4, 2, 128, 256), (2, 1100, 2, 2, 64, 128), (1, 150, 2, 2, 128, 64)])
 def test_prefill_schedules(cuda_device, schedule, B, T, H, Hqk, dk, dv):
-    """Both launch schedules: PIECED runs the chain of chunk piece k in the same
+    """Every launch schedule: PIECED runs the chain of chunk piece k in the same
     launch as the prep of piece k+1 (state carried between pieces through the
-    workspace).  Ragged last chunk, grouped heads, two value tiles (dv = 256),
-    dk = 64 and pieces of unequal length (18 chunks -> 5+5+5+3, 3 chunks -> 1+1+1)."""
+    workspace); STREAM runs prep workers and chain CTAs in one cooperative launch,
+    the chain waiting on per-record ready flags.  Ragged last chunk, grouped heads,
+    two value tiles (dv = 256), dk = 64 and pieces of unequal length (18 chunks ->
+    5+5+5+3, 3 chunks -> 1+1+1).  STREAM does the same arithmetic as SINGLE in a
+    different order of tasks, so its results are bit-identical."""
     from gdn_18646_b200 import _lib
-    mode = _lib.GDN_SCHEDULE_PIECED if schedule == "pieced" else _lib.GDN_SCHEDULE_SINGLE
-    _lib.call("gdn_prefill_set_schedule", mode)
-    try:
-        inp = O.make_prefill_inputs(60 + T, B, T, H, dk, dv, state_std=0.02, layout="bthd", Hqk=Hqk)
-        o, S = _run(inp, layout="bthd", Hqk=Hqk)
-    finally:
-        _lib.call("gdn_prefill_set_schedule", _lib.GDN_SCHEDULE_AUTO)
+    inp = O.make_prefill_inputs(60 + T, B, T, H, dk, dv, state_std=0.02, layout="bthd", Hqk=Hqk)
+    res = {}
+    for mode in (schedule, "single"):
+        _lib.call("gdn_prefill_set_schedule", _MODES[mode])
+        try:
+            res[mode] = _run(inp, layout="bthd", Hqk=Hqk)
+        finally:
+            _lib.call("gdn_prefill_set_schedule", _lib.GDN_SCHEDULE_AUTO)
+    o, S = res[schedule]
     o_r, S_r = _oracle(inp, layout="bthd")
     _check(o, S, o_r, S_r)
+    if schedule == "stream":
+        assert np.array_equal(o, res["single"][0]) and np.array_equal(S, res["single"][1])
 
 
 def test_prefill_launch_count(cuda_device):
     from gdn_18646_b200 import _lib
     lib = _lib.lib()
-    assert lib.gdn_prefill_launch_count(4, 4096, 16, 128, 128) == 3        # config 1: single schedule
+    assert lib.gdn_prefill_launch_count(4, 4096, 16, 128, 128) == 3        # config 1: gates, lead prep, stream
+    assert lib.gdn_prefill_launch_count(8, 4096, 32, 128, 128) == 3        # 256 chains >= SMs: single
     _lib.call("gdn_prefill_set_schedule", _lib.GDN_SCHEDULE_PIECED)
     try:
         assert lib.gdn_prefill_launch_count(1, 1000, 4, 128, 256) == 6     # gates, prep, 3 overlaps, chain

@@ -122,3 +122,20 @@ def test_varlen_device_checks_offsets(cuda_device):
     assert np.array_equal(to_np(s)[1], pack["state_in"][1])
     assert np.array_equal(to_np(s)[2], pack["state_in"][2])
     assert torch.isfinite(s).all()
+
+
+def test_varlen_streamed_schedule_equals_single(cuda_device):
+    """The streamed schedule (prep workers and chain CTAs in one launch, records
+    chunk-major behind ready flags) gives the single schedule's bits for packed
+    sequences too, including a sequence whose prep tasks end early."""
+    lib = _lib.lib()
+    lens = [700, 5, 64, 1300, 0, 90]
+    seqs, pack = _packed(lens, 4, 128, 128, seed=17)
+    res = []
+    for mode in (_lib.GDN_SCHEDULE_STREAM, _lib.GDN_SCHEDULE_SINGLE):
+        lib.gdn_prefill_set_schedule(mode)
+        try:
+            res.append([to_np(t) for t in _run_varlen(pack, seqs[0]["A_log"], seqs[0]["scale"])])
+        finally:
+            lib.gdn_prefill_set_schedule(_lib.GDN_SCHEDULE_AUTO)
+    assert np.array_equal(res[0][0], res[1][0]) and np.array_equal(res[0][1], res[1][1])
