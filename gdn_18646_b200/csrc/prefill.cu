@@ -173,7 +173,8 @@ constexpr uint32_t C_SLO = 192;        // S^T bf16 lo
 //   [0, 64)    U^T from A1 hi, minus S_hi^T W_hi^T and S_lo^T W_hi^T
 //   [64, 128)  U^T from A1 lo, minus S_hi^T W_lo^T            (dV^T = [0,64) + [64,128))
 //   [128, 192) O^T: + S_hi^T Q~^T, then + dV^T P^T; read and reset to 0 by the output warps
-// After dV is formed, per 32-token group g, in place: dV'^T hi at 32g, lo at 32g + 16.
+// dV'^T hi/lo go to C_SHI (free once W S has run), per 32-token group g: hi at 32g,
+// lo at 32g + 16, so that the next chunk's U can be issued into C_UT right away.
 constexpr uint32_t C_UT = 256;
 constexpr uint32_t C_O = C_UT + 128;
 constexpr uint32_t C_DVB = 448;        // dV^T bf16 (32 columns), A operand of dV^T P^T
@@ -1009,13 +1010,13 @@ __device__ __forceinline__ void chain_body(const CUtensorMap* map_q, const CUten
                 mbar_spin_or_abort(&bars->dv_done, c & 1, err, abort_flag);
                 tc_fence_after();
                 if (!*abort_flag) {
-                    // S^T += dV'^T K (K as MN-major B); dV' hi/lo sit in C_UT per 32-token half
+                    // S^T += dV'^T K (K as MN-major B); dV' hi/lo sit in C_SHI per 32-token half
                     constexpr uint32_t idst = idesc_bf16(128, DK, false, true);
 #pragma unroll
                     for (int p = 0; p < 2; ++p) {
 #pragma unroll
                         for (int kk = 0; kk < 4; ++kk)
-                            umma_bf16_ts(tmem + C_ST, tmem + C_UT + (kk >> 1) * 32 + p * 16 + (kk & 1) * 8,
+                            umma_bf16_ts(tmem + C_ST, tmem + C_SHI + (kk >> 1) * 32 + p * 16 + (kk & 1) * 8,
                                          sdesc_sw128(sk + kk * 2048, 8192, 1024), idst, 1u);
                     }
                     umma_commit(&bars->st_done);
@@ -1029,8 +1030,8 @@ __device__ __forceinline__ void chain_body(const CUtensorMap* map_q, const CUten
                     umma_commit(&bars->slot_free[slot]);
                 }
                 if (c + 1 < nchunks) {
-                    // U^T of the next chunk overwrites C_UT once the state update has read dV'
-                    mbar_spin_or_abort(&bars->st_done, c & 1, err, abort_flag);
+                    // U^T of the next chunk into C_UT, which the dV conversion has read (dv_done);
+                    // it runs on the tensor pipe while the state path splits the next S
                     const bool ok = mbar_spin_or_abort(&bars->va_full, (c + 1) & 1, err, abort_flag);
                     tc_fence_after();
                     if (ok && !*abort_flag) issue_u();
@@ -1109,8 +1110,11 @@ __device__ __forceinline__ void chain_body(const CUtensorMap* map_q, const CUten
                     bw[i] = cvt_bf16x2(d0, d1);
                     split2_bf16(d0 * edec[2 * i], d1 * edec[2 * i + 1], hi[i], lo[i]);
                 }
-                tmem_st16(tmem + lane_off + C_UT + grp * 32, hi);
-                tmem_st16(tmem + lane_off + C_UT + grp * 32 + 16, lo);
+                // dV' over the S hi columns (free once W S has run; the next split waits for
+                // the state update that reads them), so the next chunk's U can go into C_UT
+                // as soon as this conversion has read it
+                tmem_st16(tmem + lane_off + C_SHI + grp * 32, hi);
+                tmem_st16(tmem + lane_off + C_SHI + grp * 32 + 16, lo);
                 tmem_st16(tmem + lane_off + C_DVB + grp * 16, bw);
             }
             tmem_st_wait();
