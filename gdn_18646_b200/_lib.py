@@ -30,6 +30,7 @@ GDN_SCHEDULE_AUTO = 0
 GDN_SCHEDULE_SINGLE = 1
 GDN_SCHEDULE_PIECED = 2
 GDN_SCHEDULE_STREAM = 3
+GDN_DECODE_L2NORM_QK = 1
 
 _P = ctypes.c_void_p
 _I = ctypes.c_int
@@ -59,11 +60,13 @@ SIGNATURES = {
     "gdn_prefill_set_schedule": [_I],
     "gdn_prefill_launch_count": [_I, _I, _I, _I, _I],
     "gdn_decode_step": [_P, _P, _P, _P, _P, _I, _P, _P, _P, _P, _P, _I, _I, _I, _I, _I, _F, _P],
+    "gdn_decode_step_ex": [_P, _P, _P, _P, _P, _I, _P, _P, _P, _P, _P, _I, _I, _I, _I, _I, _F, _I, _P],
     "gdn_rmsnorm_fwd": [_P, _P, _P, _I, _I, _F, _P],
     "gdn_gated_rmsnorm_fwd": [_P, _I, _P, _P, _P, _I, _I, _F, _P],
     "gdn_decode_proj_fwd": [_P, _P, _F, _I, _I, ctypes.POINTER(ProjSegment), _I, _P],
     "gdn_proj_conv_silu_fwd": [_P, _P, _P, _P, _I, _I, _I, _I, _P, _P, _I, _P],
     "gdn_check_device_error": [],
+    "gdn_set_launch_overlap": [_I],
     "gdn_last_error": [],
     "gdn_version": [],
 }

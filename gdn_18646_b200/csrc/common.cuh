@@ -23,6 +23,7 @@ int fail(int code, const char* fmt, ...);
 int check_sm100();                         // GDN_OK or GDN_ERR_DEVICE / GDN_ERR_CUDA
 int launch_status(const char* what);       // cudaGetLastError after a launch
 unsigned int* device_error_word();         // per-device error flag (device pointer)
+bool launch_overlap();                     // gdn_set_launch_overlap() state
 
 inline bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
 
@@ -211,6 +212,13 @@ __device__ __forceinline__ void bulk_load(void* dst, const void* src, uint32_t b
         : "memory");
 }
 __device__ __forceinline__ void bulk_wait_all0() { asm volatile("cp.async.bulk.wait_group 0;" ::: "memory"); }
+
+// Programmatic dependent launch: let the next kernel of the stream start, and wait
+// until the kernels this one depends on have completed with their memory visible.
+// Both are no-ops for a kernel that was not launched with programmatic stream
+// serialisation or has no dependents.
+__device__ __forceinline__ void pdl_launch_dependents() { asm volatile("griddepcontrol.launch_dependents;" ::: "memory"); }
+__device__ __forceinline__ void pdl_wait_prior() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
 
 // named barrier over a subset of warps
 __device__ __forceinline__ void named_bar(int id, int nthreads) {

@@ -27,18 +27,20 @@ struct DecodeCfg {
 
 template <int DK, int DV>
 __global__ void __launch_bounds__(DecodeCfg<DK, DV>::NT)
-decode_step_kernel(const uint16_t* __restrict__ q, const uint16_t* __restrict__ k,
-                   const uint16_t* __restrict__ v, const void* __restrict__ a,
-                   const void* __restrict__ b, int gate_dtype, const float* __restrict__ A_log,
+decode_step_kernel(const uint16_t* q, const uint16_t* k, const uint16_t* v, const void* a, const void* b,
+                   int gate_dtype, const float* __restrict__ A_log,
                    const float* __restrict__ dt_bias, const float* state_in, float* state_out,
-                   float* __restrict__ out, int Hqk, int Hv, float scale) {
+                   float* __restrict__ out, int Hqk, int Hv, float scale, int l2qk) {
     using C = DecodeCfg<DK, DV>;
     __shared__ float q_s[DK];
     __shared__ float k_s[DK];
     __shared__ float red_a[C::RG][DV];
     __shared__ float red_b[C::RG][DV];
     __shared__ float qk_s;
+    __shared__ float inv_s[2];
 
+    pdl_launch_dependents();                   // the next kernel may launch (it waits for this one)
+    pdl_wait_prior();                          // inputs and state come from earlier kernels
     const int tid = threadIdx.x;
     const int cg = tid % C::CG;
     const int rg = tid / C::CG;
@@ -55,18 +57,42 @@ decode_step_kernel(const uint16_t* __restrict__ q, const uint16_t* __restrict__ 
     for (int r = 0; r < C::RPT; ++r)
         s[r] = ld_stream_f4(state_in + s_off + static_cast<long>(r * C::RG + rg) * DV + 4 * cg);
 
+    // q, k, v, a, b are outputs of the kernel just before this one, which may still
+    // run until pdl_wait_prior() above: read them through L2 (ld.global.cg), never
+    // through the non-coherent read-only path
     for (int i = tid; i < DK; i += C::NT) {
-        q_s[i] = bf16_bits_to_f32(q[qk_off + i]);
-        k_s[i] = bf16_bits_to_f32(k[qk_off + i]);
+        q_s[i] = bf16_bits_to_f32(__ldcg(q + qk_off + i));
+        k_s[i] = bf16_bits_to_f32(__ldcg(k + qk_off + i));
     }
     // gates (reference/decode_ref.py:36-38)
-    const float av = load_gate(a, bh, gate_dtype);
-    const float bv = load_gate(b, bh, gate_dtype);
+    const float av = gate_dtype == GDN_DTYPE_BF16 ? bf16_bits_to_f32(__ldcg(static_cast<const uint16_t*>(a) + bh))
+                                                  : __ldcg(static_cast<const float*>(a) + bh);
+    const float bv = gate_dtype == GDN_DTYPE_BF16 ? bf16_bits_to_f32(__ldcg(static_cast<const uint16_t*>(b) + bh))
+                                                  : __ldcg(static_cast<const float*>(b) + bh);
     const float dtb = dt_bias ? dt_bias[h] : 0.f;
     const float g = expf(-expf(A_log[h]) * softplus_f(av + dtb));
     const float beta = sigmoid_f(bv);
-    const uint2 vraw = *reinterpret_cast<const uint2*>(v + static_cast<long>(bh) * DV + 4 * cg);
+    const uint2 vraw = __ldcg(reinterpret_cast<const uint2*>(v + static_cast<long>(bh) * DV + 4 * cg));
     __syncthreads();
+    if (l2qk) {
+        // q, k L2-normalised per head (fp32, eps 1e-6) and rounded to bf16, as the
+        // layer's projection epilogue does (reference/fused_proj_conv_silu_ref.py:64-66
+        // composition); warp 0 takes q, warp 1 k
+        if (tid < 64) {
+            const float* src = tid < 32 ? q_s : k_s;
+            float ss = 0.f;
+            for (int i = tid & 31; i < DK; i += 32) ss = fmaf(src[i], src[i], ss);
+#pragma unroll
+            for (int o = 16; o > 0; o >>= 1) ss += __shfl_xor_sync(0xffffffffu, ss, o);
+            if ((tid & 31) == 0) inv_s[tid >> 5] = 1.f / sqrtf(ss + 1e-6f);
+        }
+        __syncthreads();
+        for (int i = tid; i < DK; i += C::NT) {
+            q_s[i] = bf16_bits_to_f32(f32_to_bf16_bits(q_s[i] * inv_s[0]));
+            k_s[i] = bf16_bits_to_f32(f32_to_bf16_bits(k_s[i] * inv_s[1]));
+        }
+        __syncthreads();
+    }
 
     if (tid < 32) {
         float acc = 0.f;
@@ -123,25 +149,36 @@ decode_step_kernel(const uint16_t* __restrict__ q, const uint16_t* __restrict__ 
 }
 
 template <int DK, int DV>
-void launch_decode(const void* q, const void* k, const void* v, const void* a, const void* b,
+cudaError_t launch_decode(const void* q, const void* k, const void* v, const void* a, const void* b,
                    int gate_dtype, const float* A_log, const float* dt_bias, const float* s_in,
-                   float* s_out, float* out, int B, int Hqk, int Hv, float scale, cudaStream_t st) {
+                   float* s_out, float* out, int B, int Hqk, int Hv, float scale, int l2qk, cudaStream_t st) {
     using C = DecodeCfg<DK, DV>;
-    decode_step_kernel<DK, DV><<<B * Hv, C::NT, 0, st>>>(
-        static_cast<const uint16_t*>(q), static_cast<const uint16_t*>(k),
-        static_cast<const uint16_t*>(v), a, b, gate_dtype, A_log, dt_bias, s_in, s_out, out, Hqk, Hv,
-        scale);
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3(B * Hv);
+    cfg.blockDim = dim3(C::NT);
+    cfg.stream = st;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = launch_overlap() ? 1 : 0;
+    return cudaLaunchKernelEx(&cfg, decode_step_kernel<DK, DV>, static_cast<const uint16_t*>(q),
+                       static_cast<const uint16_t*>(k), static_cast<const uint16_t*>(v), a, b, gate_dtype, A_log,
+                       dt_bias, s_in, s_out, out, Hqk, Hv, scale, l2qk);
 }
 
 }  // namespace
 }  // namespace gdn
 
-extern "C" int gdn_decode_step(const void* q, const void* k, const void* v, const void* a,
-                               const void* b, int gate_dtype, const float* A_log,
-                               const float* dt_bias, const float* state_in, float* state_out,
-                               float* out, int B, int Hqk, int Hv, int dk, int dv, float scale,
-                               void* stream) {
+extern "C" int gdn_decode_step_ex(const void* q, const void* k, const void* v, const void* a,
+                                  const void* b, int gate_dtype, const float* A_log,
+                                  const float* dt_bias, const float* state_in, float* state_out,
+                                  float* out, int B, int Hqk, int Hv, int dk, int dv, float scale,
+                                  int flags, void* stream) {
     using namespace gdn;
+    if (flags & ~GDN_DECODE_L2NORM_QK)
+        return fail(GDN_ERR_DTYPE, "gdn_decode_step: unknown flags 0x%x", flags);
+    const int l2qk = (flags & GDN_DECODE_L2NORM_QK) ? 1 : 0;
     if (!q || !k || !v || !a || !b || !A_log || !state_in || !state_out || !out)
         return fail(GDN_ERR_NULL, "gdn_decode_step: q, k, v, a, b, A_log, state_in, state_out and out are required");
     if (B <= 0 || Hqk <= 0 || Hv <= 0 || Hv % Hqk != 0)
@@ -162,8 +199,11 @@ extern "C" int gdn_decode_step(const void* q, const void* k, const void* v, cons
     cudaStream_t s = static_cast<cudaStream_t>(stream);
 #define GDN_DEC(DKV, DVV)                                                                     \
     if (dk == DKV && dv == DVV) {                                                             \
-        launch_decode<DKV, DVV>(q, k, v, a, b, gate_dtype, A_log, dt_bias, state_in, state_out, \
-                                out, B, Hqk, Hv, scale, s);                                     \
+        const cudaError_t e = launch_decode<DKV, DVV>(q, k, v, a, b, gate_dtype, A_log, dt_bias,  \
+                                                      state_in, state_out, out, B, Hqk, Hv, scale, \
+                                                      l2qk, s);                                   \
+        if (e != cudaSuccess)                                                                 \
+            return fail(GDN_ERR_CUDA, "gdn_decode_step: launch failed: %s", cudaGetErrorString(e)); \
         return launch_status("gdn_decode_step");                                              \
     }
     GDN_DEC(64, 64)
@@ -177,4 +217,13 @@ extern "C" int gdn_decode_step(const void* q, const void* k, const void* v, cons
     GDN_DEC(256, 256)
 #undef GDN_DEC
     return fail(GDN_ERR_UNSUPPORTED, "gdn_decode_step: unreachable dims");
+}
+
+extern "C" int gdn_decode_step(const void* q, const void* k, const void* v, const void* a,
+                               const void* b, int gate_dtype, const float* A_log,
+                               const float* dt_bias, const float* state_in, float* state_out,
+                               float* out, int B, int Hqk, int Hv, int dk, int dv, float scale,
+                               void* stream) {
+    return gdn_decode_step_ex(q, k, v, a, b, gate_dtype, A_log, dt_bias, state_in, state_out, out, B, Hqk, Hv, dk,
+                              dv, scale, 0, stream);
 }

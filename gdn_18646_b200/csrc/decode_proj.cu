@@ -26,15 +26,18 @@
 // token rows.  The kernel is persistent, one CTA per SM, and warp-specialised
 // so that the weight stream never waits for an epilogue:
 //
-//   producer warp   initialises the barriers and bulk-copies the B token rows
-//                   and the RMSNorm weight at once, then streams the CTA's
-//                   tiles through a shared-memory ring of 2..8 stages of 16
-//                   rows x KC columns (KC <= 2048; one cp.async.bulk per row
-//                   and stage) on full/empty mbarriers, and each conv tile's
-//                   conv weights and history into a 4-deep side ring.  4 KB
-//                   row copies stream at the HBM rate; 1 KB rows reached only
-//                   ~30% of it.  Every global read of the kernel is one of
-//                   these copies: a plain load issued behind the weight
+//   producer warp   initialises the barriers, streams the first ring's worth
+//                   of weight stages (2..8 stages of 16 rows x KC columns,
+//                   KC <= 2048, one cp.async.bulk per row and stage, on
+//                   full/empty mbarriers), waits for the kernels it depends
+//                   on (griddepcontrol: under programmatic dependent launch
+//                   the weights start streaming while the previous kernel
+//                   still runs), bulk-copies the B token rows and the RMSNorm
+//                   weight, then each conv tile's conv weights and history
+//                   into a 4-deep side ring and the remaining weight stages.
+//                   4 KB row copies stream at the HBM rate; 1 KB rows reached
+//                   only ~30% of it.  Every global read of the kernel is one
+//                   of these copies: a plain load issued behind the weight
 //                   stream waited ~2 us;
 //   8 MMA warps     RMS-normalise the token rows in place once, then each
 //                   takes one eighth of every stage's K range (ldmatrix A
@@ -93,6 +96,7 @@ struct Args {
     float eps;
     int B, D, KC, nst;         // KC: columns per ring stage; nst: ring stages
     int nseg, cl, ngroups;     // cl: CTAs per cluster = tiles per group
+    int pdl;                   // launched with programmatic stream serialisation
     unsigned int* err;         // device error word (bounded waits)
     Seg seg[kMaxSeg];
 };
@@ -247,20 +251,48 @@ decode_proj_kernel(const __grid_constant__ Args a) {
                 mbar_arrive_expect_tx(&xbar[0], a.cl * B * 4);
                 mbar_arrive_expect_tx(&xbar[1], a.cl * B * 4);
             }
-            mbar_arrive_expect_tx(&xfull, static_cast<uint32_t>(B + (a.gamma ? 1 : 0)) * D * 2);
         }
         __syncwarp();
-        if (lane < B) bulk_load(xs + lane * ldx, a.x + static_cast<long>(lane) * D, static_cast<uint32_t>(D) * 2, &xfull);
-        if (lane == kMaxRows && a.gamma) bulk_load(gs, a.gamma, static_cast<uint32_t>(D) * 2, &xfull);
         named_bar(0, kThreads);                        // barriers initialised
         cluster_arrive();
-        // Token rows and RMSNorm weight land before the weight stream starts: issued
-        // next to it they queue behind ~20 MB of weight reads (~5 us).  (Issuing a
-        // bulk copy can itself stall for microseconds once the TMA queue is full,
-        // so the barriers above come first.)
-        if (lane == 0) mbar_wait_or_abort(&xfull, 0, a.err, &abort_flag);
-        __syncwarp();
+        if (lane == 0) pdl_launch_dependents();        // the next kernel may launch (it waits for us)
+        // token rows and RMSNorm weight: data of earlier kernels, so after the wait
+        auto issue_x = [&]() {
+            pdl_wait_prior();
+            if (lane == 0) mbar_arrive_expect_tx(&xfull, static_cast<uint32_t>(B + (a.gamma ? 1 : 0)) * D * 2);
+            __syncwarp();
+            if (lane < B)
+                bulk_load(xs + lane * ldx, a.x + static_cast<long>(lane) * D, static_cast<uint32_t>(D) * 2, &xfull);
+            if (lane == kMaxRows && a.gamma) bulk_load(gs, a.gamma, static_cast<uint32_t>(D) * 2, &xfull);
+        };
+        if (!a.pdl) {
+            // launched after the previous kernel completed: the token rows go first and
+            // land before the weight stream starts (issued next to it they queue behind
+            // ~20 MB of weight reads, ~5 us)
+            issue_x();
+            if (lane == 0) mbar_wait_or_abort(&xfull, 0, a.err, &abort_flag);
+            __syncwarp();
+        }
+        // Phase A: the first ring's worth of weight stages.  Weights are constant
+        // operands: under programmatic dependent launch they stream while the
+        // previous kernel still runs.
         const uint32_t stage_bytes = static_cast<uint32_t>(kBs) * KC * 2;
+        uint32_t pre = 0;
+        for (int j = static_cast<int>(cid); j < a.ngroups && pre < static_cast<uint32_t>(nst);
+             j += static_cast<int>(ncl)) {
+            int s;
+            const int row0 = tile_of(a, j, rank, s);
+            if (row0 < 0) continue;
+            const uint16_t* W = a.seg[s].W + static_cast<long>(row0 + lane) * D;
+            for (int kc = 0; kc < nk && pre < static_cast<uint32_t>(nst); ++kc, ++pre) {
+                if (lane == 0) mbar_arrive_expect_tx(&full[pre], stage_bytes);      // fresh slot
+                __syncwarp();
+                if (lane < kBs)
+                    bulk_load(ring + (pre * kBs + lane) * lds, W + kc * KC, static_cast<uint32_t>(KC) * 2, &full[pre]);
+            }
+        }
+        if (a.pdl) issue_x();
+        // Phase B (after the wait: the conv history is data of earlier kernels): conv side data of every tile, and the weight stages past the first ring
         uint32_t q = 0, nsd = 0;
         for (int j = static_cast<int>(cid); j < a.ngroups; j += static_cast<int>(ncl)) {
             int s;
@@ -283,6 +315,7 @@ decode_proj_kernel(const __grid_constant__ Args a) {
             }
             const uint16_t* W = g.W + static_cast<long>(row0 + lane) * D;
             for (int kc = 0; kc < nk; ++kc, ++q) {
+                if (q < pre) continue;                 // issued in phase A
                 const uint32_t st = q % nst, ph = (q / nst) & 1u;
                 if (lane == 0) {
                     mbar_wait_or_abort(&empty[st], ph ^ 1u, a.err, &abort_flag);
@@ -573,13 +606,16 @@ extern "C" int gdn_decode_proj_fwd(const void* x, const void* norm_gamma, float 
     cfg.blockDim = dim3(kThreads);
     cfg.dynamicSmemBytes = smem;
     cfg.stream = static_cast<cudaStream_t>(stream);
-    cudaLaunchAttribute attr[1];
+    cudaLaunchAttribute attr[2];
     attr[0].id = cudaLaunchAttributeClusterDimension;
     attr[0].val.clusterDim.x = cl;
     attr[0].val.clusterDim.y = 1;
     attr[0].val.clusterDim.z = 1;
+    attr[1].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[1].val.programmaticStreamSerializationAllowed = 1;
     cfg.attrs = attr;
-    cfg.numAttrs = 1;
+    a.pdl = launch_overlap() ? 1 : 0;
+    cfg.numAttrs = a.pdl ? 2 : 1;
     // persistent grid: as many clusters as fit at once (cached per device, cluster size, shared memory)
     int fit = 0;
     {

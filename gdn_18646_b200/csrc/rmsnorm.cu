@@ -31,6 +31,10 @@ template <int CPT, bool GATED, bool XF32>
 __global__ void __launch_bounds__(32 * kRowsPerBlock)
 rmsnorm_kernel(const void* __restrict__ xv, const uint16_t* __restrict__ z,
                const uint16_t* __restrict__ gamma, uint16_t* __restrict__ y, int R, int D, float eps) {
+    pdl_launch_dependents();                   // the next kernel may launch (it waits for this one)
+    pdl_wait_prior();                          // x and z come from earlier kernels
+    // (x and z are read through L2 with ld.global.cg: under programmatic dependent launch
+    // the kernel that writes them may still have been running when this one started)
     const int lane = threadIdx.x & 31;
     const long row = static_cast<long>(blockIdx.x) * kRowsPerBlock + (threadIdx.x >> 5);
     if (row >= R) return;
@@ -46,13 +50,13 @@ rmsnorm_kernel(const void* __restrict__ xv, const uint16_t* __restrict__ z,
             float f[8];
             if constexpr (XF32) {
                 const float4* p = reinterpret_cast<const float4*>(static_cast<const float*>(xv) + row * D) + 2 * ch;
-                const float4 u0 = __ldcs(p), u1 = __ldcs(p + 1);
+                const float4 u0 = __ldcg(p), u1 = __ldcg(p + 1);
                 f[0] = u0.x; f[1] = u0.y; f[2] = u0.z; f[3] = u0.w;
                 f[4] = u1.x; f[5] = u1.y; f[6] = u1.z; f[7] = u1.w;
 #pragma unroll
                 for (int i = 0; i < 8; ++i) xf[c][i] = f[i];
             } else {
-                xw[c] = __ldcs(reinterpret_cast<const uint4*>(static_cast<const uint16_t*>(xv) + row * D) + ch);
+                xw[c] = __ldcg(reinterpret_cast<const uint4*>(static_cast<const uint16_t*>(xv) + row * D) + ch);
                 unpack8(xw[c], f);
             }
 #pragma unroll
@@ -78,7 +82,7 @@ rmsnorm_kernel(const void* __restrict__ xv, const uint16_t* __restrict__ z,
             float o[8];
             if constexpr (GATED) {
                 float zf[8];
-                unpack8(__ldcs(reinterpret_cast<const uint4*>(z + row * D) + ch), zf);
+                unpack8(__ldcg(reinterpret_cast<const uint4*>(z + row * D) + ch), zf);
 #pragma unroll
                 for (int i = 0; i < 8; ++i) o[i] = (f[i] * r) * gf[i] * silu_f(zf[i]);
             } else {
@@ -99,9 +103,19 @@ int launch_rmsnorm(const void* x, const void* z, const void* gamma, void* y, int
     auto* zz = static_cast<const uint16_t*>(z);
     auto* gg = static_cast<const uint16_t*>(gamma);
     auto* yy = static_cast<uint16_t*>(y);
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = grid;
+    cfg.blockDim = block;
+    cfg.stream = st;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = launch_overlap() ? 1 : 0;
 #define GDN_RMS(N)                                                                           \
     if (chunks_per_lane <= N) {                                                              \
-        rmsnorm_kernel<N, GATED, XF32><<<grid, block, 0, st>>>(x, zz, gg, yy, R, D, eps);    \
+        const cudaError_t e = cudaLaunchKernelEx(&cfg, rmsnorm_kernel<N, GATED, XF32>, x, zz, gg, yy, R, D, eps); \
+        if (e != cudaSuccess) return fail(GDN_ERR_CUDA, "%s: launch failed: %s", name, cudaGetErrorString(e)); \
         return launch_status(name);                                                          \
     }
     GDN_RMS(1)

@@ -1,5 +1,6 @@
 // status.cu -- thread-local error strings, device checks, the device-side
 // error word, and TMA tensor-map encoding through the driver entry point.
+#include <atomic>
 #include <mutex>
 
 #include "common.cuh"
@@ -119,6 +120,18 @@ int make_map_bf16(CUtensorMap* map, const void* base, int rank, const uint64_t* 
 }
 
 }  // namespace gdn
+
+namespace gdn {
+namespace {
+std::atomic<int> g_launch_overlap{0};
+}  // namespace
+bool launch_overlap() { return g_launch_overlap.load(std::memory_order_relaxed) != 0; }
+}  // namespace gdn
+
+extern "C" int gdn_set_launch_overlap(int on) {
+    gdn::g_launch_overlap.store(on ? 1 : 0, std::memory_order_relaxed);
+    return GDN_OK;
+}
 
 extern "C" const char* gdn_last_error(void) { return gdn::t_last_error.c_str(); }
 

@@ -24,7 +24,7 @@ from dataclasses import dataclass
 
 import torch
 
-from . import ops
+from . import _lib, ops
 
 
 @dataclass
@@ -125,10 +125,11 @@ class GDNLayer:
         state is updated in place; conv histories go to ``out_state`` (fresh
         buffers by default; ``out_state=state`` updates them in place too).
 
-        Four launches: RMSNorm + q|k|v (conv4, SiLU, q/k L2 norm) + z + a + b as
-        one weight-streaming GEMV over the cached conv history
-        (gdn_decode_proj_fwd), the recurrence step, the gated output norm, and
-        the output projection (the same GEMV kernel).  All shapes are static, so
+        Four launches: RMSNorm + q|k|v (conv4, SiLU) + z + a + b as one
+        weight-streaming GEMV over the cached conv history (gdn_decode_proj_fwd),
+        the recurrence step with the q/k L2 norm folded in (so the GEMV needs no
+        cross-CTA reduction), the gated output norm, and the output projection
+        (the same GEMV kernel).  All shapes are static, so
         the call can be captured in a CUDA graph."""
         c, w = self.cfg, self.w
         B = x.shape[0]
@@ -138,10 +139,8 @@ class GDNLayer:
                              conv_q=torch.empty_like(state["conv_q"]), conv_k=torch.empty_like(state["conv_k"]),
                              conv_v=torch.empty_like(state["conv_v"]))
         q, k, v, z, a, b = ops.decode_proj(x.reshape(B, D), [
-            dict(W=w["W_q"], conv_w=w["conv_q"], conv_state_in=state["conv_q"], conv_state_out=out_state["conv_q"],
-                 l2_group=c.dk),
-            dict(W=w["W_k"], conv_w=w["conv_k"], conv_state_in=state["conv_k"], conv_state_out=out_state["conv_k"],
-                 l2_group=c.dk),
+            dict(W=w["W_q"], conv_w=w["conv_q"], conv_state_in=state["conv_q"], conv_state_out=out_state["conv_q"]),
+            dict(W=w["W_k"], conv_w=w["conv_k"], conv_state_in=state["conv_k"], conv_state_out=out_state["conv_k"]),
             dict(W=w["W_v"], conv_w=w["conv_v"], conv_state_in=state["conv_v"], conv_state_out=out_state["conv_v"]),
             dict(W=w["W_z"]),
             dict(W=w["W_ab"][:c.n_v]),
@@ -149,7 +148,7 @@ class GDNLayer:
         ], norm_gamma=w["norm_gamma"], eps=c.eps)
         o = ops.decode_step(q.view(B, c.n_qk, c.dk), k.view(B, c.n_qk, c.dk), v.view(B, c.n_v, c.dv), a, b,
                             w["A_log"], w["dt_bias"], state["recurrent"], scale=self.scale,
-                            state_out=out_state["recurrent"])
+                            state_out=out_state["recurrent"], l2norm_qk=True)
         y = ops.gated_rmsnorm(o.view(B * c.n_v, c.dv), z.view(B * c.n_v, c.dv), w["onorm_gamma"], c.eps)
         (out,) = ops.decode_proj(y.view(B, c.v_dim), [dict(W=w["W_o"])])
         return out.view(B, 1, D), out_state
@@ -160,7 +159,10 @@ class DecodeGraph:
     decode loop costs one graph launch per token.  The recurrent state and the
     conv histories of ``state`` are updated in place by every step."""
 
-    def __init__(self, layer: GDNLayer, state: dict, B: int):
+    def __init__(self, layer: GDNLayer, state: dict, B: int, overlap: bool = True):
+        """``overlap``: capture the step's kernels with programmatic dependent
+        launch (gdn_set_launch_overlap), so each launches while its predecessor
+        finishes and the projections stream their weights early."""
         self.layer = layer
         dev = state["recurrent"].device
         self.x = torch.zeros(B, 1, layer.cfg.hidden, dtype=torch.bfloat16, device=dev)
@@ -173,8 +175,13 @@ class DecodeGraph:
             layer.decode(self.x, scratch, scratch)
         torch.cuda.current_stream().wait_stream(s)
         self.graph = torch.cuda.CUDAGraph()
-        with torch.cuda.graph(self.graph):
-            self.y, _ = layer.decode(self.x, state, state)
+        lib = _lib.lib()
+        lib.gdn_set_launch_overlap(1 if overlap else 0)
+        try:
+            with torch.cuda.graph(self.graph):
+                self.y, _ = layer.decode(self.x, state, state)
+        finally:
+            lib.gdn_set_launch_overlap(0)
 
     def step(self, x: torch.Tensor) -> torch.Tensor:
         self.x.copy_(x)

@@ -155,9 +155,10 @@ def prefill_varlen(q, k, v, A_log, a, b_logits, cu_seqlens, *, max_len=None, dt_
     return out, state_out
 
 
-def decode_step(q, k, v, a, b, A_log, dt_bias, state, *, scale=0.0, out=None, state_out=None):
+def decode_step(q, k, v, a, b, A_log, dt_bias, state, *, scale=0.0, out=None, state_out=None, l2norm_qk=False):
     """One decode step; updates ``state`` in place unless ``state_out`` is given.
     q,k [B,Hqk,dk] bf16; v [B,Hv,dv] bf16; a,b [B,Hv]; state [B,Hv,dk,dv] f32.
+    With ``l2norm_qk`` q and k are L2-normalised per head inside the kernel.
     Returns out f32 [B,Hv,dv]."""
     B, Hqk, dk = q.shape
     Hv, dv = v.shape[1], v.shape[2]
@@ -169,9 +170,9 @@ def decode_step(q, k, v, a, b, A_log, dt_bias, state, *, scale=0.0, out=None, st
         out = torch.empty(B, Hv, dv, dtype=torch.float32, device=q.device)
     if state_out is None:
         state_out = state
-    _lib.call("gdn_decode_step", _ptr(q), _ptr(k), _ptr(v), _ptr(a), _ptr(b), gdt, _ptr(A_log),
+    _lib.call("gdn_decode_step_ex", _ptr(q), _ptr(k), _ptr(v), _ptr(a), _ptr(b), gdt, _ptr(A_log),
               _ptr(dt_bias), _ptr(state), _ptr(state_out), _ptr(out), B, Hqk, Hv, dk, dv, float(scale),
-              _stream())
+              _lib.GDN_DECODE_L2NORM_QK if l2norm_qk else 0, _stream())
     return out
 
 

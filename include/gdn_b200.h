@@ -210,6 +210,19 @@ int gdn_decode_step(const void* q, const void* k, const void* v,
                     int B, int Hqk, int Hv, int dk, int dv, float scale, void* stream);
 
 /*
+ * gdn_decode_step with options.  flags: GDN_DECODE_L2NORM_QK L2-normalises q and k
+ * per head first (fp32 sum of squares, eps 1e-6, result rounded to bf16), the
+ * layer's q/k norm, so the projection before it needs no cross-CTA reduction.
+ * No reference counterpart (the reference layer normalises in its own glue).
+ */
+enum { GDN_DECODE_L2NORM_QK = 1 };
+int gdn_decode_step_ex(const void* q, const void* k, const void* v,
+                       const void* a, const void* b, int gate_dtype,
+                       const float* A_log, const float* dt_bias,
+                       const float* state_in, float* state_out, float* out,
+                       int B, int Hqk, int Hv, int dk, int dv, float scale, int flags, void* stream);
+
+/*
  * RMSNorm, bf16 in/out, fp32 math: y = x * rsqrt(mean(x^2) + eps) * gamma.
  * Replaces rmsnorm_forward(), kernels/rmsnorm.cu:280-293 (math: reference/rmsnorm_ref.py:9-28).
  * x, y bf16 [R, D]; gamma bf16 [D].  D % 8 == 0, D <= 8192 (D <= 4096 when x is f32).
@@ -285,6 +298,18 @@ int gdn_proj_conv_silu_fwd(const void* x, const void* W, const void* conv_w, voi
 
 /* Human-readable description of the calling thread's last error. */
 const char* gdn_last_error(void);
+
+/*
+ * Process-wide (default 0): with on != 0 the decode-step kernels
+ * (gdn_decode_proj_fwd, gdn_decode_step[_ex], gdn_rmsnorm_fwd,
+ * gdn_gated_rmsnorm_fwd) launch with programmatic stream serialisation: each
+ * lets the next kernel of the stream launch early and waits for its own
+ * predecessors before reading their outputs, and gdn_decode_proj_fwd streams its
+ * weights before that wait.  Weight operands must therefore not be written by
+ * the kernels just before it on the stream.  Works inside CUDA graph capture.
+ * No counterpart in the reference.
+ */
+int gdn_set_launch_overlap(int on);
 
 /* Library version string. */
 const char* gdn_version(void);

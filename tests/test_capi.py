@@ -203,3 +203,9 @@ def test_prefill_varlen_rejects(lib, over, code):
 def test_prefill_varlen_workspace_matches_fixed_length(lib):
     assert lib.gdn_prefill_varlen_workspace_bytes(3, 1000, 4, 128, 128) == \
         lib.gdn_prefill_workspace_bytes(3, 1000, 4, 128, 128)
+
+
+def test_decode_step_ex_rejects_unknown_flags(lib):
+    args = [FAKE, FAKE, FAKE, FAKE, FAKE, 0, FAKE, None, FAKE, FAKE, FAKE, 1, 1, 1, 128, 128, 0.0]
+    assert _lib.call_status("gdn_decode_step_ex", *args, 4, None) == _lib.GDN_ERR_DTYPE
+    assert "flags" in _lib.last_error()

@@ -70,6 +70,37 @@ def test_decode_gva_and_f32_gates(cuda_device):
     assert O.rel_fro(S1, S_r) < 1e-6
 
 
+@pytest.mark.parametrize("dk,dv,Hqk", [(128, 128, 4), (64, 256, 2), (256, 64, 1)])
+def test_decode_l2norm_qk_flag(cuda_device, dk, dv, Hqk):
+    """GDN_DECODE_L2NORM_QK: unnormalised q, k in; the kernel normalises per head and
+    rounds to bf16 before the step.  Against the oracle on the oracle-normalised
+    inputs (O.l2norm_heads, the projection epilogue's restatement): both round the
+    same fp32 values to bf16, so a q/k element may differ by one bf16 ulp where the
+    sums of squares round differently."""
+    import torch
+    from gdn_18646_b200 import ops
+    rng = np.random.default_rng(dk + dv)
+    B, Hv = 2, 4
+    q = O.f32_to_bf16(rng.standard_normal((B, Hqk, dk), dtype=np.float32) * np.float32(0.3))
+    k = O.f32_to_bf16(rng.standard_normal((B, Hqk, dk), dtype=np.float32) * np.float32(0.3))
+    v = O.f32_to_bf16(rng.standard_normal((B, Hv, dv), dtype=np.float32))
+    a = O.f32_to_bf16(rng.standard_normal((B, Hv), dtype=np.float32))
+    b = O.f32_to_bf16(rng.standard_normal((B, Hv), dtype=np.float32))
+    S = rng.standard_normal((B, Hv, dk, dv), dtype=np.float32) * np.float32(0.02)
+    A_log = np.full((Hv,), math.log(0.1), np.float32)
+    dtb = np.zeros(Hv, np.float32)
+    St = to_dev(S)
+    o = ops.decode_step(to_dev(q), to_dev(k), to_dev(v), to_dev(a), to_dev(b), to_dev(A_log), to_dev(dtb), St,
+                        l2norm_qk=True)
+    torch.cuda.synchronize()
+    qn = O.l2norm_heads(q.reshape(B, Hqk * dk), dk).reshape(B, Hqk, dk)
+    kn = O.l2norm_heads(k.reshape(B, Hqk * dk), dk).reshape(B, Hqk, dk)
+    o_r, S_r = O.decode(np.repeat(qn, Hv // Hqk, 1), np.repeat(kn, Hv // Hqk, 1), v, S, A_log, a, dtb, b,
+                        dt=np.float64)
+    np.testing.assert_allclose(to_np(o), o_r, rtol=1e-2, atol=2e-3)
+    assert O.rel_fro(to_np(St), S_r) < 1e-3
+
+
 def test_decode_inplace_equals_out_of_place(cuda_device):
     steps, S, A_log, dtb = O.make_decode_inputs(5, 4, 8, 128, 128)
     st = steps[0]

@@ -60,7 +60,10 @@ def test_layer_prefill_then_decode_matches_full_prefill(cuda_device):
         assert np.mean(g != w) <= 0.05
 
 
-def test_layer_decode_cuda_graph_matches_eager(cuda_device):
+@pytest.mark.parametrize("overlap", [True, False])
+def test_layer_decode_cuda_graph_matches_eager(cuda_device, overlap):
+    """The CUDA-graph decode step, with and without programmatic dependent launch
+    between its kernels, gives the eager step's bits."""
     import torch
     from gdn_18646_b200.layer import DecodeGraph
     layer = _layer(2)
@@ -68,7 +71,7 @@ def test_layer_decode_cuda_graph_matches_eager(cuda_device):
     x = torch.randn(B, T0 + steps, 2048, device="cuda").bfloat16()
     _, st_e = layer.prefill(x[:, :T0].contiguous())
     st_g = {k: v.clone() for k, v in st_e.items()}
-    graph = DecodeGraph(layer, st_g, B)
+    graph = DecodeGraph(layer, st_g, B, overlap=overlap)
     for t in range(T0, T0 + steps):
         ye, st_e = layer.decode(x[:, t:t + 1].contiguous(), st_e)
         yg = graph.step(x[:, t:t + 1])
