@@ -65,6 +65,8 @@ SIGNATURES = {
     "gdn_gated_rmsnorm_fwd": [_P, _I, _P, _P, _P, _I, _I, _F, _P],
     "gdn_decode_proj_fwd": [_P, _P, _F, _I, _I, ctypes.POINTER(ProjSegment), _I, _P],
     "gdn_proj_conv_silu_fwd": [_P, _P, _P, _P, _I, _I, _I, _I, _P, _P, _I, _P],
+    "gdn_outproj_rs_fwd": [_P, _P, ctypes.POINTER(ctypes.c_void_p), _I, _I, _I, _I, _I, _P],
+    "gdn_outproj_reduce": [_P, _P, _I, _I, _I, _P],
     "gdn_check_device_error": [],
     "gdn_set_launch_overlap": [_I],
     "gdn_last_error": [],

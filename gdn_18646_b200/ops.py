@@ -17,6 +17,7 @@ the sm_100a kernels of the library.
 """
 from __future__ import annotations
 
+import ctypes
 import math
 
 import torch
@@ -173,6 +174,32 @@ def decode_step(q, k, v, a, b, A_log, dt_bias, state, *, scale=0.0, out=None, st
     _lib.call("gdn_decode_step_ex", _ptr(q), _ptr(k), _ptr(v), _ptr(a), _ptr(b), gdt, _ptr(A_log),
               _ptr(dt_bias), _ptr(state), _ptr(state_out), _ptr(out), B, Hqk, Hv, dk, dv, float(scale),
               _lib.GDN_DECODE_L2NORM_QK if l2norm_qk else 0, _stream())
+    return out
+
+
+def outproj_rs(x, W, recv_ptrs, rank, world):
+    """This rank's share of a head-sharded output projection, sent to its owners
+    (gdn_outproj_rs_fwd): the partial product x [M, K] @ W[N, K]^T, cut into row
+    blocks of M/world tokens, block s written into slot ``rank`` of the receive
+    buffer at ``recv_ptrs[s]`` (device pointers of every rank's [world, M/world, N]
+    bf16 buffer, peers' mapped into this process).  Only launches; ordering the
+    reduction after every rank's call is the caller's job."""
+    _cuda_contig(x, "x", torch.bfloat16)
+    _cuda_contig(W, "W", torch.bfloat16)
+    _need(x.dim() == 2 and W.dim() == 2 and x.shape[1] == W.shape[1], "x [M, K] and W [N, K] required")
+    _need(len(recv_ptrs) == world, "one receive buffer per rank")
+    arr = (ctypes.c_void_p * world)(*[int(p) for p in recv_ptrs])
+    _lib.call("gdn_outproj_rs_fwd", _ptr(x), _ptr(W), arr, x.shape[0], W.shape[0], x.shape[1], int(rank), int(world),
+              _stream())
+
+
+def outproj_reduce(recv, out=None):
+    """out [rows, N] = bf16(sum over slots of recv [world, rows, N]) (gdn_outproj_reduce)."""
+    _cuda_contig(recv, "recv", torch.bfloat16)
+    world, rows, N = recv.shape
+    if out is None:
+        out = torch.empty(rows, N, dtype=torch.bfloat16, device=recv.device)
+    _lib.call("gdn_outproj_reduce", _ptr(recv), _ptr(out), rows, N, world, _stream())
     return out
 
 

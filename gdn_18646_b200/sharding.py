@@ -95,3 +95,83 @@ def sharded_prefill(q, k, v, A_log, a, b, shard: HeadShard, *, Hqk=None, gather=
     o, S = ops.prefill(qs, ks, vs, shard_heads(A_log, shard, 0), shard_heads(a, shard, 1),
                        shard_heads(b, shard, 1), layout="bthd", **kw)
     return (gather_heads(o, shard, group) if gather else o), S
+
+
+# ---------------------------------------------------------------------------
+# Head-sharded output projection fused with its reduce-scatter
+# ---------------------------------------------------------------------------
+def owned_rows(M: int, rank: int, world: int) -> slice:
+    """Token rows of the layer output that ``rank`` keeps after the reduce-scatter."""
+    if M % world != 0:
+        raise ValueError(f"{M} rows do not split evenly over {world} ranks")
+    per = M // world
+    return slice(rank * per, (rank + 1) * per)
+
+
+class PeerBuffer:
+    """A receive buffer [world, rows, N] bf16 on every rank, and the device
+    pointers of all ranks' buffers in this process (CUDA IPC; NVLink peer
+    access within a node).  Slot s of rank d's buffer receives rank s's
+    partial product for the rows that d owns."""
+
+    def __init__(self, rows: int, N: int, group=None):
+        import torch.distributed as dist
+        from cuda.bindings import driver as drv
+        from cuda.bindings import runtime as rt
+        self.group = group
+        self.world = dist.get_world_size(group) if dist.is_initialized() else 1
+        self.rank = dist.get_rank(group) if dist.is_initialized() else 0
+        self.local = torch.empty(self.world, rows, N, dtype=torch.bfloat16, device="cuda")
+        self.flag = torch.zeros(1, device="cuda")
+        self._opened = []
+        ptr = self.local.data_ptr()
+        if self.world == 1:
+            self.ptrs = [ptr]
+            return
+        err, base, _size = drv.cuMemGetAddressRange(ptr)
+        if err != drv.CUresult.CUDA_SUCCESS:
+            raise RuntimeError(f"cuMemGetAddressRange: {err}")
+        offset = ptr - int(base)
+        err, handle = rt.cudaIpcGetMemHandle(int(base))
+        if err != rt.cudaError_t.cudaSuccess:
+            raise RuntimeError(f"cudaIpcGetMemHandle: {err}")
+        mine = (bytes(handle.reserved), offset)
+        everyone = [None] * self.world
+        dist.all_gather_object(everyone, mine, group=group)
+        self.ptrs = []
+        for s, (h, off) in enumerate(everyone):
+            if s == self.rank:
+                self.ptrs.append(ptr)
+                continue
+            hh = rt.cudaIpcMemHandle_t()
+            hh.reserved = h
+            err, peer = rt.cudaIpcOpenMemHandle(hh, rt.cudaIpcMemLazyEnablePeerAccess)
+            if err != rt.cudaError_t.cudaSuccess:
+                raise RuntimeError(f"cudaIpcOpenMemHandle (rank {s}): {err}")
+            self._opened.append(peer)
+            self.ptrs.append(int(peer) + off)
+
+    def close(self):
+        from cuda.bindings import runtime as rt
+        torch.cuda.synchronize()
+        for p in self._opened:
+            rt.cudaIpcCloseMemHandle(p)
+        self._opened = []
+
+
+def sharded_out_proj(x_local: torch.Tensor, W_local: torch.Tensor, buf: PeerBuffer, out=None) -> torch.Tensor:
+    """y[rows owned by this rank] = sum over ranks of x_r W_r^T, with x_local [M, K_r]
+    this rank's gated-normed head outputs and W_local [N, K_r] its columns of the
+    output projection.  One fused launch computes the partial product and writes
+    each tile into its owner's buffer over NVLink (gdn_outproj_rs_fwd); two
+    1-element all-reduces order it against the other ranks (the previous call's
+    reduction done before slots are overwritten; every rank's tiles landed
+    before this reduction)."""
+    from . import ops
+    import torch.distributed as dist
+    if buf.world > 1:
+        dist.all_reduce(buf.flag, group=buf.group)
+    ops.outproj_rs(x_local, W_local, buf.ptrs, buf.rank, buf.world)
+    if buf.world > 1:
+        dist.all_reduce(buf.flag, group=buf.group)
+    return ops.outproj_reduce(buf.local, out)

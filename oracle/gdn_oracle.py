@@ -295,6 +295,22 @@ def l2norm_heads(x_bits, head_dim, eps=1e-6):
     return f32_to_bf16((xh * inv).reshape(shp))
 
 
+def outproj_reduce_scatter(x_shards, W_shards):
+    """Head-sharded output projection with its reduce-scatter, restated: rank r
+    holds x_r [M, K_r] (its heads' gated-normed outputs, bf16) and W_r [N, K_r]
+    (its columns of W_o); its partial product is rounded to bf16, and the owner
+    of each block of rows adds the partials in rank order in fp32 and rounds
+    once.  Returns the full [M, N] bf16 result (row block d = rank d's rows).  Restatement-pinned: the reference has no multi-GPU code; the full
+    product sum_r x_r W_r^T is gdn_layer.py's output projection of the
+    concatenated heads."""
+    parts = [f32_to_bf16(np.matmul(bf16_to_f32(x), bf16_to_f32(W).T, dtype=np.float32))
+             for x, W in zip(x_shards, W_shards)]
+    acc = np.zeros(parts[0].shape, np.float32)
+    for p in parts:
+        acc += bf16_to_f32(p)
+    return f32_to_bf16(acc)
+
+
 # --------------------------------------------------------------------------
 # RMSNorm and gated RMSNorm
 # --------------------------------------------------------------------------

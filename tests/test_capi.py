@@ -209,3 +209,15 @@ def test_decode_step_ex_rejects_unknown_flags(lib):
     args = [FAKE, FAKE, FAKE, FAKE, FAKE, 0, FAKE, None, FAKE, FAKE, FAKE, 1, 1, 1, 128, 128, 0.0]
     assert _lib.call_status("gdn_decode_step_ex", *args, 4, None) == _lib.GDN_ERR_DTYPE
     assert "flags" in _lib.last_error()
+
+
+def test_outproj_rs_rejects(lib):
+    import ctypes
+    two = (ctypes.c_void_p * 2)(FAKE, FAKE)
+    assert _lib.call_status("gdn_outproj_rs_fwd", None, FAKE, two, 1024, 256, 128, 0, 2, None) == _lib.GDN_ERR_NULL
+    assert _lib.call_status("gdn_outproj_rs_fwd", FAKE, FAKE, two, 1000, 256, 128, 0, 2, None) == _lib.GDN_ERR_SHAPE
+    assert _lib.call_status("gdn_outproj_rs_fwd", FAKE, FAKE, two, 1024, 200, 128, 0, 2, None) == _lib.GDN_ERR_SHAPE
+    assert _lib.call_status("gdn_outproj_rs_fwd", FAKE, FAKE, two, 1024, 256, 128, 2, 2, None) == _lib.GDN_ERR_SHAPE
+    odd = (ctypes.c_void_p * 2)(FAKE, ODD)
+    assert _lib.call_status("gdn_outproj_rs_fwd", FAKE, FAKE, odd, 1024, 256, 128, 0, 2, None) == _lib.GDN_ERR_ALIGN
+    assert _lib.call_status("gdn_outproj_reduce", FAKE, FAKE, 16, 100, 2, None) == _lib.GDN_ERR_SHAPE
