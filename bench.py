@@ -472,6 +472,8 @@ def run_long(args, rank, world, dev, stream, hbm_peak, tf_peak, peak_kind):
     tokens = c["B"] * c["T"]
     alg = prefill_alg_bytes(c["B"], c["T"], Hs, c["dk"], c["dv"])
     flops = FLOP_PER_TOKEN_HEAD(c["dk"], c["dv"]) * c["B"] * c["T"] * Hs
+    del inp, gathered
+    tail = run_layer_tail(args, rank, world, dev, stream, tf_peak)
     if rank == 0:
         line = {
             "metric": "prefill tokens/s (config 4: B=8 T=32768 H=32, heads split over GPUs, o all-gathered)",
@@ -488,9 +490,57 @@ def run_long(args, rank, world, dev, stream, hbm_peak, tf_peak, peak_kind):
                          "tensor_tflops": flops / (ms_k * 1e-3) / 1e12,
                          "tensor_frac_of_measured": flops / (ms_k * 1e-3) / 1e12 / tf_peak},
             "clocks": clocks.summary(),
+            "layer_tail": tail,
         }
         print(json.dumps(line), flush=True)
     finish(world)
+
+
+def run_layer_tail(args, rank, world, dev, stream, tf_peak):
+    """Config 4's layer tail at the config-3 widths: the head-sharded outputs y_r
+    [B*T, 4096/world] (gated-normed o of this rank's heads, synthetic) times
+    W_o [2048, 4096], each rank keeping its B*T/world rows of the result.
+    (a) NCCL all-gather of the head shards, then each rank projects its rows
+    (cuBLAS through torch); (b) the fused projection + reduce-scatter
+    (gdn_outproj_rs_fwd: partial tiles stored into the owners' buffers over
+    NVLink during the GEMM, then gdn_outproj_reduce).  Both time the whole tail
+    (CUDA events, max over ranks)."""
+    import torch
+    from gdn_18646_b200.sharding import PeerBuffer, owned_rows, sharded_out_proj
+    c = C4
+    M, N, Ktot = c["B"] * c["T"], 2048, c["H"] * c["dv"]
+    Kr = Ktot // world
+    g = torch.Generator(device=dev).manual_seed(77 + rank)
+    y_loc = torch.randn(M, Kr, generator=g, device=dev).bfloat16()
+    gw = torch.Generator(device=dev).manual_seed(78)
+    W = (torch.randn(N, Ktot, generator=gw, device=dev) * Ktot ** -0.5).bfloat16()
+    W_loc = W[:, rank * Kr:(rank + 1) * Kr].contiguous()
+    rows = owned_rows(M, rank, world)
+    steps, warm = max(3, min(args.steps, 10)), 3
+    if world > 1:
+        import torch.distributed as dist
+        gath = torch.empty(world, M, Kr, dtype=torch.bfloat16, device=dev)
+
+        def gather_then_project():
+            dist.all_gather_into_tensor(gath, y_loc)
+            o_rows = gath[:, rows, :].permute(1, 0, 2).reshape(M // world, Ktot)
+            return o_rows @ W.T
+    else:
+        def gather_then_project():
+            return y_loc @ W.T
+    ms_a = timed(gather_then_project, steps, warm, world, stream) / steps
+    buf = PeerBuffer(M // world, N)
+    out = torch.empty(M // world, N, dtype=torch.bfloat16, device=dev)
+    ms_b = timed(lambda: sharded_out_proj(y_loc, W_loc, buf, out=out), steps, warm, world, stream) / steps
+    torch.cuda.synchronize()
+    buf.close()
+    flops_rank = 2.0 * M * N * Kr
+    nvlink_bytes = (world - 1) / world * M * N * 2 if world > 1 else 0
+    return {"config": f"y [{M}, {Ktot}] head-sharded x{world} times W_o [{N}, {Ktot}]; rank keeps {M // world} rows",
+            "gather_then_project_ms": ms_a, "fused_project_reduce_scatter_ms": ms_b,
+            "fused_tflops_per_gpu": flops_rank / (ms_b * 1e-3) / 1e12,
+            "fused_frac_of_measured_bf16": flops_rank / (ms_b * 1e-3) / 1e12 / tf_peak,
+            "nvlink_bytes_sent_per_gpu": nvlink_bytes}
 
 
 def finish(world):
