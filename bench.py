@@ -261,6 +261,7 @@ def run_ours(args):
     prj = run_proj(args, world, dev, stream, tf_peak)
     lay = run_layer(world, dev, stream, hbm_peak)
     vl = run_varlen(world, dev, stream)
+    bw = run_backward(world, dev, stream, hbm_peak)
     cpu = cpu_baseline_prefill() if (rank == 0 and world == 1 and not args.no_cpu_baseline) else None
 
     if rank == 0:
@@ -287,6 +288,7 @@ def run_ours(args):
             "proj": prj,
             "layer": lay,
             "varlen": vl,
+            "backward": bw,
             "cpu_baseline": cpu,
         }
         print(json.dumps(line), flush=True)
@@ -440,6 +442,32 @@ def run_varlen(world, dev, stream):
             "varlen_ms": ms_v, "varlen_tokens_per_s": Ttot / (ms_v * 1e-3),
             "padded_ms": ms_p, "padded_tokens_per_s": Ttot / (ms_p * 1e-3),
             "launches": 3}
+
+
+def run_backward(world, dev, stream, hbm_peak):
+    """Config 1's backward (gdn_prefill_bwd): B=4, T=4096, H=16, dk=dv=128, fp32 dO and
+    a final-state gradient.  Its kernels store and reload every token's state and
+    state gradient (fp32): the traffic per call is ~4 x B*H*T*dk*dv*4 bytes."""
+    import torch
+    from gdn_18646_b200 import ops
+    c = C1
+    inp = gen_prefill(c["B"], c["T"], c["H"], c["dk"], c["dv"], 99, dev)
+    g = torch.Generator(device=dev).manual_seed(98)
+    dO = torch.randn(c["B"], c["H"], c["T"], c["dv"], generator=g, device=dev)
+    dSf = torch.randn(c["B"], c["H"], c["dk"], c["dv"], generator=g, device=dev) * 0.1
+
+    def step():
+        ops.prefill_backward(inp["q"], inp["k"], inp["v"], inp["A_log"], inp["a"], inp["b"], dO,
+                             state_in=inp["state_in"], dS_final=dSf, scale=c["dk"] ** -0.5)
+
+    ms = timed(step, 3, 1, world, stream) / 3
+    toks = c["B"] * c["T"]
+    state_bytes = c["B"] * c["H"] * c["T"] * c["dk"] * c["dv"] * 4
+    traffic = 4 * state_bytes                        # states and state gradients, written once and read once
+    return {"config": "config1 backward: B=4 T=4096 H=16 dk=dv=128, fp32 dO + final-state gradient",
+            "ms": ms, "tokens_per_s": toks / (ms * 1e-3), "workspace_gb": 2 * state_bytes / 1e9,
+            "state_traffic_gbs": traffic / (ms * 1e-3) / 1e9,
+            "state_traffic_frac_of_measured_hbm": traffic / (ms * 1e-3) / 1e9 / hbm_peak}
 
 
 def run_long(args, rank, world, dev, stream, hbm_peak, tf_peak, peak_kind):

@@ -57,6 +57,9 @@ SIGNATURES = {
     "gdn_prefill_varlen_fwd_ws": [_P, _P, _P, _P, _P, _P, _I, _F, _P, _P, _I, _I, _I, _P, _P, _P,
                                   _I, _I, _I, _I, _F, _P, _Z, _P],
     "gdn_prefill_varlen_workspace_bytes": [_I, _I, _I, _I, _I],
+    "gdn_prefill_bwd": [_P, _P, _P, _P, _P, _P, _I, _F, _P, _P, _P, _P, _I, _P,
+                        _P, _P, _P, _P, _P, _P, _P, _P, _I, _I, _I, _I, _I, _F, _P, _Z, _P],
+    "gdn_prefill_bwd_workspace_bytes": [_I, _I, _I, _I, _I],
     "gdn_prefill_set_schedule": [_I],
     "gdn_prefill_launch_count": [_I, _I, _I, _I, _I],
     "gdn_decode_step": [_P, _P, _P, _P, _P, _I, _P, _P, _P, _P, _P, _I, _I, _I, _I, _I, _F, _P],
@@ -73,7 +76,7 @@ SIGNATURES = {
     "gdn_version": [],
 }
 _STR_FUNCS = {"gdn_last_error", "gdn_version"}
-_SIZE_FUNCS = {"gdn_prefill_workspace_bytes", "gdn_prefill_varlen_workspace_bytes"}
+_SIZE_FUNCS = {"gdn_prefill_workspace_bytes", "gdn_prefill_varlen_workspace_bytes", "gdn_prefill_bwd_workspace_bytes"}
 
 _lock = threading.Lock()
 _lib = None

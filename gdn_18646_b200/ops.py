@@ -156,6 +156,42 @@ def prefill_varlen(q, k, v, A_log, a, b_logits, cu_seqlens, *, max_len=None, dt_
     return out, state_out
 
 
+def prefill_backward(q, k, v, A_log, a, b_logits, dO, *, dt_bias=0.0, mask=None, state_in=None, dS_final=None,
+                     scale=0.0, need_dstate=True):
+    """Gradients of ``prefill`` (gdn_prefill_bwd): q, k [B,H,T,dk], v [B,H,T,dv] bf16
+    (layout "bhtd", Hqk == Hv), gates as ``prefill``, dO [B,H,T,dv] (bf16 or f32),
+    dS_final [B,H,dk,dv] or None.  Returns a dict of fp32 tensors dq, dk, dv, da, db,
+    dA_log [H], ddt_bias ([H] for a per-head dt_bias, a scalar tensor otherwise) and
+    dstate_in (or None)."""
+    for name, t in (("q", q), ("k", k), ("v", v)):
+        _cuda_contig(t, name, torch.bfloat16)
+    B, H, T, dk = q.shape
+    dv = v.shape[-1]
+    gdt = _gate_dtype(a, "a")
+    _need(b_logits.dtype == a.dtype, "a and b_logits must share a dtype")
+    _cuda_contig(a, "a")
+    _cuda_contig(b_logits, "b_logits")
+    _need(dO.dtype in (torch.bfloat16, torch.float32), "dO must be bf16 or f32")
+    _cuda_contig(dO, "dO")
+    dod = GDN_DTYPE_BF16 if dO.dtype == torch.bfloat16 else GDN_DTYPE_F32
+    dt_vec = dt_bias if isinstance(dt_bias, torch.Tensor) and dt_bias.numel() > 1 else None
+    dt_scalar = 0.0 if dt_vec is not None else float(dt_bias)
+    f32 = dict(dtype=torch.float32, device=q.device)
+    g = dict(dq=torch.empty(B, H, T, dk, **f32), dk=torch.empty(B, H, T, dk, **f32), dv=torch.empty(B, H, T, dv, **f32),
+             da=torch.empty(B, H, T, **f32), db=torch.empty(B, H, T, **f32), dA_log=torch.empty(H, **f32),
+             ddt_bias=torch.empty(H, **f32),
+             dstate_in=torch.empty(B, H, dk, dv, **f32) if need_dstate else None)
+    ws_bytes = _lib.lib().gdn_prefill_bwd_workspace_bytes(B, T, H, dk, dv)
+    ws = torch.empty(max(int(ws_bytes), 1), dtype=torch.uint8, device=q.device)
+    _lib.call("gdn_prefill_bwd", _ptr(q), _ptr(k), _ptr(v), _ptr(A_log), _ptr(a), _ptr(b_logits), gdt, dt_scalar,
+              _ptr(dt_vec), _ptr(mask), _ptr(state_in), _ptr(dO), dod, _ptr(dS_final), _ptr(g["dq"]), _ptr(g["dk"]),
+              _ptr(g["dv"]), _ptr(g["da"]), _ptr(g["db"]), _ptr(g["dA_log"]), _ptr(g["ddt_bias"]),
+              _ptr(g["dstate_in"]), B, T, H, dk, dv, float(scale), _ptr(ws), int(ws_bytes), _stream())
+    if dt_vec is None:
+        g["ddt_bias"] = g["ddt_bias"].sum()
+    return g
+
+
 def decode_step(q, k, v, a, b, A_log, dt_bias, state, *, scale=0.0, out=None, state_out=None, l2norm_qk=False):
     """One decode step; updates ``state`` in place unless ``state_out`` is given.
     q,k [B,Hqk,dk] bf16; v [B,Hv,dv] bf16; a,b [B,Hv]; state [B,Hv,dk,dv] f32.

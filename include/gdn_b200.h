@@ -191,6 +191,33 @@ int gdn_prefill_varlen_fwd(const void* q, const void* k, const void* v,
                            int Hqk, int Hv, int dk, int dv, float scale, void* stream);
 
 /*
+ * Gradients of the prefill (training): dq, dk, dv, da, db, dA_log, ddt_bias and
+ * the initial state, given dO (and optionally the gradient of the final state).
+ * No reference counterpart (the reference has no backward).  Token-recurrent
+ * derivative of the same recurrence (per token S' = g S, r = S'^T k,
+ * d = b'(v - r), S <- S' + k d^T, o = m scale q^T S), fp32 on CUDA cores, over
+ * a workspace holding every token's state and state gradient.
+ *   q, k bf16 [B, H, T, dk]; v bf16 [B, H, T, dv]   (layout BHTD, Hqk == Hv)
+ *   A_log f32 [H]; a, b_logits [B, H, T] in gate_dtype; dt_bias / dt_bias_vec as
+ *   gdn_prefill_fwd; mask f32 [B, T] or NULL; state_in f32 [B, H, dk, dv] or NULL
+ *   dO [B, H, T, dv] in do_dtype (bf16 or f32); dS_final f32 [B, H, dk, dv] or NULL
+ *   dq, dk f32 [B, H, T, dk]; dv f32 [B, H, T, dv]; da, db f32 [B, H, T]
+ *   dA_log, ddt_bias f32 [H] (per head; for a scalar dt_bias sum them);
+ *   dstate_in f32 [B, H, dk, dv] or NULL.
+ * dk, dv in {64, 128}.  Workspace: gdn_prefill_bwd_workspace_bytes(B, T, H, dk, dv)
+ * (about 2 * B * H * T * dk * dv * 4 bytes), 16-byte aligned.
+ */
+size_t gdn_prefill_bwd_workspace_bytes(int B, int T, int H, int dk, int dv);
+int gdn_prefill_bwd(const void* q, const void* k, const void* v, const float* A_log,
+                    const void* a, const void* b_logits, int gate_dtype, float dt_bias,
+                    const float* dt_bias_vec, const float* mask, const float* state_in,
+                    const void* dO, int do_dtype, const float* dS_final,
+                    float* dq, float* dk, float* dv, float* da, float* db,
+                    float* dA_log, float* ddt_bias, float* dstate_in,
+                    int B, int T, int H, int dk_dim, int dv_dim, float scale,
+                    void* workspace, size_t workspace_bytes, void* stream);
+
+/*
  * Single-token decode step, state updated in place if state_out == state_in.
  * Replaces gdn_decode_cuda(), kernels/decode.cu:131-162, and its torch wrapper
  * gdn_decode_forward(), kernels/decode.cu:172-214 (math: reference/decode_ref.py:11-61).

@@ -214,6 +214,77 @@ def prefill_recurrent(q, k, v, A_log, a, dt_bias, b_logits, mask, state_in=None,
     return o, S
 
 
+def prefill_backward(q, k, v, A_log, a, dt_bias, b_logits, mask, dO, state_in=None, dS_final=None,
+                     scale=0.0, dt=np.float64):
+    """Reverse-mode derivative of prefill_recurrent (the gated delta rule of
+    reference/prefill_ref.py:18-23 / decode_ref.py:46-56, token by token),
+    written out by hand.  The reference has no backward; this restatement is
+    pinned against finite differences of prefill_recurrent (tests).
+
+    Per token, with g = gate, b' = beta * mask, S_p the state before the token:
+      S' = g S_p,  r = S'^T k,  d = b' (v - r),  S_n = S' + k d^T,  o = m scale q^T S_n
+    and in reverse, with dS the gradient of S_n:
+      dS += scale q (m dO)^T;  dq = scale S_n (m dO)
+      dd = dS^T k;  dk = dS d + S' dr;  dv = b' dd;  db' = dd.(v - r);  dr = -b' dd
+      dS' = dS + k dr^T;  dg = <S_p, dS'>;  dS_p = g dS'
+    then the gate chain rule (g = exp(-exp(A_log) softplus(a + dt_bias)),
+    b' = sigmoid(b) m).  dO [B,H,T,V]; dS_final [B,H,K,V] or None.
+    Returns dict(dq, dk, dv, da, db, dA_log [H], ddt_bias [H], dstate_in)."""
+    q = _as_f32(q, dt)
+    k = _as_f32(k, dt)
+    v = _as_f32(v, dt)
+    dO = np.asarray(dO, dtype=dt)
+    B, H, T, K = q.shape
+    V = v.shape[-1]
+    if scale == 0.0:
+        scale = 1.0 / math.sqrt(K)
+    g, beta = gates(a, A_log, dt_bias, b_logits, dt)
+    m = np.asarray(mask, dtype=dt)[:, None, :]                          # [B,1,T]
+    bm = beta * m
+    S = (np.zeros((B, H, K, V), dtype=dt) if state_in is None
+         else np.array(state_in, dtype=dt, copy=True))
+    S_prev = np.empty((T, B, H, K, V), dtype=dt)
+    for t in range(T):                                                  # forward, keeping S_p
+        S_prev[t] = S
+        Sp = S * g[:, :, t, None, None]
+        r = np.einsum("bhk,bhkv->bhv", k[:, :, t], Sp)
+        d = bm[:, :, t, None] * (v[:, :, t] - r)
+        S = Sp + np.einsum("bhk,bhv->bhkv", k[:, :, t], d)
+    dS = np.zeros((B, H, K, V), dtype=dt) if dS_final is None else np.array(dS_final, dtype=dt, copy=True)
+    dq, dk, dv = np.zeros_like(q), np.zeros_like(k), np.zeros_like(v)
+    dg, dbm = np.zeros((B, H, T), dt), np.zeros((B, H, T), dt)
+    for t in range(T - 1, -1, -1):
+        kt, qt, vt = k[:, :, t], q[:, :, t], v[:, :, t]
+        Sp = S_prev[t] * g[:, :, t, None, None]
+        r = np.einsum("bhk,bhkv->bhv", kt, Sp)
+        d = bm[:, :, t, None] * (vt - r)
+        Sn = Sp + np.einsum("bhk,bhv->bhkv", kt, d)
+        dOt = dO[:, :, t] * m[:, :, t, None]
+        dS = dS + scale * np.einsum("bhk,bhv->bhkv", qt, dOt)
+        dq[:, :, t] = scale * np.einsum("bhkv,bhv->bhk", Sn, dOt)
+        dd = np.einsum("bhkv,bhk->bhv", dS, kt)
+        dr = -bm[:, :, t, None] * dd
+        dk[:, :, t] = np.einsum("bhkv,bhv->bhk", dS, d) + np.einsum("bhkv,bhv->bhk", Sp, dr)
+        dv[:, :, t] = bm[:, :, t, None] * dd
+        dbm[:, :, t] = np.einsum("bhv,bhv->bh", dd, vt - r)
+        dSp = dS + np.einsum("bhk,bhv->bhkv", kt, dr)
+        dg[:, :, t] = np.einsum("bhkv,bhkv->bh", S_prev[t], dSp)
+        dS = g[:, :, t, None, None] * dSp
+    # gate chain rule
+    af = _as_f32(a, dt)
+    bf = _as_f32(b_logits, dt)
+    A = np.asarray(A_log, dtype=dt).reshape(1, H, 1)
+    dtb = np.asarray(dt_bias, dtype=dt)
+    x = af + (dtb.reshape(1, H, 1) if dtb.ndim == 1 and dtb.shape[0] == H and H > 1 else dtb)
+    sig_x = 1.0 / (1.0 + np.exp(-x))
+    dlogg = dg * g
+    da = dlogg * (-np.exp(A)) * np.where(x > 20.0, 1.0, sig_x)
+    sb = 1.0 / (1.0 + np.exp(-bf))
+    db = dbm * m * sb * (1.0 - sb)
+    return dict(dq=dq, dk=dk, dv=dv, da=da, db=db, dA_log=(dlogg * np.log(g)).sum(axis=(0, 2)),
+                ddt_bias=da.sum(axis=(0, 2)), dstate_in=dS)
+
+
 # --------------------------------------------------------------------------
 # Decode
 # --------------------------------------------------------------------------

@@ -221,3 +221,20 @@ def test_outproj_rs_rejects(lib):
     odd = (ctypes.c_void_p * 2)(FAKE, ODD)
     assert _lib.call_status("gdn_outproj_rs_fwd", FAKE, FAKE, odd, 1024, 256, 128, 0, 2, None) == _lib.GDN_ERR_ALIGN
     assert _lib.call_status("gdn_outproj_reduce", FAKE, FAKE, 16, 100, 2, None) == _lib.GDN_ERR_SHAPE
+
+
+def test_prefill_bwd_rejects(lib):
+    base = [FAKE] * 6 + [0, 0.0, None, None, None, FAKE, 0, None] + [FAKE] * 7 + [None]
+    def call(B=1, T=64, H=2, dk=64, dv=64, ws=FAKE, wsb=1 << 40, **over):
+        args = list(base)
+        for i, v in over.items():
+            args[int(i[1:])] = v
+        return _lib.call_status("gdn_prefill_bwd", *args, B, T, H, dk, dv, 0.0, ws, wsb, None)
+    assert call(a0=None) == _lib.GDN_ERR_NULL
+    assert call(T=0) == _lib.GDN_ERR_SHAPE
+    assert call(dk=256) == _lib.GDN_ERR_UNSUPPORTED
+    assert call(a6=7) == _lib.GDN_ERR_DTYPE
+    assert call(a12=5) == _lib.GDN_ERR_DTYPE
+    assert call(wsb=16) == _lib.GDN_ERR_SHAPE
+    assert call(ws=ODD) == _lib.GDN_ERR_ALIGN
+    assert lib.gdn_prefill_bwd_workspace_bytes(1, 64, 2, 96, 64) == 0
