@@ -192,6 +192,36 @@ def prefill_backward(q, k, v, A_log, a, b_logits, dO, *, dt_bias=0.0, mask=None,
     return g
 
 
+class PrefillFunction(torch.autograd.Function):
+    """``prefill`` as an autograd op (layout "bhtd", Hqk == Hv): forward is the
+    chunked tcgen05 prefill, backward gdn_prefill_backward.  Differentiable
+    inputs: q, k, v, A_log, a, b_logits, dt_bias (tensor) and state_in;
+    outputs (o, state_out)."""
+
+    @staticmethod
+    def forward(ctx, q, k, v, A_log, a, b_logits, dt_bias, state_in, scale):
+        o, S = prefill(q, k, v, A_log, a, b_logits, dt_bias=dt_bias, state_in=state_in, scale=scale)
+        ctx.save_for_backward(q, k, v, A_log, a, b_logits, dt_bias, state_in)
+        ctx.scale = scale
+        return o, S
+
+    @staticmethod
+    def backward(ctx, do, dS):
+        q, k, v, A_log, a, b_logits, dt_bias, state_in = ctx.saved_tensors
+        if do is None:
+            do = torch.zeros_like(v, dtype=torch.float32)
+        g = prefill_backward(q, k, v, A_log, a, b_logits, do.contiguous(), dt_bias=dt_bias, state_in=state_in,
+                             dS_final=None if dS is None else dS.contiguous(), scale=ctx.scale)
+        ddt = g["ddt_bias"].reshape(dt_bias.shape).to(dt_bias.dtype)
+        return (g["dq"].to(q.dtype), g["dk"].to(k.dtype), g["dv"].to(v.dtype), g["dA_log"], g["da"].to(a.dtype),
+                g["db"].to(b_logits.dtype), ddt, g["dstate_in"], None)
+
+
+def prefill_autograd(q, k, v, A_log, a, b_logits, dt_bias, state_in, scale=0.0):
+    """Differentiable ``prefill`` (see PrefillFunction); dt_bias a tensor ([H] or [1])."""
+    return PrefillFunction.apply(q, k, v, A_log, a, b_logits, dt_bias, state_in, scale)
+
+
 def decode_step(q, k, v, a, b, A_log, dt_bias, state, *, scale=0.0, out=None, state_out=None, l2norm_qk=False):
     """One decode step; updates ``state`` in place unless ``state_out`` is given.
     q,k [B,Hqk,dk] bf16; v [B,Hv,dv] bf16; a,b [B,Hv]; state [B,Hv,dk,dv] f32.

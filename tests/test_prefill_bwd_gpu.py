@@ -62,3 +62,28 @@ def test_prefill_bwd_scalar_dt_bias_and_no_state(cuda_device):
     assert _rel(float(got["ddt_bias"]), np.array(ref["ddt_bias"].sum())) < 1e-3
     for name in ("dq", "dk", "dv", "da", "db", "dstate_in"):
         assert _rel(to_np(got[name]).astype(np.float64), ref[name]) < 1e-3, name
+
+
+def test_prefill_autograd_function(cuda_device):
+    """PrefillFunction: torch autograd through the forward kernel and the backward
+    kernels gives prefill_backward's gradients (cast to the inputs' dtypes)."""
+    import torch
+    from gdn_18646_b200 import ops
+    B, H, T, dk, dv = 1, 2, 96, 64, 64
+    inp = O.make_prefill_inputs(21, B, T, H, dk, dv, gate_dtype="f32", state_std=0.05)
+    t = {n: to_dev(inp[n]) for n in ("q", "k", "v", "A_log", "a", "b", "state_in")}
+    dtb = torch.tensor([0.1, -0.2], device="cuda")
+    leaves = {n: x.clone().requires_grad_(True) for n, x in t.items()}
+    dtb_l = dtb.clone().requires_grad_(True)
+    o, S = ops.prefill_autograd(leaves["q"], leaves["k"], leaves["v"], leaves["A_log"], leaves["a"], leaves["b"],
+                                dtb_l, leaves["state_in"], inp["scale"])
+    rng = np.random.default_rng(5)
+    dO = to_dev(rng.standard_normal((B, H, T, dv)).astype(np.float32))
+    (o.float() * dO).sum().backward()
+    # o is bf16, so the gradient reaching the backward is dO rounded to bf16
+    g = ops.prefill_backward(t["q"], t["k"], t["v"], t["A_log"], t["a"], t["b"], dO.bfloat16(), dt_bias=dtb,
+                             state_in=t["state_in"], scale=inp["scale"])
+    torch.cuda.synchronize()
+    assert torch.allclose(leaves["v"].grad.float(), g["dv"].bfloat16().float())
+    assert torch.allclose(leaves["a"].grad, g["da"]) and torch.allclose(leaves["state_in"].grad, g["dstate_in"])
+    assert torch.allclose(dtb_l.grad, g["ddt_bias"]) and torch.allclose(leaves["A_log"].grad, g["dA_log"])
