@@ -237,21 +237,19 @@ def run_ours(args):
     achieved_gbs = alg_bytes / (ms_step * 1e-3) / 1e9
     achieved_tf = flops / (ms_step * 1e-3) / 1e12
 
-    # end-to-end through the public API with host buffers (pinned), copies inside the timed region
+    # end-to-end through the public host-buffer entry point (gdn_prefill_host): pinned
+    # host inputs copied in and results copied out inside the timed region, in
+    # token segments that overlap the prefill of the neighbouring segments
     host_in = {k_: v_.cpu().pin_memory() for k_, v_ in inp.items() if v_ is not None}
-    dev_in = {k_: torch.empty_like(v_) for k_, v_ in inp.items() if v_ is not None}
     host_o = torch.empty(out.shape, dtype=out.dtype, pin_memory=True)
     host_s = torch.empty(s_out.shape, dtype=s_out.dtype, pin_memory=True)
     h2d = sum(t.numel() * t.element_size() for t in host_in.values())
     d2h = host_o.numel() * 2 + host_s.numel() * 4
 
     def e2e_step():
-        for k_, t in host_in.items():
-            dev_in[k_].copy_(t, non_blocking=True)
-        ops.prefill(dev_in["q"], dev_in["k"], dev_in["v"], dev_in["A_log"], dev_in["a"], dev_in["b"],
-                    state_in=dev_in["state_in"], scale=scale, out=out, state_out=s_out)
-        host_o.copy_(out, non_blocking=True)
-        host_s.copy_(s_out, non_blocking=True)
+        ops.prefill_host(host_in["q"], host_in["k"], host_in["v"], host_in["A_log"], host_in["a"], host_in["b"],
+                         state_in=host_in["state_in"], scale=scale, out=host_o, state_out=host_s,
+                         synchronize=False)
 
     e2e_steps = max(3, min(args.steps, 20))
     ms_e2e = timed(e2e_step, e2e_steps, max(1, min(args.warmup, 3)), world, stream) / e2e_steps
@@ -275,7 +273,9 @@ def run_ours(args):
                        "seq_len": c["T"], "parallelism": f"batch-sharded x{world} (no collective)",
                        "l2": "inputs larger than L2 (279 MB per step), no flush"},
             "e2e": {"value": e2e_value, "unit": "tokens/s", "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h,
-                    "ms_per_step": ms_e2e},
+                    "ms_per_step": ms_e2e, "api": "gdn_prefill_host (segmented, copies overlapped)",
+                    "segment_tokens": G._lib.lib().gdn_prefill_host_segment(c["B"], c["T"], c["H"], c["H"], c["dk"],
+                                                                            c["dv"], 1, 0)},
             "gpu_launches": args.steps * G._lib.lib().gdn_prefill_launch_count(c["B"], c["T"], c["H"], c["dk"], c["dv"]),
             "roofline": {"bound": "hbm", "achieved": achieved_gbs, "peak": hbm_peak, "unit": "GB/s",
                          "frac": achieved_gbs / hbm_peak, "traffic": PREFILL_TRAFFIC_PER_STEP,
@@ -685,6 +685,15 @@ def run_only(args):
 
         def step():
             ops.decode_step(q, k, v, a, b, A_log, dtb, S, out=o)
+    elif args.only == "backward":
+        # config 1's head shape at B=1, T=1024: a 2.1 GB workspace, small enough to capture
+        inp = gen_prefill(1, 1024, C1["H"], C1["dk"], C1["dv"], 99, dev)
+        g = torch.Generator(device=dev).manual_seed(98)
+        dO = torch.randn(1, C1["H"], 1024, C1["dv"], generator=g, device=dev)
+
+        def step():
+            ops.prefill_backward(inp["q"], inp["k"], inp["v"], inp["A_log"], inp["a"], inp["b"], dO,
+                                 state_in=inp["state_in"], scale=C1["dk"] ** -0.5)
     else:
         # config 3 fused q|k|v projection: x [2, 8192, 2048] -> 8192 conv channels
         g = torch.Generator(device=dev).manual_seed(6)
@@ -708,7 +717,7 @@ def main(argv=None):
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--workload", choices=["prefill", "long"], default="prefill")
     ap.add_argument("--no-cpu-baseline", action="store_true")
-    ap.add_argument("--only", choices=["prefill", "decode", "proj", "layer_decode"], default=None,
+    ap.add_argument("--only", choices=["prefill", "decode", "proj", "layer_decode", "backward"], default=None,
                     help="run just one kernel's workload (for profiling); prints a short JSON line")
     args = ap.parse_args(argv)
     if args.only:

@@ -57,6 +57,11 @@ SIGNATURES = {
     "gdn_prefill_varlen_fwd_ws": [_P, _P, _P, _P, _P, _P, _I, _F, _P, _P, _I, _I, _I, _P, _P, _P,
                                   _I, _I, _I, _I, _F, _P, _Z, _P],
     "gdn_prefill_varlen_workspace_bytes": [_I, _I, _I, _I, _I],
+    "gdn_prefill_host": [_P, _P, _P, _P, _P, _P, _I, _F, _P, _P, _P, _P, _P,
+                         _I, _I, _I, _I, _I, _I, _I, _F, _I, _P, _Z, _P],
+    "gdn_prefill_host_workspace_bytes": [_I, _I, _I, _I, _I, _I, _I, _I],
+    "gdn_prefill_host_segment": [_I, _I, _I, _I, _I, _I, _I, _I],
+    "gdn_prefill_host_plan": [_I, _I, _I, _I, _I, _I, _I, _I, ctypes.POINTER(ctypes.c_int), _I],
     "gdn_prefill_bwd": [_P, _P, _P, _P, _P, _P, _I, _F, _P, _P, _P, _P, _I, _P,
                         _P, _P, _P, _P, _P, _P, _P, _P, _I, _I, _I, _I, _I, _F, _P, _Z, _P],
     "gdn_prefill_bwd_workspace_bytes": [_I, _I, _I, _I, _I],
@@ -76,7 +81,8 @@ SIGNATURES = {
     "gdn_version": [],
 }
 _STR_FUNCS = {"gdn_last_error", "gdn_version"}
-_SIZE_FUNCS = {"gdn_prefill_workspace_bytes", "gdn_prefill_varlen_workspace_bytes", "gdn_prefill_bwd_workspace_bytes"}
+_SIZE_FUNCS = {"gdn_prefill_workspace_bytes", "gdn_prefill_varlen_workspace_bytes", "gdn_prefill_bwd_workspace_bytes",
+               "gdn_prefill_host_workspace_bytes"}
 
 _lock = threading.Lock()
 _lib = None

@@ -82,43 +82,56 @@ struct RecLayout {
     static constexpr int ROWS = 64;                // rows per thread
 };
 
+// Tokens a recurrence stages in shared memory at once (one global round trip
+// per block instead of one per token).
+constexpr int kTB = 32;
+
 // Forward recurrence, storing S_p (the state before each token).  Grid (B*H, DV/COLS), one warp.
 template <int DK, int DV>
 __global__ void __launch_bounds__(32) bwd_states_kernel(const BwdArgs a) {
     using L = RecLayout<DK>;
     const int bh = blockIdx.x, lane = threadIdx.x;
-    const int j = blockIdx.y * L::COLS + lane % L::COLS;
+    const int jl = lane % L::COLS;
+    const int j = blockIdx.y * L::COLS + jl;
     const int i0 = (lane / L::COLS) * L::ROWS;      // first row of this thread
-    __shared__ float ks[DK];
+    __shared__ float ks[kTB][DK];
+    __shared__ float vs[kTB][L::COLS];
+    __shared__ float gs[kTB], bs[kTB];
     float S[L::ROWS];
     const long s0 = static_cast<long>(bh) * DK * DV;
 #pragma unroll
     for (int i = 0; i < L::ROWS; ++i)
         S[i] = a.state_in ? a.state_in[s0 + static_cast<long>(i0 + i) * DV + j] : 0.f;
-    for (int t = 0; t < a.T; ++t) {
-        const long tok = static_cast<long>(bh) * a.T + t;
-        float* out = a.states + (tok * DK + i0) * DV + j;
-#pragma unroll
-        for (int i = 0; i < L::ROWS; ++i) out[static_cast<long>(i) * DV] = S[i];
+    for (int tb = 0; tb < a.T; tb += kTB) {
+        const int nt = min(kTB, a.T - tb);
+        const long tok0 = static_cast<long>(bh) * a.T + tb;
         __syncwarp();
-        for (int i = lane; i < DK; i += 32) ks[i] = bf16_at(a.k, tok * DK + i);
+        for (int e = lane; e < nt * DK; e += 32) ks[e / DK][e % DK] = bf16_at(a.k, tok0 * DK + e);
+        for (int e = lane; e < nt * L::COLS; e += 32)
+            vs[e / L::COLS][e % L::COLS] = bf16_at(a.v, (tok0 + e / L::COLS) * DV + blockIdx.y * L::COLS + e % L::COLS);
+        if (lane < nt) gate_of(a, bh, tb + lane, gs[lane], bs[lane]);
         __syncwarp();
-        float g, bm;
-        gate_of(a, bh, t, g, bm);
-        float r0 = 0.f, r1 = 0.f, r2 = 0.f, r3 = 0.f;
+        for (int u = 0; u < nt; ++u) {
+            const long tok = tok0 + u;
+            float* out = a.states + (tok * DK + i0) * DV + j;
 #pragma unroll
-        for (int i = 0; i < L::ROWS; i += 4) {
-            r0 = fmaf(ks[i0 + i], S[i], r0);
-            r1 = fmaf(ks[i0 + i + 1], S[i + 1], r1);
-            r2 = fmaf(ks[i0 + i + 2], S[i + 2], r2);
-            r3 = fmaf(ks[i0 + i + 3], S[i + 3], r3);
+            for (int i = 0; i < L::ROWS; ++i) out[static_cast<long>(i) * DV] = S[i];
+            const float* kk = ks[u] + i0;
+            const float g = gs[u], bm = bs[u];
+            float r0 = 0.f, r1 = 0.f, r2 = 0.f, r3 = 0.f;
+#pragma unroll
+            for (int i = 0; i < L::ROWS; i += 4) {
+                r0 = fmaf(kk[i], S[i], r0);
+                r1 = fmaf(kk[i + 1], S[i + 1], r1);
+                r2 = fmaf(kk[i + 2], S[i + 2], r2);
+                r3 = fmaf(kk[i + 3], S[i + 3], r3);
+            }
+            float rp = (r0 + r1) + (r2 + r3);
+            if (L::PARTS == 2) rp += __shfl_xor_sync(0xffffffffu, rp, 16);
+            const float d = bm * (vs[u][jl] - g * rp);
+#pragma unroll
+            for (int i = 0; i < L::ROWS; ++i) S[i] = fmaf(kk[i], d, g * S[i]);
         }
-        float rp = (r0 + r1) + (r2 + r3);
-        if (L::PARTS == 2) rp += __shfl_xor_sync(0xffffffffu, rp, 16);
-        const float r = g * rp;
-        const float d = bm * (bf16_at(a.v, tok * DV + j) - r);
-#pragma unroll
-        for (int i = 0; i < L::ROWS; ++i) S[i] = fmaf(ks[i0 + i], d, g * S[i]);
     }
 }
 
@@ -127,54 +140,67 @@ template <int DK, int DV>
 __global__ void __launch_bounds__(32) bwd_dstate_kernel(const BwdArgs a) {
     using L = RecLayout<DK>;
     const int bh = blockIdx.x, lane = threadIdx.x;
-    const int j = blockIdx.y * L::COLS + lane % L::COLS;
+    const int jl = lane % L::COLS;
+    const int j = blockIdx.y * L::COLS + jl;
     const int i0 = (lane / L::COLS) * L::ROWS;
     const int bi = bh / a.H;
-    __shared__ float ks[DK], qs[DK];
+    __shared__ float ks[kTB][DK], qs[kTB][DK];
+    __shared__ float dos[kTB][L::COLS];
+    __shared__ float gs[kTB], bs[kTB];
     float dS[L::ROWS];
     const long s0 = static_cast<long>(bh) * DK * DV;
 #pragma unroll
     for (int i = 0; i < L::ROWS; ++i)
         dS[i] = a.dS_final ? a.dS_final[s0 + static_cast<long>(i0 + i) * DV + j] : 0.f;
-    for (int t = a.T - 1; t >= 0; --t) {
-        const long tok = static_cast<long>(bh) * a.T + t;
+    for (int tend = a.T; tend > 0; tend -= kTB) {
+        const int tb = max(0, tend - kTB), nt = tend - tb;
+        const long tok0 = static_cast<long>(bh) * a.T + tb;
         __syncwarp();
-        for (int i = lane; i < DK; i += 32) {
-            ks[i] = bf16_at(a.k, tok * DK + i);
-            qs[i] = bf16_at(a.q, tok * DK + i);
+        for (int e = lane; e < nt * DK; e += 32) {
+            ks[e / DK][e % DK] = bf16_at(a.k, tok0 * DK + e);
+            qs[e / DK][e % DK] = bf16_at(a.q, tok0 * DK + e);
         }
+        for (int e = lane; e < nt * L::COLS; e += 32) {
+            const int u = e / L::COLS;
+            const long idx = (tok0 + u) * DV + blockIdx.y * L::COLS + e % L::COLS;
+            const float m = a.mask ? a.mask[static_cast<long>(bi) * a.T + tb + u] : 1.f;
+            dos[u][e % L::COLS] =
+                a.scale * m * (a.do_dtype == GDN_DTYPE_BF16 ? bf16_at(static_cast<const uint16_t*>(a.dO), idx)
+                                                             : static_cast<const float*>(a.dO)[idx]);
+        }
+        if (lane < nt) gate_of(a, bh, tb + lane, gs[lane], bs[lane]);
         __syncwarp();
-        float g, bm;
-        gate_of(a, bh, t, g, bm);
-        const float m = a.mask ? a.mask[static_cast<long>(bi) * a.T + t] : 1.f;
-        const float dOj = m * (a.do_dtype == GDN_DTYPE_BF16
-                                   ? bf16_at(static_cast<const uint16_t*>(a.dO), tok * DV + j)
-                                   : static_cast<const float*>(a.dO)[tok * DV + j]);
-        const float sdo = a.scale * dOj;
-        float e0 = 0.f, e1 = 0.f, e2 = 0.f, e3 = 0.f;
+        for (int u = nt - 1; u >= 0; --u) {
+            const long tok = tok0 + u;
+            const float* kk = ks[u] + i0;
+            const float* qq = qs[u] + i0;
+            const float sdo = dos[u][jl];
+            const float g = gs[u], bm = bs[u];
+            float e0 = 0.f, e1 = 0.f, e2 = 0.f, e3 = 0.f;
 #pragma unroll
-        for (int i = 0; i < L::ROWS; i += 4) {
-            dS[i] = fmaf(qs[i0 + i], sdo, dS[i]);
-            dS[i + 1] = fmaf(qs[i0 + i + 1], sdo, dS[i + 1]);
-            dS[i + 2] = fmaf(qs[i0 + i + 2], sdo, dS[i + 2]);
-            dS[i + 3] = fmaf(qs[i0 + i + 3], sdo, dS[i + 3]);
-            e0 = fmaf(ks[i0 + i], dS[i], e0);
-            e1 = fmaf(ks[i0 + i + 1], dS[i + 1], e1);
-            e2 = fmaf(ks[i0 + i + 2], dS[i + 2], e2);
-            e3 = fmaf(ks[i0 + i + 3], dS[i + 3], e3);
+            for (int i = 0; i < L::ROWS; i += 4) {
+                dS[i] = fmaf(qq[i], sdo, dS[i]);
+                dS[i + 1] = fmaf(qq[i + 1], sdo, dS[i + 1]);
+                dS[i + 2] = fmaf(qq[i + 2], sdo, dS[i + 2]);
+                dS[i + 3] = fmaf(qq[i + 3], sdo, dS[i + 3]);
+                e0 = fmaf(kk[i], dS[i], e0);
+                e1 = fmaf(kk[i + 1], dS[i + 1], e1);
+                e2 = fmaf(kk[i + 2], dS[i + 2], e2);
+                e3 = fmaf(kk[i + 3], dS[i + 3], e3);
+            }
+            float* out = a.dstates + (tok * DK + i0) * DV + j;
+#pragma unroll
+            for (int i = 0; i < L::ROWS; ++i) out[static_cast<long>(i) * DV] = dS[i];
+            float ddj = (e0 + e1) + (e2 + e3);
+            if (L::PARTS == 2) ddj += __shfl_xor_sync(0xffffffffu, ddj, 16);
+            if (i0 == 0) {
+                a.dd[tok * DV + j] = ddj;
+                a.dv[tok * DV + j] = bm * ddj;
+            }
+            const float dr = -bm * ddj;
+#pragma unroll
+            for (int i = 0; i < L::ROWS; ++i) dS[i] = g * fmaf(kk[i], dr, dS[i]);
         }
-        float* out = a.dstates + (tok * DK + i0) * DV + j;
-#pragma unroll
-        for (int i = 0; i < L::ROWS; ++i) out[static_cast<long>(i) * DV] = dS[i];
-        float ddj = (e0 + e1) + (e2 + e3);
-        if (L::PARTS == 2) ddj += __shfl_xor_sync(0xffffffffu, ddj, 16);
-        if (i0 == 0) {
-            a.dd[tok * DV + j] = ddj;
-            a.dv[tok * DV + j] = bm * ddj;
-        }
-        const float dr = -bm * ddj;
-#pragma unroll
-        for (int i = 0; i < L::ROWS; ++i) dS[i] = g * fmaf(ks[i0 + i], dr, dS[i]);
     }
     if (a.dstate_in) {
 #pragma unroll

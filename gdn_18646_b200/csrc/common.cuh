@@ -25,6 +25,12 @@ int launch_status(const char* what);       // cudaGetLastError after a launch
 unsigned int* device_error_word();         // per-device error flag (device pointer)
 bool launch_overlap();                     // gdn_set_launch_overlap() state
 
+// gdn_prefill_fwd_ws with gates and mask rows gate_ld elements apart (prefill.cu)
+int prefill_segment(const void* q, const void* k, const void* v, const float* A_log, const void* a,
+                    const void* b_logits, int gate_dtype, float dt_bias, const float* dt_bias_vec, const float* mask,
+                    const float* state_in, void* out, float* state_out, int B, int T, int Hqk, int Hv, int dk, int dv,
+                    int layout, float scale, void* workspace, size_t workspace_bytes, void* stream, long gate_ld);
+
 inline bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
 
 // Device-side error flag bits.

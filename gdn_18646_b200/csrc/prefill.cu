@@ -147,6 +147,7 @@ struct GateArgs {
     int Ttot;
     unsigned int* err;
     unsigned int* ready; // streamed schedule: per-record ready flags, cleared here
+    long gate_ld;        // elements between the rows of a, b_logits [B*Hv rows] and mask [B rows]
 };
 
 struct PrepArgs {
@@ -480,19 +481,19 @@ prefill_gates_kernel(const GateArgs args) {
     // valid tokens of this sequence and the offset of its gates (varlen: [Hv, Ttot], packed)
     int start = 0;
     const int T = args.cu ? varlen_seq(args.cu, bidx, args.Ttot, start, args.err) : args.T;
-    const long base = args.cu ? static_cast<long>(h) * args.Ttot + start : static_cast<long>(bh) * T;
+    const long base = args.cu ? static_cast<long>(h) * args.Ttot + start : static_cast<long>(bh) * args.gate_ld;
     const int t0 = 2 * lane;
     const int tok = c * kC + t0;
     float a0 = 0.f, a1 = 0.f, b0 = 0.f, b1 = 0.f, m0 = 0.f, m1 = 0.f;
     if (tok < T) {
         a0 = load_gate(args.a, base + tok, args.gate_dtype);
         b0 = load_gate(args.b, base + tok, args.gate_dtype);
-        m0 = args.mask ? args.mask[static_cast<long>(bidx) * T + tok] : 1.f;
+        m0 = args.mask ? args.mask[static_cast<long>(bidx) * args.gate_ld + tok] : 1.f;
     }
     if (tok + 1 < T) {
         a1 = load_gate(args.a, base + tok + 1, args.gate_dtype);
         b1 = load_gate(args.b, base + tok + 1, args.gate_dtype);
-        m1 = args.mask ? args.mask[static_cast<long>(bidx) * T + tok + 1] : 1.f;
+        m1 = args.mask ? args.mask[static_cast<long>(bidx) * args.gate_ld + tok + 1] : 1.f;
     }
     const float A_neg = -expf(args.A_log[h]);
     const float dtb = args.dt_bias_vec ? args.dt_bias_vec[h] : args.dt_bias;
@@ -1575,11 +1576,12 @@ namespace gdn {
 namespace {
 // One prefill over B sequences of T tokens, or (cu != null) over B packed
 // sequences of at most T tokens each in tensors of Ttot tokens (layout BTHD,
-// batch 1), already validated.
+// batch 1), already validated.  gate_ld: elements between rows of a, b_logits
+// and mask (0 = T, dense).
 int run_prefill(const void* q, const void* k, const void* v, const float* A_log, const void* a, const void* b_logits,
                 int gate_dtype, float dt_bias, const float* dt_bias_vec, const float* mask, const float* state_in,
                 void* out, float* state_out, int B, int T, int Hqk, int Hv, int dk, int dv, int layout, float scale,
-                void* workspace, size_t workspace_bytes, void* stream, const int* cu, int Ttot) {
+                void* workspace, size_t workspace_bytes, void* stream, const int* cu, int Ttot, long gate_ld = 0) {
     int st = GDN_OK;
     const long ntiles = (dv + 127) / 128;
     const long nchunks = (static_cast<long>(T) + kC - 1) / kC;
@@ -1619,6 +1621,7 @@ int run_prefill(const void* q, const void* k, const void* v, const float* A_log,
     ga.Ttot = mT;
     ga.err = device_error_word();
     ga.ready = nullptr;
+    ga.gate_ld = gate_ld > 0 ? gate_ld : T;
 
     PrepArgs pa;
     pa.rec = static_cast<uint8_t*>(workspace);
@@ -1677,6 +1680,23 @@ extern "C" int gdn_prefill_fwd_ws(const void* q, const void* k, const void* v, c
     return run_prefill(q, k, v, A_log, a, b_logits, gate_dtype, dt_bias, dt_bias_vec, mask, state_in, out, state_out,
                        B, T, Hqk, Hv, dk, dv, layout, scale, workspace, workspace_bytes, stream, nullptr, 0);
 }
+
+namespace gdn {
+// gdn_prefill_fwd_ws over gates and mask whose rows are gate_ld elements apart
+// (a token segment of wider [B*Hv, T] / [B, T] arrays): the host pipeline's
+// per-segment call.
+int prefill_segment(const void* q, const void* k, const void* v, const float* A_log, const void* a,
+                    const void* b_logits, int gate_dtype, float dt_bias, const float* dt_bias_vec, const float* mask,
+                    const float* state_in, void* out, float* state_out, int B, int T, int Hqk, int Hv, int dk, int dv,
+                    int layout, float scale, void* workspace, size_t workspace_bytes, void* stream, long gate_ld) {
+    const int st = validate_prefill(q, k, v, A_log, a, b_logits, gate_dtype, state_in, out, state_out, B, T, Hqk, Hv,
+                                    dk, dv, layout);
+    if (st != GDN_OK) return st;
+    if (gate_ld < T) return fail(GDN_ERR_SHAPE, "prefill segment: gate row stride %ld below T=%d", gate_ld, T);
+    return run_prefill(q, k, v, A_log, a, b_logits, gate_dtype, dt_bias, dt_bias_vec, mask, state_in, out, state_out,
+                       B, T, Hqk, Hv, dk, dv, layout, scale, workspace, workspace_bytes, stream, nullptr, 0, gate_ld);
+}
+}  // namespace gdn
 
 // Same call with the workspace taken from the stream-ordered allocator for the
 // duration of the call.

@@ -109,6 +109,67 @@ def prefill(q, k, v, A_log, a, b_logits, *, dt_bias=0.0, mask=None, state_in=Non
     return out, state_out
 
 
+def _contig(t: torch.Tensor, name: str, dtype=None) -> None:
+    _need(t.is_contiguous(), f"{name} must be contiguous")
+    if dtype is not None:
+        _need(t.dtype == dtype, f"{name} must be {dtype}, got {t.dtype}")
+
+
+def prefill_host(q, k, v, A_log, a, b_logits, *, dt_bias=0.0, mask=None, state_in=None, scale=0.0,
+                 layout="bhtd", out=None, state_out=None, return_state=True, seg_tokens=0, device=None,
+                 synchronize=True):
+    """``prefill`` on host tensors (gdn_prefill_host): the inputs are copied to the
+    GPU and the results back in token segments that overlap the prefill of the
+    neighbouring segments.  Tensors may live on the host (pinned, for the copies
+    to overlap) or on the device; outputs default to pinned host tensors.
+    ``seg_tokens`` 0 picks the segment length.  With ``synchronize`` the current
+    stream is synchronised before returning; without it the host outputs are
+    valid once the stream completes, and the caller keeps the host inputs alive
+    until then.  Same result as ``prefill`` on the whole sequence."""
+    lay = GDN_LAYOUT_BHTD if layout == "bhtd" else GDN_LAYOUT_BTHD
+    for name, t in (("q", q), ("k", k), ("v", v)):
+        _contig(t, name, torch.bfloat16)
+    if lay == GDN_LAYOUT_BHTD:
+        B, Hqk, T, dk = q.shape
+        Hv, dv = v.shape[1], v.shape[3]
+    else:
+        B, T, Hqk, dk = q.shape
+        Hv, dv = v.shape[2], v.shape[3]
+    _need(tuple(k.shape) == tuple(q.shape), "k must have q's shape")
+    gdt = _gate_dtype(a, "a")
+    _need(b_logits.dtype == a.dtype, "a and b_logits must share a dtype")
+    _contig(a, "a")
+    _contig(b_logits, "b_logits")
+    _need(tuple(a.shape) == (B, Hv, T) and tuple(b_logits.shape) == (B, Hv, T), "a, b_logits must be [B, Hv, T]")
+    _contig(A_log, "A_log", torch.float32)
+    dt_vec, dt_scalar = None, 0.0
+    if isinstance(dt_bias, torch.Tensor) and dt_bias.numel() > 1:
+        _contig(dt_bias, "dt_bias", torch.float32)
+        dt_vec = dt_bias
+    else:
+        dt_scalar = float(dt_bias)
+    if mask is not None:
+        _contig(mask, "mask", torch.float32)
+    if state_in is not None:
+        _contig(state_in, "state_in", torch.float32)
+    dev = torch.device("cuda", torch.cuda.current_device()) if device is None else torch.device(device)
+    if out is None:
+        out = torch.empty(v.shape, dtype=torch.bfloat16, pin_memory=True)
+    if state_out is None and return_state:
+        state_out = torch.empty(B, Hv, dk, dv, dtype=torch.float32, pin_memory=True)
+    ws_bytes = int(_lib.lib().gdn_prefill_host_workspace_bytes(B, T, Hqk, Hv, dk, dv, gdt, int(seg_tokens)))
+    _need(ws_bytes > 0, f"prefill_host: unsupported shapes or seg_tokens={seg_tokens}")
+    ws = torch.empty(ws_bytes + 256, dtype=torch.uint8, device=dev)
+    ws_ptr = (ws.data_ptr() + 255) // 256 * 256
+    with torch.cuda.device(dev):
+        _lib.call("gdn_prefill_host", _ptr(q), _ptr(k), _ptr(v), _ptr(A_log), _ptr(a), _ptr(b_logits), gdt,
+                  dt_scalar, _ptr(dt_vec), _ptr(mask), _ptr(state_in), _ptr(out), _ptr(state_out),
+                  B, T, Hqk, Hv, dk, dv, lay, float(scale), int(seg_tokens), ws_ptr, ws_bytes, _stream())
+        if synchronize:
+            torch.cuda.current_stream().synchronize()
+    return out, state_out
+
+
 def prefill_varlen(q, k, v, A_log, a, b_logits, cu_seqlens, *, max_len=None, dt_bias=0.0, state_in=None,
                    scale=0.0, out=None, state_out=None, return_state=True):
     """Prefill of N sequences packed along the token axis (gdn_prefill_varlen_fwd_ws).

@@ -1,7 +1,8 @@
 /*
  * gdn_b200.h -- C ABI of the B200 (sm_100a) Gated DeltaNet hot path.
  *
- * Every entry point takes raw DEVICE pointers, explicit shapes, a CUDA
+ * Every entry point takes raw DEVICE pointers (gdn_prefill_host also host
+ * ones), explicit shapes, a CUDA
  * stream (passed as void*, a cudaStream_t; NULL = legacy default stream) and
  * returns an int status (GDN_OK == 0).  Launches are asynchronous on that
  * stream; no entry point synchronises, and only gdn_prefill_fwd allocates
@@ -189,6 +190,43 @@ int gdn_prefill_varlen_fwd(const void* q, const void* k, const void* v,
                            const int* cu_seqlens, int N, int Ttot, int max_len,
                            const float* state_in, void* out, float* state_out,
                            int Hqk, int Hv, int dk, int dv, float scale, void* stream);
+
+/*
+ * Prefill over HOST buffers (the reference's pybind op with CPU tensors moved
+ * to the GPU around it, kernels/prefill_chunked.cu:512-521): the same
+ * arguments and result as gdn_prefill_fwd, but q, k, v, a, b_logits, mask,
+ * state_in, out and state_out may be host memory (page-locked, for the copies
+ * to overlap) or device memory; A_log and dt_bias_vec too.  The token axis is
+ * cut into segments of seg_tokens tokens (0 = automatic, else a multiple of
+ * 64); segment i+1 is copied in while segment i runs on `stream` and segment
+ * i-1 is copied out, on two copy streams of the library's own that wait on
+ * `stream` at the start and that `stream` waits on at the end.  The result is
+ * the one gdn_prefill_fwd gives on the whole sequence.  Host outputs are
+ * valid after `stream` completes.  Calls on one device are serialised on the
+ * host (a mutex) while they enqueue.
+ * Workspace: device memory, 256-byte aligned, of
+ * gdn_prefill_host_workspace_bytes(B, T, Hqk, Hv, dk, dv, gate_dtype, seg_tokens)
+ * bytes (two segments of inputs and outputs, two states, the gates whole, the
+ * prefill's own workspace for one segment).  gdn_prefill_host_segment returns
+ * the largest segment a call would use, gdn_prefill_host_plan the segment
+ * count and (when starts != NULL) up to cap segment boundaries
+ * starts[0] = 0 < ... < starts[nseg] = T; both -1 for invalid shapes.  The
+ * automatic plan (seg_tokens 0) uses full segments, then halving ones down to
+ * a single chunk at the end, so the last prefill and read-back are short.
+ * These three are host-only.
+ */
+size_t gdn_prefill_host_workspace_bytes(int B, int T, int Hqk, int Hv, int dk, int dv, int gate_dtype,
+                                        int seg_tokens);
+int gdn_prefill_host_segment(int B, int T, int Hqk, int Hv, int dk, int dv, int gate_dtype, int seg_tokens);
+int gdn_prefill_host_plan(int B, int T, int Hqk, int Hv, int dk, int dv, int gate_dtype, int seg_tokens,
+                          int* starts, int cap);
+int gdn_prefill_host(const void* q, const void* k, const void* v,
+                     const float* A_log, const void* a, const void* b_logits, int gate_dtype,
+                     float dt_bias, const float* dt_bias_vec,
+                     const float* mask, const float* state_in,
+                     void* out, float* state_out,
+                     int B, int T, int Hqk, int Hv, int dk, int dv, int layout,
+                     float scale, int seg_tokens, void* workspace, size_t workspace_bytes, void* stream);
 
 /*
  * Gradients of the prefill (training): dq, dk, dv, da, db, dA_log, ddt_bias and

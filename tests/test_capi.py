@@ -238,3 +238,53 @@ def test_prefill_bwd_rejects(lib):
     assert call(wsb=16) == _lib.GDN_ERR_SHAPE
     assert call(ws=ODD) == _lib.GDN_ERR_ALIGN
     assert lib.gdn_prefill_bwd_workspace_bytes(1, 64, 2, 96, 64) == 0
+
+
+def test_prefill_host_plan(lib):
+    # config 1: segments of up to 1024 tokens (48 MiB of q, k, v), halving toward the end
+    assert lib.gdn_prefill_host_segment(4, 4096, 16, 16, 128, 128, 1, 0) == 1024
+    assert lib.gdn_prefill_host_segment(1, 100, 16, 16, 128, 128, 1, 512) == 128     # capped at T rounded up
+    assert lib.gdn_prefill_host_segment(1, 100, 16, 16, 128, 128, 1, 96) == -1       # not a multiple of 64
+    assert lib.gdn_prefill_host_segment(1, 100, 16, 16, 96, 128, 1, 0) == -1
+    big = lib.gdn_prefill_host_workspace_bytes(4, 4096, 16, 16, 128, 128, 1, 0)
+    small = lib.gdn_prefill_host_workspace_bytes(4, 4096, 16, 16, 128, 128, 1, 64)
+    assert 0 < small < big
+    # the segment prefill's own workspace is part of it
+    assert small > lib.gdn_prefill_workspace_bytes(4, 64, 16, 128, 128)
+    assert lib.gdn_prefill_host_workspace_bytes(4, 4096, 16, 16, 128, 128, 7, 0) == 0
+
+
+def test_prefill_host_rejects(lib):
+    def call(seg=0, ws=ODD, wsb=1 << 40, **over):
+        args = prefill_args(**over)[:-1]                 # drop the stream
+        return _lib.call_status("gdn_prefill_host", *args, seg, ws, wsb, None)
+    assert call(q=None) == _lib.GDN_ERR_NULL
+    assert call(T=0) == _lib.GDN_ERR_SHAPE
+    assert call(dk=96) == _lib.GDN_ERR_SHAPE
+    assert call(layout=5) == _lib.GDN_ERR_SHAPE
+    assert call(seg=96) == _lib.GDN_ERR_SHAPE
+    assert call(wsb=16) == _lib.GDN_ERR_SHAPE
+    assert call(ws=None) == _lib.GDN_ERR_SHAPE
+    assert call() == _lib.GDN_ERR_ALIGN
+    assert "gdn_prefill_host" in _lib.last_error()
+
+
+def _plan(lib, B, T, H, seg):
+    starts = (ctypes.c_int * 4096)()
+    n = lib.gdn_prefill_host_plan(B, T, H, H, 128, 128, 1, seg, starts, 4096)
+    return [starts[i] for i in range(n + 1)]
+
+
+@pytest.mark.parametrize("T", [1, 63, 64, 65, 1000, 4096, 5000, 70001])
+def test_prefill_host_plan_segments(lib, T):
+    auto = _plan(lib, 4, T, 16, 0)
+    seg = lib.gdn_prefill_host_segment(4, T, 16, 16, 128, 128, 1, 0)
+    assert auto[0] == 0 and auto[-1] == T
+    lens = [b - a for a, b in zip(auto, auto[1:])]
+    assert all(0 < x <= seg for x in lens)
+    assert all(x % 64 == 0 for x in lens[:-1])          # chunk-aligned boundaries
+    assert lens[-1] <= 64                                # the tail is one chunk
+    if T == 4096:
+        assert lens == [1024, 1024, 1024, 512, 256, 128, 64, 64]
+    uni = _plan(lib, 4, T, 16, 128)                      # explicit: uniform, ragged last
+    assert uni == list(range(0, T, 128)) + [T]
