@@ -1262,24 +1262,39 @@ struct OverlapSmem {
     static_assert(ALLOC <= 232448, "overlap kernel shared memory exceeds 227 KB");
 };
 
-// Chain piece k and prep piece k+1 in one launch: CTAs [0, nchain) run the
-// recurrence over the chunks prepared by the previous launch; every other CTA
+// Chain piece k and prep piece k+1 in one launch: roles [0, nchain) run the
+// recurrence over the chunks prepared by the previous launch; every other role
 // hosts kPrepPerCta independent prep workers (128 threads each) preparing the
-// next piece.  No CTA waits on another, so residency does not matter for
-// correctness; with one CTA per SM the two roles run side by side.
+// next piece.  With one CTA per SM the two roles run side by side.
+//
+// A CTA's role is its block index, or with by_smid its SM id.  Chain and prep
+// CTAs on neighbouring SMs slow each other down: with roles by block index
+// the prep workers of the streamed schedule ran ~1.5x slower than alone while
+// the chain ran, and the step took 13 % longer than with the chain on SMs
+// [0, nchain) and prep on the rest.  by_smid is set only for the cooperative
+// launch, where every CTA holds its own SM for the whole launch, and applies
+// only when the SM ids are exactly [0, gridDim.x) (%nsmid == gridDim.x), so
+// the roles are a permutation of the block indices.
 template <int DK>
 __global__ void __launch_bounds__(kChainThreads, 1)
 prefill_overlap_kernel(const __grid_constant__ CUtensorMap map_q, const __grid_constant__ CUtensorMap map_k,
                        const __grid_constant__ CUtensorMap map_v, const __grid_constant__ CUtensorMap map_o,
-                       const ChainArgs ca, const PrepArgs pa, const int nchain) {
+                       const ChainArgs ca, const PrepArgs pa, const int nchain, const int by_smid) {
     extern __shared__ uint8_t smem_raw[];
     uint8_t* sm = align1024(smem_raw);
-    if (static_cast<int>(blockIdx.x) < nchain) {
-        chain_body<DK>(&map_q, &map_k, &map_v, &map_o, ca, sm, blockIdx.x);
+    int role = static_cast<int>(blockIdx.x);
+    if (by_smid) {
+        unsigned smid, nsmid;
+        asm volatile("mov.u32 %0, %%smid;" : "=r"(smid));
+        asm volatile("mov.u32 %0, %%nsmid;" : "=r"(nsmid));
+        if (nsmid == gridDim.x) role = static_cast<int>(smid);
+    }
+    if (role < nchain) {
+        chain_body<DK>(&map_q, &map_k, &map_v, &map_o, ca, sm, role);
     } else {
         const int wg = threadIdx.x >> 7;
         if (wg < kPrepPerCta) {
-            const int vblock = (blockIdx.x - nchain) * kPrepPerCta + wg;
+            const int vblock = (role - nchain) * kPrepPerCta + wg;
             const int vgrid = (gridDim.x - nchain) * kPrepPerCta;
             prep_body<DK>(&map_q, &map_k, pa, sm + wg * OverlapSmem<DK>::PREP_STRIDE, threadIdx.x & 127, vblock, vgrid,
                           BAR_PREP + wg, false);
@@ -1324,13 +1339,15 @@ bool use_pieces(int nbh, int nchunks, int chain_grid, int sms) {
 // Predicted time (us) of the streamed schedule when the first `lead` chunks of
 // every sequence are prepared by a prep launch on all SMs (~12 us a round of 3
 // workers per SM) and the rest by the free SMs' workers inside the cooperative
-// launch (~15 us a round) while the chain CTAs consume them (~3.3 us a chunk):
-// the lead, then the slower of the two streams.  Per-unit costs from traces of
-// config 1 on B200 (globaltimer stamps per record and per chain chunk).
+// launch (~11 us a round, with the roles placed by SM id) while the chain CTAs
+// consume them (~3.3 us a chunk): the lead, then the slower of the two
+// streams.  Per-unit costs from traces of config 1 on B200 (clock stamps per
+// record and per chain chunk); at config 1 it picks no lead, which measured
+// fastest of leads 0-12.
 double streamed_time(int nbh, int nchunks, int chain_grid, int sms, int lead) {
     const long w_all = static_cast<long>(sms) * kPrepCtasPerSm;
     const long w_free = static_cast<long>(sms - chain_grid) * kPrepPerCta;
-    const double prep_round = 12.0, ovl_round = 15.0, first = 4.0, chunk = 3.3, launch = 7.0;
+    const double prep_round = 12.0, ovl_round = 11.0, first = 4.0, chunk = 3.3, launch = 7.0;
     const long t_lead = static_cast<long>(nbh) * lead, t_rest = static_cast<long>(nbh) * (nchunks - lead);
     const double head = lead > 0 ? static_cast<double>((t_lead + w_all - 1) / w_all) * prep_round + first + launch : 0.0;
     const double prep = static_cast<double>((t_rest + w_free - 1) / w_free) * ovl_round + chunk;
@@ -1456,7 +1473,8 @@ int launch_prefill(const CUtensorMap& mq, const CUtensorMap& mk, const CUtensorM
         attr[0].val.cooperative = 1;
         cfg.attrs = attr;
         cfg.numAttrs = 1;
-        const cudaError_t e = cudaLaunchKernelEx(&cfg, prefill_overlap_kernel<DK>, mq, mk, mv, mo, ca, pa, chain_grid);
+        const cudaError_t e =
+            cudaLaunchKernelEx(&cfg, prefill_overlap_kernel<DK>, mq, mk, mv, mo, ca, pa, chain_grid, 1);
         if (e != cudaSuccess)
             return fail(GDN_ERR_CUDA, "gdn_prefill_fwd (streamed): cooperative launch of %d CTAs failed: %s", sms,
                         cudaGetErrorString(e));
@@ -1477,7 +1495,7 @@ int launch_prefill(const CUtensorMap& mq, const CUtensorMap& mk, const CUtensorM
         // chain CTAs first, prep workers on the remaining SMs (at least one CTA of them)
         const int grid = chain_grid + (sms - chain_grid > 1 ? sms - chain_grid : 1);
         prefill_overlap_kernel<DK><<<grid, kChainThreads, OverlapSmem<DK>::ALLOC, st>>>(mq, mk, mv, mo, ca, pa,
-                                                                                       chain_grid);
+                                                                                       chain_grid, 0);
         if ((s = launch_status("gdn_prefill_fwd (overlap)")) != GDN_OK) return s;
     }
     const int kl = pieces - 1;

@@ -148,7 +148,7 @@ def test_prefill_schedules(cuda_device, schedule, B, T, H, Hqk, dk, dv):
 def test_prefill_launch_count(cuda_device):
     from gdn_18646_b200 import _lib
     lib = _lib.lib()
-    assert lib.gdn_prefill_launch_count(4, 4096, 16, 128, 128) == 3        # config 1: gates, lead prep, stream
+    assert lib.gdn_prefill_launch_count(4, 4096, 16, 128, 128) == 2        # config 1: gates, stream (no lead)
     assert lib.gdn_prefill_launch_count(8, 4096, 32, 128, 128) == 3        # 256 chains >= SMs: single
     _lib.call("gdn_prefill_set_schedule", _lib.GDN_SCHEDULE_PIECED)
     try:
