@@ -251,7 +251,6 @@ __device__ __forceinline__ bool wait_record(const unsigned int* flag, unsigned i
     asm volatile("fence.proxy.async.global;" ::: "memory");
     return true;
 }
-__device__ __forceinline__ void bulk_wait_group3() { asm volatile("cp.async.bulk.wait_group 3;" ::: "memory"); }
 
 // Varlen: first token and length of sequence b.  Offsets that are negative,
 // decreasing or past Ttot make the sequence empty (nothing read or written for
@@ -640,6 +639,14 @@ __device__ __forceinline__ void prep_body(const CUtensorMap* map_q, const CUtens
 
         // ---- [Q;K] K^T on tensor cores
         mbar_wait_or_abort(bar_qk, ph, err, abort_flag);
+        if (leader && args.ready && published >= 0) {
+            // streamed: the previous task's stores were issued before this task's q/k load,
+            // so they have (nearly) completed; publish its record now rather than a task
+            // later (a chain CTA waits for it)
+            bulk_wait_all0();
+            publish_record(args.ready + published);
+            published = -1;
+        }
         if (leader && !*abort_flag) {
             tc_fence_after();
             const uint32_t sqk = smem_u32(sm);
@@ -805,14 +812,7 @@ __device__ __forceinline__ void prep_body(const CUtensorMap* map_q, const CUtens
             bulk_store(rec + R::WTH, sm, 2 * DK * 128);
             bulk_commit();
             bulk_wait_read0();                        // the images (and A1 over N) have been read out
-            if (args.ready) {
-                // the previous task's three store groups have completed: publish it
-                if (published >= 0) {
-                    bulk_wait_group3();
-                    publish_record(args.ready + published);
-                }
-                published = rec_idx;
-            }
+            if (args.ready) published = rec_idx;       // published once the next task's q/k have landed
             // q/k shared memory is free: fetch the next task's tiles
             const int nt = next_task(task + vgrid);
             if (!*abort_flag && nt < args.ntasks) {
