@@ -685,6 +685,18 @@ def run_only(args):
 
         def step():
             ops.decode_step(q, k, v, a, b, A_log, dtb, S, out=o)
+    elif args.only == "outproj":
+        # the fused output projection's GEMM on one GPU (world 1: every tile stays local)
+        # at the config-3 widths: y [32768, 4096] x W_o [2048, 4096]^T
+        from gdn_18646_b200.sharding import PeerBuffer, sharded_out_proj
+        g = torch.Generator(device=dev).manual_seed(77)
+        y = torch.randn(32768, 4096, generator=g, device=dev).bfloat16()
+        W = (torch.randn(2048, 4096, generator=g, device=dev) * 4096 ** -0.5).bfloat16()
+        buf = PeerBuffer(32768, 2048)
+        o = torch.empty(32768, 2048, dtype=torch.bfloat16, device=dev)
+
+        def step():
+            sharded_out_proj(y, W, buf, out=o)
     elif args.only == "backward":
         # config 1's head shape at B=1, T=1024: a 2.1 GB workspace, small enough to capture
         inp = gen_prefill(1, 1024, C1["H"], C1["dk"], C1["dv"], 99, dev)
@@ -717,7 +729,7 @@ def main(argv=None):
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--workload", choices=["prefill", "long"], default="prefill")
     ap.add_argument("--no-cpu-baseline", action="store_true")
-    ap.add_argument("--only", choices=["prefill", "decode", "proj", "layer_decode", "backward"], default=None,
+    ap.add_argument("--only", choices=["prefill", "decode", "proj", "layer_decode", "backward", "outproj"], default=None,
                     help="run just one kernel's workload (for profiling); prints a short JSON line")
     args = ap.parse_args(argv)
     if args.only:

@@ -54,6 +54,7 @@ struct BwdArgs {
     float* states;             // workspace: S_p per token [B,H,T,DK,DV]
     float* dstates;            // workspace: dS per token
     float* dd;                 // workspace: [B,H,T,DV]
+    float* rp;                 // workspace: [B,H,T,DV], k . S_p per value column
     float* dlogg;              // workspace: [B,H,T]
     int B, T, H;
     float scale;
@@ -71,31 +72,46 @@ __device__ __forceinline__ void gate_of(const BwdArgs& a, int bh, int t, float& 
     bm = sigmoid_f(load_gate(a.b, i, a.gate_dtype)) * m;
 }
 
-// The recurrences keep 64 state rows of one value column per thread: with
-// dk = 128 the two halves of a column sit in lanes l and l + 16 of a warp
-// (16 columns per warp) and the column dot products add the halves with one
-// shuffle; with dk = 64 a warp covers 32 columns.
+// The recurrences keep 32 state rows of one value column per thread: a column
+// is spread over PARTS = dk/32 lanes of a warp (its dot products add the parts
+// with log2(PARTS) shuffles) and a warp covers COLS = 32/PARTS columns, so one
+// store instruction writes whole 32-byte sectors (PARTS rows x COLS columns).
+// A CTA of 4 warps covers 4 * COLS adjacent columns and shares the staged
+// tokens; config 1 (B*H = 64, dv = 128) runs 1024 warps.  (16 rows per thread
+// doubled the warps but wrote half sectors, and ran 3x slower.)
 template <int DK>
 struct RecLayout {
-    static constexpr int PARTS = DK / 64;          // threads per column
+    static constexpr int ROWS = 32;                // rows per thread
+    static constexpr int PARTS = DK / ROWS;        // threads per column
     static constexpr int COLS = 32 / PARTS;        // columns per warp
-    static constexpr int ROWS = 64;                // rows per thread
+    static constexpr int WARPS = 4;
+    static constexpr int CTA_COLS = COLS * WARPS;  // columns per CTA
+    static constexpr int THREADS = 32 * WARPS;
 };
 
 // Tokens a recurrence stages in shared memory at once (one global round trip
 // per block instead of one per token).
 constexpr int kTB = 32;
 
-// Forward recurrence, storing S_p (the state before each token).  Grid (B*H, DV/COLS), one warp.
+template <int PARTS_, int COLS_>
+__device__ __forceinline__ float sum_parts(float x) {
+#pragma unroll
+    for (int o = COLS_; o < 32; o <<= 1) x += __shfl_xor_sync(0xffffffffu, x, o);
+    return x;
+}
+
+// Forward recurrence, storing S_p (the state before each token) and rp = k . S_p
+// per value column.  Grid (B*H, DV/CTA_COLS).
 template <int DK, int DV>
-__global__ void __launch_bounds__(32) bwd_states_kernel(const BwdArgs a) {
+__global__ void __launch_bounds__(128) bwd_states_kernel(const BwdArgs a) {
     using L = RecLayout<DK>;
-    const int bh = blockIdx.x, lane = threadIdx.x;
+    const int bh = blockIdx.x, tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
     const int jl = lane % L::COLS;
-    const int j = blockIdx.y * L::COLS + jl;
-    const int i0 = (lane / L::COLS) * L::ROWS;      // first row of this thread
+    const int jc = warp * L::COLS + jl;                // column within the CTA
+    const int j = blockIdx.y * L::CTA_COLS + jc;
+    const int i0 = (lane / L::COLS) * L::ROWS;        // first row of this thread
     __shared__ float ks[kTB][DK];
-    __shared__ float vs[kTB][L::COLS];
+    __shared__ float vs[kTB][L::CTA_COLS];
     __shared__ float gs[kTB], bs[kTB];
     float S[L::ROWS];
     const long s0 = static_cast<long>(bh) * DK * DV;
@@ -105,12 +121,13 @@ __global__ void __launch_bounds__(32) bwd_states_kernel(const BwdArgs a) {
     for (int tb = 0; tb < a.T; tb += kTB) {
         const int nt = min(kTB, a.T - tb);
         const long tok0 = static_cast<long>(bh) * a.T + tb;
-        __syncwarp();
-        for (int e = lane; e < nt * DK; e += 32) ks[e / DK][e % DK] = bf16_at(a.k, tok0 * DK + e);
-        for (int e = lane; e < nt * L::COLS; e += 32)
-            vs[e / L::COLS][e % L::COLS] = bf16_at(a.v, (tok0 + e / L::COLS) * DV + blockIdx.y * L::COLS + e % L::COLS);
-        if (lane < nt) gate_of(a, bh, tb + lane, gs[lane], bs[lane]);
-        __syncwarp();
+        __syncthreads();
+        for (int e = tid; e < nt * DK; e += L::THREADS) ks[e / DK][e % DK] = bf16_at(a.k, tok0 * DK + e);
+        for (int e = tid; e < nt * L::CTA_COLS; e += L::THREADS)
+            vs[e / L::CTA_COLS][e % L::CTA_COLS] =
+                bf16_at(a.v, (tok0 + e / L::CTA_COLS) * DV + blockIdx.y * L::CTA_COLS + e % L::CTA_COLS);
+        if (tid < nt) gate_of(a, bh, tb + tid, gs[tid], bs[tid]);
+        __syncthreads();
         for (int u = 0; u < nt; ++u) {
             const long tok = tok0 + u;
             float* out = a.states + (tok * DK + i0) * DV + j;
@@ -126,26 +143,27 @@ __global__ void __launch_bounds__(32) bwd_states_kernel(const BwdArgs a) {
                 r2 = fmaf(kk[i + 2], S[i + 2], r2);
                 r3 = fmaf(kk[i + 3], S[i + 3], r3);
             }
-            float rp = (r0 + r1) + (r2 + r3);
-            if (L::PARTS == 2) rp += __shfl_xor_sync(0xffffffffu, rp, 16);
-            const float d = bm * (vs[u][jl] - g * rp);
+            const float rp = sum_parts<L::PARTS, L::COLS>((r0 + r1) + (r2 + r3));
+            if (i0 == 0) a.rp[tok * DV + j] = rp;
+            const float d = bm * (vs[u][jc] - g * rp);
 #pragma unroll
             for (int i = 0; i < L::ROWS; ++i) S[i] = fmaf(kk[i], d, g * S[i]);
         }
     }
 }
 
-// Reverse recurrence of dS, storing dS (gradient of S_n) per token, dv and dd.  Grid (B*H, DV/COLS).
+// Reverse recurrence of dS, storing dS (gradient of S_n) per token, dv and dd.  Grid (B*H, DV/CTA_COLS).
 template <int DK, int DV>
-__global__ void __launch_bounds__(32) bwd_dstate_kernel(const BwdArgs a) {
+__global__ void __launch_bounds__(128) bwd_dstate_kernel(const BwdArgs a) {
     using L = RecLayout<DK>;
-    const int bh = blockIdx.x, lane = threadIdx.x;
+    const int bh = blockIdx.x, tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
     const int jl = lane % L::COLS;
-    const int j = blockIdx.y * L::COLS + jl;
+    const int jc = warp * L::COLS + jl;
+    const int j = blockIdx.y * L::CTA_COLS + jc;
     const int i0 = (lane / L::COLS) * L::ROWS;
     const int bi = bh / a.H;
     __shared__ float ks[kTB][DK], qs[kTB][DK];
-    __shared__ float dos[kTB][L::COLS];
+    __shared__ float dos[kTB][L::CTA_COLS];
     __shared__ float gs[kTB], bs[kTB];
     float dS[L::ROWS];
     const long s0 = static_cast<long>(bh) * DK * DV;
@@ -155,26 +173,26 @@ __global__ void __launch_bounds__(32) bwd_dstate_kernel(const BwdArgs a) {
     for (int tend = a.T; tend > 0; tend -= kTB) {
         const int tb = max(0, tend - kTB), nt = tend - tb;
         const long tok0 = static_cast<long>(bh) * a.T + tb;
-        __syncwarp();
-        for (int e = lane; e < nt * DK; e += 32) {
+        __syncthreads();
+        for (int e = tid; e < nt * DK; e += L::THREADS) {
             ks[e / DK][e % DK] = bf16_at(a.k, tok0 * DK + e);
             qs[e / DK][e % DK] = bf16_at(a.q, tok0 * DK + e);
         }
-        for (int e = lane; e < nt * L::COLS; e += 32) {
-            const int u = e / L::COLS;
-            const long idx = (tok0 + u) * DV + blockIdx.y * L::COLS + e % L::COLS;
+        for (int e = tid; e < nt * L::CTA_COLS; e += L::THREADS) {
+            const int u = e / L::CTA_COLS;
+            const long idx = (tok0 + u) * DV + blockIdx.y * L::CTA_COLS + e % L::CTA_COLS;
             const float m = a.mask ? a.mask[static_cast<long>(bi) * a.T + tb + u] : 1.f;
-            dos[u][e % L::COLS] =
+            dos[u][e % L::CTA_COLS] =
                 a.scale * m * (a.do_dtype == GDN_DTYPE_BF16 ? bf16_at(static_cast<const uint16_t*>(a.dO), idx)
                                                              : static_cast<const float*>(a.dO)[idx]);
         }
-        if (lane < nt) gate_of(a, bh, tb + lane, gs[lane], bs[lane]);
-        __syncwarp();
+        if (tid < nt) gate_of(a, bh, tb + tid, gs[tid], bs[tid]);
+        __syncthreads();
         for (int u = nt - 1; u >= 0; --u) {
             const long tok = tok0 + u;
             const float* kk = ks[u] + i0;
             const float* qq = qs[u] + i0;
-            const float sdo = dos[u][jl];
+            const float sdo = dos[u][jc];
             const float g = gs[u], bm = bs[u];
             float e0 = 0.f, e1 = 0.f, e2 = 0.f, e3 = 0.f;
 #pragma unroll
@@ -191,8 +209,7 @@ __global__ void __launch_bounds__(32) bwd_dstate_kernel(const BwdArgs a) {
             float* out = a.dstates + (tok * DK + i0) * DV + j;
 #pragma unroll
             for (int i = 0; i < L::ROWS; ++i) out[static_cast<long>(i) * DV] = dS[i];
-            float ddj = (e0 + e1) + (e2 + e3);
-            if (L::PARTS == 2) ddj += __shfl_xor_sync(0xffffffffu, ddj, 16);
+            const float ddj = sum_parts<L::PARTS, L::COLS>((e0 + e1) + (e2 + e3));
             if (i0 == 0) {
                 a.dd[tok * DV + j] = ddj;
                 a.dv[tok * DV + j] = bm * ddj;
@@ -208,65 +225,71 @@ __global__ void __launch_bounds__(32) bwd_dstate_kernel(const BwdArgs a) {
     }
 }
 
-// Per token: dq, dk, da, db (and dlog g for the head sums).  One CTA of 128 threads per token.
+// Per token: dq, dk, da, db (and dlog g for the head sums), one pass over S_p and dS.
+// One CTA of 4 warps per token; every warp holds all DV columns (DV/32 per lane), so
+// the per-column vectors (r = g k.S_p from the forward pass, delta, dr, m dO) and
+// their sums are formed in registers, and each warp reduces its rows' products
+// (dq_i, dk_i) across its lanes while S_p and dS are read once, row by row.
 template <int DK, int DV>
 __global__ void __launch_bounds__(128) bwd_token_kernel(const BwdArgs a) {
-    constexpr int NT = 128, NW = NT / 32;
+    constexpr int NW = 4, CPL = DV / 32;             // warps, columns per lane
     const long tok = blockIdx.x;                  // bh * T + t
     const int bh = static_cast<int>(tok / a.T), t = static_cast<int>(tok - static_cast<long>(bh) * a.T);
     const int bi = bh / a.H, h = bh % a.H;
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
-    __shared__ float ks[DK], dlt[DV], drs[DV], dos[DV];
-    __shared__ float red[2][NW];
-    const float* Sp = a.states + tok * DK * DV;
-    const float* dS = a.dstates + tok * DK * DV;
+    __shared__ float red[NW];
     float g, bm;
     gate_of(a, bh, t, g, bm);
     const float m = a.mask ? a.mask[static_cast<long>(bi) * a.T + t] : 1.f;
-    for (int i = tid; i < DK; i += NT) ks[i] = bf16_at(a.k, tok * DK + i);
-    __syncthreads();
-    // ---- columns: r, d (= delta), dr, and the partial sums of db' and dg
-    float p_db = 0.f, p_dg = 0.f;
-    for (int j = tid; j < DV; j += NT) {
-        float rp = 0.f, sds = 0.f;
-        for (int i = 0; i < DK; ++i) {
-            const float s = Sp[static_cast<long>(i) * DV + j];
-            rp = fmaf(ks[i], s, rp);
-            sds = fmaf(s, dS[static_cast<long>(i) * DV + j], sds);
-        }
+    // ---- per-column vectors of this lane's columns j = lane * CPL + c
+    float dlt[CPL], drs[CPL], dos[CPL];
+    float p_db = 0.f, p_ddo = 0.f, p_rdr = 0.f;
+#pragma unroll
+    for (int c = 0; c < CPL; ++c) {
+        const int j = lane * CPL + c;
         const float vj = bf16_at(a.v, tok * DV + j);
+        const float rp = a.rp[tok * DV + j];
         const float ddj = a.dd[tok * DV + j];
         const float r = g * rp;
-        const float dr = -bm * ddj;
-        dlt[j] = bm * (vj - r);
-        drs[j] = dr;
-        dos[j] = m * (a.do_dtype == GDN_DTYPE_BF16 ? bf16_at(static_cast<const uint16_t*>(a.dO), tok * DV + j)
+        dlt[c] = bm * (vj - r);
+        drs[c] = -bm * ddj;
+        dos[c] = m * (a.do_dtype == GDN_DTYPE_BF16 ? bf16_at(static_cast<const uint16_t*>(a.dO), tok * DV + j)
                                                    : static_cast<const float*>(a.dO)[tok * DV + j]);
         p_db = fmaf(ddj, vj - r, p_db);
-        p_dg += sds + dr * rp;                     // <S_p, dS + k dr^T> for this column
+        p_ddo = fmaf(dlt[c], dos[c], p_ddo);
+        p_rdr = fmaf(drs[c], rp, p_rdr);
     }
 #pragma unroll
     for (int o = 16; o > 0; o >>= 1) {
         p_db += __shfl_xor_sync(0xffffffffu, p_db, o);
-        p_dg += __shfl_xor_sync(0xffffffffu, p_dg, o);
+        p_ddo += __shfl_xor_sync(0xffffffffu, p_ddo, o);
+        p_rdr += __shfl_xor_sync(0xffffffffu, p_rdr, o);
     }
-    if (lane == 0) {
-        red[0][warp] = p_db;
-        red[1][warp] = p_dg;
-    }
-    __syncthreads();
-    // ---- rows, a warp per row: dq_i = scale (g S_p[i,:].dO' + k_i (d.dO')), dk_i = dS[i,:].d + g S_p[i,:].dr
-    float p_ddo = 0.f;
-    for (int j = lane; j < DV; j += 32) p_ddo = fmaf(dlt[j], dos[j], p_ddo);
-#pragma unroll
-    for (int o = 16; o > 0; o >>= 1) p_ddo += __shfl_xor_sync(0xffffffffu, p_ddo, o);
+    // ---- rows i = warp, warp + NW, ...: dq_i = scale (g S_p[i,:].dO' + k_i (delta.dO')),
+    //      dk_i = dS[i,:].delta + g S_p[i,:].dr; <S_p, dS> accumulated for dg
+    const float* Sp = a.states + tok * DK * DV;
+    const float* dS = a.dstates + tok * DK * DV;
+    float p_sds = 0.f;
     for (int i = warp; i < DK; i += NW) {
-        float sdo = 0.f, dsd = 0.f, sdr = 0.f;
-        for (int j = lane; j < DV; j += 32) {
-            const float s = Sp[static_cast<long>(i) * DV + j];
-            sdo = fmaf(s, dos[j], sdo);
-            sdr = fmaf(s, drs[j], sdr);
-            dsd = fmaf(dS[static_cast<long>(i) * DV + j], dlt[j], dsd);
+        float s[CPL], ds[CPL];
+        if constexpr (CPL == 4) {
+            const float4 x = *reinterpret_cast<const float4*>(Sp + i * DV + lane * 4);
+            const float4 y = *reinterpret_cast<const float4*>(dS + i * DV + lane * 4);
+            s[0] = x.x; s[1] = x.y; s[2] = x.z; s[3] = x.w;
+            ds[0] = y.x; ds[1] = y.y; ds[2] = y.z; ds[3] = y.w;
+        } else {
+            const float2 x = *reinterpret_cast<const float2*>(Sp + i * DV + lane * 2);
+            const float2 y = *reinterpret_cast<const float2*>(dS + i * DV + lane * 2);
+            s[0] = x.x; s[1] = x.y;
+            ds[0] = y.x; ds[1] = y.y;
+        }
+        float sdo = 0.f, sdr = 0.f, dsd = 0.f;
+#pragma unroll
+        for (int c = 0; c < CPL; ++c) {
+            sdo = fmaf(s[c], dos[c], sdo);
+            sdr = fmaf(s[c], drs[c], sdr);
+            dsd = fmaf(ds[c], dlt[c], dsd);
+            p_sds = fmaf(s[c], ds[c], p_sds);
         }
 #pragma unroll
         for (int o = 16; o > 0; o >>= 1) {
@@ -275,24 +298,26 @@ __global__ void __launch_bounds__(128) bwd_token_kernel(const BwdArgs a) {
             dsd += __shfl_xor_sync(0xffffffffu, dsd, o);
         }
         if (lane == 0) {
-            a.dq[tok * DK + i] = a.scale * fmaf(g, sdo, ks[i] * p_ddo);
+            const float ki = bf16_at(a.k, tok * DK + i);
+            a.dq[tok * DK + i] = a.scale * fmaf(g, sdo, ki * p_ddo);
             a.dk[tok * DK + i] = fmaf(g, sdr, dsd);
         }
     }
-    if (tid == 0) {
-        float dbm = 0.f, dg = 0.f;
 #pragma unroll
-        for (int w = 0; w < NW; ++w) {
-            dbm += red[0][w];
-            dg += red[1][w];
-        }
+    for (int o = 16; o > 0; o >>= 1) p_sds += __shfl_xor_sync(0xffffffffu, p_sds, o);
+    if (lane == 0) red[warp] = p_sds;
+    __syncthreads();
+    if (tid == 0) {
+        float dg = p_rdr;                             // <S_p, dS + k dr^T> = <S_p, dS> + dr . rp
+#pragma unroll
+        for (int w = 0; w < NW; ++w) dg += red[w];
         const float dtb = a.dt_bias_vec ? a.dt_bias_vec[h] : a.dt_bias;
         const float x = load_gate(a.a, tok, a.gate_dtype) + dtb;
         const float dlogg = dg * g;
         a.dlogg[tok] = dlogg;
         a.da[tok] = dlogg * (-expf(a.A_log[h])) * (x > 20.f ? 1.f : sigmoid_f(x));
         const float sb = sigmoid_f(load_gate(a.b, tok, a.gate_dtype));
-        a.db[tok] = dbm * m * sb * (1.f - sb);
+        a.db[tok] = p_db * m * sb * (1.f - sb);
     }
 }
 
@@ -329,11 +354,11 @@ __global__ void __launch_bounds__(256) bwd_head_kernel(const BwdArgs a) {
 
 template <int DK, int DV>
 int launch_bwd(const BwdArgs& a, cudaStream_t st) {
-    const dim3 rec(a.B * a.H, DV / RecLayout<DK>::COLS);
-    bwd_states_kernel<DK, DV><<<rec, 32, 0, st>>>(a);
+    const dim3 rec(a.B * a.H, DV / RecLayout<DK>::CTA_COLS);
+    bwd_states_kernel<DK, DV><<<rec, RecLayout<DK>::THREADS, 0, st>>>(a);
     int s = launch_status("gdn_prefill_bwd (states)");
     if (s != GDN_OK) return s;
-    bwd_dstate_kernel<DK, DV><<<rec, 32, 0, st>>>(a);
+    bwd_dstate_kernel<DK, DV><<<rec, RecLayout<DK>::THREADS, 0, st>>>(a);
     if ((s = launch_status("gdn_prefill_bwd (dstate)")) != GDN_OK) return s;
     bwd_token_kernel<DK, DV><<<static_cast<unsigned>(static_cast<long>(a.B) * a.H * a.T), 128, 0, st>>>(a);
     if ((s = launch_status("gdn_prefill_bwd (tokens)")) != GDN_OK) return s;
@@ -347,7 +372,7 @@ int launch_bwd(const BwdArgs& a, cudaStream_t st) {
 extern "C" size_t gdn_prefill_bwd_workspace_bytes(int B, int T, int H, int dk, int dv) {
     if (B <= 0 || T <= 0 || H <= 0 || !(dk == 64 || dk == 128) || !(dv == 64 || dv == 128)) return 0;
     const size_t tok = static_cast<size_t>(B) * H * T;
-    return 2 * tok * dk * dv * 4 + tok * dv * 4 + tok * 4 + 1024;
+    return 2 * tok * dk * dv * 4 + 2 * tok * dv * 4 + tok * 4 + 1024;
 }
 
 extern "C" int gdn_prefill_bwd(const void* q, const void* k, const void* v, const float* A_log, const void* a,
@@ -404,7 +429,8 @@ extern "C" int gdn_prefill_bwd(const void* q, const void* k, const void* v, cons
     ar.states = reinterpret_cast<float*>(ws);
     ar.dstates = reinterpret_cast<float*>(ws + tok * dkd * dvd * 4);
     ar.dd = reinterpret_cast<float*>(ws + 2 * tok * dkd * dvd * 4);
-    ar.dlogg = reinterpret_cast<float*>(ws + 2 * tok * dkd * dvd * 4 + tok * dvd * 4);
+    ar.rp = reinterpret_cast<float*>(ws + 2 * tok * dkd * dvd * 4 + tok * dvd * 4);
+    ar.dlogg = reinterpret_cast<float*>(ws + 2 * tok * dkd * dvd * 4 + 2 * tok * dvd * 4);
     ar.B = B;
     ar.T = T;
     ar.H = H;
