@@ -697,11 +697,14 @@ def run_only(args):
 
         def step():
             sharded_out_proj(y, W, buf, out=o)
-    elif args.only == "backward":
-        # config 1's head shape at B=1, T=1024: a 2.1 GB workspace, small enough to capture
-        inp = gen_prefill(1, 1024, C1["H"], C1["dk"], C1["dv"], 99, dev)
+    elif args.only in ("backward", "backward_config1"):
+        # "backward": config 1's head shape at B=1, T=1024, a 2.1 GB workspace, small enough
+        # for a multi-pass capture; "backward_config1": config 1 itself (34 GB workspace,
+        # duration-only launch lists)
+        Bb, Tb = (1, 1024) if args.only == "backward" else (C1["B"], C1["T"])
+        inp = gen_prefill(Bb, Tb, C1["H"], C1["dk"], C1["dv"], 99, dev)
         g = torch.Generator(device=dev).manual_seed(98)
-        dO = torch.randn(1, C1["H"], 1024, C1["dv"], generator=g, device=dev)
+        dO = torch.randn(Bb, C1["H"], Tb, C1["dv"], generator=g, device=dev)
 
         def step():
             ops.prefill_backward(inp["q"], inp["k"], inp["v"], inp["A_log"], inp["a"], inp["b"], dO,
@@ -729,7 +732,7 @@ def main(argv=None):
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--workload", choices=["prefill", "long"], default="prefill")
     ap.add_argument("--no-cpu-baseline", action="store_true")
-    ap.add_argument("--only", choices=["prefill", "decode", "proj", "layer_decode", "backward", "outproj"], default=None,
+    ap.add_argument("--only", choices=["prefill", "decode", "proj", "layer_decode", "backward", "backward_config1", "outproj"], default=None,
                     help="run just one kernel's workload (for profiling); prints a short JSON line")
     args = ap.parse_args(argv)
     if args.only:

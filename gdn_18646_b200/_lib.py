@@ -69,6 +69,8 @@ SIGNATURES = {
     "gdn_prefill_launch_count": [_I, _I, _I, _I, _I],
     "gdn_decode_step": [_P, _P, _P, _P, _P, _I, _P, _P, _P, _P, _P, _I, _I, _I, _I, _I, _F, _P],
     "gdn_decode_step_ex": [_P, _P, _P, _P, _P, _I, _P, _P, _P, _P, _P, _I, _I, _I, _I, _I, _F, _I, _P],
+    "gdn_decode_step_gated": [_P, _P, _P, _P, _P, _I, _P, _P, _P, _P, _P, _P, _P, _F, _P,
+                              _I, _I, _I, _I, _I, _F, _I, _P],
     "gdn_rmsnorm_fwd": [_P, _P, _P, _I, _I, _F, _P],
     "gdn_gated_rmsnorm_fwd": [_P, _I, _P, _P, _P, _I, _I, _F, _P],
     "gdn_decode_proj_fwd": [_P, _P, _F, _I, _I, ctypes.POINTER(ProjSegment), _I, _P],

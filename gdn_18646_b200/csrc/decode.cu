@@ -11,6 +11,11 @@
 // so the update S' = g*S + k delta^T is written straight from registers.
 // Every element is read before any is written by the same thread, so
 // state_out may alias state_in (in-place update).
+//
+// With a gate (y != null) the CTA also applies the layer's gated output norm to
+// its head's o row, which is exactly one norm group: y = (o * rsqrt(mean(o^2) +
+// eps)) * gamma * silu(z), bf16 (the gated RMSNorm of rmsnorm.cu on the same
+// row), so the output projection reads y without a norm launch in between.
 #include "common.cuh"
 
 namespace gdn {
@@ -30,14 +35,17 @@ __global__ void __launch_bounds__(DecodeCfg<DK, DV>::NT)
 decode_step_kernel(const uint16_t* q, const uint16_t* k, const uint16_t* v, const void* a, const void* b,
                    int gate_dtype, const float* __restrict__ A_log,
                    const float* __restrict__ dt_bias, const float* state_in, float* state_out,
-                   float* __restrict__ out, int Hqk, int Hv, float scale, int l2qk) {
+                   float* __restrict__ out, int Hqk, int Hv, float scale, int l2qk, const uint16_t* z,
+                   const uint16_t* __restrict__ gamma, float eps, uint16_t* __restrict__ y) {
     using C = DecodeCfg<DK, DV>;
+    constexpr int kNormWarps = (C::CG + 31) / 32;      // warps holding the row's rg == 0 threads
     __shared__ float q_s[DK];
     __shared__ float k_s[DK];
     __shared__ float red_a[C::RG][DV];
     __shared__ float red_b[C::RG][DV];
     __shared__ float qk_s;
     __shared__ float inv_s[2];
+    __shared__ float nrm_s[kNormWarps];
 
     pdl_launch_dependents();                   // the next kernel may launch (it waits for this one)
     pdl_wait_prior();                          // inputs and state come from earlier kernels
@@ -131,7 +139,7 @@ decode_step_kernel(const uint16_t* q, const uint16_t* k, const uint16_t* v, cons
         delta[c] = beta * (vj[c] - g * ka[c]);             // decode_ref.py:49-52
         oj[c] = scale * (g * qa[c] + delta[c] * qk);       // decode_ref.py:56
     }
-    if (rg == 0)
+    if (rg == 0 && out)
         *reinterpret_cast<float4*>(out + static_cast<long>(bh) * DV + 4 * cg) =
             make_float4(oj[0], oj[1], oj[2], oj[3]);
 
@@ -146,12 +154,45 @@ decode_step_kernel(const uint16_t* q, const uint16_t* k, const uint16_t* v, cons
         n.w = g * s[r].w + ki * delta[3];
         st_stream_f4(state_out + s_off + static_cast<long>(i) * DV + 4 * cg, n);
     }
+
+    if (y) {
+        // gated output norm of this head's row (the rg == 0 threads hold it, 4 columns each)
+        float ss = 0.f;
+        if (rg == 0) {
+#pragma unroll
+            for (int c = 0; c < 4; ++c) ss = fmaf(oj[c], oj[c], ss);
+        }
+        if (tid < 32 * kNormWarps) {
+#pragma unroll
+            for (int o = 16; o > 0; o >>= 1) ss += __shfl_xor_sync(0xffffffffu, ss, o);
+            if ((tid & 31) == 0) nrm_s[tid >> 5] = ss;
+        }
+        __syncthreads();
+        if (rg == 0) {
+            float tot = 0.f;
+#pragma unroll
+            for (int w = 0; w < kNormWarps; ++w) tot += nrm_s[w];
+            const float r = rsqrtf(tot / static_cast<float>(DV) + eps);
+            const uint2 gw = *reinterpret_cast<const uint2*>(gamma + 4 * cg);
+            const uint2 zw = __ldcg(reinterpret_cast<const uint2*>(z + static_cast<long>(bh) * DV + 4 * cg));
+            const float gf[4] = {bf16_bits_to_f32(gw.x & 0xffffu), bf16_bits_to_f32(gw.x >> 16),
+                                 bf16_bits_to_f32(gw.y & 0xffffu), bf16_bits_to_f32(gw.y >> 16)};
+            const float zf[4] = {bf16_bits_to_f32(zw.x & 0xffffu), bf16_bits_to_f32(zw.x >> 16),
+                                 bf16_bits_to_f32(zw.y & 0xffffu), bf16_bits_to_f32(zw.y >> 16)};
+            float yo[4];
+#pragma unroll
+            for (int c = 0; c < 4; ++c) yo[c] = (oj[c] * r) * gf[c] * silu_f(zf[c]);
+            *reinterpret_cast<uint2*>(y + static_cast<long>(bh) * DV + 4 * cg) =
+                make_uint2(pack_bf16x2(yo[0], yo[1]), pack_bf16x2(yo[2], yo[3]));
+        }
+    }
 }
 
 template <int DK, int DV>
 cudaError_t launch_decode(const void* q, const void* k, const void* v, const void* a, const void* b,
                    int gate_dtype, const float* A_log, const float* dt_bias, const float* s_in,
-                   float* s_out, float* out, int B, int Hqk, int Hv, float scale, int l2qk, cudaStream_t st) {
+                   float* s_out, float* out, int B, int Hqk, int Hv, float scale, int l2qk, const void* z,
+                   const void* gamma, float eps, void* y, cudaStream_t st) {
     using C = DecodeCfg<DK, DV>;
     cudaLaunchConfig_t cfg = {};
     cfg.gridDim = dim3(B * Hv);
@@ -164,47 +205,48 @@ cudaError_t launch_decode(const void* q, const void* k, const void* v, const voi
     cfg.numAttrs = launch_overlap() ? 1 : 0;
     return cudaLaunchKernelEx(&cfg, decode_step_kernel<DK, DV>, static_cast<const uint16_t*>(q),
                        static_cast<const uint16_t*>(k), static_cast<const uint16_t*>(v), a, b, gate_dtype, A_log,
-                       dt_bias, s_in, s_out, out, Hqk, Hv, scale, l2qk);
+                       dt_bias, s_in, s_out, out, Hqk, Hv, scale, l2qk, static_cast<const uint16_t*>(z),
+                       static_cast<const uint16_t*>(gamma), eps, static_cast<uint16_t*>(y));
 }
 
 }  // namespace
 }  // namespace gdn
 
-extern "C" int gdn_decode_step_ex(const void* q, const void* k, const void* v, const void* a,
-                                  const void* b, int gate_dtype, const float* A_log,
-                                  const float* dt_bias, const float* state_in, float* state_out,
-                                  float* out, int B, int Hqk, int Hv, int dk, int dv, float scale,
-                                  int flags, void* stream) {
+namespace {
+int decode_common(const char* name, const void* q, const void* k, const void* v, const void* a, const void* b,
+                  int gate_dtype, const float* A_log, const float* dt_bias, const float* state_in, float* state_out,
+                  float* out, const void* z, const void* gamma, float eps, void* y, int B, int Hqk, int Hv, int dk,
+                  int dv, float scale, int flags, void* stream) {
     using namespace gdn;
-    if (flags & ~GDN_DECODE_L2NORM_QK)
-        return fail(GDN_ERR_DTYPE, "gdn_decode_step: unknown flags 0x%x", flags);
+    if (flags & ~GDN_DECODE_L2NORM_QK) return fail(GDN_ERR_DTYPE, "%s: unknown flags 0x%x", name, flags);
     const int l2qk = (flags & GDN_DECODE_L2NORM_QK) ? 1 : 0;
-    if (!q || !k || !v || !a || !b || !A_log || !state_in || !state_out || !out)
-        return fail(GDN_ERR_NULL, "gdn_decode_step: q, k, v, a, b, A_log, state_in, state_out and out are required");
+    if (!q || !k || !v || !a || !b || !A_log || !state_in || !state_out || (!out && !y))
+        return fail(GDN_ERR_NULL, "%s: q, k, v, a, b, A_log, state_in, state_out and an output are required", name);
+    if (y && (!z || !gamma)) return fail(GDN_ERR_NULL, "%s: the gated norm needs z and norm_gamma", name);
     if (B <= 0 || Hqk <= 0 || Hv <= 0 || Hv % Hqk != 0)
-        return fail(GDN_ERR_SHAPE, "gdn_decode_step: bad B=%d Hqk=%d Hv=%d (need B,H > 0 and Hv %% Hqk == 0)", B, Hqk, Hv);
-    if (static_cast<long>(B) * Hv > 0x7fffffffL)
-        return fail(GDN_ERR_SHAPE, "gdn_decode_step: B*Hv too large");
+        return fail(GDN_ERR_SHAPE, "%s: bad B=%d Hqk=%d Hv=%d (need B,H > 0 and Hv %% Hqk == 0)", name, B, Hqk, Hv);
+    if (static_cast<long>(B) * Hv > 0x7fffffffL) return fail(GDN_ERR_SHAPE, "%s: B*Hv too large", name);
     if (gate_dtype != GDN_DTYPE_BF16 && gate_dtype != GDN_DTYPE_F32)
-        return fail(GDN_ERR_DTYPE, "gdn_decode_step: gate_dtype must be GDN_DTYPE_BF16 or GDN_DTYPE_F32");
+        return fail(GDN_ERR_DTYPE, "%s: gate_dtype must be GDN_DTYPE_BF16 or GDN_DTYPE_F32", name);
     const bool ok_dims = (dk == 64 || dk == 128 || dk == 256) && (dv == 64 || dv == 128 || dv == 256);
     if (!ok_dims)
-        return fail(GDN_ERR_UNSUPPORTED, "gdn_decode_step: dk=%d dv=%d not supported (each must be 64, 128 or 256)", dk, dv);
-    if (!aligned16(state_in) || !aligned16(state_out) || !aligned16(out) || !aligned16(q) || !aligned16(k) ||
+        return fail(GDN_ERR_UNSUPPORTED, "%s: dk=%d dv=%d not supported (each must be 64, 128 or 256)", name, dk, dv);
+    if (!aligned16(state_in) || !aligned16(state_out) || (out && !aligned16(out)) || !aligned16(q) || !aligned16(k) ||
         (reinterpret_cast<uintptr_t>(v) & 7u))
-        return fail(GDN_ERR_ALIGN, "gdn_decode_step: state/out/q/k must be 16-byte aligned and v 8-byte aligned");
+        return fail(GDN_ERR_ALIGN, "%s: state/out/q/k must be 16-byte aligned and v 8-byte aligned", name);
+    if (y && ((reinterpret_cast<uintptr_t>(y) | reinterpret_cast<uintptr_t>(z) | reinterpret_cast<uintptr_t>(gamma)) & 7u))
+        return fail(GDN_ERR_ALIGN, "%s: z, norm_gamma and y must be 8-byte aligned", name);
     int st = check_sm100();
     if (st != GDN_OK) return st;
     if (scale == 0.f) scale = 1.f / sqrtf(static_cast<float>(dk));
     cudaStream_t s = static_cast<cudaStream_t>(stream);
-#define GDN_DEC(DKV, DVV)                                                                     \
-    if (dk == DKV && dv == DVV) {                                                             \
-        const cudaError_t e = launch_decode<DKV, DVV>(q, k, v, a, b, gate_dtype, A_log, dt_bias,  \
-                                                      state_in, state_out, out, B, Hqk, Hv, scale, \
-                                                      l2qk, s);                                   \
-        if (e != cudaSuccess)                                                                 \
-            return fail(GDN_ERR_CUDA, "gdn_decode_step: launch failed: %s", cudaGetErrorString(e)); \
-        return launch_status("gdn_decode_step");                                              \
+#define GDN_DEC(DKV, DVV)                                                                          \
+    if (dk == DKV && dv == DVV) {                                                                  \
+        const cudaError_t e = launch_decode<DKV, DVV>(q, k, v, a, b, gate_dtype, A_log, dt_bias,   \
+                                                      state_in, state_out, out, B, Hqk, Hv, scale,  \
+                                                      l2qk, z, gamma, eps, y, s);                   \
+        if (e != cudaSuccess) return fail(GDN_ERR_CUDA, "%s: launch failed: %s", name, cudaGetErrorString(e)); \
+        return launch_status(name);                                                                \
     }
     GDN_DEC(64, 64)
     GDN_DEC(64, 128)
@@ -216,7 +258,28 @@ extern "C" int gdn_decode_step_ex(const void* q, const void* k, const void* v, c
     GDN_DEC(256, 128)
     GDN_DEC(256, 256)
 #undef GDN_DEC
-    return fail(GDN_ERR_UNSUPPORTED, "gdn_decode_step: unreachable dims");
+    return fail(GDN_ERR_UNSUPPORTED, "%s: unreachable dims", name);
+}
+}  // namespace
+
+extern "C" int gdn_decode_step_ex(const void* q, const void* k, const void* v, const void* a,
+                                  const void* b, int gate_dtype, const float* A_log,
+                                  const float* dt_bias, const float* state_in, float* state_out,
+                                  float* out, int B, int Hqk, int Hv, int dk, int dv, float scale,
+                                  int flags, void* stream) {
+    if (!out) return gdn::fail(GDN_ERR_NULL, "gdn_decode_step: out is required");
+    return decode_common("gdn_decode_step", q, k, v, a, b, gate_dtype, A_log, dt_bias, state_in, state_out, out,
+                         nullptr, nullptr, 0.f, nullptr, B, Hqk, Hv, dk, dv, scale, flags, stream);
+}
+
+extern "C" int gdn_decode_step_gated(const void* q, const void* k, const void* v, const void* a, const void* b,
+                                     int gate_dtype, const float* A_log, const float* dt_bias,
+                                     const float* state_in, float* state_out, float* out, const void* z,
+                                     const void* norm_gamma, float eps, void* y, int B, int Hqk, int Hv, int dk,
+                                     int dv, float scale, int flags, void* stream) {
+    if (!y) return gdn::fail(GDN_ERR_NULL, "gdn_decode_step_gated: y is required");
+    return decode_common("gdn_decode_step_gated", q, k, v, a, b, gate_dtype, A_log, dt_bias, state_in, state_out,
+                         out, z, norm_gamma, eps, y, B, Hqk, Hv, dk, dv, scale, flags, stream);
 }
 
 extern "C" int gdn_decode_step(const void* q, const void* k, const void* v, const void* a,

@@ -125,12 +125,13 @@ class GDNLayer:
         state is updated in place; conv histories go to ``out_state`` (fresh
         buffers by default; ``out_state=state`` updates them in place too).
 
-        Four launches: RMSNorm + q|k|v (conv4, SiLU) + z + a + b as one
+        Three launches: RMSNorm + q|k|v (conv4, SiLU) + z + a + b as one
         weight-streaming GEMV over the cached conv history (gdn_decode_proj_fwd),
-        the recurrence step with the q/k L2 norm folded in (so the GEMV needs no
-        cross-CTA reduction), the gated output norm, and the output projection
-        (the same GEMV kernel).  All shapes are static, so
-        the call can be captured in a CUDA graph."""
+        the recurrence step with the q/k L2 norm and the gated output norm folded
+        in (gdn_decode_step_gated; the GEMV needs no cross-CTA reduction and the
+        output projection reads y directly), and the output projection (the same
+        GEMV kernel).  All shapes are static, so the call can be captured in a
+        CUDA graph."""
         c, w = self.cfg, self.w
         B = x.shape[0]
         D = c.hidden
@@ -146,10 +147,10 @@ class GDNLayer:
             dict(W=w["W_ab"][:c.n_v]),
             dict(W=w["W_ab"][c.n_v:]),
         ], norm_gamma=w["norm_gamma"], eps=c.eps)
-        o = ops.decode_step(q.view(B, c.n_qk, c.dk), k.view(B, c.n_qk, c.dk), v.view(B, c.n_v, c.dv), a, b,
-                            w["A_log"], w["dt_bias"], state["recurrent"], scale=self.scale,
-                            state_out=out_state["recurrent"], l2norm_qk=True)
-        y = ops.gated_rmsnorm(o.view(B * c.n_v, c.dv), z.view(B * c.n_v, c.dv), w["onorm_gamma"], c.eps)
+        y = ops.decode_step_gated(q.view(B, c.n_qk, c.dk), k.view(B, c.n_qk, c.dk), v.view(B, c.n_v, c.dv), a, b,
+                                  w["A_log"], w["dt_bias"], state["recurrent"], z.view(B, c.n_v, c.dv),
+                                  w["onorm_gamma"], c.eps, scale=self.scale, state_out=out_state["recurrent"],
+                                  l2norm_qk=True)
         (out,) = ops.decode_proj(y.view(B, c.v_dim), [dict(W=w["W_o"])])
         return out.view(B, 1, D), out_state
 

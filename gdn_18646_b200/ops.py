@@ -304,6 +304,29 @@ def decode_step(q, k, v, a, b, A_log, dt_bias, state, *, scale=0.0, out=None, st
     return out
 
 
+def decode_step_gated(q, k, v, a, b, A_log, dt_bias, state, z, norm_gamma, eps, *, scale=0.0, y=None,
+                      out=None, state_out=None, l2norm_qk=False):
+    """``decode_step`` with the layer's gated output norm applied to each head's o row in
+    the same kernel (gdn_decode_step_gated): y = rmsnorm_dv(o) * norm_gamma * silu(z), bf16.
+    z [B,Hv,dv] bf16; norm_gamma [dv] bf16.  ``out`` (the fp32 o) is written only when
+    given.  Returns y [B,Hv,dv] bf16."""
+    B, Hqk, dk = q.shape
+    Hv, dv = v.shape[1], v.shape[2]
+    for name, t in (("q", q), ("k", k), ("v", v), ("z", z), ("norm_gamma", norm_gamma)):
+        _cuda_contig(t, name, torch.bfloat16)
+    _cuda_contig(state, "state", torch.float32)
+    _need(z.numel() == B * Hv * dv and norm_gamma.numel() == dv, "z must be [B, Hv, dv] and norm_gamma [dv]")
+    gdt = _gate_dtype(a, "a")
+    if y is None:
+        y = torch.empty(B, Hv, dv, dtype=torch.bfloat16, device=q.device)
+    if state_out is None:
+        state_out = state
+    _lib.call("gdn_decode_step_gated", _ptr(q), _ptr(k), _ptr(v), _ptr(a), _ptr(b), gdt, _ptr(A_log),
+              _ptr(dt_bias), _ptr(state), _ptr(state_out), _ptr(out), _ptr(z), _ptr(norm_gamma), float(eps),
+              _ptr(y), B, Hqk, Hv, dk, dv, float(scale), _lib.GDN_DECODE_L2NORM_QK if l2norm_qk else 0, _stream())
+    return y
+
+
 def outproj_rs(x, W, recv_ptrs, rank, world):
     """This rank's share of a head-sharded output projection, sent to its owners
     (gdn_outproj_rs_fwd): the partial product x [M, K] @ W[N, K]^T, cut into row

@@ -288,6 +288,22 @@ int gdn_decode_step_ex(const void* q, const void* k, const void* v,
                        int B, int Hqk, int Hv, int dk, int dv, float scale, int flags, void* stream);
 
 /*
+ * gdn_decode_step_ex followed by the layer's gated output norm of each head's o
+ * row, in the same kernel: y = (o * rsqrt(mean(o^2) + eps)) * norm_gamma *
+ * silu(z), bf16 (gdn_gated_rmsnorm_fwd over rows of dv with an fp32 o, up to the
+ * order of the fp32 sum of squares).  z bf16 [B, Hv, dv], norm_gamma bf16 [dv],
+ * y bf16 [B, Hv, dv], all 8-byte aligned; out (the fp32 o) may be NULL.  Saves
+ * the norm launch between the recurrence and the output projection of a decode
+ * step.  No reference counterpart (the reference layer norms in its own glue).
+ */
+int gdn_decode_step_gated(const void* q, const void* k, const void* v,
+                          const void* a, const void* b, int gate_dtype,
+                          const float* A_log, const float* dt_bias,
+                          const float* state_in, float* state_out, float* out,
+                          const void* z, const void* norm_gamma, float eps, void* y,
+                          int B, int Hqk, int Hv, int dk, int dv, float scale, int flags, void* stream);
+
+/*
  * RMSNorm, bf16 in/out, fp32 math: y = x * rsqrt(mean(x^2) + eps) * gamma.
  * Replaces rmsnorm_forward(), kernels/rmsnorm.cu:280-293 (math: reference/rmsnorm_ref.py:9-28).
  * x, y bf16 [R, D]; gamma bf16 [D].  D % 8 == 0, D <= 8192 (D <= 4096 when x is f32).

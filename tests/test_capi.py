@@ -288,3 +288,16 @@ def test_prefill_host_plan_segments(lib, T):
         assert lens == [1024, 1024, 1024, 512, 256, 128, 64, 64]
     uni = _plan(lib, 4, T, 16, 128)                      # explicit: uniform, ragged last
     assert uni == list(range(0, T, 128)) + [T]
+
+
+def test_decode_step_gated_rejects(lib):
+    base = [FAKE, FAKE, FAKE, FAKE, FAKE, 0, FAKE, None, FAKE, FAKE, None]
+    def call(z=FAKE, gamma=FAKE, y=FAKE, dk=128, flags=0):
+        return _lib.call_status("gdn_decode_step_gated", *base, z, gamma, 1e-6, y, 1, 1, 1, dk, 128, 0.0, flags, None)
+    assert call(y=None) == _lib.GDN_ERR_NULL
+    assert call(z=None) == _lib.GDN_ERR_NULL
+    assert call(gamma=None) == _lib.GDN_ERR_NULL
+    assert call(dk=96) == _lib.GDN_ERR_UNSUPPORTED
+    assert call(flags=8) == _lib.GDN_ERR_DTYPE
+    assert call(y=ODD) == _lib.GDN_ERR_ALIGN
+    assert "gdn_decode_step_gated" in _lib.last_error()

@@ -150,3 +150,41 @@ def test_decode_reference_module_surface(cuda_device):
     torch.cuda.synchronize()
     np.testing.assert_allclose(to_np(o), g["o"], rtol=1e-4, atol=1e-7)
     np.testing.assert_allclose(to_np(S_out), g["state_out"], rtol=1e-4, atol=1e-7)
+
+
+@pytest.mark.parametrize("dk,dv,l2", [(128, 128, True), (64, 256, False), (256, 64, True), (128, 64, False)])
+def test_decode_gated_norm_fused(cuda_device, dk, dv, l2):
+    """gdn_decode_step_gated: the step plus the gated output norm of each head's o row
+    in one kernel.  The state and the fp32 o are the plain step's, bit for bit; y is
+    gdn_gated_rmsnorm_fwd's on the same o up to the order of the fp32 sum of squares
+    (one bf16 ulp at most)."""
+    import torch
+    from gdn_18646_b200 import ops
+    rng = np.random.default_rng(dk * 3 + dv)
+    B, Hqk, Hv = 3, 2, 4
+    q = O.f32_to_bf16(rng.standard_normal((B, Hqk, dk), dtype=np.float32) * np.float32(0.3))
+    k = O.f32_to_bf16(rng.standard_normal((B, Hqk, dk), dtype=np.float32) * np.float32(0.3))
+    v = O.f32_to_bf16(rng.standard_normal((B, Hv, dv), dtype=np.float32))
+    a = O.f32_to_bf16(rng.standard_normal((B, Hv), dtype=np.float32))
+    b = O.f32_to_bf16(rng.standard_normal((B, Hv), dtype=np.float32))
+    z = O.f32_to_bf16(rng.standard_normal((B, Hv, dv), dtype=np.float32))
+    gamma = O.f32_to_bf16(1.0 + 0.3 * rng.standard_normal(dv, dtype=np.float32))
+    S = rng.standard_normal((B, Hv, dk, dv), dtype=np.float32) * np.float32(0.02)
+    A_log = np.full((Hv,), math.log(0.1), np.float32)
+    dtb = (0.1 * rng.standard_normal(Hv)).astype(np.float32)
+    args = [to_dev(x) for x in (q, k, v, a, b, A_log, dtb)]
+    S1, S2 = to_dev(S), to_dev(S)
+    o1 = ops.decode_step(*args, S1, l2norm_qk=l2)
+    y1 = ops.gated_rmsnorm(o1.view(B * Hv, dv), to_dev(z).view(B * Hv, dv), to_dev(gamma), 1e-6)
+    o2 = torch.empty_like(o1)
+    y2 = ops.decode_step_gated(*args, S2, to_dev(z), to_dev(gamma), 1e-6, out=o2, l2norm_qk=l2)
+    torch.cuda.synchronize()
+    assert torch.equal(S1, S2) and torch.equal(o1, o2)
+    y1f, y2f = y1.float().view(-1), y2.float().view(-1)
+    ulp = torch.clamp(y1f.abs(), min=1e-30) * 2.0 ** -7
+    assert bool(((y1f - y2f).abs() <= ulp + 1e-30).all())
+    # without the fp32 o: same y
+    S3 = to_dev(S)
+    y3 = ops.decode_step_gated(*args, S3, to_dev(z), to_dev(gamma), 1e-6, l2norm_qk=l2)
+    torch.cuda.synchronize()
+    assert torch.equal(y3, y2) and torch.equal(S3, S2)
