@@ -81,6 +81,13 @@ decode_step_kernel(const uint16_t* q, const uint16_t* k, const uint16_t* v, cons
     const float g = expf(-expf(A_log[h]) * softplus_f(av + dtb));
     const float beta = sigmoid_f(bv);
     const uint2 vraw = __ldcg(reinterpret_cast<const uint2*>(v + static_cast<long>(bh) * DV + 4 * cg));
+    // the gated norm's z and gamma, fetched with the other inputs so their latency hides
+    // behind the state loads
+    uint2 zw = make_uint2(0u, 0u), gw = make_uint2(0u, 0u);
+    if (y && rg == 0) {
+        zw = __ldcg(reinterpret_cast<const uint2*>(z + static_cast<long>(bh) * DV + 4 * cg));
+        gw = *reinterpret_cast<const uint2*>(gamma + 4 * cg);
+    }
     __syncthreads();
     if (l2qk) {
         // q, k L2-normalised per head (fp32, eps 1e-6) and rounded to bf16, as the
@@ -173,8 +180,6 @@ decode_step_kernel(const uint16_t* q, const uint16_t* k, const uint16_t* v, cons
 #pragma unroll
             for (int w = 0; w < kNormWarps; ++w) tot += nrm_s[w];
             const float r = rsqrtf(tot / static_cast<float>(DV) + eps);
-            const uint2 gw = *reinterpret_cast<const uint2*>(gamma + 4 * cg);
-            const uint2 zw = __ldcg(reinterpret_cast<const uint2*>(z + static_cast<long>(bh) * DV + 4 * cg));
             const float gf[4] = {bf16_bits_to_f32(gw.x & 0xffffu), bf16_bits_to_f32(gw.x >> 16),
                                  bf16_bits_to_f32(gw.y & 0xffffu), bf16_bits_to_f32(gw.y >> 16)};
             const float zf[4] = {bf16_bits_to_f32(zw.x & 0xffffu), bf16_bits_to_f32(zw.x >> 16),
