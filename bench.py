@@ -446,8 +446,8 @@ def run_varlen(world, dev, stream):
 
 def run_backward(world, dev, stream, hbm_peak):
     """Config 1's backward (gdn_prefill_bwd): B=4, T=4096, H=16, dk=dv=128, fp32 dO and
-    a final-state gradient.  Its kernels store and reload every token's state and
-    state gradient (fp32): the traffic per call is ~4 x B*H*T*dk*dv*4 bytes."""
+    a final-state gradient.  Its kernels store and reload every token's state (fp32):
+    the state traffic per call is ~2 x B*H*T*dk*dv*4 bytes."""
     import torch
     from gdn_18646_b200 import ops
     c = C1
@@ -463,9 +463,9 @@ def run_backward(world, dev, stream, hbm_peak):
     ms = timed(step, 3, 1, world, stream) / 3
     toks = c["B"] * c["T"]
     state_bytes = c["B"] * c["H"] * c["T"] * c["dk"] * c["dv"] * 4
-    traffic = 4 * state_bytes                        # states and state gradients, written once and read once
+    traffic = 2 * state_bytes                        # states, written once and read once
     return {"config": "config1 backward: B=4 T=4096 H=16 dk=dv=128, fp32 dO + final-state gradient",
-            "ms": ms, "tokens_per_s": toks / (ms * 1e-3), "workspace_gb": 2 * state_bytes / 1e9,
+            "ms": ms, "tokens_per_s": toks / (ms * 1e-3), "workspace_gb": state_bytes / 1e9,
             "state_traffic_gbs": traffic / (ms * 1e-3) / 1e9,
             "state_traffic_frac_of_measured_hbm": traffic / (ms * 1e-3) / 1e9 / hbm_peak}
 

@@ -3,26 +3,26 @@
 //
 // The reference has no backward.  This is the token-recurrent derivative (the
 // same recurrence as the forward, per token: S' = g S_p, r = S'^T k,
-// d = b'(v - r), S_n = S' + k d^T, o = m scale q^T S_n), computed by three
-// kernels over a workspace that holds every token's state:
+// d = b'(v - r), S_n = S' + k d^T, o = m scale q^T S_n), in four launches:
 //
-//   bwd_states_kernel  the forward recurrence again, storing the state S_p
-//                      before every token (fp32 [B,H,T,dk,dv]);
-//   bwd_dstate_kernel  the reverse recurrence of dS (the gradient of S_n):
-//                      dS += scale q (m dO)^T, dd = dS^T k, dS <- g (dS - b' k dd^T),
-//                      storing dS for every token, dv = b' dd and dd itself;
-//   bwd_token_kernel   every token independently, from S_p and dS: dq, dk, the
-//                      gate gradients (dg = <S_p, dS + k dr^T>, db') and their
-//                      chain rule through g = exp(-exp(A_log) softplus(a + dt_bias))
-//                      and b' = sigmoid(b) m;
-//   bwd_head_kernel    dA_log and ddt_bias, summed per head in token order.
+//   bwd_states_kernel   the forward recurrence again, storing the state S_p
+//                       before every token (fp32 [B,H,T,dk,dv]) and k . S_p per
+//                       value column;
+//   bwd_reverse_kernel  the reverse recurrence of dS (the gradient of S_n):
+//                       dS += scale q (m dO)^T, dd = dS^T k, dv = b' dd,
+//                       dS <- g (dS - b' k dd^T); per token it also reads S_p and
+//                       leaves, per block of value columns, the row sums of
+//                       S_p (m dO) and dS delta + g S_p dr and the scalars of
+//                       db' and dg (dg = <S_p, dS + k dr^T>), so dS is never stored;
+//   bwd_finish_kernel   per token, those partials summed over the column blocks:
+//                       dq, dk, and the chain rule through g = exp(-exp(A_log)
+//                       softplus(a + dt_bias)) and b' = sigmoid(b) m into da, db;
+//   bwd_head_kernel     dA_log and ddt_bias, summed per head in token order.
 //
-// The two recurrences keep (half) a value column of the state per thread (64
-// registers), so their reductions stay inside a warp; a warp writes state rows
-// as 64- or 128-byte segments.  All arithmetic is
-// fp32 on CUDA cores; the kernels are bound by the workspace traffic
-// (2 x 4 dk dv bytes per token and head, written once and read once).
-// Restates oracle prefill_backward (pinned to finite differences).
+// The recurrences keep 32 rows of a value column per thread, so their column
+// reductions stay inside a warp; fp32 on CUDA cores throughout.  The traffic is
+// the state workspace, written once and read once (2 x 4 dk dv bytes per token
+// and head).  Restates oracle prefill_backward (pinned to finite differences).
 #include "common.cuh"
 
 namespace gdn {
@@ -52,9 +52,8 @@ struct BwdArgs {
     float* ddt_bias;           // [H] f32
     float* dstate_in;          // [B,H,DK,DV] f32 or null
     float* states;             // workspace: S_p per token [B,H,T,DK,DV]
-    float* dstates;            // workspace: dS per token
-    float* dd;                 // workspace: [B,H,T,DV]
     float* rp;                 // workspace: [B,H,T,DV], k . S_p per value column
+    float* part;               // workspace: per token and column block, row sums and scalars
     float* dlogg;              // workspace: [B,H,T]
     int B, T, H;
     float scale;
@@ -152,26 +151,73 @@ __global__ void __launch_bounds__(128) bwd_states_kernel(const BwdArgs a) {
     }
 }
 
-// Reverse recurrence of dS, storing dS (gradient of S_n) per token, dv and dd.  Grid (B*H, DV/CTA_COLS).
+// Partial sums a reverse CTA leaves per token: X_i = S_p[i,:].(m dO), Y_i = dS[i,:].delta
+// + g S_p[i,:].dr over its columns, then p_db = dd.(v - r), p_ddo = delta.(m dO),
+// p_rdr = dr.rp, p_sds = <S_p, dS>.
+template <int DK>
+struct PartLayout {
+    static constexpr int STRIDE = 2 * DK + 4;
+};
+
+// Sum 32 per-row values over the COLS lanes of a warp that share rows (lanes
+// p*COLS + jl, jl < COLS): a butterfly reduce-scatter, after which lane jl holds
+// the sums of rows (32/COLS) * jl + t, t < 32/COLS, in v[t].
+template <int COLS>
+__device__ __forceinline__ void rows_reduce_scatter(float (&v)[32], int jl) {
+    int n = 32;
+#pragma unroll
+    for (int m = COLS / 2; m >= 1; m >>= 1) {
+        n >>= 1;
+        const bool upper = (jl & m) != 0;
+#pragma unroll
+        for (int t = 0; t < 16; ++t) {
+            if (t < n) {
+                const float send = upper ? v[t] : v[t + n];
+                const float keep = upper ? v[t + n] : v[t];
+                v[t] = keep + __shfl_xor_sync(0xffffffffu, send, m);
+            }
+        }
+    }
+}
+
+constexpr int kRevTB = 16;   // tokens the reverse recurrence stages at once
+
+// Reverse recurrence of dS (the gradient of S_n) with every token's dq/dk/gate
+// work folded in, so no per-token dS is stored.  Per token: dS += scale q (m dO)^T,
+// dd = dS^T k, dv = b' dd; with S_p from the forward pass, this CTA's partial row
+// sums X, Y and scalars go to the workspace (summed over column blocks by
+// bwd_finish_kernel); then dS <- g (dS - b' k dd^T).  Grid (B*H, DV/CTA_COLS).
 template <int DK, int DV>
-__global__ void __launch_bounds__(128) bwd_dstate_kernel(const BwdArgs a) {
+__global__ void __launch_bounds__(128) bwd_reverse_kernel(const BwdArgs a) {
     using L = RecLayout<DK>;
+    constexpr int NCB = DV / L::CTA_COLS, PST = PartLayout<DK>::STRIDE, RPL = L::ROWS / L::COLS;
     const int bh = blockIdx.x, tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
     const int jl = lane % L::COLS;
     const int jc = warp * L::COLS + jl;
     const int j = blockIdx.y * L::CTA_COLS + jc;
     const int i0 = (lane / L::COLS) * L::ROWS;
     const int bi = bh / a.H;
-    __shared__ float ks[kTB][DK], qs[kTB][DK];
-    __shared__ float dos[kTB][L::CTA_COLS];
-    __shared__ float gs[kTB], bs[kTB];
+    __shared__ float ks[kRevTB][DK], qs[kRevTB][DK];
+    __shared__ float mdo[kRevTB][L::CTA_COLS], vv[kRevTB][L::CTA_COLS], rps[kRevTB][L::CTA_COLS];
+    __shared__ float gs[kRevTB], bs[kRevTB];
+    __shared__ float xr[2][L::WARPS][DK], yr[2][L::WARPS][DK];
+    __shared__ float scr[2][L::WARPS][4];
     float dS[L::ROWS];
     const long s0 = static_cast<long>(bh) * DK * DV;
 #pragma unroll
     for (int i = 0; i < L::ROWS; ++i)
         dS[i] = a.dS_final ? a.dS_final[s0 + static_cast<long>(i0 + i) * DV + j] : 0.f;
-    for (int tend = a.T; tend > 0; tend -= kTB) {
-        const int tb = max(0, tend - kTB), nt = tend - tb;
+    // S_p of the token processed next, loaded one token ahead (the loads are the
+    // long-latency part of a step)
+    float SpN[L::ROWS];
+    const long tok_first = static_cast<long>(bh) * a.T;
+    {
+        const float* sp = a.states + ((tok_first + a.T - 1) * DK + i0) * DV + j;
+#pragma unroll
+        for (int i = 0; i < L::ROWS; ++i) SpN[i] = sp[static_cast<long>(i) * DV];
+    }
+    for (int tend = a.T; tend > 0; tend -= kRevTB) {
+        const int tb = max(0, tend - kRevTB), nt = tend - tb;
         const long tok0 = static_cast<long>(bh) * a.T + tb;
         __syncthreads();
         for (int e = tid; e < nt * DK; e += L::THREADS) {
@@ -179,12 +225,13 @@ __global__ void __launch_bounds__(128) bwd_dstate_kernel(const BwdArgs a) {
             qs[e / DK][e % DK] = bf16_at(a.q, tok0 * DK + e);
         }
         for (int e = tid; e < nt * L::CTA_COLS; e += L::THREADS) {
-            const int u = e / L::CTA_COLS;
-            const long idx = (tok0 + u) * DV + blockIdx.y * L::CTA_COLS + e % L::CTA_COLS;
+            const int u = e / L::CTA_COLS, c = e % L::CTA_COLS;
+            const long idx = (tok0 + u) * DV + blockIdx.y * L::CTA_COLS + c;
             const float m = a.mask ? a.mask[static_cast<long>(bi) * a.T + tb + u] : 1.f;
-            dos[u][e % L::CTA_COLS] =
-                a.scale * m * (a.do_dtype == GDN_DTYPE_BF16 ? bf16_at(static_cast<const uint16_t*>(a.dO), idx)
-                                                             : static_cast<const float*>(a.dO)[idx]);
+            mdo[u][c] = m * (a.do_dtype == GDN_DTYPE_BF16 ? bf16_at(static_cast<const uint16_t*>(a.dO), idx)
+                                                          : static_cast<const float*>(a.dO)[idx]);
+            vv[u][c] = bf16_at(a.v, idx);
+            rps[u][c] = a.rp[idx];
         }
         if (tid < nt) gate_of(a, bh, tb + tid, gs[tid], bs[tid]);
         __syncthreads();
@@ -192,8 +239,18 @@ __global__ void __launch_bounds__(128) bwd_dstate_kernel(const BwdArgs a) {
             const long tok = tok0 + u;
             const float* kk = ks[u] + i0;
             const float* qq = qs[u] + i0;
-            const float sdo = dos[u][jc];
+            const float dos = mdo[u][jc];
+            const float sdo = a.scale * dos;
             const float g = gs[u], bm = bs[u];
+            // S_p of these rows (forward pass), loaded during the previous step; start the next
+            float Sp[L::ROWS];
+#pragma unroll
+            for (int i = 0; i < L::ROWS; ++i) Sp[i] = SpN[i];
+            if (tok > tok_first) {
+                const float* sp = a.states + ((tok - 1) * DK + i0) * DV + j;
+#pragma unroll
+                for (int i = 0; i < L::ROWS; ++i) SpN[i] = sp[static_cast<long>(i) * DV];
+            }
             float e0 = 0.f, e1 = 0.f, e2 = 0.f, e3 = 0.f;
 #pragma unroll
             for (int i = 0; i < L::ROWS; i += 4) {
@@ -206,15 +263,64 @@ __global__ void __launch_bounds__(128) bwd_dstate_kernel(const BwdArgs a) {
                 e2 = fmaf(kk[i + 2], dS[i + 2], e2);
                 e3 = fmaf(kk[i + 3], dS[i + 3], e3);
             }
-            float* out = a.dstates + (tok * DK + i0) * DV + j;
-#pragma unroll
-            for (int i = 0; i < L::ROWS; ++i) out[static_cast<long>(i) * DV] = dS[i];
             const float ddj = sum_parts<L::PARTS, L::COLS>((e0 + e1) + (e2 + e3));
-            if (i0 == 0) {
-                a.dd[tok * DV + j] = ddj;
-                a.dv[tok * DV + j] = bm * ddj;
+            if (i0 == 0) a.dv[tok * DV + j] = bm * ddj;
+            const float rp = rps[u][jc], vj = vv[u][jc];
+            const float r = g * rp, dlt = bm * (vj - r), dr = -bm * ddj;
+            // products for the row sums (dq, dk) and <S_p, dS>
+            float X[32], Y[32];
+            float sds = 0.f;
+#pragma unroll
+            for (int i = 0; i < L::ROWS; ++i) {
+                X[i] = Sp[i] * dos;
+                Y[i] = fmaf(dS[i], dlt, g * Sp[i] * dr);
+                sds = fmaf(Sp[i], dS[i], sds);
             }
-            const float dr = -bm * ddj;
+            float c0 = 0.f, c1 = 0.f, c2 = 0.f;        // column scalars, once per column
+            if (i0 == 0) {
+                c0 = ddj * (vj - r);
+                c1 = dlt * dos;
+                c2 = dr * rp;
+            }
+            rows_reduce_scatter<L::COLS>(X, jl);
+            rows_reduce_scatter<L::COLS>(Y, jl);
+#pragma unroll
+            for (int o = 16; o > 0; o >>= 1) {
+                c0 += __shfl_xor_sync(0xffffffffu, c0, o);
+                c1 += __shfl_xor_sync(0xffffffffu, c1, o);
+                c2 += __shfl_xor_sync(0xffffffffu, c2, o);
+                sds += __shfl_xor_sync(0xffffffffu, sds, o);
+            }
+            const int pb = u & 1;
+#pragma unroll
+            for (int t = 0; t < RPL; ++t) {
+                xr[pb][warp][i0 + RPL * jl + t] = X[t];
+                yr[pb][warp][i0 + RPL * jl + t] = Y[t];
+            }
+            if (lane == 0) {
+                scr[pb][warp][0] = c0;
+                scr[pb][warp][1] = c1;
+                scr[pb][warp][2] = c2;
+                scr[pb][warp][3] = sds;
+            }
+            __syncthreads();
+            float* pp = a.part + (tok * NCB + blockIdx.y) * PST;
+            for (int i = tid; i < DK; i += L::THREADS) {
+                float xs = 0.f, ys = 0.f;
+#pragma unroll
+                for (int w = 0; w < L::WARPS; ++w) {
+                    xs += xr[pb][w][i];
+                    ys += yr[pb][w][i];
+                }
+                pp[i] = xs;
+                pp[DK + i] = ys;
+            }
+            if (tid < 4) {
+                float t4 = 0.f;
+#pragma unroll
+                for (int w = 0; w < L::WARPS; ++w) t4 += scr[pb][w][tid];
+                pp[2 * DK + tid] = t4;
+            }
 #pragma unroll
             for (int i = 0; i < L::ROWS; ++i) dS[i] = g * fmaf(kk[i], dr, dS[i]);
         }
@@ -225,99 +331,43 @@ __global__ void __launch_bounds__(128) bwd_dstate_kernel(const BwdArgs a) {
     }
 }
 
-// Per token: dq, dk, da, db (and dlog g for the head sums), one pass over S_p and dS.
-// One CTA of 4 warps per token; every warp holds all DV columns (DV/32 per lane), so
-// the per-column vectors (r = g k.S_p from the forward pass, delta, dr, m dO) and
-// their sums are formed in registers, and each warp reduces its rows' products
-// (dq_i, dk_i) across its lanes while S_p and dS are read once, row by row.
+// Per token: the column blocks' partials summed into dq, dk, da, db (and dlog g for the
+// head sums).  One CTA of 128 threads per token.
 template <int DK, int DV>
-__global__ void __launch_bounds__(128) bwd_token_kernel(const BwdArgs a) {
-    constexpr int NW = 4, CPL = DV / 32;             // warps, columns per lane
+__global__ void __launch_bounds__(128) bwd_finish_kernel(const BwdArgs a) {
+    constexpr int NCB = DV / RecLayout<DK>::CTA_COLS, PST = PartLayout<DK>::STRIDE;
     const long tok = blockIdx.x;                  // bh * T + t
     const int bh = static_cast<int>(tok / a.T), t = static_cast<int>(tok - static_cast<long>(bh) * a.T);
     const int bi = bh / a.H, h = bh % a.H;
-    const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
-    __shared__ float red[NW];
+    const int tid = threadIdx.x;
+    const float* pp = a.part + tok * NCB * PST;
+    float sc[4] = {0.f, 0.f, 0.f, 0.f};
+#pragma unroll
+    for (int cb = 0; cb < NCB; ++cb)
+#pragma unroll
+        for (int q = 0; q < 4; ++q) sc[q] += pp[cb * PST + 2 * DK + q];
     float g, bm;
     gate_of(a, bh, t, g, bm);
-    const float m = a.mask ? a.mask[static_cast<long>(bi) * a.T + t] : 1.f;
-    // ---- per-column vectors of this lane's columns j = lane * CPL + c
-    float dlt[CPL], drs[CPL], dos[CPL];
-    float p_db = 0.f, p_ddo = 0.f, p_rdr = 0.f;
+    for (int i = tid; i < DK; i += 128) {
+        float X = 0.f, Y = 0.f;
 #pragma unroll
-    for (int c = 0; c < CPL; ++c) {
-        const int j = lane * CPL + c;
-        const float vj = bf16_at(a.v, tok * DV + j);
-        const float rp = a.rp[tok * DV + j];
-        const float ddj = a.dd[tok * DV + j];
-        const float r = g * rp;
-        dlt[c] = bm * (vj - r);
-        drs[c] = -bm * ddj;
-        dos[c] = m * (a.do_dtype == GDN_DTYPE_BF16 ? bf16_at(static_cast<const uint16_t*>(a.dO), tok * DV + j)
-                                                   : static_cast<const float*>(a.dO)[tok * DV + j]);
-        p_db = fmaf(ddj, vj - r, p_db);
-        p_ddo = fmaf(dlt[c], dos[c], p_ddo);
-        p_rdr = fmaf(drs[c], rp, p_rdr);
+        for (int cb = 0; cb < NCB; ++cb) {
+            X += pp[cb * PST + i];
+            Y += pp[cb * PST + DK + i];
+        }
+        a.dq[tok * DK + i] = a.scale * fmaf(g, X, bf16_at(a.k, tok * DK + i) * sc[1]);
+        a.dk[tok * DK + i] = Y;
     }
-#pragma unroll
-    for (int o = 16; o > 0; o >>= 1) {
-        p_db += __shfl_xor_sync(0xffffffffu, p_db, o);
-        p_ddo += __shfl_xor_sync(0xffffffffu, p_ddo, o);
-        p_rdr += __shfl_xor_sync(0xffffffffu, p_rdr, o);
-    }
-    // ---- rows i = warp, warp + NW, ...: dq_i = scale (g S_p[i,:].dO' + k_i (delta.dO')),
-    //      dk_i = dS[i,:].delta + g S_p[i,:].dr; <S_p, dS> accumulated for dg
-    const float* Sp = a.states + tok * DK * DV;
-    const float* dS = a.dstates + tok * DK * DV;
-    float p_sds = 0.f;
-    for (int i = warp; i < DK; i += NW) {
-        float s[CPL], ds[CPL];
-        if constexpr (CPL == 4) {
-            const float4 x = *reinterpret_cast<const float4*>(Sp + i * DV + lane * 4);
-            const float4 y = *reinterpret_cast<const float4*>(dS + i * DV + lane * 4);
-            s[0] = x.x; s[1] = x.y; s[2] = x.z; s[3] = x.w;
-            ds[0] = y.x; ds[1] = y.y; ds[2] = y.z; ds[3] = y.w;
-        } else {
-            const float2 x = *reinterpret_cast<const float2*>(Sp + i * DV + lane * 2);
-            const float2 y = *reinterpret_cast<const float2*>(dS + i * DV + lane * 2);
-            s[0] = x.x; s[1] = x.y;
-            ds[0] = y.x; ds[1] = y.y;
-        }
-        float sdo = 0.f, sdr = 0.f, dsd = 0.f;
-#pragma unroll
-        for (int c = 0; c < CPL; ++c) {
-            sdo = fmaf(s[c], dos[c], sdo);
-            sdr = fmaf(s[c], drs[c], sdr);
-            dsd = fmaf(ds[c], dlt[c], dsd);
-            p_sds = fmaf(s[c], ds[c], p_sds);
-        }
-#pragma unroll
-        for (int o = 16; o > 0; o >>= 1) {
-            sdo += __shfl_xor_sync(0xffffffffu, sdo, o);
-            sdr += __shfl_xor_sync(0xffffffffu, sdr, o);
-            dsd += __shfl_xor_sync(0xffffffffu, dsd, o);
-        }
-        if (lane == 0) {
-            const float ki = bf16_at(a.k, tok * DK + i);
-            a.dq[tok * DK + i] = a.scale * fmaf(g, sdo, ki * p_ddo);
-            a.dk[tok * DK + i] = fmaf(g, sdr, dsd);
-        }
-    }
-#pragma unroll
-    for (int o = 16; o > 0; o >>= 1) p_sds += __shfl_xor_sync(0xffffffffu, p_sds, o);
-    if (lane == 0) red[warp] = p_sds;
-    __syncthreads();
     if (tid == 0) {
-        float dg = p_rdr;                             // <S_p, dS + k dr^T> = <S_p, dS> + dr . rp
-#pragma unroll
-        for (int w = 0; w < NW; ++w) dg += red[w];
+        const float m = a.mask ? a.mask[static_cast<long>(bi) * a.T + t] : 1.f;
+        const float dg = sc[3] + sc[2];                // <S_p, dS + k dr^T> = <S_p, dS> + dr . rp
         const float dtb = a.dt_bias_vec ? a.dt_bias_vec[h] : a.dt_bias;
         const float x = load_gate(a.a, tok, a.gate_dtype) + dtb;
         const float dlogg = dg * g;
         a.dlogg[tok] = dlogg;
         a.da[tok] = dlogg * (-expf(a.A_log[h])) * (x > 20.f ? 1.f : sigmoid_f(x));
         const float sb = sigmoid_f(load_gate(a.b, tok, a.gate_dtype));
-        a.db[tok] = p_db * m * sb * (1.f - sb);
+        a.db[tok] = sc[0] * m * sb * (1.f - sb);
     }
 }
 
@@ -358,10 +408,10 @@ int launch_bwd(const BwdArgs& a, cudaStream_t st) {
     bwd_states_kernel<DK, DV><<<rec, RecLayout<DK>::THREADS, 0, st>>>(a);
     int s = launch_status("gdn_prefill_bwd (states)");
     if (s != GDN_OK) return s;
-    bwd_dstate_kernel<DK, DV><<<rec, RecLayout<DK>::THREADS, 0, st>>>(a);
-    if ((s = launch_status("gdn_prefill_bwd (dstate)")) != GDN_OK) return s;
-    bwd_token_kernel<DK, DV><<<static_cast<unsigned>(static_cast<long>(a.B) * a.H * a.T), 128, 0, st>>>(a);
-    if ((s = launch_status("gdn_prefill_bwd (tokens)")) != GDN_OK) return s;
+    bwd_reverse_kernel<DK, DV><<<rec, RecLayout<DK>::THREADS, 0, st>>>(a);
+    if ((s = launch_status("gdn_prefill_bwd (reverse)")) != GDN_OK) return s;
+    bwd_finish_kernel<DK, DV><<<static_cast<unsigned>(static_cast<long>(a.B) * a.H * a.T), 128, 0, st>>>(a);
+    if ((s = launch_status("gdn_prefill_bwd (finish)")) != GDN_OK) return s;
     bwd_head_kernel<<<a.H, 256, 0, st>>>(a);
     return launch_status("gdn_prefill_bwd (heads)");
 }
@@ -369,10 +419,29 @@ int launch_bwd(const BwdArgs& a, cudaStream_t st) {
 }  // namespace
 }  // namespace gdn
 
+namespace gdn {
+namespace {
+// Workspace: states [tok][dk][dv] | rp [tok][dv] | partials [tok][column blocks][2 dk + 4] | dlogg [tok]
+struct BwdWs {
+    size_t states, rp, part, dlogg, total;
+};
+BwdWs bwd_ws(size_t tok, int dk, int dv) {
+    const int cta_cols = dk == 128 ? RecLayout<128>::CTA_COLS : RecLayout<64>::CTA_COLS;
+    const size_t ncb = static_cast<size_t>(dv / cta_cols);
+    BwdWs w;
+    w.states = 0;
+    w.rp = w.states + tok * dk * dv * 4;
+    w.part = w.rp + tok * dv * 4;
+    w.dlogg = w.part + tok * ncb * (2 * dk + 4) * 4;
+    w.total = w.dlogg + tok * 4 + 1024;
+    return w;
+}
+}  // namespace
+}  // namespace gdn
+
 extern "C" size_t gdn_prefill_bwd_workspace_bytes(int B, int T, int H, int dk, int dv) {
     if (B <= 0 || T <= 0 || H <= 0 || !(dk == 64 || dk == 128) || !(dv == 64 || dv == 128)) return 0;
-    const size_t tok = static_cast<size_t>(B) * H * T;
-    return 2 * tok * dk * dv * 4 + 2 * tok * dv * 4 + tok * 4 + 1024;
+    return gdn::bwd_ws(static_cast<size_t>(B) * H * T, dk, dv).total;
 }
 
 extern "C" int gdn_prefill_bwd(const void* q, const void* k, const void* v, const float* A_log, const void* a,
@@ -426,11 +495,11 @@ extern "C" int gdn_prefill_bwd(const void* q, const void* k, const void* v, cons
     ar.dstate_in = dstate_in;
     const size_t tok = static_cast<size_t>(B) * H * T;
     uint8_t* ws = static_cast<uint8_t*>(workspace);
-    ar.states = reinterpret_cast<float*>(ws);
-    ar.dstates = reinterpret_cast<float*>(ws + tok * dkd * dvd * 4);
-    ar.dd = reinterpret_cast<float*>(ws + 2 * tok * dkd * dvd * 4);
-    ar.rp = reinterpret_cast<float*>(ws + 2 * tok * dkd * dvd * 4 + tok * dvd * 4);
-    ar.dlogg = reinterpret_cast<float*>(ws + 2 * tok * dkd * dvd * 4 + 2 * tok * dvd * 4);
+    const BwdWs wl = bwd_ws(tok, dkd, dvd);
+    ar.states = reinterpret_cast<float*>(ws + wl.states);
+    ar.rp = reinterpret_cast<float*>(ws + wl.rp);
+    ar.part = reinterpret_cast<float*>(ws + wl.part);
+    ar.dlogg = reinterpret_cast<float*>(ws + wl.dlogg);
     ar.B = B;
     ar.T = T;
     ar.H = H;

@@ -234,7 +234,7 @@ int gdn_prefill_host(const void* q, const void* k, const void* v,
  * No reference counterpart (the reference has no backward).  Token-recurrent
  * derivative of the same recurrence (per token S' = g S, r = S'^T k,
  * d = b'(v - r), S <- S' + k d^T, o = m scale q^T S), fp32 on CUDA cores, over
- * a workspace holding every token's state and state gradient.
+ * a workspace holding every token's state.
  *   q, k bf16 [B, H, T, dk]; v bf16 [B, H, T, dv]   (layout BHTD, Hqk == Hv)
  *   A_log f32 [H]; a, b_logits [B, H, T] in gate_dtype; dt_bias / dt_bias_vec as
  *   gdn_prefill_fwd; mask f32 [B, T] or NULL; state_in f32 [B, H, dk, dv] or NULL
@@ -243,7 +243,7 @@ int gdn_prefill_host(const void* q, const void* k, const void* v,
  *   dA_log, ddt_bias f32 [H] (per head; for a scalar dt_bias sum them);
  *   dstate_in f32 [B, H, dk, dv] or NULL.
  * dk, dv in {64, 128}.  Workspace: gdn_prefill_bwd_workspace_bytes(B, T, H, dk, dv)
- * (about 2 * B * H * T * dk * dv * 4 bytes), 16-byte aligned.
+ * (about B * H * T * dk * dv * 4 bytes), 16-byte aligned.
  */
 size_t gdn_prefill_bwd_workspace_bytes(int B, int T, int H, int dk, int dv);
 int gdn_prefill_bwd(const void* q, const void* k, const void* v, const float* A_log,
