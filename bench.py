@@ -362,7 +362,7 @@ def run_layer(world, dev, stream, hbm_peak):
     more than the 126 MB L2), so every layer-step streams its weights from
     HBM as in a deep model; the time is per layer-step."""
     import torch
-    from gdn_18646_b200.layer import DecodeGraph, GDNConfig, GDNLayer, make_weights
+    from gdn_18646_b200.layer import DecodeGraph, DecodeStackGraph, GDNConfig, GDNLayer, make_weights
     cfg = GDNConfig()
     n_layers = 4
     layers = [GDNLayer(make_weights(cfg, device=dev, seed=3 + i), cfg) for i in range(n_layers)]
@@ -382,6 +382,14 @@ def run_layer(world, dev, stream, hbm_peak):
                 graph.step(xd[t])
 
     ms_dec = timed(decode_all, 3, 1, world, stream) / (3 * n_dec * n_layers)
+    # the same steps with the 4 layers in one graph (each layer's output feeding the next)
+    stack = DecodeStackGraph(layers, [gr.state for gr in graphs], B)
+
+    def decode_stack():
+        for t in range(n_dec):
+            stack.step(xd[t])
+
+    ms_stack = timed(decode_stack, 3, 1, world, stream) / (3 * n_dec * n_layers)
     w_bytes = sum(v.numel() * v.element_size() for k_, v in layers[0].w.items() if k_.startswith("W_"))
     state_bytes = 2 * B * cfg.n_v * cfg.dk * cfg.dv * 4
     return {"config": "config3 layer: prefill x [2, 8192, 2048], then 128 decode steps through 4 layers with "
@@ -390,7 +398,9 @@ def run_layer(world, dev, stream, hbm_peak):
             "decode_ms_per_layer_step": ms_dec, "decode_tokens_per_s_per_layer": B / (ms_dec * 1e-3),
             "decode_bytes_per_layer_step": w_bytes + state_bytes,
             "decode_gbs": (w_bytes + state_bytes) / (ms_dec * 1e-3) / 1e9,
-            "decode_frac_of_measured_hbm": (w_bytes + state_bytes) / (ms_dec * 1e-3) / 1e9 / hbm_peak}
+            "decode_frac_of_measured_hbm": (w_bytes + state_bytes) / (ms_dec * 1e-3) / 1e9 / hbm_peak,
+            "decode_stacked_ms_per_layer_step": ms_stack,
+            "decode_stacked_frac_of_measured_hbm": (w_bytes + state_bytes) / (ms_stack * 1e-3) / 1e9 / hbm_peak}
 
 
 def run_varlen(world, dev, stream):

@@ -188,3 +188,42 @@ class DecodeGraph:
         self.x.copy_(x)
         self.graph.replay()
         return self.y
+
+
+class DecodeStackGraph:
+    """One decode step through a stack of layers as a single CUDA graph: the token
+    rows go through ``layers[0].decode`` ... ``layers[-1].decode``, each layer's
+    output feeding the next, with programmatic dependent launch across the whole
+    stack, so a layer's projection weights start streaming while the previous
+    layer finishes and no per-layer copy or graph launch sits between them.  The
+    recurrent states and conv histories in ``states`` are updated in place."""
+
+    def __init__(self, layers, states, B: int, overlap: bool = True):
+        self.layers = list(layers)
+        self.states = list(states)
+        dev = self.states[0]["recurrent"].device
+        self.x = torch.zeros(B, 1, self.layers[0].cfg.hidden, dtype=torch.bfloat16, device=dev)
+        s = torch.cuda.Stream()
+        s.wait_stream(torch.cuda.current_stream())
+        with torch.cuda.stream(s):                     # warm-up on scratch copies
+            y = self.x
+            for layer, st in zip(self.layers, self.states):
+                scratch = {k_: v_.clone() for k_, v_ in st.items()}
+                y, _ = layer.decode(y, scratch, scratch)
+        torch.cuda.current_stream().wait_stream(s)
+        self.graph = torch.cuda.CUDAGraph()
+        lib = _lib.lib()
+        lib.gdn_set_launch_overlap(1 if overlap else 0)
+        try:
+            with torch.cuda.graph(self.graph):
+                y = self.x
+                for layer, st in zip(self.layers, self.states):
+                    y, _ = layer.decode(y, st, st)
+                self.y = y
+        finally:
+            lib.gdn_set_launch_overlap(0)
+
+    def step(self, x: torch.Tensor) -> torch.Tensor:
+        self.x.copy_(x)
+        self.graph.replay()
+        return self.y

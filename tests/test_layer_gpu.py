@@ -78,3 +78,26 @@ def test_layer_decode_cuda_graph_matches_eager(cuda_device, overlap):
         torch.cuda.synchronize()
         assert torch.equal(ye, yg)
     assert torch.equal(st_e["recurrent"], st_g["recurrent"])
+
+
+def test_layer_decode_stacked_graph_matches_eager(cuda_device):
+    """Three layers in one CUDA graph (each layer's output feeding the next, with
+    programmatic dependent launch across the stack) give the eager chain's bits."""
+    import torch
+    from gdn_18646_b200.layer import DecodeStackGraph
+    layers = [_layer(3 + i) for i in range(3)]
+    B, T0, steps = 2, 64, 4
+    x = torch.randn(B, T0 + steps, 2048, device="cuda").bfloat16()
+    st_e = [layer.prefill(x[:, :T0].contiguous())[1] for layer in layers]
+    st_g = [{k: v.clone() for k, v in s.items()} for s in st_e]
+    stack = DecodeStackGraph(layers, st_g, B)
+    for t in range(T0, T0 + steps):
+        y = x[:, t:t + 1].contiguous()
+        for i, layer in enumerate(layers):
+            y, st_e[i] = layer.decode(y, st_e[i])
+        yg = stack.step(x[:, t:t + 1])
+        torch.cuda.synchronize()
+        assert torch.equal(y, yg)
+    for se, sg in zip(st_e, st_g):
+        assert torch.equal(se["recurrent"], sg["recurrent"])
+        assert torch.equal(se["conv_v"], sg["conv_v"])
