@@ -695,6 +695,16 @@ def run_only(args):
 
         def step():
             ops.decode_step(q, k, v, a, b, A_log, dtb, S, out=o)
+    elif args.only == "layer_prefill":
+        # config 3's layer prefill, x [2, 8192, 2048]
+        from gdn_18646_b200.layer import GDNConfig, GDNLayer, make_weights
+        cfg = GDNConfig()
+        layer = GDNLayer(make_weights(cfg, device=dev, seed=3), cfg)
+        g = torch.Generator(device=dev).manual_seed(7)
+        xl = torch.randn(2, 8192, cfg.hidden, generator=g, device=dev).bfloat16()
+
+        def step():
+            layer.prefill(xl)
     elif args.only == "outproj":
         # the fused output projection's GEMM on one GPU (world 1: every tile stays local)
         # at the config-3 widths: y [32768, 4096] x W_o [2048, 4096]^T
@@ -742,7 +752,8 @@ def main(argv=None):
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--workload", choices=["prefill", "long"], default="prefill")
     ap.add_argument("--no-cpu-baseline", action="store_true")
-    ap.add_argument("--only", choices=["prefill", "decode", "proj", "layer_decode", "backward", "backward_config1", "outproj"], default=None,
+    ap.add_argument("--only", choices=["prefill", "decode", "proj", "layer_decode", "layer_prefill", "backward", "backward_config1",
+                             "outproj"], default=None,
                     help="run just one kernel's workload (for profiling); prints a short JSON line")
     args = ap.parse_args(argv)
     if args.only:

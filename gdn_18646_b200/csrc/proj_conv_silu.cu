@@ -240,21 +240,53 @@ proj_conv_silu_kernel(const __grid_constant__ CUtensorMap map_w, const __grid_co
             if (lane == 0) mbar_arrive(&acc_empty[abuf]);
 
             if (args.l2) {
+                // per token row: the 128 channels as 16 chunks of 8 (16-byte shared-memory
+                // accesses, conflict-free per quarter warp under the 128-byte swizzle), the
+                // sum of squares per group of args.l2 channels, then every value scaled
                 named_bar(1, 128);
-                const int g = args.l2;
+                const int cpg = args.l2 >> 3;                  // chunks per group
                 for (int r = et; r < POUT; r += 128) {
-                    for (int g0 = 0; g0 < PM; g0 += g) {
+                    uint4 cw[16];
+#pragma unroll
+                    for (int c16 = 0; c16 < 16; ++c16)
+                        cw[c16] = *reinterpret_cast<const uint4*>(ysm + (c16 >> 3) * Y_SUB_BYTES + sw128_chunk(r, c16 & 7));
+                    float t[16];                                   // chunk sums of squares
+#pragma unroll
+                    for (int c16 = 0; c16 < 16; ++c16) {
+                        const uint32_t u[4] = {cw[c16].x, cw[c16].y, cw[c16].z, cw[c16].w};
                         float ss = 0.f;
-                        for (int cc = g0; cc < g0 + g; ++cc) {
-                            const float y = bf16_bits_to_f32(*reinterpret_cast<const uint16_t*>(
-                                ysm + (cc >> 6) * Y_SUB_BYTES + sw128_off(r, cc & 63)));
-                            ss += y * y;
+#pragma unroll
+                        for (int i = 0; i < 4; ++i) {
+                            const float f0 = __uint_as_float(u[i] << 16), f1 = __uint_as_float(u[i] & 0xffff0000u);
+                            ss = fmaf(f0, f0, ss);
+                            ss = fmaf(f1, f1, ss);
                         }
-                        const float inv = 1.f / sqrtf(ss + 1e-6f);
-                        for (int cc = g0; cc < g0 + g; ++cc) {
-                            uint16_t* py = reinterpret_cast<uint16_t*>(ysm + (cc >> 6) * Y_SUB_BYTES + sw128_off(r, cc & 63));
-                            *py = f32_to_bf16_bits(bf16_bits_to_f32(*py) * inv);
+                        t[c16] = ss;
+                    }
+                    // group sums over aligned blocks of cpg chunks (cpg a power of two)
+#pragma unroll
+                    for (int w = 1; w < 16; w <<= 1) {
+                        if (w < cpg) {
+                            float n[16];
+#pragma unroll
+                            for (int c = 0; c < 16; ++c) n[c] = t[c] + t[c ^ w];
+#pragma unroll
+                            for (int c = 0; c < 16; ++c) t[c] = n[c];
                         }
+                    }
+                    float inv[16];
+#pragma unroll
+                    for (int c = 0; c < 16; ++c) inv[c] = 1.f / sqrtf(t[c] + 1e-6f);
+#pragma unroll
+                    for (int c16 = 0; c16 < 16; ++c16) {
+                        const uint32_t u[4] = {cw[c16].x, cw[c16].y, cw[c16].z, cw[c16].w};
+                        uint32_t o[4];
+#pragma unroll
+                        for (int i = 0; i < 4; ++i)
+                            o[i] = (static_cast<uint32_t>(f32_to_bf16_bits(__uint_as_float(u[i] & 0xffff0000u) * inv[c16])) << 16) |
+                                   f32_to_bf16_bits(__uint_as_float(u[i] << 16) * inv[c16]);
+                        *reinterpret_cast<uint4*>(ysm + (c16 >> 3) * Y_SUB_BYTES + sw128_chunk(r, c16 & 7)) =
+                            make_uint4(o[0], o[1], o[2], o[3]);
                     }
                 }
             }
