@@ -78,13 +78,14 @@ class GDNLayer:
         self.cfg = cfg or GDNConfig()
         self.scale = self.cfg.dk ** -0.5
 
-    def init_state(self, B: int, device="cuda"):
+    def init_state(self, B: int, device="cuda", fill=torch.zeros):
+        """Zero state (``fill=torch.empty``: buffers a prefill overwrites completely)."""
         c = self.cfg
         return dict(
-            recurrent=torch.zeros(B, c.n_v, c.dk, c.dv, dtype=torch.float32, device=device),
-            conv_q=torch.zeros(B, c.qk_dim, c.conv - 1, dtype=torch.bfloat16, device=device),
-            conv_k=torch.zeros(B, c.qk_dim, c.conv - 1, dtype=torch.bfloat16, device=device),
-            conv_v=torch.zeros(B, c.v_dim, c.conv - 1, dtype=torch.bfloat16, device=device),
+            recurrent=fill(B, c.n_v, c.dk, c.dv, dtype=torch.float32, device=device),
+            conv_q=fill(B, c.qk_dim, c.conv - 1, dtype=torch.bfloat16, device=device),
+            conv_k=fill(B, c.qk_dim, c.conv - 1, dtype=torch.bfloat16, device=device),
+            conv_v=fill(B, c.v_dim, c.conv - 1, dtype=torch.bfloat16, device=device),
         )
 
     def _project(self, xn, state_in, state_out):
@@ -108,7 +109,7 @@ class GDNLayer:
         c, w = self.cfg, self.w
         B, T, D = x.shape
         xn = ops.rmsnorm(x.reshape(B * T, D), w["norm_gamma"], c.eps).reshape(B, T, D)
-        new_state = self.init_state(B, x.device)
+        new_state = self.init_state(B, x.device, fill=torch.empty)   # written by the projections and prefill
         q, k, v, z, ab = self._project(xn, state, new_state)
         a = ab[..., :c.n_v].transpose(1, 2).contiguous()        # [B, Hv, T]
         b = ab[..., c.n_v:].transpose(1, 2).contiguous()
