@@ -37,6 +37,12 @@ _I = ctypes.c_int
 _F = ctypes.c_float
 _Z = ctypes.c_size_t
 
+class ProjOutSeg(ctypes.Structure):
+    """gdn_proj_out_seg (include/gdn_b200.h): one output segment of gdn_proj_multi_fwd."""
+    _fields_ = [("W", _P), ("y", _P), ("conv_w", _P), ("conv_state_in", _P), ("conv_state_out", _P),
+                ("Dout", _I), ("l2norm_group", _I)]
+
+
 class ProjSegment(ctypes.Structure):
     """gdn_proj_segment (include/gdn_b200.h): one channel segment of gdn_decode_proj_fwd."""
     _fields_ = [("W", _P), ("y", _P), ("conv_w", _P), ("conv_state_in", _P), ("conv_state_out", _P),
@@ -75,6 +81,7 @@ SIGNATURES = {
     "gdn_gated_rmsnorm_fwd": [_P, _I, _P, _P, _P, _I, _I, _F, _P],
     "gdn_decode_proj_fwd": [_P, _P, _F, _I, _I, ctypes.POINTER(ProjSegment), _I, _P],
     "gdn_proj_conv_silu_fwd": [_P, _P, _P, _P, _I, _I, _I, _I, _P, _P, _I, _P],
+    "gdn_proj_multi_fwd": [_P, _I, _I, _I, ctypes.POINTER(ProjOutSeg), _I, _P],
     "gdn_outproj_rs_fwd": [_P, _P, ctypes.POINTER(ctypes.c_void_p), _I, _I, _I, _I, _I, _P],
     "gdn_outproj_reduce": [_P, _P, _I, _I, _I, _P],
     "gdn_check_device_error": [],

@@ -19,6 +19,7 @@
 // operands K-major), warps 2-5 = epilogue (TMEM -> conv/SiLU/L2 -> smem ->
 // TMA store).  Two TMEM accumulators (2 x 256 columns) let the epilogue of
 // tile i overlap the MMAs of tile i+1.
+#include <cstring>
 #include <mutex>
 
 #include "common.cuh"
@@ -42,21 +43,44 @@ constexpr int PROJ_SMEM = OFF_BAR + 128 + 1024;
 static_assert(PROJ_SMEM <= 232448, "proj shared memory exceeds 227 KB");
 constexpr int kProjThreads = 192;     // 6 warps
 
-struct ProjArgs {
-    const uint16_t* conv_w;      // [Dout, 4]
+constexpr int kProjMaxSeg = 4;
+
+// One output-channel segment of a launch: its own weights, conv and output tensors.
+struct ProjSeg {
+    const uint16_t* conv_w;      // [Dout, 4], or null: plain projection y = bf16(x . W[c])
     const uint16_t* state_in;    // [B, Dout, 3] or null
     uint16_t* state_out;         // [B, Dout, 3] or null
-    unsigned int* err;
-    int B, T, D, Dout;
-    int n_ct, n_tt, ntiles;
+    int Dout;
+    int ct0;                     // first channel tile of the segment in the launch
     int l2;                      // 0 or group size
 };
+
+struct ProjArgs {
+    unsigned int* err;
+    int B, T, D;
+    int n_ct, n_tt, ntiles;      // n_ct: channel tiles over all segments
+    int nseg;
+    ProjSeg seg[kProjMaxSeg];
+};
+
+struct alignas(64) ProjMaps {
+    CUtensorMap w[kProjMaxSeg];
+    CUtensorMap y[kProjMaxSeg];
+};
+
+__device__ __forceinline__ int proj_seg_of(const ProjArgs& a, int ct) {
+    int s = 0;
+#pragma unroll
+    for (int i = 1; i < kProjMaxSeg; ++i)
+        if (i < a.nseg && ct >= a.seg[i].ct0) s = i;
+    return s;
+}
 
 __device__ __forceinline__ float bf16r(float x) { return __uint_as_float(static_cast<uint32_t>(f32_to_bf16_bits(x)) << 16); }
 
 __global__ void __launch_bounds__(kProjThreads, 1)
-proj_conv_silu_kernel(const __grid_constant__ CUtensorMap map_w, const __grid_constant__ CUtensorMap map_x,
-                      const __grid_constant__ CUtensorMap map_y, const ProjArgs args) {
+proj_conv_silu_kernel(const __grid_constant__ ProjMaps maps, const __grid_constant__ CUtensorMap map_x,
+                      const __grid_constant__ ProjArgs args) {
     extern __shared__ uint8_t smem_raw[];
     uint8_t* sm = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
     uint64_t* full = reinterpret_cast<uint64_t*>(sm + OFF_BAR);   // [PSTAGES]
@@ -83,9 +107,11 @@ proj_conv_silu_kernel(const __grid_constant__ CUtensorMap map_w, const __grid_co
         }
         *abort_flag = 0;
         fence_mbar_init();
-        tma_prefetch_desc(&map_w);
+        for (int i = 0; i < args.nseg; ++i) {
+            tma_prefetch_desc(&maps.w[i]);
+            tma_prefetch_desc(&maps.y[i]);
+        }
         tma_prefetch_desc(&map_x);
-        tma_prefetch_desc(&map_y);
     }
     if (warp == 1) {
         tmem_alloc(tmem_slot, 512);
@@ -107,11 +133,14 @@ proj_conv_silu_kernel(const __grid_constant__ CUtensorMap map_w, const __grid_co
                 const int tt = rest % args.n_tt;
                 const int b = rest / args.n_tt;
                 const int ts = tt * POUT - 3;
+                const int sg = proj_seg_of(args, ct);
+                const CUtensorMap* mw = &maps.w[sg];
+                const int lct = ct - args.seg[sg].ct0;
                 for (int kb = 0; kb < nk; ++kb) {
                     if (!mbar_wait_or_abort(&empty[stage], phase ^ 1u, args.err, abort_flag)) break;
                     uint8_t* st = sm + stage * STAGE_BYTES;
                     mbar_arrive_expect_tx(&full[stage], STAGE_BYTES);
-                    tma_load_2d(st, &map_w, &full[stage], kb * PK, ct * PM);
+                    tma_load_2d(st, mw, &full[stage], kb * PK, lct * PM);
                     tma_load_3d(st + A_BYTES, &map_x, &full[stage], kb * PK, ts, b);
                     if (++stage == PSTAGES) {
                         stage = 0;
@@ -167,7 +196,10 @@ proj_conv_silu_kernel(const __grid_constant__ CUtensorMap map_w, const __grid_co
             const int b = rest / args.n_tt;
             const int t0 = tt * POUT;
             const int ts = t0 - 3;
-            const int c = ct * PM + cl;
+            const int sg = proj_seg_of(args, ct);
+            const ProjSeg& S = args.seg[sg];
+            const int lct = ct - S.ct0;
+            const int c = lct * PM + cl;                // channel within the segment
             const int abuf = local & 1;
             const uint32_t aphase = static_cast<uint32_t>(local >> 1) & 1u;
 
@@ -175,10 +207,16 @@ proj_conv_silu_kernel(const __grid_constant__ CUtensorMap map_w, const __grid_co
             if (et == 0) bulk_wait_read0();
             named_bar(1, 128);
 
-            const uint2 wraw = *reinterpret_cast<const uint2*>(args.conv_w + static_cast<long>(c) * 4);
-            const float w0 = bf16_bits_to_f32(wraw.x & 0xffffu), w1 = bf16_bits_to_f32(wraw.x >> 16);
-            const float w2 = bf16_bits_to_f32(wraw.y & 0xffffu), w3 = bf16_bits_to_f32(wraw.y >> 16);
-            const long sbase = (static_cast<long>(b) * args.Dout + c) * 3;
+            const bool conv = S.conv_w != nullptr;
+            float w0 = 0.f, w1 = 0.f, w2 = 0.f, w3 = 0.f;
+            if (conv) {
+                const uint2 wraw = *reinterpret_cast<const uint2*>(S.conv_w + static_cast<long>(c) * 4);
+                w0 = bf16_bits_to_f32(wraw.x & 0xffffu);
+                w1 = bf16_bits_to_f32(wraw.x >> 16);
+                w2 = bf16_bits_to_f32(wraw.y & 0xffffu);
+                w3 = bf16_bits_to_f32(wraw.y >> 16);
+            }
+            const long sbase = (static_cast<long>(b) * S.Dout + c) * 3;
 
             const bool ok = mbar_wait_or_abort(&acc_full[abuf], aphase, args.err, abort_flag);
             tc_fence_after();
@@ -186,13 +224,20 @@ proj_conv_silu_kernel(const __grid_constant__ CUtensorMap map_w, const __grid_co
             uint8_t* ysub = ysm + (cl >> 6) * Y_SUB_BYTES;
             const uint32_t ccol = cl & 63;
             // tiles that touch the conv history (first tile with state_in, last tile with state_out)
-            const bool special = (tt == 0 && args.state_in) || (args.state_out && ts + PN > args.T - 3);
+            const bool special = conv && ((tt == 0 && S.state_in) || (S.state_out && ts + PN > args.T - 3));
 #pragma unroll 1
             for (int blk = 0; blk < PN / 32; ++blk) {
                 float acc[32];
                 tmem_ld32(tmem + lane_off + abuf * PN + blk * 32, acc);
                 tmem_ld_wait();
-                if (!special) {
+                if (!conv) {                               // plain projection: y = bf16(x . W[c])
+#pragma unroll
+                    for (int u = 0; u < 32; ++u) {
+                        const int i = blk * 32 + u;
+                        if (i >= 3)
+                            *reinterpret_cast<uint16_t*>(ysub + sw128_off(i - 3, ccol)) = f32_to_bf16_bits(acc[u]);
+                    }
+                } else if (!special) {
 #pragma unroll
                     for (int u = 0; u < 32; ++u) {
                         const int i = blk * 32 + u;
@@ -216,9 +261,9 @@ proj_conv_silu_kernel(const __grid_constant__ CUtensorMap map_w, const __grid_co
                         const int i = blk * 32 + u;
                         const int tok = ts + i;
                         float p = bf16r(acc[u]);
-                        if (tok < 0) p = args.state_in ? bf16_bits_to_f32(args.state_in[sbase + (tok + 3)]) : 0.f;
-                        if (args.state_out && tok < args.T && tok >= args.T - 3 && (i >= 3 || tt == 0))
-                            args.state_out[sbase + (tok - (args.T - 3))] = f32_to_bf16_bits(p);
+                        if (tok < 0) p = S.state_in ? bf16_bits_to_f32(S.state_in[sbase + (tok + 3)]) : 0.f;
+                        if (S.state_out && tok < args.T && tok >= args.T - 3 && (i >= 3 || tt == 0))
+                            S.state_out[sbase + (tok - (args.T - 3))] = f32_to_bf16_bits(p);
                         if (i >= 3) {
                             float conv = p1 * w0;
                             conv = fmaf(p2, w1, conv);
@@ -239,12 +284,12 @@ proj_conv_silu_kernel(const __grid_constant__ CUtensorMap map_w, const __grid_co
             __syncwarp();
             if (lane == 0) mbar_arrive(&acc_empty[abuf]);
 
-            if (args.l2) {
+            if (S.l2) {
                 // per token row: the 128 channels as 16 chunks of 8 (16-byte shared-memory
                 // accesses, conflict-free per quarter warp under the 128-byte swizzle), the
                 // sum of squares per group of args.l2 channels, then every value scaled
                 named_bar(1, 128);
-                const int cpg = args.l2 >> 3;                  // chunks per group
+                const int cpg = S.l2 >> 3;                     // chunks per group
                 for (int r = et; r < POUT; r += 128) {
                     uint4 cw[16];
 #pragma unroll
@@ -293,8 +338,8 @@ proj_conv_silu_kernel(const __grid_constant__ CUtensorMap map_w, const __grid_co
             fence_async_smem();
             named_bar(1, 128);
             if (et == 0 && ok && !*abort_flag) {
-                tma_store_3d(&map_y, ysm, ct * PM, t0, b);
-                tma_store_3d(&map_y, ysm + Y_SUB_BYTES, ct * PM + 64, t0, b);
+                tma_store_3d(&maps.y[sg], ysm, lct * PM, t0, b);
+                tma_store_3d(&maps.y[sg], ysm + Y_SUB_BYTES, lct * PM + 64, t0, b);
                 bulk_commit();
             }
         }
@@ -329,13 +374,11 @@ int check_proj_args(const void* x, const void* W, const void* conv_w, void* y, i
 
 }  // namespace gdn
 
-extern "C" int gdn_proj_conv_silu_fwd(const void* x, const void* W, const void* conv_w, void* y, int B, int T,
-                                      int D, int Dout, const void* conv_state_in, void* conv_state_out,
-                                      int l2norm_group, void* stream) {
-    using namespace gdn;
-    int st = check_proj_args(x, W, conv_w, y, B, T, D, Dout, conv_state_in, conv_state_out, l2norm_group);
+namespace gdn {
+namespace {
+int run_proj(const void* x, int B, int T, int D, const gdn_proj_out_seg* segs, int nseg, void* stream) {
+    int st = check_sm100();
     if (st != GDN_OK) return st;
-    if ((st = check_sm100()) != GDN_OK) return st;
     int dev = 0;
     cudaGetDevice(&dev);
     std::call_once(g_proj_attr_once[dev & 63], [dev]() {
@@ -349,41 +392,87 @@ extern "C" int gdn_proj_conv_silu_fwd(const void* x, const void* W, const void* 
     if (g_proj_attr_status[dev & 63] != GDN_OK)
         return fail(GDN_ERR_CUDA, "gdn_proj_conv_silu_fwd: cannot grant %d B of shared memory", PROJ_SMEM);
 
-    CUtensorMap mw, mx, my;
-    {
-        uint64_t dims[2] = {static_cast<uint64_t>(D), static_cast<uint64_t>(Dout)};
-        uint64_t strides[1] = {static_cast<uint64_t>(D) * 2};
-        uint32_t box[2] = {PK, PM};
-        if ((st = make_map_bf16(&mw, W, 2, dims, strides, box, true)) != GDN_OK) return st;
-    }
+    ProjMaps maps;
+    memset(&maps, 0, sizeof(maps));
+    CUtensorMap mx;
     {
         uint64_t dims[3] = {static_cast<uint64_t>(D), static_cast<uint64_t>(T), static_cast<uint64_t>(B)};
         uint64_t strides[2] = {static_cast<uint64_t>(D) * 2, static_cast<uint64_t>(D) * 2 * T};
         uint32_t box[3] = {PK, PN, 1};
         if ((st = make_map_bf16(&mx, x, 3, dims, strides, box, true)) != GDN_OK) return st;
     }
-    {
-        uint64_t dims[3] = {static_cast<uint64_t>(Dout), static_cast<uint64_t>(T), static_cast<uint64_t>(B)};
-        uint64_t strides[2] = {static_cast<uint64_t>(Dout) * 2, static_cast<uint64_t>(Dout) * 2 * T};
-        uint32_t box[3] = {64, POUT, 1};
-        if ((st = make_map_bf16(&my, y, 3, dims, strides, box, true)) != GDN_OK) return st;
-    }
     ProjArgs a;
-    a.conv_w = static_cast<const uint16_t*>(conv_w);
-    a.state_in = static_cast<const uint16_t*>(conv_state_in);
-    a.state_out = static_cast<uint16_t*>(conv_state_out);
+    memset(&a, 0, sizeof(a));
     a.err = device_error_word();
     a.B = B;
     a.T = T;
     a.D = D;
-    a.Dout = Dout;
-    a.n_ct = Dout / PM;
+    a.nseg = nseg;
+    int ct = 0;
+    for (int i = 0; i < nseg; ++i) {
+        const gdn_proj_out_seg& g = segs[i];
+        {
+            uint64_t dims[2] = {static_cast<uint64_t>(D), static_cast<uint64_t>(g.Dout)};
+            uint64_t strides[1] = {static_cast<uint64_t>(D) * 2};
+            uint32_t box[2] = {PK, PM};
+            if ((st = make_map_bf16(&maps.w[i], g.W, 2, dims, strides, box, true)) != GDN_OK) return st;
+        }
+        {
+            uint64_t dims[3] = {static_cast<uint64_t>(g.Dout), static_cast<uint64_t>(T), static_cast<uint64_t>(B)};
+            uint64_t strides[2] = {static_cast<uint64_t>(g.Dout) * 2, static_cast<uint64_t>(g.Dout) * 2 * T};
+            uint32_t box[3] = {64, POUT, 1};
+            if ((st = make_map_bf16(&maps.y[i], g.y, 3, dims, strides, box, true)) != GDN_OK) return st;
+        }
+        a.seg[i].conv_w = static_cast<const uint16_t*>(g.conv_w);
+        a.seg[i].state_in = g.conv_w ? static_cast<const uint16_t*>(g.conv_state_in) : nullptr;
+        a.seg[i].state_out = g.conv_w ? static_cast<uint16_t*>(g.conv_state_out) : nullptr;
+        a.seg[i].Dout = g.Dout;
+        a.seg[i].ct0 = ct;
+        a.seg[i].l2 = g.l2norm_group;
+        ct += g.Dout / PM;
+    }
+    a.n_ct = ct;
     a.n_tt = (T + POUT - 1) / POUT;
     const long ntiles = static_cast<long>(a.n_ct) * a.n_tt * B;
     if (ntiles > 0x7fffffffL) return fail(GDN_ERR_SHAPE, "gdn_proj_conv_silu_fwd: too many tiles");
     a.ntiles = static_cast<int>(ntiles);
-    a.l2 = l2norm_group;
     const int grid = static_cast<int>(ntiles < g_sm_count[dev & 63] ? ntiles : g_sm_count[dev & 63]);
-    proj_conv_silu_kernel<<<grid, kProjThreads, PROJ_SMEM, static_cast<cudaStream_t>(stream)>>>(mw, mx, my, a);
+    proj_conv_silu_kernel<<<grid, kProjThreads, PROJ_SMEM, static_cast<cudaStream_t>(stream)>>>(maps, mx, a);
     return launch_status("gdn_proj_conv_silu_fwd");
+}
+}  // namespace
+}  // namespace gdn
+
+extern "C" int gdn_proj_conv_silu_fwd(const void* x, const void* W, const void* conv_w, void* y, int B, int T,
+                                      int D, int Dout, const void* conv_state_in, void* conv_state_out,
+                                      int l2norm_group, void* stream) {
+    using namespace gdn;
+    const int st = check_proj_args(x, W, conv_w, y, B, T, D, Dout, conv_state_in, conv_state_out, l2norm_group);
+    if (st != GDN_OK) return st;
+    gdn_proj_out_seg seg;
+    seg.W = W;
+    seg.y = y;
+    seg.conv_w = conv_w;
+    seg.conv_state_in = conv_state_in;
+    seg.conv_state_out = conv_state_out;
+    seg.Dout = Dout;
+    seg.l2norm_group = l2norm_group;
+    return run_proj(x, B, T, D, &seg, 1, stream);
+}
+
+extern "C" int gdn_proj_multi_fwd(const void* x, int B, int T, int D, const gdn_proj_out_seg* segs, int nseg,
+                                  void* stream) {
+    using namespace gdn;
+    if (!x || !segs) return fail(GDN_ERR_NULL, "gdn_proj_multi_fwd: x and segs are required");
+    if (nseg < 1 || nseg > kProjMaxSeg)
+        return fail(GDN_ERR_SHAPE, "gdn_proj_multi_fwd: 1 to %d segments (got %d)", kProjMaxSeg, nseg);
+    for (int i = 0; i < nseg; ++i) {
+        const gdn_proj_out_seg& g = segs[i];
+        if (!g.W || !g.y) return fail(GDN_ERR_NULL, "gdn_proj_multi_fwd: segment %d needs W and y", i);
+        // the shared checks, with conv_w standing in for plain segments
+        const int st = check_proj_args(x, g.W, g.conv_w ? g.conv_w : g.W, g.y, B, T, D, g.Dout,
+                                       g.conv_state_in, g.conv_state_out, g.l2norm_group);
+        if (st != GDN_OK) return st;
+    }
+    return run_proj(x, B, T, D, segs, nseg, stream);
 }

@@ -93,12 +93,14 @@ class GDNLayer:
         c, w = self.cfg, self.w
         B, T, D = xn.shape
         si = state_in or {}
-        q = ops.proj_conv_silu(xn, w["W_q"], w["conv_q"], l2norm_group=c.dk, conv_state_in=si.get("conv_q"),
-                               conv_state_out=state_out["conv_q"])
-        k = ops.proj_conv_silu(xn, w["W_k"], w["conv_k"], l2norm_group=c.dk, conv_state_in=si.get("conv_k"),
-                               conv_state_out=state_out["conv_k"])
-        v = ops.proj_conv_silu(xn, w["W_v"], w["conv_v"], conv_state_in=si.get("conv_v"),
-                               conv_state_out=state_out["conv_v"])
+        # q | k | v (conv4 + SiLU, q/k L2-normalised per head) in one launch
+        q, k, v = ops.proj_multi(xn, [
+            dict(W=w["W_q"], conv_w=w["conv_q"], l2norm_group=c.dk, conv_state_in=si.get("conv_q"),
+                 conv_state_out=state_out["conv_q"]),
+            dict(W=w["W_k"], conv_w=w["conv_k"], l2norm_group=c.dk, conv_state_in=si.get("conv_k"),
+                 conv_state_out=state_out["conv_k"]),
+            dict(W=w["W_v"], conv_w=w["conv_v"], conv_state_in=si.get("conv_v"), conv_state_out=state_out["conv_v"]),
+        ])
         z = xn @ w["W_z"].T
         ab = xn @ w["W_ab"].T                                    # [B, T, 2*Hv]
         return q, k, v, z, ab

@@ -395,6 +395,38 @@ def proj_conv_silu(x, W, conv_w, *, conv_state_in=None, conv_state_out=None, l2n
     return out
 
 
+def proj_multi(x, segments):
+    """Several projections of the same x [B,T,D] bf16 in one launch (gdn_proj_multi_fwd).
+    ``segments``: up to 4 dicts with ``W`` [Dout, D] bf16 and optionally ``conv_w``
+    [Dout, 4] (without it: a plain projection x @ W^T rounded to bf16),
+    ``conv_state_in`` / ``conv_state_out`` [B, Dout, 3], ``l2norm_group`` and ``out``
+    [B, T, Dout].  Returns the list of outputs, each as ``proj_conv_silu`` (or the
+    plain projection) would give it."""
+    _cuda_contig(x, "x", torch.bfloat16)
+    _need(x.dim() == 3, "x must be [B, T, D]")
+    B, T, D = x.shape
+    segs = (_lib.ProjOutSeg * len(segments))()
+    outs = []
+    for i, sg in enumerate(segments):
+        W = sg["W"]
+        _cuda_contig(W, f"segments[{i}].W", torch.bfloat16)
+        _need(W.dim() == 2 and W.shape[1] == D, f"segments[{i}].W must be [Dout, {D}]")
+        Dout = W.shape[0]
+        out = sg.get("out")
+        if out is None:
+            out = torch.empty(B, T, Dout, dtype=torch.bfloat16, device=x.device)
+        _cuda_contig(out, f"segments[{i}].out", torch.bfloat16)
+        cw = sg.get("conv_w")
+        if cw is not None:
+            _cuda_contig(cw, f"segments[{i}].conv_w", torch.bfloat16)
+        segs[i].W, segs[i].y, segs[i].conv_w = _ptr(W), _ptr(out), _ptr(cw)
+        segs[i].conv_state_in, segs[i].conv_state_out = _ptr(sg.get("conv_state_in")), _ptr(sg.get("conv_state_out"))
+        segs[i].Dout, segs[i].l2norm_group = Dout, int(sg.get("l2norm_group", 0))
+        outs.append(out)
+    _lib.call("gdn_proj_multi_fwd", _ptr(x), B, T, D, segs, len(segments), _stream())
+    return outs
+
+
 def decode_proj(x, segments, *, norm_gamma=None, eps=1e-6):
     """Input projections of one decode step in one launch (gdn_decode_proj_fwd).
 

@@ -377,6 +377,29 @@ int gdn_proj_conv_silu_fwd(const void* x, const void* W, const void* conv_w, voi
                            const void* conv_state_in, void* conv_state_out,
                            int l2norm_group, void* stream);
 
+/*
+ * gdn_proj_conv_silu_fwd over up to 4 output segments in one launch, all from
+ * the same x [B, T, D] bf16: each segment has its own weights W [Dout, D], output
+ * y [B, T, Dout] and, optionally, conv weights (NULL: a plain projection
+ * y = bf16(x . W^T), no conv or SiLU), conv histories and per-head L2 norm.
+ * One persistent launch walks the tiles of all segments, so e.g. a layer's
+ * q | k | v projections share one pass over the tiles (no per-call tail) while
+ * their outputs stay separate tensors.  Each segment follows the rules of
+ * gdn_proj_conv_silu_fwd (Dout % 128 == 0, l2norm_group 0 or a divisor of 128).
+ * No reference counterpart (kernels/fused_proj_conv_silu.cu:298-355 is one segment).
+ */
+typedef struct {
+    const void* W;              /* bf16 [Dout, D] */
+    void* y;                    /* bf16 [B, T, Dout] */
+    const void* conv_w;         /* bf16 [Dout, 4] or NULL (plain projection) */
+    const void* conv_state_in;  /* bf16 [B, Dout, 3] or NULL (zeros); conv segments only */
+    void* conv_state_out;       /* bf16 [B, Dout, 3] or NULL; conv segments only */
+    int Dout;
+    int l2norm_group;
+} gdn_proj_out_seg;
+int gdn_proj_multi_fwd(const void* x, int B, int T, int D, const gdn_proj_out_seg* segs, int nseg,
+                       void* stream);
+
 /* Human-readable description of the calling thread's last error. */
 const char* gdn_last_error(void);
 

@@ -301,3 +301,18 @@ def test_decode_step_gated_rejects(lib):
     assert call(flags=8) == _lib.GDN_ERR_DTYPE
     assert call(y=ODD) == _lib.GDN_ERR_ALIGN
     assert "gdn_decode_step_gated" in _lib.last_error()
+
+
+def test_proj_multi_rejects(lib):
+    segs = (_lib.ProjOutSeg * 2)()
+    for s_ in segs:
+        s_.W, s_.y, s_.conv_w, s_.Dout, s_.l2norm_group = FAKE, FAKE, None, 128, 0
+    assert _lib.call_status("gdn_proj_multi_fwd", None, 1, 8, 64, segs, 2, None) == _lib.GDN_ERR_NULL
+    assert _lib.call_status("gdn_proj_multi_fwd", FAKE, 1, 8, 64, segs, 0, None) == _lib.GDN_ERR_SHAPE
+    assert _lib.call_status("gdn_proj_multi_fwd", FAKE, 1, 8, 64, segs, 5, None) == _lib.GDN_ERR_SHAPE
+    segs[1].Dout = 100
+    assert _lib.call_status("gdn_proj_multi_fwd", FAKE, 1, 8, 64, segs, 2, None) == _lib.GDN_ERR_SHAPE
+    segs[1].Dout, segs[1].y = 128, ODD
+    assert _lib.call_status("gdn_proj_multi_fwd", FAKE, 1, 8, 64, segs, 2, None) == _lib.GDN_ERR_ALIGN
+    segs[1].y, segs[1].W = FAKE, None
+    assert _lib.call_status("gdn_proj_multi_fwd", FAKE, 1, 8, 64, segs, 2, None) == _lib.GDN_ERR_NULL

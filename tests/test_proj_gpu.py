@@ -110,3 +110,34 @@ def test_proj_reference_module_surface_and_tolerance(cuda_device):
         diff = (y.float() - ref.float()).abs()
         assert diff.max().item() < 5e-2
         assert (diff / (ref.float().abs() + 1e-8)).max().item() < 0.1 or diff.max().item() < 2e-2
+
+
+def test_proj_multi_matches_single_launches(cuda_device):
+    """gdn_proj_multi_fwd: q | k | v-like conv segments (two L2-normalised, with and
+    without conv histories) and a plain segment in one launch give the bits of the
+    separate single-segment launches (the plain one: bf16 of the fp32 product, the
+    conv ones: gdn_proj_conv_silu_fwd)."""
+    import torch
+    from gdn_18646_b200 import ops
+    g = torch.Generator(device="cuda").manual_seed(21)
+    B, T, D = 2, 700, 256
+    x = torch.randn(B, T, D, generator=g, device="cuda").bfloat16()
+    Ws = [(torch.randn(C, D, generator=g, device="cuda") * 0.05).bfloat16() for C in (256, 128, 384, 128)]
+    cws = [(torch.randn(C, 4, generator=g, device="cuda") * 0.5).bfloat16() for C in (256, 128, 384)]
+    hin = [(torch.randn(B, C, 3, generator=g, device="cuda")).bfloat16() for C in (256, 128, 384)]
+    hout_m = [torch.empty(B, C, 3, dtype=torch.bfloat16, device="cuda") for C in (256, 128, 384)]
+    hout_s = [torch.empty_like(h) for h in hout_m]
+    l2s = (128, 64, 0)
+    outs = ops.proj_multi(x, [dict(W=Ws[i], conv_w=cws[i], l2norm_group=l2s[i],
+                                   conv_state_in=hin[i] if i != 1 else None, conv_state_out=hout_m[i])
+                              for i in range(3)] + [dict(W=Ws[3])])
+    for i in range(3):
+        ref = ops.proj_conv_silu(x, Ws[i], cws[i], l2norm_group=l2s[i], conv_state_in=hin[i] if i != 1 else None,
+                                 conv_state_out=hout_s[i])
+        torch.cuda.synchronize()
+        assert torch.equal(outs[i], ref), f"segment {i}"
+        assert torch.equal(hout_m[i], hout_s[i]), f"segment {i} history"
+    plain = (x.float() @ Ws[3].float().T).bfloat16()
+    # tensor-core fp32 accumulation vs torch's: compare within one bf16 ulp
+    diff = (outs[3].float() - plain.float()).abs()
+    assert bool((diff <= plain.float().abs() * 2.0 ** -7 + 1e-3).all())
