@@ -1381,9 +1381,13 @@ int pick_schedule(int mode, int nbh, int nchunks, int chain_grid, int sms, bool 
     if (mode == GDN_SCHEDULE_STREAM) return can_stream ? GDN_SCHEDULE_STREAM : GDN_SCHEDULE_SINGLE;
     if (mode == GDN_SCHEDULE_PIECED) return (!varlen && nchunks >= 2) ? GDN_SCHEDULE_PIECED : GDN_SCHEDULE_SINGLE;
     if (mode == GDN_SCHEDULE_SINGLE) return GDN_SCHEDULE_SINGLE;
+    // STREAM only on a clear predicted win: where the free SMs' prep workers cannot keep up
+    // with the chain (a long lead launch does most of the prep), the model is within its
+    // error of SINGLE, and the config-4 head shard on 2 GPUs (128 chains, predicted 0.95 of
+    // SINGLE) measured 4.0 ms streamed against 3.2 ms single
     if (can_stream &&
         streamed_time(nbh, nchunks, chain_grid, sms, stream_lead(nbh, nchunks, chain_grid, sms)) <
-            0.95 * unpieced_time(nbh, nchunks, sms))
+            0.85 * unpieced_time(nbh, nchunks, sms))
         return GDN_SCHEDULE_STREAM;
     if (!varlen && use_pieces(nbh, nchunks, chain_grid, sms)) return GDN_SCHEDULE_PIECED;
     return GDN_SCHEDULE_SINGLE;
