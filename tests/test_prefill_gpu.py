@@ -244,3 +244,24 @@ def test_prefill_reference_module_surface(cuda_device):
     torch.cuda.synchronize()
     assert ref_tol_ok(to_np(o), g["o"], 1e-2, 0.05)
     assert O.rel_fro(to_np(S), g["state_out"]) <= S_TOL
+
+
+@pytest.mark.parametrize("T", [1, 5, 63, 65])
+def test_prefill_tiny_and_ragged_T(cuda_device, T):
+    """A single token, a few tokens, one short of a chunk, one past it: the ragged
+    last chunk is padded like the reference (prefill_ref.py:67-74)."""
+    inp = O.make_prefill_inputs(50 + T, 2, T, 2, 128, 128, state_std=0.02)
+    o, S = _run(inp)
+    o_r, S_r = _oracle(inp)
+    _check(o, S, o_r, S_r)
+
+
+def test_prefill_strong_decay_direct_path(cuda_device):
+    """Decay strong enough that a chunk's total log decay passes the u_t * w_s
+    overflow guard (the direct exp2-per-element path) in every chunk, next to a
+    head with the config distribution."""
+    inp = O.make_prefill_inputs(57, 1, 256, 2, 128, 128, state_std=0.02)
+    inp["A_log"] = np.array([math.log(40.0), math.log(0.1)], np.float32)
+    o, S = _run(inp)
+    o_r, S_r = _oracle(inp)
+    _check(o, S, o_r, S_r)
