@@ -21,38 +21,45 @@
 namespace gdn {
 namespace {
 
-template <int DK, int DV>
+// SPLIT CTAs (a cluster) share a head, each owning DV/SPLIT value columns: for
+// small batches, where one CTA per head leaves most SMs idle, the head's state
+// streams through twice the SMs.  Every reduction over the key dimension stays
+// inside a CTA; only the gated norm's sum of squares crosses the pair (DSMEM).
+template <int DK, int DV, int SPLIT = 1>
 struct DecodeCfg {
-    static constexpr int CG = DV / 4;                                   // column groups (float4 each)
-    static constexpr int RPT = DK * DV >= 65536 ? 16 : (DK / 4 < 32 ? DK / 4 : 32);  // rows per thread
+    static constexpr int DVC = DV / SPLIT;                              // value columns per CTA
+    static constexpr int CG = DVC / 4;                                  // column groups (float4 each)
+    static constexpr int RPT = DK * DVC >= 65536 ? 16 : (DK / 4 < 32 ? DK / 4 : 32);  // rows per thread
     static constexpr int RG = DK / RPT;                                 // row groups
     static constexpr int NT = CG * RG;                                  // threads per CTA
     static_assert(RPT <= 32 && NT <= 1024, "state slice too large for registers");
 };
 
-template <int DK, int DV>
-__global__ void __launch_bounds__(DecodeCfg<DK, DV>::NT)
+template <int DK, int DV, int SPLIT>
+__global__ void __launch_bounds__(DecodeCfg<DK, DV, SPLIT>::NT)
 decode_step_kernel(const uint16_t* q, const uint16_t* k, const uint16_t* v, const void* a, const void* b,
                    int gate_dtype, const float* __restrict__ A_log,
                    const float* __restrict__ dt_bias, const float* state_in, float* state_out,
                    float* __restrict__ out, int Hqk, int Hv, float scale, int l2qk, const uint16_t* z,
                    const uint16_t* __restrict__ gamma, float eps, uint16_t* __restrict__ y) {
-    using C = DecodeCfg<DK, DV>;
+    using C = DecodeCfg<DK, DV, SPLIT>;
     constexpr int kNormWarps = (C::CG + 31) / 32;      // warps holding the row's rg == 0 threads
     __shared__ float q_s[DK];
     __shared__ float k_s[DK];
-    __shared__ float red_a[C::RG][DV];
-    __shared__ float red_b[C::RG][DV];
+    __shared__ float red_a[C::RG][C::DVC];
+    __shared__ float red_b[C::RG][C::DVC];
     __shared__ float qk_s;
     __shared__ float inv_s[2];
     __shared__ float nrm_s[kNormWarps];
+    __shared__ float nrm_peer;                 // SPLIT == 2: the other CTA's sum of squares
 
     pdl_launch_dependents();                   // the next kernel may launch (it waits for this one)
     pdl_wait_prior();                          // inputs and state come from earlier kernels
     const int tid = threadIdx.x;
-    const int cg = tid % C::CG;
+    const int rank = SPLIT > 1 ? static_cast<int>(blockIdx.x % SPLIT) : 0;   // cluster rank = column half
+    const int cg = tid % C::CG + rank * C::CG;  // this thread's float4 column group within the head
     const int rg = tid / C::CG;
-    const int bh = blockIdx.x;                 // b * Hv + h
+    const int bh = blockIdx.x / SPLIT;         // b * Hv + h
     const int h = bh % Hv;
     const int bidx = bh / Hv;
     const int hq = h / (Hv / Hqk);
@@ -125,15 +132,16 @@ decode_step_kernel(const uint16_t* q, const uint16_t* k, const uint16_t* v, cons
         pa[0] += ki * s[r].x; pa[1] += ki * s[r].y; pa[2] += ki * s[r].z; pa[3] += ki * s[r].w;
         pb[0] += qi * s[r].x; pb[1] += qi * s[r].y; pb[2] += qi * s[r].z; pb[3] += qi * s[r].w;
     }
-    *reinterpret_cast<float4*>(&red_a[rg][4 * cg]) = make_float4(pa[0], pa[1], pa[2], pa[3]);
-    *reinterpret_cast<float4*>(&red_b[rg][4 * cg]) = make_float4(pb[0], pb[1], pb[2], pb[3]);
+    const int cl = 4 * (cg - rank * C::CG);             // column within this CTA's slice
+    *reinterpret_cast<float4*>(&red_a[rg][cl]) = make_float4(pa[0], pa[1], pa[2], pa[3]);
+    *reinterpret_cast<float4*>(&red_b[rg][cl]) = make_float4(pb[0], pb[1], pb[2], pb[3]);
     __syncthreads();
 
     float ka[4] = {0.f, 0.f, 0.f, 0.f}, qa[4] = {0.f, 0.f, 0.f, 0.f};
 #pragma unroll
     for (int x = 0; x < C::RG; ++x) {
-        const float4 ra = *reinterpret_cast<const float4*>(&red_a[x][4 * cg]);
-        const float4 rb = *reinterpret_cast<const float4*>(&red_b[x][4 * cg]);
+        const float4 ra = *reinterpret_cast<const float4*>(&red_a[x][cl]);
+        const float4 rb = *reinterpret_cast<const float4*>(&red_b[x][cl]);
         ka[0] += ra.x; ka[1] += ra.y; ka[2] += ra.z; ka[3] += ra.w;
         qa[0] += rb.x; qa[1] += rb.y; qa[2] += rb.z; qa[3] += rb.w;
     }
@@ -175,10 +183,22 @@ decode_step_kernel(const uint16_t* q, const uint16_t* k, const uint16_t* v, cons
             if ((tid & 31) == 0) nrm_s[tid >> 5] = ss;
         }
         __syncthreads();
-        if (rg == 0) {
-            float tot = 0.f;
+        float tot = 0.f;
 #pragma unroll
-            for (int w = 0; w < kNormWarps; ++w) tot += nrm_s[w];
+        for (int w = 0; w < kNormWarps; ++w) tot += nrm_s[w];
+        if constexpr (SPLIT == 2) {
+            // the pair's other half of the row: write this CTA's sum into the peer's
+            // shared memory, then a cluster barrier (release / acquire) for both
+            if (tid == 0) {
+                uint32_t ra;
+                asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(ra) : "r"(smem_u32(&nrm_peer)), "r"(rank ^ 1));
+                asm volatile("st.shared::cluster.f32 [%0], %1;" ::"r"(ra), "f"(tot) : "memory");
+            }
+            asm volatile("barrier.cluster.arrive.aligned;" ::: "memory");
+            asm volatile("barrier.cluster.wait.aligned;" ::: "memory");
+            tot = rank == 0 ? tot + nrm_peer : nrm_peer + tot;   // the same order in both CTAs
+        }
+        if (rg == 0) {
             const float r = rsqrtf(tot / static_cast<float>(DV) + eps);
             const float gf[4] = {bf16_bits_to_f32(gw.x & 0xffffu), bf16_bits_to_f32(gw.x >> 16),
                                  bf16_bits_to_f32(gw.y & 0xffffu), bf16_bits_to_f32(gw.y >> 16)};
@@ -193,25 +213,57 @@ decode_step_kernel(const uint16_t* q, const uint16_t* k, const uint16_t* v, cons
     }
 }
 
-template <int DK, int DV>
-cudaError_t launch_decode(const void* q, const void* k, const void* v, const void* a, const void* b,
-                   int gate_dtype, const float* A_log, const float* dt_bias, const float* s_in,
-                   float* s_out, float* out, int B, int Hqk, int Hv, float scale, int l2qk, const void* z,
-                   const void* gamma, float eps, void* y, cudaStream_t st) {
-    using C = DecodeCfg<DK, DV>;
+template <int DK, int DV, int SPLIT>
+cudaError_t launch_decode_split(const void* q, const void* k, const void* v, const void* a, const void* b,
+                                int gate_dtype, const float* A_log, const float* dt_bias, const float* s_in,
+                                float* s_out, float* out, int B, int Hqk, int Hv, float scale, int l2qk,
+                                const void* z, const void* gamma, float eps, void* y, cudaStream_t st) {
+    using C = DecodeCfg<DK, DV, SPLIT>;
     cudaLaunchConfig_t cfg = {};
-    cfg.gridDim = dim3(B * Hv);
+    cfg.gridDim = dim3(B * Hv * SPLIT);
     cfg.blockDim = dim3(C::NT);
     cfg.stream = st;
-    cudaLaunchAttribute attr[1];
-    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
-    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    cudaLaunchAttribute attr[2];
+    int na = 0;
+    if (SPLIT > 1) {
+        attr[na].id = cudaLaunchAttributeClusterDimension;
+        attr[na].val.clusterDim.x = SPLIT;
+        attr[na].val.clusterDim.y = 1;
+        attr[na].val.clusterDim.z = 1;
+        ++na;
+    }
+    if (launch_overlap()) {
+        attr[na].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+        attr[na].val.programmaticStreamSerializationAllowed = 1;
+        ++na;
+    }
     cfg.attrs = attr;
-    cfg.numAttrs = launch_overlap() ? 1 : 0;
-    return cudaLaunchKernelEx(&cfg, decode_step_kernel<DK, DV>, static_cast<const uint16_t*>(q),
+    cfg.numAttrs = na;
+    return cudaLaunchKernelEx(&cfg, decode_step_kernel<DK, DV, SPLIT>, static_cast<const uint16_t*>(q),
                        static_cast<const uint16_t*>(k), static_cast<const uint16_t*>(v), a, b, gate_dtype, A_log,
                        dt_bias, s_in, s_out, out, Hqk, Hv, scale, l2qk, static_cast<const uint16_t*>(z),
                        static_cast<const uint16_t*>(gamma), eps, static_cast<uint16_t*>(y));
+}
+
+// One CTA per head, or a pair of CTAs per head: for few heads (dv >= 128) so that
+// the state streams through twice the SMs, and always at dv = 256, where one CTA
+// would need 1024 threads of at most 64 registers and spill.
+template <int DK, int DV>
+cudaError_t launch_decode(const void* q, const void* k, const void* v, const void* a, const void* b,
+                          int gate_dtype, const float* A_log, const float* dt_bias, const float* s_in,
+                          float* s_out, float* out, int B, int Hqk, int Hv, float scale, int l2qk, const void* z,
+                          const void* gamma, float eps, void* y, cudaStream_t st) {
+    int dev = 0, sms = 148;
+    if (cudaGetDevice(&dev) == cudaSuccess) cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+    if constexpr (DV >= 128) {
+        if (DV == 256 || 2L * B * Hv <= sms)
+            return launch_decode_split<DK, DV, 2>(q, k, v, a, b, gate_dtype, A_log, dt_bias, s_in, s_out, out, B, Hqk,
+                                                  Hv, scale, l2qk, z, gamma, eps, y, st);
+    }
+    if constexpr (DV < 256)
+        return launch_decode_split<DK, DV, 1>(q, k, v, a, b, gate_dtype, A_log, dt_bias, s_in, s_out, out, B, Hqk,
+                                              Hv, scale, l2qk, z, gamma, eps, y, st);
+    return cudaErrorInvalidValue;                      // unreachable: dv = 256 always splits
 }
 
 }  // namespace
