@@ -55,6 +55,8 @@ SIGNATURES = {
                         _I, _I, _I, _I, _I, _I, _I, _F, _P],
     "gdn_prefill_fwd_ws": [_P, _P, _P, _P, _P, _P, _I, _F, _P, _P, _P, _P, _P,
                            _I, _I, _I, _I, _I, _I, _I, _F, _P, _Z, _P],
+    "gdn_prefill_window_ws": [_P, _P, _P, _P, _P, _P, _I, _F, _P, _P, _P, _P, _P,
+                              _I, _I, _I, _I, _I, _I, _I, _I, _I, _F, _P, _Z, _P],
     "gdn_prefill_workspace_bytes": [_I, _I, _I, _I, _I],
     "gdn_prefill_fwd_noalloc": [_P, _P, _P, _P, _P, _P, _I, _F, _P, _P, _P, _P, _P,
                                 _I, _I, _I, _I, _I, _I, _I, _F, _P],
@@ -84,6 +86,7 @@ SIGNATURES = {
     "gdn_proj_multi_fwd": [_P, _I, _I, _I, ctypes.POINTER(ProjOutSeg), _I, _P],
     "gdn_outproj_rs_fwd": [_P, _P, ctypes.POINTER(ctypes.c_void_p), _I, _I, _I, _I, _I, _P],
     "gdn_outproj_reduce": [_P, _P, _I, _I, _I, _P],
+    "gdn_gather_window": [_P, ctypes.POINTER(ctypes.c_void_p), _I, _I, _I, _I, _I, _I, _I, _I, _I, _P],
     "gdn_check_device_error": [],
     "gdn_set_launch_overlap": [_I],
     "gdn_last_error": [],

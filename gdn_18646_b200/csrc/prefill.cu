@@ -1508,19 +1508,21 @@ int launch_prefill(const CUtensorMap& mq, const CUtensorMap& mk, const CUtensorM
 }
 
 // q/k/v/o map: dims (D, T, H, B) innermost first, box (64, 64, 1, 1), 128B swizzle.
-int make_act_map(CUtensorMap* m, const void* base, int D, int T, int H, int B, int layout) {
+// tld: tokens per row of the tensor the map reads (T for a whole tensor; the full
+// length when the map covers a token window starting at `base`).
+int make_act_map(CUtensorMap* m, const void* base, int D, int T, int H, int B, int layout, long tld = 0) {
     uint64_t dims[4] = {static_cast<uint64_t>(D), static_cast<uint64_t>(T), static_cast<uint64_t>(H),
                         static_cast<uint64_t>(B)};
     uint64_t strides[3];
-    const uint64_t e = 2;
+    const uint64_t e = 2, L = static_cast<uint64_t>(tld > 0 ? tld : T);
     if (layout == GDN_LAYOUT_BHTD) {
         strides[0] = e * D;                  // T
-        strides[1] = e * D * T;              // H
-        strides[2] = e * D * T * H;          // B
+        strides[1] = e * D * L;              // H
+        strides[2] = e * D * L * H;          // B
     } else {
         strides[0] = e * D * H;              // T
         strides[1] = e * D;                  // H
-        strides[2] = e * D * H * T;          // B
+        strides[2] = e * D * H * L;          // B
     }
     uint32_t box[4] = {64, 64, 1, 1};
     return make_map_bf16(m, base, 4, dims, strides, box, true);
@@ -1599,11 +1601,13 @@ namespace {
 // One prefill over B sequences of T tokens, or (cu != null) over B packed
 // sequences of at most T tokens each in tensors of Ttot tokens (layout BTHD,
 // batch 1), already validated.  gate_ld: elements between rows of a, b_logits
-// and mask (0 = T, dense).
+// and mask (0 = T, dense); tld: tokens per row of q, k, v and out (0 = T, dense;
+// larger when the call covers a token window of longer tensors).
 int run_prefill(const void* q, const void* k, const void* v, const float* A_log, const void* a, const void* b_logits,
                 int gate_dtype, float dt_bias, const float* dt_bias_vec, const float* mask, const float* state_in,
                 void* out, float* state_out, int B, int T, int Hqk, int Hv, int dk, int dv, int layout, float scale,
-                void* workspace, size_t workspace_bytes, void* stream, const int* cu, int Ttot, long gate_ld = 0) {
+                void* workspace, size_t workspace_bytes, void* stream, const int* cu, int Ttot, long gate_ld = 0,
+                long tld = 0) {
     int st = GDN_OK;
     const long ntiles = (dv + 127) / 128;
     const long nchunks = (static_cast<long>(T) + kC - 1) / kC;
@@ -1620,10 +1624,10 @@ int run_prefill(const void* q, const void* k, const void* v, const float* A_log,
     // varlen: the packed tensors are one batch of Ttot tokens
     const int mT = cu ? Ttot : T, mB = cu ? 1 : B;
     CUtensorMap mq, mk, mv, mo;
-    if ((st = make_act_map(&mq, q, dk, mT, Hqk, mB, layout)) != GDN_OK) return st;
-    if ((st = make_act_map(&mk, k, dk, mT, Hqk, mB, layout)) != GDN_OK) return st;
-    if ((st = make_act_map(&mv, v, dv, mT, Hv, mB, layout)) != GDN_OK) return st;
-    if ((st = make_act_map(&mo, out, dv, mT, Hv, mB, layout)) != GDN_OK) return st;
+    if ((st = make_act_map(&mq, q, dk, mT, Hqk, mB, layout, tld)) != GDN_OK) return st;
+    if ((st = make_act_map(&mk, k, dk, mT, Hqk, mB, layout, tld)) != GDN_OK) return st;
+    if ((st = make_act_map(&mv, v, dv, mT, Hv, mB, layout, tld)) != GDN_OK) return st;
+    if ((st = make_act_map(&mo, out, dv, mT, Hv, mB, layout, tld)) != GDN_OK) return st;
 
     GateArgs ga;
     ga.a = a;
@@ -1719,6 +1723,35 @@ int prefill_segment(const void* q, const void* k, const void* v, const float* A_
                        B, T, Hqk, Hv, dk, dv, layout, scale, workspace, workspace_bytes, stream, nullptr, 0, gate_ld);
 }
 }  // namespace gdn
+
+// Tokens [t0, t0 + Tw) of tensors holding T tokens per sequence: q, k, v, out,
+// the gates and the mask are the whole tensors, read and written in place (no
+// copies); state_in is the state before token t0, state_out the state after token
+// t0 + Tw - 1.  Consecutive windows chained through their states give the whole
+// call's result; with window bounds on 64-token chunk boundaries, bit for bit.
+extern "C" int gdn_prefill_window_ws(const void* q, const void* k, const void* v, const float* A_log, const void* a,
+                                     const void* b_logits, int gate_dtype, float dt_bias, const float* dt_bias_vec,
+                                     const float* mask, const float* state_in, void* out, float* state_out, int B,
+                                     int T, int t0, int Tw, int Hqk, int Hv, int dk, int dv, int layout, float scale,
+                                     void* workspace, size_t workspace_bytes, void* stream) {
+    using namespace gdn;
+    const int st = validate_prefill(q, k, v, A_log, a, b_logits, gate_dtype, state_in, out, state_out, B, T, Hqk, Hv,
+                                    dk, dv, layout);
+    if (st != GDN_OK) return st;
+    if (t0 < 0 || Tw <= 0 || static_cast<long>(t0) + Tw > T)
+        return fail(GDN_ERR_SHAPE, "gdn_prefill_window_ws: window [%d, %d + %d) outside T=%d", t0, t0, Tw, T);
+    const bool bhtd = layout == GDN_LAYOUT_BHTD;
+    const long tq = bhtd ? dk : static_cast<long>(Hqk) * dk;     // elements between tokens
+    const long tv = bhtd ? dv : static_cast<long>(Hv) * dv;
+    const size_t ge = gate_dtype == GDN_DTYPE_BF16 ? 2 : 4;
+    const auto at = [](const void* p, size_t bytes) {
+        return static_cast<const void*>(static_cast<const uint8_t*>(p) + bytes);
+    };
+    return run_prefill(at(q, t0 * tq * 2), at(k, t0 * tq * 2), at(v, t0 * tv * 2), A_log, at(a, t0 * ge),
+                       at(b_logits, t0 * ge), gate_dtype, dt_bias, dt_bias_vec, mask ? mask + t0 : nullptr, state_in,
+                       static_cast<uint8_t*>(out) + t0 * tv * 2, state_out, B, Tw, Hqk, Hv, dk, dv, layout, scale,
+                       workspace, workspace_bytes, stream, nullptr, 0, T, T);
+}
 
 // Same call with the workspace taken from the stream-ordered allocator for the
 // duration of the call.

@@ -70,6 +70,49 @@ def prefill(q, k, v, A_log, a, b_logits, *, dt_bias=0.0, mask=None, state_in=Non
     mask [B,T] f32 or None; state_in [B,Hv,dk,dv] f32 or None.
     Returns (out bf16 in v's layout, state_out f32 [B,Hv,dk,dv] or None).
     """
+    lay, B, T, Hqk, Hv, dk, dv, gdt, dt_scalar, dt_vec = _prefill_checks(q, k, v, A_log, a, b_logits, dt_bias, mask,
+                                                                         state_in, layout)
+    if out is None:
+        out = torch.empty_like(v)
+    if state_out is None and return_state:
+        state_out = torch.empty(B, Hv, dk, dv, dtype=torch.float32, device=q.device)
+    ws_bytes = _lib.lib().gdn_prefill_workspace_bytes(B, T, Hv, dk, dv)
+    ws = torch.empty(max(int(ws_bytes), 1), dtype=torch.uint8, device=q.device)
+    _lib.call("gdn_prefill_fwd_ws", _ptr(q), _ptr(k), _ptr(v), _ptr(A_log), _ptr(a), _ptr(b_logits), gdt,
+              dt_scalar, _ptr(dt_vec), _ptr(mask), _ptr(state_in), _ptr(out), _ptr(state_out),
+              B, T, Hqk, Hv, dk, dv, lay, float(scale), _ptr(ws), int(ws_bytes), _stream())
+    return out, state_out
+
+
+def prefill_window(q, k, v, A_log, a, b_logits, t0, Tw, *, out, dt_bias=0.0, mask=None, state_in=None,
+                   state_out=None, scale=0.0, layout="bhtd", workspace=None):
+    """``prefill`` over the tokens [t0, t0 + Tw) of the given (whole) tensors
+    (gdn_prefill_window_ws): reads the window's q, k, v, gates and mask in place
+    and writes its o into the same tokens of ``out``; ``state_in`` is the state
+    before token t0, ``state_out`` the state after the window.  ``workspace``: a
+    uint8 CUDA tensor of at least gdn_prefill_workspace_bytes(B, Tw, Hv, dk, dv)
+    bytes (allocated per call if None)."""
+    lay, B, T, Hqk, Hv, dk, dv, gdt, dt_scalar, dt_vec = _prefill_checks(q, k, v, A_log, a, b_logits, dt_bias, mask,
+                                                                         state_in, layout)
+    _cuda_contig(out, "out", torch.bfloat16)
+    _need(tuple(out.shape) == tuple(v.shape), "out must have v's shape")
+    if state_out is not None:
+        _cuda_contig(state_out, "state_out", torch.float32)
+    ws_bytes = int(_lib.lib().gdn_prefill_workspace_bytes(B, max(int(Tw), 1), Hv, dk, dv))
+    if workspace is None:
+        workspace = torch.empty(max(ws_bytes, 1), dtype=torch.uint8, device=q.device)
+    _need(workspace.is_cuda and workspace.dtype == torch.uint8 and workspace.numel() >= ws_bytes,
+          f"workspace: uint8 CUDA tensor of at least {ws_bytes} bytes required")
+    _lib.call("gdn_prefill_window_ws", _ptr(q), _ptr(k), _ptr(v), _ptr(A_log), _ptr(a), _ptr(b_logits), gdt,
+              dt_scalar, _ptr(dt_vec), _ptr(mask), _ptr(state_in), _ptr(out), _ptr(state_out),
+              B, T, int(t0), int(Tw), Hqk, Hv, dk, dv, lay, float(scale), _ptr(workspace), workspace.numel(),
+              _stream())
+    return out, state_out
+
+
+def _prefill_checks(q, k, v, A_log, a, b_logits, dt_bias, mask, state_in, layout):
+    """Shape, dtype and device checks shared by the prefill wrappers; returns
+    (layout code, B, T, Hqk, Hv, dk, dv, gate dtype code, dt_bias scalar, dt_bias vector)."""
     lay = GDN_LAYOUT_BHTD if layout == "bhtd" else GDN_LAYOUT_BTHD
     for name, t in (("q", q), ("k", k), ("v", v)):
         _cuda_contig(t, name, torch.bfloat16)
@@ -97,16 +140,7 @@ def prefill(q, k, v, A_log, a, b_logits, *, dt_bias=0.0, mask=None, state_in=Non
         _cuda_contig(mask, "mask", torch.float32)
     if state_in is not None:
         _cuda_contig(state_in, "state_in", torch.float32)
-    if out is None:
-        out = torch.empty_like(v)
-    if state_out is None and return_state:
-        state_out = torch.empty(B, Hv, dk, dv, dtype=torch.float32, device=q.device)
-    ws_bytes = _lib.lib().gdn_prefill_workspace_bytes(B, T, Hv, dk, dv)
-    ws = torch.empty(max(int(ws_bytes), 1), dtype=torch.uint8, device=q.device)
-    _lib.call("gdn_prefill_fwd_ws", _ptr(q), _ptr(k), _ptr(v), _ptr(A_log), _ptr(a), _ptr(b_logits), gdt,
-              dt_scalar, _ptr(dt_vec), _ptr(mask), _ptr(state_in), _ptr(out), _ptr(state_out),
-              B, T, Hqk, Hv, dk, dv, lay, float(scale), _ptr(ws), int(ws_bytes), _stream())
-    return out, state_out
+    return lay, B, T, Hqk, Hv, dk, dv, gdt, dt_scalar, dt_vec
 
 
 def _contig(t: torch.Tensor, name: str, dtype=None) -> None:
@@ -341,6 +375,29 @@ def outproj_rs(x, W, recv_ptrs, rank, world):
     arr = (ctypes.c_void_p * world)(*[int(p) for p in recv_ptrs])
     _lib.call("gdn_outproj_rs_fwd", _ptr(x), _ptr(W), arr, x.shape[0], W.shape[0], x.shape[1], int(rank), int(world),
               _stream())
+
+
+def gather_window(gathered, peer_ptrs, rank, t0, Tw, layout="bhtd", stream=None):
+    """Pull tokens [t0, t0 + Tw) of every peer's slot of a head-sharded o into the
+    same slots of ``gathered`` [world, B, H_local, T, dv] ("bhtd") or [world, B, T,
+    H_local, dv] ("bthd") (gdn_gather_window): one copy-engine transfer per peer
+    from ``peer_ptrs[p]`` (rank p's gathered buffer, mapped into this process),
+    enqueued on ``stream`` (default: the current stream).  Only enqueues; the
+    caller orders it after the peers wrote the window."""
+    _cuda_contig(gathered, "gathered", torch.bfloat16)
+    _need(gathered.dim() == 5, "gathered must be [world, B, H, T, dv] or [world, B, T, H, dv]")
+    _need(layout in ("bhtd", "bthd"), f"layout must be 'bhtd' or 'bthd', got {layout!r}")
+    world = gathered.shape[0]
+    _need(len(peer_ptrs) == world, "one peer pointer per rank")
+    if layout == "bhtd":
+        _, B, H, T, dv = gathered.shape
+        lay = GDN_LAYOUT_BHTD
+    else:
+        _, B, T, H, dv = gathered.shape
+        lay = GDN_LAYOUT_BTHD
+    arr = (ctypes.c_void_p * world)(*[int(p) for p in peer_ptrs])
+    s = stream.cuda_stream if stream is not None else _stream()
+    _lib.call("gdn_gather_window", _ptr(gathered), arr, world, int(rank), B, T, H, dv, lay, int(t0), int(Tw), s)
 
 
 def outproj_reduce(recv, out=None):

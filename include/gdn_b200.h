@@ -122,6 +122,28 @@ int gdn_prefill_fwd_ws(const void* q, const void* k, const void* v,
                        float scale, void* workspace, size_t workspace_bytes, void* stream);
 
 /*
+ * gdn_prefill_fwd_ws over the token window [t0, t0 + Tw) of tensors that hold T
+ * tokens per sequence.  q, k, v, out, a, b_logits and mask are the WHOLE tensors
+ * (read and written in place at the window's tokens; nothing is copied);
+ * state_in is the state before token t0 (NULL: zeros), state_out the state
+ * after token t0 + Tw - 1.  The workspace is sized for the window:
+ * gdn_prefill_workspace_bytes(B, Tw, Hv, dk, dv).  Windows chained through
+ * their states give the whole call's o and final state, bit-identical when
+ * every window starts on a 64-token chunk boundary.  Used to overlap the
+ * all-gather of a head-sharded o with the prefill (a window's o is shipped
+ * while the next window runs).  No counterpart in the reference.
+ * Errors: GDN_ERR_SHAPE when the window leaves [0, T); otherwise as
+ * gdn_prefill_fwd_ws.
+ */
+int gdn_prefill_window_ws(const void* q, const void* k, const void* v,
+                          const float* A_log, const void* a, const void* b_logits, int gate_dtype,
+                          float dt_bias, const float* dt_bias_vec,
+                          const float* mask, const float* state_in,
+                          void* out, float* state_out,
+                          int B, int T, int t0, int Tw, int Hqk, int Hv, int dk, int dv, int layout,
+                          float scale, void* workspace, size_t workspace_bytes, void* stream);
+
+/*
  * gdn_prefill_fwd for callers that cannot allocate device memory.  No
  * counterpart in the reference, whose kernel needs no workspace.
  *
@@ -414,6 +436,42 @@ const char* gdn_last_error(void);
  * No counterpart in the reference.
  */
 int gdn_set_launch_overlap(int on);
+
+/*
+ * Multi-GPU entries (one process per GPU of a node; peer buffers are CUDA IPC
+ * mappings of the other ranks' device memory).  No counterpart in the
+ * reference, which runs on one GPU.
+ *
+ * gdn_outproj_rs_fwd: the head-sharded output projection fused with its
+ * reduce-scatter.  x bf16 [M, K] (this rank's gated-normed head outputs), W
+ * bf16 [N, K] (its columns of the projection); the partial product x W^T is
+ * written tile by tile into recv[d] + rank * (M / world) * N, the slot of
+ * rank d's receive buffer [world][M / world][N] for the rows d owns
+ * ([d * M / world, (d + 1) * M / world)).  recv[r] for every rank r, 16-byte
+ * aligned.  Needs N % 128 == 0, K % 64 == 0, M % (256 * world) == 0,
+ * 1 <= world <= 8.  The caller orders it after the previous reduction on every
+ * rank and orders gdn_outproj_reduce after every rank's launch.
+ * gdn_outproj_reduce: out bf16 [rows, N] = the sum of the world slots of recv
+ * [world][rows][N] (fp32 accumulation).
+ */
+int gdn_outproj_rs_fwd(const void* x, const void* W, void* const* recv, int M, int N, int K, int rank,
+                       int world, void* stream);
+int gdn_outproj_reduce(const void* recv, void* out, int rows, int N, int world, void* stream);
+
+/*
+ * The all-gather of a head-sharded prefill output, one token window at a time.
+ * gathered: this rank's buffer [world][B][H_local][T][dv] (layout BHTD) or
+ * [world][B][T][H_local][dv] (BTHD) bf16, whose slot `rank` holds this rank's o;
+ * peer_gathered[p]: rank p's gathered buffer mapped into this process (entry
+ * `rank` unused).  Copies tokens [t0, t0 + Tw) of slot p from every peer p
+ * into slot p of `gathered`, one strided copy-engine transfer per peer on
+ * `stream` (no kernel, no SM).  The caller orders it after each peer wrote
+ * that window (gdn_prefill_window_ws on the peer) and before any peer rewrites
+ * it.  Errors: GDN_ERR_NULL, GDN_ERR_SHAPE (window outside [0, T)),
+ * GDN_ERR_DTYPE (layout), GDN_ERR_CUDA.
+ */
+int gdn_gather_window(void* gathered, const void* const* peer_gathered, int world, int rank, int B, int T,
+                      int H_local, int dv, int layout, int t0, int Tw, void* stream);
 
 /* Library version string. */
 const char* gdn_version(void);

@@ -316,3 +316,34 @@ def test_proj_multi_rejects(lib):
     assert _lib.call_status("gdn_proj_multi_fwd", FAKE, 1, 8, 64, segs, 2, None) == _lib.GDN_ERR_ALIGN
     segs[1].y, segs[1].W = FAKE, None
     assert _lib.call_status("gdn_proj_multi_fwd", FAKE, 1, 8, 64, segs, 2, None) == _lib.GDN_ERR_NULL
+
+
+def test_prefill_window_rejects(lib):
+    def call(t0=0, Tw=64, ws=ODD, wsb=1 << 40, **over):
+        args = prefill_args(**over)
+        head, tail = args[:15], args[15:-2]              # ... B, T | Hqk, Hv, dk, dv, layout
+        scale = args[-2]
+        return _lib.call_status("gdn_prefill_window_ws", *head, t0, Tw, *tail, scale, ws, wsb, None)
+    assert call(q=None) == _lib.GDN_ERR_NULL
+    assert call(T=128, t0=-64) == _lib.GDN_ERR_SHAPE
+    assert call(T=128, t0=64, Tw=65) == _lib.GDN_ERR_SHAPE
+    assert call(T=128, Tw=0) == _lib.GDN_ERR_SHAPE
+    assert "window" in _lib.last_error()
+    assert call(T=128, t0=64, Tw=64, wsb=16) == _lib.GDN_ERR_SHAPE   # workspace below the window's size
+    assert call(T=128, t0=64, Tw=64) == _lib.GDN_ERR_ALIGN            # everything else valid: the workspace
+    assert call(T=128, t0=64, Tw=64, dk=96) == _lib.GDN_ERR_UNSUPPORTED
+
+
+def test_gather_window_rejects(lib):
+    two = (ctypes.c_void_p * 2)(FAKE, FAKE)
+    one_missing = (ctypes.c_void_p * 2)(FAKE, None)
+    def call(g=FAKE, peers=two, world=2, rank=0, B=1, T=128, H=2, dv=128, layout=0, t0=0, Tw=64):
+        return _lib.call_status("gdn_gather_window", g, peers, world, rank, B, T, H, dv, layout, t0, Tw, None)
+    assert call(g=None) == _lib.GDN_ERR_NULL
+    assert call(peers=None) == _lib.GDN_ERR_NULL
+    assert call(peers=one_missing) == _lib.GDN_ERR_NULL               # rank 1's buffer is needed by rank 0
+    assert call(rank=2) == _lib.GDN_ERR_SHAPE
+    assert call(world=0) == _lib.GDN_ERR_SHAPE
+    assert call(t0=64, Tw=128) == _lib.GDN_ERR_SHAPE
+    assert call(layout=3) == _lib.GDN_ERR_DTYPE
+    assert call(world=1, rank=0, peers=one_missing) == _lib.GDN_OK   # nothing to pull, nothing enqueued

@@ -39,6 +39,27 @@ def test_head_shard_plan():
     assert [(s.start, s.stop) for s in sl] == [(0, 3), (3, 6), (6, 8), (8, 10)]
 
 
+@pytest.mark.parametrize("T", [1, 63, 64, 65, 1000, 4096, 32768, 70001])
+@pytest.mark.parametrize("w", [0, 64, 1000, 4096])
+def test_window_plan(T, w):
+    for ladder in (True, False):
+        plan = SH.window_plan(T, w, ladder)
+        assert plan[0][0] == 0 and sum(tw for _, tw in plan) == T
+        assert all(t0 + tw == nxt for (t0, tw), (nxt, _) in zip(plan, plan[1:]))   # contiguous
+        assert all(t0 % 64 == 0 for t0, _ in plan)                                  # chunk-aligned starts
+        wt = -(-w // 64) * 64 if w else None
+        if wt:
+            assert max(tw for _, tw in plan) <= wt
+        if ladder and len(plan) > 1:
+            assert plan[-1][1] <= 64                                                # a one-chunk tail
+    assert [tw for _, tw in SH.window_plan(32768, 4096, False)] == [4096] * 8
+    assert [tw for _, tw in SH.window_plan(32768, 4096, True)] == [4096] * 7 + [2048, 1024, 512, 256, 128, 64, 64]
+    with pytest.raises(ValueError):
+        SH.window_plan(0)
+    with pytest.raises(ValueError):
+        SH.window_plan(64, -1)
+
+
 def _gather_worker(rank, world, port, q):
     _init(rank, world, port)
     try:
