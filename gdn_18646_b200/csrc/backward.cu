@@ -207,19 +207,14 @@ __global__ void __launch_bounds__(128) bwd_reverse_kernel(const BwdArgs a) {
 #pragma unroll
     for (int i = 0; i < L::ROWS; ++i)
         dS[i] = a.dS_final ? a.dS_final[s0 + static_cast<long>(i0 + i) * DV + j] : 0.f;
-    // S_p of the next two tokens, loaded two tokens ahead (the loads are the
-    // long-latency part of a step; one token of compute did not always cover them)
-    float SpN[L::ROWS], SpNN[L::ROWS];
+    // S_p of the token processed next, loaded one token ahead (the loads are the
+    // long-latency part of a step)
+    float SpN[L::ROWS];
     const long tok_first = static_cast<long>(bh) * a.T;
     {
         const float* sp = a.states + ((tok_first + a.T - 1) * DK + i0) * DV + j;
 #pragma unroll
         for (int i = 0; i < L::ROWS; ++i) SpN[i] = sp[static_cast<long>(i) * DV];
-        if (a.T >= 2) {
-            sp -= static_cast<long>(DK) * DV;
-#pragma unroll
-            for (int i = 0; i < L::ROWS; ++i) SpNN[i] = sp[static_cast<long>(i) * DV];
-        }
     }
     for (int tend = a.T; tend > 0; tend -= kRevTB) {
         const int tb = max(0, tend - kRevTB), nt = tend - tb;
@@ -247,17 +242,14 @@ __global__ void __launch_bounds__(128) bwd_reverse_kernel(const BwdArgs a) {
             const float dos = mdo[u][jc];
             const float sdo = a.scale * dos;
             const float g = gs[u], bm = bs[u];
-            // S_p of these rows (forward pass), loaded two steps ago; start the one after next
+            // S_p of these rows (forward pass), loaded during the previous step; start the next
             float Sp[L::ROWS];
 #pragma unroll
-            for (int i = 0; i < L::ROWS; ++i) {
-                Sp[i] = SpN[i];
-                SpN[i] = SpNN[i];
-            }
-            if (tok - 2 >= tok_first) {
-                const float* sp = a.states + ((tok - 2) * DK + i0) * DV + j;
+            for (int i = 0; i < L::ROWS; ++i) Sp[i] = SpN[i];
+            if (tok > tok_first) {
+                const float* sp = a.states + ((tok - 1) * DK + i0) * DV + j;
 #pragma unroll
-                for (int i = 0; i < L::ROWS; ++i) SpNN[i] = sp[static_cast<long>(i) * DV];
+                for (int i = 0; i < L::ROWS; ++i) SpN[i] = sp[static_cast<long>(i) * DV];
             }
             float e0 = 0.f, e1 = 0.f, e2 = 0.f, e3 = 0.f;
 #pragma unroll
