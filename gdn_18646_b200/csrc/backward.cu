@@ -266,14 +266,14 @@ __global__ void __launch_bounds__(128) bwd_reverse_kernel(const BwdArgs a) {
             const float ddj = sum_parts<L::PARTS, L::COLS>((e0 + e1) + (e2 + e3));
             if (i0 == 0) a.dv[tok * DV + j] = bm * ddj;
             const float rp = rps[u][jc], vj = vv[u][jc];
-            const float r = g * rp, dlt = bm * (vj - r), dr = -bm * ddj;
+            const float r = g * rp, dlt = bm * (vj - r), dr = -bm * ddj, gdr = g * dr;
             // products for the row sums (dq, dk) and <S_p, dS>
             float X[32], Y[32];
             float sds = 0.f;
 #pragma unroll
             for (int i = 0; i < L::ROWS; ++i) {
                 X[i] = Sp[i] * dos;
-                Y[i] = fmaf(dS[i], dlt, g * Sp[i] * dr);
+                Y[i] = fmaf(dS[i], dlt, Sp[i] * gdr);
                 sds = fmaf(Sp[i], dS[i], sds);
             }
             float c0 = 0.f, c1 = 0.f, c2 = 0.f;        // column scalars, once per column
@@ -285,11 +285,14 @@ __global__ void __launch_bounds__(128) bwd_reverse_kernel(const BwdArgs a) {
             rows_reduce_scatter<L::COLS>(X, jl);
             rows_reduce_scatter<L::COLS>(Y, jl);
 #pragma unroll
-            for (int o = 16; o > 0; o >>= 1) {
+            for (int o = 16; o > 0; o >>= 1) sds += __shfl_xor_sync(0xffffffffu, sds, o);
+            // the column scalars live on lanes 0 .. COLS-1 (zero elsewhere): their sum
+            // reaches lane 0, the only reader, in log2(COLS) steps
+#pragma unroll
+            for (int o = L::COLS / 2; o > 0; o >>= 1) {
                 c0 += __shfl_xor_sync(0xffffffffu, c0, o);
                 c1 += __shfl_xor_sync(0xffffffffu, c1, o);
                 c2 += __shfl_xor_sync(0xffffffffu, c2, o);
-                sds += __shfl_xor_sync(0xffffffffu, sds, o);
             }
             const int pb = u & 1;
 #pragma unroll
