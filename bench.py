@@ -482,7 +482,7 @@ def run_backward(world, dev, stream, hbm_peak):
 
 # Config 4's o all-gather runs window by window beside the prefill: windows of
 # this many tokens, the last one cut into halving windows down to one chunk.
-C4_WINDOW = 4096
+C4_WINDOW = 8192
 C4_LADDER = True
 
 
