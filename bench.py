@@ -260,6 +260,8 @@ def run_ours(args):
     lay = run_layer(world, dev, stream, hbm_peak)
     vl = run_varlen(world, dev, stream)
     bw = run_backward(world, dev, stream, hbm_peak)
+    nrm = run_norm(world, dev, stream, hbm_peak)
+    lng = long_context(args, rank, world, dev, stream, hbm_peak, tf_peak)
     cpu = cpu_baseline_prefill() if (rank == 0 and world == 1 and not args.no_cpu_baseline) else None
 
     if rank == 0:
@@ -289,16 +291,23 @@ def run_ours(args):
             "layer": lay,
             "varlen": vl,
             "backward": bw,
+            "norm": nrm,
+            "long": lng,
             "cpu_baseline": cpu,
         }
         print(json.dumps(line), flush=True)
     finish(world)
 
 
-# ncu-measured DRAM bytes (dram__bytes_read.sum + dram__bytes_write.sum): one
-# config-1 prefill step (its gates, lead prep and streamed prep + chain launches,
-# summed) from profiles/prefill_config1.md, and one decode launch from
-# profiles/decode_step_kernel_config2.md (543.2 + 479.7 MB).
+# DRAM bytes per launch (dram__bytes_read.sum + dram__bytes_write.sum) from one
+# ncu capture each; they are constants of the build they were taken on and are
+# re-taken when the kernels change:
+#   prefill: one config-1 step (gates + the streamed prep/chain launch, summed),
+#     ncu --metrics gpu__time_duration.sum,dram__bytes_read.sum,dram__bytes_write.sum
+#         --clock-control none -k regex:prefill -c 2 python bench.py --only prefill --steps 1 --warmup 0
+#   decode: one config-2 step (543.2 MB read + 479.7 MB written),
+#     ncu --metrics dram__bytes_read.sum,dram__bytes_write.sum --clock-control none
+#         -k regex:decode_step -c 1 python bench.py --only decode --steps 1 --warmup 0
 PREFILL_TRAFFIC_PER_STEP = 677.6e6
 DECODE_TRAFFIC_PER_LAUNCH = 1022.9e6
 
@@ -403,6 +412,52 @@ def run_layer(world, dev, stream, hbm_peak):
             "decode_stacked_frac_of_measured_hbm": (w_bytes + state_bytes) / (ms_stack * 1e-3) / 1e9 / hbm_peak}
 
 
+def run_norm(world, dev, stream, hbm_peak):
+    """Config 3's norms alone, HBM-bound: the input RMSNorm over x [2*8192, 2048]
+    (bf16 in and out: 4 B per element) and the gated output norm over the
+    prefill's o [2*8192*32, 128] with z (bf16 x, z, y: 6 B per element).  Four
+    rotating input sets (RMSNorm: 4 x 64 MB) and outputs larger than L2 together,
+    so every launch reads its input from HBM."""
+    import torch
+    from gdn_18646_b200 import ops
+    g = torch.Generator(device=dev).manual_seed(21)
+    R, D = 2 * 8192, 2048
+    xs = [torch.randn(R, D, generator=g, device=dev).bfloat16() for _ in range(4)]
+    ys = [torch.empty_like(x) for x in xs]
+    gamma = (1.0 + 0.1 * torch.randn(D, generator=g, device=dev)).bfloat16()
+    it = {"i": 0}
+
+    def rms():
+        i = it["i"] % 4
+        it["i"] += 1
+        ops.rmsnorm(xs[i], gamma, 1e-6, out=ys[i])
+
+    steps = 40
+    ms_r = timed(rms, steps, 4, world, stream) / steps
+    bytes_r = R * D * 4
+    del xs, ys
+    Rg, Dg = 2 * 8192 * 32, 128
+    os_ = [torch.randn(Rg, Dg, generator=g, device=dev).bfloat16() for _ in range(2)]
+    zs = [torch.randn(Rg, Dg, generator=g, device=dev).bfloat16() for _ in range(2)]
+    yg = [torch.empty_like(o) for o in os_]
+    gam = (1.0 + 0.1 * torch.randn(Dg, generator=g, device=dev)).bfloat16()
+
+    def gated():
+        i = it["i"] % 2
+        it["i"] += 1
+        ops.gated_rmsnorm(os_[i], zs[i], gam, 1e-6, out=yg[i])
+
+    ms_g = timed(gated, steps, 4, world, stream) / steps
+    bytes_g = Rg * Dg * 6
+    gbs_r, gbs_g = bytes_r / (ms_r * 1e-3) / 1e9, bytes_g / (ms_g * 1e-3) / 1e9
+    return {"rmsnorm": {"config": f"x [{R}, {D}] bf16 -> bf16 (config 3's input norm)", "ms": ms_r,
+                        "bytes": bytes_r, "gbs": gbs_r, "frac_of_measured_hbm": gbs_r / hbm_peak,
+                        "frac_of_8000": gbs_r / 8000.0},
+            "gated_rmsnorm": {"config": f"o, z [{Rg}, {Dg}] bf16 -> y bf16 (config 3's output norm)", "ms": ms_g,
+                              "bytes": bytes_g, "gbs": gbs_g, "frac_of_measured_hbm": gbs_g / hbm_peak,
+                              "frac_of_8000": gbs_g / 8000.0}}
+
+
 def run_varlen(world, dev, stream):
     """Packed variable-length prefill against the same sequences padded to the
     longest one: 16 sequences of seeded lengths in [64, 4096] (H=16, dk=dv=128,
@@ -486,21 +541,36 @@ C4_WINDOW = 8192
 C4_LADDER = True
 
 
-def run_long(args, rank, world, dev, stream, hbm_peak, tf_peak, peak_kind):
-    """Config 4: head-sharded long-context prefill with o all-gathered: the
-    overlapped copy-engine gather (the line's value) and, for comparison, the
-    whole prefill followed by an NCCL all-gather."""
+# NVLink per-direction peer-copy bandwidth measured on this pool's B200s (GB/s);
+# the copy-engine pulls of the config-4 gather are reported against it.
+NVLINK_PEER_GBS = 770.0
+
+
+def long_context(args, rank, world, dev, stream, hbm_peak, tf_peak, clocks=None):
+    """Config 4 (B=8, T=32768, H=32, dk=dv=128): heads split evenly over the N
+    ranks.  Measures, per N:
+      kernel_only  the prefill of this rank's heads, no gather;
+      windowed     (N>1) the prefill with the all-gather of o overlapped window by
+                   window (copy-engine pulls over NVLink, WindowedHeadGather);
+      nccl_gather  (N>1) the whole prefill, then NCCL all_gather_into_tensor;
+      gather_pull  (N>1) the pulls alone: GB received per rank, GB/s against the
+                   measured NVLink per-direction peer-copy rate;
+      layer_tail   the head-sharded output projection (see run_layer_tail).
+    Tokens/s count the whole job (B*T); kernel-only and gather-included scaling
+    are separate numbers."""
     import torch
     from gdn_18646_b200 import _lib, ops
     c = C4
     H = c["H"]
     assert H % world == 0, "heads must split evenly"
     Hs = H // world
+    steps, warm = max(3, min(args.steps, 10)), 3
     inp = gen_prefill(c["B"], c["T"], H, c["dk"], c["dv"], 4321 + rank, dev, layout="bhtd", Hs=Hs, state=False)
     out = torch.empty_like(inp["v"])
     s_out = torch.empty(c["B"], Hs, c["dk"], c["dv"], device=dev)
     gathered = torch.empty((world,) + tuple(out.shape), dtype=out.dtype, device=dev) if world > 1 else None
     scale = 1.0 / math.sqrt(c["dk"])
+    tokens = c["B"] * c["T"]
 
     def kernel_only():
         ops.prefill(inp["q"], inp["k"], inp["v"], inp["A_log"], inp["a"], inp["b"], scale=scale, out=out,
@@ -508,59 +578,75 @@ def run_long(args, rank, world, dev, stream, hbm_peak, tf_peak, peak_kind):
 
     def with_gather():
         kernel_only()
-        if world > 1:
-            import torch.distributed as dist
-            dist.all_gather_into_tensor(gathered, out)
+        import torch.distributed as dist
+        dist.all_gather_into_tensor(gathered, out)
 
-    gath = None
+    ms_k = timed(kernel_only, steps, warm, world, stream, clocks if world == 1 else None) / steps
+    alg = prefill_alg_bytes(c["B"], c["T"], Hs, c["dk"], c["dv"])
+    flops = FLOP_PER_TOKEN_HEAD(c["dk"], c["dv"]) * c["B"] * c["T"] * Hs
+    res = {"config": f"config4 B={c['B']} T={c['T']} H={H}, {Hs} heads per GPU x{world}",
+           "kernel_only": {"tokens_per_s": tokens / (ms_k * 1e-3), "ms_per_step": ms_k,
+                           "alg_gbs_per_gpu": alg / (ms_k * 1e-3) / 1e9,
+                           "frac_of_measured_hbm": alg / (ms_k * 1e-3) / 1e9 / hbm_peak,
+                           "tensor_tflops_per_gpu": flops / (ms_k * 1e-3) / 1e12},
+           "launches_per_step": _lib.lib().gdn_prefill_launch_count(c["B"], c["T"], Hs, c["dk"], c["dv"])}
     if world > 1:
         from gdn_18646_b200.sharding import WindowedHeadGather, window_plan
         gath = WindowedHeadGather(c["B"], c["T"], Hs, c["dv"], layout="bhtd")
         plan = window_plan(c["T"], C4_WINDOW, C4_LADDER)
 
-    def windowed():
-        gath.prefill(inp["q"], inp["k"], inp["v"], inp["A_log"], inp["a"], inp["b"], scale=scale, state_out=s_out,
-                     window_tokens=C4_WINDOW, ladder=C4_LADDER)
+        def windowed():
+            gath.prefill(inp["q"], inp["k"], inp["v"], inp["A_log"], inp["a"], inp["b"], scale=scale, state_out=s_out,
+                         window_tokens=C4_WINDOW, ladder=C4_LADDER)
 
-    ms_k = timed(kernel_only, args.steps, args.warmup, world, stream) / args.steps
-    clocks = ClockSampler(int(os.environ.get("LOCAL_RANK", "0")))
-    nccl = None
-    if world > 1:
-        ms_n = timed(with_gather, args.steps, args.warmup, world, stream) / args.steps
-        ms = timed(windowed, args.steps, args.warmup, world, stream, clocks) / args.steps
-        nccl = {"value": c["B"] * c["T"] / (ms_n * 1e-3), "ms_per_step": ms_n,
-                "what": "the whole prefill, then NCCL all_gather_into_tensor of o"}
-        launches = sum(_lib.lib().gdn_prefill_launch_count(c["B"], tw, Hs, c["dk"], c["dv"]) for _, tw in plan)
+        ms_n = timed(with_gather, steps, warm, world, stream) / steps
+        ms_w = timed(windowed, steps, warm, world, stream, clocks) / steps
+        ms_p = timed(gath.pull, steps, warm, world, stream) / steps
+        recv = (world - 1) * c["B"] * Hs * c["T"] * c["dv"] * 2
+        res["windowed"] = {"tokens_per_s": tokens / (ms_w * 1e-3), "ms_per_step": ms_w,
+                           "window_tokens": C4_WINDOW, "windows": len(plan),
+                           "what": "prefill window by window, o of every window pulled from the peers over NVLink "
+                                   "by copy-engine transfers while the next window computes"}
+        res["nccl_gather"] = {"tokens_per_s": tokens / (ms_n * 1e-3), "ms_per_step": ms_n,
+                              "what": "the whole prefill, then NCCL all_gather_into_tensor of o"}
+        res["gather_pull"] = {"gb_received_per_gpu": recv / 1e9, "ms": ms_p, "gbs_per_gpu": recv / (ms_p * 1e-3) / 1e9,
+                              "frac_of_nvlink_peer_copy": recv / (ms_p * 1e-3) / 1e9 / NVLINK_PEER_GBS,
+                              "nvlink_peer_copy_gbs": NVLINK_PEER_GBS}
+        res["launches_per_step"] = sum(_lib.lib().gdn_prefill_launch_count(c["B"], tw, Hs, c["dk"], c["dv"])
+                                       for _, tw in plan)
+        torch.cuda.synchronize()
         gath.close()
-    else:
-        ms = timed(with_gather, args.steps, args.warmup, world, stream, clocks) / args.steps
-        launches = _lib.lib().gdn_prefill_launch_count(c["B"], c["T"], Hs, c["dk"], c["dv"])
-    tokens = c["B"] * c["T"]
-    alg = prefill_alg_bytes(c["B"], c["T"], Hs, c["dk"], c["dv"])
-    flops = FLOP_PER_TOKEN_HEAD(c["dk"], c["dv"]) * c["B"] * c["T"] * Hs
-    del inp, gathered
-    tail = run_layer_tail(args, rank, world, dev, stream, tf_peak)
+    del inp, gathered, out
+    torch.cuda.empty_cache()
+    res["layer_tail"] = run_layer_tail(args, rank, world, dev, stream, tf_peak)
+    return res
+
+
+def run_long(args, rank, world, dev, stream, hbm_peak, tf_peak, peak_kind):
+    """``--workload long``: config 4 as the line's own workload; ``value`` is the
+    window-overlapped gather at N>1 and the kernel alone at N=1."""
+    c = C4
+    clocks = ClockSampler(int(os.environ.get("LOCAL_RANK", "0")))
+    res = long_context(args, rank, world, dev, stream, hbm_peak, tf_peak, clocks)
+    head = res["windowed"] if world > 1 else res["kernel_only"]
     if rank == 0:
         line = {
             "metric": "prefill tokens/s (config 4: B=8 T=32768 H=32, heads split over GPUs, o all-gathered)",
-            "value": tokens / (ms * 1e-3), "unit": "tokens/s", "n_gpus": world, "steps": args.steps,
-            "warmup": args.warmup, "ms_per_step": ms, "higher_is_better": True, "scaling": "strong",
+            "value": head["tokens_per_s"], "unit": "tokens/s", "n_gpus": world, "steps": max(3, min(args.steps, 10)),
+            "warmup": 3, "ms_per_step": head["ms_per_step"], "higher_is_better": True, "scaling": "strong",
             "vs_baseline": None, "dtype": "bf16", "data": "synthetic (seeded; BASELINE config-4 distributions)",
-            "config": {"workload": "config4_long_context_head_sharded", "B": c["B"], "T": c["T"], "H": H,
-                       "heads_per_gpu": Hs,
+            "config": {"workload": "config4_long_context_head_sharded", "B": c["B"], "T": c["T"], "H": c["H"],
+                       "heads_per_gpu": c["H"] // world,
                        "parallelism": (f"heads x{world}; o gathered by copy-engine pulls over NVLink, overlapped "
                                        f"with the prefill window by window ({C4_WINDOW}-token windows)"
                                        if world > 1 else "heads x1"),
                        "l2": "inputs larger than L2, no flush"},
-            "kernel_only": {"value": tokens / (ms_k * 1e-3), "ms_per_step": ms_k},
-            "nccl_gather": nccl,
-            "gpu_launches": args.steps * launches,
-            "roofline": {"bound": "hbm", "achieved": alg / (ms_k * 1e-3) / 1e9, "peak": hbm_peak, "unit": "GB/s",
-                         "frac": alg / (ms_k * 1e-3) / 1e9 / hbm_peak, "traffic": None, "peak_kind": peak_kind,
-                         "tensor_tflops": flops / (ms_k * 1e-3) / 1e12,
-                         "tensor_frac_of_measured": flops / (ms_k * 1e-3) / 1e12 / tf_peak},
+            "gpu_launches": max(3, min(args.steps, 10)) * res["launches_per_step"],
+            "roofline": {"bound": "hbm", "achieved": res["kernel_only"]["alg_gbs_per_gpu"], "peak": hbm_peak,
+                         "unit": "GB/s", "frac": res["kernel_only"]["frac_of_measured_hbm"], "traffic": None,
+                         "peak_kind": peak_kind},
             "clocks": clocks.summary(),
-            "layer_tail": tail,
+            "long": res,
         }
         print(json.dumps(line), flush=True)
     finish(world)

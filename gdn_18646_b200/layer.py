@@ -106,8 +106,10 @@ class GDNLayer:
         return q, k, v, z, ab
 
     @torch.no_grad()
-    def prefill(self, x: torch.Tensor, state: dict | None = None):
-        """x [B,T,D] bf16 -> (y [B,T,D] bf16, state after the last token)."""
+    def prefill(self, x: torch.Tensor, state: dict | None = None, trace: dict | None = None):
+        """x [B,T,D] bf16 -> (y [B,T,D] bf16, state after the last token).
+        ``trace``: a dict that receives the intermediate tensors (xn, q, k, v, z,
+        a, b [B,Hv,T], o [B,T,Hv,dv], y_norm) for stage-by-stage checks."""
         c, w = self.cfg, self.w
         B, T, D = x.shape
         xn = ops.rmsnorm(x.reshape(B * T, D), w["norm_gamma"], c.eps).reshape(B, T, D)
@@ -120,6 +122,8 @@ class GDNLayer:
                            state_in=None if state is None else state["recurrent"],
                            scale=self.scale, layout="bthd", state_out=new_state["recurrent"])
         y = ops.gated_rmsnorm(o.view(B * T * c.n_v, c.dv), z.view(B * T * c.n_v, c.dv), w["onorm_gamma"], c.eps)
+        if trace is not None:
+            trace.update(xn=xn, q=q, k=k, v=v, z=z, a=a, b=b, o=o, y_norm=y.view(B, T, c.v_dim))
         return y.view(B, T, c.v_dim) @ w["W_o"].T, new_state
 
     @torch.no_grad()

@@ -295,3 +295,19 @@ class WindowedHeadGather:
                     ops.gather_window(self.gathered, self.ptrs, self.rank, t0, tw, self.layout, stream=self.comm)
         main.wait_stream(self.comm)
         return self.gathered, state_out
+
+    def pull(self, t0: int = 0, Tw: int | None = None) -> None:
+        """Only the gather: tokens [t0, t0 + Tw) of every peer's slot into this
+        rank's buffer (1-element all-reduce, then the copy-engine pulls), on the
+        copy stream, ordered after and before the current stream's work; the
+        cost of the transfer that the windowed prefill overlaps."""
+        import torch.distributed as dist
+        from . import ops
+        Tw = self.T - t0 if Tw is None else Tw
+        main = torch.cuda.current_stream()
+        self.comm.wait_stream(main)
+        with torch.cuda.stream(self.comm):
+            if self.world > 1:
+                dist.all_reduce(self.flag, group=self.group)
+                ops.gather_window(self.gathered, self.ptrs, self.rank, t0, Tw, self.layout, stream=self.comm)
+        main.wait_stream(self.comm)

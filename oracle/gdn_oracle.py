@@ -33,9 +33,13 @@ import numpy as np
 def f32_to_bf16(x) -> np.ndarray:
     """Round fp32 values to bf16 bit patterns (uint16), nearest-even."""
     x = np.ascontiguousarray(np.asarray(x, dtype=np.float32))
-    u = x.view(np.uint32).astype(np.uint64)
-    rounded = (u + 0x7FFF + ((u >> 16) & 1)) >> 16
-    out = rounded.astype(np.uint16)
+    # u + 0x7FFF + lsb stays below 2^32 for every non-NaN pattern (NaNs are patched below)
+    u = x.view(np.uint32)
+    r = (u >> np.uint32(16)) & np.uint32(1)
+    r += np.uint32(0x7FFF)
+    r += u
+    r >>= np.uint32(16)
+    out = r.astype(np.uint16)
     nan = np.isnan(x)
     if nan.any():
         out[nan] = 0x7FC0
@@ -341,7 +345,7 @@ def proj_conv_silu(x, W, conv_w, conv_state=None):
     cw = bf16_to_f32(conv_w)
     B, T, D = xf.shape
     Dout, KC = cw.shape
-    proj = bf16_round(np.einsum("btd,od->bto", xf, Wf, dtype=np.float32))
+    proj = bf16_round(np.matmul(xf, Wf.T))                # fp32 accumulate (BLAS)
     if conv_state is None:
         hist = np.zeros((B, KC - 1, Dout), dtype=np.float32)
     else:
@@ -496,7 +500,7 @@ def rel_fro(a, b) -> float:
 
 def _bf16_matmul(x_bits, W_bits):
     """bf16 x @ W^T with fp32 accumulation rounded to bf16 (a torch bf16 matmul)."""
-    return f32_to_bf16(np.einsum("...d,od->...o", bf16_to_f32(x_bits), bf16_to_f32(W_bits), dtype=np.float32))
+    return f32_to_bf16(np.matmul(bf16_to_f32(x_bits), bf16_to_f32(W_bits).T))
 
 
 def layer_prefill(x, w, n_qk=16, n_v=32, dk=128, dv=128, eps=1e-6):

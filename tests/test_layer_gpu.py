@@ -101,3 +101,88 @@ def test_layer_decode_stacked_graph_matches_eager(cuda_device):
     for se, sg in zip(st_e, st_g):
         assert torch.equal(se["recurrent"], sg["recurrent"])
         assert torch.equal(se["conv_v"], sg["conv_v"])
+
+
+def _stage(report, name, got_bits, want_bits, atol=0.0, ulps=1, max_frac=0.01):
+    """Record one stage's agreement: every element within ``atol`` plus ``ulps``
+    bf16 ulps of the oracle's value, and at most ``max_frac`` of them different.
+    bf16 results of the same op with a different fp32 summation order differ by
+    one ulp where the exact value sits near a rounding boundary; where a stage
+    subtracts nearby values (the conv sums neighbouring projected tokens) such a
+    one-ulp change of an input becomes several ulps of the output, which atol
+    absorbs."""
+    g, w = O.bf16_to_f32(got_bits).astype(np.float64), O.bf16_to_f32(want_bits).astype(np.float64)
+    d = np.abs(g - w)
+    tol = atol + ulps * np.abs(w) * 2.0 ** -7
+    report[name] = (float(d.max()), float(np.mean(d > 0)), bool(np.all(d <= tol)) and float(np.mean(d > 0)) <= max_frac)
+
+
+def test_layer_prefill_config3_shape(cuda_device):
+    """Config 3's layer prefill at its shape (B=2, T=8192, hidden 2048, 16 q/k
+    and 32 value heads) against the oracle composition (gdn_layer.py:120-159
+    plus the BASELINE additions).
+
+    Stage by stage, each kernel on the GPU's own inputs: RMSNorm, the q|k|v
+    projections (conv4 + SiLU, q/k L2 norm) and z/a/b on sampled token windows,
+    the prefill on sampled heads at the north_star bar, the gated norm, and the
+    output projection on sampled rows.  Then end to end: the layer's y and final
+    state against the whole oracle layer run on x alone, at north_star's bar
+    (y max-abs <= 2e-2, state rel-Frobenius <= 1e-3)."""
+    import torch
+    layer = _layer(11)
+    B, T, D = 2, 8192, 2048
+    g = torch.Generator(device="cuda").manual_seed(31)
+    x = torch.randn(B, T, D, generator=g, device="cuda").bfloat16()
+    tr = {}
+    y, st = layer.prefill(x, trace=tr)
+    torch.cuda.synchronize()
+    wn = {k_: to_np(v_) for k_, v_ in layer.w.items()}
+    xb = to_np(x)
+    t = {k_: to_np(v_) for k_, v_ in tr.items()}
+    rep = {}
+
+    _stage(rep, "rmsnorm", t["xn"], O.rmsnorm(xb.reshape(B * T, D), wn["norm_gamma"]).reshape(B, T, D))
+    # projections on token windows (3 tokens of conv history before each), GPU xn as input
+    for t0 in (0, 4093, T - 64):
+        lo = max(t0 - 3, 0)
+        xw = t["xn"][:, lo:t0 + 64]
+        for name, Wn, cw, l2 in (("q", "W_q", "conv_q", True), ("k", "W_k", "conv_k", True),
+                                 ("v", "W_v", "conv_v", False)):
+            ref = O.proj_conv_silu(xw, wn[Wn], wn[cw])[0][:, t0 - lo:]
+            if l2:
+                ref = O.l2norm_heads(ref, 128)
+            _stage(rep, f"{name}@{t0}", t[name][:, t0:t0 + 64], ref, atol=4e-3 if l2 else 1e-2, max_frac=0.02)
+        _stage(rep, f"z@{t0}", t["z"][:, t0:t0 + 64], O._bf16_matmul(t["xn"][:, t0:t0 + 64], wn["W_z"]))
+        ab = O._bf16_matmul(t["xn"][:, t0:t0 + 64], wn["W_ab"])
+        _stage(rep, f"a@{t0}", np.swapaxes(t["a"][:, :, t0:t0 + 64], 1, 2), ab[..., :32])
+        _stage(rep, f"b@{t0}", np.swapaxes(t["b"][:, :, t0:t0 + 64], 1, 2), ab[..., 32:])
+    # prefill on sampled (b, value head) pairs of the GPU's q/k/v/a/b (head h reads q/k head h // 2)
+    S_gpu = to_np(st["recurrent"])
+    for bi, h in ((0, 0), (1, 13), (1, 31)):
+        hq = h // 2
+        qh = np.swapaxes(t["q"].reshape(B, T, 16, 128)[bi:bi + 1, :, hq:hq + 1], 1, 2)
+        kh = np.swapaxes(t["k"].reshape(B, T, 16, 128)[bi:bi + 1, :, hq:hq + 1], 1, 2)
+        vh = np.swapaxes(t["v"].reshape(B, T, 32, 128)[bi:bi + 1, :, h:h + 1], 1, 2)
+        o_r, S_r = O.prefill(qh, kh, vh, wn["A_log"][h:h + 1], t["a"][bi:bi + 1, h:h + 1],
+                             float(wn["dt_bias"][h]), t["b"][bi:bi + 1, h:h + 1], np.ones((1, T), np.float32),
+                             scale=128 ** -0.5, chunk_size=64, dt=np.float64)
+        o_g = O.bf16_to_f32(np.swapaxes(t["o"][bi:bi + 1, :, h:h + 1], 1, 2))
+        e_o, e_s = float(np.abs(o_g - o_r).max()), O.rel_fro(S_gpu[bi:bi + 1, h:h + 1], S_r)
+        rep[f"prefill({bi},{h})"] = (e_o, e_s, e_o <= 2e-2 and e_s <= 1e-3)
+    # gated norm over every head row, GPU o and z as input
+    _stage(rep, "gated_norm", t["y_norm"].reshape(-1, 128),
+           O.gated_rmsnorm(t["o"].reshape(-1, 128), t["z"].reshape(-1, 128), wn["onorm_gamma"]))
+    # output projection on sampled rows
+    yb = to_np(y)
+    for r0 in (0, 5000, T - 32):
+        _stage(rep, f"out@{r0}", yb[:, r0:r0 + 32], O._bf16_matmul(t["y_norm"][:, r0:r0 + 32], wn["W_o"]))
+
+    # end to end: the whole oracle layer on x
+    y_ref, S_ref = O.layer_prefill(xb, wn)
+    err_y = float(np.abs(O.bf16_to_f32(yb) - O.bf16_to_f32(y_ref)).max())
+    err_s = O.rel_fro(S_gpu, S_ref)
+    rep["end_to_end"] = (err_y, err_s, err_y <= 2e-2 and err_s <= 1e-3)
+    for k_, v_ in rep.items():
+        print(f"config-3 layer {k_}: {v_[0]:.3e} {v_[1]:.3e} {'ok' if v_[2] else 'FAIL'}")
+    bad = [k_ for k_, v_ in rep.items() if not v_[2]]
+    assert not bad, f"stages outside their bar: {bad}"

@@ -265,3 +265,64 @@ def test_prefill_strong_decay_direct_path(cuda_device):
     o, S = _run(inp)
     o_r, S_r = _oracle(inp)
     _check(o, S, o_r, S_r)
+
+
+def _device_inputs(B, T, H, dk, dv, seed, state_std=0.0):
+    """Config-0/4 distributions generated on the device (a full config-4 batch is
+    6.4 GB of q/k/v, too large to generate in numpy for a test)."""
+    import torch
+    g = torch.Generator(device="cuda").manual_seed(seed)
+    q = torch.nn.functional.normalize(torch.randn(B, H, T, dk, generator=g, device="cuda"), dim=-1).bfloat16()
+    k = torch.nn.functional.normalize(torch.randn(B, H, T, dk, generator=g, device="cuda"), dim=-1).bfloat16()
+    v = torch.randn(B, H, T, dv, generator=g, device="cuda").bfloat16()
+    a = torch.randn(B, H, T, generator=g, device="cuda")
+    b = torch.randn(B, H, T, generator=g, device="cuda")
+    s0 = torch.randn(B, H, dk, dv, generator=g, device="cuda") * state_std if state_std > 0 else None
+    return q, k, v, a, b, s0
+
+
+def _sampled_oracle_check(q, k, v, a, b, A_log, s0, o, S, picks, scale):
+    """The fp64 oracle on whole sampled (b, h) sequences of device tensors."""
+    errs = []
+    for bi, hi in picks:
+        sub = dict(q=to_np(q[bi:bi + 1, hi:hi + 1]), k=to_np(k[bi:bi + 1, hi:hi + 1]),
+                   v=to_np(v[bi:bi + 1, hi:hi + 1]), a=to_np(a[bi:bi + 1, hi:hi + 1]),
+                   b=to_np(b[bi:bi + 1, hi:hi + 1]), A_log=to_np(A_log[hi:hi + 1]), dt_bias=0.0,
+                   mask=np.ones((1, q.shape[2]), np.float32),
+                   state_in=None if s0 is None else to_np(s0[bi:bi + 1, hi:hi + 1]), scale=scale)
+        o_r, S_r = _oracle(sub)
+        errs.append(_check(to_np(o[bi:bi + 1, hi:hi + 1]), to_np(S[bi:bi + 1, hi:hi + 1]), o_r, S_r))
+        errs.append(O.rel_fro(to_np(S[bi:bi + 1, hi:hi + 1]), S_r))
+    return errs
+
+
+def test_prefill_config4_length_sampled(cuda_device):
+    """Config 4 on one GPU at its full length: B=8, T=32768 (512 chunks), H=32,
+    dk=dv=128, config-0 distributions, zero initial state.  Sampled whole
+    sequences against the fp64 oracle at the north_star bar: error accumulation
+    over 512 chunks of hi/lo state products."""
+    import torch
+    from gdn_18646_b200 import ops
+    B, T, H, dk, dv = 8, 32768, 32, 128, 128
+    q, k, v, a, b, _ = _device_inputs(B, T, H, dk, dv, 4321)
+    A_log = torch.full((H,), math.log(0.1), device="cuda")
+    scale = dk ** -0.5
+    o, S = ops.prefill(q, k, v, A_log, a, b, scale=scale)
+    torch.cuda.synchronize()
+    assert bool(torch.isfinite(o).all()) and bool(torch.isfinite(S).all())
+    _sampled_oracle_check(q, k, v, a, b, A_log, None, o, S, ((0, 0), (3, 17), (7, 31)), scale)
+
+
+def test_prefill_slow_decay_config4_length(cuda_device):
+    """The worst case for accumulation at config 4's length: weak decay
+    (A_log = ln 0.002: the state remembers ~500 tokens) over T = 32768 with a
+    N(0, 0.02) initial state, one sequence per head."""
+    import torch
+    from gdn_18646_b200 import ops
+    B, T, H, dk, dv = 1, 32768, 2, 128, 128
+    q, k, v, a, b, s0 = _device_inputs(B, T, H, dk, dv, 4322, state_std=0.02)
+    A_log = torch.full((H,), math.log(0.002), device="cuda")
+    scale = dk ** -0.5
+    o, S = ops.prefill(q, k, v, A_log, a, b, state_in=s0, scale=scale)
+    torch.cuda.synchronize()
+    _sampled_oracle_check(q, k, v, a, b, A_log, s0, o, S, ((0, 0), (0, 1)), scale)
