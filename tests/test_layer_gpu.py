@@ -103,18 +103,26 @@ def test_layer_decode_stacked_graph_matches_eager(cuda_device):
         assert torch.equal(se["conv_v"], sg["conv_v"])
 
 
-def _stage(report, name, got_bits, want_bits, atol=0.0, ulps=1, max_frac=0.01):
+def _stage(report, name, got_bits, want_bits, atol=0.0, ulps=1, max_frac=0.01, gemm=False):
     """Record one stage's agreement: every element within ``atol`` plus ``ulps``
     bf16 ulps of the oracle's value, and at most ``max_frac`` of them different.
+
     bf16 results of the same op with a different fp32 summation order differ by
-    one ulp where the exact value sits near a rounding boundary; where a stage
-    subtracts nearby values (the conv sums neighbouring projected tokens) such a
-    one-ulp change of an input becomes several ulps of the output, which atol
-    absorbs."""
+    an ulp where the exact value sits near a rounding boundary.  A GEMM output
+    (``gemm``: 2048- or 4096-term dot products) carries an fp32 summation error
+    proportional to the sum of |terms|, not to the result, so small results
+    differ by more ulps: those stages get two ulps plus an absolute 2^-8 of the
+    output's RMS.  Where a stage sums neighbouring values (the conv over four
+    projected tokens) a one-ulp change of an input becomes several ulps of a
+    small output, which ``atol`` absorbs."""
     g, w = O.bf16_to_f32(got_bits).astype(np.float64), O.bf16_to_f32(want_bits).astype(np.float64)
     d = np.abs(g - w)
+    if gemm:
+        ulps, atol = 2, max(atol, float(np.sqrt(np.mean(w * w))) * 2.0 ** -8)
     tol = atol + ulps * np.abs(w) * 2.0 ** -7
-    report[name] = (float(d.max()), float(np.mean(d > 0)), bool(np.all(d <= tol)) and float(np.mean(d > 0)) <= max_frac)
+    worst = np.unravel_index(np.argmax(d - tol), d.shape)
+    report[name] = (float(d.max()), float(np.mean(d > 0)), bool(np.all(d <= tol)) and float(np.mean(d > 0)) <= max_frac,
+                    f"worst: got {g[worst]:.6g} want {w[worst]:.6g} tol {tol[worst]:.3g}")
 
 
 def test_layer_prefill_config3_shape(cuda_device):
@@ -151,11 +159,12 @@ def test_layer_prefill_config3_shape(cuda_device):
             ref = O.proj_conv_silu(xw, wn[Wn], wn[cw])[0][:, t0 - lo:]
             if l2:
                 ref = O.l2norm_heads(ref, 128)
-            _stage(rep, f"{name}@{t0}", t[name][:, t0:t0 + 64], ref, atol=4e-3 if l2 else 1e-2, max_frac=0.02)
-        _stage(rep, f"z@{t0}", t["z"][:, t0:t0 + 64], O._bf16_matmul(t["xn"][:, t0:t0 + 64], wn["W_z"]))
+            _stage(rep, f"{name}@{t0}", t[name][:, t0:t0 + 64], ref, atol=4e-3 if l2 else 1e-2, ulps=2,
+                   max_frac=0.02)
+        _stage(rep, f"z@{t0}", t["z"][:, t0:t0 + 64], O._bf16_matmul(t["xn"][:, t0:t0 + 64], wn["W_z"]), gemm=True)
         ab = O._bf16_matmul(t["xn"][:, t0:t0 + 64], wn["W_ab"])
-        _stage(rep, f"a@{t0}", np.swapaxes(t["a"][:, :, t0:t0 + 64], 1, 2), ab[..., :32])
-        _stage(rep, f"b@{t0}", np.swapaxes(t["b"][:, :, t0:t0 + 64], 1, 2), ab[..., 32:])
+        _stage(rep, f"a@{t0}", np.swapaxes(t["a"][:, :, t0:t0 + 64], 1, 2), ab[..., :32], gemm=True)
+        _stage(rep, f"b@{t0}", np.swapaxes(t["b"][:, :, t0:t0 + 64], 1, 2), ab[..., 32:], gemm=True)
     # prefill on sampled (b, value head) pairs of the GPU's q/k/v/a/b (head h reads q/k head h // 2)
     S_gpu = to_np(st["recurrent"])
     for bi, h in ((0, 0), (1, 13), (1, 31)):
@@ -168,21 +177,21 @@ def test_layer_prefill_config3_shape(cuda_device):
                              scale=128 ** -0.5, chunk_size=64, dt=np.float64)
         o_g = O.bf16_to_f32(np.swapaxes(t["o"][bi:bi + 1, :, h:h + 1], 1, 2))
         e_o, e_s = float(np.abs(o_g - o_r).max()), O.rel_fro(S_gpu[bi:bi + 1, h:h + 1], S_r)
-        rep[f"prefill({bi},{h})"] = (e_o, e_s, e_o <= 2e-2 and e_s <= 1e-3)
+        rep[f"prefill({bi},{h})"] = (e_o, e_s, e_o <= 2e-2 and e_s <= 1e-3, "o max-abs, state rel-F")
     # gated norm over every head row, GPU o and z as input
     _stage(rep, "gated_norm", t["y_norm"].reshape(-1, 128),
            O.gated_rmsnorm(t["o"].reshape(-1, 128), t["z"].reshape(-1, 128), wn["onorm_gamma"]))
     # output projection on sampled rows
     yb = to_np(y)
     for r0 in (0, 5000, T - 32):
-        _stage(rep, f"out@{r0}", yb[:, r0:r0 + 32], O._bf16_matmul(t["y_norm"][:, r0:r0 + 32], wn["W_o"]))
+        _stage(rep, f"out@{r0}", yb[:, r0:r0 + 32], O._bf16_matmul(t["y_norm"][:, r0:r0 + 32], wn["W_o"]), gemm=True)
 
     # end to end: the whole oracle layer on x
     y_ref, S_ref = O.layer_prefill(xb, wn)
     err_y = float(np.abs(O.bf16_to_f32(yb) - O.bf16_to_f32(y_ref)).max())
     err_s = O.rel_fro(S_gpu, S_ref)
-    rep["end_to_end"] = (err_y, err_s, err_y <= 2e-2 and err_s <= 1e-3)
+    rep["end_to_end"] = (err_y, err_s, err_y <= 2e-2 and err_s <= 1e-3, "y max-abs, state rel-F")
     for k_, v_ in rep.items():
-        print(f"config-3 layer {k_}: {v_[0]:.3e} {v_[1]:.3e} {'ok' if v_[2] else 'FAIL'}")
+        print(f"config-3 layer {k_}: {v_[0]:.3e} {v_[1]:.3e} {'ok' if v_[2] else 'FAIL'} ({v_[3]})")
     bad = [k_ for k_, v_ in rep.items() if not v_[2]]
     assert not bad, f"stages outside their bar: {bad}"
