@@ -218,6 +218,10 @@ __device__ __forceinline__ void bulk_load(void* dst, const void* src, uint32_t b
         : "memory");
 }
 __device__ __forceinline__ void bulk_wait_all0() { asm volatile("cp.async.bulk.wait_group 0;" ::: "memory"); }
+// bring `bytes` (a multiple of 16, 16-byte aligned) of global memory into L2 ahead of a bulk load
+__device__ __forceinline__ void bulk_prefetch_l2(const void* src, uint32_t bytes) {
+    asm volatile("cp.async.bulk.prefetch.L2.global [%0], %1;" ::"l"(src), "r"(bytes) : "memory");
+}
 
 // Programmatic dependent launch: let the next kernel of the stream start, and wait
 // until the kernels this one depends on have completed with their memory visible.
@@ -326,6 +330,24 @@ __device__ __forceinline__ void umma_bf16_ts(uint32_t d_tmem, uint32_t a_tmem, u
         "r"(a_tmem), "l"(b_desc), "r"(idesc), "r"(accumulate)
         : "memory");
 }
+// D[tmem] (+)= A[tmem] * B[smem], kind::tf32: A is M rows on the TMEM lanes, K fp32
+// values one per column (K step of 8 = 8 columns; the tensor core reads the
+// top 19 bits of each), B tf32 in shared memory.
+__device__ __forceinline__ void umma_tf32_ts(uint32_t d_tmem, uint32_t a_tmem, uint64_t b_desc, uint32_t idesc,
+                                             uint32_t accumulate) {
+    asm volatile(
+        "{\n\t.reg .pred p;\n\t"
+        "setp.ne.b32 p, %4, 0;\n\t"
+        "tcgen05.mma.cta_group::1.kind::tf32 [%0], [%1], %2, %3, p;\n\t}" ::"r"(d_tmem),
+        "r"(a_tmem), "l"(b_desc), "r"(idesc), "r"(accumulate)
+        : "memory");
+}
+// fp32 -> tf32 (10-bit mantissa), round to nearest, returned as an fp32 bit pattern
+__device__ __forceinline__ float round_tf32(float x) {
+    uint32_t r;
+    asm("cvt.rna.tf32.f32 %0, %1;" : "=r"(r) : "f"(x));
+    return __uint_as_float(r);
+}
 // arrive on an mbarrier once every tcgen05.mma issued so far by this thread completed
 __device__ __forceinline__ void umma_commit(uint64_t* bar) {
     asm volatile(
@@ -340,6 +362,16 @@ __device__ __forceinline__ void umma_commit(uint64_t* bar) {
 __host__ __device__ constexpr uint32_t idesc_bf16(int M, int N, bool a_mn, bool b_mn) {
     return (1u << 4) | (1u << 7) | (1u << 10) | ((a_mn ? 1u : 0u) << 15) | ((b_mn ? 1u : 0u) << 16) |
            (static_cast<uint32_t>(N >> 3) << 17) | (static_cast<uint32_t>(M >> 4) << 24);
+}
+// Instruction descriptor, kind::tf32: D=f32, A=B=tf32 (format code 2), dense.
+__host__ __device__ constexpr uint32_t idesc_tf32(int M, int N, bool a_mn, bool b_mn) {
+    return (1u << 4) | (2u << 7) | (2u << 10) | ((a_mn ? 1u : 0u) << 15) | ((b_mn ? 1u : 0u) << 16) |
+           (static_cast<uint32_t>(N >> 3) << 17) | (static_cast<uint32_t>(M >> 4) << 24);
+}
+// Byte offset of fp32 element (row, col) of a K-major 128B-swizzled tf32 image:
+// 32-column blocks of rows x 128 B, `rows` rows per block.
+__device__ __forceinline__ uint32_t sw128_f32(uint32_t row, uint32_t col, uint32_t rows) {
+    return (col >> 5) * rows * 128u + row * 128u + ((((col & 31u) >> 2) ^ (row & 7u)) << 4) + (col & 3u) * 4u;
 }
 
 // Shared-memory matrix descriptor with 128-byte swizzle (version 1, base offset 0).

@@ -68,24 +68,24 @@ constexpr int BAR_OUT = 2;             // named barrier of the chain kernel's ou
 // ---------------------------------------------------------------------------
 // Chunk record (bytes, 1024-aligned images), written by the gate and prep kernels:
 //   GB        gate vectors of the chunk for the prep kernel (PrepGate layout)
-//   A1H, A1L  A diag(beta'), rows t, cols s        (K-major B of U^T = V^T A1^T)
-//   WTH, WTL  W^T, rows d, cols t                  (MN-major B of S^T W^T)
+//   A1        A diag(beta') as bf16 lo then hi images, rows t, cols s
+//             (one K-major B of [U_l^T | U_h^T] = V^T [A1_lo^T | A1_hi^T])
+//   W         W, rows t, cols d, tf32 (rounded to nearest), 32-column blocks
+//             (rows 0-63 of the K-major B of S^T [W^T | Q~^T])
 //   P         rows t, cols s                       (K-major B of dV^T P^T)
 //   G         floats: [0,64) oc_t = m_t scale e^Lambda_t, [64,128) e^{Lambda_last - Lambda_t},
 //             [128] gamma = e^{Lambda_last}
-// The part from WTH to the end is fetched per chunk as one bulk copy, A1 as another.
+// The chain fetches A1, W (one copy per 32-key block) and P | G per chunk with bulk copies.
 // ---------------------------------------------------------------------------
 template <int DK>
 struct Rec {
     static constexpr int GB = 0;                      // gate vectors for the prep kernel (PrepGate)
-    static constexpr int A1H = 2048, A1L = A1H + 8192;
-    static constexpr int WTH = A1L + 8192;
-    static constexpr int WTL = WTH + DK * 128;
-    static constexpr int P = WTL + DK * 128;
+    static constexpr int A1 = 2048;                   // lo, then hi at + 8192
+    static constexpr int W = A1 + 16384;
+    static constexpr int P = W + DK * 256;
     static constexpr int G = P + 8192;
     static constexpr int BYTES = G + 1024;
-    static constexpr int SLOT_BYTES = BYTES - WTH;   // WTH .. end
-    static_assert(BYTES % 1024 == 0 && SLOT_BYTES % 1024 == 0, "record images must stay 1024-aligned");
+    static_assert(BYTES % 1024 == 0, "record images must stay 1024-aligned");
 };
 
 // ---------------------------------------------------------------------------
@@ -167,46 +167,40 @@ struct PrepArgs {
 // ---------------------------------------------------------------------------
 constexpr int kChainThreads = 448;     // 14 warps
 constexpr int kChainTmemCols = 512;
-constexpr uint32_t C_ST = 0;           // S^T fp32 (DK columns)
-constexpr uint32_t C_SHI = 128;        // S^T bf16 hi, packed pairs (DK/2 columns)
-constexpr uint32_t C_SLO = 192;        // S^T bf16 lo
-// C_UT: 192 columns, one N=192 accumulator.
-//   [0, 64)    U^T from A1 hi, minus S_hi^T W_hi^T and S_lo^T W_hi^T
-//   [64, 128)  U^T from A1 lo, minus S_hi^T W_lo^T            (dV^T = [0,64) + [64,128))
-//   [128, 192) O^T: + S_hi^T Q~^T, then + dV^T P^T; read and reset to 0 by the output warps
-// dV'^T hi/lo go to C_SHI (free once W S has run), per 32-token group g: hi at 32g,
-// lo at 32g + 16, so that the next chunk's U can be issued into C_UT right away.
-constexpr uint32_t C_UT = 256;
-constexpr uint32_t C_O = C_UT + 128;
-constexpr uint32_t C_DVB = 448;        // dV^T bf16 (32 columns), A operand of dV^T P^T
+// TMEM columns (128 lanes; lane j = value column of the tile):
+constexpr uint32_t C_X = 0;            // S^T fp32 (DK columns): A operand of [W | Q~] S (tf32)
+constexpr uint32_t C_UL = 128;         // U_l^T = V^T A1_lo^T (64 token columns)
+constexpr uint32_t C_UH = 192;         // U_h^T = V^T A1_hi^T, then - (W S)^T: U_l + U_h = dV^T
+constexpr uint32_t C_O = 256;          // O^T: + (Q~ S)^T in the same MMAs as W S, + (P dV)^T; zeroed after read
+constexpr uint32_t C_DVH = 320;        // dV'^T hi/lo bf16 pairs: token half g, hi at 32g, lo at 32g + 16
+constexpr uint32_t C_DVB = 384;        // dV^T bf16 pairs (32 columns): A operand of dV^T P^T
 
 template <int DK>
 struct ChainSmem {
-    static constexpr int CB = DK / 64;
-    // one slot per chunk: K tile (TMA), W^T hi | W^T lo (record), q tile (TMA; rebuilt in place
-    // as Q~^T, so the three 64-column B blocks of the N=192 MMA are DK*128 bytes apart), P, gates
+    static constexpr int CB = DK / 64;      // 64-column bf16 blocks of the q/k tiles
+    // one slot per chunk: K tile (TMA; MN-major B of the state update), q tile (TMA; read
+    // once to build Q~), then from the record P and the gates
     static constexpr int K_OFF = 0;
-    static constexpr int R_WTH = CB * 8192;
-    static constexpr int R_WTL = R_WTH + DK * 128;
-    static constexpr int Q_OFF = R_WTL + DK * 128;
-    static constexpr int R_P = Q_OFF + CB * 8192;
-    static constexpr int R_G = R_P + 8192;
-    static constexpr int SLOT_BYTES = R_G + 1024;
-    static constexpr int OFF_V = 2 * SLOT_BYTES;           // v tile, 2 blocks of 64 columns
-    static constexpr int OFF_A1 = OFF_V + 16384;           // A1 hi | lo
+    static constexpr int Q_OFF = CB * 8192;
+    static constexpr int P_OFF = 2 * CB * 8192;
+    static constexpr int G_OFF = P_OFF + 8192;
+    static constexpr int SLOT_BYTES = G_OFF + 1024;
+    // [W | -Q~] image of the current chunk, K-major tf32: key block kb (32 keys) at kb * 16 KB,
+    // rows 0-63 W (bulk-copied from the record), rows 64-127 -oc Q (built by the output warps)
+    static constexpr int OFF_IMG = 2 * SLOT_BYTES;
+    static constexpr int OFF_V = OFF_IMG + DK * 512;       // v tile, 2 blocks of 64 columns
+    static constexpr int OFF_A1 = OFF_V + 16384;           // A1 lo | hi
     static constexpr int OFF_O = OFF_A1 + 16384;           // output staging, 2 x (2 blocks x 8 KB)
     static constexpr int OFF_BAR = OFF_O + 32768;
     static constexpr int BYTES = OFF_BAR + 256;
     static constexpr int ALLOC = BYTES + 1024;
-    static_assert(R_WTL - R_WTH == DK * 128 && Q_OFF - R_WTL == DK * 128 && CB * 8192 == DK * 128,
-                  "the N=192 B operand needs equally spaced blocks");
     static_assert(SLOT_BYTES % 1024 == 0, "slot images must stay 1024-aligned");
     static_assert(ALLOC <= 232448, "chain kernel shared memory exceeds 227 KB");
 };
 
 struct ChainBars {
-    uint64_t slot_full[2], slot_free[2], va_full, va_free;
-    uint64_t split_half[2], qt_ready[2], ws_done, dv_done, st_done, pdv_done, o_free;
+    uint64_t slot_full[2], slot_free[2], va_full, va_free, w_full;
+    uint64_t ws_done, dv_done, st_done, pdv_done, qt_ready, o_free, init_done;
 };
 
 struct ChainArgs {
@@ -232,6 +226,12 @@ struct ChainArgs {
 __device__ __forceinline__ void publish_record(unsigned int* flag) {
     asm volatile("fence.proxy.async.global;" ::: "memory");
     asm volatile("st.release.gpu.global.u32 [%0], %1;" ::"l"(flag), "r"(1u) : "memory");
+}
+// Current value of a record flag (no ordering: only decides whether to prefetch the record)
+__device__ __forceinline__ uint32_t ld_relaxed_u32(const unsigned int* flag) {
+    uint32_t v;
+    asm volatile("ld.relaxed.gpu.global.u32 %0, [%1];" : "=r"(v) : "l"(flag) : "memory");
+    return v;
 }
 // Bounded wait for a record flag (~2^31 cycles, then DERR_TIMEOUT and the CTA's abort flag).
 __device__ __forceinline__ bool wait_record(const unsigned int* flag, unsigned int* err, volatile int* abort) {
@@ -295,18 +295,6 @@ __device__ __forceinline__ uint4 pack8(const float* v) {
     return make_uint4(cvt_bf16x2(v[0], v[1]), cvt_bf16x2(v[2], v[3]), cvt_bf16x2(v[4], v[5]),
                       cvt_bf16x2(v[6], v[7]));
 }
-// 64 fp32 -> one 128-byte row of a 128B-swizzled tile, bf16 hi and lo parts
-__device__ __forceinline__ void store_row_split(uint8_t* hi_tile, uint8_t* lo_tile, int row, const float (&v)[64]) {
-#pragma unroll
-    for (int ch = 0; ch < 8; ++ch) {
-        uint4 h, l;
-        split8(&v[8 * ch], h, l);
-        const uint32_t off = sw128_chunk(row, ch);
-        *reinterpret_cast<uint4*>(hi_tile + off) = h;
-        *reinterpret_cast<uint4*>(lo_tile + off) = l;
-    }
-}
-
 // ---------------------------------------------------------------------------
 // 16x16 block product on one warp: acc (two 16x8 halves, C fragments) +=
 // L (16x16 fp32, row stride ldl) * R (16x16 fp32, row stride ldr), with both
@@ -766,8 +754,8 @@ __device__ __forceinline__ void prep_body(const CUtensorMap* map_q, const CUtens
 #pragma unroll
             for (int ch = 0; ch < 4; ++ch) {
                 const uint32_t off = sw128_chunk(t, 4 * hf + ch);
-                *reinterpret_cast<uint4*>(a1 + off) = h1[ch];
-                *reinterpret_cast<uint4*>(a1 + 8192 + off) = l1[ch];
+                *reinterpret_cast<uint4*>(a1 + off) = l1[ch];
+                *reinterpret_cast<uint4*>(a1 + 8192 + off) = h1[ch];
                 *reinterpret_cast<uint4*>(sm + L::OFF_A2H + off) = h2[ch];
                 *reinterpret_cast<uint4*>(sm + L::OFF_A2L + off) = l2[ch];
             }
@@ -776,7 +764,7 @@ __device__ __forceinline__ void prep_body(const CUtensorMap* map_q, const CUtens
         tc_fence_before();
         named_bar(bar_id, kPrepThreads);
         if (leader) {
-            bulk_store(rec + R::A1H, Nsm, 16384);
+            bulk_store(rec + R::A1, Nsm, 16384);
             bulk_commit();
         }
 
@@ -798,18 +786,20 @@ __device__ __forceinline__ void prep_body(const CUtensorMap* map_q, const CUtens
         mbar_wait_or_abort(bar_w, ph, err, abort_flag);
         tc_fence_after();
 
-        // ---- W^T rows (lane d) -> bf16 hi/lo images over the dead q/k tiles -> record
+        // ---- W (rows t, columns d) as a K-major tf32 image over the dead q/k tiles -> record;
+        //      TMEM row d of W^T is column d of W (a warp stores 128 contiguous bytes per row t)
         if (tid < DK) {
             float row[64];
             tmem_ld64(tmem + lane_off + P_COL_WT, row);
-            store_row_split(sm, sm + DK * 128, tid, row);
+#pragma unroll
+            for (int t = 0; t < kC; ++t) *reinterpret_cast<float*>(sm + sw128_f32(t, tid, kC)) = round_tf32(row[t]);
         }
         fence_async_smem();
         tc_fence_before();
         named_bar(bar_id, kPrepThreads);
         bool pending = false;
         if (leader) {
-            bulk_store(rec + R::WTH, sm, 2 * DK * 128);
+            bulk_store(rec + R::W, sm, DK * 256);
             bulk_commit();
             bulk_wait_read0();                        // the images (and A1 over N) have been read out
             if (args.ready) published = rec_idx;       // published once the next task's q/k have landed
@@ -848,6 +838,16 @@ prefill_prep_kernel(const __grid_constant__ CUtensorMap map_q, const __grid_cons
 // Kernel 2: the sequential state recurrence, one CTA per (b, h, value tile)
 // ===========================================================================
 // One chain CTA (all 448 threads), working on (b, h, value tile) number `cta`.
+//
+// Per chunk c (S^T in TMEM, lane j = value column):
+//   [U_l^T | U_h^T] = V^T [A1_lo^T | A1_hi^T]           4 bf16 MMAs (N = 128)
+//   [U_h^T | O^T] -= S^T [W^T | -Q~^T]                  16 tf32 MMAs (N = 128), A = the fp32
+//                                                       state straight from TMEM, B = [W | -oc Q]
+//   state path: dV = U_l + U_h -> bf16 and dV' = dV e^{Lambda_last - Lambda} -> hi/lo;
+//               S <- gamma_c S in place
+//   S^T += dV'^T K                                      8 bf16 MMAs (hi and lo)
+//   O^T += dV^T P^T;  o = O -> bf16 -> TMA store, O zeroed for the next chunk
+// The critical path per chunk is [W | Q~] S -> state-path pass -> state update.
 template <int DK>
 __device__ __forceinline__ void chain_body(const CUtensorMap* map_q, const CUtensorMap* map_k,
                                            const CUtensorMap* map_v, const CUtensorMap* map_o, const ChainArgs& args,
@@ -855,9 +855,9 @@ __device__ __forceinline__ void chain_body(const CUtensorMap* map_q, const CUten
     using L = ChainSmem<DK>;
     using R = Rec<DK>;
     constexpr int HALF = DK / 2;                   // key columns per state-path thread group
-    constexpr int NBLK = HALF / 32;                // 32-column split blocks per group
+    constexpr int NBLK = HALF / 32;                // 32-column blocks per group
     ChainBars* bars = reinterpret_cast<ChainBars*>(sm + L::OFF_BAR);
-    uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(sm + L::OFF_BAR + sizeof(ChainBars));
+    uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 1);
     volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
 
     const int tid = threadIdx.x;
@@ -884,19 +884,18 @@ __device__ __forceinline__ void chain_body(const CUtensorMap* map_q, const CUten
     if (tid == 0) {
         mbar_init(&bars->slot_full[0], 1);
         mbar_init(&bars->slot_full[1], 1);
-        mbar_init(&bars->slot_free[0], 2);         // MMA commit + output warps (Q~^T built)
+        mbar_init(&bars->slot_free[0], 2);         // MMA commit + output warps (gates read)
         mbar_init(&bars->slot_free[1], 2);
         mbar_init(&bars->va_full, 1);
         mbar_init(&bars->va_free, 1);
-        mbar_init(&bars->split_half[0], 256);
-        mbar_init(&bars->split_half[1], 256);
-        mbar_init(&bars->qt_ready[0], 1);          // per slot: the output warps run a chunk ahead
-        mbar_init(&bars->qt_ready[1], 1);
+        mbar_init(&bars->w_full, 1);
         mbar_init(&bars->ws_done, 1);
         mbar_init(&bars->dv_done, 256);
         mbar_init(&bars->st_done, 1);
         mbar_init(&bars->pdv_done, 1);
+        mbar_init(&bars->qt_ready, 1);
         mbar_init(&bars->o_free, 128);
+        mbar_init(&bars->init_done, 256);
         *abort_flag = 0;
         fence_mbar_init();
         tma_prefetch_desc(map_q);
@@ -912,6 +911,9 @@ __device__ __forceinline__ void chain_body(const CUtensorMap* map_q, const CUten
     __syncthreads();
     tc_fence_after();
     const uint32_t tmem = *tmem_slot;
+    auto gates_of = [&](int c) {
+        return reinterpret_cast<const float*>(sm + (c & 1) * L::SLOT_BYTES + L::G_OFF);
+    };
 
     if (warp == 0) {
         // ======================= producer: lane 0 the per-chunk slot, lane 1 V and A1
@@ -924,7 +926,7 @@ __device__ __forceinline__ void chain_body(const CUtensorMap* map_q, const CUten
                 if (args.ready &&
                     !wait_record(args.ready + static_cast<long>(bh) * args.nchunks_total + c0 + c, err, abort_flag))
                     break;
-                mbar_arrive_expect_tx(&bars->slot_full[slot], 2 * L::CB * 8192 + 2 * DK * 128 + 8192 + 1024);
+                mbar_arrive_expect_tx(&bars->slot_full[slot], 2 * L::CB * 8192 + 8192 + 1024);
 #pragma unroll
                 for (int cb = 0; cb < L::CB; ++cb) {
                     tma_load_4d(dst + L::Q_OFF + cb * 8192, map_q, &bars->slot_full[slot], cb * 64,
@@ -932,8 +934,7 @@ __device__ __forceinline__ void chain_body(const CUtensorMap* map_q, const CUten
                     tma_load_4d(dst + L::K_OFF + cb * 8192, map_k, &bars->slot_full[slot], cb * 64,
                                 trow0 + (c0 + c) * kC, hq, bco);
                 }
-                bulk_load(dst + L::R_WTH, rec + R::WTH, 2 * DK * 128, &bars->slot_full[slot]);
-                bulk_load(dst + L::R_P, rec + R::P, 8192 + 1024, &bars->slot_full[slot]);
+                bulk_load(dst + L::P_OFF, rec + R::P, 8192 + 1024, &bars->slot_full[slot]);
             }
         } else if (lane == 1) {
             for (int c = 0; c < nchunks; ++c) {
@@ -945,7 +946,7 @@ __device__ __forceinline__ void chain_body(const CUtensorMap* map_q, const CUten
                 for (int vb = 0; vb < nvb; ++vb)
                     tma_load_4d(sm + L::OFF_V + vb * 8192, map_v, &bars->va_full, v0 + vb * 64, trow0 + (c0 + c) * kC, h,
                                 bco);
-                bulk_load(sm + L::OFF_A1, rec0 + static_cast<long>(c) * R::BYTES + R::A1H, 16384, &bars->va_full);
+                bulk_load(sm + L::OFF_A1, rec0 + static_cast<long>(c) * R::BYTES + R::A1, 16384, &bars->va_full);
             }
         }
     } else if (warp == 1) {
@@ -953,13 +954,12 @@ __device__ __forceinline__ void chain_body(const CUtensorMap* map_q, const CUten
         if (lane == 0) {
             const uint32_t sv = smem_u32(sm + L::OFF_V);
             const uint32_t sa1 = smem_u32(sm + L::OFF_A1);
-            // [U_h^T | U_l^T] = V^T [A1_hi^T | A1_lo^T] into C_UT: V as MN-major A, the
-            // two A1 parts as one K-major B of 128 rows (N = 128)
+            // [U_l^T | U_h^T] = V^T [A1_lo^T | A1_hi^T]: V as MN-major A, A1 lo | hi as one K-major B
             auto issue_u = [&]() {
                 constexpr uint32_t id_u = idesc_bf16(128, 128, true, false);
 #pragma unroll
                 for (int kk = 0; kk < 4; ++kk)
-                    umma_bf16_ss(tmem + C_UT, sdesc_sw128(sv + kk * 2048, 8192, 1024),
+                    umma_bf16_ss(tmem + C_UL, sdesc_sw128(sv + kk * 2048, 8192, 1024),
                                  sdesc_sw128(sa1 + kk * 32, 16, 1024), id_u, kk > 0 ? 1u : 0u);
                 umma_commit(&bars->va_free);
             };
@@ -967,72 +967,54 @@ __device__ __forceinline__ void chain_body(const CUtensorMap* map_q, const CUten
                 tc_fence_after();
                 issue_u();
             }
+            mbar_spin_or_abort(&bars->init_done, 0, err, abort_flag);
+            const uint32_t simg = smem_u32(sm + L::OFF_IMG);
 #pragma unroll 1
             for (int c = 0; c < nchunks; ++c) {
                 const int slot = c & 1;
                 const uint32_t sbase = smem_u32(sm + slot * L::SLOT_BYTES);
-                const uint32_t sk = sbase + L::K_OFF, swt = sbase + L::R_WTH;
-                mbar_spin_or_abort(&bars->slot_full[slot], (c >> 1) & 1, err, abort_flag);
-                mbar_spin_or_abort(&bars->qt_ready[slot], (c >> 1) & 1, err, abort_flag);
-                if (c >= 1) mbar_spin_or_abort(&bars->o_free, (c - 1) & 1, err, abort_flag);
-                // [U_h^T - S^T W_hi^T | U_l^T - S_hi^T W_lo^T | O^T + S_hi^T Q~^T], B negated:
-                // S_hi^T [W_hi^T | W_lo^T | -Q~^T] is one N=192 MMA (three MN-major 64-column
-                // blocks LBO apart, Q~ = -diag(oc) Q built in place by the output warps), then
-                // S_lo^T W_hi^T into the first 64 columns.  Issued per split block as S^T
-                // hi/lo arrive from the state-path threads.
-                constexpr uint32_t id_w3 = idesc_bf16(128, 192, false, true) | (1u << 14);
-                constexpr uint32_t id_w1 = idesc_bf16(128, 64, false, true) | (1u << 14);
-#pragma unroll
-                for (int blk = 0; blk < NBLK; ++blk) {
-                    mbar_spin_or_abort(&bars->split_half[blk], c & 1, err, abort_flag);
-                    tc_fence_after();
-                    if (!*abort_flag) {
-#pragma unroll
-                        for (int g2 = 0; g2 < 2; ++g2) {
-#pragma unroll
-                            for (int k2 = 0; k2 < 2; ++k2) {
-                                const int kk = (g2 * HALF + blk * 32) / 16 + k2;
-                                umma_bf16_ts(tmem + C_UT, tmem + C_SHI + kk * 8,
-                                             sdesc_sw128(swt + kk * 2048, DK * 128, 1024), id_w3, 1u);
-                            }
-                        }
-#pragma unroll
-                        for (int g2 = 0; g2 < 2; ++g2) {
-#pragma unroll
-                            for (int k2 = 0; k2 < 2; ++k2) {
-                                const int kk = (g2 * HALF + blk * 32) / 16 + k2;
-                                umma_bf16_ts(tmem + C_UT, tmem + C_SLO + kk * 8, sdesc_sw128(swt + kk * 2048, 16, 1024),
-                                             id_w1, 1u);
-                            }
-                        }
-                    }
+                mbar_spin_or_abort(&bars->w_full, c & 1, err, abort_flag);
+                mbar_spin_or_abort(&bars->qt_ready, c & 1, err, abort_flag);
+                if (c >= 1) {
+                    mbar_spin_or_abort(&bars->st_done, (c - 1) & 1, err, abort_flag);
+                    mbar_spin_or_abort(&bars->o_free, (c - 1) & 1, err, abort_flag);
                 }
-                if (!*abort_flag) umma_commit(&bars->ws_done);
-                mbar_spin_or_abort(&bars->dv_done, c & 1, err, abort_flag);
                 tc_fence_after();
                 if (!*abort_flag) {
-                    // S^T += dV'^T K (K as MN-major B); dV' hi/lo sit in C_SHI per 32-token half
+                    // [U_h^T | O^T] -= S^T [W^T | -Q~^T]: tf32, A = the fp32 state, B negated
+                    constexpr uint32_t id_w = idesc_tf32(128, 128, false, false) | (1u << 14);
+#pragma unroll
+                    for (int kk = 0; kk < DK / 8; ++kk)
+                        umma_tf32_ts(tmem + C_UH, tmem + C_X + 8 * kk,
+                                     sdesc_sw128(simg + (kk >> 2) * 16384 + (kk & 3) * 32, 16, 1024), id_w, 1u);
+                    umma_commit(&bars->ws_done);
+                }
+                mbar_spin_or_abort(&bars->dv_done, c & 1, err, abort_flag);
+                mbar_spin_or_abort(&bars->slot_full[slot], (c >> 1) & 1, err, abort_flag);
+                tc_fence_after();
+                if (!*abort_flag) {
+                    // S^T = gamma_c S^T (scaled in place by the state path) + dV'^T K, K as MN-major B;
+                    // dV' hi/lo per 32-token half in C_DVH
                     constexpr uint32_t idst = idesc_bf16(128, DK, false, true);
 #pragma unroll
                     for (int p = 0; p < 2; ++p) {
 #pragma unroll
                         for (int kk = 0; kk < 4; ++kk)
-                            umma_bf16_ts(tmem + C_ST, tmem + C_SHI + (kk >> 1) * 32 + p * 16 + (kk & 1) * 8,
-                                         sdesc_sw128(sk + kk * 2048, 8192, 1024), idst, 1u);
+                            umma_bf16_ts(tmem + C_X, tmem + C_DVH + (kk >> 1) * 32 + p * 16 + (kk & 1) * 8,
+                                         sdesc_sw128(sbase + L::K_OFF + kk * 2048, 8192, 1024), idst, 1u);
                     }
                     umma_commit(&bars->st_done);
                     // O^T += dV^T P^T
                     constexpr uint32_t id64 = idesc_bf16(128, 64, false, false);
 #pragma unroll
                     for (int kk = 0; kk < 4; ++kk)
-                        umma_bf16_ts(tmem + C_O, tmem + C_DVB + kk * 8, sdesc_sw128(sbase + L::R_P + kk * 32, 16, 1024),
-                                     id64, 1u);
+                        umma_bf16_ts(tmem + C_O, tmem + C_DVB + kk * 8,
+                                     sdesc_sw128(sbase + L::P_OFF + kk * 32, 16, 1024), id64, 1u);
                     umma_commit(&bars->pdv_done);
                     umma_commit(&bars->slot_free[slot]);
                 }
                 if (c + 1 < nchunks) {
-                    // U^T of the next chunk into C_UT, which the dV conversion has read (dv_done);
-                    // it runs on the tensor pipe while the state path splits the next S
+                    // U of the next chunk, whose region the state-path pass has read (dv_done)
                     const bool ok = mbar_spin_or_abort(&bars->va_full, (c + 1) & 1, err, abort_flag);
                     tc_fence_after();
                     if (ok && !*abort_flag) issue_u();
@@ -1040,14 +1022,14 @@ __device__ __forceinline__ void chain_body(const CUtensorMap* map_q, const CUten
             }
         }
     } else if (warp < 10) {
-        // ======================= state path: 256 threads, lane j twice (one half of the key columns each)
+        // ======================= state path: 256 threads, lane j twice (token half / key half grp)
         const int ct = tid - 64;
         const int grp = ct >> 7;
         const int j = ((warp & 3) << 5) | lane;
         const uint32_t lane_off = static_cast<uint32_t>(warp & 3) << 21;
         const long s_base = static_cast<long>(bh) * DK * args.dv + v0;
 
-        // initial state -> TMEM (S^T: lane j = value column, column d = key index); O^T = 0
+        // initial state -> TMEM (S^T: lane j = value column, column d = key index)
 #pragma unroll
         for (int blk = 0; blk < NBLK; ++blk) {
             float vals[32];
@@ -1057,80 +1039,61 @@ __device__ __forceinline__ void chain_body(const CUtensorMap* map_q, const CUten
                 vals[i] = (args.state_in && j < dv_valid) ? args.state_in[s_base + static_cast<long>(d) * args.dv + j]
                                                           : 0.f;
             }
-            tmem_st32(tmem + lane_off + C_ST + grp * HALF + blk * 32, vals);
-        }
-        {
-            float z[32];
-#pragma unroll
-            for (int i = 0; i < 32; ++i) z[i] = 0.f;
-            tmem_st32(tmem + lane_off + C_O + grp * 32, z);
+            tmem_st32(tmem + lane_off + C_X + grp * HALF + blk * 32, vals);
         }
         tmem_st_wait();
+        tc_fence_before();
+        mbar_arrive(&bars->init_done);
 
 #pragma unroll 1
         for (int c = 0; c < nchunks; ++c) {
-            const int slot = c & 1;
-            const float* G = reinterpret_cast<const float*>(sm + slot * L::SLOT_BYTES + L::R_G);
-            mbar_wait_or_abort(&bars->slot_full[slot], (c >> 1) & 1, err, abort_flag);
-            if (c >= 1) mbar_wait_or_abort(&bars->st_done, (c - 1) & 1, err, abort_flag);
-            tc_fence_after();
-            // ---- S^T -> bf16 hi/lo (TMEM), S^T *= gamma_c; one arrive per 32-column block
-            const float gamma_c = G[128];
-#pragma unroll
-            for (int blk = 0; blk < NBLK; ++blk) {
-                const uint32_t col = grp * HALF + blk * 32;
-                float v[32];
-                tmem_ld32(tmem + lane_off + C_ST + col, v);
-                tmem_ld_wait();
-                uint32_t hi[16], lo[16];
-#pragma unroll
-                for (int i = 0; i < 16; ++i) split2_bf16(v[2 * i], v[2 * i + 1], hi[i], lo[i]);
-                tmem_st16(tmem + lane_off + C_SHI + col / 2, hi);
-                tmem_st16(tmem + lane_off + C_SLO + col / 2, lo);
-#pragma unroll
-                for (int i = 0; i < 32; ++i) v[i] *= gamma_c;
-                tmem_st32(tmem + lane_off + C_ST + col, v);
-                tmem_st_wait();
-                tc_fence_before();
-                mbar_arrive(&bars->split_half[blk]);
-            }
-
-            // ---- dV (bf16) and dV' = dV * exp(Lambda_last - Lambda) (hi/lo), tokens [32 grp, 32 grp + 32)
+            const float* G = gates_of(c);
+            mbar_wait_or_abort(&bars->slot_full[c & 1], (c >> 1) & 1, err, abort_flag);
             mbar_wait_or_abort(&bars->ws_done, c & 1, err, abort_flag);
             tc_fence_after();
+            // ---- dV = U_l + U_h (bf16, for P dV) and dV' = dV e^{Lambda_last - Lambda} (hi/lo),
+            //      tokens [32 grp, 32 grp + 32)
             {
-                float v[32], w[32];
-                tmem_ld32(tmem + lane_off + C_UT + grp * 32, v);
-                tmem_ld32(tmem + lane_off + C_UT + 64 + grp * 32, w);
+                float ul[32], uh[32];
+                tmem_ld32(tmem + lane_off + C_UL + grp * 32, ul);
+                tmem_ld32(tmem + lane_off + C_UH + grp * 32, uh);
                 tmem_ld_wait();
                 const float* edec = G + 64 + grp * 32;
                 uint32_t bw[16], hi[16], lo[16];
 #pragma unroll
                 for (int i = 0; i < 16; ++i) {
-                    const float d0 = v[2 * i] + w[2 * i], d1 = v[2 * i + 1] + w[2 * i + 1];
+                    const float d0 = ul[2 * i] + uh[2 * i], d1 = ul[2 * i + 1] + uh[2 * i + 1];
                     bw[i] = cvt_bf16x2(d0, d1);
                     split2_bf16(d0 * edec[2 * i], d1 * edec[2 * i + 1], hi[i], lo[i]);
                 }
-                // dV' over the S hi columns (free once W S has run; the next split waits for
-                // the state update that reads them), so the next chunk's U can go into C_UT
-                // as soon as this conversion has read it
-                tmem_st16(tmem + lane_off + C_SHI + grp * 32, hi);
-                tmem_st16(tmem + lane_off + C_SHI + grp * 32 + 16, lo);
+                tmem_st16(tmem + lane_off + C_DVH + grp * 32, hi);
+                tmem_st16(tmem + lane_off + C_DVH + grp * 32 + 16, lo);
                 tmem_st16(tmem + lane_off + C_DVB + grp * 16, bw);
+            }
+            // ---- S <- gamma_c S in place, key columns of half grp ([W | Q~] S has read S)
+            const float gamma_c = G[128];
+#pragma unroll
+            for (int blk = 0; blk < NBLK; ++blk) {
+                float v[32];
+                tmem_ld32(tmem + lane_off + C_X + grp * HALF + blk * 32, v);
+                tmem_ld_wait();
+#pragma unroll
+                for (int i = 0; i < 32; ++i) v[i] *= gamma_c;
+                tmem_st32(tmem + lane_off + C_X + grp * HALF + blk * 32, v);
             }
             tmem_st_wait();
             tc_fence_before();
             mbar_arrive(&bars->dv_done);
         }
 
-        // ---- final state S^T -> state_out [dk][dv]
+        // ---- final state -> state_out [dk][dv]
         mbar_wait_or_abort(&bars->st_done, (nchunks - 1) & 1, err, abort_flag);
         tc_fence_after();
         if (!*abort_flag && args.state_out) {
 #pragma unroll
             for (int blk = 0; blk < NBLK; ++blk) {
                 float vals[32];
-                tmem_ld32(tmem + lane_off + C_ST + grp * HALF + blk * 32, vals);
+                tmem_ld32(tmem + lane_off + C_X + grp * HALF + blk * 32, vals);
                 tmem_ld_wait();
                 if (j < dv_valid) {
 #pragma unroll
@@ -1145,60 +1108,80 @@ __device__ __forceinline__ void chain_body(const CUtensorMap* map_q, const CUten
         const int j = ((warp & 3) << 5) | lane;
         const uint32_t lane_off = static_cast<uint32_t>(warp & 3) << 21;
         const bool oleader = (ot == 0);
-        // Q~^T = -diag(oc) Q, transposed in place over chunk cc's q tile: row d of the
-        // MN-major image holds the 64 tokens (B operand of the N=192 MMA, third block)
+        uint8_t* img = sm + L::OFF_IMG;
+        // The image of chunk cc, once [W | Q~] S of chunk cc - 1 has read it: W into rows 0-63
+        // (bulk copies issued by the leader; the record is published, since its slot landed),
+        // -Q~ = -oc Q into rows 64-127 (K-major tf32; the tensor core reads the top 19 bits)
         auto build_qt = [&](int cc) {
             const int slot = cc & 1;
-            uint8_t* qt = sm + slot * L::SLOT_BYTES + L::Q_OFF;
-            const float* oc = reinterpret_cast<const float*>(sm + slot * L::SLOT_BYTES + L::R_G);
+            const uint8_t* qsrc = sm + slot * L::SLOT_BYTES + L::Q_OFF;
+            const float* oc = gates_of(cc);
             mbar_wait_or_abort(&bars->slot_full[slot], (cc >> 1) & 1, err, abort_flag);
-            uint32_t pk[32];
-            const int d = ot;
-            if (d < DK) {
-                const uint8_t* src = qt + (d >> 6) * 8192;
+            if (cc >= 1) mbar_wait_or_abort(&bars->ws_done, (cc - 1) & 1, err, abort_flag);
+            if (oleader && !*abort_flag) {
+                mbar_arrive_expect_tx(&bars->w_full, DK * 256);
+                const uint8_t* rec = rec0 + static_cast<long>(cc) * R::BYTES + R::W;
 #pragma unroll
-                for (int i = 0; i < 32; ++i) {
-                    const float x0 = bf16_bits_to_f32(*reinterpret_cast<const uint16_t*>(src + sw128_off(2 * i, d & 63)));
-                    const float x1 =
-                        bf16_bits_to_f32(*reinterpret_cast<const uint16_t*>(src + sw128_off(2 * i + 1, d & 63)));
-                    pk[i] = cvt_bf16x2(-oc[2 * i] * x0, -oc[2 * i + 1] * x1);
-                }
+                for (int kb = 0; kb < DK / 32; ++kb)
+                    bulk_load(img + kb * 16384, rec + kb * 8192, 8192, &bars->w_full);
+                // the next chunk's W waits for this chunk's product: bring it into L2 now
+                if (cc + 1 < nchunks &&
+                    (!args.ready || ld_relaxed_u32(args.ready + static_cast<long>(bh) * args.nchunks_total + c0 + cc + 1)))
+                    bulk_prefetch_l2(rec + R::BYTES, DK * 256);
             }
-            named_bar(BAR_OUT, 128);                   // every q element has been read
-            if (d < DK) {
+            constexpr int CPR = DK / 8;                    // 16-byte bf16 chunks per token row
 #pragma unroll
-                for (int ch = 0; ch < 8; ++ch)
-                    *reinterpret_cast<uint4*>(qt + sw128_chunk(d, ch)) =
-                        make_uint4(pk[4 * ch], pk[4 * ch + 1], pk[4 * ch + 2], pk[4 * ch + 3]);
+            for (int task = ot; task < kC * CPR; task += 128) {
+                const int t = task / CPR, ch = task % CPR;
+                const uint4 w = *reinterpret_cast<const uint4*>(qsrc + (ch >> 3) * 8192 + sw128_chunk(t, ch & 7));
+                const float s = -oc[t];
+                const uint32_t wv[4] = {w.x, w.y, w.z, w.w};
+                float f[8];
+#pragma unroll
+                for (int u = 0; u < 4; ++u) {
+                    f[2 * u] = __uint_as_float(wv[u] << 16) * s;
+                    f[2 * u + 1] = __uint_as_float(wv[u] & 0xffff0000u) * s;
+                }
+                uint8_t* row = img + (ch >> 2) * 16384 + 8192 + t * 128;
+                *reinterpret_cast<float4*>(row + ((((2 * ch) & 7) ^ (t & 7)) << 4)) = make_float4(f[0], f[1], f[2], f[3]);
+                *reinterpret_cast<float4*>(row + ((((2 * ch + 1) & 7) ^ (t & 7)) << 4)) =
+                    make_float4(f[4], f[5], f[6], f[7]);
             }
             fence_async_smem();
             named_bar(BAR_OUT, 128);
             if (oleader) {
-                mbar_arrive(&bars->qt_ready[slot]);
+                mbar_arrive(&bars->qt_ready);
                 mbar_arrive(&bars->slot_free[slot]);      // the output warps are done with this slot
             }
         };
+        {
+            // O accumulates from the first chunk's [W | Q~] S: start it at zero
+            float z[32];
+#pragma unroll
+            for (int i = 0; i < 32; ++i) z[i] = 0.f;
+            tmem_st32(tmem + lane_off + C_O, z);
+            tmem_st32(tmem + lane_off + C_O + 32, z);
+            tmem_st_wait();
+            tc_fence_before();
+        }
         build_qt(0);
 #pragma unroll 1
         for (int c = 0; c < nchunks; ++c) {
             if (c + 1 < nchunks) build_qt(c + 1);
-            // ---- o[t, j] = O^T[j, t]; the accumulator is reset for the next chunk
+            // ---- o[t, j] = O^T[j, t]
             mbar_wait_or_abort(&bars->pdv_done, c & 1, err, abort_flag);
             tc_fence_after();
             uint32_t ob2[32];                              // bf16 results, tokens (2i, 2i+1)
             {
-                float o[32];
+                float o[64];
+                tmem_ld64(tmem + lane_off + C_O, o);
                 float z[32];
 #pragma unroll
                 for (int i = 0; i < 32; ++i) z[i] = 0.f;
+                tmem_st32(tmem + lane_off + C_O, z);          // O starts at zero for the next chunk
+                tmem_st32(tmem + lane_off + C_O + 32, z);
 #pragma unroll
-                for (int half = 0; half < 2; ++half) {
-                    tmem_ld32(tmem + lane_off + C_O + 32 * half, o);
-                    tmem_ld_wait();
-                    tmem_st32(tmem + lane_off + C_O + 32 * half, z);
-#pragma unroll
-                    for (int i = 0; i < 16; ++i) ob2[16 * half + i] = cvt_bf16x2(o[2 * i], o[2 * i + 1]);
-                }
+                for (int i = 0; i < 32; ++i) ob2[i] = cvt_bf16x2(o[2 * i], o[2 * i + 1]);
                 tmem_st_wait();
             }
             tc_fence_before();

@@ -4,8 +4,9 @@ vectors and the CPU oracle.
 Bar: bf16 output max-abs <= 2e-2 and fp32 final-state
 relative Frobenius error <= 1e-3 versus the fp32 oracle; the reference's own
 harness tolerance (|d| < 1e-2 + 0.05|ref|, tests/test_prefill.py:61-62) is
-checked as a second gate.  The kernel carries ~16-bit products on the state
-path, so the measured state error is far below the bar (~1e-5).
+checked as a second gate.  The state update carries ~16-bit products (bf16
+hi/lo) and W S reads the fp32 state as tf32, so the state error is ~1e-5 at
+the config gates and a few 1e-4 under weak decay.
 """
 import math
 
@@ -107,13 +108,15 @@ def test_prefill_per_head_dt_bias_and_mask(cuda_device):
 
 def test_prefill_slow_decay_long_sequence_precision(cuda_device):
     """Weak decay makes the state remember ~500 tokens: the worst case for
-    error accumulation across chunks (T = 2048, A_log = ln 0.002)."""
+    error accumulation across chunks (T = 2048, A_log = ln 0.002).  The W S
+    product reads the fp32 state as tf32 (a CPU emulation of the scheme puts
+    the state error near 2.5e-4 here, 4x under the bar)."""
     inp = O.make_prefill_inputs(44, 1, 2048, 2, 128, 128, state_std=0.02)
     inp["A_log"] = np.full((2,), math.log(0.002), np.float32)
     o, S = _run(inp)
     o_r, S_r = _oracle(inp)
     _check(o, S, o_r, S_r)
-    assert O.rel_fro(S, S_r) < 1e-4
+    assert O.rel_fro(S, S_r) < 5e-4
 
 
 _MODES = {"pieced": 2, "single": 1, "stream": 3}     # GDN_SCHEDULE_*
