@@ -21,6 +21,7 @@ GDN_ERR_UNSUPPORTED = 5
 GDN_ERR_CUDA = 6
 GDN_ERR_DEVICE = 7
 GDN_ERR_DEVICE_TIMEOUT = 8
+GDN_ERR_ARG = 9
 
 GDN_DTYPE_BF16 = 0
 GDN_DTYPE_F32 = 1
@@ -31,6 +32,8 @@ GDN_SCHEDULE_SINGLE = 1
 GDN_SCHEDULE_PIECED = 2
 GDN_SCHEDULE_STREAM = 3
 GDN_DECODE_L2NORM_QK = 1
+GDN_GATES_BHT = 0
+GDN_GATES_BTH = 1
 
 _P = ctypes.c_void_p
 _I = ctypes.c_int
@@ -41,6 +44,11 @@ class ProjOutSeg(ctypes.Structure):
     """gdn_proj_out_seg (include/gdn_b200.h): one output segment of gdn_proj_multi_fwd."""
     _fields_ = [("W", _P), ("y", _P), ("conv_w", _P), ("conv_state_in", _P), ("conv_state_out", _P),
                 ("Dout", _I), ("l2norm_group", _I)]
+
+
+class PrefillOpts(ctypes.Structure):
+    """gdn_prefill_opts (include/gdn_b200.h): per-call options of gdn_prefill_fwd_ex."""
+    _fields_ = [("schedule", _I), ("gate_layout", _I), ("gate_ld", ctypes.c_long)]
 
 
 class ProjSegment(ctypes.Structure):
@@ -55,6 +63,8 @@ SIGNATURES = {
                         _I, _I, _I, _I, _I, _I, _I, _F, _P],
     "gdn_prefill_fwd_ws": [_P, _P, _P, _P, _P, _P, _I, _F, _P, _P, _P, _P, _P,
                            _I, _I, _I, _I, _I, _I, _I, _F, _P, _Z, _P],
+    "gdn_prefill_fwd_ex": [_P, _P, _P, _P, _P, _P, _I, _F, _P, _P, _P, _P, _P,
+                           _I, _I, _I, _I, _I, _I, _I, _F, _P, _P, _Z, _P],
     "gdn_prefill_window_ws": [_P, _P, _P, _P, _P, _P, _I, _F, _P, _P, _P, _P, _P,
                               _I, _I, _I, _I, _I, _I, _I, _I, _I, _F, _P, _Z, _P],
     "gdn_prefill_workspace_bytes": [_I, _I, _I, _I, _I],
@@ -75,6 +85,7 @@ SIGNATURES = {
     "gdn_prefill_bwd_workspace_bytes": [_I, _I, _I, _I, _I],
     "gdn_prefill_set_schedule": [_I],
     "gdn_prefill_launch_count": [_I, _I, _I, _I, _I],
+    "gdn_prefill_launch_count_ex": [_I, _I, _I, _I, _I, _I],
     "gdn_decode_step": [_P, _P, _P, _P, _P, _I, _P, _P, _P, _P, _P, _I, _I, _I, _I, _I, _F, _P],
     "gdn_decode_step_ex": [_P, _P, _P, _P, _P, _I, _P, _P, _P, _P, _P, _I, _I, _I, _I, _I, _F, _I, _P],
     "gdn_decode_step_gated": [_P, _P, _P, _P, _P, _I, _P, _P, _P, _P, _P, _P, _P, _F, _P,

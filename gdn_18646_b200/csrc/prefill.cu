@@ -147,7 +147,8 @@ struct GateArgs {
     int Ttot;
     unsigned int* err;
     unsigned int* ready; // streamed schedule: per-record ready flags, cleared here
-    long gate_ld;        // elements between the rows of a, b_logits [B*Hv rows] and mask [B rows]
+    long gate_ld;        // elements between the rows of mask [B rows]
+    long g_b, g_h, g_t;  // element strides of a, b_logits over (batch, value head, token)
 };
 
 struct PrepArgs {
@@ -468,18 +469,20 @@ prefill_gates_kernel(const GateArgs args) {
     // valid tokens of this sequence and the offset of its gates (varlen: [Hv, Ttot], packed)
     int start = 0;
     const int T = args.cu ? varlen_seq(args.cu, bidx, args.Ttot, start, args.err) : args.T;
-    const long base = args.cu ? static_cast<long>(h) * args.Ttot + start : static_cast<long>(bh) * args.gate_ld;
+    const long base = args.cu ? static_cast<long>(h) * args.Ttot + start
+                              : static_cast<long>(bidx) * args.g_b + static_cast<long>(h) * args.g_h;
+    const long gt = args.cu ? 1 : args.g_t;
     const int t0 = 2 * lane;
     const int tok = c * kC + t0;
     float a0 = 0.f, a1 = 0.f, b0 = 0.f, b1 = 0.f, m0 = 0.f, m1 = 0.f;
     if (tok < T) {
-        a0 = load_gate(args.a, base + tok, args.gate_dtype);
-        b0 = load_gate(args.b, base + tok, args.gate_dtype);
+        a0 = load_gate(args.a, base + tok * gt, args.gate_dtype);
+        b0 = load_gate(args.b, base + tok * gt, args.gate_dtype);
         m0 = args.mask ? args.mask[static_cast<long>(bidx) * args.gate_ld + tok] : 1.f;
     }
     if (tok + 1 < T) {
-        a1 = load_gate(args.a, base + tok + 1, args.gate_dtype);
-        b1 = load_gate(args.b, base + tok + 1, args.gate_dtype);
+        a1 = load_gate(args.a, base + (tok + 1) * gt, args.gate_dtype);
+        b1 = load_gate(args.b, base + (tok + 1) * gt, args.gate_dtype);
         m1 = args.mask ? args.mask[static_cast<long>(bidx) * args.gate_ld + tok + 1] : 1.f;
     }
     const float A_neg = -expf(args.A_log[h]);
@@ -1291,7 +1294,7 @@ int g_attr_status[2][64];
 int g_sm_count[64];
 
 constexpr int kMaxPieces = 4;
-std::atomic<int> g_schedule{GDN_SCHEDULE_AUTO};
+thread_local int t_schedule = GDN_SCHEDULE_AUTO;   // gdn_prefill_set_schedule: the calling thread's default
 
 // Predicted time (us) of the two schedules, from per-unit costs measured on
 // B200 (config-1 shapes): a round of prep tasks takes ~10 us in the prep
@@ -1385,7 +1388,7 @@ int pick_schedule(int mode, int nbh, int nchunks, int chain_grid, int sms, bool 
 template <int DK>
 int launch_prefill(const CUtensorMap& mq, const CUtensorMap& mk, const CUtensorMap& mv, const CUtensorMap& mo,
                    GateArgs ga, PrepArgs pa, ChainArgs ca, int chain_grid, float* state_tmp, unsigned int* ready,
-                   cudaStream_t st) {
+                   int mode, cudaStream_t st) {
     int dev = 0;
     cudaGetDevice(&dev);
     const int which = DK == 128 ? 1 : 0;
@@ -1408,8 +1411,7 @@ int launch_prefill(const CUtensorMap& mq, const CUtensorMap& mk, const CUtensorM
     const int sms = g_sm_count[dev & 63];
     const int nchunks = ca.nchunks_total;
     const int nbh = ga.ntasks / nchunks;                     // B * Hv
-    const int sched = pick_schedule(g_schedule.load(std::memory_order_relaxed), nbh, nchunks, chain_grid, sms,
-                                    ca.cu != nullptr);
+    const int sched = pick_schedule(mode, nbh, nchunks, chain_grid, sms, ca.cu != nullptr);
     if (sched == GDN_SCHEDULE_STREAM) ga.ready = ready;
 
     prefill_gates_kernel<DK><<<(ga.ntasks + 3) / 4, 128, 0, st>>>(ga);
@@ -1516,15 +1518,15 @@ size_t record_bytes(int dk) { return dk == 128 ? Rec<128>::BYTES : Rec<64>::BYTE
 }  // namespace
 }  // namespace gdn
 
-extern "C" int gdn_prefill_launch_count(int B, int T, int Hv, int dk, int dv) {
+extern "C" int gdn_prefill_launch_count_ex(int B, int T, int Hv, int dk, int dv, int schedule) {
+    if (schedule < GDN_SCHEDULE_AUTO || schedule > GDN_SCHEDULE_STREAM) return -1;
     if (B <= 0 || T <= 0 || Hv <= 0 || !(dk == 64 || dk == 128) || !(dv == 64 || dv == 128 || dv == 256)) return -1;
     int dev = 0, sms = 0;
     if (cudaGetDevice(&dev) != cudaSuccess || cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess)
         return -1;
     const int nchunks = (T + gdn::kC - 1) / gdn::kC;
     const int nbh = B * Hv, chain_grid = nbh * ((dv + 127) / 128);
-    const int sched = gdn::pick_schedule(gdn::g_schedule.load(std::memory_order_relaxed), nbh, nchunks, chain_grid,
-                                         sms, false);
+    const int sched = gdn::pick_schedule(schedule, nbh, nchunks, chain_grid, sms, false);
     if (sched == GDN_SCHEDULE_STREAM)                     // gates, (lead prep), the cooperative prep + chain launch
         return gdn::stream_lead(nbh, nchunks, chain_grid, sms) > 0 ? 3 : 2;
     if (sched == GDN_SCHEDULE_SINGLE) return 3;
@@ -1532,11 +1534,16 @@ extern "C" int gdn_prefill_launch_count(int B, int T, int Hv, int dk, int dv) {
     return 2 + (nchunks + per - 1) / per;                // gates, prep(piece 0), overlaps, last chain
 }
 
+extern "C" int gdn_prefill_launch_count(int B, int T, int Hv, int dk, int dv) {
+    return gdn_prefill_launch_count_ex(B, T, Hv, dk, dv, gdn::t_schedule);
+}
+
+// The calling host thread's default schedule (other threads keep theirs).
 extern "C" int gdn_prefill_set_schedule(int mode) {
     if (mode != GDN_SCHEDULE_AUTO && mode != GDN_SCHEDULE_SINGLE && mode != GDN_SCHEDULE_PIECED &&
         mode != GDN_SCHEDULE_STREAM)
-        return gdn::fail(GDN_ERR_DTYPE, "gdn_prefill_set_schedule: unknown mode %d", mode);
-    gdn::g_schedule.store(mode);
+        return gdn::fail(GDN_ERR_ARG, "gdn_prefill_set_schedule: unknown mode %d", mode);
+    gdn::t_schedule = mode;
     return GDN_OK;
 }
 
@@ -1590,7 +1597,7 @@ int run_prefill(const void* q, const void* k, const void* v, const float* A_log,
                 int gate_dtype, float dt_bias, const float* dt_bias_vec, const float* mask, const float* state_in,
                 void* out, float* state_out, int B, int T, int Hqk, int Hv, int dk, int dv, int layout, float scale,
                 void* workspace, size_t workspace_bytes, void* stream, const int* cu, int Ttot, long gate_ld = 0,
-                long tld = 0) {
+                long tld = 0, int schedule = -1, int gate_layout = GDN_GATES_BHT, long gate_tok_ld = 0) {
     int st = GDN_OK;
     const long ntiles = (dv + 127) / 128;
     const long nchunks = (static_cast<long>(T) + kC - 1) / kC;
@@ -1631,6 +1638,15 @@ int run_prefill(const void* q, const void* k, const void* v, const float* A_log,
     ga.err = device_error_word();
     ga.ready = nullptr;
     ga.gate_ld = gate_ld > 0 ? gate_ld : T;
+    if (gate_layout == GDN_GATES_BTH) {            // [B, T, gate_tok_ld], head h at column h
+        ga.g_t = gate_tok_ld;
+        ga.g_h = 1;
+        ga.g_b = static_cast<long>(T) * gate_tok_ld;
+    } else {                                        // [B, Hv, T] rows gate_ld apart
+        ga.g_t = 1;
+        ga.g_h = ga.gate_ld;
+        ga.g_b = static_cast<long>(Hv) * ga.gate_ld;
+    }
 
     PrepArgs pa;
     pa.rec = static_cast<uint8_t*>(workspace);
@@ -1671,8 +1687,9 @@ int run_prefill(const void* q, const void* k, const void* v, const float* A_log,
     cudaStream_t s = static_cast<cudaStream_t>(stream);
     unsigned int* ready = reinterpret_cast<unsigned int*>(reinterpret_cast<uint8_t*>(state_tmp) +
                                                           static_cast<size_t>(B) * Hv * dk * dv * 4);
-    if (dk == 128) return launch_prefill<128>(mq, mk, mv, mo, ga, pa, ca, grid, state_tmp, ready, s);
-    return launch_prefill<64>(mq, mk, mv, mo, ga, pa, ca, grid, state_tmp, ready, s);
+    const int mode = schedule >= 0 ? schedule : t_schedule;
+    if (dk == 128) return launch_prefill<128>(mq, mk, mv, mo, ga, pa, ca, grid, state_tmp, ready, mode, s);
+    return launch_prefill<64>(mq, mk, mv, mo, ga, pa, ca, grid, state_tmp, ready, mode, s);
 }
 }  // namespace
 }  // namespace gdn
@@ -1688,6 +1705,32 @@ extern "C" int gdn_prefill_fwd_ws(const void* q, const void* k, const void* v, c
     if (st != GDN_OK) return st;
     return run_prefill(q, k, v, A_log, a, b_logits, gate_dtype, dt_bias, dt_bias_vec, mask, state_in, out, state_out,
                        B, T, Hqk, Hv, dk, dv, layout, scale, workspace, workspace_bytes, stream, nullptr, 0);
+}
+
+// gdn_prefill_fwd_ws with per-call options: the launch schedule and the gate layout
+// ([B, Hv, T], or token rows [B, T, gate_ld] read in place).
+extern "C" int gdn_prefill_fwd_ex(const void* q, const void* k, const void* v, const float* A_log, const void* a,
+                                  const void* b_logits, int gate_dtype, float dt_bias, const float* dt_bias_vec,
+                                  const float* mask, const float* state_in, void* out, float* state_out, int B,
+                                  int T, int Hqk, int Hv, int dk, int dv, int layout, float scale,
+                                  const gdn_prefill_opts* opts, void* workspace, size_t workspace_bytes,
+                                  void* stream) {
+    using namespace gdn;
+    const int st = validate_prefill(q, k, v, A_log, a, b_logits, gate_dtype, state_in, out, state_out, B, T, Hqk, Hv,
+                                    dk, dv, layout);
+    if (st != GDN_OK) return st;
+    const int schedule = opts ? opts->schedule : GDN_SCHEDULE_AUTO;
+    const int gl = opts ? opts->gate_layout : GDN_GATES_BHT;
+    const long gld = opts ? opts->gate_ld : 0;
+    if (schedule < GDN_SCHEDULE_AUTO || schedule > GDN_SCHEDULE_STREAM)
+        return fail(GDN_ERR_ARG, "gdn_prefill_fwd_ex: unknown schedule %d", schedule);
+    if (gl != GDN_GATES_BHT && gl != GDN_GATES_BTH)
+        return fail(GDN_ERR_ARG, "gdn_prefill_fwd_ex: unknown gate layout %d", gl);
+    if (gl == GDN_GATES_BTH && gld < Hv)
+        return fail(GDN_ERR_SHAPE, "gdn_prefill_fwd_ex: gate_ld %ld below Hv=%d", gld, Hv);
+    return run_prefill(q, k, v, A_log, a, b_logits, gate_dtype, dt_bias, dt_bias_vec, mask, state_in, out, state_out,
+                       B, T, Hqk, Hv, dk, dv, layout, scale, workspace, workspace_bytes, stream, nullptr, 0, 0, 0,
+                       schedule, gl, gld);
 }
 
 namespace gdn {

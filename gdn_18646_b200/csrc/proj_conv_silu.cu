@@ -43,7 +43,7 @@ constexpr int PROJ_SMEM = OFF_BAR + 128 + 1024;
 static_assert(PROJ_SMEM <= 232448, "proj shared memory exceeds 227 KB");
 constexpr int kProjThreads = 192;     // 6 warps
 
-constexpr int kProjMaxSeg = 4;
+constexpr int kProjMaxSeg = 6;
 
 // One output-channel segment of a launch: its own weights, conv and output tensors.
 struct ProjSeg {

@@ -123,13 +123,13 @@ int make_map_bf16(CUtensorMap* map, const void* base, int rank, const uint64_t* 
 
 namespace gdn {
 namespace {
-std::atomic<int> g_launch_overlap{0};
+thread_local int t_launch_overlap = 0;
 }  // namespace
-bool launch_overlap() { return g_launch_overlap.load(std::memory_order_relaxed) != 0; }
+bool launch_overlap() { return t_launch_overlap != 0; }
 }  // namespace gdn
 
 extern "C" int gdn_set_launch_overlap(int on) {
-    gdn::g_launch_overlap.store(on ? 1 : 0, std::memory_order_relaxed);
+    gdn::t_launch_overlap = on ? 1 : 0;
     return GDN_OK;
 }
 

@@ -1,10 +1,12 @@
 """Gated DeltaNet layer on the libgdn_b200 kernels.
 
-Prefill (T tokens):
-    x [B,T,D] -> RMSNorm -> q,k = L2norm(SiLU(conv4(x Wq^T))), v = SiLU(conv4(x Wv^T))
-              -> z = x Wz^T, a = x Wa^T, b = x Wb^T  (cuBLAS, plain GEMMs)
-              -> chunked gated delta rule (grouped value heads, [B,T,H,D] layout)
-              -> gated RMSNorm(o) * SiLU(z) -> x Wo^T
+Prefill (T tokens), five launches of the library's kernels:
+    x [B,T,D] -> RMSNorm
+              -> q,k = L2norm(SiLU(conv4(x Wq^T))), v = SiLU(conv4(x Wv^T)), z = x Wz^T and
+                 [a | b] = x [Wa | Wb]^T, one persistent tcgen05 GEMM launch over the five segments
+              -> chunked gated delta rule (grouped value heads, [B,T,H,D] layout; a and b read
+                 in place from the [B,T,2Hv] projection output as token rows)
+              -> gated RMSNorm(o) * SiLU(z) -> y Wo^T (the same GEMM kernel, one plain segment)
 Decode (1 token) runs the same blocks with the carried recurrent state
 [B,Hv,dk,dv] fp32 and the three conv histories [B,C,3] bf16 (the last three
 projected values per channel); ``prefill`` returns both so decode continues a
@@ -70,13 +72,16 @@ def make_weights(cfg: GDNConfig, device="cuda", seed=0, std=0.02):
 
 
 class GDNLayer:
-    """B200 Gated DeltaNet layer; every op is a libgdn_b200 kernel except the
-    plain z / a,b / output GEMMs (cuBLAS through torch)."""
+    """B200 Gated DeltaNet layer; every op is a libgdn_b200 kernel."""
 
     def __init__(self, weights: dict, cfg: GDNConfig | None = None):
         self.w = weights
         self.cfg = cfg or GDNConfig()
         self.scale = self.cfg.dk ** -0.5
+        # the a | b gate rows padded with zero rows to the projection kernel's 128-channel tile
+        W_ab = weights["W_ab"]
+        pad = (-W_ab.shape[0]) % 128
+        self.W_ab_tile = torch.cat([W_ab, W_ab.new_zeros(pad, W_ab.shape[1])]) if pad else W_ab
 
     def init_state(self, B: int, device="cuda", fill=torch.zeros):
         """Zero state (``fill=torch.empty``: buffers a prefill overwrites completely)."""
@@ -89,20 +94,20 @@ class GDNLayer:
         )
 
     def _project(self, xn, state_in, state_out):
-        """q, k (L2-normalised per head), v, z and the a/b gate logits for xn [B,T,D]."""
+        """q, k (L2-normalised per head), v, z and the a|b gate logits [B,T,128] for
+        xn [B,T,D], all in one launch."""
         c, w = self.cfg, self.w
-        B, T, D = xn.shape
         si = state_in or {}
-        # q | k | v (conv4 + SiLU, q/k L2-normalised per head) in one launch
-        q, k, v = ops.proj_multi(xn, [
+        # q | k | v (conv4 + SiLU, q/k L2-normalised per head), z, a | b (plain rows)
+        q, k, v, z, ab = ops.proj_multi(xn, [
             dict(W=w["W_q"], conv_w=w["conv_q"], l2norm_group=c.dk, conv_state_in=si.get("conv_q"),
                  conv_state_out=state_out["conv_q"]),
             dict(W=w["W_k"], conv_w=w["conv_k"], l2norm_group=c.dk, conv_state_in=si.get("conv_k"),
                  conv_state_out=state_out["conv_k"]),
             dict(W=w["W_v"], conv_w=w["conv_v"], conv_state_in=si.get("conv_v"), conv_state_out=state_out["conv_v"]),
+            dict(W=w["W_z"]),
+            dict(W=self.W_ab_tile),
         ])
-        z = xn @ w["W_z"].T
-        ab = xn @ w["W_ab"].T                                    # [B, T, 2*Hv]
         return q, k, v, z, ab
 
     @torch.no_grad()
@@ -115,16 +120,17 @@ class GDNLayer:
         xn = ops.rmsnorm(x.reshape(B * T, D), w["norm_gamma"], c.eps).reshape(B, T, D)
         new_state = self.init_state(B, x.device, fill=torch.empty)   # written by the projections and prefill
         q, k, v, z, ab = self._project(xn, state, new_state)
-        a = ab[..., :c.n_v].transpose(1, 2).contiguous()        # [B, Hv, T]
-        b = ab[..., c.n_v:].transpose(1, 2).contiguous()
+        a, b = ab[..., :c.n_v], ab[..., c.n_v:2 * c.n_v]          # [B, T, Hv] token rows, read in place
         o, S = ops.prefill(q.view(B, T, c.n_qk, c.dk), k.view(B, T, c.n_qk, c.dk), v.view(B, T, c.n_v, c.dv),
                            w["A_log"], a, b, dt_bias=w["dt_bias"],
                            state_in=None if state is None else state["recurrent"],
-                           scale=self.scale, layout="bthd", state_out=new_state["recurrent"])
+                           scale=self.scale, layout="bthd", state_out=new_state["recurrent"], gates="bth")
         y = ops.gated_rmsnorm(o.view(B * T * c.n_v, c.dv), z.view(B * T * c.n_v, c.dv), w["onorm_gamma"], c.eps)
+        (out,) = ops.proj_multi(y.view(B, T, c.v_dim), [dict(W=w["W_o"])])
         if trace is not None:
-            trace.update(xn=xn, q=q, k=k, v=v, z=z, a=a, b=b, o=o, y_norm=y.view(B, T, c.v_dim))
-        return y.view(B, T, c.v_dim) @ w["W_o"].T, new_state
+            trace.update(xn=xn, q=q, k=k, v=v, z=z, a=a.transpose(1, 2), b=b.transpose(1, 2), o=o,
+                         y_norm=y.view(B, T, c.v_dim))
+        return out, new_state
 
     @torch.no_grad()
     def decode(self, x: torch.Tensor, state: dict, out_state: dict | None = None):

@@ -61,26 +61,36 @@ def _cuda_contig(t: torch.Tensor, name: str, dtype=None) -> None:
 # ---------------------------------------------------------------------------
 
 
+_SCHEDULES = {None: 0, "auto": 0, "single": 1, "pieced": 2, "stream": 3}
+
+
 def prefill(q, k, v, A_log, a, b_logits, *, dt_bias=0.0, mask=None, state_in=None,
-            scale=0.0, layout="bhtd", out=None, state_out=None, return_state=True):
+            scale=0.0, layout="bhtd", out=None, state_out=None, return_state=True, gates="bht", schedule=None):
     """Chunked gated-delta-rule prefill (reference/prefill_ref.py semantics).
 
     layout "bhtd": q,k [B,Hqk,T,dk], v [B,Hv,T,dv]; "bthd": q,k [B,T,Hqk,dk], v [B,T,Hv,dv].
-    a, b_logits [B,Hv,T] (bf16 or f32); A_log [Hv] f32; dt_bias float or f32 [Hv];
-    mask [B,T] f32 or None; state_in [B,Hv,dk,dv] f32 or None.
+    a, b_logits [B,Hv,T] (bf16 or f32), or with gates="bth" [B,T,Hv] views whose
+    token rows share one stride (read in place, e.g. the halves of a [B,T,2Hv]
+    projection); A_log [Hv] f32; dt_bias float or f32 [Hv]; mask [B,T] f32 or None;
+    state_in [B,Hv,dk,dv] f32 or None; schedule None/"auto", "single", "pieced" or
+    "stream" for this call (gdn_prefill_fwd_ex).
     Returns (out bf16 in v's layout, state_out f32 [B,Hv,dk,dv] or None).
     """
+    _need(gates in ("bht", "bth"), f"gates must be 'bht' or 'bth', got {gates!r}")
+    _need(schedule in _SCHEDULES, f"schedule must be one of {sorted(k_ for k_ in _SCHEDULES if k_)}, got {schedule!r}")
     lay, B, T, Hqk, Hv, dk, dv, gdt, dt_scalar, dt_vec = _prefill_checks(q, k, v, A_log, a, b_logits, dt_bias, mask,
-                                                                         state_in, layout)
+                                                                         state_in, layout, gates)
     if out is None:
         out = torch.empty_like(v)
     if state_out is None and return_state:
         state_out = torch.empty(B, Hv, dk, dv, dtype=torch.float32, device=q.device)
     ws_bytes = _lib.lib().gdn_prefill_workspace_bytes(B, T, Hv, dk, dv)
     ws = torch.empty(max(int(ws_bytes), 1), dtype=torch.uint8, device=q.device)
-    _lib.call("gdn_prefill_fwd_ws", _ptr(q), _ptr(k), _ptr(v), _ptr(A_log), _ptr(a), _ptr(b_logits), gdt,
+    opts = _lib.PrefillOpts(_SCHEDULES[schedule], _lib.GDN_GATES_BTH if gates == "bth" else _lib.GDN_GATES_BHT,
+                            a.stride(1) if gates == "bth" else 0)
+    _lib.call("gdn_prefill_fwd_ex", _ptr(q), _ptr(k), _ptr(v), _ptr(A_log), _ptr(a), _ptr(b_logits), gdt,
               dt_scalar, _ptr(dt_vec), _ptr(mask), _ptr(state_in), _ptr(out), _ptr(state_out),
-              B, T, Hqk, Hv, dk, dv, lay, float(scale), _ptr(ws), int(ws_bytes), _stream())
+              B, T, Hqk, Hv, dk, dv, lay, float(scale), ctypes.byref(opts), _ptr(ws), int(ws_bytes), _stream())
     return out, state_out
 
 
@@ -110,9 +120,11 @@ def prefill_window(q, k, v, A_log, a, b_logits, t0, Tw, *, out, dt_bias=0.0, mas
     return out, state_out
 
 
-def _prefill_checks(q, k, v, A_log, a, b_logits, dt_bias, mask, state_in, layout):
+def _prefill_checks(q, k, v, A_log, a, b_logits, dt_bias, mask, state_in, layout, gates="bht"):
     """Shape, dtype and device checks shared by the prefill wrappers; returns
-    (layout code, B, T, Hqk, Hv, dk, dv, gate dtype code, dt_bias scalar, dt_bias vector)."""
+    (layout code, B, T, Hqk, Hv, dk, dv, gate dtype code, dt_bias scalar, dt_bias vector).
+    ``gates`` "bht": a, b_logits contiguous [B, Hv, T]; "bth": [B, T, Hv] views whose
+    tokens are rows of one stride (e.g. the halves of a [B, T, 2 Hv] projection)."""
     lay = GDN_LAYOUT_BHTD if layout == "bhtd" else GDN_LAYOUT_BTHD
     for name, t in (("q", q), ("k", k), ("v", v)):
         _cuda_contig(t, name, torch.bfloat16)
@@ -125,9 +137,17 @@ def _prefill_checks(q, k, v, A_log, a, b_logits, dt_bias, mask, state_in, layout
     _need(tuple(k.shape) == tuple(q.shape), "k must have q's shape")
     gdt = _gate_dtype(a, "a")
     _need(b_logits.dtype == a.dtype, "a and b_logits must share a dtype")
-    _cuda_contig(a, "a")
-    _cuda_contig(b_logits, "b_logits")
-    _need(tuple(a.shape) == (B, Hv, T) and tuple(b_logits.shape) == (B, Hv, T), "a, b_logits must be [B, Hv, T]")
+    if gates == "bth":
+        _need(a.is_cuda and b_logits.is_cuda, "a and b_logits must be CUDA tensors")
+        _need(tuple(a.shape) == (B, T, Hv) and tuple(b_logits.shape) == (B, T, Hv),
+              "a, b_logits must be [B, T, Hv] with gates='bth'")
+        ld = a.stride(1)
+        _need(a.stride(2) == 1 and tuple(b_logits.stride()) == tuple(a.stride()) and a.stride(0) == T * ld
+              and ld >= Hv, "a, b_logits (gates='bth'): token rows of one stride, heads contiguous")
+    else:
+        _cuda_contig(a, "a")
+        _cuda_contig(b_logits, "b_logits")
+        _need(tuple(a.shape) == (B, Hv, T) and tuple(b_logits.shape) == (B, Hv, T), "a, b_logits must be [B, Hv, T]")
     _cuda_contig(A_log, "A_log", torch.float32)
     dt_vec = None
     dt_scalar = 0.0
@@ -454,7 +474,7 @@ def proj_conv_silu(x, W, conv_w, *, conv_state_in=None, conv_state_out=None, l2n
 
 def proj_multi(x, segments):
     """Several projections of the same x [B,T,D] bf16 in one launch (gdn_proj_multi_fwd).
-    ``segments``: up to 4 dicts with ``W`` [Dout, D] bf16 and optionally ``conv_w``
+    ``segments``: up to 6 dicts with ``W`` [Dout, D] bf16 and optionally ``conv_w``
     [Dout, 4] (without it: a plain projection x @ W^T rounded to bf16),
     ``conv_state_in`` / ``conv_state_out`` [B, Dout, 3], ``l2norm_group`` and ``out``
     [B, T, Dout].  Returns the list of outputs, each as ``proj_conv_silu`` (or the

@@ -34,7 +34,8 @@ enum {
     GDN_ERR_UNSUPPORTED = 5, /* head dims or widths this build does not cover  */
     GDN_ERR_CUDA = 6,        /* a CUDA runtime/driver call or launch failed    */
     GDN_ERR_DEVICE = 7,      /* the current device is not an sm_100 part       */
-    GDN_ERR_DEVICE_TIMEOUT = 8 /* a kernel gave up on a bounded wait           */
+    GDN_ERR_DEVICE_TIMEOUT = 8, /* a kernel gave up on a bounded wait          */
+    GDN_ERR_ARG = 9          /* an option value (schedule, gate layout) out of range */
 };
 
 /* dtype codes for gate / activation inputs */
@@ -85,7 +86,9 @@ int gdn_prefill_fwd(const void* q, const void* k, const void* v,
 size_t gdn_prefill_workspace_bytes(int B, int T, int Hv, int dk, int dv);
 
 /*
- * Prefill launch schedule (process-wide; default GDN_SCHEDULE_AUTO):
+ * Prefill launch schedule (default GDN_SCHEDULE_AUTO).  gdn_prefill_set_schedule
+ * sets the default for calls made from the CALLING HOST THREAD only (other
+ * threads keep theirs); gdn_prefill_fwd_ex takes the schedule per call.
  *   SINGLE  one prep launch over all chunks, then one chain launch;
  *   PIECED  the chunks cut into up to 4 pieces, the chain of piece k running
  *           in the same launch as the prep of piece k+1;
@@ -100,11 +103,44 @@ size_t gdn_prefill_workspace_bytes(int B, int T, int Hv, int dk, int dv);
  * reference (single kernel).
  */
 enum { GDN_SCHEDULE_AUTO = 0, GDN_SCHEDULE_SINGLE = 1, GDN_SCHEDULE_PIECED = 2, GDN_SCHEDULE_STREAM = 3 };
-int gdn_prefill_set_schedule(int mode);
+int gdn_prefill_set_schedule(int mode);      /* GDN_ERR_ARG for an unknown mode */
 
 /* Kernel launches one gdn_prefill_fwd call makes on the current device under
- * the current schedule (3 for SINGLE, 2 or 3 for STREAM), or -1 for invalid shapes / no device. */
+ * the calling thread's schedule (3 for SINGLE, 2 or 3 for STREAM), or -1 for
+ * invalid shapes / no device; _ex: under the given schedule. */
 int gdn_prefill_launch_count(int B, int T, int Hv, int dk, int dv);
+int gdn_prefill_launch_count_ex(int B, int T, int Hv, int dk, int dv, int schedule);
+
+/*
+ * Per-call options of gdn_prefill_fwd_ex.  No counterpart in the reference.
+ *   schedule     GDN_SCHEDULE_* for this call (AUTO: the cost model's choice).
+ *   gate_layout  GDN_GATES_BHT: a, b_logits [B, Hv, T] (the reference's layout);
+ *                GDN_GATES_BTH: one row of gate_ld elements per token, [B, T, gate_ld],
+ *                head h at column h -- e.g. the a and b halves of a [B, T, 2 Hv]
+ *                projection output read in place (b_logits = a + Hv, gate_ld = 2 Hv).
+ *   gate_ld      GDN_GATES_BTH: elements between consecutive tokens' rows (>= Hv).
+ */
+enum { GDN_GATES_BHT = 0, GDN_GATES_BTH = 1 };
+typedef struct {
+    int schedule;
+    int gate_layout;
+    long gate_ld;
+} gdn_prefill_opts;
+
+/*
+ * gdn_prefill_fwd_ws with per-call options (opts == NULL: AUTO schedule, BHT
+ * gates).  The mask stays [B, T].  Errors as gdn_prefill_fwd_ws, plus
+ * GDN_ERR_ARG for an unknown schedule or gate layout and GDN_ERR_SHAPE for a
+ * gate_ld below Hv.
+ */
+int gdn_prefill_fwd_ex(const void* q, const void* k, const void* v,
+                       const float* A_log, const void* a, const void* b_logits, int gate_dtype,
+                       float dt_bias, const float* dt_bias_vec,
+                       const float* mask, const float* state_in,
+                       void* out, float* state_out,
+                       int B, int T, int Hqk, int Hv, int dk, int dv, int layout,
+                       float scale, const gdn_prefill_opts* opts,
+                       void* workspace, size_t workspace_bytes, void* stream);
 
 /*
  * gdn_prefill_fwd with a caller-provided workspace (device memory,
@@ -400,7 +436,7 @@ int gdn_proj_conv_silu_fwd(const void* x, const void* W, const void* conv_w, voi
                            int l2norm_group, void* stream);
 
 /*
- * gdn_proj_conv_silu_fwd over up to 4 output segments in one launch, all from
+ * gdn_proj_conv_silu_fwd over up to 6 output segments in one launch, all from
  * the same x [B, T, D] bf16: each segment has its own weights W [Dout, D], output
  * y [B, T, Dout] and, optionally, conv weights (NULL: a plain projection
  * y = bf16(x . W^T), no conv or SiLU), conv histories and per-head L2 norm.
@@ -426,7 +462,7 @@ int gdn_proj_multi_fwd(const void* x, int B, int T, int D, const gdn_proj_out_se
 const char* gdn_last_error(void);
 
 /*
- * Process-wide (default 0): with on != 0 the decode-step kernels
+ * Per calling host thread (default 0): with on != 0 the decode-step kernels
  * (gdn_decode_proj_fwd, gdn_decode_step[_ex], gdn_rmsnorm_fwd,
  * gdn_gated_rmsnorm_fwd) launch with programmatic stream serialisation: each
  * lets the next kernel of the stream launch early and waits for its own

@@ -132,7 +132,7 @@ def test_python_surface_raises_runtime_error(lib):
 
 
 def test_prefill_workspace_and_schedule_entry_points(lib):
-    rec = 2048 + 16384 + 2 * 128 * 128 + 8192 + 1024           # gate block, A1 hi/lo, W^T hi/lo, P, gates
+    rec = 2048 + 16384 + 2 * 128 * 128 + 8192 + 1024           # gate block, A1 lo/hi, W (tf32), P, gates
 
     def flags(n):                                               # one 4-byte ready flag per record, 128 B granules
         return (4 * n + 127) // 128 * 128
@@ -142,7 +142,7 @@ def test_prefill_workspace_and_schedule_entry_points(lib):
         2 * 64 * 64 * 4 + flags(2 * 2)
     assert lib.gdn_prefill_workspace_bytes(1, 64, 2, 96, 64) == 0
     assert lib.gdn_prefill_workspace_bytes(0, 64, 2, 128, 128) == 0
-    assert _lib.call_status("gdn_prefill_set_schedule", 7) == _lib.GDN_ERR_DTYPE
+    assert _lib.call_status("gdn_prefill_set_schedule", 7) == _lib.GDN_ERR_ARG
     assert _lib.call_status("gdn_prefill_set_schedule", _lib.GDN_SCHEDULE_AUTO) == _lib.GDN_OK
     assert lib.gdn_prefill_launch_count(1, 64, 2, 96, 64) == -1
 
@@ -309,7 +309,7 @@ def test_proj_multi_rejects(lib):
         s_.W, s_.y, s_.conv_w, s_.Dout, s_.l2norm_group = FAKE, FAKE, None, 128, 0
     assert _lib.call_status("gdn_proj_multi_fwd", None, 1, 8, 64, segs, 2, None) == _lib.GDN_ERR_NULL
     assert _lib.call_status("gdn_proj_multi_fwd", FAKE, 1, 8, 64, segs, 0, None) == _lib.GDN_ERR_SHAPE
-    assert _lib.call_status("gdn_proj_multi_fwd", FAKE, 1, 8, 64, segs, 5, None) == _lib.GDN_ERR_SHAPE
+    assert _lib.call_status("gdn_proj_multi_fwd", FAKE, 1, 8, 64, segs, 7, None) == _lib.GDN_ERR_SHAPE
     segs[1].Dout = 100
     assert _lib.call_status("gdn_proj_multi_fwd", FAKE, 1, 8, 64, segs, 2, None) == _lib.GDN_ERR_SHAPE
     segs[1].Dout, segs[1].y = 128, ODD
@@ -347,3 +347,38 @@ def test_gather_window_rejects(lib):
     assert call(t0=64, Tw=128) == _lib.GDN_ERR_SHAPE
     assert call(layout=3) == _lib.GDN_ERR_DTYPE
     assert call(world=1, rank=0, peers=one_missing) == _lib.GDN_OK   # nothing to pull, nothing enqueued
+
+
+def test_prefill_fwd_ex_rejects(lib):
+    """Per-call options: unknown schedule or gate layout -> GDN_ERR_ARG, a token-row
+    gate stride below Hv -> GDN_ERR_SHAPE; otherwise the _ws checks apply."""
+    def call(schedule=0, gl=0, gld=0, ws=ODD, wsb=1 << 40, **over):
+        args = prefill_args(**over)[:-1]                      # ... scale (stream goes last)
+        opts = _lib.PrefillOpts(schedule, gl, gld)
+        return _lib.call_status("gdn_prefill_fwd_ex", *args, ctypes.byref(opts), ws, wsb, None)
+    assert call(schedule=4) == _lib.GDN_ERR_ARG
+    assert call(schedule=-1) == _lib.GDN_ERR_ARG
+    assert call(gl=2) == _lib.GDN_ERR_ARG
+    assert "gate layout" in _lib.last_error()
+    assert call(gl=1, gld=1) == _lib.GDN_ERR_SHAPE             # Hv = 2 gates per token row at least
+    assert call(q=None) == _lib.GDN_ERR_NULL
+    assert call(gl=1, gld=64) == _lib.GDN_ERR_ALIGN             # everything else valid: the workspace
+    args = prefill_args()[:-1]
+    assert _lib.call_status("gdn_prefill_fwd_ex", *args, None, ODD, 1 << 40, None) == _lib.GDN_ERR_ALIGN
+
+
+def test_schedule_is_per_thread(lib):
+    """gdn_prefill_set_schedule changes the calling thread's default only."""
+    import threading
+    seen = {}
+
+    def other():
+        seen["count"] = lib.gdn_prefill_launch_count_ex(1, 1000, 4, 128, 256, _lib.GDN_SCHEDULE_PIECED)
+        seen["default"] = _lib.call_status("gdn_prefill_set_schedule", _lib.GDN_SCHEDULE_SINGLE)
+    _lib.call("gdn_prefill_set_schedule", _lib.GDN_SCHEDULE_AUTO)
+    t = threading.Thread(target=other)
+    t.start()
+    t.join()
+    assert seen["default"] == _lib.GDN_OK
+    assert lib.gdn_prefill_launch_count_ex(1, 64, 2, 96, 64, 0) == -1
+    assert lib.gdn_prefill_launch_count_ex(1, 64, 2, 128, 64, 9) == -1

@@ -22,7 +22,7 @@ O_TOL = 2e-2
 S_TOL = 1e-3
 
 
-def _run(inp, *, layout="bhtd", Hqk=None, state_out=True, dt_vec=None):
+def _run(inp, *, layout="bhtd", Hqk=None, state_out=True, dt_vec=None, schedule=None):
     import torch
     from gdn_18646_b200 import ops
     q, k, v = to_dev(inp["q"]), to_dev(inp["k"]), to_dev(inp["v"])
@@ -32,7 +32,7 @@ def _run(inp, *, layout="bhtd", Hqk=None, state_out=True, dt_vec=None):
     dtb = to_dev(dt_vec) if dt_vec is not None else float(inp["dt_bias"])
     out = torch.full_like(v, float("nan"))       # poisoned: every element must be written
     o, S = ops.prefill(q, k, v, to_dev(inp["A_log"]), a, b, dt_bias=dtb, mask=mask, state_in=s_in,
-                       scale=float(inp["scale"]), layout=layout, out=out, return_state=state_out)
+                       scale=float(inp["scale"]), layout=layout, out=out, return_state=state_out, schedule=schedule)
     torch.cuda.synchronize()
     return to_np(o), (to_np(S) if S is not None else None)
 
@@ -119,9 +119,6 @@ def test_prefill_slow_decay_long_sequence_precision(cuda_device):
     assert O.rel_fro(S, S_r) < 5e-4
 
 
-_MODES = {"pieced": 2, "single": 1, "stream": 3}     # GDN_SCHEDULE_*
-
-
 @pytest.mark.parametrize("schedule", ["pieced", "single", "stream"])
 @pytest.mark.parametrize("B,T,H,Hqk,dk,dv", [(1, 1000, 4, 2, 128, 256), (2, 1100, 2, 2, 64, 128), (1, 150, 2, 2, 128, 64)])
 def test_prefill_schedules(cuda_device, schedule, B, T, H, Hqk, dk, dv):
@@ -132,15 +129,8 @@ def test_prefill_schedules(cuda_device, schedule, B, T, H, Hqk, dk, dv):
     two value tiles (dv = 256), dk = 64 and pieces of unequal length (18 chunks ->
     5+5+5+3, 3 chunks -> 1+1+1).  STREAM does the same arithmetic as SINGLE in a
     different order of tasks, so its results are bit-identical."""
-    from gdn_18646_b200 import _lib
     inp = O.make_prefill_inputs(60 + T, B, T, H, dk, dv, state_std=0.02, layout="bthd", Hqk=Hqk)
-    res = {}
-    for mode in (schedule, "single"):
-        _lib.call("gdn_prefill_set_schedule", _MODES[mode])
-        try:
-            res[mode] = _run(inp, layout="bthd", Hqk=Hqk)
-        finally:
-            _lib.call("gdn_prefill_set_schedule", _lib.GDN_SCHEDULE_AUTO)
+    res = {mode: _run(inp, layout="bthd", Hqk=Hqk, schedule=mode) for mode in (schedule, "single")}
     o, S = res[schedule]
     o_r, S_r = _oracle(inp, layout="bthd")
     _check(o, S, o_r, S_r)
@@ -151,14 +141,29 @@ def test_prefill_schedules(cuda_device, schedule, B, T, H, Hqk, dk, dv):
 def test_prefill_launch_count(cuda_device):
     from gdn_18646_b200 import _lib
     lib = _lib.lib()
-    assert lib.gdn_prefill_launch_count(4, 4096, 16, 128, 128) == 2        # config 1: gates, stream (no lead)
+    assert lib.gdn_prefill_launch_count(4, 4096, 16, 128, 128) in (2, 3)   # config 1: gates, (lead prep), stream
     assert lib.gdn_prefill_launch_count(8, 4096, 32, 128, 128) == 3        # 256 chains >= SMs: single
-    _lib.call("gdn_prefill_set_schedule", _lib.GDN_SCHEDULE_PIECED)
-    try:
-        assert lib.gdn_prefill_launch_count(1, 1000, 4, 128, 256) == 6     # gates, prep, 3 overlaps, chain
-        assert lib.gdn_prefill_launch_count(1, 150, 2, 128, 64) == 5       # 3 one-chunk pieces
-    finally:
-        _lib.call("gdn_prefill_set_schedule", _lib.GDN_SCHEDULE_AUTO)
+    pieced = _lib.GDN_SCHEDULE_PIECED
+    assert lib.gdn_prefill_launch_count_ex(1, 1000, 4, 128, 256, pieced) == 6   # gates, prep, 3 overlaps, chain
+    assert lib.gdn_prefill_launch_count_ex(1, 150, 2, 128, 64, pieced) == 5     # 3 one-chunk pieces
+
+
+def test_prefill_token_row_gates_in_place(cuda_device):
+    """Gates read in place from token rows (the a | b halves of one [B, T, 2 Hv]
+    projection output, gdn_prefill_fwd_ex with GDN_GATES_BTH) give the bits of the
+    same gates as contiguous [B, Hv, T] tensors."""
+    import torch
+    from gdn_18646_b200 import ops
+    inp = O.make_prefill_inputs(71, 2, 300, 4, 128, 128, state_std=0.02, layout="bthd", Hqk=2)
+    q, k, v = to_dev(inp["q"]), to_dev(inp["k"]), to_dev(inp["v"])
+    a, b = to_dev(inp["a"]), to_dev(inp["b"])                       # [B, Hv, T]
+    ab = torch.cat([a.transpose(1, 2), b.transpose(1, 2), torch.zeros_like(a.transpose(1, 2))], -1).contiguous()
+    A_log, s0 = to_dev(inp["A_log"]), to_dev(inp["state_in"])
+    o1, S1 = ops.prefill(q, k, v, A_log, a, b, state_in=s0, scale=inp["scale"], layout="bthd")
+    o2, S2 = ops.prefill(q, k, v, A_log, ab[..., :4], ab[..., 4:8], state_in=s0, scale=inp["scale"], layout="bthd",
+                         gates="bth")
+    torch.cuda.synchronize()
+    assert torch.equal(o1, o2) and torch.equal(S1, S2)
 
 
 def test_prefill_state_continuation(cuda_device):
