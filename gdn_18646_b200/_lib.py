@@ -99,6 +99,7 @@ SIGNATURES = {
     "gdn_outproj_reduce": [_P, _P, _I, _I, _I, _P],
     "gdn_gather_window": [_P, ctypes.POINTER(ctypes.c_void_p), _I, _I, _I, _I, _I, _I, _I, _I, _I, _P],
     "gdn_check_device_error": [],
+    "gdn_test_prefill_hooks": [ctypes.c_longlong, ctypes.c_longlong],
     "gdn_set_launch_overlap": [_I],
     "gdn_last_error": [],
     "gdn_version": [],

@@ -108,9 +108,14 @@ __device__ __forceinline__ float load_gate(const void* p, long idx, int dtype) {
 }
 
 // ---------------------------------------------------------------------------
-// mbarrier (bounded waits: a wait that exceeds ~2^31 cycles records
-// DERR_TIMEOUT in the error word and returns false instead of hanging)
+// mbarrier (bounded waits: a wait that exceeds its cycle budget, ~2^31 cycles,
+// records DERR_TIMEOUT in the error word and returns false instead of hanging)
 // ---------------------------------------------------------------------------
+// Cycle budget of the bounded waits of the kernels in this translation unit
+// (each .cu file has its own copy); a test hook of the prefill lowers it.
+static __device__ long long g_wait_budget = 1ll << 31;
+__device__ __forceinline__ long long wait_budget() { return *const_cast<volatile long long*>(&g_wait_budget); }
+
 __device__ __forceinline__ void mbar_init(uint64_t* bar, uint32_t count) {
     asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(smem_u32(bar)), "r"(count));
 }
@@ -140,9 +145,9 @@ __device__ __forceinline__ bool mbar_try_wait(uint64_t* bar, uint32_t parity) {
 // the cycle budget ran out (the error word is then set).
 __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, unsigned int* err) {
     if (mbar_try_wait(bar, parity)) return true;
-    const long long t0 = clock64();
+    const long long t0 = clock64(), budget = wait_budget();
     while (!mbar_try_wait(bar, parity)) {
-        if (clock64() - t0 > (1ll << 31)) {
+        if (clock64() - t0 > budget) {
             if (err) atomicOr(err, DERR_TIMEOUT);
             return false;
         }
@@ -240,10 +245,10 @@ __device__ __forceinline__ void named_bar(int id, int nthreads) {
 __device__ __forceinline__ bool mbar_wait_or_abort(uint64_t* bar, uint32_t parity, unsigned int* err,
                                                    volatile int* abort) {
     if (mbar_try_wait(bar, parity)) return true;
-    const long long t0 = clock64();
+    const long long t0 = clock64(), budget = wait_budget();
     while (!mbar_try_wait(bar, parity)) {
         if (*abort) return false;
-        if (clock64() - t0 > (1ll << 31)) {
+        if (clock64() - t0 > budget) {
             if (err) atomicOr(err, DERR_TIMEOUT);
             *abort = 1;
             return false;
@@ -269,10 +274,10 @@ __device__ __forceinline__ bool mbar_test_wait(uint64_t* bar, uint32_t parity) {
 __device__ __forceinline__ bool mbar_spin_or_abort(uint64_t* bar, uint32_t parity, unsigned int* err,
                                                    volatile int* abort) {
     if (mbar_test_wait(bar, parity)) return true;
-    const long long t0 = clock64();
+    const long long t0 = clock64(), budget = wait_budget();
     while (!mbar_test_wait(bar, parity)) {
         if (*abort) return false;
-        if (clock64() - t0 > (1ll << 31)) {
+        if (clock64() - t0 > budget) {
             if (err) atomicOr(err, DERR_TIMEOUT);
             *abort = 1;
             return false;

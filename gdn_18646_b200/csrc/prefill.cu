@@ -62,6 +62,9 @@ namespace gdn {
 namespace {
 
 constexpr int kC = 64;                 // chunk length
+// Test hook (gdn_test_prefill_hooks): a record whose ready flag the streamed
+// schedule's prep workers leave unset, or -1.
+static __device__ long long g_unpublished_record = -1;
 constexpr int BAR_PREP = 1;            // named barrier of the prep kernel's 128 threads
 constexpr int BAR_OUT = 2;             // named barrier of the chain kernel's output warps
 
@@ -201,7 +204,7 @@ struct ChainSmem {
 
 struct ChainBars {
     uint64_t slot_full[2], slot_free[2], va_full, va_free, w_full;
-    uint64_t ws_done, dv_done, st_done, pdv_done, qt_ready, o_free, init_done;
+    uint64_t ws_done, dv_done, st_done, pdv_done, qt_ready, o_free, init_done, mma_drain;
 };
 
 struct ChainArgs {
@@ -234,15 +237,15 @@ __device__ __forceinline__ uint32_t ld_relaxed_u32(const unsigned int* flag) {
     asm volatile("ld.relaxed.gpu.global.u32 %0, [%1];" : "=r"(v) : "l"(flag) : "memory");
     return v;
 }
-// Bounded wait for a record flag (~2^31 cycles, then DERR_TIMEOUT and the CTA's abort flag).
+// Bounded wait for a record flag (the wait budget, then DERR_TIMEOUT and the CTA's abort flag).
 __device__ __forceinline__ bool wait_record(const unsigned int* flag, unsigned int* err, volatile int* abort) {
-    const long long t0 = clock64();
+    const long long t0 = clock64(), budget = wait_budget();
     for (;;) {
         uint32_t v;
         asm volatile("ld.acquire.gpu.global.u32 %0, [%1];" : "=r"(v) : "l"(flag) : "memory");
         if (v != 0) break;
         if (*abort) return false;
-        if (clock64() - t0 > (1ll << 31)) {
+        if (clock64() - t0 > budget) {
             if (err) atomicOr(err, DERR_TIMEOUT);
             *abort = 1;
             return false;
@@ -635,7 +638,7 @@ __device__ __forceinline__ void prep_body(const CUtensorMap* map_q, const CUtens
             // so they have (nearly) completed; publish its record now rather than a task
             // later (a chain CTA waits for it)
             bulk_wait_all0();
-            publish_record(args.ready + published);
+            if (published != g_unpublished_record) publish_record(args.ready + published);
             published = -1;
         }
         if (leader && !*abort_flag) {
@@ -822,7 +825,7 @@ __device__ __forceinline__ void prep_body(const CUtensorMap* map_q, const CUtens
 
     if (leader) {
         bulk_wait_all0();                              // record stores complete before the worker ends
-        if (args.ready && published >= 0) publish_record(args.ready + published);
+        if (args.ready && published >= 0 && published != g_unpublished_record) publish_record(args.ready + published);
     }
     tc_fence_before();
     named_bar(bar_id, kPrepThreads);
@@ -899,6 +902,7 @@ __device__ __forceinline__ void chain_body(const CUtensorMap* map_q, const CUten
         mbar_init(&bars->qt_ready, 1);
         mbar_init(&bars->o_free, 128);
         mbar_init(&bars->init_done, 256);
+        mbar_init(&bars->mma_drain, 1);
         *abort_flag = 0;
         fence_mbar_init();
         tma_prefetch_desc(map_q);
@@ -920,6 +924,8 @@ __device__ __forceinline__ void chain_body(const CUtensorMap* map_q, const CUten
 
     if (warp == 0) {
         // ======================= producer: lane 0 the per-chunk slot, lane 1 V and A1
+        // each lane waits (bounded) for its last copy to land before the CTA can exit
+        int last = -1;
         if (lane == 0) {
             for (int c = 0; c < nchunks; ++c) {
                 const int slot = c & 1;
@@ -938,7 +944,9 @@ __device__ __forceinline__ void chain_body(const CUtensorMap* map_q, const CUten
                                 trow0 + (c0 + c) * kC, hq, bco);
                 }
                 bulk_load(dst + L::P_OFF, rec + R::P, 8192 + 1024, &bars->slot_full[slot]);
+                last = c;
             }
+            if (last >= 0) mbar_wait(&bars->slot_full[last & 1], (last >> 1) & 1, err);
         } else if (lane == 1) {
             for (int c = 0; c < nchunks; ++c) {
                 if (c >= 1 && !mbar_wait_or_abort(&bars->va_free, (c - 1) & 1, err, abort_flag)) break;
@@ -950,7 +958,9 @@ __device__ __forceinline__ void chain_body(const CUtensorMap* map_q, const CUten
                     tma_load_4d(sm + L::OFF_V + vb * 8192, map_v, &bars->va_full, v0 + vb * 64, trow0 + (c0 + c) * kC, h,
                                 bco);
                 bulk_load(sm + L::OFF_A1, rec0 + static_cast<long>(c) * R::BYTES + R::A1, 16384, &bars->va_full);
+                last = c;
             }
+            if (last >= 0) mbar_wait(&bars->va_full, last & 1, err);
         }
     } else if (warp == 1) {
         // ======================= MMA issuer (one thread)
@@ -1023,6 +1033,9 @@ __device__ __forceinline__ void chain_body(const CUtensorMap* map_q, const CUten
                     if (ok && !*abort_flag) issue_u();
                 }
             }
+            // every MMA issued has completed before TMEM is released (also after an abort)
+            umma_commit(&bars->mma_drain);
+            mbar_wait(&bars->mma_drain, 0, err);
         }
     } else if (warp < 10) {
         // ======================= state path: 256 threads, lane j twice (token half / key half grp)
@@ -1112,6 +1125,7 @@ __device__ __forceinline__ void chain_body(const CUtensorMap* map_q, const CUten
         const uint32_t lane_off = static_cast<uint32_t>(warp & 3) << 21;
         const bool oleader = (ot == 0);
         uint8_t* img = sm + L::OFF_IMG;
+        int w_last = -1;                                   // last chunk whose W copy the leader issued
         // The image of chunk cc, once [W | Q~] S of chunk cc - 1 has read it: W into rows 0-63
         // (bulk copies issued by the leader; the record is published, since its slot landed),
         // -Q~ = -oc Q into rows 64-127 (K-major tf32; the tensor core reads the top 19 bits)
@@ -1122,6 +1136,7 @@ __device__ __forceinline__ void chain_body(const CUtensorMap* map_q, const CUten
             mbar_wait_or_abort(&bars->slot_full[slot], (cc >> 1) & 1, err, abort_flag);
             if (cc >= 1) mbar_wait_or_abort(&bars->ws_done, (cc - 1) & 1, err, abort_flag);
             if (oleader && !*abort_flag) {
+                w_last = cc;
                 mbar_arrive_expect_tx(&bars->w_full, DK * 256);
                 const uint8_t* rec = rec0 + static_cast<long>(cc) * R::BYTES + R::W;
 #pragma unroll
@@ -1222,7 +1237,10 @@ __device__ __forceinline__ void chain_body(const CUtensorMap* map_q, const CUten
                 bulk_commit();
             }
         }
-        if (oleader) bulk_wait_all0();
+        if (oleader) {
+            bulk_wait_all0();
+            if (w_last >= 0) mbar_wait(&bars->w_full, w_last & 1, err);   // the last W copy has landed
+        }
     }
 
     tc_fence_before();
@@ -1536,6 +1554,20 @@ extern "C" int gdn_prefill_launch_count_ex(int B, int T, int Hv, int dk, int dv,
 
 extern "C" int gdn_prefill_launch_count(int B, int T, int Hv, int dk, int dv) {
     return gdn_prefill_launch_count_ex(B, T, Hv, dk, dv, gdn::t_schedule);
+}
+
+// Test hooks of the prefill kernels on the current device: the cycle budget of
+// their bounded waits (0: the default, ~2^31) and a streamed-schedule record left
+// unpublished (-1: none).
+extern "C" int gdn_test_prefill_hooks(long long wait_budget_cycles, long long unpublished_record) {
+    if (wait_budget_cycles < 0 || unpublished_record < -1)
+        return gdn::fail(GDN_ERR_ARG, "gdn_test_prefill_hooks: budget %lld / record %lld out of range",
+                         wait_budget_cycles, unpublished_record);
+    const long long budget = wait_budget_cycles > 0 ? wait_budget_cycles : (1ll << 31);
+    if (cudaMemcpyToSymbol(gdn::g_wait_budget, &budget, sizeof(budget)) != cudaSuccess ||
+        cudaMemcpyToSymbol(gdn::g_unpublished_record, &unpublished_record, sizeof(unpublished_record)) != cudaSuccess)
+        return gdn::fail(GDN_ERR_CUDA, "gdn_test_prefill_hooks: %s", cudaGetErrorString(cudaGetLastError()));
+    return GDN_OK;
 }
 
 // The calling host thread's default schedule (other threads keep theirs).

@@ -520,6 +520,22 @@ const char* gdn_version(void);
  */
 int gdn_check_device_error(void);
 
+/*
+ * Test hooks of the prefill kernels on the current device, for exercising the
+ * bounded waits without faulting the GPU.  No counterpart in the reference.
+ *   wait_budget_cycles  > 0: the cycle budget of every bounded wait of the
+ *                       prefill kernels (0 restores the default, about 2^31 cycles);
+ *   unpublished_record  >= 0: the streamed schedule's prep workers leave the ready
+ *                       flag of that chunk record (index b * Hv * nchunks + h *
+ *                       nchunks + chunk) unset; -1 publishes every record.
+ * With both set, a streamed prefill's chain CTA gives up waiting for that record:
+ * every role of the CTA drains (its copies land, its MMAs complete) and returns,
+ * gdn_check_device_error() reports GDN_ERR_DEVICE_TIMEOUT, and that call's outputs
+ * are undefined.  Reset both (0, -1) before ordinary use.  Synchronous.
+ * Errors: GDN_ERR_ARG (negative budget, record below -1), GDN_ERR_CUDA.
+ */
+int gdn_test_prefill_hooks(long long wait_budget_cycles, long long unpublished_record);
+
 #ifdef __cplusplus
 }
 #endif

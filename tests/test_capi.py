@@ -382,3 +382,8 @@ def test_schedule_is_per_thread(lib):
     assert seen["default"] == _lib.GDN_OK
     assert lib.gdn_prefill_launch_count_ex(1, 64, 2, 96, 64, 0) == -1
     assert lib.gdn_prefill_launch_count_ex(1, 64, 2, 128, 64, 9) == -1
+
+
+def test_prefill_test_hooks_reject(lib):
+    assert _lib.call_status("gdn_test_prefill_hooks", -1, -1) == _lib.GDN_ERR_ARG
+    assert _lib.call_status("gdn_test_prefill_hooks", 0, -2) == _lib.GDN_ERR_ARG
