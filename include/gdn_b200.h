@@ -197,7 +197,9 @@ int gdn_prefill_window_ws(const void* q, const void* k, const void* v,
  *     8 sequences of 4096 tokens); use gdn_prefill_fwd_ws for larger ones.
  *   - The first call on a device looks up the array's device address
  *     (cudaGetSymbolAddress, once per device); make that first call before
- *     any stream capture.
+ *     any stream capture.  The address is kept for the life of the process:
+ *     after a cudaDeviceReset (or anything else that recreates the device's
+ *     primary context) this entry point must not be called again.
  *   - Every call uses the same array, which keeps the previous call's
  *     contents; each call writes every value it uses before using it, so
  *     nothing needs clearing.  Calls that overlap on the GPU (different
