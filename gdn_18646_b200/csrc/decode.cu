@@ -206,7 +206,7 @@ decode_step_kernel(const uint16_t* q, const uint16_t* k, const uint16_t* v, cons
                                  bf16_bits_to_f32(zw.y & 0xffffu), bf16_bits_to_f32(zw.y >> 16)};
             float yo[4];
 #pragma unroll
-            for (int c = 0; c < 4; ++c) yo[c] = (oj[c] * r) * gf[c] * silu_f(zf[c]);
+            for (int c = 0; c < 4; ++c) yo[c] = (oj[c] * r) * gf[c] * silu_fast(zf[c]);
             *reinterpret_cast<uint2*>(y + static_cast<long>(bh) * DV + 4 * cg) =
                 make_uint2(pack_bf16x2(yo[0], yo[1]), pack_bf16x2(yo[2], yo[3]));
         }

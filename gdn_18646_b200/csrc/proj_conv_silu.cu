@@ -7,18 +7,30 @@
 // (kernels/fused_proj_conv_silu.cu:105-295, WMMA + cp.async).
 //
 // The GEMM is computed TRANSPOSED: D[c, t] = sum_d W[c, d] x[t, d], with
-// 128 output channels on the TMEM lanes (MMA M = 128) and 256 consecutive
-// tokens on the TMEM columns (MMA N = 256).  Each epilogue thread therefore
-// owns one channel across 256 tokens and the causal conv along tokens is a
-// register-local sliding window.  A tile's GEMM rows start 3 tokens before
-// its first output token (TMA zero-fills negative token coordinates, which is
-// exactly the reference's causal zero padding), so each tile emits 253 tokens.
+// output channels on the TMEM lanes and 256 consecutive tokens on the TMEM
+// columns (MMA N = 256).  Each epilogue thread therefore owns one channel
+// across 256 tokens and the causal conv along tokens is a register-local
+// sliding window.  A tile's GEMM rows start 3 tokens before its first output
+// token (TMA zero-fills negative token coordinates, which is exactly the
+// reference's causal zero padding), so each tile emits 253 tokens.
+//
+// The CTAs run in pairs (clusters of 2) issuing tcgen05 cta_group::2 MMAs of
+// M = 256: each CTA loads its own 128 channel rows of W and HALF of the 256
+// token rows of x, and the pair's MMA reads the other half from the peer's
+// shared memory.  Per CTA that is 32 KB of operands per 64-deep k step instead
+// of 48 KB for a one-CTA 128 x 256 tile, which is what bounded that version (its
+// shared-memory fill plus the MMA reads exceeded the SM's shared-memory
+// bandwidth).  No load is multicast.  The two channel tiles of a pair are
+// independent (they may belong to different segments); with an odd number of
+// channel tiles the last pair's second CTA repeats the last tile and stores
+// nothing.
 //
 // Persistent, warp-specialised: warp 0 = TMA producer (W and x tiles, 128B
-// swizzle, 3-stage ring), warp 1 = MMA issuer (tcgen05.mma kind::f16, both
-// operands K-major), warps 2-5 = epilogue (TMEM -> conv/SiLU/L2 -> smem ->
-// TMA store).  Two TMEM accumulators (2 x 256 columns) let the epilogue of
-// tile i overlap the MMAs of tile i+1.
+// swizzle, 5-stage ring, completion counted on the even CTA's barriers),
+// warp 1 = MMA issuer (even CTA only; its commits arrive on both CTAs'
+// barriers), warps 2-5 = epilogue (TMEM -> conv/SiLU/L2 -> smem -> TMA store;
+// each CTA its own 128 channels).  Two TMEM accumulators (2 x 256 columns) let
+// the epilogue of tile i overlap the MMAs of tile i+1.
 #include <cstring>
 #include <mutex>
 
@@ -32,9 +44,10 @@ constexpr int PM = 128;               // channels per tile (MMA M)
 constexpr int PN = 256;               // token rows per tile (MMA N)
 constexpr int POUT = PN - 3;          // output tokens per tile
 constexpr int PK = 64;                // K per stage (one 128-byte swizzle atom of bf16)
-constexpr int PSTAGES = 3;
+constexpr int PSTAGES = 5;
+constexpr int PNH = PN / 2;           // token rows of x each CTA of the pair loads
 constexpr int A_BYTES = PM * PK * 2;  // 16 KB
-constexpr int B_BYTES = PN * PK * 2;  // 32 KB
+constexpr int B_BYTES = PNH * PK * 2; // 16 KB
 constexpr int STAGE_BYTES = A_BYTES + B_BYTES;
 constexpr int Y_SUB_BYTES = PN * 128; // one 64-channel output sub-tile: 256 rows x 128 B
 constexpr int OFF_Y = PSTAGES * STAGE_BYTES;
@@ -58,7 +71,7 @@ struct ProjSeg {
 struct ProjArgs {
     unsigned int* err;
     int B, T, D;
-    int n_ct, n_tt, ntiles;      // n_ct: channel tiles over all segments
+    int n_ct, n_tt, ntiles;      // n_ct: channel tiles over all segments; ntiles: pair tiles
     int nseg;
     ProjSeg seg[kProjMaxSeg];
 };
@@ -78,7 +91,7 @@ __device__ __forceinline__ int proj_seg_of(const ProjArgs& a, int ct) {
 
 __device__ __forceinline__ float bf16r(float x) { return __uint_as_float(static_cast<uint32_t>(f32_to_bf16_bits(x)) << 16); }
 
-__global__ void __launch_bounds__(kProjThreads, 1)
+__global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kProjThreads, 1)
 proj_conv_silu_kernel(const __grid_constant__ ProjMaps maps, const __grid_constant__ CUtensorMap map_x,
                       const __grid_constant__ ProjArgs args) {
     extern __shared__ uint8_t smem_raw[];
@@ -95,6 +108,15 @@ proj_conv_silu_kernel(const __grid_constant__ ProjMaps maps, const __grid_consta
     const int warp = tid >> 5;
     const int lane = tid & 31;
     const int nk = args.D / PK;
+    const uint32_t rank = cluster_ctarank();        // 0: the pair's MMA issuer
+    const int pair = static_cast<int>(blockIdx.x >> 1), npairs = static_cast<int>(gridDim.x >> 1);
+    const int n_cp = (args.n_ct + 1) >> 1;          // channel-tile pairs
+    // this CTA's channel tile of pair tile `pt` (the last tile again when n_ct is odd: not stored)
+    auto my_ct = [&](int pt, bool& valid) {
+        const int ct = 2 * (pt % n_cp) + static_cast<int>(rank);
+        valid = ct < args.n_ct;
+        return valid ? ct : args.n_ct - 1;
+    };
 
     if (tid == 0) {
         for (int s = 0; s < PSTAGES; ++s) {
@@ -103,7 +125,7 @@ proj_conv_silu_kernel(const __grid_constant__ ProjMaps maps, const __grid_consta
         }
         for (int s = 0; s < 2; ++s) {
             mbar_init(&acc_full[s], 1);
-            mbar_init(&acc_empty[s], 4);
+            mbar_init(&acc_empty[s], 8);            // even CTA's: 4 epilogue warps of each CTA
         }
         *abort_flag = 0;
         fence_mbar_init();
@@ -114,11 +136,11 @@ proj_conv_silu_kernel(const __grid_constant__ ProjMaps maps, const __grid_consta
         tma_prefetch_desc(&map_x);
     }
     if (warp == 1) {
-        tmem_alloc(tmem_slot, 512);
-        tmem_relinquish();
+        tmem_alloc_pair(tmem_slot, 512);
+        tmem_relinquish_pair();
     }
     tc_fence_before();
-    __syncthreads();
+    cluster_sync();                                 // both CTAs' barriers initialised before any remote arrive
     tc_fence_after();
     const uint32_t tmem = *tmem_slot;
 
@@ -127,9 +149,10 @@ proj_conv_silu_kernel(const __grid_constant__ ProjMaps maps, const __grid_consta
         if (lane == 0) {
             int stage = 0;
             uint32_t phase = 0;
-            for (int tile = blockIdx.x; tile < args.ntiles; tile += gridDim.x) {
-                const int ct = tile % args.n_ct;
-                const int rest = tile / args.n_ct;
+            for (int tile = pair; tile < args.ntiles; tile += npairs) {
+                bool valid;
+                const int ct = my_ct(tile, valid);
+                const int rest = tile / n_cp;
                 const int tt = rest % args.n_tt;
                 const int b = rest / args.n_tt;
                 const int ts = tt * POUT - 3;
@@ -139,9 +162,11 @@ proj_conv_silu_kernel(const __grid_constant__ ProjMaps maps, const __grid_consta
                 for (int kb = 0; kb < nk; ++kb) {
                     if (!mbar_wait_or_abort(&empty[stage], phase ^ 1u, args.err, abort_flag)) break;
                     uint8_t* st = sm + stage * STAGE_BYTES;
-                    mbar_arrive_expect_tx(&full[stage], STAGE_BYTES);
-                    tma_load_2d(st, mw, &full[stage], kb * PK, lct * PM);
-                    tma_load_3d(st + A_BYTES, &map_x, &full[stage], kb * PK, ts, b);
+                    // both CTAs' bytes complete on the even CTA's barrier, which expects them all
+                    const uint32_t fb = mapa_shared(smem_u32(&full[stage]), 0);
+                    if (rank == 0) mbar_arrive_expect_tx(&full[stage], 2 * STAGE_BYTES);
+                    tma_load_2d_pair(st, mw, fb, kb * PK, lct * PM);
+                    tma_load_3d_pair(st + A_BYTES, &map_x, fb, kb * PK, ts + static_cast<int>(rank) * PNH, b);
                     if (++stage == PSTAGES) {
                         stage = 0;
                         phase ^= 1u;
@@ -151,13 +176,13 @@ proj_conv_silu_kernel(const __grid_constant__ ProjMaps maps, const __grid_consta
             }
         }
     } else if (warp == 1) {
-        // ---------------- MMA issuer
-        if (lane == 0) {
+        // ---------------- MMA issuer (the pair's even CTA)
+        if (lane == 0 && rank == 0) {
             int stage = 0;
             uint32_t phase = 0;
             int local = 0;
-            constexpr uint32_t idesc = idesc_bf16(PM, PN, false, false);
-            for (int tile = blockIdx.x; tile < args.ntiles; tile += gridDim.x, ++local) {
+            constexpr uint32_t idesc = idesc_bf16(2 * PM, PN, false, false);
+            for (int tile = pair; tile < args.ntiles; tile += npairs, ++local) {
                 const int abuf = local & 1;
                 const uint32_t aphase = static_cast<uint32_t>(local >> 1) & 1u;
                 if (!mbar_wait_or_abort(&acc_empty[abuf], aphase ^ 1u, args.err, abort_flag)) break;
@@ -170,16 +195,16 @@ proj_conv_silu_kernel(const __grid_constant__ ProjMaps maps, const __grid_consta
                     const uint32_t sb = sa + A_BYTES;
 #pragma unroll
                     for (int k = 0; k < PK / 16; ++k)
-                        umma_bf16_ss(d_tmem, sdesc_sw128(sa + k * 32, 16, 1024), sdesc_sw128(sb + k * 32, 16, 1024),
-                                     idesc, (kb > 0 || k > 0) ? 1u : 0u);
-                    umma_commit(&empty[stage]);
+                        umma_bf16_ss_pair(d_tmem, sdesc_sw128(sa + k * 32, 16, 1024),
+                                          sdesc_sw128(sb + k * 32, 16, 1024), idesc, (kb > 0 || k > 0) ? 1u : 0u);
+                    umma_commit_pair(&empty[stage]);
                     if (++stage == PSTAGES) {
                         stage = 0;
                         phase ^= 1u;
                     }
                 }
                 if (*abort_flag) break;
-                umma_commit(&acc_full[abuf]);
+                umma_commit_pair(&acc_full[abuf]);
             }
         }
     } else {
@@ -189,9 +214,12 @@ proj_conv_silu_kernel(const __grid_constant__ ProjMaps maps, const __grid_consta
         const int et = tid - 64;                    // 0..127
         const uint32_t lane_off = static_cast<uint32_t>(quad * 32) << 16;
         int local = 0;
-        for (int tile = blockIdx.x; tile < args.ntiles; tile += gridDim.x, ++local) {
-            const int ct = tile % args.n_ct;
-            const int rest = tile / args.n_ct;
+        const uint32_t acc_empty_even[2] = {mapa_shared(smem_u32(&acc_empty[0]), 0),
+                                            mapa_shared(smem_u32(&acc_empty[1]), 0)};
+        for (int tile = pair; tile < args.ntiles; tile += npairs, ++local) {
+            bool valid;
+            const int ct = my_ct(tile, valid);
+            const int rest = tile / n_cp;
             const int tt = rest % args.n_tt;
             const int b = rest / args.n_tt;
             const int t0 = tt * POUT;
@@ -225,6 +253,7 @@ proj_conv_silu_kernel(const __grid_constant__ ProjMaps maps, const __grid_consta
             const uint32_t ccol = cl & 63;
             // tiles that touch the conv history (first tile with state_in, last tile with state_out)
             const bool special = conv && ((tt == 0 && S.state_in) || (S.state_out && ts + PN > args.T - 3));
+            uint16_t* const state_out = valid ? S.state_out : nullptr;    // a repeated tile writes nothing
 #pragma unroll 1
             for (int blk = 0; blk < PN / 32; ++blk) {
                 float acc[32];
@@ -262,8 +291,8 @@ proj_conv_silu_kernel(const __grid_constant__ ProjMaps maps, const __grid_consta
                         const int tok = ts + i;
                         float p = bf16r(acc[u]);
                         if (tok < 0) p = S.state_in ? bf16_bits_to_f32(S.state_in[sbase + (tok + 3)]) : 0.f;
-                        if (S.state_out && tok < args.T && tok >= args.T - 3 && (i >= 3 || tt == 0))
-                            S.state_out[sbase + (tok - (args.T - 3))] = f32_to_bf16_bits(p);
+                        if (state_out && tok < args.T && tok >= args.T - 3 && (i >= 3 || tt == 0))
+                            state_out[sbase + (tok - (args.T - 3))] = f32_to_bf16_bits(p);
                         if (i >= 3) {
                             float conv = p1 * w0;
                             conv = fmaf(p2, w1, conv);
@@ -279,10 +308,10 @@ proj_conv_silu_kernel(const __grid_constant__ ProjMaps maps, const __grid_consta
                     }
                 }
             }
-            // accumulator buffer free for the MMA warp
+            // accumulator buffer free for the MMA warp (on the even CTA's barrier)
             tc_fence_before();
             __syncwarp();
-            if (lane == 0) mbar_arrive(&acc_empty[abuf]);
+            if (lane == 0) mbar_arrive_cluster(acc_empty_even[abuf]);
 
             if (S.l2) {
                 // per token row: the 128 channels as 16 chunks of 8 (16-byte shared-memory
@@ -337,7 +366,7 @@ proj_conv_silu_kernel(const __grid_constant__ ProjMaps maps, const __grid_consta
             }
             fence_async_smem();
             named_bar(1, 128);
-            if (et == 0 && ok && !*abort_flag) {
+            if (et == 0 && ok && valid && !*abort_flag) {
                 tma_store_3d(&maps.y[sg], ysm, lct * PM, t0, b);
                 tma_store_3d(&maps.y[sg], ysm + Y_SUB_BYTES, lct * PM + 64, t0, b);
                 bulk_commit();
@@ -347,8 +376,8 @@ proj_conv_silu_kernel(const __grid_constant__ ProjMaps maps, const __grid_consta
     }
 
     tc_fence_before();
-    __syncthreads();
-    if (warp == 1) tmem_dealloc(tmem, 512);
+    cluster_sync();                                 // the pair's MMAs and both epilogues are done with TMEM
+    if (warp == 1) tmem_dealloc_pair(tmem, 512);
 }
 
 std::once_flag g_proj_attr_once[64];
@@ -398,7 +427,7 @@ int run_proj(const void* x, int B, int T, int D, const gdn_proj_out_seg* segs, i
     {
         uint64_t dims[3] = {static_cast<uint64_t>(D), static_cast<uint64_t>(T), static_cast<uint64_t>(B)};
         uint64_t strides[2] = {static_cast<uint64_t>(D) * 2, static_cast<uint64_t>(D) * 2 * T};
-        uint32_t box[3] = {PK, PN, 1};
+        uint32_t box[3] = {PK, PNH, 1};
         if ((st = make_map_bf16(&mx, x, 3, dims, strides, box, true)) != GDN_OK) return st;
     }
     ProjArgs a;
@@ -433,10 +462,11 @@ int run_proj(const void* x, int B, int T, int D, const gdn_proj_out_seg* segs, i
     }
     a.n_ct = ct;
     a.n_tt = (T + POUT - 1) / POUT;
-    const long ntiles = static_cast<long>(a.n_ct) * a.n_tt * B;
+    const long ntiles = static_cast<long>((a.n_ct + 1) / 2) * a.n_tt * B;    // pair tiles (256 channels)
     if (ntiles > 0x7fffffffL) return fail(GDN_ERR_SHAPE, "gdn_proj_conv_silu_fwd: too many tiles");
     a.ntiles = static_cast<int>(ntiles);
-    const int grid = static_cast<int>(ntiles < g_sm_count[dev & 63] ? ntiles : g_sm_count[dev & 63]);
+    const long pairs = g_sm_count[dev & 63] / 2;
+    const int grid = 2 * static_cast<int>(ntiles < pairs ? ntiles : pairs);
     proj_conv_silu_kernel<<<grid, kProjThreads, PROJ_SMEM, static_cast<cudaStream_t>(stream)>>>(maps, mx, a);
     return launch_status("gdn_proj_conv_silu_fwd");
 }

@@ -84,7 +84,7 @@ rmsnorm_kernel(const void* __restrict__ xv, const uint16_t* __restrict__ z,
                 float zf[8];
                 unpack8(__ldcg(reinterpret_cast<const uint4*>(z + row * D) + ch), zf);
 #pragma unroll
-                for (int i = 0; i < 8; ++i) o[i] = (f[i] * r) * gf[i] * silu_f(zf[i]);
+                for (int i = 0; i < 8; ++i) o[i] = (f[i] * r) * gf[i] * silu_fast(zf[i]);
             } else {
 #pragma unroll
                 for (int i = 0; i < 8; ++i) o[i] = (f[i] * r) * gf[i];
@@ -95,55 +95,51 @@ rmsnorm_kernel(const void* __restrict__ xv, const uint16_t* __restrict__ z,
 }
 
 // Rows of at most 16 chunks (D <= 128, e.g. the gated norm over one head's dv):
-// a warp normalises 32/LPR rows at once, LPR lanes per row, and walks the rows
-// grid-stride, so no lane idles and a CTA does more than one row each.  Same
-// arithmetic and summation tree as rmsnorm_kernel (whose idle lanes add zeros).
+// a warp normalises 32/LPR rows, LPR lanes per row, one 16-byte chunk per lane,
+// so no lane idles.  One warp per row group and no loop: a lane issues its x and z
+// loads at once and holds few registers, so an SM keeps its full complement of
+// warps (and their loads) in flight.  Same arithmetic and summation tree as
+// rmsnorm_kernel (whose idle lanes add zeros).
 template <int LPR, bool GATED, bool XF32>
 __global__ void __launch_bounds__(32 * kRowsPerBlock)
 rmsnorm_small_kernel(const void* __restrict__ xv, const uint16_t* __restrict__ z,
                      const uint16_t* __restrict__ gamma, uint16_t* __restrict__ y, int R, int D, float eps) {
     pdl_launch_dependents();
     pdl_wait_prior();
-    constexpr int RPW = 32 / LPR;                  // rows per warp and iteration
+    constexpr int RPW = 32 / LPR;                  // rows per warp
     const int lane = threadIdx.x & 31, sub = lane / LPR, ch = lane % LPR;
-    const long warp_g = static_cast<long>(blockIdx.x) * kRowsPerBlock + (threadIdx.x >> 5);
-    const long stride = static_cast<long>(gridDim.x) * kRowsPerBlock * RPW;
-    const int nchunk = D >> 3;
-    const bool lane_on = ch < nchunk;
-    float gf[8];
-    if (lane_on) unpack8(__ldg(reinterpret_cast<const uint4*>(gamma) + ch), gf);
-    for (long row = warp_g * RPW + sub; row - sub < R; row += stride) {
-        const bool on = lane_on && row < R;
-        float f[8];
-        float ss = 0.f;
-        if (on) {
-            if constexpr (XF32) {
-                const float4* p = reinterpret_cast<const float4*>(static_cast<const float*>(xv) + row * D) + 2 * ch;
-                const float4 u0 = __ldcg(p), u1 = __ldcg(p + 1);
-                f[0] = u0.x; f[1] = u0.y; f[2] = u0.z; f[3] = u0.w;
-                f[4] = u1.x; f[5] = u1.y; f[6] = u1.z; f[7] = u1.w;
-            } else {
-                unpack8(__ldcg(reinterpret_cast<const uint4*>(static_cast<const uint16_t*>(xv) + row * D) + ch), f);
-            }
-#pragma unroll
-            for (int i = 0; i < 8; ++i) ss += f[i] * f[i];
+    const long row = (static_cast<long>(blockIdx.x) * kRowsPerBlock + (threadIdx.x >> 5)) * RPW + sub;
+    const bool on = ch < (D >> 3) && row < R;
+    float f[8], zf[8];
+    float ss = 0.f;
+    if (on) {
+        if constexpr (XF32) {
+            const float4* p = reinterpret_cast<const float4*>(static_cast<const float*>(xv) + row * D) + 2 * ch;
+            const float4 u0 = __ldcg(p), u1 = __ldcg(p + 1);
+            f[0] = u0.x; f[1] = u0.y; f[2] = u0.z; f[3] = u0.w;
+            f[4] = u1.x; f[5] = u1.y; f[6] = u1.z; f[7] = u1.w;
+        } else {
+            unpack8(__ldcg(reinterpret_cast<const uint4*>(static_cast<const uint16_t*>(xv) + row * D) + ch), f);
         }
+        if constexpr (GATED) unpack8(__ldcg(reinterpret_cast<const uint4*>(z + row * D) + ch), zf);
 #pragma unroll
-        for (int o = LPR / 2; o > 0; o >>= 1) ss += __shfl_xor_sync(0xffffffffu, ss, o);
-        const float r = rsqrtf(ss / static_cast<float>(D) + eps);
-        if (on) {
-            float o[8];
-            if constexpr (GATED) {
-                float zf[8];
-                unpack8(__ldcg(reinterpret_cast<const uint4*>(z + row * D) + ch), zf);
+        for (int i = 0; i < 8; ++i) ss += f[i] * f[i];
+    }
 #pragma unroll
-                for (int i = 0; i < 8; ++i) o[i] = (f[i] * r) * gf[i] * silu_f(zf[i]);
-            } else {
+    for (int o = LPR / 2; o > 0; o >>= 1) ss += __shfl_xor_sync(0xffffffffu, ss, o);
+    const float r = rsqrtf(ss / static_cast<float>(D) + eps);
+    if (on) {
+        float gf[8];
+        unpack8(__ldg(reinterpret_cast<const uint4*>(gamma) + ch), gf);
+        float o[8];
+        if constexpr (GATED) {
 #pragma unroll
-                for (int i = 0; i < 8; ++i) o[i] = (f[i] * r) * gf[i];
-            }
-            __stcs(reinterpret_cast<uint4*>(y + row * D) + ch, pack8(o));
+            for (int i = 0; i < 8; ++i) o[i] = (f[i] * r) * gf[i] * silu_fast(zf[i]);
+        } else {
+#pragma unroll
+            for (int i = 0; i < 8; ++i) o[i] = (f[i] * r) * gf[i];
         }
+        __stcs(reinterpret_cast<uint4*>(y + row * D) + ch, pack8(o));
     }
 }
 
@@ -168,9 +164,8 @@ int launch_rmsnorm(const void* x, const void* z, const void* gamma, void* y, int
     if (D <= 128) {                                 // small rows: several per warp, grid-stride
         const int lpr = D <= 64 ? 8 : 16;
         const long groups = (static_cast<long>(R) * lpr + 32 * kRowsPerBlock - 1) / (32 * kRowsPerBlock);
-        int dev = 0, sms = 148;
-        if (cudaGetDevice(&dev) == cudaSuccess) cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
-        cfg.gridDim = dim3(static_cast<unsigned>(groups < 8L * sms ? groups : 8L * sms));
+        if (groups > 0x7fffffffL) return fail(GDN_ERR_SHAPE, "%s: R=%d too large", name, R);
+        cfg.gridDim = dim3(static_cast<unsigned>(groups));
         const cudaError_t e = lpr == 8 ? cudaLaunchKernelEx(&cfg, rmsnorm_small_kernel<8, GATED, XF32>, x, zz, gg, yy, R, D, eps)
                                        : cudaLaunchKernelEx(&cfg, rmsnorm_small_kernel<16, GATED, XF32>, x, zz, gg, yy, R, D, eps);
         if (e != cudaSuccess) return fail(GDN_ERR_CUDA, "%s: launch failed: %s", name, cudaGetErrorString(e));
