@@ -22,7 +22,7 @@
 //    parallel (persistent CTAs, 3 per SM).  Gates, [Q;K] K^T on tensor cores,
 //    P and N, the 64x64 inverse, A1 = A diag(beta'), A2 = A diag(beta' e^Lambda),
 //    W^T = K^T A2^T on tensor cores.  It writes one chunk record to a workspace:
-//    A1 and W^T as bf16 hi/lo pairs, P in bf16, and the gate vectors the
+//    A1 as bf16 hi/lo pairs, W in tf32, P in bf16, and the gate vectors the
 //    recurrence needs -- each operand already in the 128-byte-swizzled shared
 //    memory image the second kernel's MMAs read, so it is fetched with one
 //    bulk copy.
@@ -30,23 +30,24 @@
 //    tile) walks the chunks in order.  The fp32 state lives in TMEM,
 //    TRANSPOSED (S^T: value index = TMEM lane, so the value tile is the
 //    M = 128 dimension of every product), for the whole sequence.  Per chunk:
-//      U^T   = V^T A1^T                          (A, B from shared memory; hi|lo as one N=128 MMA)
-//      S^T  -> bf16 hi/lo, kept in TMEM          (CUDA cores, TMEM -> TMEM)
-//      dV^T  = U^T - S^T W^T                     (A = S^T hi/lo from TMEM: S_hi [W_hi|W_lo] as one
-//                                                 N=128 MMA, then S_lo W_hi; halves summed on CUDA cores)
-//      (Q S_hi)^T                                (A from TMEM)
-//      dV^T -> bf16 and dV'^T = dV^T diag(e^{Lambda_last - Lambda}) hi/lo, in TMEM
-//      S^T   = gamma S^T + dV'^T K               (A from TMEM, K as MN-major B)
-//      (P dV)^T                                  (A from TMEM)
-//      o     = oc * (Q S) + P dV -> bf16 tile -> TMA store
-//    with warp roles: warp 0 TMA/bulk producer, warp 1 MMA issuer, warps 2-9
-//    the state path (each TMEM lane quadrant twice, one half of the columns
-//    each), warps 10-13 the output tile.  Only the state path's CUDA-core work
-//    and its MMAs sit on the sequential critical path.
+//      [U_l^T | U_h^T] = V^T [A1_lo^T | A1_hi^T]   (A, B from shared memory; one N=128 MMA per K step)
+//      [U_h^T | O^T] -= S^T [W^T | -Q~^T]          (tf32: A = the fp32 state straight from TMEM,
+//                                                   B = W from the record and -oc Q built in place)
+//      dV^T = U_l^T + U_h^T -> bf16 and dV'^T = dV^T diag(e^{Lambda_last - Lambda}) -> hi/lo, in TMEM;
+//      S^T <- gamma S^T in place                  (CUDA cores, TMEM -> TMEM)
+//      S^T  += dV'^T K                             (A from TMEM, K as MN-major B)
+//      O^T  += dV^T P^T                            (A from TMEM)
+//      o     = O -> bf16 tile -> TMA store
+//    with warp roles: warp 0 the copies, warp 1 the MMA issuer, warps 2-9 the
+//    state path (each TMEM lane quadrant twice, one token half each) and the
+//    output tile, warps 10-13 the -oc Q image.  Only the state path's
+//    CUDA-core work and the [W | Q~] S and update MMAs sit on the sequential
+//    critical path; the chunk buffers in TMEM are double-buffered so P dV of
+//    one chunk and U of the next run in the tensor pipe meanwhile.
 //
-// fp32 values feeding the state path (S, W, A diag beta', dV') are split into
-// bf16 hi + lo pairs (~16 mantissa bits per product); q/k/v are exact bf16
-// inputs; the output path (Q S_hi, P dV) uses single bf16.  Decay ratios
+// Precision: A diag(beta') and dV' enter their products as bf16 hi + lo pairs
+// (~16 mantissa bits), W S runs in tf32 straight from the fp32 state (fp32
+// accumulation), q/k/v are exact bf16 inputs, P dV uses single bf16 (o is bf16).  Decay ratios
 // exp(Lambda_t - Lambda_s) are formed as u_t * w_s with u_t = 2^(l_t - m),
 // w_s = 2^(m - l_s) around the chunk's mid decay m (never gamma_t / gamma_s);
 // chunks whose total decay could overflow that product fall back to one exp2
@@ -66,7 +67,8 @@ constexpr int kC = 64;                 // chunk length
 // schedule's prep workers leave unset, or -1.
 static __device__ long long g_unpublished_record = -1;
 constexpr int BAR_PREP = 1;            // named barrier of the prep kernel's 128 threads
-constexpr int BAR_OUT = 2;             // named barrier of the chain kernel's output warps
+constexpr int BAR_OUT = 2;             // named barrier of the chain kernel's Q~ warps
+constexpr int BAR_STATE = 3;           // named barrier of the chain kernel's state-path warps
 
 // ---------------------------------------------------------------------------
 // Chunk record (bytes, 1024-aligned images), written by the gate and prep kernels:
@@ -173,39 +175,48 @@ constexpr int kChainThreads = 448;     // 14 warps
 constexpr int kChainTmemCols = 512;
 // TMEM columns (128 lanes; lane j = value column of the tile):
 constexpr uint32_t C_X = 0;            // S^T fp32 (DK columns): A operand of [W | Q~] S (tf32)
-constexpr uint32_t C_UL = 128;         // U_l^T = V^T A1_lo^T (64 token columns)
-constexpr uint32_t C_UH = 192;         // U_h^T = V^T A1_hi^T, then - (W S)^T: U_l + U_h = dV^T
-constexpr uint32_t C_O = 256;          // O^T: + (Q~ S)^T in the same MMAs as W S, + (P dV)^T; zeroed after read
-constexpr uint32_t C_DVH = 320;        // dV'^T hi/lo bf16 pairs: token half g, hi at 32g, lo at 32g + 16
-constexpr uint32_t C_DVB = 384;        // dV^T bf16 pairs (32 columns): A operand of dV^T P^T
+constexpr uint32_t C_BUF = 128;        // two chunk buffers of 192 columns, buffer c & 1 for chunk c:
+                                       //   +0   U_l^T = V^T A1_lo^T (64 token columns); after the state-path
+                                       //        pass: dV^T bf16 pairs, token half g at 32g (16 columns)
+                                       //   +64  U_h^T = V^T A1_hi^T, then - (W S)^T: U_l + U_h = dV^T; after the
+                                       //        state-path pass: dV'^T hi/lo pairs, half g hi at 32g, lo at 32g + 16
+                                       //   +128 O^T: (Q~ S)^T in the same MMAs as W S, + (P dV)^T; zeroed after read
+constexpr uint32_t C_BUF_STRIDE = 192;
+static_assert(C_BUF + 2 * C_BUF_STRIDE <= kChainTmemCols, "chain TMEM map exceeds 512 columns");
 
 template <int DK>
 struct ChainSmem {
     static constexpr int CB = DK / 64;      // 64-column bf16 blocks of the q/k tiles
-    // one slot per chunk: K tile (TMA; MN-major B of the state update), q tile (TMA; read
-    // once to build Q~), then from the record P and the gates
-    static constexpr int K_OFF = 0;
-    static constexpr int Q_OFF = CB * 8192;
-    static constexpr int P_OFF = 2 * CB * 8192;
-    static constexpr int G_OFF = P_OFF + 8192;
-    static constexpr int SLOT_BYTES = G_OFF + 1024;
+    // q/k ring, 2 slots: K tile (TMA; MN-major B of the state update) and q tile (TMA; read once
+    // to build Q~); a slot is refilled once the state update and the Q~ build have read it
+    static constexpr int KQ_K = 0;
+    static constexpr int KQ_Q = CB * 8192;
+    static constexpr int KQ_BYTES = 2 * CB * 8192;
+    static constexpr int OFF_KQ = 0;
+    // record ring, 3 slots: P (K-major B of dV^T P^T) and the chunk's gate floats, as they lie
+    // in the record; P dV of chunk c is issued during chunk c + 1, so this ring is one deeper
+    static constexpr int PG_P = 0;
+    static constexpr int PG_G = 8192;
+    static constexpr int PG_BYTES = 8192 + 1024;
+    static constexpr int OFF_PG = 2 * KQ_BYTES;
     // [W | -Q~] image of the current chunk, K-major tf32: key block kb (32 keys) at kb * 16 KB,
     // rows 0-63 W (bulk-copied from the record), rows 64-127 -oc Q (built by the output warps)
-    static constexpr int OFF_IMG = 2 * SLOT_BYTES;
+    static constexpr int OFF_IMG = OFF_PG + 3 * PG_BYTES;
     static constexpr int OFF_V = OFF_IMG + DK * 512;       // v tile, 2 blocks of 64 columns
     static constexpr int OFF_A1 = OFF_V + 16384;           // A1 lo | hi
     static constexpr int OFF_O = OFF_A1 + 16384;           // output staging, 2 x (2 blocks x 8 KB)
     static constexpr int OFF_BAR = OFF_O + 32768;
     static constexpr int BYTES = OFF_BAR + 256;
     static constexpr int ALLOC = BYTES + 1024;
-    static_assert(SLOT_BYTES % 1024 == 0, "slot images must stay 1024-aligned");
+    static_assert(KQ_BYTES % 1024 == 0 && PG_BYTES % 1024 == 0, "slot images must stay 1024-aligned");
     static_assert(ALLOC <= 232448, "chain kernel shared memory exceeds 227 KB");
 };
 
 struct ChainBars {
-    uint64_t slot_full[2], slot_free[2], va_full, va_free, w_full;
+    uint64_t kq_full[2], kq_free[2], pg_full[3], pg_free[3], va_full, va_free, w_full;
     uint64_t ws_done, dv_done, st_done, pdv_done, qt_ready, o_free, init_done, mma_drain;
 };
+static_assert(sizeof(ChainBars) + 8 <= 256, "chain barriers exceed their shared-memory block");
 
 struct ChainArgs {
     const uint8_t* rec;
@@ -237,21 +248,12 @@ __device__ __forceinline__ uint32_t ld_relaxed_u32(const unsigned int* flag) {
     asm volatile("ld.relaxed.gpu.global.u32 %0, [%1];" : "=r"(v) : "l"(flag) : "memory");
     return v;
 }
-// Bounded wait for a record flag (the wait budget, then DERR_TIMEOUT and the CTA's abort flag).
-__device__ __forceinline__ bool wait_record(const unsigned int* flag, unsigned int* err, volatile int* abort) {
-    const long long t0 = clock64(), budget = wait_budget();
-    for (;;) {
-        uint32_t v;
-        asm volatile("ld.acquire.gpu.global.u32 %0, [%1];" : "=r"(v) : "l"(flag) : "memory");
-        if (v != 0) break;
-        if (*abort) return false;
-        if (clock64() - t0 > budget) {
-            if (err) atomicOr(err, DERR_TIMEOUT);
-            *abort = 1;
-            return false;
-        }
-        __nanosleep(100);
-    }
+// Non-blocking check of a record flag: true (with the async-proxy fence taken) once it is set;
+// the caller bounds how long it keeps polling.
+__device__ __forceinline__ bool record_ready(const unsigned int* flag) {
+    uint32_t v;
+    asm volatile("ld.acquire.gpu.global.u32 %0, [%1];" : "=r"(v) : "l"(flag) : "memory");
+    if (v == 0) return false;
     asm volatile("fence.proxy.async.global;" ::: "memory");
     return true;
 }
@@ -845,15 +847,19 @@ prefill_prep_kernel(const __grid_constant__ CUtensorMap map_q, const __grid_cons
 // ===========================================================================
 // One chain CTA (all 448 threads), working on (b, h, value tile) number `cta`.
 //
-// Per chunk c (S^T in TMEM, lane j = value column):
-//   [U_l^T | U_h^T] = V^T [A1_lo^T | A1_hi^T]           4 bf16 MMAs (N = 128)
-//   [U_h^T | O^T] -= S^T [W^T | -Q~^T]                  16 tf32 MMAs (N = 128), A = the fp32
+// Per chunk c (S^T in TMEM, lane j = value column; buffer c & 1 of [U | O]):
+//   U^T  = V^T A1_lo^T + V^T A1_hi^T                    8 bf16 MMAs (N = 64), issued one chunk ahead
+//   [U^T | O^T] -= S^T [W^T | -Q~^T]                    DK/8 tf32 MMAs (N = 128), A = the fp32
 //                                                       state straight from TMEM, B = [W | -oc Q]
-//   state path: dV = U_l + U_h -> bf16 and dV' = dV e^{Lambda_last - Lambda} -> hi/lo;
+//   state path: dV = U -> bf16 and dV' = dV e^{Lambda_last - Lambda} -> hi/lo;
 //               S <- gamma_c S in place
 //   S^T += dV'^T K                                      8 bf16 MMAs (hi and lo)
-//   O^T += dV^T P^T;  o = O -> bf16 -> TMA store, O zeroed for the next chunk
-// The critical path per chunk is [W | Q~] S -> state-path pass -> state update.
+//   O^T += dV^T P^T                                     4 bf16 MMAs, issued after the next
+//                                                       chunk's [W | Q~] S; o = O -> bf16 -> TMA store
+// The critical path per chunk is [W | Q~] S -> state-path pass -> state update -> the next
+// [W | Q~] S; P dV of the previous chunk and U of the next one fill the tensor pipe while
+// the state path works, which is why U, O and the bf16 dV are double-buffered in TMEM.
+// Barrier arrivals from a group of warps are one per warp (after __syncwarp).
 template <int DK>
 __device__ __forceinline__ void chain_body(const CUtensorMap* map_q, const CUtensorMap* map_k,
                                            const CUtensorMap* map_v, const CUtensorMap* map_o, const ChainArgs& args,
@@ -886,22 +892,27 @@ __device__ __forceinline__ void chain_body(const CUtensorMap* map_q, const CUten
     unsigned int* err = args.err;
     const int c0 = args.c0;
     const uint8_t* rec0 = args.rec + (static_cast<long>(bh) * args.nchunks_total + c0) * R::BYTES;
+    const unsigned int* flags = args.ready ? args.ready + static_cast<long>(bh) * args.nchunks_total + c0 : nullptr;
 
     if (tid == 0) {
-        mbar_init(&bars->slot_full[0], 1);
-        mbar_init(&bars->slot_full[1], 1);
-        mbar_init(&bars->slot_free[0], 2);         // MMA commit + output warps (gates read)
-        mbar_init(&bars->slot_free[1], 2);
+        for (int s = 0; s < 2; ++s) {
+            mbar_init(&bars->kq_full[s], 1);
+            mbar_init(&bars->kq_free[s], 2);       // state-update commit + output warps (q tile read)
+        }
+        for (int s = 0; s < 3; ++s) {
+            mbar_init(&bars->pg_full[s], 1);
+            mbar_init(&bars->pg_free[s], 2);       // P dV commit + output warps (gates read)
+        }
         mbar_init(&bars->va_full, 1);
         mbar_init(&bars->va_free, 1);
         mbar_init(&bars->w_full, 1);
         mbar_init(&bars->ws_done, 1);
-        mbar_init(&bars->dv_done, 256);
+        mbar_init(&bars->dv_done, 8);              // one arrival per state-path warp
         mbar_init(&bars->st_done, 1);
         mbar_init(&bars->pdv_done, 1);
         mbar_init(&bars->qt_ready, 1);
-        mbar_init(&bars->o_free, 128);
-        mbar_init(&bars->init_done, 256);
+        mbar_init(&bars->o_free, 8);               // one arrival per state-path warp (O read and zeroed)
+        mbar_init(&bars->init_done, 8);
         mbar_init(&bars->mma_drain, 1);
         *abort_flag = 0;
         fence_mbar_init();
@@ -918,121 +929,160 @@ __device__ __forceinline__ void chain_body(const CUtensorMap* map_q, const CUten
     __syncthreads();
     tc_fence_after();
     const uint32_t tmem = *tmem_slot;
-    auto gates_of = [&](int c) {
-        return reinterpret_cast<const float*>(sm + (c & 1) * L::SLOT_BYTES + L::G_OFF);
-    };
+    auto kq_of = [&](int c) { return sm + L::OFF_KQ + (c & 1) * L::KQ_BYTES; };
+    auto pg_of = [&](int c) { return sm + L::OFF_PG + (c % 3) * L::PG_BYTES; };
+    auto gates_of = [&](int c) { return reinterpret_cast<const float*>(pg_of(c) + L::PG_G); };
 
     if (warp == 0) {
-        // ======================= producer: lane 0 the per-chunk slot, lane 1 V and A1
-        // each lane waits (bounded) for its last copy to land before the CTA can exit
-        int last = -1;
+        // ======================= producer: one thread drives the four streams of copies, polling
+        // their barriers without blocking (lanes of one warp spinning on different barriers would
+        // take turns); the W rows of the image go first, being on the critical path
         if (lane == 0) {
-            for (int c = 0; c < nchunks; ++c) {
-                const int slot = c & 1;
-                if (c >= 2 && !mbar_wait_or_abort(&bars->slot_free[slot], ((c >> 1) - 1) & 1, err, abort_flag)) break;
-                uint8_t* dst = sm + slot * L::SLOT_BYTES;
-                const uint8_t* rec = rec0 + static_cast<long>(c) * R::BYTES;
-                if (args.ready &&
-                    !wait_record(args.ready + static_cast<long>(bh) * args.nchunks_total + c0 + c, err, abort_flag))
-                    break;
-                mbar_arrive_expect_tx(&bars->slot_full[slot], 2 * L::CB * 8192 + 8192 + 1024);
+            uint8_t* img = sm + L::OFF_IMG;
+            int nw = 0, nkq = 0, npg = 0, nva = 0;      // next chunk of each stream
+            const long long budget = wait_budget();
+            long long t_moved = clock64();
+            while ((nw < nchunks || nkq < nchunks || npg < nchunks || nva < nchunks) && !*abort_flag) {
+                bool moved = false;
+                // W rows of the image: chunk nw once [W | Q~] S of chunk nw - 1 has read it
+                if (nw < nchunks && (nw == 0 || mbar_test_wait(&bars->ws_done, (nw - 1) & 1)) &&
+                    (!flags || record_ready(flags + nw))) {
+                    const uint8_t* rec = rec0 + static_cast<long>(nw) * R::BYTES;
+                    mbar_arrive_expect_tx(&bars->w_full, DK * 256);
 #pragma unroll
-                for (int cb = 0; cb < L::CB; ++cb) {
-                    tma_load_4d(dst + L::Q_OFF + cb * 8192, map_q, &bars->slot_full[slot], cb * 64,
-                                trow0 + (c0 + c) * kC, hq, bco);
-                    tma_load_4d(dst + L::K_OFF + cb * 8192, map_k, &bars->slot_full[slot], cb * 64,
-                                trow0 + (c0 + c) * kC, hq, bco);
+                    for (int kb = 0; kb < DK / 32; ++kb)
+                        bulk_load(img + kb * 16384, rec + R::W + kb * 8192, 8192, &bars->w_full);
+                    // the next chunk's W waits for this chunk's product: bring it into L2 now
+                    if (nw + 1 < nchunks && (!flags || ld_relaxed_u32(flags + nw + 1)))
+                        bulk_prefetch_l2(rec + R::BYTES + R::W, DK * 256);
+                    ++nw;
+                    moved = true;
                 }
-                bulk_load(dst + L::P_OFF, rec + R::P, 8192 + 1024, &bars->slot_full[slot]);
-                last = c;
+                // q/k ring (inputs, no record): chunk nkq into slot nkq & 1
+                if (nkq < nchunks && (nkq < 2 || mbar_test_wait(&bars->kq_free[nkq & 1], ((nkq >> 1) - 1) & 1))) {
+                    const int s = nkq & 1;
+                    uint8_t* dst = kq_of(nkq);
+                    mbar_arrive_expect_tx(&bars->kq_full[s], L::KQ_BYTES);
+#pragma unroll
+                    for (int cb = 0; cb < L::CB; ++cb) {
+                        tma_load_4d(dst + L::KQ_Q + cb * 8192, map_q, &bars->kq_full[s], cb * 64,
+                                    trow0 + (c0 + nkq) * kC, hq, bco);
+                        tma_load_4d(dst + L::KQ_K + cb * 8192, map_k, &bars->kq_full[s], cb * 64,
+                                    trow0 + (c0 + nkq) * kC, hq, bco);
+                    }
+                    ++nkq;
+                    moved = true;
+                }
+                // P | gates ring: chunk npg into slot npg % 3
+                if (npg < nchunks && (npg < 3 || mbar_test_wait(&bars->pg_free[npg % 3], ((npg / 3) - 1) & 1)) &&
+                    (!flags || record_ready(flags + npg))) {
+                    mbar_arrive_expect_tx(&bars->pg_full[npg % 3], L::PG_BYTES);
+                    bulk_load(pg_of(npg), rec0 + static_cast<long>(npg) * R::BYTES + R::P, L::PG_BYTES,
+                              &bars->pg_full[npg % 3]);
+                    ++npg;
+                    moved = true;
+                }
+                // V tile and A1 (single buffer): chunk nva once U of chunk nva - 1 has read them
+                if (nva < nchunks && (nva == 0 || mbar_test_wait(&bars->va_free, (nva - 1) & 1)) &&
+                    (!flags || record_ready(flags + nva))) {
+                    mbar_arrive_expect_tx(&bars->va_full, nvb * 8192 + 16384);
+                    for (int vb = 0; vb < nvb; ++vb)
+                        tma_load_4d(sm + L::OFF_V + vb * 8192, map_v, &bars->va_full, v0 + vb * 64,
+                                    trow0 + (c0 + nva) * kC, h, bco);
+                    bulk_load(sm + L::OFF_A1, rec0 + static_cast<long>(nva) * R::BYTES + R::A1, 16384, &bars->va_full);
+                    ++nva;
+                    moved = true;
+                }
+                if (moved) {
+                    t_moved = clock64();
+                } else if (clock64() - t_moved > budget) {
+                    atomicOr(err, DERR_TIMEOUT);
+                    *abort_flag = 1;
+                }
             }
-            if (last >= 0) mbar_wait(&bars->slot_full[last & 1], (last >> 1) & 1, err);
-        } else if (lane == 1) {
-            for (int c = 0; c < nchunks; ++c) {
-                if (c >= 1 && !mbar_wait_or_abort(&bars->va_free, (c - 1) & 1, err, abort_flag)) break;
-                if (args.ready &&
-                    !wait_record(args.ready + static_cast<long>(bh) * args.nchunks_total + c0 + c, err, abort_flag))
-                    break;
-                mbar_arrive_expect_tx(&bars->va_full, nvb * 8192 + 16384);
-                for (int vb = 0; vb < nvb; ++vb)
-                    tma_load_4d(sm + L::OFF_V + vb * 8192, map_v, &bars->va_full, v0 + vb * 64, trow0 + (c0 + c) * kC, h,
-                                bco);
-                bulk_load(sm + L::OFF_A1, rec0 + static_cast<long>(c) * R::BYTES + R::A1, 16384, &bars->va_full);
-                last = c;
-            }
-            if (last >= 0) mbar_wait(&bars->va_full, last & 1, err);
+            // every copy issued lands before the CTA can exit (bounded waits)
+            if (nw > 0) mbar_wait(&bars->w_full, (nw - 1) & 1, err);
+            for (int c = max(nkq - 2, 0); c < nkq; ++c) mbar_wait(&bars->kq_full[c & 1], (c >> 1) & 1, err);
+            for (int c = max(npg - 3, 0); c < npg; ++c) mbar_wait(&bars->pg_full[c % 3], (c / 3) & 1, err);
+            if (nva > 0) mbar_wait(&bars->va_full, (nva - 1) & 1, err);
         }
     } else if (warp == 1) {
         // ======================= MMA issuer (one thread)
         if (lane == 0) {
             const uint32_t sv = smem_u32(sm + L::OFF_V);
             const uint32_t sa1 = smem_u32(sm + L::OFF_A1);
-            // [U_l^T | U_h^T] = V^T [A1_lo^T | A1_hi^T]: V as MN-major A, A1 lo | hi as one K-major B
-            auto issue_u = [&]() {
+            const uint32_t simg = smem_u32(sm + L::OFF_IMG);
+            // [U_l^T | U_h^T] of chunk c = V^T [A1_lo^T | A1_hi^T] into buffer c & 1: V as MN-major A,
+            // the two A1 parts as one 128-row K-major B
+            auto issue_u = [&](int c) {
+                const bool ok = mbar_spin_or_abort(&bars->va_full, c & 1, err, abort_flag);
+                tc_fence_after();
+                if (!ok || *abort_flag) return;
                 constexpr uint32_t id_u = idesc_bf16(128, 128, true, false);
 #pragma unroll
                 for (int kk = 0; kk < 4; ++kk)
-                    umma_bf16_ss(tmem + C_UL, sdesc_sw128(sv + kk * 2048, 8192, 1024),
+                    umma_bf16_ss(tmem + C_BUF + (c & 1) * C_BUF_STRIDE, sdesc_sw128(sv + kk * 2048, 8192, 1024),
                                  sdesc_sw128(sa1 + kk * 32, 16, 1024), id_u, kk > 0 ? 1u : 0u);
                 umma_commit(&bars->va_free);
             };
-            if (mbar_spin_or_abort(&bars->va_full, 0, err, abort_flag) && !*abort_flag) {
+            // O^T += dV^T P^T of chunk c into the O columns of buffer c & 1; frees its P | gates slot
+            auto issue_pdv = [&](int c) {
+                const bool ok = mbar_spin_or_abort(&bars->pg_full[c % 3], (c / 3) & 1, err, abort_flag);
                 tc_fence_after();
-                issue_u();
-            }
+                if (!ok || *abort_flag) return;
+                constexpr uint32_t id64 = idesc_bf16(128, 64, false, false);
+                const uint32_t sp = smem_u32(pg_of(c) + L::PG_P);
+#pragma unroll
+                for (int kk = 0; kk < 4; ++kk)
+                    umma_bf16_ts(tmem + C_BUF + (c & 1) * C_BUF_STRIDE + 128,
+                                 tmem + C_BUF + (c & 1) * C_BUF_STRIDE + (kk >> 1) * 32 + (kk & 1) * 8,
+                                 sdesc_sw128(sp + kk * 32, 16, 1024), id64, 1u);
+                umma_commit(&bars->pdv_done);
+                umma_commit(&bars->pg_free[c % 3]);
+            };
+            if (nchunks > 0) issue_u(0);
             mbar_spin_or_abort(&bars->init_done, 0, err, abort_flag);
-            const uint32_t simg = smem_u32(sm + L::OFF_IMG);
 #pragma unroll 1
             for (int c = 0; c < nchunks; ++c) {
-                const int slot = c & 1;
-                const uint32_t sbase = smem_u32(sm + slot * L::SLOT_BYTES);
                 mbar_spin_or_abort(&bars->w_full, c & 1, err, abort_flag);
                 mbar_spin_or_abort(&bars->qt_ready, c & 1, err, abort_flag);
-                if (c >= 1) {
-                    mbar_spin_or_abort(&bars->st_done, (c - 1) & 1, err, abort_flag);
-                    mbar_spin_or_abort(&bars->o_free, (c - 1) & 1, err, abort_flag);
-                }
+                if (c >= 1) mbar_spin_or_abort(&bars->st_done, (c - 1) & 1, err, abort_flag);
+                if (c >= 2) mbar_spin_or_abort(&bars->o_free, c & 1, err, abort_flag);   // O of chunk c - 2 read
                 tc_fence_after();
                 if (!*abort_flag) {
-                    // [U_h^T | O^T] -= S^T [W^T | -Q~^T]: tf32, A = the fp32 state, B negated
+                    // [U^T | O^T] -= S^T [W^T | -Q~^T]: tf32, A = the fp32 state, B negated
                     constexpr uint32_t id_w = idesc_tf32(128, 128, false, false) | (1u << 14);
 #pragma unroll
                     for (int kk = 0; kk < DK / 8; ++kk)
-                        umma_tf32_ts(tmem + C_UH, tmem + C_X + 8 * kk,
+                        umma_tf32_ts(tmem + C_BUF + (c & 1) * C_BUF_STRIDE + 64, tmem + C_X + 8 * kk,
                                      sdesc_sw128(simg + (kk >> 2) * 16384 + (kk & 3) * 32, 16, 1024), id_w, 1u);
                     umma_commit(&bars->ws_done);
                 }
+                // the tensor pipe is idle while the state path works: P dV of the previous chunk and
+                // U of the next one go here
+                if (c >= 1) issue_pdv(c - 1);
+                if (c + 1 < nchunks) issue_u(c + 1);
                 mbar_spin_or_abort(&bars->dv_done, c & 1, err, abort_flag);
-                mbar_spin_or_abort(&bars->slot_full[slot], (c >> 1) & 1, err, abort_flag);
+                mbar_spin_or_abort(&bars->kq_full[c & 1], (c >> 1) & 1, err, abort_flag);
                 tc_fence_after();
                 if (!*abort_flag) {
                     // S^T = gamma_c S^T (scaled in place by the state path) + dV'^T K, K as MN-major B;
-                    // dV' hi/lo per 32-token half in C_DVH
+                    // dV' hi/lo per 32-token half over U_h of buffer c & 1
                     constexpr uint32_t idst = idesc_bf16(128, DK, false, true);
+                    const uint32_t dvh = tmem + C_BUF + (c & 1) * C_BUF_STRIDE + 64;
+                    const uint32_t sk = smem_u32(kq_of(c) + L::KQ_K);
 #pragma unroll
                     for (int p = 0; p < 2; ++p) {
 #pragma unroll
                         for (int kk = 0; kk < 4; ++kk)
-                            umma_bf16_ts(tmem + C_X, tmem + C_DVH + (kk >> 1) * 32 + p * 16 + (kk & 1) * 8,
-                                         sdesc_sw128(sbase + L::K_OFF + kk * 2048, 8192, 1024), idst, 1u);
+                            umma_bf16_ts(tmem + C_X, dvh + (kk >> 1) * 32 + p * 16 + (kk & 1) * 8,
+                                         sdesc_sw128(sk + kk * 2048, 8192, 1024), idst, 1u);
                     }
                     umma_commit(&bars->st_done);
-                    // O^T += dV^T P^T
-                    constexpr uint32_t id64 = idesc_bf16(128, 64, false, false);
-#pragma unroll
-                    for (int kk = 0; kk < 4; ++kk)
-                        umma_bf16_ts(tmem + C_O, tmem + C_DVB + kk * 8,
-                                     sdesc_sw128(sbase + L::P_OFF + kk * 32, 16, 1024), id64, 1u);
-                    umma_commit(&bars->pdv_done);
-                    umma_commit(&bars->slot_free[slot]);
-                }
-                if (c + 1 < nchunks) {
-                    // U of the next chunk, whose region the state-path pass has read (dv_done)
-                    const bool ok = mbar_spin_or_abort(&bars->va_full, (c + 1) & 1, err, abort_flag);
-                    tc_fence_after();
-                    if (ok && !*abort_flag) issue_u();
+                    umma_commit(&bars->kq_free[c & 1]);
                 }
             }
+            if (nchunks > 0) issue_pdv(nchunks - 1);
             // every MMA issued has completed before TMEM is released (also after an abort)
             umma_commit(&bars->mma_drain);
             mbar_wait(&bars->mma_drain, 0, err);
@@ -1044,6 +1094,63 @@ __device__ __forceinline__ void chain_body(const CUtensorMap* map_q, const CUten
         const int j = ((warp & 3) << 5) | lane;
         const uint32_t lane_off = static_cast<uint32_t>(warp & 3) << 21;
         const long s_base = static_cast<long>(bh) * DK * args.dv + v0;
+
+        const bool sleader = (ct == 0);
+        // ---- o of chunk cc, tokens [32 grp, 32 grp + 32) of value column j: O^T -> bf16 ->
+        //      staging image -> TMA store; O is zeroed for chunk cc + 2
+        auto store_o = [&](int cc) {
+            mbar_wait_or_abort(&bars->pdv_done, cc & 1, err, abort_flag);
+            tc_fence_after();
+            uint32_t ob2[16];                              // bf16 results, tokens 32 grp + (2i, 2i+1)
+            {
+                const uint32_t ocol = tmem + lane_off + C_BUF + (cc & 1) * C_BUF_STRIDE + 128 + grp * 32;
+                float o[32], z[32];
+                tmem_ld32(ocol, o);
+#pragma unroll
+                for (int i = 0; i < 32; ++i) z[i] = 0.f;
+                tmem_ld_wait();
+                tmem_st32(ocol, z);
+#pragma unroll
+                for (int i = 0; i < 16; ++i) ob2[i] = cvt_bf16x2(o[2 * i], o[2 * i + 1]);
+                tmem_st_wait();
+            }
+            tc_fence_before();
+            __syncwarp();
+            if (lane == 0) mbar_arrive(&bars->o_free);
+            // varlen: a sequence's last chunk is stored row by row, only its own tokens (the
+            // rows past its end belong to the next sequence); coalesced over the 128 columns
+            const int cabs = c0 + cc;
+            const bool tail = args.cu && (cabs + 1) * kC > seq_len;
+            if (tail && j < dv_valid && !*abort_flag) {
+                const int nvalid = seq_len - cabs * kC - 32 * grp;
+                uint16_t* orow = args.out + (static_cast<long>(trow0 + cabs * kC + 32 * grp) * args.Hv + h) * args.dv + v0 + j;
+                const long ostride = static_cast<long>(args.Hv) * args.dv;
+#pragma unroll
+                for (int i = 0; i < 16; ++i) {
+                    if (2 * i < nvalid) orow[(2 * i) * ostride] = static_cast<uint16_t>(ob2[i] & 0xffffu);
+                    if (2 * i + 1 < nvalid) orow[(2 * i + 1) * ostride] = static_cast<uint16_t>(ob2[i] >> 16);
+                }
+            }
+            if (sleader) bulk_wait_read1();                // the store of two chunks ago left this buffer
+            named_bar(BAR_STATE, 256);
+            uint8_t* ob = sm + L::OFF_O + (cc & 1) * 16384 + (j >> 6) * 8192;
+            const uint32_t jj = j & 63;
+#pragma unroll
+            for (int i = 0; i < 16; ++i) {
+                const uint32_t t = 32 * grp + 2 * i;
+                *reinterpret_cast<uint16_t*>(ob + sw128_off(t, jj)) = static_cast<uint16_t>(ob2[i] & 0xffffu);
+                *reinterpret_cast<uint16_t*>(ob + sw128_off(t + 1, jj)) = static_cast<uint16_t>(ob2[i] >> 16);
+            }
+            fence_async_smem();
+            named_bar(BAR_STATE, 256);
+            if (sleader) {
+                if (!*abort_flag && !tail)
+                    for (int vb = 0; vb < nvb; ++vb)
+                        tma_store_4d(map_o, sm + L::OFF_O + (cc & 1) * 16384 + vb * 8192, v0 + vb * 64,
+                                     trow0 + cabs * kC, h, bco);
+                bulk_commit();
+            }
+        };
 
         // initial state -> TMEM (S^T: lane j = value column, column d = key index)
 #pragma unroll
@@ -1059,20 +1166,23 @@ __device__ __forceinline__ void chain_body(const CUtensorMap* map_q, const CUten
         }
         tmem_st_wait();
         tc_fence_before();
-        mbar_arrive(&bars->init_done);
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&bars->init_done);
 
 #pragma unroll 1
         for (int c = 0; c < nchunks; ++c) {
             const float* G = gates_of(c);
-            mbar_wait_or_abort(&bars->slot_full[c & 1], (c >> 1) & 1, err, abort_flag);
+            mbar_wait_or_abort(&bars->pg_full[c % 3], (c / 3) & 1, err, abort_flag);
             mbar_wait_or_abort(&bars->ws_done, c & 1, err, abort_flag);
             tc_fence_after();
-            // ---- dV = U_l + U_h (bf16, for P dV) and dV' = dV e^{Lambda_last - Lambda} (hi/lo),
-            //      tokens [32 grp, 32 grp + 32)
+            const float gamma_c = G[128];
             {
+                // dV = U_l + U_h (bf16, for P dV) and dV' = dV e^{Lambda_last - Lambda} (hi/lo), tokens
+                // [32 grp, 32 grp + 32), written over the U columns this thread has just read
+                const uint32_t buf = tmem + lane_off + C_BUF + (c & 1) * C_BUF_STRIDE;
                 float ul[32], uh[32];
-                tmem_ld32(tmem + lane_off + C_UL + grp * 32, ul);
-                tmem_ld32(tmem + lane_off + C_UH + grp * 32, uh);
+                tmem_ld32(buf + grp * 32, ul);
+                tmem_ld32(buf + 64 + grp * 32, uh);
                 tmem_ld_wait();
                 const float* edec = G + 64 + grp * 32;
                 uint32_t bw[16], hi[16], lo[16];
@@ -1082,12 +1192,11 @@ __device__ __forceinline__ void chain_body(const CUtensorMap* map_q, const CUten
                     bw[i] = cvt_bf16x2(d0, d1);
                     split2_bf16(d0 * edec[2 * i], d1 * edec[2 * i + 1], hi[i], lo[i]);
                 }
-                tmem_st16(tmem + lane_off + C_DVH + grp * 32, hi);
-                tmem_st16(tmem + lane_off + C_DVH + grp * 32 + 16, lo);
-                tmem_st16(tmem + lane_off + C_DVB + grp * 16, bw);
+                tmem_st16(buf + 64 + grp * 32, hi);
+                tmem_st16(buf + 64 + grp * 32 + 16, lo);
+                tmem_st16(buf + grp * 32, bw);
             }
-            // ---- S <- gamma_c S in place, key columns of half grp ([W | Q~] S has read S)
-            const float gamma_c = G[128];
+            // S <- gamma_c S in place, key columns of half grp ([W | Q~] S has read S)
 #pragma unroll
             for (int blk = 0; blk < NBLK; ++blk) {
                 float v[32];
@@ -1099,11 +1208,15 @@ __device__ __forceinline__ void chain_body(const CUtensorMap* map_q, const CUten
             }
             tmem_st_wait();
             tc_fence_before();
-            mbar_arrive(&bars->dv_done);
+            __syncwarp();
+            if (lane == 0) mbar_arrive(&bars->dv_done);
+            // the previous chunk's output while the state update and the next [W | Q~] S run
+            if (c >= 1) store_o(c - 1);
         }
+        if (nchunks > 0) store_o(nchunks - 1);
 
         // ---- final state -> state_out [dk][dv]
-        mbar_wait_or_abort(&bars->st_done, (nchunks - 1) & 1, err, abort_flag);
+        if (nchunks > 0) mbar_wait_or_abort(&bars->st_done, (nchunks - 1) & 1, err, abort_flag);
         tc_fence_after();
         if (!*abort_flag && args.state_out) {
 #pragma unroll
@@ -1118,35 +1231,35 @@ __device__ __forceinline__ void chain_body(const CUtensorMap* map_q, const CUten
                 }
             }
         }
+        if (sleader) bulk_wait_all0();
     } else {
-        // ======================= output warps
+        // ======================= Q~ warps (4): -Q~ = -oc Q of every chunk into the image
         const int ot = tid - 320;
-        const int j = ((warp & 3) << 5) | lane;
-        const uint32_t lane_off = static_cast<uint32_t>(warp & 3) << 21;
         const bool oleader = (ot == 0);
         uint8_t* img = sm + L::OFF_IMG;
-        int w_last = -1;                                   // last chunk whose W copy the leader issued
-        // The image of chunk cc, once [W | Q~] S of chunk cc - 1 has read it: W into rows 0-63
-        // (bulk copies issued by the leader; the record is published, since its slot landed),
-        // -Q~ = -oc Q into rows 64-127 (K-major tf32; the tensor core reads the top 19 bits)
-        auto build_qt = [&](int cc) {
-            const int slot = cc & 1;
-            const uint8_t* qsrc = sm + slot * L::SLOT_BYTES + L::Q_OFF;
-            const float* oc = gates_of(cc);
-            mbar_wait_or_abort(&bars->slot_full[slot], (cc >> 1) & 1, err, abort_flag);
-            if (cc >= 1) mbar_wait_or_abort(&bars->ws_done, (cc - 1) & 1, err, abort_flag);
-            if (oleader && !*abort_flag) {
-                w_last = cc;
-                mbar_arrive_expect_tx(&bars->w_full, DK * 256);
-                const uint8_t* rec = rec0 + static_cast<long>(cc) * R::BYTES + R::W;
+        {
+            // O accumulates from each chunk's [W | Q~] S: both buffers start at zero
+            const uint32_t lane_off = static_cast<uint32_t>(warp & 3) << 21;
+            float z[32];
 #pragma unroll
-                for (int kb = 0; kb < DK / 32; ++kb)
-                    bulk_load(img + kb * 16384, rec + kb * 8192, 8192, &bars->w_full);
-                // the next chunk's W waits for this chunk's product: bring it into L2 now
-                if (cc + 1 < nchunks &&
-                    (!args.ready || ld_relaxed_u32(args.ready + static_cast<long>(bh) * args.nchunks_total + c0 + cc + 1)))
-                    bulk_prefetch_l2(rec + R::BYTES, DK * 256);
+            for (int i = 0; i < 32; ++i) z[i] = 0.f;
+#pragma unroll
+            for (int b = 0; b < 2; ++b) {
+                tmem_st32(tmem + lane_off + C_BUF + b * C_BUF_STRIDE + 128, z);
+                tmem_st32(tmem + lane_off + C_BUF + b * C_BUF_STRIDE + 160, z);
             }
+            tmem_st_wait();
+            tc_fence_before();
+        }
+        // rows 64-127 of the image (K-major tf32; the tensor core reads the top 19 bits) for
+        // chunk cc, once [W | Q~] S of chunk cc - 1 has read them
+#pragma unroll 1
+        for (int cc = 0; cc < nchunks; ++cc) {
+            const uint8_t* qsrc = kq_of(cc) + L::KQ_Q;
+            const float* oc = gates_of(cc);
+            mbar_wait_or_abort(&bars->kq_full[cc & 1], (cc >> 1) & 1, err, abort_flag);
+            mbar_wait_or_abort(&bars->pg_full[cc % 3], (cc / 3) & 1, err, abort_flag);
+            if (cc >= 1) mbar_wait_or_abort(&bars->ws_done, (cc - 1) & 1, err, abort_flag);
             constexpr int CPR = DK / 8;                    // 16-byte bf16 chunks per token row
 #pragma unroll
             for (int task = ot; task < kC * CPR; task += 128) {
@@ -1169,77 +1282,9 @@ __device__ __forceinline__ void chain_body(const CUtensorMap* map_q, const CUten
             named_bar(BAR_OUT, 128);
             if (oleader) {
                 mbar_arrive(&bars->qt_ready);
-                mbar_arrive(&bars->slot_free[slot]);      // the output warps are done with this slot
+                mbar_arrive(&bars->kq_free[cc & 1]);       // the q tile has been read
+                mbar_arrive(&bars->pg_free[cc % 3]);       // the gates have been read
             }
-        };
-        {
-            // O accumulates from the first chunk's [W | Q~] S: start it at zero
-            float z[32];
-#pragma unroll
-            for (int i = 0; i < 32; ++i) z[i] = 0.f;
-            tmem_st32(tmem + lane_off + C_O, z);
-            tmem_st32(tmem + lane_off + C_O + 32, z);
-            tmem_st_wait();
-            tc_fence_before();
-        }
-        build_qt(0);
-#pragma unroll 1
-        for (int c = 0; c < nchunks; ++c) {
-            if (c + 1 < nchunks) build_qt(c + 1);
-            // ---- o[t, j] = O^T[j, t]
-            mbar_wait_or_abort(&bars->pdv_done, c & 1, err, abort_flag);
-            tc_fence_after();
-            uint32_t ob2[32];                              // bf16 results, tokens (2i, 2i+1)
-            {
-                float o[64];
-                tmem_ld64(tmem + lane_off + C_O, o);
-                float z[32];
-#pragma unroll
-                for (int i = 0; i < 32; ++i) z[i] = 0.f;
-                tmem_st32(tmem + lane_off + C_O, z);          // O starts at zero for the next chunk
-                tmem_st32(tmem + lane_off + C_O + 32, z);
-#pragma unroll
-                for (int i = 0; i < 32; ++i) ob2[i] = cvt_bf16x2(o[2 * i], o[2 * i + 1]);
-                tmem_st_wait();
-            }
-            tc_fence_before();
-            mbar_arrive(&bars->o_free);
-            // varlen: a sequence's last chunk is stored row by row, only its own tokens (the
-            // rows past its end belong to the next sequence); coalesced over the 128 columns
-            const int cabs = c0 + c;
-            const bool tail = args.cu && (cabs + 1) * kC > seq_len;
-            if (tail && j < dv_valid && !*abort_flag) {
-                const int nvalid = seq_len - cabs * kC;
-                uint16_t* orow = args.out + (static_cast<long>(trow0 + cabs * kC) * args.Hv + h) * args.dv + v0 + j;
-                const long ostride = static_cast<long>(args.Hv) * args.dv;
-#pragma unroll
-                for (int i = 0; i < 32; ++i) {
-                    if (2 * i < nvalid) orow[(2 * i) * ostride] = static_cast<uint16_t>(ob2[i] & 0xffffu);
-                    if (2 * i + 1 < nvalid) orow[(2 * i + 1) * ostride] = static_cast<uint16_t>(ob2[i] >> 16);
-                }
-            }
-            if (oleader) bulk_wait_read1();                // the store of two chunks ago left this buffer
-            named_bar(BAR_OUT, 128);
-            uint8_t* ob = sm + L::OFF_O + (c & 1) * 16384 + (j >> 6) * 8192;
-            const uint32_t jj = j & 63;
-#pragma unroll
-            for (int i = 0; i < 32; ++i) {
-                *reinterpret_cast<uint16_t*>(ob + sw128_off(2 * i, jj)) = static_cast<uint16_t>(ob2[i] & 0xffffu);
-                *reinterpret_cast<uint16_t*>(ob + sw128_off(2 * i + 1, jj)) = static_cast<uint16_t>(ob2[i] >> 16);
-            }
-            fence_async_smem();
-            named_bar(BAR_OUT, 128);
-            if (oleader) {
-                if (!*abort_flag && !tail)
-                    for (int vb = 0; vb < nvb; ++vb)
-                        tma_store_4d(map_o, sm + L::OFF_O + (c & 1) * 16384 + vb * 8192, v0 + vb * 64,
-                                     trow0 + cabs * kC, h, bco);
-                bulk_commit();
-            }
-        }
-        if (oleader) {
-            bulk_wait_all0();
-            if (w_last >= 0) mbar_wait(&bars->w_full, w_last & 1, err);   // the last W copy has landed
         }
     }
 
