@@ -635,14 +635,6 @@ __device__ __forceinline__ void prep_body(const CUtensorMap* map_q, const CUtens
 
         // ---- [Q;K] K^T on tensor cores
         mbar_wait_or_abort(bar_qk, ph, err, abort_flag);
-        if (leader && args.ready && published >= 0) {
-            // streamed: the previous task's stores were issued before this task's q/k load,
-            // so they have (nearly) completed; publish its record now rather than a task
-            // later (a chain CTA waits for it)
-            bulk_wait_all0();
-            if (published != g_unpublished_record) publish_record(args.ready + published);
-            published = -1;
-        }
         if (leader && !*abort_flag) {
             tc_fence_after();
             const uint32_t sqk = smem_u32(sm);
@@ -654,6 +646,13 @@ __device__ __forceinline__ void prep_body(const CUtensorMap* map_q, const CUtens
                              sdesc_sw128(sqk + o + 8192, 16, 1024), id64, kk > 0);
             }
             umma_commit(bar_qkk);
+        }
+        if (leader && args.ready && published >= 0) {
+            // streamed: publish the previous task's record once its bulk stores have completed;
+            // after this task's MMAs are issued, so that waiting for the stores does not delay them
+            bulk_wait_all0();
+            if (published != g_unpublished_record) publish_record(args.ready + published);
+            published = -1;
         }
 
         const bool direct = g[G_FLAG * 64] != 0.f;
