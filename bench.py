@@ -308,7 +308,7 @@ def run_ours(args):
 #   decode: one config-2 step (543.2 MB read + 479.7 MB written),
 #     ncu --metrics dram__bytes_read.sum,dram__bytes_write.sum --clock-control none
 #         -k regex:decode_step -c 1 python bench.py --only decode --steps 1 --warmup 0
-PREFILL_TRAFFIC_PER_STEP = 677.6e6
+PREFILL_TRAFFIC_PER_STEP = 537.0e6
 DECODE_TRAFFIC_PER_LAUNCH = 1022.9e6
 
 
@@ -823,6 +823,21 @@ def run_only(args):
 
         def step():
             layer.prefill(xl)
+    elif args.only == "norm":
+        # config 3's two norms, one launch each per step: the input RMSNorm over x [16384, 2048]
+        # and the gated output norm over o, z [524288, 128]
+        g = torch.Generator(device=dev).manual_seed(21)
+        x = torch.randn(2 * 8192, 2048, generator=g, device=dev).bfloat16()
+        y = torch.empty_like(x)
+        gamma = (1.0 + 0.1 * torch.randn(2048, generator=g, device=dev)).bfloat16()
+        o = torch.randn(2 * 8192 * 32, 128, generator=g, device=dev).bfloat16()
+        z = torch.randn(2 * 8192 * 32, 128, generator=g, device=dev).bfloat16()
+        yg = torch.empty_like(o)
+        gam = (1.0 + 0.1 * torch.randn(128, generator=g, device=dev)).bfloat16()
+
+        def step():
+            ops.rmsnorm(x, gamma, 1e-6, out=y)
+            ops.gated_rmsnorm(o, z, gam, 1e-6, out=yg)
     elif args.only == "outproj":
         # the fused output projection's GEMM on one GPU (world 1: every tile stays local)
         # at the config-3 widths: y [32768, 4096] x W_o [2048, 4096]^T
@@ -871,7 +886,7 @@ def main(argv=None):
     ap.add_argument("--workload", choices=["prefill", "long"], default="prefill")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--only", choices=["prefill", "decode", "proj", "layer_decode", "layer_prefill", "backward", "backward_config1",
-                             "outproj"], default=None,
+                             "outproj", "norm"], default=None,
                     help="run just one kernel's workload (for profiling); prints a short JSON line")
     args = ap.parse_args(argv)
     if args.only:
