@@ -301,6 +301,7 @@ def _sampled_oracle_check(q, k, v, a, b, A_log, s0, o, S, picks, scale):
         o_r, S_r = _oracle(sub)
         errs.append(_check(to_np(o[bi:bi + 1, hi:hi + 1]), to_np(S[bi:bi + 1, hi:hi + 1]), o_r, S_r))
         errs.append(O.rel_fro(to_np(S[bi:bi + 1, hi:hi + 1]), S_r))
+    print("sampled (b, h) against the fp64 oracle: o max-abs / state rel-F", ["%.2e" % e for e in errs])
     return errs
 
 
