@@ -360,9 +360,10 @@ __device__ __forceinline__ void blk_load(float (&acc)[2][4], const float* src, i
 // ---------------------------------------------------------------------------
 // A = (I - N)^-1 for the 64x64 strictly-lower N held in Nsm (row stride NLD),
 // by the 128 prep threads (4 warps):
-//   1. warp w inverts the 16x16 diagonal block w by forward substitution in
-//      registers (row i of the block becomes final at step i and is broadcast
-//      by shuffles); D_w overwrites the diagonal block of Nsm;
+//   1. warps 0 and 1 invert the four 16x16 diagonal blocks by forward
+//      substitution, one column of D_i per lane (16 lanes per block, the rows
+//      of N_ii read as shared-memory broadcasts); D_i overwrites the diagonal
+//      block of Nsm;
 //   2. off-diagonal blocks, A_ij = D_i sum_{k=j}^{i-1} N_ik A_kj (A_jj = D_j),
 //      as warp-level MMAs on 16x16 blocks, with the D-only terms issued first:
 //        a) Y_{i,i-1} = N_{i,i-1} D_{i-1};  Z20 = N20 D0, Z31 = N31 D1, Z30 = N30 D0
@@ -372,32 +373,29 @@ __device__ __forceinline__ void blk_load(float (&acc)[2][4], const float* src, i
 // ---------------------------------------------------------------------------
 template <int NLD, int AOLD>
 __device__ __forceinline__ void invert_unit_lower(float* Nsm, float* Ao, float* Xs, int pw, int lane, int bar_id) {
-    {
-        const int r = lane >> 1, hf = lane & 1;
-        const int row0 = 16 * pw;
-        float n[16], x[8];
-        const float4* nr = reinterpret_cast<const float4*>(Nsm + (row0 + r) * NLD + row0);
+    if (pw < 2) {
+        // diagonal block blk = 2 pw + (lane >> 4); lane j = lane & 15 computes column j of D:
+        // x_i = delta_ij + sum_{k<i} N_ik x_k (x_k = 0 for k < j), N rows read as shared-memory
+        // broadcasts, no cross-lane exchange
+        const int blk = 2 * pw + (lane >> 4), j = lane & 15, row0 = 16 * blk;
+        float* nb = Nsm + row0 * NLD + row0;
+        float x[16];
 #pragma unroll
-        for (int q = 0; q < 4; ++q) {
-            const float4 t4 = nr[q];
-            n[4 * q] = t4.x; n[4 * q + 1] = t4.y; n[4 * q + 2] = t4.z; n[4 * q + 3] = t4.w;
-        }
+        for (int i = 0; i < 16; ++i) {
+            float a0 = (i == j) ? 1.f : 0.f, a1 = 0.f;
 #pragma unroll
-        for (int cc = 0; cc < 8; ++cc) x[cc] = (8 * hf + cc == r) ? 1.f : 0.f;
-#pragma unroll
-        for (int i = 0; i < 15; ++i) {
-            float bi[8];
-#pragma unroll
-            for (int cc = 0; cc < 8; ++cc) bi[cc] = __shfl_sync(0xffffffffu, x[cc], 2 * i + hf);
-            if (r > i) {
-#pragma unroll
-                for (int cc = 0; cc < 8; ++cc) x[cc] = fmaf(n[i], bi[cc], x[cc]);
+            for (int k4 = 0; k4 < i; k4 += 4) {
+                const float4 n4 = *reinterpret_cast<const float4*>(nb + i * NLD + k4);
+                a0 = fmaf(n4.x, x[k4], a0);
+                if (k4 + 1 < i) a1 = fmaf(n4.y, x[k4 + 1], a1);
+                if (k4 + 2 < i) a0 = fmaf(n4.z, x[k4 + 2], a0);
+                if (k4 + 3 < i) a1 = fmaf(n4.w, x[k4 + 3], a1);
             }
+            x[i] = a0 + a1;
         }
-        __syncwarp();
-        float4* dst = reinterpret_cast<float4*>(Nsm + (row0 + r) * NLD + row0 + 8 * hf);
-        dst[0] = make_float4(x[0], x[1], x[2], x[3]);
-        dst[1] = make_float4(x[4], x[5], x[6], x[7]);
+        __syncwarp();                              // every lane has read its block's rows
+#pragma unroll
+        for (int i = 0; i < 16; ++i) nb[i * NLD + j] = x[i];
     }
     named_bar(bar_id, 128);
     auto Nb = [&](int i, int j) { return Nsm + (16 * i) * NLD + 16 * j; };   // N_ij (i > j) or D_i (i == j)
