@@ -289,6 +289,128 @@ def prefill_backward(q, k, v, A_log, a, dt_bias, b_logits, mask, dO, state_in=No
                 ddt_bias=da.sum(axis=(0, 2)), dstate_in=dS)
 
 
+def prefill_backward_chunked(q, k, v, A_log, a, dt_bias, b_logits, mask, dO, state_in=None, dS_final=None,
+                             scale=0.0, chunk_size=64, dt=np.float64):
+    """The same gradients as prefill_backward, computed chunk by chunk (the form
+    a chunked GPU backward takes).  Restatement-pinned: it matches
+    prefill_backward, itself pinned to finite differences (tests).
+
+    Per chunk of C tokens, with S the state entering it, Sb the gradient of the
+    state leaving it, G_t = prod_{i<=t} g_i, b = beta * mask, dO' = mask * dO,
+    M = (K K^T) * [G_t/G_s, s < t], R+ = [G_t/G_s, s <= t]:
+      forward substitution  d_t = b_t (v_t - r_t),  r_t = G_t (K S)_t + sum_{s<t} M_ts d_s
+      X  = diag(G_L/G) K Sb + (scale Q K^T * R+)^T dO'
+      back substitution     dd_s = X_s - sum_{u>s} M_us b_u dd_u     (dd = A^T X)
+      dr = -b dd,  dv = b dd,  db' = dd . (v - r)
+      S_bar = G_L Sb + scale (diag(G) Q)^T dO' - (diag(G b) K)^T dd   (the state gradient entering)
+      dq = scale diag(G) dO' S^T + scale ((dO' D^T) * R+) K
+      dk = diag(G_L/G) D Sb^T + scale ((dO' D^T) * R+)^T Q + ((dr D^T) * R-)^T K
+           + diag(G) dr S^T + ((dr D^T) * R-) K                     (R- = strict part of R+)
+    and g_t dg_t (the log-gate gradient) from the pairwise decay factors:
+      G_L <S, Sb> + sum_{u>=t} G_u scale q_u.(S dO'_u) + sum_{u>t} G_u k_u.(S dr_u)
+      + sum_{s<t} (G_L/G_s) k_s.(Sb d_s) + sum_{s<t<=u} F_us + sum_{s<t<u} H_us + r_t . dr_t
+    with F_us = scale (q_u.k_s)(dO'_u.d_s) G_u/G_s and H_us = (k_u.k_s)(dr_u.d_s) G_u/G_s.
+    Only S at chunk starts and Sb at chunk ends are carried; no per-token state.
+    Arguments and result as prefill_backward."""
+    q = _as_f32(q, dt)
+    k = _as_f32(k, dt)
+    v = _as_f32(v, dt)
+    dO = np.asarray(dO, dtype=dt)
+    B, H, T, K = q.shape
+    V = v.shape[-1]
+    C = chunk_size
+    if scale == 0.0:
+        scale = 1.0 / math.sqrt(K)
+    g, beta = gates(a, A_log, dt_bias, b_logits, dt)
+    m = np.broadcast_to(np.asarray(mask, dtype=dt)[:, None, :], (B, H, T))
+    bm = beta * m
+    lg = np.log(g)
+    n = (T + C - 1) // C
+    mm = lambda x, y: np.einsum("bhij,bhjk->bhik", x, y)
+    tr = lambda x: np.swapaxes(x, -1, -2)
+
+    def chunk(c):
+        t0, t1 = c * C, min(T, c * C + C)
+        L = np.cumsum(lg[:, :, t0:t1], axis=-1)
+        G = np.exp(L)
+        diff = L[..., :, None] - L[..., None, :]
+        Cn = t1 - t0
+        le = np.tril(np.ones((Cn, Cn), dtype=bool))
+        Rle = np.where(le, np.exp(np.where(le, diff, 0.0)), 0.0)
+        Rlt = np.where(np.tril(le, -1), Rle, 0.0)
+        Kc = k[:, :, t0:t1]
+        return t0, t1, Cn, L, G, Rle, Rlt, mm(Kc, tr(Kc)) * Rlt
+
+    def fwd_sub(S, c):                                 # D and v - r of chunk c from its entering state S
+        t0, t1, Cn, L, G, Rle, Rlt, M = chunk(c)
+        KS = mm(k[:, :, t0:t1], S)
+        D = np.zeros((B, H, Cn, V), dt)
+        Vr = np.zeros((B, H, Cn, V), dt)
+        for t in range(Cn):
+            r = G[..., t, None] * KS[:, :, t] + np.einsum("bhs,bhsv->bhv", M[:, :, t, :t], D[:, :, :t])
+            Vr[:, :, t] = v[:, :, t0 + t] - r
+            D[:, :, t] = bm[:, :, t0 + t, None] * Vr[:, :, t]
+        return D, Vr, KS
+
+    S = np.zeros((B, H, K, V), dt) if state_in is None else np.array(state_in, dt, copy=True)
+    ckpt = []
+    for c in range(n):                                 # forward: the state at every chunk start
+        ckpt.append(S)
+        t0, t1, Cn, L, G, Rle, Rlt, M = chunk(c)
+        D, _, _ = fwd_sub(S, c)
+        GL = G[..., -1]
+        S = GL[..., None, None] * S + mm(tr(k[:, :, t0:t1] * (GL[..., None] / G)[..., None]), D)
+
+    dq, dk, dv = np.zeros_like(q), np.zeros_like(k), np.zeros_like(v)
+    dlogg, dbm = np.zeros((B, H, T), dt), np.zeros((B, H, T), dt)
+    Sb = np.zeros((B, H, K, V), dt) if dS_final is None else np.array(dS_final, dt, copy=True)
+    for c in range(n - 1, -1, -1):                     # reverse over chunks
+        t0, t1, Cn, L, G, Rle, Rlt, M = chunk(c)
+        S = ckpt[c]
+        Qc, Kc, Vc, bc = q[:, :, t0:t1], k[:, :, t0:t1], v[:, :, t0:t1], bm[:, :, t0:t1]
+        dOp = dO[:, :, t0:t1] * m[:, :, t0:t1, None]
+        GL = G[..., -1]
+        D, Vr, KS = fwd_sub(S, c)
+        P = scale * mm(Qc, tr(Kc)) * Rle
+        KSb = mm(Kc, Sb)
+        X = (GL[..., None] / G)[..., None] * KSb + mm(tr(P), dOp)
+        DD = np.zeros_like(X)
+        for s in range(Cn - 1, -1, -1):
+            DD[:, :, s] = X[:, :, s] - np.einsum("bhu,bhuv->bhv", M[:, :, s + 1:, s] * bc[:, :, s + 1:], DD[:, :, s + 1:])
+        dR = -bc[..., None] * DD
+        dOD, dRD = mm(dOp, tr(D)), mm(dR, tr(D))
+        dq[:, :, t0:t1] = scale * G[..., None] * mm(dOp, tr(S)) + scale * mm(dOD * Rle, Kc)
+        dk[:, :, t0:t1] = ((GL[..., None] / G)[..., None] * mm(D, tr(Sb)) + scale * mm(tr(dOD * Rle), Qc)
+                           + mm(tr(dRD * Rlt), Kc) + G[..., None] * mm(dR, tr(S)) + mm(dRD * Rlt, Kc))
+        dv[:, :, t0:t1] = bc[..., None] * DD
+        dbm[:, :, t0:t1] = (DD * Vr).sum(-1)
+        a_u = G * scale * (mm(Qc, S) * dOp).sum(-1)
+        c_u = G * (KS * dR).sum(-1)
+        e_s = (GL[..., None] / G) * (KSb * D).sum(-1)
+        ex = np.exp(L[..., :, None] - L[..., None, :])
+        F = scale * mm(Qc, tr(Kc)) * dOD * ex          # [u, s]
+        Hm = mm(Kc, tr(Kc)) * dRD * ex
+        r_dr = ((Vc - Vr) * dR).sum(-1)
+        base = GL * (S * Sb).sum(axis=(-1, -2))
+        for t in range(Cn):
+            dlogg[:, :, t0 + t] = (base + a_u[..., t:].sum(-1) + c_u[..., t + 1:].sum(-1) + e_s[..., :t].sum(-1)
+                                   + F[..., t:, :t].sum(axis=(-1, -2)) + Hm[..., t + 1:, :t].sum(axis=(-1, -2))
+                                   + r_dr[..., t])
+        Sb = (GL[..., None, None] * Sb + scale * mm(tr(Qc * G[..., None]), dOp)
+              - mm(tr(Kc * (G * bc)[..., None]), DD))
+    af = _as_f32(a, dt)
+    bf = _as_f32(b_logits, dt)
+    A = np.asarray(A_log, dtype=dt).reshape(1, H, 1)
+    dtb = np.asarray(dt_bias, dtype=dt)
+    x = af + (dtb.reshape(1, H, 1) if dtb.ndim == 1 and dtb.shape[0] == H and H > 1 else dtb)
+    sig_x = 1.0 / (1.0 + np.exp(-x))
+    da = dlogg * (-np.exp(A)) * np.where(x > 20.0, 1.0, sig_x)
+    sb = 1.0 / (1.0 + np.exp(-bf))
+    db = dbm * m * sb * (1.0 - sb)
+    return dict(dq=dq, dk=dk, dv=dv, da=da, db=db, dA_log=(dlogg * lg).sum(axis=(0, 2)),
+                ddt_bias=da.sum(axis=(0, 2)), dstate_in=Sb)
+
+
 # --------------------------------------------------------------------------
 # Decode
 # --------------------------------------------------------------------------

@@ -43,3 +43,25 @@ def test_prefill_backward_matches_finite_differences():
             lm = _loss(**{**args, arg: xm}, mask=mask, dO=dO, dSf=dSf, scale=scale)
             num[idx] = (lp - lm) / (2 * eps)
         np.testing.assert_allclose(gr[gname], num, rtol=1e-5, atol=1e-7, err_msg=arg)
+
+
+def test_chunked_backward_matches_token_recurrent():
+    """prefill_backward_chunked (per-chunk checkpoints only, the form of a chunked
+    GPU backward) equals prefill_backward on the same inputs: ragged last chunks,
+    a mask, a per-head dt_bias, an initial state and a final-state gradient."""
+    for (B, H, T, K, V, C, seed) in [(1, 2, 70, 16, 8, 16, 1), (2, 2, 130, 32, 16, 32, 2), (1, 1, 128, 64, 64, 64, 3)]:
+        inp = O.make_prefill_inputs(seed, B, T, H, K, V, state_std=0.1)
+        mask = np.ones((B, T), np.float32)
+        mask[:, 5:9] = 0.0
+        mask[-1, -3:] = 0.0
+        rng = np.random.default_rng(seed)
+        dtb = rng.standard_normal(H) * 0.3 if H > 1 else 0.1
+        dO = rng.standard_normal((B, H, T, V))
+        dSf = rng.standard_normal((B, H, K, V)) * 0.1
+        args = (inp["q"], inp["k"], inp["v"], inp["A_log"], inp["a"], dtb, inp["b"], mask, dO)
+        ref = O.prefill_backward(*args, state_in=inp["state_in"], dS_final=dSf, scale=inp["scale"])
+        got = O.prefill_backward_chunked(*args, state_in=inp["state_in"], dS_final=dSf, scale=inp["scale"],
+                                         chunk_size=C)
+        for name in ref:
+            np.testing.assert_allclose(got[name], ref[name], rtol=1e-9, atol=1e-11 * np.abs(ref[name]).max(),
+                                       err_msg=f"{name} at {(B, H, T, K, V, C)}")
