@@ -83,6 +83,7 @@ SIGNATURES = {
     "gdn_prefill_bwd": [_P, _P, _P, _P, _P, _P, _I, _F, _P, _P, _P, _P, _I, _P,
                         _P, _P, _P, _P, _P, _P, _P, _P, _I, _I, _I, _I, _I, _F, _P, _Z, _P],
     "gdn_prefill_bwd_workspace_bytes": [_I, _I, _I, _I, _I],
+    "gdn_prefill_bwd_set_window": [_I],
     "gdn_prefill_set_schedule": [_I],
     "gdn_prefill_launch_count": [_I, _I, _I, _I, _I],
     "gdn_prefill_launch_count_ex": [_I, _I, _I, _I, _I, _I],

@@ -51,12 +51,21 @@ struct BwdArgs {
     float* dA_log;             // [H] f32
     float* ddt_bias;           // [H] f32
     float* dstate_in;          // [B,H,DK,DV] f32 or null
-    float* states;             // workspace: S_p per token [B,H,T,DK,DV]
-    float* rp;                 // workspace: [B,H,T,DV], k . S_p per value column
-    float* part;               // workspace: per token and column block, row sums and scalars
+    float* states;             // workspace: S_p per token of the window [B*H][WT][DK][DV]
+    float* rp;                 // workspace: [B*H][WT][DV], k . S_p per value column
+    float* part;               // workspace: per token of the window and column block, row sums and scalars
     float* dlogg;              // workspace: [B,H,T]
     int B, T, H;
     float scale;
+    // token window of a launch: tokens [t0, t1); the window buffers (states, rp, part) hold
+    // WT tokens per sequence-head, indexed from t0
+    int t0, t1, WT;
+    const float* S0;           // states kernel: the state before token t0, S0 + bh * S0_stride; null = zeros
+    long S0_stride;
+    float* ckpt;               // checkpoint pass: the state before every token t % win == 0,
+    int win, nwin;             //   ckpt[(bh * nwin + t / win) * DK * DV]; no per-token state stored
+    const float* dS_in;        // reverse kernel: the gradient of the state after token t1 - 1 (null = 0)
+    float* dS_out;             //   and, at the end, of the state before token t0 (null = not stored)
 };
 
 __device__ __forceinline__ float bf16_at(const uint16_t* p, long i) { return bf16_bits_to_f32(p[i]); }
@@ -113,13 +122,13 @@ __global__ void __launch_bounds__(128) bwd_states_kernel(const BwdArgs a) {
     __shared__ float vs[kTB][L::CTA_COLS];
     __shared__ float gs[kTB], bs[kTB];
     float S[L::ROWS];
-    const long s0 = static_cast<long>(bh) * DK * DV;
+    const long s0 = static_cast<long>(bh) * a.S0_stride;
 #pragma unroll
-    for (int i = 0; i < L::ROWS; ++i)
-        S[i] = a.state_in ? a.state_in[s0 + static_cast<long>(i0 + i) * DV + j] : 0.f;
-    for (int tb = 0; tb < a.T; tb += kTB) {
-        const int nt = min(kTB, a.T - tb);
+    for (int i = 0; i < L::ROWS; ++i) S[i] = a.S0 ? a.S0[s0 + static_cast<long>(i0 + i) * DV + j] : 0.f;
+    for (int tb = a.t0; tb < a.t1; tb += kTB) {
+        const int nt = min(kTB, a.t1 - tb);
         const long tok0 = static_cast<long>(bh) * a.T + tb;
+        const long loc0 = static_cast<long>(bh) * a.WT + (tb - a.t0);      // window-local token index
         __syncthreads();
         for (int e = tid; e < nt * DK; e += L::THREADS) ks[e / DK][e % DK] = bf16_at(a.k, tok0 * DK + e);
         for (int e = tid; e < nt * L::CTA_COLS; e += L::THREADS)
@@ -128,10 +137,18 @@ __global__ void __launch_bounds__(128) bwd_states_kernel(const BwdArgs a) {
         if (tid < nt) gate_of(a, bh, tb + tid, gs[tid], bs[tid]);
         __syncthreads();
         for (int u = 0; u < nt; ++u) {
-            const long tok = tok0 + u;
-            float* out = a.states + (tok * DK + i0) * DV + j;
+            const long loc = loc0 + u;
+            if (a.ckpt) {
+                if ((tb + u) % a.win == 0) {
+                    float* out = a.ckpt + ((static_cast<long>(bh) * a.nwin + (tb + u) / a.win) * DK + i0) * DV + j;
 #pragma unroll
-            for (int i = 0; i < L::ROWS; ++i) out[static_cast<long>(i) * DV] = S[i];
+                    for (int i = 0; i < L::ROWS; ++i) out[static_cast<long>(i) * DV] = S[i];
+                }
+            } else {
+                float* out = a.states + (loc * DK + i0) * DV + j;
+#pragma unroll
+                for (int i = 0; i < L::ROWS; ++i) out[static_cast<long>(i) * DV] = S[i];
+            }
             const float* kk = ks[u] + i0;
             const float g = gs[u], bm = bs[u];
             float r0 = 0.f, r1 = 0.f, r2 = 0.f, r3 = 0.f;
@@ -143,7 +160,7 @@ __global__ void __launch_bounds__(128) bwd_states_kernel(const BwdArgs a) {
                 r3 = fmaf(kk[i + 3], S[i + 3], r3);
             }
             const float rp = sum_parts<L::PARTS, L::COLS>((r0 + r1) + (r2 + r3));
-            if (i0 == 0) a.rp[tok * DV + j] = rp;
+            if (i0 == 0 && !a.ckpt) a.rp[loc * DV + j] = rp;
             const float d = bm * (vs[u][jc] - g * rp);
 #pragma unroll
             for (int i = 0; i < L::ROWS; ++i) S[i] = fmaf(kk[i], d, g * S[i]);
@@ -205,20 +222,20 @@ __global__ void __launch_bounds__(128) bwd_reverse_kernel(const BwdArgs a) {
     float dS[L::ROWS];
     const long s0 = static_cast<long>(bh) * DK * DV;
 #pragma unroll
-    for (int i = 0; i < L::ROWS; ++i)
-        dS[i] = a.dS_final ? a.dS_final[s0 + static_cast<long>(i0 + i) * DV + j] : 0.f;
+    for (int i = 0; i < L::ROWS; ++i) dS[i] = a.dS_in ? a.dS_in[s0 + static_cast<long>(i0 + i) * DV + j] : 0.f;
     // S_p of the token processed next, loaded one token ahead (the loads are the
-    // long-latency part of a step)
+    // long-latency part of a step); window-local token indices
     float SpN[L::ROWS];
-    const long tok_first = static_cast<long>(bh) * a.T;
+    const long loc_first = static_cast<long>(bh) * a.WT;
     {
-        const float* sp = a.states + ((tok_first + a.T - 1) * DK + i0) * DV + j;
+        const float* sp = a.states + ((loc_first + (a.t1 - 1 - a.t0)) * DK + i0) * DV + j;
 #pragma unroll
         for (int i = 0; i < L::ROWS; ++i) SpN[i] = sp[static_cast<long>(i) * DV];
     }
-    for (int tend = a.T; tend > 0; tend -= kRevTB) {
-        const int tb = max(0, tend - kRevTB), nt = tend - tb;
+    for (int tend = a.t1; tend > a.t0; tend -= kRevTB) {
+        const int tb = max(a.t0, tend - kRevTB), nt = tend - tb;
         const long tok0 = static_cast<long>(bh) * a.T + tb;
+        const long loc0 = loc_first + (tb - a.t0);
         __syncthreads();
         for (int e = tid; e < nt * DK; e += L::THREADS) {
             ks[e / DK][e % DK] = bf16_at(a.k, tok0 * DK + e);
@@ -231,12 +248,13 @@ __global__ void __launch_bounds__(128) bwd_reverse_kernel(const BwdArgs a) {
             mdo[u][c] = m * (a.do_dtype == GDN_DTYPE_BF16 ? bf16_at(static_cast<const uint16_t*>(a.dO), idx)
                                                           : static_cast<const float*>(a.dO)[idx]);
             vv[u][c] = bf16_at(a.v, idx);
-            rps[u][c] = a.rp[idx];
+            rps[u][c] = a.rp[(loc0 + u) * DV + blockIdx.y * L::CTA_COLS + c];
         }
         if (tid < nt) gate_of(a, bh, tb + tid, gs[tid], bs[tid]);
         __syncthreads();
         for (int u = nt - 1; u >= 0; --u) {
             const long tok = tok0 + u;
+            const long loc = loc0 + u;
             const float* kk = ks[u] + i0;
             const float* qq = qs[u] + i0;
             const float dos = mdo[u][jc];
@@ -246,8 +264,8 @@ __global__ void __launch_bounds__(128) bwd_reverse_kernel(const BwdArgs a) {
             float Sp[L::ROWS];
 #pragma unroll
             for (int i = 0; i < L::ROWS; ++i) Sp[i] = SpN[i];
-            if (tok > tok_first) {
-                const float* sp = a.states + ((tok - 1) * DK + i0) * DV + j;
+            if (loc > loc_first) {
+                const float* sp = a.states + ((loc - 1) * DK + i0) * DV + j;
 #pragma unroll
                 for (int i = 0; i < L::ROWS; ++i) SpN[i] = sp[static_cast<long>(i) * DV];
             }
@@ -307,7 +325,7 @@ __global__ void __launch_bounds__(128) bwd_reverse_kernel(const BwdArgs a) {
                 scr[pb][warp][3] = sds;
             }
             __syncthreads();
-            float* pp = a.part + (tok * NCB + blockIdx.y) * PST;
+            float* pp = a.part + (loc * NCB + blockIdx.y) * PST;
             for (int i = tid; i < DK; i += L::THREADS) {
                 float xs = 0.f, ys = 0.f;
 #pragma unroll
@@ -328,9 +346,9 @@ __global__ void __launch_bounds__(128) bwd_reverse_kernel(const BwdArgs a) {
             for (int i = 0; i < L::ROWS; ++i) dS[i] = g * fmaf(kk[i], dr, dS[i]);
         }
     }
-    if (a.dstate_in) {
+    if (a.dS_out) {
 #pragma unroll
-        for (int i = 0; i < L::ROWS; ++i) a.dstate_in[s0 + static_cast<long>(i0 + i) * DV + j] = dS[i];
+        for (int i = 0; i < L::ROWS; ++i) a.dS_out[s0 + static_cast<long>(i0 + i) * DV + j] = dS[i];
     }
 }
 
@@ -339,11 +357,12 @@ __global__ void __launch_bounds__(128) bwd_reverse_kernel(const BwdArgs a) {
 template <int DK, int DV>
 __global__ void __launch_bounds__(128) bwd_finish_kernel(const BwdArgs a) {
     constexpr int NCB = DV / RecLayout<DK>::CTA_COLS, PST = PartLayout<DK>::STRIDE;
-    const long tok = blockIdx.x;                  // bh * T + t
-    const int bh = static_cast<int>(tok / a.T), t = static_cast<int>(tok - static_cast<long>(bh) * a.T);
+    const int nw = a.t1 - a.t0;                   // one CTA per token of the window
+    const int bh = static_cast<int>(blockIdx.x / nw), t = a.t0 + static_cast<int>(blockIdx.x % nw);
+    const long tok = static_cast<long>(bh) * a.T + t;
     const int bi = bh / a.H, h = bh % a.H;
     const int tid = threadIdx.x;
-    const float* pp = a.part + tok * NCB * PST;
+    const float* pp = a.part + (static_cast<long>(bh) * a.WT + (t - a.t0)) * NCB * PST;
     float sc[4] = {0.f, 0.f, 0.f, 0.f};
 #pragma unroll
     for (int cb = 0; cb < NCB; ++cb)
@@ -405,16 +424,46 @@ __global__ void __launch_bounds__(256) bwd_head_kernel(const BwdArgs a) {
     }
 }
 
+// The backward runs window by window, last window first, so that only one window's
+// per-token states are in the workspace at a time: a checkpoint pass of the forward
+// recurrence over the whole sequence stores the state at every window start, then
+// per window the states kernel recomputes the window's per-token states from its
+// checkpoint, the reverse kernel carries dS through the window (in and out of the
+// carry buffer) and the finish kernel completes its tokens.  One window covering
+// the sequence needs no checkpoint pass.
 template <int DK, int DV>
-int launch_bwd(const BwdArgs& a, cudaStream_t st) {
+int launch_bwd(BwdArgs a, int W, float* ckpt, float* carry, cudaStream_t st) {
     const dim3 rec(a.B * a.H, DV / RecLayout<DK>::CTA_COLS);
-    bwd_states_kernel<DK, DV><<<rec, RecLayout<DK>::THREADS, 0, st>>>(a);
-    int s = launch_status("gdn_prefill_bwd (states)");
-    if (s != GDN_OK) return s;
-    bwd_reverse_kernel<DK, DV><<<rec, RecLayout<DK>::THREADS, 0, st>>>(a);
-    if ((s = launch_status("gdn_prefill_bwd (reverse)")) != GDN_OK) return s;
-    bwd_finish_kernel<DK, DV><<<static_cast<unsigned>(static_cast<long>(a.B) * a.H * a.T), 128, 0, st>>>(a);
-    if ((s = launch_status("gdn_prefill_bwd (finish)")) != GDN_OK) return s;
+    const int nwin = (a.T + W - 1) / W;
+    const float* state_in = a.state_in;
+    int s;
+    a.WT = W;
+    a.win = W;
+    a.nwin = nwin;
+    if (nwin > 1) {
+        a.t0 = 0;
+        a.t1 = a.T;
+        a.S0 = state_in;
+        a.S0_stride = static_cast<long>(DK) * DV;
+        a.ckpt = ckpt;
+        bwd_states_kernel<DK, DV><<<rec, RecLayout<DK>::THREADS, 0, st>>>(a);
+        if ((s = launch_status("gdn_prefill_bwd (checkpoints)")) != GDN_OK) return s;
+    }
+    a.ckpt = nullptr;
+    for (int w = nwin - 1; w >= 0; --w) {
+        a.t0 = w * W;
+        a.t1 = a.t0 + W < a.T ? a.t0 + W : a.T;
+        a.S0 = nwin > 1 ? ckpt + static_cast<long>(w) * DK * DV : state_in;
+        a.S0_stride = static_cast<long>(nwin > 1 ? nwin : 1) * DK * DV;
+        bwd_states_kernel<DK, DV><<<rec, RecLayout<DK>::THREADS, 0, st>>>(a);
+        if ((s = launch_status("gdn_prefill_bwd (states)")) != GDN_OK) return s;
+        a.dS_in = w == nwin - 1 ? a.dS_final : carry;
+        a.dS_out = w == 0 ? a.dstate_in : carry;
+        bwd_reverse_kernel<DK, DV><<<rec, RecLayout<DK>::THREADS, 0, st>>>(a);
+        if ((s = launch_status("gdn_prefill_bwd (reverse)")) != GDN_OK) return s;
+        bwd_finish_kernel<DK, DV><<<static_cast<unsigned>(static_cast<long>(a.B) * a.H * (a.t1 - a.t0)), 128, 0, st>>>(a);
+        if ((s = launch_status("gdn_prefill_bwd (finish)")) != GDN_OK) return s;
+    }
     bwd_head_kernel<<<a.H, 256, 0, st>>>(a);
     return launch_status("gdn_prefill_bwd (heads)");
 }
@@ -424,27 +473,52 @@ int launch_bwd(const BwdArgs& a, cudaStream_t st) {
 
 namespace gdn {
 namespace {
-// Workspace: states [tok][dk][dv] | rp [tok][dv] | partials [tok][column blocks][2 dk + 4] | dlogg [tok]
+thread_local int t_bwd_window = 0;   // gdn_prefill_bwd_set_window: the calling thread's window (0 = automatic)
+
+// Window length in tokens: the calling thread's setting, else max(256, sqrt T) rounded up to
+// 32 tokens (the checkpoints and one window's states together, B H dk dv 4 (T / W + W) bytes,
+// are then near their minimum without many short windows); never more than T.
+int bwd_window(int T) {
+    int w = t_bwd_window;
+    if (w <= 0) {
+        const int r = (static_cast<int>(sqrtf(static_cast<float>(T))) + 31) / 32 * 32;
+        w = r > 256 ? r : 256;
+    }
+    return w < T ? w : T;
+}
+
+// Workspace: checkpoints [bh][nwin][dk][dv] (several windows only) | window states [bh][W][dk][dv] |
+// rp [bh][W][dv] | partials [bh][W][column blocks][2 dk + 4] | dlogg [bh][T] | dS carry [bh][dk][dv]
 struct BwdWs {
-    size_t states, rp, part, dlogg, total;
+    size_t ckpt, states, rp, part, dlogg, carry, total;
 };
-BwdWs bwd_ws(size_t tok, int dk, int dv) {
+BwdWs bwd_ws(size_t bh, int T, int dk, int dv, int W) {
     const int cta_cols = dk == 128 ? RecLayout<128>::CTA_COLS : RecLayout<64>::CTA_COLS;
     const size_t ncb = static_cast<size_t>(dv / cta_cols);
+    const size_t nwin = (static_cast<size_t>(T) + W - 1) / W;
+    const size_t sd = static_cast<size_t>(dk) * dv * 4;
     BwdWs w;
-    w.states = 0;
-    w.rp = w.states + tok * dk * dv * 4;
-    w.part = w.rp + tok * dv * 4;
-    w.dlogg = w.part + tok * ncb * (2 * dk + 4) * 4;
-    w.total = w.dlogg + tok * 4 + 1024;
+    w.ckpt = 0;
+    w.states = w.ckpt + (nwin > 1 ? bh * nwin * sd : 0);
+    w.rp = w.states + bh * W * sd;
+    w.part = w.rp + bh * W * dv * 4;
+    w.dlogg = w.part + bh * W * ncb * (2 * dk + 4) * 4;
+    w.carry = w.dlogg + (bh * T * 4 + 255) / 256 * 256;
+    w.total = w.carry + bh * sd + 1024;
     return w;
 }
 }  // namespace
 }  // namespace gdn
 
+extern "C" int gdn_prefill_bwd_set_window(int tokens) {
+    if (tokens < 0) return gdn::fail(GDN_ERR_ARG, "gdn_prefill_bwd_set_window: tokens must be >= 0 (got %d)", tokens);
+    gdn::t_bwd_window = tokens;
+    return GDN_OK;
+}
+
 extern "C" size_t gdn_prefill_bwd_workspace_bytes(int B, int T, int H, int dk, int dv) {
     if (B <= 0 || T <= 0 || H <= 0 || !(dk == 64 || dk == 128) || !(dv == 64 || dv == 128)) return 0;
-    return gdn::bwd_ws(static_cast<size_t>(B) * H * T, dk, dv).total;
+    return gdn::bwd_ws(static_cast<size_t>(B) * H, T, dk, dv, gdn::bwd_window(T)).total;
 }
 
 extern "C" int gdn_prefill_bwd(const void* q, const void* k, const void* v, const float* A_log, const void* a,
@@ -496,9 +570,11 @@ extern "C" int gdn_prefill_bwd(const void* q, const void* k, const void* v, cons
     ar.dA_log = dA_log;
     ar.ddt_bias = ddt_bias;
     ar.dstate_in = dstate_in;
-    const size_t tok = static_cast<size_t>(B) * H * T;
     uint8_t* ws = static_cast<uint8_t*>(workspace);
-    const BwdWs wl = bwd_ws(tok, dkd, dvd);
+    const int W = bwd_window(T);
+    const BwdWs wl = bwd_ws(static_cast<size_t>(B) * H, T, dkd, dvd, W);
+    float* ckpt = reinterpret_cast<float*>(ws + wl.ckpt);
+    float* carry = reinterpret_cast<float*>(ws + wl.carry);
     ar.states = reinterpret_cast<float*>(ws + wl.states);
     ar.rp = reinterpret_cast<float*>(ws + wl.rp);
     ar.part = reinterpret_cast<float*>(ws + wl.part);
@@ -508,8 +584,8 @@ extern "C" int gdn_prefill_bwd(const void* q, const void* k, const void* v, cons
     ar.H = H;
     ar.scale = scale == 0.f ? 1.f / sqrtf(static_cast<float>(dkd)) : scale;
     cudaStream_t s = static_cast<cudaStream_t>(stream);
-    if (dkd == 128 && dvd == 128) return launch_bwd<128, 128>(ar, s);
-    if (dkd == 128 && dvd == 64) return launch_bwd<128, 64>(ar, s);
-    if (dkd == 64 && dvd == 128) return launch_bwd<64, 128>(ar, s);
-    return launch_bwd<64, 64>(ar, s);
+    if (dkd == 128 && dvd == 128) return launch_bwd<128, 128>(ar, W, ckpt, carry, s);
+    if (dkd == 128 && dvd == 64) return launch_bwd<128, 64>(ar, W, ckpt, carry, s);
+    if (dkd == 64 && dvd == 128) return launch_bwd<64, 128>(ar, W, ckpt, carry, s);
+    return launch_bwd<64, 64>(ar, W, ckpt, carry, s);
 }

@@ -272,12 +272,13 @@ def prefill_varlen(q, k, v, A_log, a, b_logits, cu_seqlens, *, max_len=None, dt_
 
 
 def prefill_backward(q, k, v, A_log, a, b_logits, dO, *, dt_bias=0.0, mask=None, state_in=None, dS_final=None,
-                     scale=0.0, need_dstate=True):
+                     scale=0.0, need_dstate=True, window=None):
     """Gradients of ``prefill`` (gdn_prefill_bwd): q, k [B,H,T,dk], v [B,H,T,dv] bf16
     (layout "bhtd", Hqk == Hv), gates as ``prefill``, dO [B,H,T,dv] (bf16 or f32),
-    dS_final [B,H,dk,dv] or None.  Returns a dict of fp32 tensors dq, dk, dv, da, db,
-    dA_log [H], ddt_bias ([H] for a per-head dt_bias, a scalar tensor otherwise) and
-    dstate_in (or None)."""
+    dS_final [B,H,dk,dv] or None.  ``window``: tokens per window of the windowed
+    backward (None: automatic, max(256, sqrt T)).  Returns a dict of fp32 tensors
+    dq, dk, dv, da, db, dA_log [H], ddt_bias ([H] for a per-head dt_bias, a scalar
+    tensor otherwise) and dstate_in (or None)."""
     for name, t in (("q", q), ("k", k), ("v", v)):
         _cuda_contig(t, name, torch.bfloat16)
     B, H, T, dk = q.shape
@@ -296,12 +297,19 @@ def prefill_backward(q, k, v, A_log, a, b_logits, dO, *, dt_bias=0.0, mask=None,
              da=torch.empty(B, H, T, **f32), db=torch.empty(B, H, T, **f32), dA_log=torch.empty(H, **f32),
              ddt_bias=torch.empty(H, **f32),
              dstate_in=torch.empty(B, H, dk, dv, **f32) if need_dstate else None)
-    ws_bytes = _lib.lib().gdn_prefill_bwd_workspace_bytes(B, T, H, dk, dv)
-    ws = torch.empty(max(int(ws_bytes), 1), dtype=torch.uint8, device=q.device)
-    _lib.call("gdn_prefill_bwd", _ptr(q), _ptr(k), _ptr(v), _ptr(A_log), _ptr(a), _ptr(b_logits), gdt, dt_scalar,
-              _ptr(dt_vec), _ptr(mask), _ptr(state_in), _ptr(dO), dod, _ptr(dS_final), _ptr(g["dq"]), _ptr(g["dk"]),
-              _ptr(g["dv"]), _ptr(g["da"]), _ptr(g["db"]), _ptr(g["dA_log"]), _ptr(g["ddt_bias"]),
-              _ptr(g["dstate_in"]), B, T, H, dk, dv, float(scale), _ptr(ws), int(ws_bytes), _stream())
+    _need(window is None or int(window) > 0, f"window must be a positive token count, got {window!r}")
+    lib = _lib.lib()
+    _lib.call("gdn_prefill_bwd_set_window", 0 if window is None else int(window))
+    try:
+        ws_bytes = lib.gdn_prefill_bwd_workspace_bytes(B, T, H, dk, dv)
+        ws = torch.empty(max(int(ws_bytes), 1), dtype=torch.uint8, device=q.device)
+        _lib.call("gdn_prefill_bwd", _ptr(q), _ptr(k), _ptr(v), _ptr(A_log), _ptr(a), _ptr(b_logits), gdt,
+                  dt_scalar, _ptr(dt_vec), _ptr(mask), _ptr(state_in), _ptr(dO), dod, _ptr(dS_final), _ptr(g["dq"]),
+                  _ptr(g["dk"]), _ptr(g["dv"]), _ptr(g["da"]), _ptr(g["db"]), _ptr(g["dA_log"]),
+                  _ptr(g["ddt_bias"]), _ptr(g["dstate_in"]), B, T, H, dk, dv, float(scale), _ptr(ws),
+                  int(ws_bytes), _stream())
+    finally:
+        _lib.call("gdn_prefill_bwd_set_window", 0)
     if dt_vec is None:
         g["ddt_bias"] = g["ddt_bias"].sum()
     return g

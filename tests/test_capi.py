@@ -238,6 +238,18 @@ def test_prefill_bwd_rejects(lib):
     assert call(wsb=16) == _lib.GDN_ERR_SHAPE
     assert call(ws=ODD) == _lib.GDN_ERR_ALIGN
     assert lib.gdn_prefill_bwd_workspace_bytes(1, 64, 2, 96, 64) == 0
+    # windowed: checkpoints plus one window of per-token states, not every token's state
+    c1 = lib.gdn_prefill_bwd_workspace_bytes(4, 4096, 16, 128, 128)
+    assert c1 <= 1.5e9, c1                                   # config 1 (was B H T dk dv 4 = 17.2 GB)
+    c4 = lib.gdn_prefill_bwd_workspace_bytes(8, 32768, 32, 128, 128)
+    assert c4 <= 8e9, c4                                     # config 4 fits one GPU (was 275 GB)
+    assert _lib.call_status("gdn_prefill_bwd_set_window", -1) == _lib.GDN_ERR_ARG
+    assert _lib.call_status("gdn_prefill_bwd_set_window", 64) == _lib.GDN_OK
+    try:
+        small = lib.gdn_prefill_bwd_workspace_bytes(4, 4096, 16, 128, 128)
+        assert small < c1                                    # 64-token windows hold fewer states
+    finally:
+        _lib.call_status("gdn_prefill_bwd_set_window", 0)
 
 
 def test_prefill_host_plan(lib):

@@ -18,9 +18,12 @@ def _rel(got, want):
     return float(np.abs(got - want).max() / max(np.abs(want).max(), 1e-12))
 
 
+@pytest.mark.parametrize("window", [None, 32])
 @pytest.mark.parametrize("B,H,T,dk,dv,do_bf16", [(2, 2, 100, 64, 64, False), (1, 3, 130, 128, 128, True),
                                                   (1, 2, 70, 128, 64, False), (2, 1, 65, 64, 128, True)])
-def test_prefill_bwd_vs_oracle(cuda_device, B, H, T, dk, dv, do_bf16):
+def test_prefill_bwd_vs_oracle(cuda_device, B, H, T, dk, dv, do_bf16, window):
+    """window=32 runs the backward in several token windows (the last one ragged) from
+    checkpoints of the state at every window start."""
     import torch
     from gdn_18646_b200 import ops
     rng = np.random.default_rng(B * 100 + T + dk + dv)
@@ -39,7 +42,8 @@ def test_prefill_bwd_vs_oracle(cuda_device, B, H, T, dk, dv, do_bf16):
         dO_t = dO_t.bfloat16()
     got = ops.prefill_backward(to_dev(inp["q"]), to_dev(inp["k"]), to_dev(inp["v"]), to_dev(inp["A_log"]),
                                to_dev(inp["a"]), to_dev(inp["b"]), dO_t, dt_bias=to_dev(dtb), mask=to_dev(mask),
-                               state_in=to_dev(inp["state_in"]), dS_final=to_dev(dSf), scale=inp["scale"])
+                               state_in=to_dev(inp["state_in"]), dS_final=to_dev(dSf), scale=inp["scale"],
+                               window=window)
     torch.cuda.synchronize()
     for name in ("dq", "dk", "dv", "da", "db", "dA_log", "ddt_bias", "dstate_in"):
         err = _rel(to_np(got[name]).astype(np.float64), ref[name])
@@ -87,3 +91,27 @@ def test_prefill_autograd_function(cuda_device):
     assert torch.allclose(leaves["v"].grad.float(), g["dv"].bfloat16().float())
     assert torch.allclose(leaves["a"].grad, g["da"]) and torch.allclose(leaves["state_in"].grad, g["dstate_in"])
     assert torch.allclose(dtb_l.grad, g["ddt_bias"]) and torch.allclose(leaves["A_log"].grad, g["dA_log"])
+
+
+def test_prefill_bwd_windows_bit_identical(cuda_device):
+    """The windowed backward recomputes each window's states from checkpoints with the
+    same fp32 recurrence and carries dS through memory exactly: every gradient equals
+    the one-window run bit for bit, for windows that divide T and ragged ones."""
+    import torch
+    from gdn_18646_b200 import ops
+    B, H, T, dk, dv = 2, 2, 200, 128, 128
+    inp = O.make_prefill_inputs(17, B, T, H, dk, dv, gate_dtype="f32", state_std=0.05)
+    rng = np.random.default_rng(5)
+    mask = np.ones((B, T), np.float32)
+    mask[1, 150:] = 0.0
+    dO = to_dev(rng.standard_normal((B, H, T, dv)).astype(np.float32))
+    dSf = to_dev((rng.standard_normal((B, H, dk, dv)) * 0.1).astype(np.float32))
+    args = (to_dev(inp["q"]), to_dev(inp["k"]), to_dev(inp["v"]), to_dev(inp["A_log"]), to_dev(inp["a"]),
+            to_dev(inp["b"]), dO)
+    kw = dict(dt_bias=0.1, mask=to_dev(mask), state_in=to_dev(inp["state_in"]), dS_final=dSf, scale=inp["scale"])
+    whole = ops.prefill_backward(*args, **kw, window=T)
+    for w in (32, 40, 64, 199):
+        got = ops.prefill_backward(*args, **kw, window=w)
+        torch.cuda.synchronize()
+        for name in whole:
+            assert torch.equal(got[name], whole[name]), f"{name} differs with {w}-token windows"
