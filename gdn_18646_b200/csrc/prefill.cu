@@ -200,7 +200,7 @@ struct ChainSmem {
     static constexpr int PG_BYTES = 8192 + 1024;
     static constexpr int OFF_PG = 2 * KQ_BYTES;
     // [W | -Q~] image of the current chunk, K-major tf32: key block kb (32 keys) at kb * 16 KB,
-    // rows 0-63 W (bulk-copied from the record), rows 64-127 -oc Q (built by the output warps)
+    // rows 0-63 W (bulk-copied from the record), rows 64-127 -oc Q (built by the Q~ warps)
     static constexpr int OFF_IMG = OFF_PG + 3 * PG_BYTES;
     static constexpr int OFF_V = OFF_IMG + DK * 512;       // v tile, 2 blocks of 64 columns
     static constexpr int OFF_A1 = OFF_V + 16384;           // A1 lo | hi
@@ -894,11 +894,11 @@ __device__ __forceinline__ void chain_body(const CUtensorMap* map_q, const CUten
     if (tid == 0) {
         for (int s = 0; s < 2; ++s) {
             mbar_init(&bars->kq_full[s], 1);
-            mbar_init(&bars->kq_free[s], 2);       // state-update commit + output warps (q tile read)
+            mbar_init(&bars->kq_free[s], 2);       // state-update commit + Q~ warps (q tile read)
         }
         for (int s = 0; s < 3; ++s) {
             mbar_init(&bars->pg_full[s], 1);
-            mbar_init(&bars->pg_free[s], 2);       // P dV commit + output warps (gates read)
+            mbar_init(&bars->pg_free[s], 2);       // P dV commit + Q~ warps (gates read)
         }
         mbar_init(&bars->va_full, 1);
         mbar_init(&bars->va_free, 1);
@@ -1389,7 +1389,11 @@ bool use_pieces(int nbh, int nchunks, int chain_grid, int sms) {
 // consume them (~3.3 us a chunk): the lead, then the slower of the two
 // streams.  Per-unit costs from traces of config 1 on B200 (clock stamps per
 // record and per chain chunk); at config 1 it picks no lead, which measured
-// fastest of leads 0-12.
+// fastest of leads 0-32.  The chunk cost is the chain's pace inside the streamed
+// launch, where record production sets it; the chain alone (SINGLE) now runs a
+// chunk in ~2.2 us.  With these constants the choices match the measured
+// schedules: STREAM at config 1 (0.237 ms against 0.286 ms SINGLE), SINGLE for
+// the 128-chain head shard of config 4 (2.97 ms against 8.7-12.5 ms streamed).
 double streamed_time(int nbh, int nchunks, int chain_grid, int sms, int lead) {
     const long w_all = static_cast<long>(sms) * kPrepCtasPerSm;
     const long w_free = static_cast<long>(sms - chain_grid) * kPrepPerCta;
