@@ -22,6 +22,7 @@ GDN_ERR_CUDA = 6
 GDN_ERR_DEVICE = 7
 GDN_ERR_DEVICE_TIMEOUT = 8
 GDN_ERR_ARG = 9
+GDN_BWD_AUTO, GDN_BWD_TOKEN, GDN_BWD_CHUNKED = 0, 1, 2
 
 GDN_DTYPE_BF16 = 0
 GDN_DTYPE_F32 = 1
@@ -84,6 +85,7 @@ SIGNATURES = {
                         _P, _P, _P, _P, _P, _P, _P, _P, _I, _I, _I, _I, _I, _F, _P, _Z, _P],
     "gdn_prefill_bwd_workspace_bytes": [_I, _I, _I, _I, _I],
     "gdn_prefill_bwd_set_window": [_I],
+    "gdn_prefill_bwd_set_algorithm": [_I],
     "gdn_prefill_set_schedule": [_I],
     "gdn_prefill_launch_count": [_I, _I, _I, _I, _I],
     "gdn_prefill_launch_count_ex": [_I, _I, _I, _I, _I, _I],

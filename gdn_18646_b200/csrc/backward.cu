@@ -472,12 +472,45 @@ int launch_bwd(BwdArgs a, int W, float* ckpt, float* carry, cudaStream_t st) {
 }  // namespace gdn
 
 namespace gdn {
+
+// The head sums for the chunked backward (backward_chunked.cu), which leaves dlogg and da in
+// the same layouts.
+void launch_bwd_head_sums(const float* A_log, const void* a, int gate_dtype, float dt_bias, const float* dt_bias_vec,
+                          const float* dlogg, const float* da, float* dA_log, float* ddt_bias, int B, int T, int H,
+                          cudaStream_t st) {
+    BwdArgs ar{};
+    ar.A_log = A_log;
+    ar.a = a;
+    ar.gate_dtype = gate_dtype;
+    ar.dt_bias = dt_bias;
+    ar.dt_bias_vec = dt_bias_vec;
+    ar.dlogg = const_cast<float*>(dlogg);
+    ar.da = const_cast<float*>(da);
+    ar.dA_log = dA_log;
+    ar.ddt_bias = ddt_bias;
+    ar.B = B;
+    ar.T = T;
+    ar.H = H;
+    bwd_head_kernel<<<H, 256, 0, st>>>(ar);
+}
+
+size_t prefill_bwd_chunked_workspace(int B, int T, int H, int dk, int dv);
+int prefill_bwd_chunked(const void* q, const void* k, const void* v, const float* A_log, const void* a,
+                        const void* b_logits, int gate_dtype, float dt_bias, const float* dt_bias_vec, const float* mask,
+                        const float* state_in, const void* dO, int do_dtype, const float* dS_final, float* dq, float* dk,
+                        float* dv, float* da, float* db, float* dA_log, float* ddt_bias, float* dstate_in, int B, int T,
+                        int H, int dkd, int dvd, float scale, void* workspace, cudaStream_t st);
+
 namespace {
 thread_local int t_bwd_window = 0;   // gdn_prefill_bwd_set_window: the calling thread's window (0 = automatic)
 
 // Window length in tokens: the calling thread's setting, else max(256, sqrt T) rounded up to
 // 32 tokens (the checkpoints and one window's states together, B H dk dv 4 (T / W + W) bytes,
 // are then near their minimum without many short windows); never more than T.
+thread_local int t_bwd_algo = GDN_BWD_AUTO;   // gdn_prefill_bwd_set_algorithm: the calling thread's choice
+
+bool bwd_chunked() { return t_bwd_algo != GDN_BWD_TOKEN; }   // the default is the chunked backward
+
 int bwd_window(int T) {
     int w = t_bwd_window;
     if (w <= 0) {
@@ -516,8 +549,16 @@ extern "C" int gdn_prefill_bwd_set_window(int tokens) {
     return GDN_OK;
 }
 
+extern "C" int gdn_prefill_bwd_set_algorithm(int algorithm) {
+    if (algorithm != GDN_BWD_AUTO && algorithm != GDN_BWD_TOKEN && algorithm != GDN_BWD_CHUNKED)
+        return gdn::fail(GDN_ERR_ARG, "gdn_prefill_bwd_set_algorithm: unknown algorithm %d", algorithm);
+    gdn::t_bwd_algo = algorithm;
+    return GDN_OK;
+}
+
 extern "C" size_t gdn_prefill_bwd_workspace_bytes(int B, int T, int H, int dk, int dv) {
     if (B <= 0 || T <= 0 || H <= 0 || !(dk == 64 || dk == 128) || !(dv == 64 || dv == 128)) return 0;
+    if (gdn::bwd_chunked()) return gdn::prefill_bwd_chunked_workspace(B, T, H, dk, dv);
     return gdn::bwd_ws(static_cast<size_t>(B) * H, T, dk, dv, gdn::bwd_window(T)).total;
 }
 
@@ -547,6 +588,11 @@ extern "C" int gdn_prefill_bwd(const void* q, const void* k, const void* v, cons
     if (!aligned16(workspace)) return fail(GDN_ERR_ALIGN, "gdn_prefill_bwd: workspace must be 16-byte aligned");
     int st = check_sm100();
     if (st != GDN_OK) return st;
+    if (bwd_chunked())
+        return prefill_bwd_chunked(q, k, v, A_log, a, b_logits, gate_dtype, dt_bias, dt_bias_vec, mask, state_in, dO,
+                                   do_dtype, dS_final, dq, dk, dv, da, db, dA_log, ddt_bias, dstate_in, B, T, H, dkd,
+                                   dvd, scale == 0.f ? 1.f / sqrtf(static_cast<float>(dkd)) : scale, workspace,
+                                   static_cast<cudaStream_t>(stream));
     BwdArgs ar;
     ar.q = static_cast<const uint16_t*>(q);
     ar.k = static_cast<const uint16_t*>(k);

@@ -272,11 +272,13 @@ def prefill_varlen(q, k, v, A_log, a, b_logits, cu_seqlens, *, max_len=None, dt_
 
 
 def prefill_backward(q, k, v, A_log, a, b_logits, dO, *, dt_bias=0.0, mask=None, state_in=None, dS_final=None,
-                     scale=0.0, need_dstate=True, window=None):
+                     scale=0.0, need_dstate=True, window=None, algorithm=None):
     """Gradients of ``prefill`` (gdn_prefill_bwd): q, k [B,H,T,dk], v [B,H,T,dv] bf16
     (layout "bhtd", Hqk == Hv), gates as ``prefill``, dO [B,H,T,dv] (bf16 or f32),
-    dS_final [B,H,dk,dv] or None.  ``window``: tokens per window of the windowed
-    backward (None: automatic, max(256, sqrt T)).  Returns a dict of fp32 tensors
+    dS_final [B,H,dk,dv] or None.  ``algorithm``: "token" (token-recurrent, in
+    windows), "chunked" (64-token chunks) or None (the library's choice).
+    ``window``: tokens per window of the token-recurrent backward (None: automatic,
+    max(256, sqrt T)).  Returns a dict of fp32 tensors
     dq, dk, dv, da, db, dA_log [H], ddt_bias ([H] for a per-head dt_bias, a scalar
     tensor otherwise) and dstate_in (or None)."""
     for name, t in (("q", q), ("k", k), ("v", v)):
@@ -298,8 +300,11 @@ def prefill_backward(q, k, v, A_log, a, b_logits, dO, *, dt_bias=0.0, mask=None,
              ddt_bias=torch.empty(H, **f32),
              dstate_in=torch.empty(B, H, dk, dv, **f32) if need_dstate else None)
     _need(window is None or int(window) > 0, f"window must be a positive token count, got {window!r}")
+    algos = {None: 0, "token": 1, "chunked": 2}
+    _need(algorithm in algos, f"algorithm must be None, 'token' or 'chunked', got {algorithm!r}")
     lib = _lib.lib()
     _lib.call("gdn_prefill_bwd_set_window", 0 if window is None else int(window))
+    _lib.call("gdn_prefill_bwd_set_algorithm", algos[algorithm])
     try:
         ws_bytes = lib.gdn_prefill_bwd_workspace_bytes(B, T, H, dk, dv)
         ws = torch.empty(max(int(ws_bytes), 1), dtype=torch.uint8, device=q.device)
@@ -310,6 +315,7 @@ def prefill_backward(q, k, v, A_log, a, b_logits, dO, *, dt_bias=0.0, mask=None,
                   int(ws_bytes), _stream())
     finally:
         _lib.call("gdn_prefill_bwd_set_window", 0)
+        _lib.call("gdn_prefill_bwd_set_algorithm", 0)
     if dt_vec is None:
         g["ddt_bias"] = g["ddt_bias"].sum()
     return g

@@ -291,9 +291,9 @@ int gdn_prefill_host(const void* q, const void* k, const void* v,
 /*
  * Gradients of the prefill (training): dq, dk, dv, da, db, dA_log, ddt_bias and
  * the initial state, given dO (and optionally the gradient of the final state).
- * No reference counterpart (the reference has no backward).  Token-recurrent
- * derivative of the same recurrence (per token S' = g S, r = S'^T k,
- * d = b'(v - r), S <- S' + k d^T, o = m scale q^T S), fp32 on CUDA cores.
+ * No reference counterpart (the reference has no backward).  The derivative of
+ * the same recurrence (per token S' = g S, r = S'^T k, d = b'(v - r),
+ * S <- S' + k d^T, o = m scale q^T S), computed in fp32.
  *   q, k bf16 [B, H, T, dk]; v bf16 [B, H, T, dv]   (layout BHTD, Hqk == Hv)
  *   A_log f32 [H]; a, b_logits [B, H, T] in gate_dtype; dt_bias / dt_bias_vec as
  *   gdn_prefill_fwd; mask f32 [B, T] or NULL; state_in f32 [B, H, dk, dv] or NULL
@@ -301,18 +301,35 @@ int gdn_prefill_host(const void* q, const void* k, const void* v,
  *   dq, dk f32 [B, H, T, dk]; dv f32 [B, H, T, dv]; da, db f32 [B, H, T]
  *   dA_log, ddt_bias f32 [H] (per head; for a scalar dt_bias sum them);
  *   dstate_in f32 [B, H, dk, dv] or NULL.
- * dk, dv in {64, 128}.  The sequence is processed in token windows, last first: a
- * checkpoint pass stores the state at every window start, and only one window's
- * per-token states are held at a time.  Workspace:
- * gdn_prefill_bwd_workspace_bytes(B, T, H, dk, dv), about B * H * dk * dv * 4 * (T / W + W)
- * bytes for windows of W tokens (config 1: 1.2 GB), 16-byte aligned.  The window is
- * max(256, sqrt T) tokens, or the calling thread's gdn_prefill_bwd_set_window; the
- * workspace size and the call must see the same setting.  No reference counterpart.
+ * dk, dv in {64, 128}.  Two algorithms (gdn_prefill_bwd_set_algorithm):
+ *   chunked (the default): per 64-token chunk, the chunk's matrices and the
+ *     per-token gradients on tcgen05 (bf16 hi/lo operands, fp32 accumulate) from
+ *     the state at every chunk start and its gradient at every chunk end, which two
+ *     recurrences over the chunks produce; q, k, v, dO, dq, dk, dv 16-byte aligned
+ *     (GDN_ERR_ALIGN).  Workspace about B H T (dk dv / 32 + 2 dv + 200) 4 bytes
+ *     (config 1: 1.0 GB);
+ *   token-recurrent: fp32 on CUDA cores, in token windows, last first: a checkpoint
+ *     pass stores the state at every window start, and only one window's per-token
+ *     states are held at a time.  Workspace about B H dk dv 4 (T / W + W) bytes for
+ *     windows of W tokens (config 1: 1.2 GB).  The window is max(256, sqrt T)
+ *     tokens, or the calling thread's gdn_prefill_bwd_set_window.
+ * Workspace: gdn_prefill_bwd_workspace_bytes(B, T, H, dk, dv), 16-byte aligned; the
+ * workspace size and the call must see the same algorithm and window settings.
  */
 size_t gdn_prefill_bwd_workspace_bytes(int B, int T, int H, int dk, int dv);
 /* The calling thread's window for gdn_prefill_bwd, in tokens (0 = automatic).
  * GDN_ERR_ARG for a negative value. */
 int gdn_prefill_bwd_set_window(int tokens);
+/* The calling thread's backward algorithm:
+ *   GDN_BWD_TOKEN    the token-recurrent windows above;
+ *   GDN_BWD_CHUNKED  chunk by chunk (64 tokens): only the state at every chunk start and
+ *                    its gradient at every chunk end are carried, the per-token gradients
+ *                    come from chunk-local products (workspace about
+ *                    B * H * T * (dk dv / 32 + 2 dv + 200) * 4 bytes; no windows);
+ *   GDN_BWD_AUTO     the library's choice (the default): chunked.
+ * The workspace size and the call must see the same setting.  GDN_ERR_ARG otherwise. */
+enum { GDN_BWD_AUTO = 0, GDN_BWD_TOKEN = 1, GDN_BWD_CHUNKED = 2 };
+int gdn_prefill_bwd_set_algorithm(int algorithm);
 int gdn_prefill_bwd(const void* q, const void* k, const void* v, const float* A_log,
                     const void* a, const void* b_logits, int gate_dtype, float dt_bias,
                     const float* dt_bias_vec, const float* mask, const float* state_in,

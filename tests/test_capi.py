@@ -238,18 +238,27 @@ def test_prefill_bwd_rejects(lib):
     assert call(wsb=16) == _lib.GDN_ERR_SHAPE
     assert call(ws=ODD) == _lib.GDN_ERR_ALIGN
     assert lib.gdn_prefill_bwd_workspace_bytes(1, 64, 2, 96, 64) == 0
-    # windowed: checkpoints plus one window of per-token states, not every token's state
+    # chunked (the default): per 64-token chunk the state entering it, its gradient
+    # leaving it, the d and dd rows and the chunk's 64 x 64 matrices
+    n1 = 4 * 16 * 4096 // 64
     c1 = lib.gdn_prefill_bwd_workspace_bytes(4, 4096, 16, 128, 128)
-    assert c1 <= 1.5e9, c1                                   # config 1 (was B H T dk dv 4 = 17.2 GB)
-    c4 = lib.gdn_prefill_bwd_workspace_bytes(8, 32768, 32, 128, 128)
-    assert c4 <= 8e9, c4                                     # config 4 fits one GPU (was 275 GB)
-    assert _lib.call_status("gdn_prefill_bwd_set_window", -1) == _lib.GDN_ERR_ARG
-    assert _lib.call_status("gdn_prefill_bwd_set_window", 64) == _lib.GDN_OK
+    assert n1 * (2 * 128 * 128 + 2 * 64 * 128 + 3 * 64 * 64) * 4 <= c1 <= 1.1e9, c1   # config 1
+    assert _lib.call_status("gdn_prefill_bwd_set_algorithm", 3) == _lib.GDN_ERR_ARG
+    assert _lib.call_status("gdn_prefill_bwd_set_algorithm", _lib.GDN_BWD_TOKEN) == _lib.GDN_OK
     try:
+        # token-recurrent in windows: checkpoints plus one window of per-token states
+        t1 = lib.gdn_prefill_bwd_workspace_bytes(4, 4096, 16, 128, 128)
+        assert t1 <= 1.5e9, t1                               # config 1 (one window: 17.2 GB)
+        t4 = lib.gdn_prefill_bwd_workspace_bytes(8, 32768, 32, 128, 128)
+        assert t4 <= 8e9, t4                                 # config 4 (one window: 275 GB)
+        assert _lib.call_status("gdn_prefill_bwd_set_window", -1) == _lib.GDN_ERR_ARG
+        assert _lib.call_status("gdn_prefill_bwd_set_window", 64) == _lib.GDN_OK
         small = lib.gdn_prefill_bwd_workspace_bytes(4, 4096, 16, 128, 128)
-        assert small < c1                                    # 64-token windows hold fewer states
+        assert small < t1                                    # 64-token windows hold fewer states
     finally:
         _lib.call_status("gdn_prefill_bwd_set_window", 0)
+        _lib.call_status("gdn_prefill_bwd_set_algorithm", _lib.GDN_BWD_AUTO)
+    assert lib.gdn_prefill_bwd_workspace_bytes(4, 4096, 16, 128, 128) == c1
 
 
 def test_prefill_host_plan(lib):

@@ -1,8 +1,9 @@
 """Prefill backward (gdn_prefill_bwd) against the oracle's hand-written
 derivative (oracle prefill_backward, itself pinned to finite differences),
-in float64 on the same bf16-quantised inputs.  The kernels run the recurrence
-in fp32: every gradient must match to a relative max error of 1e-3 of its
-own magnitude."""
+in float64 on the same bf16-quantised inputs, for both algorithms: the
+chunked one (tcgen05 products on bf16 hi/lo operands, fp32 accumulation) and
+the token-recurrent one (fp32 on CUDA cores).  Every gradient must match to a
+relative max error of 1e-3 of its own magnitude."""
 import math
 
 import numpy as np
@@ -18,18 +19,21 @@ def _rel(got, want):
     return float(np.abs(got - want).max() / max(np.abs(want).max(), 1e-12))
 
 
-@pytest.mark.parametrize("window", [None, 32])
+@pytest.mark.parametrize("algorithm,window", [("token", None), ("token", 32), ("chunked", None)])
 @pytest.mark.parametrize("B,H,T,dk,dv,do_bf16", [(2, 2, 100, 64, 64, False), (1, 3, 130, 128, 128, True),
                                                   (1, 2, 70, 128, 64, False), (2, 1, 65, 64, 128, True)])
-def test_prefill_bwd_vs_oracle(cuda_device, B, H, T, dk, dv, do_bf16, window):
-    """window=32 runs the backward in several token windows (the last one ragged) from
-    checkpoints of the state at every window start."""
+def test_prefill_bwd_vs_oracle(cuda_device, B, H, T, dk, dv, do_bf16, algorithm, window):
+    """window=32 runs the token-recurrent backward in several token windows (the last one
+    ragged) from checkpoints of the state at every window start; "chunked" runs the
+    64-token chunk form (every T here ends in a ragged chunk).  The mask zeroes tokens
+    inside a chunk as well as at the end."""
     import torch
     from gdn_18646_b200 import ops
     rng = np.random.default_rng(B * 100 + T + dk + dv)
     inp = O.make_prefill_inputs(7 + T, B, T, H, dk, dv, gate_dtype="f32", state_std=0.05)
     mask = np.ones((B, T), np.float32)
     mask[:, T - 3:] = 0.0
+    mask[0, 20:23] = 0.0
     dtb = (rng.standard_normal(H) * 0.2).astype(np.float32)
     dO = rng.standard_normal((B, H, T, dv)).astype(np.float32)
     if do_bf16:
@@ -43,25 +47,28 @@ def test_prefill_bwd_vs_oracle(cuda_device, B, H, T, dk, dv, do_bf16, window):
     got = ops.prefill_backward(to_dev(inp["q"]), to_dev(inp["k"]), to_dev(inp["v"]), to_dev(inp["A_log"]),
                                to_dev(inp["a"]), to_dev(inp["b"]), dO_t, dt_bias=to_dev(dtb), mask=to_dev(mask),
                                state_in=to_dev(inp["state_in"]), dS_final=to_dev(dSf), scale=inp["scale"],
-                               window=window)
+                               window=window, algorithm=algorithm)
     torch.cuda.synchronize()
     for name in ("dq", "dk", "dv", "da", "db", "dA_log", "ddt_bias", "dstate_in"):
         err = _rel(to_np(got[name]).astype(np.float64), ref[name])
         assert err < 1e-3, f"{name}: relative max error {err:.2e}"
 
 
-def test_prefill_bwd_scalar_dt_bias_and_no_state(cuda_device):
-    """Scalar dt_bias (its gradient summed over heads), no initial state, no mask."""
+@pytest.mark.parametrize("algorithm", ["token", "chunked"])
+def test_prefill_bwd_scalar_dt_bias_and_no_state(cuda_device, algorithm):
+    """Scalar dt_bias (its gradient summed over heads), no initial state, no mask,
+    no final-state gradient, T a multiple of the chunk."""
     import torch
     from gdn_18646_b200 import ops
-    B, H, T, dk, dv = 1, 2, 80, 64, 64
+    B, H, T, dk, dv = 1, 2, 128, 64, 64
     inp = O.make_prefill_inputs(3, B, T, H, dk, dv, gate_dtype="f32")
     rng = np.random.default_rng(4)
     dO = rng.standard_normal((B, H, T, dv)).astype(np.float32)
     ref = O.prefill_backward(inp["q"], inp["k"], inp["v"], inp["A_log"], inp["a"], 0.3, inp["b"], np.ones((B, T)),
                              dO, scale=inp["scale"])
     got = ops.prefill_backward(to_dev(inp["q"]), to_dev(inp["k"]), to_dev(inp["v"]), to_dev(inp["A_log"]),
-                               to_dev(inp["a"]), to_dev(inp["b"]), to_dev(dO), dt_bias=0.3, scale=inp["scale"])
+                               to_dev(inp["a"]), to_dev(inp["b"]), to_dev(dO), dt_bias=0.3, scale=inp["scale"],
+                               algorithm=algorithm)
     torch.cuda.synchronize()
     assert _rel(float(got["ddt_bias"]), np.array(ref["ddt_bias"].sum())) < 1e-3
     for name in ("dq", "dk", "dv", "da", "db", "dstate_in"):
@@ -109,9 +116,38 @@ def test_prefill_bwd_windows_bit_identical(cuda_device):
     args = (to_dev(inp["q"]), to_dev(inp["k"]), to_dev(inp["v"]), to_dev(inp["A_log"]), to_dev(inp["a"]),
             to_dev(inp["b"]), dO)
     kw = dict(dt_bias=0.1, mask=to_dev(mask), state_in=to_dev(inp["state_in"]), dS_final=dSf, scale=inp["scale"])
-    whole = ops.prefill_backward(*args, **kw, window=T)
+    whole = ops.prefill_backward(*args, **kw, window=T, algorithm="token")
     for w in (32, 40, 64, 199):
-        got = ops.prefill_backward(*args, **kw, window=w)
+        got = ops.prefill_backward(*args, **kw, window=w, algorithm="token")
         torch.cuda.synchronize()
         for name in whole:
             assert torch.equal(got[name], whole[name]), f"{name} differs with {w}-token windows"
+
+
+@pytest.mark.parametrize("B,H,T,dk,dv", [(1, 4, 4096, 128, 128), (2, 2, 1000, 64, 128)])
+def test_prefill_bwd_chunked_vs_token_long(cuda_device, B, H, T, dk, dv):
+    """At sequence lengths the float64 oracle is too slow for, the chunked backward
+    agrees with the token-recurrent one (both fp32, different summation orders) to a
+    relative max error of 1e-3 per gradient, bf16 inputs, a bf16 dO and a masked tail."""
+    import torch
+    from gdn_18646_b200 import ops
+    inp = O.make_prefill_inputs(31 + T, B, T, H, dk, dv, gate_dtype="bf16", state_std=0.05)
+    rng = np.random.default_rng(T)
+    mask = np.ones((B, T), np.float32)
+    mask[-1, T - 77:] = 0.0
+    dO = to_dev(rng.standard_normal((B, H, T, dv)).astype(np.float32)).bfloat16()
+    dSf = to_dev((rng.standard_normal((B, H, dk, dv)) * 0.1).astype(np.float32))
+    a = to_dev(inp["a"])
+    b = to_dev(inp["b"])
+    args = (to_dev(inp["q"]), to_dev(inp["k"]), to_dev(inp["v"]), to_dev(inp["A_log"]), a, b, dO)
+    kw = dict(dt_bias=to_dev((rng.standard_normal(H) * 0.2).astype(np.float32)), mask=to_dev(mask),
+              state_in=to_dev(inp["state_in"]), dS_final=dSf, scale=inp["scale"])
+    want = ops.prefill_backward(*args, **kw, algorithm="token")
+    got = ops.prefill_backward(*args, **kw, algorithm="chunked")
+    torch.cuda.synchronize()
+    for name in want:
+        w = want[name].double().cpu().numpy()
+        g = got[name].double().cpu().numpy()
+        assert np.isfinite(g).all(), name
+        err = _rel(g, w)
+        assert err < 1e-3, f"{name}: relative max error {err:.2e}"
