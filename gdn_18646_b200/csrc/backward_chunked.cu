@@ -69,7 +69,7 @@ struct CbArgs {
     float* dstate_in;                   // [B,H,DK,DV] or null
     // workspace, per chunk cid = bh * n + c
     float* gv;                          // [cid][3][64]: Lambda (in-chunk cumulative log g), b, m
-    float* mp;                          // [cid][3][64][64]: M, P, A
+    uint8_t* rec;                       // [cid]: the chain kernel's record (CRec)
     float* ckS;                         // [cid][DK][DV]: the state entering the chunk
     float* ckD;                         // [cid][64][DV]: the chunk's d rows
     float* ckSb;                        // [cid][DK][DV]: the gradient of the state leaving the chunk
@@ -95,10 +95,6 @@ __device__ __forceinline__ void split_store8(uint8_t* hi, uint8_t* lo, const flo
     *reinterpret_cast<uint4*>(hi) = make_uint4(h[0], h[1], h[2], h[3]);
     *reinterpret_cast<uint4*>(lo) = make_uint4(l[0], l[1], l[2], l[3]);
 }
-__device__ __forceinline__ void load_f8(const float* p, float (&x)[8]) {
-    const float4 a = *reinterpret_cast<const float4*>(p), b = *reinterpret_cast<const float4*>(p + 4);
-    x[0] = a.x; x[1] = a.y; x[2] = a.z; x[3] = a.w; x[4] = b.x; x[5] = b.y; x[6] = b.z; x[7] = b.w;
-}
 __device__ __forceinline__ float warp_sum(float v) {
 #pragma unroll
     for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
@@ -106,14 +102,41 @@ __device__ __forceinline__ float warp_sum(float v) {
 }
 
 // ---------------------------------------------------------------------------
-// Per chunk (one CTA of 128 threads): the gate vectors (Lambda, b, m), then
-// [Q; K] K^T on the tensor cores (bf16 q, k, fp32 accumulate: TMEM lane r < 64
-// holds row r of Q K^T, lane 64 + t row t of K K^T), P = scale (Q K^T) * [G_t/G_s,
-// s <= t] and A = (I + diag(b) M)^-1 with M = (K K^T) * [G_t/G_s, s < t]:
-// the four 16 x 16 diagonal blocks by forward substitution (one column per
-// thread), then the blocks below them by distance from the diagonal,
-// A_ij = -A_ii sum_{j <= k < i} (diag(b) M)_ik A_kj.  Writes A^T, P and A.
-// Padded tokens (past T) get log g = 0, b = m = 0 and zero k, q.
+// Per-chunk record for the chain kernel, written by cb_mats_kernel: bf16 images
+// in the shared-memory operand layout of the tcgen05 products (K-major, 128-byte
+// swizzle, blocks of 64 columns x rows of 128 B), hi/lo pairs for fp32 values, so
+// that the chain kernel moves a chunk's operands with bulk copies.  The forward
+// role reads [KIMG .. FWD_END), the reverse role KIMG, TAB and [FWD_END .. BYTES).
+// ---------------------------------------------------------------------------
+template <int DK, int DV>
+struct CRec {
+    static constexpr int KIMG = 0;                      // k, rows t, DK/64 blocks of 64 rows
+    static constexpr int TAB = KIMG + DK * 128;         // tables [5][64] f32: G, G_L/G, b, G b, m
+    static constexpr int AH = TAB + 2048;               // A, rows t, columns s (hi, lo)
+    static constexpr int AL = AH + 8192;
+    static constexpr int VR = AL + 8192;                // v as stored, bf16 [64][DV], rows past T zero
+    static constexpr int FWD_END = VR + kCC * DV * 2;
+    static constexpr int QGH = FWD_END;                 // scale G_t q_t, rows t (hi, lo)
+    static constexpr int QGL = QGH + DK * 128;
+    static constexpr int ATH = QGL + DK * 128;          // A^T, rows s, columns u
+    static constexpr int ATL = ATH + 8192;
+    static constexpr int PTH = ATL + 8192;              // P^T, rows t, columns u
+    static constexpr int PTL = PTH + 8192;
+    static constexpr int OH = PTL + 8192;               // (m dO)^T, rows v (128, zero past DV), columns u
+    static constexpr int OL = OH + 16384;
+    static constexpr int BYTES = OL + 16384;
+    static constexpr int T_G = 0, T_CF = 64, T_B = 128, T_GB = 192, T_M = 256;   // table rows (floats)
+};
+
+// ---------------------------------------------------------------------------
+// Per chunk (one CTA of 128 threads): the gate vectors (Lambda, b, m) and the
+// chunk's record.  [Q; K] K^T runs on the tensor cores (bf16 q, k, fp32
+// accumulate: TMEM lane r < 64 holds row r of Q K^T, lane 64 + t row t of K K^T);
+// P = scale (Q K^T) * [G_t/G_s, s <= t]; A = (I + diag(b) M)^-1 with
+// M = (K K^T) * [G_t/G_s, s < t]: the four 16 x 16 diagonal blocks by forward
+// substitution (one column per thread), then the blocks below them by distance
+// from the diagonal, A_ij = -A_ii sum_{j <= k < i} (diag(b) M)_ik A_kj.
+// Padded tokens (past T) get log g = 0, b = m = 0 and zero k, q, v, dO.
 // ---------------------------------------------------------------------------
 template <int DK>
 struct MatsSmem {
@@ -121,23 +144,27 @@ struct MatsSmem {
     static constexpr int OFF_QK = 0;                               // [Q; K] image, 128 rows x DK
     static constexpr int OFF_L = OFF_QK + (DK / 64) * QK_KB;       // diag(b) M   [64][65] fp32
     static constexpr int OFF_A = OFF_L + kCC * 65 * 4;             // A           [64][65]
-    static constexpr int OFF_T = OFF_A + kCC * 65 * 4;             // block sums  [3][16][17]
+    static constexpr int OFF_P = OFF_A + kCC * 65 * 4;             // P           [64][65]
+    static constexpr int OFF_T = OFF_P + kCC * 65 * 4;             // block sums  [3][16][17]
     static constexpr int OFF_G = OFF_T + 3 * 16 * 17 * 4;          // Lambda, b, m [3][64]
     static constexpr int OFF_BAR = OFF_G + 3 * kCC * 4;
     static constexpr int BYTES = OFF_BAR + 16 + 1024;
 };
 
-template <int DK>
+template <int DK, int DV>
 __global__ void __launch_bounds__(128) cb_mats_kernel(const CbArgs a) {
     using L = MatsSmem<DK>;
+    using R = CRec<DK, DV>;
     constexpr int CPK = DK / 8;
     extern __shared__ uint8_t smem_raw[];
     uint8_t* sm = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
     float* Ls = reinterpret_cast<float*>(sm + L::OFF_L);
     float* As = reinterpret_cast<float*>(sm + L::OFF_A);
+    float* Ps = reinterpret_cast<float*>(sm + L::OFF_P);
     float* Ts = reinterpret_cast<float*>(sm + L::OFF_T);
     float* lam = reinterpret_cast<float*>(sm + L::OFF_G);
     float* bms = lam + kCC;
+    float* mks = lam + 2 * kCC;
     uint64_t* bar = reinterpret_cast<uint64_t*>(sm + L::OFF_BAR);
     uint32_t* tslot = reinterpret_cast<uint32_t*>(bar + 1);
     const int cid = blockIdx.x, bh = cid / a.n, c = cid - bh * a.n;
@@ -145,6 +172,7 @@ __global__ void __launch_bounds__(128) cb_mats_kernel(const CbArgs a) {
     const int t0 = c * kCC, nt = min(kCC, a.T - t0);
     const int tid = threadIdx.x, warp = tid >> 5;
     const long tokbase = static_cast<long>(bh) * a.T + t0;
+    uint8_t* rec = a.rec + static_cast<long>(cid) * R::BYTES;
 
     if (tid == 0) {
         mbar_init(bar, 1);
@@ -173,6 +201,7 @@ __global__ void __launch_bounds__(128) cb_mats_kernel(const CbArgs a) {
         }
         lam[t] = lg;
         bms[t] = bm;
+        mks[t] = m;
         gv[kCC + t] = bm;
         gv[2 * kCC + t] = m;
     }
@@ -197,13 +226,34 @@ __global__ void __launch_bounds__(128) cb_mats_kernel(const CbArgs a) {
             lam[t] = s;
         }
     }
+    // v rows and (m dO)^T as stored: independent of the product
+    for (int it = tid; it < kCC * DV / 8; it += 128) {
+        const int t = it / (DV / 8), ch = it - t * (DV / 8);
+        const uint4 u = t < nt ? __ldg(reinterpret_cast<const uint4*>(a.v + (tokbase + t) * DV + ch * 8))
+                               : make_uint4(0u, 0u, 0u, 0u);
+        *reinterpret_cast<uint4*>(rec + R::VR + (t * DV + ch * 8) * 2) = u;
+    }
     __syncthreads();
+    for (int it = tid; it < 8 * 128; it += 128) {
+        const int ch = it >> 7, vr = it & 127;         // rows v of the image, 8 tokens u per item
+        float x[8];
+#pragma unroll
+        for (int i = 0; i < 8; ++i) {
+            const int u = ch * 8 + i;
+            float d = 0.f;
+            if (vr < DV && u < nt) {
+                const long gi = (tokbase + u) * DV + vr;
+                d = mks[u] * (a.do_dtype == GDN_DTYPE_BF16 ? bf16_bits_to_f32(static_cast<const uint16_t*>(a.dO)[gi])
+                                                           : static_cast<const float*>(a.dO)[gi]);
+            }
+            x[i] = d;
+        }
+        const uint32_t off = sw128_chunk(vr, ch);
+        split_store8(rec + R::OH + off, rec + R::OL + off, x);
+    }
     if (tid < kCC) gv[tid] = lam[tid];
     const bool ok = mbar_wait(bar, 0, a.err);
     tc_fence_after();
-    float* At = a.mp + static_cast<long>(cid) * 3 * kCC * kCC;
-    float* P = At + kCC * kCC;
-    float* A = P + kCC * kCC;
     {
         // row r of the product: P row r (r < 64) or diag(b) M row r - 64
         const int r = tid, t = r & (kCC - 1);
@@ -218,23 +268,12 @@ __global__ void __launch_bounds__(128) cb_mats_kernel(const CbArgs a) {
 #pragma unroll
                 for (int i = 0; i < 32; ++i) x[i] = 0.f;
             }
-            if (r < kCC) {
+            float* dst = r < kCC ? Ps : Ls;
 #pragma unroll
-                for (int i = 0; i < 32; i += 4) {
-                    float o[4];
-#pragma unroll
-                    for (int q = 0; q < 4; ++q) {
-                        const int s = cb + i + q;
-                        o[q] = s <= t ? a.scale * x[i + q] * expf(lt - lam[s]) : 0.f;
-                    }
-                    *reinterpret_cast<float4*>(P + t * kCC + cb + i) = make_float4(o[0], o[1], o[2], o[3]);
-                }
-            } else {
-#pragma unroll
-                for (int i = 0; i < 32; ++i) {
-                    const int s = cb + i;
-                    Ls[t * 65 + s] = s < t ? bt * x[i] * expf(lt - lam[s]) : 0.f;
-                }
+            for (int i = 0; i < 32; ++i) {
+                const int s = cb + i;
+                dst[t * 65 + s] = r < kCC ? (s <= t ? a.scale * x[i] * expf(lt - lam[s]) : 0.f)
+                                          : (s < t ? bt * x[i] * expf(lt - lam[s]) : 0.f);
             }
         }
     }
@@ -253,8 +292,7 @@ __global__ void __launch_bounds__(128) cb_mats_kernel(const CbArgs a) {
 #pragma unroll
         for (int t = 0; t < 16; ++t) As[(o + t) * 65 + o + col] = x[t];
     }
-    // blocks above the diagonal are zero
-    for (int e = tid; e < kCC * kCC; e += 128) {
+    for (int e = tid; e < kCC * kCC; e += 128) {      // blocks above the diagonal are zero
         const int r = e >> 6, s = e & 63;
         if ((s >> 4) > (r >> 4)) As[r * 65 + s] = 0.f;
     }
@@ -283,12 +321,41 @@ __global__ void __launch_bounds__(128) cb_mats_kernel(const CbArgs a) {
         }
         __syncthreads();
     }
-    for (int e = tid; e < kCC * kCC / 4; e += 128) {
-        const int r = e >> 4, s = (e & 15) * 4;
-        *reinterpret_cast<float4*>(A + r * kCC + s) =
-            make_float4(As[r * 65 + s], As[r * 65 + s + 1], As[r * 65 + s + 2], As[r * 65 + s + 3]);
-        *reinterpret_cast<float4*>(At + r * kCC + s) =
-            make_float4(As[s * 65 + r], As[(s + 1) * 65 + r], As[(s + 2) * 65 + r], As[(s + 3) * 65 + r]);
+    // the record: A, A^T, P^T (hi/lo), k and scale G q images, tables
+    for (int it = tid; it < 3 * 512; it += 128) {
+        const int img = it >> 9, row = (it >> 3) & 63, ch = it & 7;
+        float x[8];
+#pragma unroll
+        for (int i = 0; i < 8; ++i) {
+            const int cc = ch * 8 + i;
+            x[i] = img == 0 ? As[row * 65 + cc] : (img == 1 ? As[cc * 65 + row] : Ps[cc * 65 + row]);
+        }
+        const uint32_t off = sw128_chunk(row, ch);
+        const int hi = img == 0 ? R::AH : (img == 1 ? R::ATH : R::PTH);
+        const int lo = img == 0 ? R::AL : (img == 1 ? R::ATL : R::PTL);
+        split_store8(rec + hi + off, rec + lo + off, x);
+    }
+    for (int it = tid; it < (DK / 64) * 512; it += 128) {
+        const int b = it >> 9, t = (it >> 3) & 63, ch = it & 7;
+        const uint4 kq = *reinterpret_cast<const uint4*>(sm + L::OFF_QK + b * L::QK_KB + sw128_chunk(kCC + t, ch));
+        *reinterpret_cast<uint4*>(rec + R::KIMG + b * 8192 + sw128_chunk(t, ch)) = kq;
+        const uint4 qq = *reinterpret_cast<const uint4*>(sm + L::OFF_QK + b * L::QK_KB + sw128_chunk(t, ch));
+        float x[8];
+        unpack_bf16x8(qq, x);
+        const float gq = a.scale * expf(lam[t]);
+#pragma unroll
+        for (int i = 0; i < 8; ++i) x[i] *= gq;
+        split_store8(rec + R::QGH + b * 8192 + sw128_chunk(t, ch), rec + R::QGL + b * 8192 + sw128_chunk(t, ch), x);
+    }
+    if (tid < kCC) {
+        const int t = tid;
+        float* tab = reinterpret_cast<float*>(rec + R::TAB);
+        const float G = expf(lam[t]);
+        tab[R::T_G + t] = G;
+        tab[R::T_CF + t] = expf(lam[kCC - 1] - lam[t]);
+        tab[R::T_B + t] = bms[t];
+        tab[R::T_GB + t] = G * bms[t];
+        tab[R::T_M + t] = mks[t];
     }
     tc_fence_before();
     __syncthreads();
@@ -296,398 +363,271 @@ __global__ void __launch_bounds__(128) cb_mats_kernel(const CbArgs a) {
 }
 
 // ---------------------------------------------------------------------------
-// The chunk recurrences, grid (B*H, DV/64), 256 threads.  Thread (rg, col) keeps
-// rows [32 rg, 32 rg + 32) of value column 64 blockIdx.y + col of the state in
-// registers (rg < DK/32); for the per-token passes thread (g, col), g = tid / 64,
-// takes token rows [16 g, 16 g + 16).  The next chunk's operands are loaded into
-// registers while the current chunk computes and are stored to shared memory at
-// its end, so no chunk waits on a global load.  k and q are held in fp32 and read
-// as float4 broadcasts (one per four multiply-adds); the decay factors are tables.
+// The two chunk recurrences in one launch of 2 B H CTAs of 128 threads: CTA
+// bh < B H runs the forward recurrence of (b, h), CTA B H + bh the reverse one
+// (they are independent).  Thread v = TMEM lane v keeps value column v of the
+// state (S or Sb, fp32, DK registers; v >= DV holds zeros).  Per chunk, three
+// tcgen05 rounds with bf16 hi/lo operands, the record of the chunk in shared
+// memory (bulk-copied once the previous chunk's last product has completed, and
+// prefetched into L2 a chunk ahead):
+//   forward  D1 = S^T K^T;  y_t = b_t (v_t - G_t D1_t)  -> D2 = y^T A^T = d^T
+//            U = (d diag(G_L/G))^T K;  S <- G_L S + U
+//   reverse  D1 = Sb^T K^T, Z = (m dO)^T P;  X_t = (G_L/G_t) D1_t + Z_t
+//            D2 = X^T A = dd^T;  U = (-diag(G b) dd)^T K + (m dO)^T diag(scale G) Q
+//            Sb <- G_L Sb + U
+// storing S (Sb) at every chunk start (end) and the d (dd) rows.
 // ---------------------------------------------------------------------------
-template <int DK>
-struct RecSmem {
-    static constexpr int RG = DK / 32;
-    static constexpr int KF = 0;                   // k [64][DK] fp32
-    static constexpr int QF = KF + kCC * DK;       // q [64][DK] fp32 (reverse)
-    static constexpr int M0 = QF + kCC * DK;       // A^T (forward) or P (reverse) [64][64]
-    static constexpr int M1 = M0 + kCC * kCC;      // A (reverse)
-    static constexpr int CB = M1 + kCC * kCC;      // v (forward) or dO (reverse), this CTA's 64 columns
-    static constexpr int PART = CB + kCC * 64;     // [RG][64][64] partial row sums over state rows
-    static constexpr int XB = PART + RG * kCC * 64;   // [64][64] y then d (forward), X then dd (reverse)
-    static constexpr int GVR = XB + kCC * 64;      // the next chunk's gate vectors as stored (Lambda, b, m)
-    static constexpr int TB = GVR + 3 * kCC;       // tables: G, G_L/G, b, m
-    static constexpr int FLOATS = TB + 4 * kCC;
-    static constexpr int BYTES = FLOATS * 4;
+template <int DK, int DV>
+struct ChainSmem {
+    using R = CRec<DK, DV>;
+    static constexpr int SB = (DK / 64) * 16384;             // state image (hi or lo): 128 rows x DK
+    static constexpr int OFF_SH = 0, OFF_SL = SB;
+    static constexpr int OFF_XH = 2 * SB, OFF_XL = OFF_XH + 16384;   // 128 rows x 64 tokens
+    static constexpr int OFF_REC = OFF_XL + 16384;
+    static constexpr int REV_BASE = R::TAB + 2048;           // reverse part of the record in shared memory
+    static constexpr int REC_FWD = R::FWD_END, REC_REV = REV_BASE + R::BYTES - R::FWD_END;
+    static constexpr int REC = REC_FWD > REC_REV ? REC_FWD : REC_REV;
+    static constexpr int OFF_BAR = OFF_REC + REC;
+    static constexpr int BYTES = OFF_BAR + 64 + 1024;
+    static constexpr int rev(int rec_off) { return REV_BASE + rec_off - R::FWD_END; }
+    static_assert(BYTES <= 232448, "shared memory");
 };
 
-__device__ __forceinline__ void bf8_to_f32(const uint4 u, float* dst) {
-    float x[8];
-    unpack_bf16x8(u, x);
-    *reinterpret_cast<float4*>(dst) = make_float4(x[0], x[1], x[2], x[3]);
-    *reinterpret_cast<float4*>(dst + 4) = make_float4(x[4], x[5], x[6], x[7]);
-}
-
-// The tables of the chunk whose gate vectors are in GVR.
-__device__ __forceinline__ void rec_tables(float* sm_f, int gvr, int tb, int tid) {
-    if (tid < kCC) {
-        const float l = sm_f[gvr + tid], lL = sm_f[gvr + kCC - 1];
-        sm_f[tb + tid] = expf(l);
-        sm_f[tb + kCC + tid] = expf(lL - l);
-        sm_f[tb + 2 * kCC + tid] = sm_f[gvr + kCC + tid];
-        sm_f[tb + 3 * kCC + tid] = sm_f[gvr + 2 * kCC + tid];
-    }
-}
-
 template <int DK, int DV>
-__global__ void __launch_bounds__(256, 1) cb_forward_kernel(const CbArgs a) {
-    using L = RecSmem<DK>;
-    constexpr int RG = L::RG, NK = DK / 32;        // k pieces (8 bf16) per thread
-    extern __shared__ float smf[];
-    float* KF = smf + L::KF;
-    float* At = smf + L::M0;
-    float* Vb = smf + L::CB;
-    float* part = smf + L::PART;
-    float* XB = smf + L::XB;
-    const float* Gt_ = smf + L::TB;
-    const float* CF = smf + L::TB + kCC;
-    const float* Bt = smf + L::TB + 2 * kCC;
-    const int bh = blockIdx.x, tid = threadIdx.x, col = tid & 63, rg = tid >> 6;
-    const int j = blockIdx.y * 64 + col;
-    const bool rows_ok = rg < RG;
+__global__ void __launch_bounds__(128, 1) cb_chain_kernel(const CbArgs a) {
+    using R = CRec<DK, DV>;
+    using L = ChainSmem<DK, DV>;
+    extern __shared__ uint8_t smem_raw[];
+    uint8_t* sm = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+    uint8_t* rs = sm + L::OFF_REC;
+    uint64_t* bars = reinterpret_cast<uint64_t*>(sm + L::OFF_BAR);   // [0] record landed, [1] products done
+    uint32_t* tslot = reinterpret_cast<uint32_t*>(bars + 2);
+    int* dead = reinterpret_cast<int*>(bars + 3);
+    const float* tab = reinterpret_cast<const float*>(rs + R::TAB);
+    const int BH = a.B * a.H;
+    const bool rev = static_cast<int>(blockIdx.x) >= BH;
+    const int bh = rev ? blockIdx.x - BH : blockIdx.x;
+    const int tid = threadIdx.x, warp = tid >> 5, v = tid;
+    const bool col_ok = v < DV;
+    const uint32_t sbase = smem_u32(sm), rbase = sbase + L::OFF_REC;
+    const uint32_t T_D1 = 0, T_Z = 64, T_D2 = 128, T_U = 256;
 
-    uint4 pk[NK], pv[2];
-    float4 pa[4], pg = make_float4(0.f, 0.f, 0.f, 0.f);
-    auto load = [&](int c) {
-        const int t0 = c * kCC, nt = min(kCC, a.T - t0);
-        const long tb = static_cast<long>(bh) * a.T + t0, cid = static_cast<long>(bh) * a.n + c;
-#pragma unroll
-        for (int i = 0; i < NK; ++i) {
-            const int p = tid + 256 * i, row = p / (DK / 8);
-            pk[i] = row < nt ? __ldg(reinterpret_cast<const uint4*>(a.k + tb * DK) + p) : make_uint4(0u, 0u, 0u, 0u);
+    auto rec_of = [&](int c) { return a.rec + (static_cast<long>(bh) * a.n + c) * R::BYTES; };
+    auto issue = [&](int c) {                      // bulk-copy chunk c's record (thread 0)
+        const uint8_t* g = rec_of(c);
+        if (!rev) {
+            mbar_arrive_expect_tx(&bars[0], R::FWD_END);
+            bulk_load(rs, g, R::FWD_END, &bars[0]);
+        } else {
+            mbar_arrive_expect_tx(&bars[0], L::REV_BASE + R::BYTES - R::FWD_END);
+            bulk_load(rs, g, L::REV_BASE, &bars[0]);
+            bulk_load(rs + L::REV_BASE, g + R::FWD_END, R::BYTES - R::FWD_END, &bars[0]);
         }
-#pragma unroll
-        for (int i = 0; i < 2; ++i) {
-            const int p = tid + 256 * i, row = p >> 3;
-            pv[i] = row < nt ? __ldg(reinterpret_cast<const uint4*>(a.v + (tb + row) * DV + blockIdx.y * 64) + (p & 7))
-                             : make_uint4(0u, 0u, 0u, 0u);
-        }
-#pragma unroll
-        for (int i = 0; i < 4; ++i)
-            pa[i] = __ldg(reinterpret_cast<const float4*>(a.mp + (cid * 3 + 0) * kCC * kCC) + tid + 256 * i);
-        if (tid < 48) pg = __ldg(reinterpret_cast<const float4*>(a.gv + cid * 3 * kCC) + tid);
     };
-    auto store = [&]() {
-#pragma unroll
-        for (int i = 0; i < NK; ++i) bf8_to_f32(pk[i], KF + (tid + 256 * i) * 8);
-#pragma unroll
-        for (int i = 0; i < 2; ++i) {
-            const int p = tid + 256 * i;
-            bf8_to_f32(pv[i], Vb + (p >> 3) * 64 + (p & 7) * 8);
+    auto prefetch = [&](int c) {
+        const uint8_t* g = rec_of(c);
+        if (!rev) {
+            bulk_prefetch_l2(g, R::FWD_END);
+        } else {
+            bulk_prefetch_l2(g, L::REV_BASE);
+            bulk_prefetch_l2(g + R::FWD_END, R::BYTES - R::FWD_END);
         }
-#pragma unroll
-        for (int i = 0; i < 4; ++i) reinterpret_cast<float4*>(At)[tid + 256 * i] = pa[i];
-        if (tid < 48) reinterpret_cast<float4*>(smf + L::GVR)[tid] = pg;
-        __syncthreads();
-        rec_tables(smf, L::GVR, L::TB, tid);
-        __syncthreads();
     };
 
-    float S[32];
-    const long s0 = static_cast<long>(bh) * DK * DV;
+    if (tid == 0) {
+        mbar_init(&bars[0], 1);
+        mbar_init(&bars[1], 1);
+        *dead = 0;
+        fence_mbar_init();
+        issue(rev ? a.n - 1 : 0);
+    }
+    if (warp == 0) tmem_alloc(tslot, 512);
+    float S[DK];
+    {
+        const float* src = rev ? a.dS_final : a.state_in;
+        const long s0 = static_cast<long>(bh) * DK * DV;
 #pragma unroll
-    for (int i = 0; i < 32; ++i)
-        S[i] = (rows_ok && a.state_in) ? a.state_in[s0 + static_cast<long>(rg * 32 + i) * DV + j] : 0.f;
-    load(0);
-    store();
+        for (int d = 0; d < DK; ++d) S[d] = (src && col_ok) ? src[s0 + static_cast<long>(d) * DV + v] : 0.f;
+    }
+    tc_fence_before();
+    __syncthreads();
+    tc_fence_after();
+    const uint32_t tmem = *tslot, lane_t = tmem + (static_cast<uint32_t>(warp * 32) << 16);
+    uint32_t mph = 0;                              // parity of the next products-done phase
+    bool ok = true;
+    auto mma_wait = [&]() {
+        if (!mbar_wait(&bars[1], mph, a.err)) ok = false;
+        mph ^= 1u;
+        tc_fence_after();
+    };
+    // columns 32 j .. 32 j + 31 of row v of a 64-column image, split into hi/lo
+    auto put32 = [&](uint32_t off_h, uint32_t off_l, int j, const float (&x)[32]) {
+#pragma unroll
+        for (int q = 0; q < 4; ++q) {
+            float y[8];
+#pragma unroll
+            for (int i = 0; i < 8; ++i) y[i] = x[q * 8 + i];
+            split_store8(sm + off_h + sw128_chunk(v, 4 * j + q), sm + off_l + sw128_chunk(v, 4 * j + q), y);
+        }
+    };
+
 #pragma unroll 1
-    for (int c = 0; c < a.n; ++c) {
+    for (int step = 0; step < a.n; ++step) {
+        const int c = rev ? a.n - 1 - step : step;
         const long cid = static_cast<long>(bh) * a.n + c;
-        if (c + 1 < a.n) load(c + 1);
-        if (rows_ok) {
-            float* ck = a.ckS + cid * DK * DV + static_cast<long>(rg * 32) * DV + j;
-#pragma unroll
-            for (int i = 0; i < 32; ++i) ck[static_cast<long>(i) * DV] = S[i];
-            // (K S) partials over this thread's 32 rows, four tokens at a time
-#pragma unroll 1
-            for (int t = 0; t < kCC; t += 4) {
-                float acc[4][2] = {{0.f, 0.f}, {0.f, 0.f}, {0.f, 0.f}, {0.f, 0.f}};
-#pragma unroll
-                for (int i = 0; i < 32; i += 4)
-#pragma unroll
-                    for (int u = 0; u < 4; ++u) {
-                        const float4 k4 = *reinterpret_cast<const float4*>(KF + (t + u) * DK + rg * 32 + i);
-                        acc[u][0] = fmaf(k4.x, S[i], fmaf(k4.y, S[i + 1], acc[u][0]));
-                        acc[u][1] = fmaf(k4.z, S[i + 2], fmaf(k4.w, S[i + 3], acc[u][1]));
-                    }
-#pragma unroll
-                for (int u = 0; u < 4; ++u) part[(rg * kCC + t + u) * 64 + col] = acc[u][0] + acc[u][1];
-            }
-        }
-        __syncthreads();
-        // y = b (v - G K S), rows [16 rg, 16 rg + 16)
-#pragma unroll
-        for (int r = 0; r < 16; ++r) {
-            const int t = rg * 16 + r;
-            float kS = 0.f;
-#pragma unroll
-            for (int g = 0; g < RG; ++g) kS += part[(g * kCC + t) * 64 + col];
-            XB[t * 64 + col] = Bt[t] * (Vb[t * 64 + col] - Gt_[t] * kS);
-        }
-        __syncthreads();
-        // d = A y: A^T rows give a thread's 16 rows as float4 broadcasts (A[t][s] = 0 for s > t)
-        float acc[16];
-#pragma unroll
-        for (int r = 0; r < 16; ++r) acc[r] = 0.f;
-#pragma unroll 2
-        for (int s = 0; s < rg * 16 + 16; ++s) {
-            const float ys = XB[s * 64 + col];
-            const float4* ar = reinterpret_cast<const float4*>(At + s * kCC + rg * 16);
-#pragma unroll
-            for (int q4 = 0; q4 < 4; ++q4) {
-                const float4 a4 = ar[q4];
-                acc[4 * q4] = fmaf(a4.x, ys, acc[4 * q4]);
-                acc[4 * q4 + 1] = fmaf(a4.y, ys, acc[4 * q4 + 1]);
-                acc[4 * q4 + 2] = fmaf(a4.z, ys, acc[4 * q4 + 2]);
-                acc[4 * q4 + 3] = fmaf(a4.w, ys, acc[4 * q4 + 3]);
-            }
-        }
-        __syncthreads();
+        if (!mbar_wait(&bars[0], step & 1, a.err)) ok = false;
+        if (tid == 0 && step + 1 < a.n) prefetch(rev ? c - 1 : c + 1);
+        // ---- the state entering (forward) or leaving (reverse) the chunk: checkpoint and image
         {
-            float* ckd = a.ckD + cid * kCC * DV + j;
+            float* ck = (rev ? a.ckSb : a.ckS) + cid * DK * DV + v;
+            if (col_ok) {
 #pragma unroll
-            for (int r = 0; r < 16; ++r) {
-                XB[(rg * 16 + r) * 64 + col] = acc[r];
-                ckd[static_cast<long>(rg * 16 + r) * DV] = acc[r];
+                for (int d = 0; d < DK; ++d) ck[static_cast<long>(d) * DV] = S[d];
             }
+#pragma unroll
+            for (int b = 0; b < DK / 64; ++b)
+#pragma unroll
+                for (int ch = 0; ch < 8; ++ch) {
+                    float y[8];
+#pragma unroll
+                    for (int i = 0; i < 8; ++i) y[i] = S[b * 64 + ch * 8 + i];
+                    const uint32_t off = b * 16384 + sw128_chunk(v, ch);
+                    split_store8(sm + L::OFF_SH + off, sm + L::OFF_SL + off, y);
+                }
         }
+        fence_async_smem();
         __syncthreads();
-        // S <- G_L S + K^T diag(G_L/G) D
-        if (rows_ok) {
-            const float GL = Gt_[kCC - 1];
+        const float GL = tab[R::T_G + kCC - 1];
+        if (tid == 0) {
+            tc_fence_after();
+            constexpr uint32_t id64 = idesc_bf16(128, 64, false, false);
+            const uint32_t sh = sbase + L::OFF_SH, sl = sbase + L::OFF_SL, kim = rbase + R::KIMG;
 #pragma unroll
-            for (int i = 0; i < 32; ++i) S[i] *= GL;
-#pragma unroll 2
-            for (int t = 0; t < kCC; ++t) {
-                const float cf = CF[t] * XB[t * 64 + col];
+            for (int p = 0; p < 2; ++p)
 #pragma unroll
-                for (int i = 0; i < 32; i += 4) {
-                    const float4 k4 = *reinterpret_cast<const float4*>(KF + t * DK + rg * 32 + i);
-                    S[i] = fmaf(k4.x, cf, S[i]);
-                    S[i + 1] = fmaf(k4.y, cf, S[i + 1]);
-                    S[i + 2] = fmaf(k4.z, cf, S[i + 2]);
-                    S[i + 3] = fmaf(k4.w, cf, S[i + 3]);
+                for (int kk = 0; kk < DK / 16; ++kk)
+                    umma_bf16_ss(tmem + T_D1, sdesc_sw128((p ? sl : sh) + (kk >> 2) * 16384 + (kk & 3) * 32, 16, 1024),
+                                 sdesc_sw128(kim + (kk >> 2) * 8192 + (kk & 3) * 32, 16, 1024), id64,
+                                 (p > 0 || kk > 0) ? 1u : 0u);
+            if (rev) {
+                const uint32_t oh = rbase + L::rev(R::OH), ol = rbase + L::rev(R::OL);
+                const uint32_t ph_ = rbase + L::rev(R::PTH), pl = rbase + L::rev(R::PTL);
+                const uint32_t pa[3] = {oh, oh, ol}, pb[3] = {ph_, pl, ph_};
+#pragma unroll
+                for (int p = 0; p < 3; ++p)
+#pragma unroll
+                    for (int kk = 0; kk < 4; ++kk)
+                        umma_bf16_ss(tmem + T_Z, sdesc_sw128(pa[p] + kk * 32, 16, 1024),
+                                     sdesc_sw128(pb[p] + kk * 32, 16, 1024), id64, (p > 0 || kk > 0) ? 1u : 0u);
+            }
+            umma_commit(&bars[1]);
+        }
+        mma_wait();
+        // ---- y (forward) or X (reverse) -> the 64-column image
+#pragma unroll
+        for (int cb = 0; cb < kCC; cb += 32) {
+            float d1[32], z[32];
+            tmem_ld32(lane_t + T_D1 + cb, d1);
+            if (rev) tmem_ld32(lane_t + T_Z + cb, z);
+            tmem_ld_wait();
+#pragma unroll
+            for (int i = 0; i < 32; ++i) {
+                const int t = cb + i;
+                if (!rev) {
+                    const float vt = col_ok ? bf16_bits_to_f32(*reinterpret_cast<const uint16_t*>(
+                                                  rs + R::VR + (t * DV + (col_ok ? v : 0)) * 2))
+                                            : 0.f;
+                    d1[i] = tab[R::T_B + t] * (vt - tab[R::T_G + t] * d1[i]);
+                } else {
+                    d1[i] = fmaf(tab[R::T_CF + t], d1[i], z[i]);
                 }
             }
+            put32(L::OFF_XH, L::OFF_XL, cb >> 5, d1);
         }
+        fence_async_smem();
         __syncthreads();
-        if (c + 1 < a.n) store();
-    }
-}
-
-template <int DK, int DV>
-__global__ void __launch_bounds__(256, 1) cb_reverse_kernel(const CbArgs a) {
-    using L = RecSmem<DK>;
-    constexpr int RG = L::RG, NK = DK / 32;
-    extern __shared__ float smf[];
-    float* KF = smf + L::KF;
-    float* QF = smf + L::QF;
-    float* Pm = smf + L::M0;
-    float* Am = smf + L::M1;
-    float* Ob = smf + L::CB;
-    float* part = smf + L::PART;
-    float* XB = smf + L::XB;
-    const float* Gt_ = smf + L::TB;
-    const float* CF = smf + L::TB + kCC;
-    const float* Bt = smf + L::TB + 2 * kCC;
-    const float* Mt = smf + L::TB + 3 * kCC;
-    const int bh = blockIdx.x, tid = threadIdx.x, col = tid & 63, rg = tid >> 6;
-    const int j = blockIdx.y * 64 + col;
-    const bool rows_ok = rg < RG;
-    const bool do_bf = a.do_dtype == GDN_DTYPE_BF16;
-
-    uint4 pk[NK], pq[NK];
-    float4 pp[4], pa[4], po[4], pg = make_float4(0.f, 0.f, 0.f, 0.f);
-    auto load = [&](int c) {
-        const int t0 = c * kCC, nt = min(kCC, a.T - t0);
-        const long tb = static_cast<long>(bh) * a.T + t0, cid = static_cast<long>(bh) * a.n + c;
+        if (tid == 0) {
+            tc_fence_after();
+            constexpr uint32_t id64 = idesc_bf16(128, 64, false, false);
+            const uint32_t xh = sbase + L::OFF_XH, xl = sbase + L::OFF_XL;
+            const uint32_t bh_ = rev ? rbase + L::rev(R::ATH) : rbase + R::AH;
+            const uint32_t bl_ = rev ? rbase + L::rev(R::ATL) : rbase + R::AL;
+            const uint32_t pa[3] = {xh, xh, xl}, pb[3] = {bh_, bl_, bh_};
 #pragma unroll
-        for (int i = 0; i < NK; ++i) {
-            const int p = tid + 256 * i, row = p / (DK / 8);
-            const bool in = row < nt;
-            pk[i] = in ? __ldg(reinterpret_cast<const uint4*>(a.k + tb * DK) + p) : make_uint4(0u, 0u, 0u, 0u);
-            pq[i] = in ? __ldg(reinterpret_cast<const uint4*>(a.q + tb * DK) + p) : make_uint4(0u, 0u, 0u, 0u);
+            for (int p = 0; p < 3; ++p)
+#pragma unroll
+                for (int kk = 0; kk < 4; ++kk)
+                    umma_bf16_ss(tmem + T_D2, sdesc_sw128(pa[p] + kk * 32, 16, 1024),
+                                 sdesc_sw128(pb[p] + kk * 32, 16, 1024), id64, (p > 0 || kk > 0) ? 1u : 0u);
+            umma_commit(&bars[1]);
         }
-#pragma unroll
-        for (int i = 0; i < 4; ++i) {
-            pp[i] = __ldg(reinterpret_cast<const float4*>(a.mp + (cid * 3 + 1) * kCC * kCC) + tid + 256 * i);
-            pa[i] = __ldg(reinterpret_cast<const float4*>(a.mp + (cid * 3 + 2) * kCC * kCC) + tid + 256 * i);
-        }
-        if (do_bf) {
-#pragma unroll
-            for (int i = 0; i < 2; ++i) {
-                const int p = tid + 256 * i, row = p >> 3;
-                const uint4 u = row < nt ? __ldg(reinterpret_cast<const uint4*>(static_cast<const uint16_t*>(a.dO) +
-                                                                                (tb + row) * DV + blockIdx.y * 64) +
-                                                 (p & 7))
-                                         : make_uint4(0u, 0u, 0u, 0u);
-                po[2 * i] = make_float4(__uint_as_float(u.x), __uint_as_float(u.y), __uint_as_float(u.z),
-                                        __uint_as_float(u.w));
-            }
-        } else {
-#pragma unroll
-            for (int i = 0; i < 4; ++i) {
-                const int p = tid + 256 * i, row = p >> 4;
-                po[i] = row < nt ? __ldg(reinterpret_cast<const float4*>(static_cast<const float*>(a.dO) +
-                                                                        (tb + row) * DV + blockIdx.y * 64) +
-                                         (p & 15))
-                                 : make_float4(0.f, 0.f, 0.f, 0.f);
-            }
-        }
-        if (tid < 48) pg = __ldg(reinterpret_cast<const float4*>(a.gv + cid * 3 * kCC) + tid);
-    };
-    auto store = [&]() {
-#pragma unroll
-        for (int i = 0; i < NK; ++i) {
-            bf8_to_f32(pk[i], KF + (tid + 256 * i) * 8);
-            bf8_to_f32(pq[i], QF + (tid + 256 * i) * 8);
-        }
-#pragma unroll
-        for (int i = 0; i < 4; ++i) {
-            reinterpret_cast<float4*>(Pm)[tid + 256 * i] = pp[i];
-            reinterpret_cast<float4*>(Am)[tid + 256 * i] = pa[i];
-        }
-        if (do_bf) {
-#pragma unroll
-            for (int i = 0; i < 2; ++i) {
-                const int p = tid + 256 * i;
-                const float4 f = po[2 * i];
-                bf8_to_f32(make_uint4(__float_as_uint(f.x), __float_as_uint(f.y), __float_as_uint(f.z),
-                                      __float_as_uint(f.w)),
-                           Ob + (p >> 3) * 64 + (p & 7) * 8);
-            }
-        } else {
-#pragma unroll
-            for (int i = 0; i < 4; ++i) {
-                const int p = tid + 256 * i;
-                *reinterpret_cast<float4*>(Ob + (p >> 4) * 64 + (p & 15) * 4) = po[i];
-            }
-        }
-        if (tid < 48) reinterpret_cast<float4*>(smf + L::GVR)[tid] = pg;
-        __syncthreads();
-        rec_tables(smf, L::GVR, L::TB, tid);
-        __syncthreads();
-    };
-
-    float Sb[32];
-    const long s0 = static_cast<long>(bh) * DK * DV;
-#pragma unroll
-    for (int i = 0; i < 32; ++i)
-        Sb[i] = (rows_ok && a.dS_final) ? a.dS_final[s0 + static_cast<long>(rg * 32 + i) * DV + j] : 0.f;
-    load(a.n - 1);
-    store();
-#pragma unroll 1
-    for (int c = a.n - 1; c >= 0; --c) {
-        const long cid = static_cast<long>(bh) * a.n + c;
-        if (c > 0) load(c - 1);
-        if (rows_ok) {
-            float* ck = a.ckSb + cid * DK * DV + static_cast<long>(rg * 32) * DV + j;
-#pragma unroll
-            for (int i = 0; i < 32; ++i) ck[static_cast<long>(i) * DV] = Sb[i];
-#pragma unroll 1
-            for (int t = 0; t < kCC; t += 4) {
-                float acc[4][2] = {{0.f, 0.f}, {0.f, 0.f}, {0.f, 0.f}, {0.f, 0.f}};
-#pragma unroll
-                for (int i = 0; i < 32; i += 4)
-#pragma unroll
-                    for (int u = 0; u < 4; ++u) {
-                        const float4 k4 = *reinterpret_cast<const float4*>(KF + (t + u) * DK + rg * 32 + i);
-                        acc[u][0] = fmaf(k4.x, Sb[i], fmaf(k4.y, Sb[i + 1], acc[u][0]));
-                        acc[u][1] = fmaf(k4.z, Sb[i + 2], fmaf(k4.w, Sb[i + 3], acc[u][1]));
-                    }
-#pragma unroll
-                for (int u = 0; u < 4; ++u) part[(rg * kCC + t + u) * 64 + col] = acc[u][0] + acc[u][1];
-            }
-        }
-        __syncthreads();
-        // X_t = (G_L/G_t)(K Sb)_t + sum_{u >= t} P_ut m_u dO_u, rows [16 rg, 16 rg + 16)
-        float acc[16];
-#pragma unroll
-        for (int r = 0; r < 16; ++r) {
-            const int t = rg * 16 + r;
-            float kS = 0.f;
-#pragma unroll
-            for (int g = 0; g < RG; ++g) kS += part[(g * kCC + t) * 64 + col];
-            acc[r] = CF[t] * kS;
-        }
-#pragma unroll 2
-        for (int u = rg * 16; u < kCC; ++u) {
-            const float d = Mt[u] * Ob[u * 64 + col];
-            const float4* pr = reinterpret_cast<const float4*>(Pm + u * kCC + rg * 16);
-#pragma unroll
-            for (int q4 = 0; q4 < 4; ++q4) {
-                const float4 p4 = pr[q4];
-                acc[4 * q4] = fmaf(p4.x, d, acc[4 * q4]);
-                acc[4 * q4 + 1] = fmaf(p4.y, d, acc[4 * q4 + 1]);
-                acc[4 * q4 + 2] = fmaf(p4.z, d, acc[4 * q4 + 2]);
-                acc[4 * q4 + 3] = fmaf(p4.w, d, acc[4 * q4 + 3]);
-            }
-        }
-#pragma unroll
-        for (int r = 0; r < 16; ++r) XB[(rg * 16 + r) * 64 + col] = acc[r];
-        __syncthreads();
-        // dd_s = sum_{u >= s} A_us X_u
-#pragma unroll
-        for (int r = 0; r < 16; ++r) acc[r] = 0.f;
-#pragma unroll 2
-        for (int u = rg * 16; u < kCC; ++u) {
-            const float x = XB[u * 64 + col];
-            const float4* ar = reinterpret_cast<const float4*>(Am + u * kCC + rg * 16);
-#pragma unroll
-            for (int q4 = 0; q4 < 4; ++q4) {
-                const float4 a4 = ar[q4];
-                acc[4 * q4] = fmaf(a4.x, x, acc[4 * q4]);
-                acc[4 * q4 + 1] = fmaf(a4.y, x, acc[4 * q4 + 1]);
-                acc[4 * q4 + 2] = fmaf(a4.z, x, acc[4 * q4 + 2]);
-                acc[4 * q4 + 3] = fmaf(a4.w, x, acc[4 * q4 + 3]);
-            }
-        }
-        __syncthreads();
+        mma_wait();
+        // ---- d (forward) or dd (reverse): store, then the scaled image for the state update
         {
-            float* ckdd = a.ckDD + cid * kCC * DV + j;
+            float* ckd = (rev ? a.ckDD : a.ckD) + cid * kCC * DV + v;
 #pragma unroll
-            for (int r = 0; r < 16; ++r) {
-                XB[(rg * 16 + r) * 64 + col] = acc[r];
-                ckdd[static_cast<long>(rg * 16 + r) * DV] = acc[r];
-            }
-        }
-        __syncthreads();
-        // Sb <- G_L Sb + scale (diag(G) Q)^T dO' - (diag(G b) K)^T dd
-        if (rows_ok) {
-            const float GL = Gt_[kCC - 1];
+            for (int cb = 0; cb < kCC; cb += 32) {
+                float d2[32];
+                tmem_ld32(lane_t + T_D2 + cb, d2);
+                tmem_ld_wait();
 #pragma unroll
-            for (int i = 0; i < 32; ++i) Sb[i] *= GL;
-#pragma unroll 2
-            for (int t = 0; t < kCC; ++t) {
-                const float G = Gt_[t];
-                const float cq = a.scale * G * Mt[t] * Ob[t * 64 + col], ck_ = -G * Bt[t] * XB[t * 64 + col];
-#pragma unroll
-                for (int i = 0; i < 32; i += 4) {
-                    const float4 q4 = *reinterpret_cast<const float4*>(QF + t * DK + rg * 32 + i);
-                    const float4 k4 = *reinterpret_cast<const float4*>(KF + t * DK + rg * 32 + i);
-                    Sb[i] = fmaf(q4.x, cq, fmaf(k4.x, ck_, Sb[i]));
-                    Sb[i + 1] = fmaf(q4.y, cq, fmaf(k4.y, ck_, Sb[i + 1]));
-                    Sb[i + 2] = fmaf(q4.z, cq, fmaf(k4.z, ck_, Sb[i + 2]));
-                    Sb[i + 3] = fmaf(q4.w, cq, fmaf(k4.w, ck_, Sb[i + 3]));
+                for (int i = 0; i < 32; ++i) {
+                    const int t = cb + i;
+                    if (col_ok) ckd[static_cast<long>(t) * DV] = d2[i];
+                    d2[i] = rev ? -tab[R::T_GB + t] * d2[i] : tab[R::T_CF + t] * d2[i];
                 }
+                put32(L::OFF_XH, L::OFF_XL, cb >> 5, d2);
             }
         }
+        fence_async_smem();
         __syncthreads();
-        if (c > 0) store();
-    }
-    if (rows_ok && a.dstate_in) {
+        if (tid == 0) {
+            tc_fence_after();
+            constexpr uint32_t idU = idesc_bf16(128, DK, false, true);
+            const uint32_t xh = sbase + L::OFF_XH, xl = sbase + L::OFF_XL, kim = rbase + R::KIMG;
 #pragma unroll
-        for (int i = 0; i < 32; ++i) a.dstate_in[s0 + static_cast<long>(rg * 32 + i) * DV + j] = Sb[i];
+            for (int p = 0; p < 2; ++p)
+#pragma unroll
+                for (int kk = 0; kk < 4; ++kk)
+                    umma_bf16_ss(tmem + T_U, sdesc_sw128((p ? xl : xh) + kk * 32, 16, 1024),
+                                 sdesc_sw128(kim + kk * 2048, 8192, 1024), idU, (p > 0 || kk > 0) ? 1u : 0u);
+            if (rev) {
+                const uint32_t oh = rbase + L::rev(R::OH), ol = rbase + L::rev(R::OL);
+                const uint32_t qh = rbase + L::rev(R::QGH), ql = rbase + L::rev(R::QGL);
+                const uint32_t pa[3] = {oh, oh, ol}, pb[3] = {qh, ql, qh};
+#pragma unroll
+                for (int p = 0; p < 3; ++p)
+#pragma unroll
+                    for (int kk = 0; kk < 4; ++kk)
+                        umma_bf16_ss(tmem + T_U, sdesc_sw128(pa[p] + kk * 32, 16, 1024),
+                                     sdesc_sw128(pb[p] + kk * 2048, 8192, 1024), idU, 1u);
+            }
+            umma_commit(&bars[1]);
+        }
+        mma_wait();
+        if (tid == 0 && step + 1 < a.n) issue(rev ? c - 1 : c + 1);   // the record is no longer read
+        // ---- S <- G_L S + U
+#pragma unroll
+        for (int cb = 0; cb < DK; cb += 32) {
+            float u[32];
+            tmem_ld32(lane_t + T_U + cb, u);
+            tmem_ld_wait();
+#pragma unroll
+            for (int i = 0; i < 32; ++i) S[cb + i] = fmaf(GL, S[cb + i], u[i]);
+        }
+        if (!ok) *dead = 1;
+        tc_fence_before();
+        __syncthreads();
+        if (*dead) break;
     }
+    if (rev && col_ok && a.dstate_in && *dead == 0) {
+        const long s0 = static_cast<long>(bh) * DK * DV;
+#pragma unroll
+        for (int d = 0; d < DK; ++d) a.dstate_in[s0 + static_cast<long>(d) * DV + v] = S[d];
+    }
+    tc_fence_before();
+    __syncthreads();
+    if (warp == 0) tmem_dealloc(tmem, 512);
 }
 
 // ---------------------------------------------------------------------------
@@ -735,7 +675,7 @@ struct GtLayout {
 };
 
 template <int DK, int DV>
-__global__ void __launch_bounds__(256, 1) cb_grads_tc_kernel(const CbArgs a) {
+__global__ void __launch_bounds__(256, 1) cb_grads_tc_kernel(const CbArgs a, int nchunks) {
     using L = GtLayout<DK, DV>;
     constexpr int CPR = DV / 8;                    // 8-value chunks per value row
     constexpr int CPK = DK / 8;                    // per key row
@@ -760,16 +700,24 @@ __global__ void __launch_bounds__(256, 1) cb_grads_tc_kernel(const CbArgs a) {
     float* F1s = reinterpret_cast<float*>(sm + L::OFF_QK);          // [64][64], row t rotated by t
     float* F2s = F1s + 4096;
 
-    const int cid = blockIdx.x, bh = cid / a.n, c = cid - bh * a.n;
-    const int h = bh % a.H;
-    const int t0 = c * kCC, nt = min(kCC, a.T - t0);
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
-    const long tokbase = static_cast<long>(bh) * a.T + t0;
     const uint32_t sbase = smem_u32(sm);
-    const float* ckS = a.ckS + static_cast<long>(cid) * DK * DV;
-    const float* ckSb = a.ckSb + static_cast<long>(cid) * DK * DV;
-    const float* ckD = a.ckD + static_cast<long>(cid) * kCC * DV;
-    const float* ckDD = a.ckDD + static_cast<long>(cid) * kCC * DV;
+    const bool do_bf = a.do_dtype == GDN_DTYPE_BF16;
+    // the inputs of chunk cx -> L2 (issued one chunk ahead)
+    auto prefetch = [&](int cx) {
+        const int bx = cx / a.n, tx0 = (cx - bx * a.n) * kCC, ntx = min(kCC, a.T - tx0);
+        const long tb = static_cast<long>(bx) * a.T + tx0;
+        bulk_prefetch_l2(a.ckS + static_cast<long>(cx) * DK * DV, DK * DV * 4);
+        bulk_prefetch_l2(a.ckSb + static_cast<long>(cx) * DK * DV, DK * DV * 4);
+        bulk_prefetch_l2(a.ckD + static_cast<long>(cx) * kCC * DV, kCC * DV * 4);
+        bulk_prefetch_l2(a.ckDD + static_cast<long>(cx) * kCC * DV, kCC * DV * 4);
+        const uint32_t ob = do_bf ? 2u : 4u;
+        bulk_prefetch_l2(static_cast<const uint8_t*>(a.dO) + tb * DV * ob, ntx * DV * ob);
+        bulk_prefetch_l2(a.q + tb * DK, ntx * DK * 2);
+        bulk_prefetch_l2(a.k + tb * DK, ntx * DK * 2);
+        bulk_prefetch_l2(a.v + tb * DV, ntx * DV * 2);
+        bulk_prefetch_l2(a.gv + static_cast<long>(cx) * 3 * kCC, 3 * kCC * 4);
+    };
 
     if (tid == 0) {
         mbar_init(&bars[0], 1);
@@ -777,8 +725,25 @@ __global__ void __launch_bounds__(256, 1) cb_grads_tc_kernel(const CbArgs a) {
         mbar_init(&bars[2], 1);
         *dead = 0;
         fence_mbar_init();
+        if (static_cast<int>(blockIdx.x) < nchunks) prefetch(blockIdx.x);
     }
     if (warp == 0) tmem_alloc(tslot, 512);
+    tc_fence_before();
+    __syncthreads();
+    tc_fence_after();
+    const uint32_t tmem = *tslot;
+    uint32_t ph = 0;                               // barrier parity of this CTA's current chunk
+#pragma unroll 1
+    for (int cid = blockIdx.x; cid < nchunks; cid += gridDim.x, ph ^= 1u) {
+    const int bh = cid / a.n, c = cid - bh * a.n;
+    const int h = bh % a.H;
+    const int t0 = c * kCC, nt = min(kCC, a.T - t0);
+    const long tokbase = static_cast<long>(bh) * a.T + t0;
+    const float* ckS = a.ckS + static_cast<long>(cid) * DK * DV;
+    const float* ckSb = a.ckSb + static_cast<long>(cid) * DK * DV;
+    const float* ckD = a.ckD + static_cast<long>(cid) * kCC * DV;
+    const float* ckDD = a.ckDD + static_cast<long>(cid) * kCC * DV;
+    if (tid == 0 && cid + static_cast<int>(gridDim.x) < nchunks) prefetch(cid + gridDim.x);
     if (tid < kCC) {
         const float* gv = a.gv + static_cast<long>(cid) * 3 * kCC;
         lam[tid] = gv[tid];
@@ -786,61 +751,109 @@ __global__ void __launch_bounds__(256, 1) cb_grads_tc_kernel(const CbArgs a) {
         bms[tid] = gv[kCC + tid];
         ms[tid] = gv[2 * kCC + tid];
     }
-    tc_fence_before();
     __syncthreads();
-    tc_fence_after();
-    const uint32_t tmem = *tslot;
 
-    // ---- phase A: [dO'; dd; D] and S as bf16 hi/lo images, [Q; K]; dv = b dd; dd . v
-    for (int it = tid; it < 192 * CPR; it += 256) {
-        const int row = it / CPR, ch = it - row * CPR;
-        float x[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
-        float dvp = 0.f;
-        if (row < kCC) {
-            if (row < nt) {
-                const long gi = (tokbase + row) * DV + ch * 8;
-                if (a.do_dtype == GDN_DTYPE_BF16)
-                    unpack_bf16x8(*reinterpret_cast<const uint4*>(static_cast<const uint16_t*>(a.dO) + gi), x);
-                else
-                    load_f8(static_cast<const float*>(a.dO) + gi, x);
-                const float m = ms[row];
+    // ---- phase A: [dO'; dd; D] and S as bf16 hi/lo images, [Q; K]; dv = b dd; dd . v.
+    //      Items in groups whose loads are all issued before any is used.
+    {
+        constexpr int RN = 192 * CPR / 256, RGP = RN >= 6 ? 6 : RN;
 #pragma unroll
-                for (int i = 0; i < 8; ++i) x[i] *= m;
-            }
-        } else if (row < 2 * kCC) {
-            const int t = row - kCC;
-            load_f8(ckDD + t * DV + ch * 8, x);
-            if (t < nt) {
-                const float b = bms[t];
-                float* dst = a.dv + (tokbase + t) * DV + ch * 8;
-                *reinterpret_cast<float4*>(dst) = make_float4(b * x[0], b * x[1], b * x[2], b * x[3]);
-                *reinterpret_cast<float4*>(dst + 4) = make_float4(b * x[4], b * x[5], b * x[6], b * x[7]);
-                float vv[8];
-                unpack_bf16x8(*reinterpret_cast<const uint4*>(a.v + (tokbase + t) * DV + ch * 8), vv);
+        for (int k0 = 0; k0 < RN; k0 += RGP) {
+            float x[RGP][8];
+            uint4 vv[RGP];
 #pragma unroll
-                for (int i = 0; i < 8; ++i) dvp = fmaf(x[i], vv[i], dvp);
+            for (int u = 0; u < RGP; ++u) {
+                const int it = tid + 256 * (k0 + u), row = it / CPR, ch = it - row * CPR;
+                vv[u] = make_uint4(0u, 0u, 0u, 0u);
+#pragma unroll
+                for (int i = 0; i < 8; ++i) x[u][i] = 0.f;
+                if (row < kCC) {
+                    if (row < nt) {
+                        const long gi = (tokbase + row) * DV + ch * 8;
+                        if (do_bf) {
+                            uint4 w = __ldg(reinterpret_cast<const uint4*>(static_cast<const uint16_t*>(a.dO) + gi));
+                            unpack_bf16x8(w, x[u]);
+                        } else {
+                            const float4 f0 = __ldg(reinterpret_cast<const float4*>(static_cast<const float*>(a.dO) + gi));
+                            const float4 f1 =
+                                __ldg(reinterpret_cast<const float4*>(static_cast<const float*>(a.dO) + gi + 4));
+                            x[u][0] = f0.x; x[u][1] = f0.y; x[u][2] = f0.z; x[u][3] = f0.w;
+                            x[u][4] = f1.x; x[u][5] = f1.y; x[u][6] = f1.z; x[u][7] = f1.w;
+                        }
+                    }
+                } else {
+                    const float* src = row < 2 * kCC ? ckDD + (row - kCC) * DV : ckD + (row - 2 * kCC) * DV;
+                    const float4 f0 = __ldg(reinterpret_cast<const float4*>(src + ch * 8));
+                    const float4 f1 = __ldg(reinterpret_cast<const float4*>(src + ch * 8 + 4));
+                    x[u][0] = f0.x; x[u][1] = f0.y; x[u][2] = f0.z; x[u][3] = f0.w;
+                    x[u][4] = f1.x; x[u][5] = f1.y; x[u][6] = f1.z; x[u][7] = f1.w;
+                    if (row < 2 * kCC && row - kCC < nt)
+                        vv[u] = __ldg(reinterpret_cast<const uint4*>(a.v + (tokbase + row - kCC) * DV + ch * 8));
+                }
             }
-        } else {
-            load_f8(ckD + (row - 2 * kCC) * DV + ch * 8, x);
+#pragma unroll
+            for (int u = 0; u < RGP; ++u) {
+                const int it = tid + 256 * (k0 + u), row = it / CPR, ch = it - row * CPR;
+                float dvp = 0.f;
+                if (row < kCC) {
+                    const float m = ms[row];
+#pragma unroll
+                    for (int i = 0; i < 8; ++i) x[u][i] *= m;
+                } else if (row < 2 * kCC && row - kCC < nt) {
+                    const int t = row - kCC;
+                    const float b = bms[t];
+                    float* dst = a.dv + (tokbase + t) * DV + ch * 8;
+                    *reinterpret_cast<float4*>(dst) = make_float4(b * x[u][0], b * x[u][1], b * x[u][2], b * x[u][3]);
+                    *reinterpret_cast<float4*>(dst + 4) =
+                        make_float4(b * x[u][4], b * x[u][5], b * x[u][6], b * x[u][7]);
+                    float v8[8];
+                    unpack_bf16x8(vv[u], v8);
+#pragma unroll
+                    for (int i = 0; i < 8; ++i) dvp = fmaf(x[u][i], v8[i], dvp);
+                }
+#pragma unroll
+                for (int o = CPR / 2; o > 0; o >>= 1) dvp += __shfl_xor_sync(0xffffffffu, dvp, o);
+                if (row >= kCC && row < 2 * kCC && ch == 0) ddv[row - kCC] = dvp;
+                const uint32_t off = (ch >> 3) * L::R_KB + sw128_chunk(row, ch & 7);
+                split_store8(sm + L::OFF_RH + off, sm + L::OFF_RL + off, x[u]);
+            }
+        }
+    }
+    {
+        constexpr int SN = DK * CPR / 256, SGP = SN >= 4 ? 4 : SN;
+#pragma unroll
+        for (int k0 = 0; k0 < SN; k0 += SGP) {
+            float x[SGP][8];
+#pragma unroll
+            for (int u = 0; u < SGP; ++u) {
+                const int it = tid + 256 * (k0 + u), d = it / CPR, ch = it - d * CPR;
+                const float4 f0 = __ldg(reinterpret_cast<const float4*>(ckS + d * DV + ch * 8));
+                const float4 f1 = __ldg(reinterpret_cast<const float4*>(ckS + d * DV + ch * 8 + 4));
+                x[u][0] = f0.x; x[u][1] = f0.y; x[u][2] = f0.z; x[u][3] = f0.w;
+                x[u][4] = f1.x; x[u][5] = f1.y; x[u][6] = f1.z; x[u][7] = f1.w;
+            }
+#pragma unroll
+            for (int u = 0; u < SGP; ++u) {
+                const int it = tid + 256 * (k0 + u), d = it / CPR, ch = it - d * CPR;
+                const uint32_t off = (ch >> 3) * L::S_KB + sw128_chunk(d, ch & 7);
+                split_store8(sm + L::OFF_SH + off, sm + L::OFF_SL + off, x[u]);
+            }
+        }
+    }
+    {
+        constexpr int QN = 128 * CPK / 256;
+        uint4 w[QN];
+#pragma unroll
+        for (int u = 0; u < QN; ++u) {
+            const int it = tid + 256 * u, row = it / CPK, ch = it - row * CPK, t = row & (kCC - 1);
+            w[u] = t < nt ? __ldg(reinterpret_cast<const uint4*>((row < kCC ? a.q : a.k) + (tokbase + t) * DK + ch * 8))
+                          : make_uint4(0u, 0u, 0u, 0u);
         }
 #pragma unroll
-        for (int o = CPR / 2; o > 0; o >>= 1) dvp += __shfl_xor_sync(0xffffffffu, dvp, o);
-        if (row >= kCC && row < 2 * kCC && ch == 0) ddv[row - kCC] = dvp;
-        const uint32_t off = (ch >> 3) * L::R_KB + sw128_chunk(row, ch & 7);
-        split_store8(sm + L::OFF_RH + off, sm + L::OFF_RL + off, x);
-    }
-    for (int it = tid; it < DK * CPR; it += 256) {
-        const int d = it / CPR, ch = it - d * CPR;
-        float x[8];
-        load_f8(ckS + d * DV + ch * 8, x);
-        const uint32_t off = (ch >> 3) * L::S_KB + sw128_chunk(d, ch & 7);
-        split_store8(sm + L::OFF_SH + off, sm + L::OFF_SL + off, x);
-    }
-    for (int it = tid; it < 128 * CPK; it += 256) {
-        const int row = it / CPK, ch = it - row * CPK, t = row & (kCC - 1);
-        uint4 u = make_uint4(0u, 0u, 0u, 0u);
-        if (t < nt) u = *reinterpret_cast<const uint4*>((row < kCC ? a.q : a.k) + (tokbase + t) * DK + ch * 8);
-        *reinterpret_cast<uint4*>(sm + L::OFF_QK + (ch >> 3) * L::QK_KB + sw128_chunk(row, ch & 7)) = u;
+        for (int u = 0; u < QN; ++u) {
+            const int it = tid + 256 * u, row = it / CPK, ch = it - row * CPK;
+            *reinterpret_cast<uint4*>(sm + L::OFF_QK + (ch >> 3) * L::QK_KB + sw128_chunk(row, ch & 7)) = w[u];
+        }
     }
     fence_async_smem();
     __syncthreads();
@@ -872,18 +885,35 @@ __global__ void __launch_bounds__(256, 1) cb_grads_tc_kernel(const CbArgs a) {
     }
 
     // ---- phase B: Sb over the S image once T1 has read it, <S, Sb>, then T2
-    if (!mbar_wait(&bars[0], 0, a.err)) *dead = 1;
+    if (!mbar_wait(&bars[0], ph, a.err)) *dead = 1;
     tc_fence_after();
     float sp = 0.f;
-    for (int it = tid; it < DK * CPR; it += 256) {
-        const int d = it / CPR, ch = it - d * CPR;
-        float x[8], s8[8];
-        load_f8(ckSb + d * DV + ch * 8, x);
-        load_f8(ckS + d * DV + ch * 8, s8);
+    {
+        constexpr int SN = DK * CPR / 256, SGP = SN >= 4 ? 4 : SN;
 #pragma unroll
-        for (int i = 0; i < 8; ++i) sp = fmaf(s8[i], x[i], sp);
-        const uint32_t off = (ch >> 3) * L::S_KB + sw128_chunk(d, ch & 7);
-        split_store8(sm + L::OFF_SH + off, sm + L::OFF_SL + off, x);
+        for (int k0 = 0; k0 < SN; k0 += SGP) {
+            float x[SGP][8], s8[SGP][8];
+#pragma unroll
+            for (int u = 0; u < SGP; ++u) {
+                const int it = tid + 256 * (k0 + u), d = it / CPR, ch = it - d * CPR;
+                const float4 f0 = __ldg(reinterpret_cast<const float4*>(ckSb + d * DV + ch * 8));
+                const float4 f1 = __ldg(reinterpret_cast<const float4*>(ckSb + d * DV + ch * 8 + 4));
+                const float4 g0 = __ldg(reinterpret_cast<const float4*>(ckS + d * DV + ch * 8));
+                const float4 g1 = __ldg(reinterpret_cast<const float4*>(ckS + d * DV + ch * 8 + 4));
+                x[u][0] = f0.x; x[u][1] = f0.y; x[u][2] = f0.z; x[u][3] = f0.w;
+                x[u][4] = f1.x; x[u][5] = f1.y; x[u][6] = f1.z; x[u][7] = f1.w;
+                s8[u][0] = g0.x; s8[u][1] = g0.y; s8[u][2] = g0.z; s8[u][3] = g0.w;
+                s8[u][4] = g1.x; s8[u][5] = g1.y; s8[u][6] = g1.z; s8[u][7] = g1.w;
+            }
+#pragma unroll
+            for (int u = 0; u < SGP; ++u) {
+                const int it = tid + 256 * (k0 + u), d = it / CPR, ch = it - d * CPR;
+#pragma unroll
+                for (int i = 0; i < 8; ++i) sp = fmaf(s8[u][i], x[u][i], sp);
+                const uint32_t off = (ch >> 3) * L::S_KB + sw128_chunk(d, ch & 7);
+                split_store8(sm + L::OFF_SH + off, sm + L::OFF_SL + off, x[u]);
+            }
+        }
     }
     sp = warp_sum(sp);
     if (lane == 0) basep[warp] = sp;
@@ -932,7 +962,8 @@ __global__ void __launch_bounds__(256, 1) cb_grads_tc_kernel(const CbArgs a) {
         const float lt = lam[t], Gt = Gs[t], bt = bms[t];
         float* Fs = side ? F2s : F1s;
         float pre = 0.f, krs = 0.f;
-#pragma unroll 1
+        float cv[kCC];                              // this row's contribution to each token's pair sum
+#pragma unroll
         for (int cb = 0; cb < kCC; cb += 32) {
             float x[32], y[32];
             tmem_ld32(lb + L::T_DD + cb, x);        // dO' D^T row (side 0) or Y = dd D^T row (side 1)
@@ -957,11 +988,25 @@ __global__ void __launch_bounds__(256, 1) cb_grads_tc_kernel(const CbArgs a) {
                 }
                 Fs[t * kCC + ((s + t) & (kCC - 1))] = f;
                 // pair sums: token s gets sum_{s' < s} e_{s'} from rows u >= s (side 0) or u > s (side 1)
-                const float v = warp_sum(in || (side == 0 && s == t) ? pre : 0.f);
-                if (lane == 0) pairp[warp * kCC + s] = v;
+                cv[s] = in ? pre : 0.f;
                 pre += e;
             }
         }
+        // sum cv over the warp's 32 rows by a butterfly reduce-scatter: after the
+        // stage of lane bit o a lane keeps the half of its values selected by that
+        // bit, so lane L ends with the sums for tokens 2L and 2L + 1
+#pragma unroll
+        for (int o = 16, n = kCC; o > 0; o >>= 1, n >>= 1) {
+            const bool up = (lane & o) != 0;
+#pragma unroll
+            for (int i = 0; i < n / 2; ++i) {
+                const float send = up ? cv[i] : cv[i + n / 2];
+                const float keep = up ? cv[i + n / 2] : cv[i];
+                cv[i] = keep + __shfl_xor_sync(0xffffffffu, send, o);
+            }
+        }
+        pairp[warp * kCC + 2 * lane] = cv[0];
+        pairp[warp * kCC + 2 * lane + 1] = cv[1];
         if (side == 0) {
             s_a[t] = Gt * scale * dot;
         } else {
@@ -973,7 +1018,7 @@ __global__ void __launch_bounds__(256, 1) cb_grads_tc_kernel(const CbArgs a) {
     }
 
     // ---- phase C: the T4 operands over the freed images once T2 completed
-    if (tid == 0 && !dead_b && !mbar_wait(&bars[1], 0, a.err)) *dead = 1;
+    if (tid == 0 && !dead_b && !mbar_wait(&bars[1], ph, a.err)) *dead = 1;
     __syncthreads();
     const bool dead_c = *dead != 0;
     tc_fence_after();
@@ -996,6 +1041,7 @@ __global__ void __launch_bounds__(256, 1) cb_grads_tc_kernel(const CbArgs a) {
             split_store8(sm + L::OFF_A1H + off, sm + L::OFF_A1L + off, f1);
             split_store8(sm + L::OFF_A2H + off, sm + L::OFF_A2L + off, f2);
         }
+#pragma unroll
         for (int it = tid; it < 8 * DK; it += 256) {
             const int ch = it / DK, d = it - ch * DK;
             uint16_t kv[8], qv[8];
@@ -1069,7 +1115,7 @@ __global__ void __launch_bounds__(256, 1) cb_grads_tc_kernel(const CbArgs a) {
     }
 
     // ---- phase D: dq, dk (warps w and w + 4 share lanes 32 (w % 4) .. + 31, half the columns each)
-    if (tid == 0 && !dead_c && !mbar_wait(&bars[2], 0, a.err)) *dead = 1;
+    if (tid == 0 && !dead_c && !mbar_wait(&bars[2], ph, a.err)) *dead = 1;
     __syncthreads();
     tc_fence_after();
     if (*dead == 0) {
@@ -1099,23 +1145,29 @@ __global__ void __launch_bounds__(256, 1) cb_grads_tc_kernel(const CbArgs a) {
         }
     }
     tc_fence_before();
-    __syncthreads();
+    __syncthreads();                               // TMEM and shared memory free for the next chunk
+    if (*dead) break;
+    }
     if (warp == 0) tmem_dealloc(tmem, 512);
 }
 
 
-// Workspace of the chunked backward: gate vectors | M, P, A | S checkpoints | d rows |
-// Sb checkpoints | dd rows | dlogg, each 256-byte aligned.
+// Workspace of the chunked backward: gate vectors | records | S checkpoints | d rows |
+// Sb checkpoints | dd rows | dlogg, each 1024-byte aligned.
 struct CbWs {
-    size_t gv, mp, ckS, ckD, ckSb, ckDD, dlogg, total;
+    size_t gv, rec, ckS, ckD, ckSb, ckDD, dlogg, total;
 };
+size_t crec_bytes(int dk, int dv) {
+    if (dk == 128) return dv == 128 ? CRec<128, 128>::BYTES : CRec<128, 64>::BYTES;
+    return dv == 128 ? CRec<64, 128>::BYTES : CRec<64, 64>::BYTES;
+}
 CbWs cb_ws(size_t bh, int T, int dk, int dv) {
     const size_t n = (static_cast<size_t>(T) + kCC - 1) / kCC, nc = bh * n;
-    auto al = [](size_t x) { return (x + 255) / 256 * 256; };
+    auto al = [](size_t x) { return (x + 1023) / 1024 * 1024; };
     CbWs w;
     w.gv = 0;
-    w.mp = w.gv + al(nc * 3 * kCC * 4);
-    w.ckS = w.mp + al(nc * 3 * kCC * kCC * 4);
+    w.rec = w.gv + al(nc * 3 * kCC * 4);
+    w.ckS = w.rec + al(nc * crec_bytes(dk, dv));
     w.ckD = w.ckS + al(nc * dk * dv * 4);
     w.ckSb = w.ckD + al(nc * kCC * dv * 4);
     w.ckDD = w.ckSb + al(nc * dk * dv * 4);
@@ -1128,27 +1180,28 @@ template <int DK, int DV>
 int launch_cb(const CbArgs& a, cudaStream_t st) {
     static int attr_ok = -1;                       // set once per process: the kernels' shared-memory limits
     if (attr_ok < 0)
-        attr_ok = cudaFuncSetAttribute(cb_mats_kernel<DK>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+        attr_ok = cudaFuncSetAttribute(cb_mats_kernel<DK, DV>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                        MatsSmem<DK>::BYTES) == cudaSuccess &&
-                          cudaFuncSetAttribute(cb_forward_kernel<DK, DV>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                               RecSmem<DK>::BYTES) == cudaSuccess &&
-                          cudaFuncSetAttribute(cb_reverse_kernel<DK, DV>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                               RecSmem<DK>::BYTES) == cudaSuccess &&
+                          cudaFuncSetAttribute(cb_chain_kernel<DK, DV>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                               ChainSmem<DK, DV>::BYTES) == cudaSuccess &&
                           cudaFuncSetAttribute(cb_grads_tc_kernel<DK, DV>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                                GtLayout<DK, DV>::BYTES) == cudaSuccess
                       ? 1
                       : 0;
     if (!attr_ok) return fail(GDN_ERR_CUDA, "gdn_prefill_bwd (chunked): cannot configure the kernels' shared memory");
     const unsigned nchunks = static_cast<unsigned>(static_cast<long>(a.B) * a.H * a.n);
-    const dim3 rec(a.B * a.H, DV / 64);
-    cb_mats_kernel<DK><<<nchunks, 128, MatsSmem<DK>::BYTES, st>>>(a);
+    cb_mats_kernel<DK, DV><<<nchunks, 128, MatsSmem<DK>::BYTES, st>>>(a);
     int s = launch_status("gdn_prefill_bwd (chunk matrices)");
     if (s != GDN_OK) return s;
-    cb_forward_kernel<DK, DV><<<rec, 256, RecSmem<DK>::BYTES, st>>>(a);
-    if ((s = launch_status("gdn_prefill_bwd (chunk forward)")) != GDN_OK) return s;
-    cb_reverse_kernel<DK, DV><<<rec, 256, RecSmem<DK>::BYTES, st>>>(a);
-    if ((s = launch_status("gdn_prefill_bwd (chunk reverse)")) != GDN_OK) return s;
-    cb_grads_tc_kernel<DK, DV><<<nchunks, 256, GtLayout<DK, DV>::BYTES, st>>>(a);
+    cb_chain_kernel<DK, DV><<<2 * a.B * a.H, 128, ChainSmem<DK, DV>::BYTES, st>>>(a);
+    if ((s = launch_status("gdn_prefill_bwd (chunk recurrences)")) != GDN_OK) return s;
+    int nsm = 148;
+    {
+        int dev = 0;
+        if (cudaGetDevice(&dev) == cudaSuccess) cudaDeviceGetAttribute(&nsm, cudaDevAttrMultiProcessorCount, dev);
+    }
+    const int gridg = static_cast<int>(nchunks) < nsm ? static_cast<int>(nchunks) : nsm;
+    cb_grads_tc_kernel<DK, DV><<<gridg, 256, GtLayout<DK, DV>::BYTES, st>>>(a, static_cast<int>(nchunks));
     return launch_status("gdn_prefill_bwd (chunk gradients)");
 }
 
@@ -1191,7 +1244,7 @@ int prefill_bwd_chunked(const void* q, const void* k, const void* v, const float
     uint8_t* ws = static_cast<uint8_t*>(workspace);
     const CbWs wl = cb_ws(static_cast<size_t>(B) * H, T, dkd, dvd);
     ar.gv = reinterpret_cast<float*>(ws + wl.gv);
-    ar.mp = reinterpret_cast<float*>(ws + wl.mp);
+    ar.rec = ws + wl.rec;
     ar.ckS = reinterpret_cast<float*>(ws + wl.ckS);
     ar.ckD = reinterpret_cast<float*>(ws + wl.ckD);
     ar.ckSb = reinterpret_cast<float*>(ws + wl.ckSb);
