@@ -306,8 +306,8 @@ int gdn_prefill_host(const void* q, const void* k, const void* v,
  *     per-token gradients on tcgen05 (bf16 hi/lo operands, fp32 accumulate) from
  *     the state at every chunk start and its gradient at every chunk end, which two
  *     recurrences over the chunks produce; q, k, v, dO, dq, dk, dv 16-byte aligned
- *     (GDN_ERR_ALIGN).  Workspace about B H T (dk dv / 32 + 2 dv + 200) 4 bytes
- *     (config 1: 1.0 GB);
+ *     (GDN_ERR_ALIGN).  Workspace about B H T (dk dv / 8 + 10 dv + 6 dk + 1328)
+ *     bytes (config 1: 1.42 GB);
  *   token-recurrent: fp32 on CUDA cores, in token windows, last first: a checkpoint
  *     pass stores the state at every window start, and only one window's per-token
  *     states are held at a time.  Workspace about B H dk dv 4 (T / W + W) bytes for
@@ -324,8 +324,7 @@ int gdn_prefill_bwd_set_window(int tokens);
  *   GDN_BWD_TOKEN    the token-recurrent windows above;
  *   GDN_BWD_CHUNKED  chunk by chunk (64 tokens): only the state at every chunk start and
  *                    its gradient at every chunk end are carried, the per-token gradients
- *                    come from chunk-local products (workspace about
- *                    B * H * T * (dk dv / 32 + 2 dv + 200) * 4 bytes; no windows);
+ *                    come from chunk-local products (workspace above; no windows);
  *   GDN_BWD_AUTO     the library's choice (the default): chunked.
  * The workspace size and the call must see the same setting.  GDN_ERR_ARG otherwise. */
 enum { GDN_BWD_AUTO = 0, GDN_BWD_TOKEN = 1, GDN_BWD_CHUNKED = 2 };

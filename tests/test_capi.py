@@ -239,10 +239,10 @@ def test_prefill_bwd_rejects(lib):
     assert call(ws=ODD) == _lib.GDN_ERR_ALIGN
     assert lib.gdn_prefill_bwd_workspace_bytes(1, 64, 2, 96, 64) == 0
     # chunked (the default): per 64-token chunk the state entering it, its gradient
-    # leaving it, the d and dd rows and the chunk's 64 x 64 matrices
+    # leaving it, the d and dd rows and the chunk's operand record
     n1 = 4 * 16 * 4096 // 64
     c1 = lib.gdn_prefill_bwd_workspace_bytes(4, 4096, 16, 128, 128)
-    assert n1 * (2 * 128 * 128 + 2 * 64 * 128 + 3 * 64 * 64) * 4 <= c1 <= 1.1e9, c1   # config 1
+    assert n1 * (2 * 128 * 128 + 2 * 64 * 128) * 4 <= c1 <= 1.5e9, c1   # config 1
     assert _lib.call_status("gdn_prefill_bwd_set_algorithm", 3) == _lib.GDN_ERR_ARG
     assert _lib.call_status("gdn_prefill_bwd_set_algorithm", _lib.GDN_BWD_TOKEN) == _lib.GDN_OK
     try:
