@@ -152,7 +152,7 @@ struct MatsSmem {
 };
 
 template <int DK, int DV>
-__global__ void __launch_bounds__(128) cb_mats_kernel(const CbArgs a) {
+__global__ void __launch_bounds__(256) cb_mats_kernel(const CbArgs a) {
     using L = MatsSmem<DK>;
     using R = CRec<DK, DV>;
     constexpr int CPK = DK / 8;
@@ -182,11 +182,20 @@ __global__ void __launch_bounds__(128) cb_mats_kernel(const CbArgs a) {
         tmem_alloc(tslot, 64);
         tmem_relinquish();
     }
-    for (int it = tid; it < 128 * CPK; it += 128) {
-        const int row = it / CPK, ch = it - row * CPK, t = row & (kCC - 1);
-        uint4 u = make_uint4(0u, 0u, 0u, 0u);
-        if (t < nt) u = __ldg(reinterpret_cast<const uint4*>((row < kCC ? a.q : a.k) + (tokbase + t) * DK + ch * 8));
-        *reinterpret_cast<uint4*>(sm + L::OFF_QK + (ch >> 3) * L::QK_KB + sw128_chunk(row, ch & 7)) = u;
+    {
+        constexpr int QN = 128 * CPK / 256;
+        uint4 w[QN];
+#pragma unroll
+        for (int u = 0; u < QN; ++u) {
+            const int it = tid + 256 * u, row = it / CPK, ch = it - row * CPK, t = row & (kCC - 1);
+            w[u] = t < nt ? __ldg(reinterpret_cast<const uint4*>((row < kCC ? a.q : a.k) + (tokbase + t) * DK + ch * 8))
+                          : make_uint4(0u, 0u, 0u, 0u);
+        }
+#pragma unroll
+        for (int u = 0; u < QN; ++u) {
+            const int it = tid + 256 * u, row = it / CPK, ch = it - row * CPK;
+            *reinterpret_cast<uint4*>(sm + L::OFF_QK + (ch >> 3) * L::QK_KB + sw128_chunk(row, ch & 7)) = w[u];
+        }
     }
     float* gv = a.gv + static_cast<long>(cid) * 3 * kCC;
     if (tid < kCC) {
@@ -227,34 +236,54 @@ __global__ void __launch_bounds__(128) cb_mats_kernel(const CbArgs a) {
         }
     }
     // v rows and (m dO)^T as stored: independent of the product
-    for (int it = tid; it < kCC * DV / 8; it += 128) {
-        const int t = it / (DV / 8), ch = it - t * (DV / 8);
-        const uint4 u = t < nt ? __ldg(reinterpret_cast<const uint4*>(a.v + (tokbase + t) * DV + ch * 8))
-                               : make_uint4(0u, 0u, 0u, 0u);
-        *reinterpret_cast<uint4*>(rec + R::VR + (t * DV + ch * 8) * 2) = u;
+    {
+        constexpr int VN = kCC * DV / 8 / 256;
+        uint4 w[VN];
+#pragma unroll
+        for (int u = 0; u < VN; ++u) {
+            const int it = tid + 256 * u, t = it / (DV / 8), ch = it - t * (DV / 8);
+            w[u] = t < nt ? __ldg(reinterpret_cast<const uint4*>(a.v + (tokbase + t) * DV + ch * 8))
+                          : make_uint4(0u, 0u, 0u, 0u);
+        }
+#pragma unroll
+        for (int u = 0; u < VN; ++u) {
+            const int it = tid + 256 * u;
+            *reinterpret_cast<uint4*>(rec + R::VR + it * 16) = w[u];
+        }
     }
     __syncthreads();
-    for (int it = tid; it < 8 * 128; it += 128) {
-        const int ch = it >> 7, vr = it & 127;         // rows v of the image, 8 tokens u per item
-        float x[8];
+    {
+        // item (ch, row v): tokens 8 ch .. 8 ch + 7 of value column v; all loads issued first
+        const bool bfo = a.do_dtype == GDN_DTYPE_BF16;
+        float x[4][8];
 #pragma unroll
-        for (int i = 0; i < 8; ++i) {
-            const int u = ch * 8 + i;
-            float d = 0.f;
-            if (vr < DV && u < nt) {
-                const long gi = (tokbase + u) * DV + vr;
-                d = mks[u] * (a.do_dtype == GDN_DTYPE_BF16 ? bf16_bits_to_f32(static_cast<const uint16_t*>(a.dO)[gi])
-                                                           : static_cast<const float*>(a.dO)[gi]);
+        for (int u = 0; u < 4; ++u) {
+            const int it = tid + 256 * u, ch = it >> 7, vr = it & 127;
+#pragma unroll
+            for (int i = 0; i < 8; ++i) {
+                const int tk = ch * 8 + i;
+                float d = 0.f;
+                if (vr < DV && tk < nt) {
+                    const long gi = (tokbase + tk) * DV + vr;
+                    d = bfo ? bf16_bits_to_f32(__ldg(static_cast<const uint16_t*>(a.dO) + gi))
+                            : __ldg(static_cast<const float*>(a.dO) + gi);
+                }
+                x[u][i] = d;
             }
-            x[i] = d;
         }
-        const uint32_t off = sw128_chunk(vr, ch);
-        split_store8(rec + R::OH + off, rec + R::OL + off, x);
+#pragma unroll
+        for (int u = 0; u < 4; ++u) {
+            const int it = tid + 256 * u, ch = it >> 7, vr = it & 127;
+#pragma unroll
+            for (int i = 0; i < 8; ++i) x[u][i] *= mks[ch * 8 + i];
+            const uint32_t off = sw128_chunk(vr, ch);
+            split_store8(rec + R::OH + off, rec + R::OL + off, x[u]);
+        }
     }
     if (tid < kCC) gv[tid] = lam[tid];
     const bool ok = mbar_wait(bar, 0, a.err);
     tc_fence_after();
-    {
+    if (tid < 128) {
         // row r of the product: P row r (r < 64) or diag(b) M row r - 64
         const int r = tid, t = r & (kCC - 1);
         const float lt = lam[t];
@@ -292,7 +321,7 @@ __global__ void __launch_bounds__(128) cb_mats_kernel(const CbArgs a) {
 #pragma unroll
         for (int t = 0; t < 16; ++t) As[(o + t) * 65 + o + col] = x[t];
     }
-    for (int e = tid; e < kCC * kCC; e += 128) {      // blocks above the diagonal are zero
+    for (int e = tid; e < kCC * kCC; e += 256) {      // blocks above the diagonal are zero
         const int r = e >> 6, s = e & 63;
         if ((s >> 4) > (r >> 4)) As[r * 65 + s] = 0.f;
     }
@@ -301,7 +330,7 @@ __global__ void __launch_bounds__(128) cb_mats_kernel(const CbArgs a) {
 #pragma unroll 1
     for (int dd = 1; dd < 4; ++dd) {
         const int nb = 4 - dd;
-        for (int e = tid; e < nb * 256; e += 128) {
+        for (int e = tid; e < nb * 256; e += 256) {
             const int jb = e >> 8, rr = (e >> 4) & 15, cc = e & 15, ib = jb + dd;
             float acc = 0.f;
             for (int kb = jb; kb < ib; ++kb)
@@ -311,7 +340,7 @@ __global__ void __launch_bounds__(128) cb_mats_kernel(const CbArgs a) {
             Ts[(jb * 16 + rr) * 17 + cc] = acc;
         }
         __syncthreads();
-        for (int e = tid; e < nb * 256; e += 128) {
+        for (int e = tid; e < nb * 256; e += 256) {
             const int jb = e >> 8, rr = (e >> 4) & 15, cc = e & 15, ib = jb + dd;
             float acc = 0.f;
 #pragma unroll
@@ -322,7 +351,7 @@ __global__ void __launch_bounds__(128) cb_mats_kernel(const CbArgs a) {
         __syncthreads();
     }
     // the record: A, A^T, P^T (hi/lo), k and scale G q images, tables
-    for (int it = tid; it < 3 * 512; it += 128) {
+    for (int it = tid; it < 3 * 512; it += 256) {
         const int img = it >> 9, row = (it >> 3) & 63, ch = it & 7;
         float x[8];
 #pragma unroll
@@ -335,7 +364,7 @@ __global__ void __launch_bounds__(128) cb_mats_kernel(const CbArgs a) {
         const int lo = img == 0 ? R::AL : (img == 1 ? R::ATL : R::PTL);
         split_store8(rec + hi + off, rec + lo + off, x);
     }
-    for (int it = tid; it < (DK / 64) * 512; it += 128) {
+    for (int it = tid; it < (DK / 64) * 512; it += 256) {
         const int b = it >> 9, t = (it >> 3) & 63, ch = it & 7;
         const uint4 kq = *reinterpret_cast<const uint4*>(sm + L::OFF_QK + b * L::QK_KB + sw128_chunk(kCC + t, ch));
         *reinterpret_cast<uint4*>(rec + R::KIMG + b * 8192 + sw128_chunk(t, ch)) = kq;
@@ -1190,7 +1219,7 @@ int launch_cb(const CbArgs& a, cudaStream_t st) {
                       : 0;
     if (!attr_ok) return fail(GDN_ERR_CUDA, "gdn_prefill_bwd (chunked): cannot configure the kernels' shared memory");
     const unsigned nchunks = static_cast<unsigned>(static_cast<long>(a.B) * a.H * a.n);
-    cb_mats_kernel<DK, DV><<<nchunks, 128, MatsSmem<DK>::BYTES, st>>>(a);
+    cb_mats_kernel<DK, DV><<<nchunks, 256, MatsSmem<DK>::BYTES, st>>>(a);
     int s = launch_status("gdn_prefill_bwd (chunk matrices)");
     if (s != GDN_OK) return s;
     cb_chain_kernel<DK, DV><<<2 * a.B * a.H, 128, ChainSmem<DK, DV>::BYTES, st>>>(a);
