@@ -70,9 +70,9 @@ struct CbArgs {
     // workspace, per chunk cid = bh * n + c
     float* gv;                          // [cid][3][64]: Lambda (in-chunk cumulative log g), b, m
     uint8_t* rec;                       // [cid]: the chain kernel's record (CRec)
-    float* ckS;                         // [cid][DK][DV]: the state entering the chunk
+    uint8_t* ckS;                       // [cid]: the state entering the chunk, S^T image (hi, lo)
     float* ckD;                         // [cid][64][DV]: the chunk's d rows
-    float* ckSb;                        // [cid][DK][DV]: the gradient of the state leaving the chunk
+    uint8_t* ckSb;                      // [cid]: the gradient of the state leaving it, Sb^T image (hi, lo)
     float* ckDD;                        // [cid][64][DV]: the chunk's dd rows
     float* dlogg;                       // [B,H,T]: g dg per token
     unsigned int* err;                  // device error word (bounded waits)
@@ -506,13 +506,9 @@ __global__ void __launch_bounds__(128, 1) cb_chain_kernel(const CbArgs a) {
         const long cid = static_cast<long>(bh) * a.n + c;
         if (!mbar_wait(&bars[0], step & 1, a.err)) ok = false;
         if (tid == 0 && step + 1 < a.n) prefetch(rev ? c - 1 : c + 1);
-        // ---- the state entering (forward) or leaving (reverse) the chunk: checkpoint and image
+        // ---- the state entering (forward) or leaving (reverse) the chunk as a bf16 hi/lo
+        //      image (rows v), which is also the checkpoint: bulk-stored for the gradient kernel
         {
-            float* ck = (rev ? a.ckSb : a.ckS) + cid * DK * DV + v;
-            if (col_ok) {
-#pragma unroll
-                for (int d = 0; d < DK; ++d) ck[static_cast<long>(d) * DV] = S[d];
-            }
 #pragma unroll
             for (int b = 0; b < DK / 64; ++b)
 #pragma unroll
@@ -528,6 +524,8 @@ __global__ void __launch_bounds__(128, 1) cb_chain_kernel(const CbArgs a) {
         __syncthreads();
         const float GL = tab[R::T_G + kCC - 1];
         if (tid == 0) {
+            bulk_store((rev ? a.ckSb : a.ckS) + cid * 2 * L::SB, sm + L::OFF_SH, 2 * L::SB);
+            bulk_commit();
             tc_fence_after();
             constexpr uint32_t id64 = idesc_bf16(128, 64, false, false);
             const uint32_t sh = sbase + L::OFF_SH, sl = sbase + L::OFF_SL, kim = rbase + R::KIMG;
@@ -645,10 +643,12 @@ __global__ void __launch_bounds__(128, 1) cb_chain_kernel(const CbArgs a) {
             for (int i = 0; i < 32; ++i) S[cb + i] = fmaf(GL, S[cb + i], u[i]);
         }
         if (!ok) *dead = 1;
+        if (tid == 0) bulk_wait_read0();           // the state image may be rewritten
         tc_fence_before();
         __syncthreads();
         if (*dead) break;
     }
+    if (tid == 0) bulk_wait_all0();
     if (rev && col_ok && a.dstate_in && *dead == 0) {
         const long s0 = static_cast<long>(bh) * DK * DV;
 #pragma unroll
@@ -683,8 +683,7 @@ template <int DK, int DV>
 struct GtLayout {
     static constexpr int R_KB = 192 * 128;                 // one 64-column block of the 192-row image
     static constexpr int R_BYTES = (DV / 64) * R_KB;
-    static constexpr int S_KB = DK * 128;
-    static constexpr int S_BYTES = (DV / 64) * S_KB;
+    static constexpr int S_BYTES = (DK / 64) * 16384;      // S^T image (hi or lo): rows v (128), DK columns
     static constexpr int QK_KB = 128 * 128;
     static constexpr int QK_BYTES = (DK / 64) * QK_KB;
     static constexpr int OFF_RH = 0, OFF_RL = R_BYTES, OFF_SH = 2 * R_BYTES, OFF_SL = OFF_SH + S_BYTES;
@@ -725,7 +724,7 @@ __global__ void __launch_bounds__(256, 1) cb_grads_tc_kernel(const CbArgs a, int
     float* basep = misc + 896;                     // [8 warps] <S, Sb> partials
     int* dead = reinterpret_cast<int*>(misc + 904);
     uint64_t* bars = reinterpret_cast<uint64_t*>(sm + L::OFF_BAR);
-    uint32_t* tslot = reinterpret_cast<uint32_t*>(bars + 4);
+    uint32_t* tslot = reinterpret_cast<uint32_t*>(bars + 5);
     float* F1s = reinterpret_cast<float*>(sm + L::OFF_QK);          // [64][64], row t rotated by t
     float* F2s = F1s + 4096;
 
@@ -736,8 +735,8 @@ __global__ void __launch_bounds__(256, 1) cb_grads_tc_kernel(const CbArgs a, int
     auto prefetch = [&](int cx) {
         const int bx = cx / a.n, tx0 = (cx - bx * a.n) * kCC, ntx = min(kCC, a.T - tx0);
         const long tb = static_cast<long>(bx) * a.T + tx0;
-        bulk_prefetch_l2(a.ckS + static_cast<long>(cx) * DK * DV, DK * DV * 4);
-        bulk_prefetch_l2(a.ckSb + static_cast<long>(cx) * DK * DV, DK * DV * 4);
+        bulk_prefetch_l2(a.ckS + static_cast<long>(cx) * 2 * L::S_BYTES, 2 * L::S_BYTES);
+        bulk_prefetch_l2(a.ckSb + static_cast<long>(cx) * 2 * L::S_BYTES, 2 * L::S_BYTES);
         bulk_prefetch_l2(a.ckD + static_cast<long>(cx) * kCC * DV, kCC * DV * 4);
         bulk_prefetch_l2(a.ckDD + static_cast<long>(cx) * kCC * DV, kCC * DV * 4);
         const uint32_t ob = do_bf ? 2u : 4u;
@@ -752,6 +751,7 @@ __global__ void __launch_bounds__(256, 1) cb_grads_tc_kernel(const CbArgs a, int
         mbar_init(&bars[0], 1);
         mbar_init(&bars[1], 1);
         mbar_init(&bars[2], 1);
+        mbar_init(&bars[3], 1);
         *dead = 0;
         fence_mbar_init();
         if (static_cast<int>(blockIdx.x) < nchunks) prefetch(blockIdx.x);
@@ -768,11 +768,15 @@ __global__ void __launch_bounds__(256, 1) cb_grads_tc_kernel(const CbArgs a, int
     const int h = bh % a.H;
     const int t0 = c * kCC, nt = min(kCC, a.T - t0);
     const long tokbase = static_cast<long>(bh) * a.T + t0;
-    const float* ckS = a.ckS + static_cast<long>(cid) * DK * DV;
-    const float* ckSb = a.ckSb + static_cast<long>(cid) * DK * DV;
+    const uint8_t* ckS = a.ckS + static_cast<long>(cid) * 2 * L::S_BYTES;
+    const uint8_t* ckSb = a.ckSb + static_cast<long>(cid) * 2 * L::S_BYTES;
     const float* ckD = a.ckD + static_cast<long>(cid) * kCC * DV;
     const float* ckDD = a.ckDD + static_cast<long>(cid) * kCC * DV;
-    if (tid == 0 && cid + static_cast<int>(gridDim.x) < nchunks) prefetch(cid + gridDim.x);
+    if (tid == 0) {
+        mbar_arrive_expect_tx(&bars[3], 2 * L::S_BYTES);   // the S^T image (hi, lo) -> the S region
+        bulk_load(sm + L::OFF_SH, ckS, 2 * L::S_BYTES, &bars[3]);
+        if (cid + static_cast<int>(gridDim.x) < nchunks) prefetch(cid + gridDim.x);
+    }
     if (tid < kCC) {
         const float* gv = a.gv + static_cast<long>(cid) * 3 * kCC;
         lam[tid] = gv[tid];
@@ -849,27 +853,6 @@ __global__ void __launch_bounds__(256, 1) cb_grads_tc_kernel(const CbArgs a, int
         }
     }
     {
-        constexpr int SN = DK * CPR / 256, SGP = SN >= 4 ? 4 : SN;
-#pragma unroll
-        for (int k0 = 0; k0 < SN; k0 += SGP) {
-            float x[SGP][8];
-#pragma unroll
-            for (int u = 0; u < SGP; ++u) {
-                const int it = tid + 256 * (k0 + u), d = it / CPR, ch = it - d * CPR;
-                const float4 f0 = __ldg(reinterpret_cast<const float4*>(ckS + d * DV + ch * 8));
-                const float4 f1 = __ldg(reinterpret_cast<const float4*>(ckS + d * DV + ch * 8 + 4));
-                x[u][0] = f0.x; x[u][1] = f0.y; x[u][2] = f0.z; x[u][3] = f0.w;
-                x[u][4] = f1.x; x[u][5] = f1.y; x[u][6] = f1.z; x[u][7] = f1.w;
-            }
-#pragma unroll
-            for (int u = 0; u < SGP; ++u) {
-                const int it = tid + 256 * (k0 + u), d = it / CPR, ch = it - d * CPR;
-                const uint32_t off = (ch >> 3) * L::S_KB + sw128_chunk(d, ch & 7);
-                split_store8(sm + L::OFF_SH + off, sm + L::OFF_SL + off, x[u]);
-            }
-        }
-    }
-    {
         constexpr int QN = 128 * CPK / 256;
         uint4 w[QN];
 #pragma unroll
@@ -888,18 +871,20 @@ __global__ void __launch_bounds__(256, 1) cb_grads_tc_kernel(const CbArgs a, int
     __syncthreads();
     const uint32_t rh = sbase + L::OFF_RH, rl = sbase + L::OFF_RL, sh = sbase + L::OFF_SH, sl = sbase + L::OFF_SL;
     if (tid == 0) {
+        if (!mbar_wait(&bars[3], 0, a.err)) *dead = 1;
         tc_fence_after();
-        constexpr uint32_t idN = idesc_bf16(128, DK, false, false);
+        // S^T image rows v as the MN-major B operand (N = d): 16 rows per K step, next 64 d at 16 KB
+        constexpr uint32_t idN = idesc_bf16(128, DK, false, true);
         constexpr uint32_t id64 = idesc_bf16(128, 64, false, false);
         const uint32_t pa[3] = {rh, rh, rl}, pbs[3] = {sh, sl, sh}, pbd[3] = {rh, rl, rh};
 #pragma unroll
         for (int p = 0; p < 3; ++p)
 #pragma unroll
             for (int kk = 0; kk < DV / 16; ++kk) {
-                const uint32_t ko = (kk >> 2) * L::R_KB + (kk & 3) * 32, so = (kk >> 2) * L::S_KB + (kk & 3) * 32;
+                const uint32_t ko = (kk >> 2) * L::R_KB + (kk & 3) * 32;
                 const uint32_t acc = (p > 0 || kk > 0) ? 1u : 0u;
-                umma_bf16_ss(tmem + L::T_XS, sdesc_sw128(pa[p] + ko, 16, 1024), sdesc_sw128(pbs[p] + so, 16, 1024),
-                             idN, acc);
+                umma_bf16_ss(tmem + L::T_XS, sdesc_sw128(pa[p] + ko, 16, 1024),
+                             sdesc_sw128(pbs[p] + kk * 2048, 16384, 1024), idN, acc);
                 umma_bf16_ss(tmem + L::T_DD, sdesc_sw128(pa[p] + ko, 16, 1024),
                              sdesc_sw128(pbd[p] + ko + 2 * kCC * 128, 16, 1024), id64, acc);
             }
@@ -913,35 +898,35 @@ __global__ void __launch_bounds__(256, 1) cb_grads_tc_kernel(const CbArgs a, int
         umma_commit(&bars[0]);
     }
 
-    // ---- phase B: Sb over the S image once T1 has read it, <S, Sb>, then T2
+    // ---- phase B: the Sb^T image over the S image once T1 has read it, <S, Sb>, then T2
     if (!mbar_wait(&bars[0], ph, a.err)) *dead = 1;
     tc_fence_after();
+    if (tid == 0) {
+        mbar_arrive_expect_tx(&bars[3], 2 * L::S_BYTES);
+        bulk_load(sm + L::OFF_SH, ckSb, 2 * L::S_BYTES, &bars[3]);
+    }
     float sp = 0.f;
     {
-        constexpr int SN = DK * CPR / 256, SGP = SN >= 4 ? 4 : SN;
+        // <S, Sb> over the images: S (hi, lo) from memory (just read into L2), Sb from shared memory
+        constexpr int NQ = 2 * L::S_BYTES / 2 / 16 / 256;     // uint4 of one image (hi or lo) per thread
+        uint4 shv[NQ], slv[NQ];
 #pragma unroll
-        for (int k0 = 0; k0 < SN; k0 += SGP) {
-            float x[SGP][8], s8[SGP][8];
+        for (int u = 0; u < NQ; ++u) {
+            const int q = tid + 256 * u;
+            shv[u] = __ldg(reinterpret_cast<const uint4*>(ckS) + q);
+            slv[u] = __ldg(reinterpret_cast<const uint4*>(ckS + L::S_BYTES) + q);
+        }
+        if (!mbar_wait(&bars[3], 1, a.err)) *dead = 1;
 #pragma unroll
-            for (int u = 0; u < SGP; ++u) {
-                const int it = tid + 256 * (k0 + u), d = it / CPR, ch = it - d * CPR;
-                const float4 f0 = __ldg(reinterpret_cast<const float4*>(ckSb + d * DV + ch * 8));
-                const float4 f1 = __ldg(reinterpret_cast<const float4*>(ckSb + d * DV + ch * 8 + 4));
-                const float4 g0 = __ldg(reinterpret_cast<const float4*>(ckS + d * DV + ch * 8));
-                const float4 g1 = __ldg(reinterpret_cast<const float4*>(ckS + d * DV + ch * 8 + 4));
-                x[u][0] = f0.x; x[u][1] = f0.y; x[u][2] = f0.z; x[u][3] = f0.w;
-                x[u][4] = f1.x; x[u][5] = f1.y; x[u][6] = f1.z; x[u][7] = f1.w;
-                s8[u][0] = g0.x; s8[u][1] = g0.y; s8[u][2] = g0.z; s8[u][3] = g0.w;
-                s8[u][4] = g1.x; s8[u][5] = g1.y; s8[u][6] = g1.z; s8[u][7] = g1.w;
-            }
+        for (int u = 0; u < NQ; ++u) {
+            const int q = tid + 256 * u;
+            float a8[8], b8[8], c8[8], d8[8];
+            unpack_bf16x8(shv[u], a8);
+            unpack_bf16x8(slv[u], b8);
+            unpack_bf16x8(*reinterpret_cast<const uint4*>(sm + L::OFF_SH + q * 16), c8);
+            unpack_bf16x8(*reinterpret_cast<const uint4*>(sm + L::OFF_SL + q * 16), d8);
 #pragma unroll
-            for (int u = 0; u < SGP; ++u) {
-                const int it = tid + 256 * (k0 + u), d = it / CPR, ch = it - d * CPR;
-#pragma unroll
-                for (int i = 0; i < 8; ++i) sp = fmaf(s8[u][i], x[u][i], sp);
-                const uint32_t off = (ch >> 3) * L::S_KB + sw128_chunk(d, ch & 7);
-                split_store8(sm + L::OFF_SH + off, sm + L::OFF_SL + off, x[u]);
-            }
+            for (int i = 0; i < 8; ++i) sp = fmaf(a8[i] + b8[i], c8[i] + d8[i], sp);
         }
     }
     sp = warp_sum(sp);
@@ -951,15 +936,15 @@ __global__ void __launch_bounds__(256, 1) cb_grads_tc_kernel(const CbArgs a, int
     const bool dead_b = *dead != 0;
     if (tid == 0 && !dead_b) {
         tc_fence_after();
-        constexpr uint32_t idN = idesc_bf16(128, DK, false, false);
+        constexpr uint32_t idN = idesc_bf16(128, DK, false, true);
         const uint32_t pa[3] = {rh, rh, rl}, pbs[3] = {sh, sl, sh};
 #pragma unroll
         for (int p = 0; p < 3; ++p)
 #pragma unroll
             for (int kk = 0; kk < DV / 16; ++kk) {
-                const uint32_t ko = (kk >> 2) * L::R_KB + (kk & 3) * 32, so = (kk >> 2) * L::S_KB + (kk & 3) * 32;
+                const uint32_t ko = (kk >> 2) * L::R_KB + (kk & 3) * 32;
                 umma_bf16_ss(tmem + L::T_XE, sdesc_sw128(pa[p] + ko + kCC * 128, 16, 1024),
-                             sdesc_sw128(pbs[p] + so, 16, 1024), idN, (p > 0 || kk > 0) ? 1u : 0u);
+                             sdesc_sw128(pbs[p] + kk * 2048, 16384, 1024), idN, (p > 0 || kk > 0) ? 1u : 0u);
             }
         umma_commit(&bars[1]);
     }
@@ -1197,9 +1182,9 @@ CbWs cb_ws(size_t bh, int T, int dk, int dv) {
     w.gv = 0;
     w.rec = w.gv + al(nc * 3 * kCC * 4);
     w.ckS = w.rec + al(nc * crec_bytes(dk, dv));
-    w.ckD = w.ckS + al(nc * dk * dv * 4);
+    w.ckD = w.ckS + al(nc * dk * 512);               // S^T image (hi, lo): 128 rows x dk bf16 each
     w.ckSb = w.ckD + al(nc * kCC * dv * 4);
-    w.ckDD = w.ckSb + al(nc * dk * dv * 4);
+    w.ckDD = w.ckSb + al(nc * dk * 512);
     w.dlogg = w.ckDD + al(nc * kCC * dv * 4);
     w.total = w.dlogg + al(bh * static_cast<size_t>(T) * 4) + 1024;
     return w;
@@ -1274,9 +1259,9 @@ int prefill_bwd_chunked(const void* q, const void* k, const void* v, const float
     const CbWs wl = cb_ws(static_cast<size_t>(B) * H, T, dkd, dvd);
     ar.gv = reinterpret_cast<float*>(ws + wl.gv);
     ar.rec = ws + wl.rec;
-    ar.ckS = reinterpret_cast<float*>(ws + wl.ckS);
+    ar.ckS = ws + wl.ckS;
     ar.ckD = reinterpret_cast<float*>(ws + wl.ckD);
-    ar.ckSb = reinterpret_cast<float*>(ws + wl.ckSb);
+    ar.ckSb = ws + wl.ckSb;
     ar.ckDD = reinterpret_cast<float*>(ws + wl.ckDD);
     ar.dlogg = reinterpret_cast<float*>(ws + wl.dlogg);
     ar.err = device_error_word();
