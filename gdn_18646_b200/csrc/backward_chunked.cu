@@ -71,9 +71,9 @@ struct CbArgs {
     float* gv;                          // [cid][3][64]: Lambda (in-chunk cumulative log g), b, m
     uint8_t* rec;                       // [cid]: the chain kernel's record (CRec)
     uint8_t* ckS;                       // [cid]: the state entering the chunk, S^T image (hi, lo)
-    float* ckD;                         // [cid][64][DV]: the chunk's d rows
+    uint8_t* ckD;                       // [cid]: the chunk's d rows as a d^T image (hi, lo; rows v)
     uint8_t* ckSb;                      // [cid]: the gradient of the state leaving it, Sb^T image (hi, lo)
-    float* ckDD;                        // [cid][64][DV]: the chunk's dd rows
+    uint8_t* ckDD;                      // [cid]: the chunk's dd rows as a dd^T image (hi, lo; rows v)
     float* dlogg;                       // [B,H,T]: g dg per token
     unsigned int* err;                  // device error word (bounded waits)
     int B, T, H, n;
@@ -571,6 +571,7 @@ __global__ void __launch_bounds__(128, 1) cb_chain_kernel(const CbArgs a) {
             }
             put32(L::OFF_XH, L::OFF_XL, cb >> 5, d1);
         }
+        if (tid == 0) bulk_wait_read0();           // the state image may now be overwritten (d / dd image)
         fence_async_smem();
         __syncthreads();
         if (tid == 0) {
@@ -589,18 +590,21 @@ __global__ void __launch_bounds__(128, 1) cb_chain_kernel(const CbArgs a) {
             umma_commit(&bars[1]);
         }
         mma_wait();
-        // ---- d (forward) or dd (reverse): store, then the scaled image for the state update
+        // ---- d (forward) or dd (reverse): its image over the state image (bulk-stored for the
+        //      gradient kernel), dv = b dd (reverse), then the scaled image for the state update
         {
-            float* ckd = (rev ? a.ckDD : a.ckD) + cid * kCC * DV + v;
+            const int nt = min(kCC, a.T - c * kCC);
+            float* dvo = a.dv + (static_cast<long>(bh) * a.T + c * kCC) * DV + v;
 #pragma unroll
             for (int cb = 0; cb < kCC; cb += 32) {
                 float d2[32];
                 tmem_ld32(lane_t + T_D2 + cb, d2);
                 tmem_ld_wait();
+                put32(L::OFF_SH, L::OFF_SH + 16384, cb >> 5, d2);
 #pragma unroll
                 for (int i = 0; i < 32; ++i) {
                     const int t = cb + i;
-                    if (col_ok) ckd[static_cast<long>(t) * DV] = d2[i];
+                    if (rev && col_ok && t < nt) dvo[static_cast<long>(t) * DV] = tab[R::T_B + t] * d2[i];
                     d2[i] = rev ? -tab[R::T_GB + t] * d2[i] : tab[R::T_CF + t] * d2[i];
                 }
                 put32(L::OFF_XH, L::OFF_XL, cb >> 5, d2);
@@ -609,6 +613,8 @@ __global__ void __launch_bounds__(128, 1) cb_chain_kernel(const CbArgs a) {
         fence_async_smem();
         __syncthreads();
         if (tid == 0) {
+            bulk_store((rev ? a.ckDD : a.ckD) + cid * 32768, sm + L::OFF_SH, 32768);
+            bulk_commit();
             tc_fence_after();
             constexpr uint32_t idU = idesc_bf16(128, DK, false, true);
             const uint32_t xh = sbase + L::OFF_XH, xl = sbase + L::OFF_XL, kim = rbase + R::KIMG;
@@ -681,8 +687,7 @@ __global__ void __launch_bounds__(128, 1) cb_chain_kernel(const CbArgs a) {
 // ---------------------------------------------------------------------------
 template <int DK, int DV>
 struct GtLayout {
-    static constexpr int R_KB = 192 * 128;                 // one 64-column block of the 192-row image
-    static constexpr int R_BYTES = (DV / 64) * R_KB;
+    static constexpr int R_BYTES = 3 * 16384;              // [dO'^T | dd^T | d^T] (hi or lo): rows v, 64 t each
     static constexpr int S_BYTES = (DK / 64) * 16384;      // S^T image (hi or lo): rows v (128), DK columns
     static constexpr int QK_KB = 128 * 128;
     static constexpr int QK_BYTES = (DK / 64) * QK_KB;
@@ -705,7 +710,6 @@ struct GtLayout {
 template <int DK, int DV>
 __global__ void __launch_bounds__(256, 1) cb_grads_tc_kernel(const CbArgs a, int nchunks) {
     using L = GtLayout<DK, DV>;
-    constexpr int CPR = DV / 8;                    // 8-value chunks per value row
     constexpr int CPK = DK / 8;                    // per key row
     extern __shared__ uint8_t smem_raw[];
     uint8_t* sm = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
@@ -730,17 +734,15 @@ __global__ void __launch_bounds__(256, 1) cb_grads_tc_kernel(const CbArgs a, int
 
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
     const uint32_t sbase = smem_u32(sm);
-    const bool do_bf = a.do_dtype == GDN_DTYPE_BF16;
     // the inputs of chunk cx -> L2 (issued one chunk ahead)
     auto prefetch = [&](int cx) {
         const int bx = cx / a.n, tx0 = (cx - bx * a.n) * kCC, ntx = min(kCC, a.T - tx0);
         const long tb = static_cast<long>(bx) * a.T + tx0;
         bulk_prefetch_l2(a.ckS + static_cast<long>(cx) * 2 * L::S_BYTES, 2 * L::S_BYTES);
         bulk_prefetch_l2(a.ckSb + static_cast<long>(cx) * 2 * L::S_BYTES, 2 * L::S_BYTES);
-        bulk_prefetch_l2(a.ckD + static_cast<long>(cx) * kCC * DV, kCC * DV * 4);
-        bulk_prefetch_l2(a.ckDD + static_cast<long>(cx) * kCC * DV, kCC * DV * 4);
-        const uint32_t ob = do_bf ? 2u : 4u;
-        bulk_prefetch_l2(static_cast<const uint8_t*>(a.dO) + tb * DV * ob, ntx * DV * ob);
+        bulk_prefetch_l2(a.ckD + static_cast<long>(cx) * 32768, 32768);
+        bulk_prefetch_l2(a.ckDD + static_cast<long>(cx) * 32768, 32768);
+        bulk_prefetch_l2(a.rec + static_cast<long>(cx) * CRec<DK, DV>::BYTES + CRec<DK, DV>::OH, 32768);
         bulk_prefetch_l2(a.q + tb * DK, ntx * DK * 2);
         bulk_prefetch_l2(a.k + tb * DK, ntx * DK * 2);
         bulk_prefetch_l2(a.v + tb * DV, ntx * DV * 2);
@@ -770,11 +772,19 @@ __global__ void __launch_bounds__(256, 1) cb_grads_tc_kernel(const CbArgs a, int
     const long tokbase = static_cast<long>(bh) * a.T + t0;
     const uint8_t* ckS = a.ckS + static_cast<long>(cid) * 2 * L::S_BYTES;
     const uint8_t* ckSb = a.ckSb + static_cast<long>(cid) * 2 * L::S_BYTES;
-    const float* ckD = a.ckD + static_cast<long>(cid) * kCC * DV;
-    const float* ckDD = a.ckDD + static_cast<long>(cid) * kCC * DV;
+    const uint8_t* ckD = a.ckD + static_cast<long>(cid) * 32768;
+    const uint8_t* ckDD = a.ckDD + static_cast<long>(cid) * 32768;
+    const uint8_t* rec = a.rec + static_cast<long>(cid) * CRec<DK, DV>::BYTES;
     if (tid == 0) {
-        mbar_arrive_expect_tx(&bars[3], 2 * L::S_BYTES);   // the S^T image (hi, lo) -> the S region
+        // the S^T image -> the S region; [dO'^T | dd^T | d^T] (hi, lo) -> the T image
+        mbar_arrive_expect_tx(&bars[3], 2 * L::S_BYTES + 6 * 16384);
         bulk_load(sm + L::OFF_SH, ckS, 2 * L::S_BYTES, &bars[3]);
+        bulk_load(sm + L::OFF_RH, rec + CRec<DK, DV>::OH, 16384, &bars[3]);
+        bulk_load(sm + L::OFF_RL, rec + CRec<DK, DV>::OL, 16384, &bars[3]);
+        bulk_load(sm + L::OFF_RH + 16384, ckDD, 16384, &bars[3]);
+        bulk_load(sm + L::OFF_RL + 16384, ckDD + 16384, 16384, &bars[3]);
+        bulk_load(sm + L::OFF_RH + 32768, ckD, 16384, &bars[3]);
+        bulk_load(sm + L::OFF_RL + 32768, ckD + 16384, 16384, &bars[3]);
         if (cid + static_cast<int>(gridDim.x) < nchunks) prefetch(cid + gridDim.x);
     }
     if (tid < kCC) {
@@ -786,72 +796,7 @@ __global__ void __launch_bounds__(256, 1) cb_grads_tc_kernel(const CbArgs a, int
     }
     __syncthreads();
 
-    // ---- phase A: [dO'; dd; D] and S as bf16 hi/lo images, [Q; K]; dv = b dd; dd . v.
-    //      Items in groups whose loads are all issued before any is used.
-    {
-        constexpr int RN = 192 * CPR / 256, RGP = RN >= 6 ? 6 : RN;
-#pragma unroll
-        for (int k0 = 0; k0 < RN; k0 += RGP) {
-            float x[RGP][8];
-            uint4 vv[RGP];
-#pragma unroll
-            for (int u = 0; u < RGP; ++u) {
-                const int it = tid + 256 * (k0 + u), row = it / CPR, ch = it - row * CPR;
-                vv[u] = make_uint4(0u, 0u, 0u, 0u);
-#pragma unroll
-                for (int i = 0; i < 8; ++i) x[u][i] = 0.f;
-                if (row < kCC) {
-                    if (row < nt) {
-                        const long gi = (tokbase + row) * DV + ch * 8;
-                        if (do_bf) {
-                            uint4 w = __ldg(reinterpret_cast<const uint4*>(static_cast<const uint16_t*>(a.dO) + gi));
-                            unpack_bf16x8(w, x[u]);
-                        } else {
-                            const float4 f0 = __ldg(reinterpret_cast<const float4*>(static_cast<const float*>(a.dO) + gi));
-                            const float4 f1 =
-                                __ldg(reinterpret_cast<const float4*>(static_cast<const float*>(a.dO) + gi + 4));
-                            x[u][0] = f0.x; x[u][1] = f0.y; x[u][2] = f0.z; x[u][3] = f0.w;
-                            x[u][4] = f1.x; x[u][5] = f1.y; x[u][6] = f1.z; x[u][7] = f1.w;
-                        }
-                    }
-                } else {
-                    const float* src = row < 2 * kCC ? ckDD + (row - kCC) * DV : ckD + (row - 2 * kCC) * DV;
-                    const float4 f0 = __ldg(reinterpret_cast<const float4*>(src + ch * 8));
-                    const float4 f1 = __ldg(reinterpret_cast<const float4*>(src + ch * 8 + 4));
-                    x[u][0] = f0.x; x[u][1] = f0.y; x[u][2] = f0.z; x[u][3] = f0.w;
-                    x[u][4] = f1.x; x[u][5] = f1.y; x[u][6] = f1.z; x[u][7] = f1.w;
-                    if (row < 2 * kCC && row - kCC < nt)
-                        vv[u] = __ldg(reinterpret_cast<const uint4*>(a.v + (tokbase + row - kCC) * DV + ch * 8));
-                }
-            }
-#pragma unroll
-            for (int u = 0; u < RGP; ++u) {
-                const int it = tid + 256 * (k0 + u), row = it / CPR, ch = it - row * CPR;
-                float dvp = 0.f;
-                if (row < kCC) {
-                    const float m = ms[row];
-#pragma unroll
-                    for (int i = 0; i < 8; ++i) x[u][i] *= m;
-                } else if (row < 2 * kCC && row - kCC < nt) {
-                    const int t = row - kCC;
-                    const float b = bms[t];
-                    float* dst = a.dv + (tokbase + t) * DV + ch * 8;
-                    *reinterpret_cast<float4*>(dst) = make_float4(b * x[u][0], b * x[u][1], b * x[u][2], b * x[u][3]);
-                    *reinterpret_cast<float4*>(dst + 4) =
-                        make_float4(b * x[u][4], b * x[u][5], b * x[u][6], b * x[u][7]);
-                    float v8[8];
-                    unpack_bf16x8(vv[u], v8);
-#pragma unroll
-                    for (int i = 0; i < 8; ++i) dvp = fmaf(x[u][i], v8[i], dvp);
-                }
-#pragma unroll
-                for (int o = CPR / 2; o > 0; o >>= 1) dvp += __shfl_xor_sync(0xffffffffu, dvp, o);
-                if (row >= kCC && row < 2 * kCC && ch == 0) ddv[row - kCC] = dvp;
-                const uint32_t off = (ch >> 3) * L::R_KB + sw128_chunk(row, ch & 7);
-                split_store8(sm + L::OFF_RH + off, sm + L::OFF_RL + off, x[u]);
-            }
-        }
-    }
+    // ---- phase A: [Q; K] (the images land on bars[3])
     {
         constexpr int QN = 128 * CPK / 256;
         uint4 w[QN];
@@ -873,27 +818,30 @@ __global__ void __launch_bounds__(256, 1) cb_grads_tc_kernel(const CbArgs a, int
     if (tid == 0) {
         if (!mbar_wait(&bars[3], 0, a.err)) *dead = 1;
         tc_fence_after();
-        // S^T image rows v as the MN-major B operand (N = d): 16 rows per K step, next 64 d at 16 KB
-        constexpr uint32_t idN = idesc_bf16(128, DK, false, true);
-        constexpr uint32_t id64 = idesc_bf16(128, 64, false, false);
+        // Every operand here is MN-major (rows v of the images, 16 rows per K step): A = the
+        // [dO'^T | dd^T] blocks (M = 128 tokens, next 64 at 16 KB), B = the S^T image (N = d)
+        // or the d^T block (N = 64 tokens)
+        constexpr uint32_t idN = idesc_bf16(128, DK, true, true);
+        constexpr uint32_t id64 = idesc_bf16(128, 64, true, true);
         const uint32_t pa[3] = {rh, rh, rl}, pbs[3] = {sh, sl, sh}, pbd[3] = {rh, rl, rh};
 #pragma unroll
         for (int p = 0; p < 3; ++p)
 #pragma unroll
             for (int kk = 0; kk < DV / 16; ++kk) {
-                const uint32_t ko = (kk >> 2) * L::R_KB + (kk & 3) * 32;
                 const uint32_t acc = (p > 0 || kk > 0) ? 1u : 0u;
-                umma_bf16_ss(tmem + L::T_XS, sdesc_sw128(pa[p] + ko, 16, 1024),
+                umma_bf16_ss(tmem + L::T_XS, sdesc_sw128(pa[p] + kk * 2048, 16384, 1024),
                              sdesc_sw128(pbs[p] + kk * 2048, 16384, 1024), idN, acc);
-                umma_bf16_ss(tmem + L::T_DD, sdesc_sw128(pa[p] + ko, 16, 1024),
-                             sdesc_sw128(pbd[p] + ko + 2 * kCC * 128, 16, 1024), id64, acc);
+                umma_bf16_ss(tmem + L::T_DD, sdesc_sw128(pa[p] + kk * 2048, 16384, 1024),
+                             sdesc_sw128(pbd[p] + 32768 + kk * 2048, 16384, 1024), id64, acc);
             }
+        // [Q; K] K^T: both operands K-major
+        constexpr uint32_t id64k = idesc_bf16(128, 64, false, false);
         const uint32_t qk = sbase + L::OFF_QK;
 #pragma unroll
         for (int kk = 0; kk < DK / 16; ++kk) {
             const uint32_t ko = (kk >> 2) * L::QK_KB + (kk & 3) * 32;
             umma_bf16_ss(tmem + L::T_QK, sdesc_sw128(qk + ko, 16, 1024), sdesc_sw128(qk + ko + kCC * 128, 16, 1024),
-                         id64, kk > 0 ? 1u : 0u);
+                         id64k, kk > 0 ? 1u : 0u);
         }
         umma_commit(&bars[0]);
     }
@@ -931,19 +879,42 @@ __global__ void __launch_bounds__(256, 1) cb_grads_tc_kernel(const CbArgs a, int
     }
     sp = warp_sum(sp);
     if (lane == 0) basep[warp] = sp;
+    {
+        // dd_t . v_t: four threads per token, 32 value columns each, dd from the image (hi + lo)
+        const int t = tid & (kCC - 1), qv = tid >> 6;
+        float pv = 0.f;
+        if (t < nt && qv * 32 < DV) {
+            const uint16_t* vr = a.v + (tokbase + t) * DV + qv * 32;
+#pragma unroll
+            for (int j = 0; j < 4; ++j) {
+                float v8[8];
+                unpack_bf16x8(__ldg(reinterpret_cast<const uint4*>(vr) + j), v8);
+#pragma unroll
+                for (int i = 0; i < 8; ++i) {
+                    const int vv = qv * 32 + j * 8 + i;
+                    const uint32_t o = 16384 + sw128_off(vv, t);
+                    pv = fmaf(bf16_bits_to_f32(*reinterpret_cast<const uint16_t*>(sm + L::OFF_RH + o)) +
+                                  bf16_bits_to_f32(*reinterpret_cast<const uint16_t*>(sm + L::OFF_RL + o)),
+                              v8[i], pv);
+                }
+            }
+        }
+        pairp[qv * kCC + t] = pv;                   // pairp is free until the row work below
+    }
+    __syncthreads();
+    if (tid < kCC) ddv[tid] = pairp[tid] + pairp[kCC + tid] + pairp[2 * kCC + tid] + pairp[3 * kCC + tid];
     fence_async_smem();
     __syncthreads();
     const bool dead_b = *dead != 0;
     if (tid == 0 && !dead_b) {
         tc_fence_after();
-        constexpr uint32_t idN = idesc_bf16(128, DK, false, true);
+        constexpr uint32_t idN = idesc_bf16(128, DK, true, true);
         const uint32_t pa[3] = {rh, rh, rl}, pbs[3] = {sh, sl, sh};
 #pragma unroll
         for (int p = 0; p < 3; ++p)
 #pragma unroll
             for (int kk = 0; kk < DV / 16; ++kk) {
-                const uint32_t ko = (kk >> 2) * L::R_KB + (kk & 3) * 32;
-                umma_bf16_ss(tmem + L::T_XE, sdesc_sw128(pa[p] + ko + kCC * 128, 16, 1024),
+                umma_bf16_ss(tmem + L::T_XE, sdesc_sw128(pa[p] + 16384 + kk * 2048, 16384, 1024),
                              sdesc_sw128(pbs[p] + kk * 2048, 16384, 1024), idN, (p > 0 || kk > 0) ? 1u : 0u);
             }
         umma_commit(&bars[1]);
@@ -1183,9 +1154,9 @@ CbWs cb_ws(size_t bh, int T, int dk, int dv) {
     w.rec = w.gv + al(nc * 3 * kCC * 4);
     w.ckS = w.rec + al(nc * crec_bytes(dk, dv));
     w.ckD = w.ckS + al(nc * dk * 512);               // S^T image (hi, lo): 128 rows x dk bf16 each
-    w.ckSb = w.ckD + al(nc * kCC * dv * 4);
+    w.ckSb = w.ckD + al(nc * 32768);                 // d^T image (hi, lo): 128 rows x 64 bf16 each
     w.ckDD = w.ckSb + al(nc * dk * 512);
-    w.dlogg = w.ckDD + al(nc * kCC * dv * 4);
+    w.dlogg = w.ckDD + al(nc * 32768);
     w.total = w.dlogg + al(bh * static_cast<size_t>(T) * 4) + 1024;
     return w;
 }
@@ -1260,9 +1231,9 @@ int prefill_bwd_chunked(const void* q, const void* k, const void* v, const float
     ar.gv = reinterpret_cast<float*>(ws + wl.gv);
     ar.rec = ws + wl.rec;
     ar.ckS = ws + wl.ckS;
-    ar.ckD = reinterpret_cast<float*>(ws + wl.ckD);
+    ar.ckD = ws + wl.ckD;
     ar.ckSb = ws + wl.ckSb;
-    ar.ckDD = reinterpret_cast<float*>(ws + wl.ckDD);
+    ar.ckDD = ws + wl.ckDD;
     ar.dlogg = reinterpret_cast<float*>(ws + wl.dlogg);
     ar.err = device_error_word();
     ar.B = B;
