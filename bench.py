@@ -511,31 +511,43 @@ def run_varlen(world, dev, stream):
 
 def run_backward(world, dev, stream, hbm_peak):
     """Config 1's backward (gdn_prefill_bwd): B=4, T=4096, H=16, dk=dv=128, fp32 dO and
-    a final-state gradient.  It runs in token windows from checkpoints of the state at
-    every window start; its kernels store and reload every token's state of the window
-    (fp32): the state traffic per call is ~2 x B*H*T*dk*dv*4 bytes."""
+    a final-state gradient, with both algorithms:
+      chunked (the default): per-chunk products on tcgen05 and the two chunk
+        recurrences, workspace of chunk checkpoints and operand records;
+      token: token-recurrent on CUDA cores, in token windows from state checkpoints.
+    Algorithmic bytes per call: what any backward moves at least, q, k, v (bf16), dO
+    (fp32), the gates (fp32) in and dq, dk, dv (fp32), da, db out:
+    B*H*T*(2*dk*2 + dv*2 + dv*4 + 8 + 2*dk*4 + dv*4 + 8) = 742 MB at config 1."""
     import torch
-    from gdn_18646_b200 import ops
+    from gdn_18646_b200 import ops, _lib
     c = C1
     inp = gen_prefill(c["B"], c["T"], c["H"], c["dk"], c["dv"], 99, dev)
     g = torch.Generator(device=dev).manual_seed(98)
     dO = torch.randn(c["B"], c["H"], c["T"], c["dv"], generator=g, device=dev)
     dSf = torch.randn(c["B"], c["H"], c["dk"], c["dv"], generator=g, device=dev) * 0.1
 
-    def step():
+    def step(algorithm):
         ops.prefill_backward(inp["q"], inp["k"], inp["v"], inp["A_log"], inp["a"], inp["b"], dO,
-                             state_in=inp["state_in"], dS_final=dSf, scale=c["dk"] ** -0.5)
+                             state_in=inp["state_in"], dS_final=dSf, scale=c["dk"] ** -0.5, algorithm=algorithm)
 
-    ms = timed(step, 3, 1, world, stream) / 3
+    ms = timed(lambda: step("chunked"), 5, 2, world, stream) / 5
+    ms_token = timed(lambda: step("token"), 2, 1, world, stream) / 2
     toks = c["B"] * c["T"]
-    state_bytes = c["B"] * c["H"] * c["T"] * c["dk"] * c["dv"] * 4
-    traffic = 2 * state_bytes                        # states, written once and read once
-    from gdn_18646_b200 import _lib
-    ws = _lib.lib().gdn_prefill_bwd_workspace_bytes(c["B"], c["T"], c["H"], c["dk"], c["dv"])
+    alg = c["B"] * c["H"] * c["T"] * (2 * c["dk"] * 2 + c["dv"] * 2 + c["dv"] * 4 + 8 + 2 * c["dk"] * 4
+                                      + c["dv"] * 4 + 8)
+    lib = _lib.lib()
+    ws = lib.gdn_prefill_bwd_workspace_bytes(c["B"], c["T"], c["H"], c["dk"], c["dv"])
+    _lib.call("gdn_prefill_bwd_set_algorithm", _lib.GDN_BWD_TOKEN)
+    try:
+        ws_token = lib.gdn_prefill_bwd_workspace_bytes(c["B"], c["T"], c["H"], c["dk"], c["dv"])
+    finally:
+        _lib.call("gdn_prefill_bwd_set_algorithm", _lib.GDN_BWD_AUTO)
     return {"config": "config1 backward: B=4 T=4096 H=16 dk=dv=128, fp32 dO + final-state gradient",
-            "ms": ms, "tokens_per_s": toks / (ms * 1e-3), "workspace_gb": ws / 1e9,
-            "state_traffic_gbs": traffic / (ms * 1e-3) / 1e9,
-            "state_traffic_frac_of_measured_hbm": traffic / (ms * 1e-3) / 1e9 / hbm_peak}
+            "algorithm": "chunked", "ms": ms, "tokens_per_s": toks / (ms * 1e-3), "workspace_gb": ws / 1e9,
+            "alg_bytes_per_call": alg, "alg_gbs": alg / (ms * 1e-3) / 1e9,
+            "alg_frac_of_measured_hbm": alg / (ms * 1e-3) / 1e9 / hbm_peak,
+            "token_recurrent": {"ms": ms_token, "workspace_gb": ws_token / 1e9},
+            "speedup_over_token_recurrent": ms_token / ms}
 
 
 # Config 4's o all-gather runs window by window beside the prefill: windows of
@@ -854,9 +866,8 @@ def run_only(args):
         def step():
             sharded_out_proj(y, W, buf, out=o)
     elif args.only in ("backward", "backward_config1"):
-        # "backward": config 1's head shape at B=1, T=1024, a 2.1 GB workspace, small enough
-        # for a multi-pass capture; "backward_config1": config 1 itself (34 GB workspace,
-        # duration-only launch lists)
+        # "backward": config 1's head shape at B=1, T=1024, small enough for a multi-pass
+        # capture; "backward_config1": config 1 itself (the default, chunked, algorithm)
         Bb, Tb = (1, 1024) if args.only == "backward" else (C1["B"], C1["T"])
         inp = gen_prefill(Bb, Tb, C1["H"], C1["dk"], C1["dv"], 99, dev)
         g = torch.Generator(device=dev).manual_seed(98)

@@ -22,17 +22,26 @@
 //                  + sum_{u>t} G_u k_u.(S dr_u) + sum_{s<t} (G_L/G_s) k_s.(Sb d_s)
 //                  + sum_{s<t<=u} P_us (dO'_u.d_s) + sum_{s<t<u} M_us (dr_u.d_s) + r_t.dr_t
 //
-// Launches (all fp32 on CUDA cores):
-//   cb_mats_kernel     per chunk: M, P, A = (I + diag(b) M)^-1 and the gate vectors (Lambda, b,
-//                      m), all chunks in parallel, so that both substitutions become products:
-//                      d = A (b (v - G K S)) and dd = A^T X;
-//   cb_forward_kernel  per (b, h, 64 value columns): the forward chunk recurrence, storing S at
-//                      every chunk start and the chunk's d rows;
-//   cb_reverse_kernel  per (b, h, 64 value columns): the reverse chunk recurrence, storing Sb at
-//                      every chunk end and the dd rows (the value columns are independent in both);
-//   cb_grads_kernel    per chunk: every per-token gradient from S, Sb, D and dd, then the gate
-//                      chain rule into da, db;
-//   the head sums of dA_log, ddt_bias (the token-recurrent backward's bwd_head_kernel).
+// Four launches; every product on tcgen05 (kind::f16, fp32 accumulation in TMEM)
+// with fp32 operands split into bf16 hi + lo (hi.hi + hi.lo + lo.hi, relative
+// error ~2^-16; q, k, v exact in bf16):
+//   cb_mats_kernel      per chunk, all chunks in parallel: the gate vectors, [Q; K] K^T,
+//                       P, M and A = (I + diag(b) M)^-1 (16 x 16 diagonal blocks by
+//                       substitution, the blocks below by products), written as the
+//                       chunk's record: operand images in the shared-memory layout of the
+//                       products (k, A, A^T, P^T, scale G q, (m dO)^T, v) and decay tables;
+//   cb_chain_kernel     both chunk recurrences at once (one CTA per (b, h) and direction,
+//                       one value column of the state per thread in registers): per chunk
+//                       three products (K S or K Sb, then A or A^T, then the rank-64 state
+//                       update), the record bulk-copied in and prefetched into L2 a chunk
+//                       ahead; it stores the state at every chunk start (S) or end (Sb)
+//                       and the chunk's d (dd) rows as bf16 hi/lo images, and dv = b dd;
+//   cb_grads_tc_kernel  per chunk, persistent: the images bulk-loaded as MN-major
+//                       operands of five products ([dO'; dd] S^T, [dO'; dd] D^T, [Q; K] K^T,
+//                       [dd; D] Sb^T, and the decay-masked 64 x 64 matrices times k and q),
+//                       the per-token scalars of g dg and db' from the same accumulators,
+//                       then the gate chain rule into da, db;
+//   the head sums of dA_log, ddt_bias (backward.cu's bwd_head_kernel).
 #include "common.cuh"
 
 namespace gdn {
