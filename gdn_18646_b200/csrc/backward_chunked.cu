@@ -682,8 +682,8 @@ __global__ void __launch_bounds__(128, 1) cb_chain_kernel(const CbArgs a) {
 //   T3 = [dO'; dd] D^T      -> lanes 0-63 dO' D^T,       lanes 64-127 Y = dd D^T
 //   T5 = [Q; K] K^T         -> lanes 0-63 Q K^T,         lanes 64-127 K K^T
 //   T2 = [dd; D] Sb^T       -> lanes 64-127 X_e = D Sb^T
-//   T4 = [F1; F2 + F2^T] K^T' + [0; scale F1^T] Q^T'  (K^T', Q^T' the k, q tiles
-//        transposed; F1 = (dO' D^T) * [G_t/G_s, s <= t], F2 = -b (Y * [G_t/G_s, s < t]))
+//   T4 = [F1; F2 + F2^T] K + [0; scale F1^T] Q  (k, q rows of [Q; K] as MN-major operands;
+//        F1 = (dO' D^T) * [G_t/G_s, s <= t], F2 = -b (Y * [G_t/G_s, s < t]))
 // so that, with TMEM lane = token row (lanes 0-63 the dq side, 64-127 the dk side),
 //   dq_t = scale (G_t X_q + T4)_t,   dk_t = (G_L/G_t) X_e - G_t b_t X_dd + T4_{64+t},
 // and the per-token scalars of g dg and db' are row dot products of the same
@@ -703,18 +703,21 @@ struct GtLayout {
     static constexpr int OFF_RH = 0, OFF_RL = R_BYTES, OFF_SH = 2 * R_BYTES, OFF_SL = OFF_SH + S_BYTES;
     static constexpr int AB_END = OFF_SL + S_BYTES;
     static constexpr int OFF_A1H = 0, OFF_A1L = 16384, OFF_A2H = 32768, OFF_A2L = 49152;   // after T2
-    static constexpr int OFF_KT = 65536, OFF_QT = OFF_KT + DK * 128;
-    static constexpr int C_END = OFF_QT + DK * 128;
+    static constexpr int C_END = 65536;
     static constexpr int OFF_QK = AB_END > C_END ? AB_END : C_END;
-    static constexpr int QK_REGION = QK_BYTES > 32768 ? QK_BYTES : 32768;       // then F1, F2 fp32 [64][64]
-    static constexpr int OFF_MISC = OFF_QK + QK_REGION;
-    static constexpr int MISC_FLOATS = 912;
+    static constexpr int OFF_F = OFF_QK + QK_BYTES;                 // F1 (s <= t), F2 (s < t): packed rows
+    static constexpr int OFF_MISC = OFF_F + 4096 * 4;
+    static constexpr int MISC_FLOATS = 1024;
     static constexpr int OFF_BAR = OFF_MISC + MISC_FLOATS * 4;
     static constexpr int BYTES = OFF_BAR + 64 + 1024;      // + slack to align the dynamic base to 1024
     static constexpr uint32_t T_XS = 0, T_XE = DK, T_X4 = 2 * DK, T_DD = 3 * DK, T_QK = 3 * DK + 64;
     static_assert(BYTES <= 232448, "shared memory");
     static_assert(T_QK + 64 <= 512, "TMEM columns");
 };
+
+// The thread of the gradient kernel that issues its MMAs and bulk copies and waits for them: in
+// warp 7, which has no row work, so that issuing never delays the row threads (warps 0-3).
+constexpr int kIssuer = 255;
 
 template <int DK, int DV>
 __global__ void __launch_bounds__(256, 1) cb_grads_tc_kernel(const CbArgs a, int nchunks) {
@@ -738,8 +741,9 @@ __global__ void __launch_bounds__(256, 1) cb_grads_tc_kernel(const CbArgs a, int
     int* dead = reinterpret_cast<int*>(misc + 904);
     uint64_t* bars = reinterpret_cast<uint64_t*>(sm + L::OFF_BAR);
     uint32_t* tslot = reinterpret_cast<uint32_t*>(bars + 5);
-    float* F1s = reinterpret_cast<float*>(sm + L::OFF_QK);          // [64][64], row t rotated by t
-    float* F2s = F1s + 4096;
+    float* F1s = reinterpret_cast<float*>(sm + L::OFF_F);           // row t at t (t + 1) / 2, s <= t
+    float* F2s = F1s + kCC * (kCC + 1) / 2;                         // row t at t (t - 1) / 2, s < t
+    float* lam2 = misc + 912;                      // Lambda log2(e) [64]
 
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
     const uint32_t sbase = smem_u32(sm);
@@ -784,7 +788,7 @@ __global__ void __launch_bounds__(256, 1) cb_grads_tc_kernel(const CbArgs a, int
     const uint8_t* ckD = a.ckD + static_cast<long>(cid) * 32768;
     const uint8_t* ckDD = a.ckDD + static_cast<long>(cid) * 32768;
     const uint8_t* rec = a.rec + static_cast<long>(cid) * CRec<DK, DV>::BYTES;
-    if (tid == 0) {
+    if (tid == kIssuer) {
         // the S^T image -> the S region; [dO'^T | dd^T | d^T] (hi, lo) -> the T image
         mbar_arrive_expect_tx(&bars[3], 2 * L::S_BYTES + 6 * 16384);
         bulk_load(sm + L::OFF_SH, ckS, 2 * L::S_BYTES, &bars[3]);
@@ -799,6 +803,7 @@ __global__ void __launch_bounds__(256, 1) cb_grads_tc_kernel(const CbArgs a, int
     if (tid < kCC) {
         const float* gv = a.gv + static_cast<long>(cid) * 3 * kCC;
         lam[tid] = gv[tid];
+        lam2[tid] = gv[tid] * 1.4426950408889634f;
         Gs[tid] = expf(gv[tid]);
         bms[tid] = gv[kCC + tid];
         ms[tid] = gv[2 * kCC + tid];
@@ -824,7 +829,7 @@ __global__ void __launch_bounds__(256, 1) cb_grads_tc_kernel(const CbArgs a, int
     fence_async_smem();
     __syncthreads();
     const uint32_t rh = sbase + L::OFF_RH, rl = sbase + L::OFF_RL, sh = sbase + L::OFF_SH, sl = sbase + L::OFF_SL;
-    if (tid == 0) {
+    if (tid == kIssuer) {
         if (!mbar_wait(&bars[3], 0, a.err)) *dead = 1;
         tc_fence_after();
         // Every operand here is MN-major (rows v of the images, 16 rows per K step): A = the
@@ -858,7 +863,7 @@ __global__ void __launch_bounds__(256, 1) cb_grads_tc_kernel(const CbArgs a, int
     // ---- phase B: the Sb^T image over the S image once T1 has read it, <S, Sb>, then T2
     if (!mbar_wait(&bars[0], ph, a.err)) *dead = 1;
     tc_fence_after();
-    if (tid == 0) {
+    if (tid == kIssuer) {
         mbar_arrive_expect_tx(&bars[3], 2 * L::S_BYTES);
         bulk_load(sm + L::OFF_SH, ckSb, 2 * L::S_BYTES, &bars[3]);
     }
@@ -915,7 +920,7 @@ __global__ void __launch_bounds__(256, 1) cb_grads_tc_kernel(const CbArgs a, int
     fence_async_smem();
     __syncthreads();
     const bool dead_b = *dead != 0;
-    if (tid == 0 && !dead_b) {
+    if (tid == kIssuer && !dead_b) {
         tc_fence_after();
         constexpr uint32_t idN = idesc_bf16(128, DK, true, true);
         const uint32_t pa[3] = {rh, rh, rl}, pbs[3] = {sh, sl, sh};
@@ -952,9 +957,31 @@ __global__ void __launch_bounds__(256, 1) cb_grads_tc_kernel(const CbArgs a, int
                 for (int i = 0; i < 8; ++i) dot = fmaf(x[8 * j + i], y[i], dot);
             }
         }
-        named_bar(1, 128);                          // [Q; K] read by all: its bytes become F1, F2
-        const float lt = lam[t], Gt = Gs[t], bt = bms[t];
-        float* Fs = side ? F2s : F1s;
+        if (side == 1) {
+            // k_t . X_e once T2 has completed (X_e = D Sb^T on these lanes)
+            if (!mbar_wait(&bars[1], ph, a.err)) *dead = 1;
+            tc_fence_after();
+            float de = 0.f;
+#pragma unroll 1
+            for (int cb = 0; cb < DK; cb += 32) {
+                float x[32];
+                tmem_ld32(lb + L::T_XE + cb, x);
+                tmem_ld_wait();
+#pragma unroll
+                for (int j = 0; j < 4; ++j) {
+                    const int col = cb + 8 * j;
+                    float y[8];
+                    unpack_bf16x8(*reinterpret_cast<const uint4*>(sm + L::OFF_QK + (col >> 6) * L::QK_KB +
+                                                                  sw128_chunk(r, (col & 63) >> 3)),
+                                  y);
+#pragma unroll
+                    for (int i = 0; i < 8; ++i) de = fmaf(x[8 * j + i], y[i], de);
+                }
+            }
+            s_e[t] = expf(lL - lam[t]) * de;
+        }
+        const float lt2 = lam2[t], Gt = Gs[t], bt = bms[t];
+        float* Fs = side ? F2s + t * (t - 1) / 2 : F1s + t * (t + 1) / 2;
         float pre = 0.f, krs = 0.f;
         float cv[kCC];                              // this row's contribution to each token's pair sum
 #pragma unroll
@@ -966,7 +993,7 @@ __global__ void __launch_bounds__(256, 1) cb_grads_tc_kernel(const CbArgs a, int
 #pragma unroll
             for (int i = 0; i < 32; ++i) {
                 const int s = cb + i;
-                const float ex = expf(lt - lam[s]);
+                const float ex = ex2_approx(lt2 - lam2[s]);   // G_t / G_s
                 float f, e;
                 bool in;
                 if (side == 0) {
@@ -980,7 +1007,7 @@ __global__ void __launch_bounds__(256, 1) cb_grads_tc_kernel(const CbArgs a, int
                     f = in ? -bt * x[i] * ex : 0.f; // F2
                     e = -bt * my;                   // M_ts (dr_t . d_s)
                 }
-                Fs[t * kCC + ((s + t) & (kCC - 1))] = f;
+                if (in) Fs[s] = f;
                 // pair sums: token s gets sum_{s' < s} e_{s'} from rows u >= s (side 0) or u > s (side 1)
                 cv[s] = in ? pre : 0.f;
                 pre += e;
@@ -1012,7 +1039,7 @@ __global__ void __launch_bounds__(256, 1) cb_grads_tc_kernel(const CbArgs a, int
     }
 
     // ---- phase C: the T4 operands over the freed images once T2 completed
-    if (tid == 0 && !dead_b && !mbar_wait(&bars[1], ph, a.err)) *dead = 1;
+    if (tid == kIssuer && !dead_b && !mbar_wait(&bars[1], ph, a.err)) *dead = 1;
     __syncthreads();
     const bool dead_c = *dead != 0;
     tc_fence_after();
@@ -1024,68 +1051,34 @@ __global__ void __launch_bounds__(256, 1) cb_grads_tc_kernel(const CbArgs a, int
             for (int i = 0; i < 8; ++i) {
                 const int s = ch * 8 + i;
                 if (row < kCC) {
-                    f1[i] = F1s[t * kCC + ((s + t) & (kCC - 1))];
+                    f1[i] = s <= t ? F1s[t * (t + 1) / 2 + s] : 0.f;
                     f2[i] = 0.f;
                 } else {
-                    f1[i] = F2s[t * kCC + ((s + t) & (kCC - 1))] + F2s[s * kCC + ((t + s) & (kCC - 1))];
-                    f2[i] = scale * F1s[s * kCC + ((t + s) & (kCC - 1))];
+                    f1[i] = s < t ? F2s[t * (t - 1) / 2 + s] : (s > t ? F2s[s * (s - 1) / 2 + t] : 0.f);
+                    f2[i] = s >= t ? scale * F1s[s * (s + 1) / 2 + t] : 0.f;
                 }
             }
             const uint32_t off = sw128_chunk(row, ch);
             split_store8(sm + L::OFF_A1H + off, sm + L::OFF_A1L + off, f1);
             split_store8(sm + L::OFF_A2H + off, sm + L::OFF_A2L + off, f2);
         }
-#pragma unroll
-        for (int it = tid; it < 8 * DK; it += 256) {
-            const int ch = it / DK, d = it - ch * DK;
-            uint16_t kv[8], qv[8];
-#pragma unroll
-            for (int i = 0; i < 8; ++i) {
-                const int s = ch * 8 + i;
-                kv[i] = s < nt ? a.k[(tokbase + s) * DK + d] : static_cast<uint16_t>(0);
-                qv[i] = s < nt ? a.q[(tokbase + s) * DK + d] : static_cast<uint16_t>(0);
-            }
-            const uint32_t off = sw128_chunk(d, ch);
-            *reinterpret_cast<uint4*>(sm + L::OFF_KT + off) =
-                make_uint4(kv[0] | (uint32_t(kv[1]) << 16), kv[2] | (uint32_t(kv[3]) << 16),
-                           kv[4] | (uint32_t(kv[5]) << 16), kv[6] | (uint32_t(kv[7]) << 16));
-            *reinterpret_cast<uint4*>(sm + L::OFF_QT + off) =
-                make_uint4(qv[0] | (uint32_t(qv[1]) << 16), qv[2] | (uint32_t(qv[3]) << 16),
-                           qv[4] | (uint32_t(qv[5]) << 16), qv[6] | (uint32_t(qv[7]) << 16));
-        }
     }
     fence_async_smem();
     __syncthreads();
-    if (tid == 0 && !dead_c) {
+    if (tid == kIssuer && !dead_c) {
         tc_fence_after();
-        constexpr uint32_t idN = idesc_bf16(128, DK, false, false);
+        constexpr uint32_t idN = idesc_bf16(128, DK, false, true);
         const uint32_t pa[4] = {sbase + L::OFF_A1H, sbase + L::OFF_A1L, sbase + L::OFF_A2H, sbase + L::OFF_A2L};
-        const uint32_t pb[4] = {sbase + L::OFF_KT, sbase + L::OFF_KT, sbase + L::OFF_QT, sbase + L::OFF_QT};
+        // B = the k rows (8 KB into each 16 KB block of [Q; K]) or the q rows, MN-major (N = d)
+        const uint32_t qk = sbase + L::OFF_QK;
+        const uint32_t pb[4] = {qk + kCC * 128, qk + kCC * 128, qk, qk};
 #pragma unroll
         for (int p = 0; p < 4; ++p)
 #pragma unroll
             for (int kk = 0; kk < 4; ++kk)
                 umma_bf16_ss(tmem + L::T_X4, sdesc_sw128(pa[p] + kk * 32, 16, 1024),
-                             sdesc_sw128(pb[p] + kk * 32, 16, 1024), idN, (p > 0 || kk > 0) ? 1u : 0u);
+                             sdesc_sw128(pb[p] + kk * 2048, L::QK_KB, 1024), idN, (p > 0 || kk > 0) ? 1u : 0u);
         umma_commit(&bars[2]);
-    }
-    // k_t . X_e on the dk side (k_t read from the transposed k tile)
-    if (tid >= 64 && tid < 128 && !dead_c) {
-        const int t = tid - kCC;
-        const uint32_t lb = tmem + (static_cast<uint32_t>(warp * 32) << 16);
-        float dot = 0.f;
-#pragma unroll 1
-        for (int cb = 0; cb < DK; cb += 32) {
-            float x[32];
-            tmem_ld32(lb + L::T_XE + cb, x);
-            tmem_ld_wait();
-#pragma unroll
-            for (int i = 0; i < 32; ++i)
-                dot = fmaf(x[i], bf16_bits_to_f32(*reinterpret_cast<const uint16_t*>(sm + L::OFF_KT +
-                                                                                     sw128_off(cb + i, t))),
-                           dot);
-        }
-        s_e[t] = expf(lL - lam[t]) * dot;
     }
     __syncthreads();
     if (tid < kCC && tid < nt && !dead_c) {
@@ -1094,9 +1087,12 @@ __global__ void __launch_bounds__(256, 1) cb_grads_tc_kernel(const CbArgs a, int
 #pragma unroll
         for (int w = 0; w < 8; ++w) base += basep[w];
         float sa = 0.f, scc = 0.f, se = 0.f;
-        for (int u = t; u < kCC; ++u) sa += s_a[u];
-        for (int u = t + 1; u < kCC; ++u) scc += s_c[u];
-        for (int s = 0; s < t; ++s) se += s_e[s];
+#pragma unroll
+        for (int u = 0; u < kCC; ++u) {            // masked sums, fully unrolled: all loads in flight
+            sa += u >= t ? s_a[u] : 0.f;
+            scc += u > t ? s_c[u] : 0.f;
+            se += u < t ? s_e[u] : 0.f;
+        }
         const float pair = pairp[t] + pairp[kCC + t] + pairp[2 * kCC + t] + pairp[3 * kCC + t];
         const float dlogg = GL * base + sa + scc + se + pair + s_rdr[t];
         const long tok = tokbase + t;
@@ -1109,7 +1105,7 @@ __global__ void __launch_bounds__(256, 1) cb_grads_tc_kernel(const CbArgs a, int
     }
 
     // ---- phase D: dq, dk (warps w and w + 4 share lanes 32 (w % 4) .. + 31, half the columns each)
-    if (tid == 0 && !dead_c && !mbar_wait(&bars[2], ph, a.err)) *dead = 1;
+    if (tid == kIssuer && !dead_c && !mbar_wait(&bars[2], ph, a.err)) *dead = 1;
     __syncthreads();
     tc_fence_after();
     if (*dead == 0) {
