@@ -432,7 +432,7 @@ struct ChainSmem {
 };
 
 template <int DK, int DV>
-__global__ void __launch_bounds__(128, 1) cb_chain_kernel(const CbArgs a) {
+__global__ void __launch_bounds__(256, 1) cb_chain_kernel(const CbArgs a) {
     using R = CRec<DK, DV>;
     using L = ChainSmem<DK, DV>;
     extern __shared__ uint8_t smem_raw[];
@@ -445,7 +445,11 @@ __global__ void __launch_bounds__(128, 1) cb_chain_kernel(const CbArgs a) {
     const int BH = a.B * a.H;
     const bool rev = static_cast<int>(blockIdx.x) >= BH;
     const int bh = rev ? blockIdx.x - BH : blockIdx.x;
-    const int tid = threadIdx.x, warp = tid >> 5, v = tid;
+    // thread (half, v): TMEM lane v (warps w and w + 4 share lanes 32 (w % 4) ..), state
+    // columns d in [half DK/2, half DK/2 + DK/2) and tokens [32 half, 32 half + 32)
+    const int tid = threadIdx.x, warp = tid >> 5, v = tid & 127, half = tid >> 7;
+    constexpr int DH = DK / 2;
+    const int d0 = half * DH, t0h = half * 32;
     const bool col_ok = v < DV;
     const uint32_t sbase = smem_u32(sm), rbase = sbase + L::OFF_REC;
     const uint32_t T_D1 = 0, T_Z = 64, T_D2 = 128, T_U = 256;
@@ -480,17 +484,17 @@ __global__ void __launch_bounds__(128, 1) cb_chain_kernel(const CbArgs a) {
         issue(rev ? a.n - 1 : 0);
     }
     if (warp == 0) tmem_alloc(tslot, 512);
-    float S[DK];
+    float S[DH];
     {
         const float* src = rev ? a.dS_final : a.state_in;
         const long s0 = static_cast<long>(bh) * DK * DV;
 #pragma unroll
-        for (int d = 0; d < DK; ++d) S[d] = (src && col_ok) ? src[s0 + static_cast<long>(d) * DV + v] : 0.f;
+        for (int d = 0; d < DH; ++d) S[d] = (src && col_ok) ? src[s0 + static_cast<long>(d0 + d) * DV + v] : 0.f;
     }
     tc_fence_before();
     __syncthreads();
     tc_fence_after();
-    const uint32_t tmem = *tslot, lane_t = tmem + (static_cast<uint32_t>(warp * 32) << 16);
+    const uint32_t tmem = *tslot, lane_t = tmem + (static_cast<uint32_t>((warp & 3) * 32) << 16);
     uint32_t mph = 0;                              // parity of the next products-done phase
     bool ok = true;
     auto mma_wait = [&]() {
@@ -519,15 +523,14 @@ __global__ void __launch_bounds__(128, 1) cb_chain_kernel(const CbArgs a) {
         //      image (rows v), which is also the checkpoint: bulk-stored for the gradient kernel
         {
 #pragma unroll
-            for (int b = 0; b < DK / 64; ++b)
+            for (int q = 0; q < DH / 8; ++q) {
+                float y[8];
 #pragma unroll
-                for (int ch = 0; ch < 8; ++ch) {
-                    float y[8];
-#pragma unroll
-                    for (int i = 0; i < 8; ++i) y[i] = S[b * 64 + ch * 8 + i];
-                    const uint32_t off = b * 16384 + sw128_chunk(v, ch);
-                    split_store8(sm + L::OFF_SH + off, sm + L::OFF_SL + off, y);
-                }
+                for (int i = 0; i < 8; ++i) y[i] = S[q * 8 + i];
+                const int col = d0 + 8 * q;
+                const uint32_t off = (col >> 6) * 16384 + sw128_chunk(v, (col & 63) >> 3);
+                split_store8(sm + L::OFF_SH + off, sm + L::OFF_SL + off, y);
+            }
         }
         fence_async_smem();
         __syncthreads();
@@ -560,8 +563,8 @@ __global__ void __launch_bounds__(128, 1) cb_chain_kernel(const CbArgs a) {
         }
         mma_wait();
         // ---- y (forward) or X (reverse) -> the 64-column image
-#pragma unroll
-        for (int cb = 0; cb < kCC; cb += 32) {
+        {
+            const int cb = t0h;
             float d1[32], z[32];
             tmem_ld32(lane_t + T_D1 + cb, d1);
             if (rev) tmem_ld32(lane_t + T_Z + cb, z);
@@ -604,8 +607,8 @@ __global__ void __launch_bounds__(128, 1) cb_chain_kernel(const CbArgs a) {
         {
             const int nt = min(kCC, a.T - c * kCC);
             float* dvo = a.dv + (static_cast<long>(bh) * a.T + c * kCC) * DV + v;
-#pragma unroll
-            for (int cb = 0; cb < kCC; cb += 32) {
+            {
+                const int cb = t0h;
                 float d2[32];
                 tmem_ld32(lane_t + T_D2 + cb, d2);
                 tmem_ld_wait();
@@ -650,9 +653,9 @@ __global__ void __launch_bounds__(128, 1) cb_chain_kernel(const CbArgs a) {
         if (tid == 0 && step + 1 < a.n) issue(rev ? c - 1 : c + 1);   // the record is no longer read
         // ---- S <- G_L S + U
 #pragma unroll
-        for (int cb = 0; cb < DK; cb += 32) {
+        for (int cb = 0; cb < DH; cb += 32) {
             float u[32];
-            tmem_ld32(lane_t + T_U + cb, u);
+            tmem_ld32(lane_t + T_U + d0 + cb, u);
             tmem_ld_wait();
 #pragma unroll
             for (int i = 0; i < 32; ++i) S[cb + i] = fmaf(GL, S[cb + i], u[i]);
@@ -667,7 +670,7 @@ __global__ void __launch_bounds__(128, 1) cb_chain_kernel(const CbArgs a) {
     if (rev && col_ok && a.dstate_in && *dead == 0) {
         const long s0 = static_cast<long>(bh) * DK * DV;
 #pragma unroll
-        for (int d = 0; d < DK; ++d) a.dstate_in[s0 + static_cast<long>(d) * DV + v] = S[d];
+        for (int d = 0; d < DH; ++d) a.dstate_in[s0 + static_cast<long>(d0 + d) * DV + v] = S[d];
     }
     tc_fence_before();
     __syncthreads();
@@ -1183,7 +1186,7 @@ int launch_cb(const CbArgs& a, cudaStream_t st) {
     cb_mats_kernel<DK, DV><<<nchunks, 256, MatsSmem<DK>::BYTES, st>>>(a);
     int s = launch_status("gdn_prefill_bwd (chunk matrices)");
     if (s != GDN_OK) return s;
-    cb_chain_kernel<DK, DV><<<2 * a.B * a.H, 128, ChainSmem<DK, DV>::BYTES, st>>>(a);
+    cb_chain_kernel<DK, DV><<<2 * a.B * a.H, 256, ChainSmem<DK, DV>::BYTES, st>>>(a);
     if ((s = launch_status("gdn_prefill_bwd (chunk recurrences)")) != GDN_OK) return s;
     int nsm = 148;
     {
