@@ -710,7 +710,7 @@ struct GtLayout {
     static constexpr int OFF_QK = AB_END > C_END ? AB_END : C_END;
     static constexpr int OFF_F = OFF_QK + QK_BYTES;                 // F1 (s <= t), F2 (s < t): packed rows
     static constexpr int OFF_MISC = OFF_F + 4096 * 4;
-    static constexpr int MISC_FLOATS = 1024;
+    static constexpr int MISC_FLOATS = 2048;
     static constexpr int OFF_BAR = OFF_MISC + MISC_FLOATS * 4;
     static constexpr int BYTES = OFF_BAR + 64 + 1024;      // + slack to align the dynamic base to 1024
     static constexpr uint32_t T_XS = 0, T_XE = DK, T_X4 = 2 * DK, T_DD = 3 * DK, T_QK = 3 * DK + 64;
@@ -747,6 +747,10 @@ __global__ void __launch_bounds__(256, 1) cb_grads_tc_kernel(const CbArgs a, int
     float* F1s = reinterpret_cast<float*>(sm + L::OFF_F);           // row t at t (t + 1) / 2, s <= t
     float* F2s = F1s + kCC * (kCC + 1) / 2;                         // row t at t (t - 1) / 2, s < t
     float* lam2 = misc + 912;                      // Lambda log2(e) [64]
+    float* dotp = misc + 1024;                     // [2 halves][128 rows] row dot partials
+    float* dep = misc + 1280;                      // [2][128] k . X_e partials
+    float* krsp = misc + 1536;                     // [2][128] r . dd partials (the M Y part)
+    float* pre32 = misc + 1792;                    // [128] per row: sum of its pair terms over s < 32
 
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
     const uint32_t sbase = smem_u32(sm);
@@ -938,37 +942,19 @@ __global__ void __launch_bounds__(256, 1) cb_grads_tc_kernel(const CbArgs a, int
     }
     const float scale = a.scale;
     const float lL = lam[kCC - 1], GL = Gs[kCC - 1];
-    // row work on warps 0-3: thread r = TMEM lane r, token t = r % 64, side = r / 64
-    if (tid < 128 && !dead_b) {
-        const int r = tid, t = r & (kCC - 1), side = r >> 6;
-        const uint32_t lb = tmem + (static_cast<uint32_t>(warp * 32) << 16);
-        // q_t . X_q (side 0) or k_t . X_dd (side 1): row r of T1 against row r of [Q; K]
-        float dot = 0.f;
+    // row work on all 8 warps: thread (hf, r) = TMEM lane r (warps w and w + 4 share lanes
+    // 32 (w % 4) ..), token t = r % 64, side = r / 64; half hf takes half the columns of the
+    // row dot products and the tokens s in [32 hf, 32 hf + 32) of the decay-masked rows
+    if (!dead_b) {
+        const int hf = tid >> 7, r = tid & 127, t = r & (kCC - 1), side = r >> 6;
+        const uint32_t lb = tmem + (static_cast<uint32_t>((warp & 3) * 32) << 16);
+        // row r of an accumulator (columns [hf DK/2, hf DK/2 + DK/2)) against row r of [Q; K]
+        auto row_dot = [&](uint32_t col0) {
+            float acc = 0.f;
 #pragma unroll 1
-        for (int cb = 0; cb < DK; cb += 32) {
-            float x[32];
-            tmem_ld32(lb + L::T_XS + cb, x);
-            tmem_ld_wait();
-#pragma unroll
-            for (int j = 0; j < 4; ++j) {
-                const int col = cb + 8 * j;
-                float y[8];
-                unpack_bf16x8(*reinterpret_cast<const uint4*>(sm + L::OFF_QK + (col >> 6) * L::QK_KB +
-                                                              sw128_chunk(r, (col & 63) >> 3)),
-                              y);
-#pragma unroll
-                for (int i = 0; i < 8; ++i) dot = fmaf(x[8 * j + i], y[i], dot);
-            }
-        }
-        if (side == 1) {
-            // k_t . X_e once T2 has completed (X_e = D Sb^T on these lanes)
-            if (!mbar_wait(&bars[1], ph, a.err)) *dead = 1;
-            tc_fence_after();
-            float de = 0.f;
-#pragma unroll 1
-            for (int cb = 0; cb < DK; cb += 32) {
+            for (int cb = hf * (DK / 2); cb < (hf + 1) * (DK / 2); cb += 32) {
                 float x[32];
-                tmem_ld32(lb + L::T_XE + cb, x);
+                tmem_ld32(lb + col0 + cb, x);
                 tmem_ld_wait();
 #pragma unroll
                 for (int j = 0; j < 4; ++j) {
@@ -978,17 +964,24 @@ __global__ void __launch_bounds__(256, 1) cb_grads_tc_kernel(const CbArgs a, int
                                                                   sw128_chunk(r, (col & 63) >> 3)),
                                   y);
 #pragma unroll
-                    for (int i = 0; i < 8; ++i) de = fmaf(x[8 * j + i], y[i], de);
+                    for (int i = 0; i < 8; ++i) acc = fmaf(x[8 * j + i], y[i], acc);
                 }
             }
-            s_e[t] = expf(lL - lam[t]) * de;
+            return acc;
+        };
+        // q_t . X_q (side 0) or k_t . X_dd (side 1), then k_t . X_e (side 1) once T2 has completed
+        dotp[hf * 128 + r] = row_dot(L::T_XS);
+        if (side == 1) {
+            if (!mbar_wait(&bars[1], ph, a.err)) *dead = 1;
+            tc_fence_after();
+            dep[hf * 128 + r] = row_dot(L::T_XE);
         }
-        const float lt2 = lam2[t], Gt = Gs[t], bt = bms[t];
+        const float lt2 = lam2[t], bt = bms[t];
         float* Fs = side ? F2s + t * (t - 1) / 2 : F1s + t * (t + 1) / 2;
         float pre = 0.f, krs = 0.f;
-        float cv[kCC];                              // this row's contribution to each token's pair sum
-#pragma unroll
-        for (int cb = 0; cb < kCC; cb += 32) {
+        float cv[32];                               // this row's contribution to each token's pair sum
+        {
+            const int cb = hf * 32;
             float x[32], y[32];
             tmem_ld32(lb + L::T_DD + cb, x);        // dO' D^T row (side 0) or Y = dd D^T row (side 1)
             tmem_ld32(lb + L::T_QK + cb, y);        // Q K^T row or K K^T row
@@ -1011,16 +1004,20 @@ __global__ void __launch_bounds__(256, 1) cb_grads_tc_kernel(const CbArgs a, int
                     e = -bt * my;                   // M_ts (dr_t . d_s)
                 }
                 if (in) Fs[s] = f;
-                // pair sums: token s gets sum_{s' < s} e_{s'} from rows u >= s (side 0) or u > s (side 1)
-                cv[s] = in ? pre : 0.f;
+                // pair sums: token s gets sum_{s' < s} e_{s'} from rows u >= s (side 0) or u > s
+                // (side 1); the second half's prefix starts at zero, and the first half's row
+                // totals (pre32) are added back per token after the reduction
+                cv[i] = in ? pre : 0.f;
                 pre += e;
             }
         }
-        // sum cv over the warp's 32 rows by a butterfly reduce-scatter: after the
-        // stage of lane bit o a lane keeps the half of its values selected by that
-        // bit, so lane L ends with the sums for tokens 2L and 2L + 1
+        if (hf == 0) pre32[r] = pre;
+        krsp[hf * 128 + r] = krs;
+        // sum cv over the warp's 32 rows by a butterfly reduce-scatter: after the stage of lane
+        // bit o a lane keeps the half of its values selected by that bit, so lane L ends with
+        // the sum for token 32 hf + L
 #pragma unroll
-        for (int o = 16, n = kCC; o > 0; o >>= 1, n >>= 1) {
+        for (int o = 16, n = 32; o > 0; o >>= 1, n >>= 1) {
             const bool up = (lane & o) != 0;
 #pragma unroll
             for (int i = 0; i < n / 2; ++i) {
@@ -1029,15 +1026,21 @@ __global__ void __launch_bounds__(256, 1) cb_grads_tc_kernel(const CbArgs a, int
                 cv[i] = keep + __shfl_xor_sync(0xffffffffu, send, o);
             }
         }
-        pairp[warp * kCC + 2 * lane] = cv[0];
-        pairp[warp * kCC + 2 * lane + 1] = cv[1];
+        pairp[(warp & 3) * kCC + hf * 32 + lane] = cv[0];
+    }
+    __syncthreads();
+    if (tid < 128 && !dead_b) {
+        const int r = tid, t = r & (kCC - 1), side = r >> 6;
+        const float Gt = Gs[t], bt = bms[t];
+        const float dot = dotp[r] + dotp[128 + r];
         if (side == 0) {
             s_a[t] = Gt * scale * dot;
         } else {
-            const float kr = Gt * dot + krs;        // r_t . dd_t
+            const float kr = Gt * dot + krsp[r] + krsp[128 + r];   // r_t . dd_t
             s_c[t] = -Gt * bt * dot;
             s_dbm[t] = ddv[t] - kr;
             s_rdr[t] = -bt * kr;
+            s_e[t] = expf(lL - lam[t]) * (dep[r] + dep[128 + r]);
         }
     }
 
@@ -1096,7 +1099,11 @@ __global__ void __launch_bounds__(256, 1) cb_grads_tc_kernel(const CbArgs a, int
             scc += u > t ? s_c[u] : 0.f;
             se += u < t ? s_e[u] : 0.f;
         }
-        const float pair = pairp[t] + pairp[kCC + t] + pairp[2 * kCC + t] + pairp[3 * kCC + t];
+        float pair = pairp[t] + pairp[kCC + t] + pairp[2 * kCC + t] + pairp[3 * kCC + t];
+        if (t >= 32) {                             // the first half's row totals, rows u >= t / u > t
+#pragma unroll
+            for (int u = 32; u < kCC; ++u) pair += (u >= t ? pre32[u] : 0.f) + (u > t ? pre32[kCC + u] : 0.f);
+        }
         const float dlogg = GL * base + sa + scc + se + pair + s_rdr[t];
         const long tok = tokbase + t;
         a.dlogg[tok] = dlogg;
