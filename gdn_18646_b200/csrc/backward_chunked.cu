@@ -155,8 +155,8 @@ struct MatsSmem {
     static constexpr int OFF_A = OFF_L + kCC * 65 * 4;             // A           [64][65]
     static constexpr int OFF_P = OFF_A + kCC * 65 * 4;             // P           [64][65]
     static constexpr int OFF_T = OFF_P + kCC * 65 * 4;             // block sums  [3][16][17]
-    static constexpr int OFF_G = OFF_T + 3 * 16 * 17 * 4;          // Lambda, b, m [3][64]
-    static constexpr int OFF_BAR = OFF_G + 3 * kCC * 4;
+    static constexpr int OFF_G = OFF_T + 3 * 16 * 17 * 4;          // Lambda, b, m, Lambda log2(e) [4][64]
+    static constexpr int OFF_BAR = OFF_G + 4 * kCC * 4;
     static constexpr int BYTES = OFF_BAR + 16 + 1024;
 };
 
@@ -174,6 +174,7 @@ __global__ void __launch_bounds__(256) cb_mats_kernel(const CbArgs a) {
     float* lam = reinterpret_cast<float*>(sm + L::OFF_G);
     float* bms = lam + kCC;
     float* mks = lam + 2 * kCC;
+    float* lam2 = lam + 3 * kCC;
     uint64_t* bar = reinterpret_cast<uint64_t*>(sm + L::OFF_BAR);
     uint32_t* tslot = reinterpret_cast<uint32_t*>(bar + 1);
     const int cid = blockIdx.x, bh = cid / a.n, c = cid - bh * a.n;
@@ -238,11 +239,22 @@ __global__ void __launch_bounds__(256) cb_mats_kernel(const CbArgs a) {
                          kk > 0 ? 1u : 0u);
         }
         umma_commit(bar);
-        float s = 0.f;                                 // in-chunk cumulative log decay, in token order
-        for (int t = 0; t < kCC; ++t) {
-            s += lam[t];
-            lam[t] = s;
+    }
+    if (warp == 1) {
+        // in-chunk cumulative log decay: lane L holds tokens 2L, 2L + 1; inclusive scan over lanes
+        const int l = tid & 31;
+        const float x0 = lam[2 * l], x1 = lam[2 * l + 1];
+        float inc = x0 + x1;
+#pragma unroll
+        for (int o = 1; o < 32; o <<= 1) {
+            const float y = __shfl_up_sync(0xffffffffu, inc, o);
+            if (l >= o) inc += y;
         }
+        const float c0 = inc - x1;
+        lam[2 * l] = c0;
+        lam[2 * l + 1] = inc;
+        lam2[2 * l] = c0 * 1.4426950408889634f;
+        lam2[2 * l + 1] = inc * 1.4426950408889634f;
     }
     // v rows and (m dO)^T as stored: independent of the product
     {
@@ -295,7 +307,7 @@ __global__ void __launch_bounds__(256) cb_mats_kernel(const CbArgs a) {
     if (tid < 128) {
         // row r of the product: P row r (r < 64) or diag(b) M row r - 64
         const int r = tid, t = r & (kCC - 1);
-        const float lt = lam[t];
+        const float lt2 = lam2[t];
         const float bt = bms[t];
 #pragma unroll 1
         for (int cb = 0; cb < kCC; cb += 32) {
@@ -310,8 +322,8 @@ __global__ void __launch_bounds__(256) cb_mats_kernel(const CbArgs a) {
 #pragma unroll
             for (int i = 0; i < 32; ++i) {
                 const int s = cb + i;
-                dst[t * 65 + s] = r < kCC ? (s <= t ? a.scale * x[i] * expf(lt - lam[s]) : 0.f)
-                                          : (s < t ? bt * x[i] * expf(lt - lam[s]) : 0.f);
+                const float ex = ex2_approx(lt2 - lam2[s]);   // G_t / G_s
+                dst[t * 65 + s] = r < kCC ? (s <= t ? a.scale * x[i] * ex : 0.f) : (s < t ? bt * x[i] * ex : 0.f);
             }
         }
     }
