@@ -417,8 +417,8 @@ __global__ void __launch_bounds__(256) cb_mats_kernel(const CbArgs a) {
 // bh < B H runs the forward recurrence of (b, h), CTA B H + bh the reverse one
 // (they are independent).  Threads v and 128 + v share TMEM lane v and value
 // column v of the state (S or Sb, fp32; v >= DV holds zeros): each keeps half
-// its rows in DK/2 registers and takes half the chunk's tokens in the row passes.  Per chunk, three
-// tcgen05 rounds with bf16 hi/lo operands, the record of the chunk in shared
+// its rows in DK/2 registers and takes half the chunk's tokens in the row passes.
+// Per chunk, three tcgen05 rounds with bf16 hi/lo operands, the record of the chunk in shared
 // memory (bulk-copied once the previous chunk's last product has completed, and
 // prefetched into L2 a chunk ahead):
 //   forward  D1 = S^T K^T;  y_t = b_t (v_t - G_t D1_t)  -> D2 = y^T A^T = d^T
