@@ -151,3 +151,28 @@ def test_prefill_bwd_chunked_vs_token_long(cuda_device, B, H, T, dk, dv):
         assert np.isfinite(g).all(), name
         err = _rel(g, w)
         assert err < 1e-3, f"{name}: relative max error {err:.2e}"
+
+
+@pytest.mark.parametrize("T", [1, 5, 64])
+@pytest.mark.parametrize("algorithm", ["chunked", "token"])
+def test_prefill_bwd_short_sequences(cuda_device, T, algorithm):
+    """A sequence shorter than one chunk, or exactly one: a single (ragged) chunk, no
+    chunk recurrence steps, against the oracle at the same 1e-3 bar."""
+    import torch
+    from gdn_18646_b200 import ops
+    B, H, dk, dv = 2, 3, 128, 64
+    inp = O.make_prefill_inputs(100 + T, B, T, H, dk, dv, gate_dtype="f32", state_std=0.05)
+    rng = np.random.default_rng(T)
+    dtb = (rng.standard_normal(H) * 0.2).astype(np.float32)
+    dO = rng.standard_normal((B, H, T, dv)).astype(np.float32)
+    dSf = (rng.standard_normal((B, H, dk, dv)) * 0.1).astype(np.float32)
+    ref = O.prefill_backward(inp["q"], inp["k"], inp["v"], inp["A_log"], inp["a"], dtb, inp["b"], np.ones((B, T)), dO,
+                             state_in=inp["state_in"], dS_final=dSf, scale=inp["scale"])
+    got = ops.prefill_backward(to_dev(inp["q"]), to_dev(inp["k"]), to_dev(inp["v"]), to_dev(inp["A_log"]),
+                               to_dev(inp["a"]), to_dev(inp["b"]), to_dev(dO), dt_bias=to_dev(dtb),
+                               state_in=to_dev(inp["state_in"]), dS_final=to_dev(dSf), scale=inp["scale"],
+                               algorithm=algorithm)
+    torch.cuda.synchronize()
+    for name in ("dq", "dk", "dv", "da", "db", "dA_log", "ddt_bias", "dstate_in"):
+        err = _rel(to_np(got[name]).astype(np.float64), ref[name])
+        assert err < 1e-3, f"{name}: relative max error {err:.2e}"
