@@ -43,6 +43,7 @@
 //                       then the gate chain rule into da, db;
 //   the head sums of dA_log, ddt_bias (backward.cu's bwd_head_kernel).
 #include "common.cuh"
+#include "tensormap.h"
 
 namespace gdn {
 
@@ -736,9 +737,10 @@ struct GtLayout {
 constexpr int kIssuer = 255;
 
 template <int DK, int DV>
-__global__ void __launch_bounds__(256, 1) cb_grads_tc_kernel(const CbArgs a, int nchunks) {
+__global__ void __launch_bounds__(256, 1) cb_grads_tc_kernel(const CbArgs a, int nchunks,
+                                                             const __grid_constant__ CUtensorMap map_q,
+                                                             const __grid_constant__ CUtensorMap map_k) {
     using L = GtLayout<DK, DV>;
-    constexpr int CPK = DK / 8;                    // per key row
     extern __shared__ uint8_t smem_raw[];
     uint8_t* sm = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
     float* misc = reinterpret_cast<float*>(sm + L::OFF_MISC);
@@ -809,8 +811,14 @@ __global__ void __launch_bounds__(256, 1) cb_grads_tc_kernel(const CbArgs a, int
     const uint8_t* ckDD = a.ckDD + static_cast<long>(cid) * 32768;
     const uint8_t* rec = a.rec + static_cast<long>(cid) * CRec<DK, DV>::BYTES;
     if (tid == kIssuer) {
-        // the S^T image -> the S region; [dO'^T | dd^T | d^T] (hi, lo) -> the T image
-        mbar_arrive_expect_tx(&bars[3], 2 * L::S_BYTES + 6 * 16384);
+        // the S^T image -> the S region; [dO'^T | dd^T | d^T] (hi, lo) -> the T image; q, k rows
+        // (TMA, 128-byte swizzle, rows past T zero) -> the [Q; K] image
+        mbar_arrive_expect_tx(&bars[3], 2 * L::S_BYTES + 6 * 16384 + 2 * (DK / 64) * 8192);
+#pragma unroll
+        for (int cb = 0; cb < DK / 64; ++cb) {
+            tma_load_3d(sm + L::OFF_QK + cb * L::QK_KB, &map_q, &bars[3], cb * 64, t0, bh);
+            tma_load_3d(sm + L::OFF_QK + cb * L::QK_KB + kCC * 128, &map_k, &bars[3], cb * 64, t0, bh);
+        }
         bulk_load(sm + L::OFF_SH, ckS, 2 * L::S_BYTES, &bars[3]);
         bulk_load(sm + L::OFF_RH, rec + CRec<DK, DV>::OH, 16384, &bars[3]);
         bulk_load(sm + L::OFF_RL, rec + CRec<DK, DV>::OL, 16384, &bars[3]);
@@ -831,21 +839,6 @@ __global__ void __launch_bounds__(256, 1) cb_grads_tc_kernel(const CbArgs a, int
     __syncthreads();
 
     // ---- phase A: [Q; K] (the images land on bars[3])
-    {
-        constexpr int QN = 128 * CPK / 256;
-        uint4 w[QN];
-#pragma unroll
-        for (int u = 0; u < QN; ++u) {
-            const int it = tid + 256 * u, row = it / CPK, ch = it - row * CPK, t = row & (kCC - 1);
-            w[u] = t < nt ? __ldg(reinterpret_cast<const uint4*>((row < kCC ? a.q : a.k) + (tokbase + t) * DK + ch * 8))
-                          : make_uint4(0u, 0u, 0u, 0u);
-        }
-#pragma unroll
-        for (int u = 0; u < QN; ++u) {
-            const int it = tid + 256 * u, row = it / CPK, ch = it - row * CPK;
-            *reinterpret_cast<uint4*>(sm + L::OFF_QK + (ch >> 3) * L::QK_KB + sw128_chunk(row, ch & 7)) = w[u];
-        }
-    }
     fence_async_smem();
     __syncthreads();
     const uint32_t rh = sbase + L::OFF_RH, rl = sbase + L::OFF_RL, sh = sbase + L::OFF_SH, sl = sbase + L::OFF_SL;
@@ -1214,7 +1207,18 @@ int launch_cb(const CbArgs& a, cudaStream_t st) {
         if (cudaGetDevice(&dev) == cudaSuccess) cudaDeviceGetAttribute(&nsm, cudaDevAttrMultiProcessorCount, dev);
     }
     const int gridg = static_cast<int>(nchunks) < nsm ? static_cast<int>(nchunks) : nsm;
-    cb_grads_tc_kernel<DK, DV><<<gridg, 256, GtLayout<DK, DV>::BYTES, st>>>(a, static_cast<int>(nchunks));
+    // q, k as [B H][T][DK] bf16 for the TMA loads of the gradient kernel's [Q; K] image
+    CUtensorMap mq, mk;
+    {
+        const uint64_t dims[3] = {static_cast<uint64_t>(DK), static_cast<uint64_t>(a.T),
+                                  static_cast<uint64_t>(a.B) * a.H};
+        const uint64_t strides[2] = {static_cast<uint64_t>(DK) * 2, static_cast<uint64_t>(a.T) * DK * 2};
+        const uint32_t box[3] = {64, 64, 1};
+        int ms;
+        if ((ms = make_map_bf16(&mq, a.q, 3, dims, strides, box, true)) != GDN_OK) return ms;
+        if ((ms = make_map_bf16(&mk, a.k, 3, dims, strides, box, true)) != GDN_OK) return ms;
+    }
+    cb_grads_tc_kernel<DK, DV><<<gridg, 256, GtLayout<DK, DV>::BYTES, st>>>(a, static_cast<int>(nchunks), mq, mk);
     return launch_status("gdn_prefill_bwd (chunk gradients)");
 }
 
