@@ -758,7 +758,9 @@ __global__ void __launch_bounds__(256, 1) cb_grads_tc_kernel(const CbArgs a, int
     float* basep = misc + 896;                     // [8 warps] <S, Sb> partials
     int* dead = reinterpret_cast<int*>(misc + 904);
     uint64_t* bars = reinterpret_cast<uint64_t*>(sm + L::OFF_BAR);
-    uint32_t* tslot = reinterpret_cast<uint32_t*>(bars + 5);
+    // bars: [0] T1/T3/T5 done, [1] T2 done, [2] T4 done, [3] the T image and [Q; K] landed,
+    // [4] the S image landed, [5] the Sb image landed; each completes once per chunk
+    uint32_t* tslot = reinterpret_cast<uint32_t*>(bars + 6);
     float* F1s = reinterpret_cast<float*>(sm + L::OFF_F);           // row t at t (t + 1) / 2, s <= t
     float* F2s = F1s + kCC * (kCC + 1) / 2;                         // row t at t (t - 1) / 2, s < t
     float* lam2 = misc + 912;                      // Lambda log2(e) [64]
@@ -784,14 +786,46 @@ __global__ void __launch_bounds__(256, 1) cb_grads_tc_kernel(const CbArgs a, int
         bulk_prefetch_l2(a.gv + static_cast<long>(cx) * 3 * kCC, 3 * kCC * 4);
     };
 
+    // chunk cx's S^T image -> the S region (issued once the previous chunk's T2 has read it)
+    auto load_s = [&](int cx) {
+        mbar_arrive_expect_tx(&bars[4], 2 * L::S_BYTES);
+        bulk_load(sm + L::OFF_SH, a.ckS + static_cast<long>(cx) * 2 * L::S_BYTES, 2 * L::S_BYTES, &bars[4]);
+    };
+    // chunk cx's [dO'^T | dd^T | d^T] (hi, lo) -> the T image and its q, k rows (TMA, 128-byte
+    // swizzle, rows past T zero) -> the [Q; K] image (issued once the previous chunk's T4 completed)
+    auto load_t = [&](int cx) {
+        const int bx = cx / a.n, tx0 = (cx - bx * a.n) * kCC;
+        const uint8_t* rx = a.rec + static_cast<long>(cx) * CRec<DK, DV>::BYTES;
+        const uint8_t* dd = a.ckDD + static_cast<long>(cx) * 32768;
+        const uint8_t* d1 = a.ckD + static_cast<long>(cx) * 32768;
+        mbar_arrive_expect_tx(&bars[3], 6 * 16384 + 2 * (DK / 64) * 8192);
+#pragma unroll
+        for (int cb = 0; cb < DK / 64; ++cb) {
+            tma_load_3d(sm + L::OFF_QK + cb * L::QK_KB, &map_q, &bars[3], cb * 64, tx0, bx);
+            tma_load_3d(sm + L::OFF_QK + cb * L::QK_KB + kCC * 128, &map_k, &bars[3], cb * 64, tx0, bx);
+        }
+        bulk_load(sm + L::OFF_RH, rx + CRec<DK, DV>::OH, 16384, &bars[3]);
+        bulk_load(sm + L::OFF_RL, rx + CRec<DK, DV>::OL, 16384, &bars[3]);
+        bulk_load(sm + L::OFF_RH + 16384, dd, 16384, &bars[3]);
+        bulk_load(sm + L::OFF_RL + 16384, dd + 16384, 16384, &bars[3]);
+        bulk_load(sm + L::OFF_RH + 32768, d1, 16384, &bars[3]);
+        bulk_load(sm + L::OFF_RL + 32768, d1 + 16384, 16384, &bars[3]);
+    };
+
     if (tid == 0) {
         mbar_init(&bars[0], 1);
         mbar_init(&bars[1], 1);
         mbar_init(&bars[2], 1);
         mbar_init(&bars[3], 1);
+        mbar_init(&bars[4], 1);
+        mbar_init(&bars[5], 1);
         *dead = 0;
         fence_mbar_init();
-        if (static_cast<int>(blockIdx.x) < nchunks) prefetch(blockIdx.x);
+        if (static_cast<int>(blockIdx.x) < nchunks) {
+            load_s(blockIdx.x);
+            load_t(blockIdx.x);
+            if (static_cast<int>(blockIdx.x + gridDim.x) < nchunks) prefetch(blockIdx.x + gridDim.x);
+        }
     }
     if (warp == 0) tmem_alloc(tslot, 512);
     tc_fence_before();
@@ -807,27 +841,9 @@ __global__ void __launch_bounds__(256, 1) cb_grads_tc_kernel(const CbArgs a, int
     const long tokbase = static_cast<long>(bh) * a.T + t0;
     const uint8_t* ckS = a.ckS + static_cast<long>(cid) * 2 * L::S_BYTES;
     const uint8_t* ckSb = a.ckSb + static_cast<long>(cid) * 2 * L::S_BYTES;
-    const uint8_t* ckD = a.ckD + static_cast<long>(cid) * 32768;
-    const uint8_t* ckDD = a.ckDD + static_cast<long>(cid) * 32768;
     const uint8_t* rec = a.rec + static_cast<long>(cid) * CRec<DK, DV>::BYTES;
-    if (tid == kIssuer) {
-        // the S^T image -> the S region; [dO'^T | dd^T | d^T] (hi, lo) -> the T image; q, k rows
-        // (TMA, 128-byte swizzle, rows past T zero) -> the [Q; K] image
-        mbar_arrive_expect_tx(&bars[3], 2 * L::S_BYTES + 6 * 16384 + 2 * (DK / 64) * 8192);
-#pragma unroll
-        for (int cb = 0; cb < DK / 64; ++cb) {
-            tma_load_3d(sm + L::OFF_QK + cb * L::QK_KB, &map_q, &bars[3], cb * 64, t0, bh);
-            tma_load_3d(sm + L::OFF_QK + cb * L::QK_KB + kCC * 128, &map_k, &bars[3], cb * 64, t0, bh);
-        }
-        bulk_load(sm + L::OFF_SH, ckS, 2 * L::S_BYTES, &bars[3]);
-        bulk_load(sm + L::OFF_RH, rec + CRec<DK, DV>::OH, 16384, &bars[3]);
-        bulk_load(sm + L::OFF_RL, rec + CRec<DK, DV>::OL, 16384, &bars[3]);
-        bulk_load(sm + L::OFF_RH + 16384, ckDD, 16384, &bars[3]);
-        bulk_load(sm + L::OFF_RL + 16384, ckDD + 16384, 16384, &bars[3]);
-        bulk_load(sm + L::OFF_RH + 32768, ckD, 16384, &bars[3]);
-        bulk_load(sm + L::OFF_RL + 32768, ckD + 16384, 16384, &bars[3]);
-        if (cid + static_cast<int>(gridDim.x) < nchunks) prefetch(cid + gridDim.x);
-    }
+    const int next = cid + static_cast<int>(gridDim.x);   // this CTA's next chunk
+    if (tid == kIssuer && next + static_cast<int>(gridDim.x) < nchunks) prefetch(next + gridDim.x);
     if (tid < kCC) {
         const float* gv = a.gv + static_cast<long>(cid) * 3 * kCC;
         lam[tid] = gv[tid];
@@ -838,12 +854,12 @@ __global__ void __launch_bounds__(256, 1) cb_grads_tc_kernel(const CbArgs a, int
     }
     __syncthreads();
 
-    // ---- phase A: [Q; K] (the images land on bars[3])
+    // ---- phase A: the images of this chunk (issued during the previous one) land on bars[3], bars[4]
     fence_async_smem();
     __syncthreads();
     const uint32_t rh = sbase + L::OFF_RH, rl = sbase + L::OFF_RL, sh = sbase + L::OFF_SH, sl = sbase + L::OFF_SL;
     if (tid == kIssuer) {
-        if (!mbar_wait(&bars[3], 0, a.err)) *dead = 1;
+        if (!mbar_wait(&bars[4], ph, a.err) || !mbar_wait(&bars[3], ph, a.err)) *dead = 1;
         tc_fence_after();
         // Every operand here is MN-major (rows v of the images, 16 rows per K step): A = the
         // [dO'^T | dd^T] blocks (M = 128 tokens, next 64 at 16 KB), B = the S^T image (N = d)
@@ -877,8 +893,8 @@ __global__ void __launch_bounds__(256, 1) cb_grads_tc_kernel(const CbArgs a, int
     if (!mbar_wait(&bars[0], ph, a.err)) *dead = 1;
     tc_fence_after();
     if (tid == kIssuer) {
-        mbar_arrive_expect_tx(&bars[3], 2 * L::S_BYTES);
-        bulk_load(sm + L::OFF_SH, ckSb, 2 * L::S_BYTES, &bars[3]);
+        mbar_arrive_expect_tx(&bars[5], 2 * L::S_BYTES);
+        bulk_load(sm + L::OFF_SH, ckSb, 2 * L::S_BYTES, &bars[5]);
     }
     float sp = 0.f;
     {
@@ -891,7 +907,7 @@ __global__ void __launch_bounds__(256, 1) cb_grads_tc_kernel(const CbArgs a, int
             shv[u] = __ldg(reinterpret_cast<const uint4*>(ckS) + q);
             slv[u] = __ldg(reinterpret_cast<const uint4*>(ckS + L::S_BYTES) + q);
         }
-        if (!mbar_wait(&bars[3], 1, a.err)) *dead = 1;
+        if (!mbar_wait(&bars[5], ph, a.err)) *dead = 1;
 #pragma unroll
         for (int u = 0; u < NQ; ++u) {
             const int q = tid + 256 * u;
@@ -1051,7 +1067,10 @@ __global__ void __launch_bounds__(256, 1) cb_grads_tc_kernel(const CbArgs a, int
     }
 
     // ---- phase C: the T4 operands over the freed images once T2 completed
-    if (tid == kIssuer && !dead_b && !mbar_wait(&bars[1], ph, a.err)) *dead = 1;
+    if (tid == kIssuer && !dead_b) {
+        if (!mbar_wait(&bars[1], ph, a.err)) *dead = 1;
+        else if (next < nchunks) load_s(next);     // T2 has read the S region
+    }
     __syncthreads();
     const bool dead_c = *dead != 0;
     tc_fence_after();
@@ -1121,7 +1140,10 @@ __global__ void __launch_bounds__(256, 1) cb_grads_tc_kernel(const CbArgs a, int
     }
 
     // ---- phase D: dq, dk (warps w and w + 4 share lanes 32 (w % 4) .. + 31, half the columns each)
-    if (tid == kIssuer && !dead_c && !mbar_wait(&bars[2], ph, a.err)) *dead = 1;
+    if (tid == kIssuer && !dead_c) {
+        if (!mbar_wait(&bars[2], ph, a.err)) *dead = 1;
+        else if (next < nchunks) load_t(next);     // T4 has read the T image, A1, A2 and [Q; K]
+    }
     __syncthreads();
     tc_fence_after();
     if (*dead == 0) {
