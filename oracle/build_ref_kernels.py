@@ -1,16 +1,16 @@
 """Test infrastructure: the reference repository's own CUDA kernels, built for
 B200 as same-box GPU comparators.
 
-Compiles ``kernels/rmsnorm.cu``, ``kernels/decode.cu`` and
-``kernels/fused_proj_conv_silu.cu`` of the reference checkout (read in place,
-never copied) into torch extension modules under ``oracle/_ref/``, with the
-reference's own flags (bench_gdn.py:28-42: -O3 --use_fast_math, and
---expt-relaxed-constexpr for the projection) and the B200 architecture in place
-of sm_80.  Only the tests load them (``load``), to check the library's kernels
-against them and time both on the same GPU; nothing in the library or in
-bench.py's timed legs does.  The reference's prefill kernels are left out:
-prefill_chunked.cu hard-codes H=16, dk=128, dv=256 (kernels/prefill_chunked.cu:15-18)
-and runs none of the BASELINE configs.
+Compiles ``kernels/rmsnorm.cu``, ``kernels/decode.cu``,
+``kernels/fused_proj_conv_silu.cu`` and ``kernels/prefill_chunked.cu`` of the
+reference checkout (read in place, never copied) into torch extension modules
+under ``oracle/_ref/``, with the reference's own flags (bench_gdn.py:28-42:
+-O3 --use_fast_math, and --expt-relaxed-constexpr for the projection) and the
+B200 architecture in place of sm_80.  Only the tests load them (``load``), to
+check the library's kernels against them and time both on the same GPU;
+nothing in the library or in bench.py's timed legs does.  The prefill kernel
+hard-codes H=16, dk=128, dv=256 (kernels/prefill_chunked.cu:15-18), so it is
+compared at that head shape only.
 
 Usage (where the reference checkout exists; the built modules then travel with
 the repository):  python oracle/build_ref_kernels.py <reference checkout>
@@ -31,6 +31,7 @@ KERNELS = {
     "gdn_ref_rmsnorm": ("rmsnorm.cu", ()),
     "gdn_ref_decode": ("decode.cu", ()),
     "gdn_ref_proj": ("fused_proj_conv_silu.cu", ("--expt-relaxed-constexpr",)),
+    "gdn_ref_prefill": ("prefill_chunked.cu", ()),
 }
 
 

@@ -9,7 +9,11 @@ The ops and their calls are the reference bench's per-op list
 (bench_gdn.py:275-300); the shapes are the benchmark configurations': decode at
 config 2 (B=256, H=32, dk=dv=128), and at config 3 (x [2, 8192, 2048]) the
 RMSNorm of 16384 rows of 2048 and the fused q/k/v projection W [8192, 2048]
-(2048 + 2048 + 4096 output channels) with the k=4 causal conv and SiLU.
+(2048 + 2048 + 4096 output channels) with the k=4 causal conv and SiLU.  The
+reference's prefill kernel only runs H=16, dk=128, dv=256
+(kernels/prefill_chunked.cu:15-18): it is compared at config 1's batch, length
+and distributions with that head shape, both outputs also against the fp64
+oracle on a sampled head.
 
 Skipped when the comparator modules were not built (no reference checkout on the
 machine that built the repository)."""
@@ -147,3 +151,47 @@ def test_proj_vs_reference_kernel(cuda_device):
     t_ref = _time_ms(lambda: ref.forward(x, W, cw), iters=10)
     t_our = _time_ms(lambda: ours.forward(x, W, cw), iters=10)
     _report("proj_conv_silu", "x [2,8192,2048] W [8192,2048]", t_our, t_ref, flops=2.0 * B * T * D * Dout)
+
+
+def test_prefill_vs_reference_kernel(cuda_device):
+    import torch
+    from gdn_18646_b200 import ops
+    from oracle import gdn_oracle as O
+    from tests._util import to_np
+    ref = _ref("gdn_ref_prefill")
+    ours = ops.exts()["prefill"]
+    B, T, H, dk, dv = 4, 4096, 16, 128, 256
+    g = torch.Generator(device="cuda").manual_seed(3)
+    bf = torch.bfloat16
+    q = torch.nn.functional.normalize(torch.randn(B, H, T, dk, device="cuda", generator=g), dim=-1).to(bf)
+    k = torch.nn.functional.normalize(torch.randn(B, H, T, dk, device="cuda", generator=g), dim=-1).to(bf)
+    v = torch.randn(B, H, T, dv, device="cuda", generator=g).to(bf)
+    a = torch.randn(B, H, T, device="cuda", generator=g).to(bf)
+    b = torch.randn(B, H, T, device="cuda", generator=g).to(bf)
+    A_log = torch.full((H,), float(np.log(0.1)), device="cuda")
+    mask = torch.ones(B, T, device="cuda")
+    S0 = torch.randn(B, H, dk, dv, device="cuda", generator=g) * 0.02
+    scale = dk ** -0.5
+    o_r, S_r = ref.prefill(q, k, v, A_log, a, 0.0, b, mask, S0, scale)
+    o_o, S_o = ours.prefill(q, k, v, A_log, a, 0.0, b, mask, S0, scale)
+    torch.cuda.synchronize()
+    # the library against the fp64 oracle on one sampled head (the north_star bar)
+    bi, hi = 1, 5
+    sl = lambda t: to_np(t[bi:bi + 1, hi:hi + 1])
+    o_x, S_x = O.prefill(sl(q), sl(k), sl(v), to_np(A_log[hi:hi + 1]), sl(a), 0.0, sl(b), np.ones((1, T)),
+                         state_in=sl(S0), scale=scale, chunk_size=64, dt=np.float64)
+    err_o_ours = float(np.abs(O.bf16_to_f32(sl(o_o)) - o_x).max())
+    err_s_ours = O.rel_fro(sl(S_o), S_x)
+    err_o_ref = float(np.abs(O.bf16_to_f32(sl(o_r)) - o_x).max())
+    err_s_ref = O.rel_fro(sl(S_r), S_x)
+    print(f"REFCMP prefill vs fp64 oracle (b={bi}, h={hi}): library o {err_o_ours:.2e} state {err_s_ours:.2e}; "
+          f"reference kernel o {err_o_ref:.2e} state {err_s_ref:.2e}")
+    assert err_o_ours <= 2e-2 and err_s_ours <= 1e-3
+    # the two GPU outputs against each other, with the reference harness's mixed
+    # tolerance (tests/test_prefill.py:61-62) over every element
+    diff = (o_o.float() - o_r.float()).abs()
+    assert bool((diff < 1e-2 + 0.05 * o_r.float().abs()).all()), f"max diff {float(diff.max()):.3e}"
+    t_ref = _time_ms(lambda: ref.prefill(q, k, v, A_log, a, 0.0, b, mask, S0, scale), iters=5, warmup=1)
+    t_our = _time_ms(lambda: ours.prefill(q, k, v, A_log, a, 0.0, b, mask, S0, scale), iters=10)
+    alg = B * H * T * (2 * dk * 2 + 2 * dv * 2 + 2 * 2) + 2 * B * H * dk * dv * 4
+    _report("prefill", "B=4 T=4096 H=16 dk=128 dv=256", t_our, t_ref, alg_bytes=alg)
