@@ -148,14 +148,17 @@ struct CRec {
 // from the diagonal, A_ij = -A_ii sum_{j <= k < i} (diag(b) M)_ik A_kj.
 // Padded tokens (past T) get log g = 0, b = m = 0 and zero k, q, v, dO.
 // ---------------------------------------------------------------------------
+// P overlays the [Q; K] image, which is copied into the record as soon as the
+// product has read it: at DK = 128 the CTA then takes ~70 KB, three per SM.
 template <int DK>
 struct MatsSmem {
     static constexpr int QK_KB = 128 * 128;
     static constexpr int OFF_QK = 0;                               // [Q; K] image, 128 rows x DK
-    static constexpr int OFF_L = OFF_QK + (DK / 64) * QK_KB;       // diag(b) M   [64][65] fp32
+    static constexpr int OFF_P = OFF_QK;                           // P           [64][65] fp32, after the product
+    static constexpr int QK_END = (DK / 64) * QK_KB > kCC * 65 * 4 ? (DK / 64) * QK_KB : kCC * 65 * 4;
+    static constexpr int OFF_L = OFF_QK + QK_END;                  // diag(b) M   [64][65] fp32
     static constexpr int OFF_A = OFF_L + kCC * 65 * 4;             // A           [64][65]
-    static constexpr int OFF_P = OFF_A + kCC * 65 * 4;             // P           [64][65]
-    static constexpr int OFF_T = OFF_P + kCC * 65 * 4;             // block sums  [3][16][17]
+    static constexpr int OFF_T = OFF_A + kCC * 65 * 4;             // block sums  [3][16][17]
     static constexpr int OFF_G = OFF_T + 3 * 16 * 17 * 4;          // Lambda, b, m, Lambda log2(e) [4][64]
     static constexpr int OFF_BAR = OFF_G + 4 * kCC * 4;
     static constexpr int BYTES = OFF_BAR + 16 + 1024;
@@ -305,6 +308,21 @@ __global__ void __launch_bounds__(256) cb_mats_kernel(const CbArgs a) {
     if (tid < kCC) gv[tid] = lam[tid];
     const bool ok = mbar_wait(bar, 0, a.err);
     tc_fence_after();
+    // the k and scale G q images of the record, from the [Q; K] image the product has
+    // finished reading (P overwrites it next)
+    for (int it = tid; it < (DK / 64) * 512; it += 256) {
+        const int b = it >> 9, t = (it >> 3) & 63, ch = it & 7;
+        const uint4 kq = *reinterpret_cast<const uint4*>(sm + L::OFF_QK + b * L::QK_KB + sw128_chunk(kCC + t, ch));
+        *reinterpret_cast<uint4*>(rec + R::KIMG + b * 8192 + sw128_chunk(t, ch)) = kq;
+        const uint4 qq = *reinterpret_cast<const uint4*>(sm + L::OFF_QK + b * L::QK_KB + sw128_chunk(t, ch));
+        float x[8];
+        unpack_bf16x8(qq, x);
+        const float gq = a.scale * expf(lam[t]);
+#pragma unroll
+        for (int i = 0; i < 8; ++i) x[i] *= gq;
+        split_store8(rec + R::QGH + b * 8192 + sw128_chunk(t, ch), rec + R::QGL + b * 8192 + sw128_chunk(t, ch), x);
+    }
+    __syncthreads();
     if (tid < 128) {
         // row r of the product: P row r (r < 64) or diag(b) M row r - 64
         const int r = tid, t = r & (kCC - 1);
@@ -385,18 +403,6 @@ __global__ void __launch_bounds__(256) cb_mats_kernel(const CbArgs a) {
         const int hi = img == 0 ? R::AH : (img == 1 ? R::ATH : R::PTH);
         const int lo = img == 0 ? R::AL : (img == 1 ? R::ATL : R::PTL);
         split_store8(rec + hi + off, rec + lo + off, x);
-    }
-    for (int it = tid; it < (DK / 64) * 512; it += 256) {
-        const int b = it >> 9, t = (it >> 3) & 63, ch = it & 7;
-        const uint4 kq = *reinterpret_cast<const uint4*>(sm + L::OFF_QK + b * L::QK_KB + sw128_chunk(kCC + t, ch));
-        *reinterpret_cast<uint4*>(rec + R::KIMG + b * 8192 + sw128_chunk(t, ch)) = kq;
-        const uint4 qq = *reinterpret_cast<const uint4*>(sm + L::OFF_QK + b * L::QK_KB + sw128_chunk(t, ch));
-        float x[8];
-        unpack_bf16x8(qq, x);
-        const float gq = a.scale * expf(lam[t]);
-#pragma unroll
-        for (int i = 0; i < 8; ++i) x[i] *= gq;
-        split_store8(rec + R::QGH + b * 8192 + sw128_chunk(t, ch), rec + R::QGL + b * 8192 + sw128_chunk(t, ch), x);
     }
     if (tid < kCC) {
         const int t = tid;
