@@ -895,39 +895,9 @@ __global__ void __launch_bounds__(256, 1) cb_grads_tc_kernel(const CbArgs a, int
         umma_commit(&bars[0]);
     }
 
-    // ---- phase B: the Sb^T image over the S image once T1 has read it, <S, Sb>, then T2
-    if (!mbar_wait(&bars[0], ph, a.err)) *dead = 1;
-    tc_fence_after();
-    if (tid == kIssuer) {
-        mbar_arrive_expect_tx(&bars[5], 2 * L::S_BYTES);
-        bulk_load(sm + L::OFF_SH, ckSb, 2 * L::S_BYTES, &bars[5]);
-    }
-    float sp = 0.f;
-    {
-        // <S, Sb> over the images: S (hi, lo) from memory (just read into L2), Sb from shared memory
-        constexpr int NQ = 2 * L::S_BYTES / 2 / 16 / 256;     // uint4 of one image (hi or lo) per thread
-        uint4 shv[NQ], slv[NQ];
-#pragma unroll
-        for (int u = 0; u < NQ; ++u) {
-            const int q = tid + 256 * u;
-            shv[u] = __ldg(reinterpret_cast<const uint4*>(ckS) + q);
-            slv[u] = __ldg(reinterpret_cast<const uint4*>(ckS + L::S_BYTES) + q);
-        }
-        if (!mbar_wait(&bars[5], ph, a.err)) *dead = 1;
-#pragma unroll
-        for (int u = 0; u < NQ; ++u) {
-            const int q = tid + 256 * u;
-            float a8[8], b8[8], c8[8], d8[8];
-            unpack_bf16x8(shv[u], a8);
-            unpack_bf16x8(slv[u], b8);
-            unpack_bf16x8(*reinterpret_cast<const uint4*>(sm + L::OFF_SH + q * 16), c8);
-            unpack_bf16x8(*reinterpret_cast<const uint4*>(sm + L::OFF_SL + q * 16), d8);
-#pragma unroll
-            for (int i = 0; i < 8; ++i) sp = fmaf(a8[i] + b8[i], c8[i] + d8[i], sp);
-        }
-    }
-    sp = warp_sum(sp);
-    if (lane == 0) basep[warp] = sp;
+    // ---- phase B: dd . v while T1, T3, T5 run (the T image has landed), then the Sb^T image
+    //      over the S image once T1 has read it, <S, Sb>, then T2
+    if (!mbar_wait(&bars[3], ph, a.err)) *dead = 1;
     {
         // dd_t . v_t: four threads per token, 32 value columns each, dd from the image (hi + lo)
         const int t = tid & (kCC - 1), qv = tid >> 6;
@@ -950,6 +920,39 @@ __global__ void __launch_bounds__(256, 1) cb_grads_tc_kernel(const CbArgs a, int
         }
         pairp[qv * kCC + t] = pv;                   // pairp is free until the row work below
     }
+    float sp = 0.f;
+    {
+        // <S, Sb> over the images: S (hi, lo) from memory (in L2; loaded while T1 runs), Sb
+        // from shared memory once T1 has read the S image it replaces
+        constexpr int NQ = 2 * L::S_BYTES / 2 / 16 / 256;     // uint4 of one image (hi or lo) per thread
+        uint4 shv[NQ], slv[NQ];
+#pragma unroll
+        for (int u = 0; u < NQ; ++u) {
+            const int q = tid + 256 * u;
+            shv[u] = __ldg(reinterpret_cast<const uint4*>(ckS) + q);
+            slv[u] = __ldg(reinterpret_cast<const uint4*>(ckS + L::S_BYTES) + q);
+        }
+        if (!mbar_wait(&bars[0], ph, a.err)) *dead = 1;
+        tc_fence_after();
+        if (tid == kIssuer) {
+            mbar_arrive_expect_tx(&bars[5], 2 * L::S_BYTES);
+            bulk_load(sm + L::OFF_SH, ckSb, 2 * L::S_BYTES, &bars[5]);
+        }
+        if (!mbar_wait(&bars[5], ph, a.err)) *dead = 1;
+#pragma unroll
+        for (int u = 0; u < NQ; ++u) {
+            const int q = tid + 256 * u;
+            float a8[8], b8[8], c8[8], d8[8];
+            unpack_bf16x8(shv[u], a8);
+            unpack_bf16x8(slv[u], b8);
+            unpack_bf16x8(*reinterpret_cast<const uint4*>(sm + L::OFF_SH + q * 16), c8);
+            unpack_bf16x8(*reinterpret_cast<const uint4*>(sm + L::OFF_SL + q * 16), d8);
+#pragma unroll
+            for (int i = 0; i < 8; ++i) sp = fmaf(a8[i] + b8[i], c8[i] + d8[i], sp);
+        }
+    }
+    sp = warp_sum(sp);
+    if (lane == 0) basep[warp] = sp;
     __syncthreads();
     if (tid < kCC) ddv[tid] = pairp[tid] + pairp[kCC + tid] + pairp[2 * kCC + tid] + pairp[3 * kCC + tid];
     fence_async_smem();
