@@ -1000,13 +1000,9 @@ __global__ void __launch_bounds__(256, 1) cb_grads_tc_kernel(const CbArgs a, int
             }
             return acc;
         };
-        // q_t . X_q (side 0) or k_t . X_dd (side 1), then k_t . X_e (side 1) once T2 has completed
+        // q_t . X_q (side 0) or k_t . X_dd (side 1); k_t . X_e (side 1) comes last, so that
+        // T2 runs in the tensor pipe during the decay-masked rows
         dotp[hf * 128 + r] = row_dot(L::T_XS);
-        if (side == 1) {
-            if (!mbar_wait(&bars[1], ph, a.err)) *dead = 1;
-            tc_fence_after();
-            dep[hf * 128 + r] = row_dot(L::T_XE);
-        }
         const float lt2 = lam2[t], bt = bms[t];
         float* Fs = side ? F2s + t * (t - 1) / 2 : F1s + t * (t + 1) / 2;
         float pre = 0.f, krs = 0.f;
@@ -1058,6 +1054,11 @@ __global__ void __launch_bounds__(256, 1) cb_grads_tc_kernel(const CbArgs a, int
             }
         }
         pairp[(warp & 3) * kCC + hf * 32 + lane] = cv[0];
+        if (side == 1) {
+            if (!mbar_wait(&bars[1], ph, a.err)) *dead = 1;
+            tc_fence_after();
+            dep[hf * 128 + r] = row_dot(L::T_XE);
+        }
     }
     __syncthreads();
     if (tid < 128 && !dead_b) {
