@@ -42,6 +42,8 @@
 //                       the per-token scalars of g dg and db' from the same accumulators,
 //                       then the gate chain rule into da, db;
 //   the head sums of dA_log, ddt_bias (backward.cu's bwd_head_kernel).
+#include <type_traits>
+
 #include "common.cuh"
 #include "tensormap.h"
 
@@ -1085,24 +1087,42 @@ __global__ void __launch_bounds__(256, 1) cb_grads_tc_kernel(const CbArgs a, int
     const bool dead_c = *dead != 0;
     tc_fence_after();
     if (!dead_c) {
-        for (int it = tid; it < 8 * 128; it += 256) {
-            const int ch = it >> 7, row = it & 127, t = row & (kCC - 1);
-            float f1[8], f2[8];
+        // thread (half, row): row `row` of A1 and A2, column chunks 4 half .. 4 half + 3; the
+        // token s of every element is a constant of the unrolled loops, so the transposed
+        // reads (F2 row s, F1 row s at column t) take immediate offsets
+        const int row = tid & 127, t = row & (kCC - 1);
+        auto build = [&](auto half_c) {
+            constexpr int H4 = decltype(half_c)::value * 4;
 #pragma unroll
-            for (int i = 0; i < 8; ++i) {
-                const int s = ch * 8 + i;
+            for (int q = 0; q < 4; ++q) {
+                const int ch = H4 + q;
+                float f1[8], f2[8];
                 if (row < kCC) {
-                    f1[i] = s <= t ? F1s[t * (t + 1) / 2 + s] : 0.f;
-                    f2[i] = 0.f;
+                    const float* fr = F1s + t * (t + 1) / 2;
+#pragma unroll
+                    for (int i = 0; i < 8; ++i) {
+                        const int s = ch * 8 + i;
+                        f1[i] = s <= t ? fr[s] : 0.f;
+                        f2[i] = 0.f;
+                    }
                 } else {
-                    f1[i] = s < t ? F2s[t * (t - 1) / 2 + s] : (s > t ? F2s[s * (s - 1) / 2 + t] : 0.f);
-                    f2[i] = s >= t ? scale * F1s[s * (s + 1) / 2 + t] : 0.f;
+                    const float* fr = F2s + t * (t - 1) / 2;
+#pragma unroll
+                    for (int i = 0; i < 8; ++i) {
+                        const int s = ch * 8 + i;
+                        const float lower = fr[s < t ? s : 0];                                  // F2[t][s], s < t
+                        const float upper = F2s[s * (s - 1) / 2 + (t < s ? t : 0)];             // F2[s][t], s > t
+                        f1[i] = s < t ? lower : (s > t ? upper : 0.f);
+                        f2[i] = s >= t ? scale * F1s[s * (s + 1) / 2 + (t <= s ? t : 0)] : 0.f;   // F1[s][t]
+                    }
                 }
+                const uint32_t off = sw128_chunk(row, ch);
+                split_store8(sm + L::OFF_A1H + off, sm + L::OFF_A1L + off, f1);
+                split_store8(sm + L::OFF_A2H + off, sm + L::OFF_A2L + off, f2);
             }
-            const uint32_t off = sw128_chunk(row, ch);
-            split_store8(sm + L::OFF_A1H + off, sm + L::OFF_A1L + off, f1);
-            split_store8(sm + L::OFF_A2H + off, sm + L::OFF_A2L + off, f2);
-        }
+        };
+        if (tid < 128) build(std::integral_constant<int, 0>());
+        else build(std::integral_constant<int, 1>());
     }
     fence_async_smem();
     __syncthreads();
