@@ -776,6 +776,8 @@ __global__ void __launch_bounds__(256, 1) cb_grads_tc_kernel(const CbArgs a, int
     float* dep = misc + 1280;                      // [2][128] k . X_e partials
     float* krsp = misc + 1536;                     // [2][128] r . dd partials (the M Y part)
     float* pre32 = misc + 1792;                    // [128] per row: sum of its pair terms over s < 32
+    float* dfac = misc + 1920;                     // d(da)/d(g dg) per token: -e^{A_log} sigmoid(a + dt_bias)
+    float* dbfac = misc + 1984;                    // d(db)/d(db') per token: mask sigmoid'(b)
 
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
     const uint32_t sbase = smem_u32(sm);
@@ -854,11 +856,23 @@ __global__ void __launch_bounds__(256, 1) cb_grads_tc_kernel(const CbArgs a, int
     if (tid == kIssuer && next + static_cast<int>(gridDim.x) < nchunks) prefetch(next + gridDim.x);
     if (tid < kCC) {
         const float* gv = a.gv + static_cast<long>(cid) * 3 * kCC;
-        lam[tid] = gv[tid];
-        lam2[tid] = gv[tid] * 1.4426950408889634f;
-        Gs[tid] = expf(gv[tid]);
+        // the gate chain-rule factors of the chunk's tokens, loaded with the gate vectors so
+        // that the token sums at the end of the chunk read no global memory
+        float xg = 0.f, xb = 0.f;
+        if (tid < nt) {
+            const long tok = tokbase + tid;
+            xg = load_gate(a.a, tok, a.gate_dtype) + (a.dt_bias_vec ? a.dt_bias_vec[h] : a.dt_bias);
+            xb = load_gate(a.b, tok, a.gate_dtype);
+        }
+        const float g0 = gv[tid], m0 = gv[2 * kCC + tid];
+        lam[tid] = g0;
+        lam2[tid] = g0 * 1.4426950408889634f;
+        Gs[tid] = expf(g0);
         bms[tid] = gv[kCC + tid];
-        ms[tid] = gv[2 * kCC + tid];
+        ms[tid] = m0;
+        dfac[tid] = -expf(a.A_log[h]) * (xg > 20.f ? 1.f : sigmoid_f(xg));
+        const float sb = sigmoid_f(xb);
+        dbfac[tid] = m0 * sb * (1.f - sb);
     }
     __syncthreads();
 
@@ -1162,11 +1176,8 @@ __global__ void __launch_bounds__(256, 1) cb_grads_tc_kernel(const CbArgs a, int
         const float dlogg = GL * base + sa + scc + se + pair + s_rdr[t];
         const long tok = tokbase + t;
         a.dlogg[tok] = dlogg;
-        const float dtb = a.dt_bias_vec ? a.dt_bias_vec[h] : a.dt_bias;
-        const float xg = load_gate(a.a, tok, a.gate_dtype) + dtb;
-        a.da[tok] = dlogg * (-expf(a.A_log[h])) * (xg > 20.f ? 1.f : sigmoid_f(xg));
-        const float sb = sigmoid_f(load_gate(a.b, tok, a.gate_dtype));
-        a.db[tok] = s_dbm[t] * ms[t] * sb * (1.f - sb);
+        a.da[tok] = dlogg * dfac[t];
+        a.db[tok] = s_dbm[t] * dbfac[t];
     }
 
     // ---- phase D: dq, dk (warps w and w + 4 share lanes 32 (w % 4) .. + 31, half the columns each)
