@@ -539,10 +539,9 @@ __global__ void __launch_bounds__(256, 1) cb_chain_kernel(const CbArgs a) {
     for (int step = 0; step < a.n; ++step) {
         const int c = rev ? a.n - 1 - step : step;
         const long cid = static_cast<long>(bh) * a.n + c;
-        if (!mbar_wait(&bars[0], step & 1, a.err)) ok = false;
-        if (tid == 0 && step + 1 < a.n) prefetch(rev ? c - 1 : c + 1);
         // ---- the state entering (forward) or leaving (reverse) the chunk as a bf16 hi/lo
-        //      image (rows v), which is also the checkpoint: bulk-stored for the gradient kernel
+        //      image (rows v), which is also the checkpoint: bulk-stored for the gradient kernel;
+        //      built while the chunk's record is still landing
         {
 #pragma unroll
             for (int q = 0; q < DH / 8; ++q) {
@@ -554,6 +553,8 @@ __global__ void __launch_bounds__(256, 1) cb_chain_kernel(const CbArgs a) {
                 split_store8(sm + L::OFF_SH + off, sm + L::OFF_SL + off, y);
             }
         }
+        if (!mbar_wait(&bars[0], step & 1, a.err)) ok = false;
+        if (tid == 0 && step + 1 < a.n) prefetch(rev ? c - 1 : c + 1);
         fence_async_smem();
         __syncthreads();
         const float GL = tab[R::T_G + kCC - 1];
