@@ -25,6 +25,7 @@ import sys
 
 HERE = os.path.dirname(os.path.abspath(__file__))
 OUT = os.path.join(HERE, "_ref")
+BUILD_TIMEOUT_S = 1200                          # per module compile
 
 # module name -> (source under kernels/, extra nvcc flags of the reference's bench)
 KERNELS = {
@@ -52,7 +53,13 @@ def build(ref_dir: str, only: str | None = None) -> list[str]:
     if only is None and len(missing) > 1:
         procs = [subprocess.Popen([sys.executable, os.path.abspath(__file__), ref_dir, "--only", n])
                  for n in missing]
-        rcs = [p.wait() for p in procs]
+        rcs = []
+        for p in procs:
+            try:
+                rcs.append(p.wait(timeout=BUILD_TIMEOUT_S))
+            except subprocess.TimeoutExpired:
+                p.kill()
+                rcs.append("timeout")
         if any(rcs):
             raise RuntimeError(f"comparator build failed: {dict(zip(missing, rcs))}")
     elif missing:
@@ -61,6 +68,9 @@ def build(ref_dir: str, only: str | None = None) -> list[str]:
         src, extra = KERNELS[name]
         bdir = os.path.join(OUT, name)
         os.makedirs(bdir, exist_ok=True)
+        stale = os.path.join(bdir, "lock")         # left by an interrupted build; torch would wait on it
+        if os.path.exists(stale):
+            os.remove(stale)
         load(name=name, sources=[os.path.join(ref_dir, "kernels", src)], build_directory=bdir,
              extra_cuda_cflags=["-O3", "--use_fast_math", "-lineinfo", *extra], verbose=False)
     return [so_path(n) for n in names]
