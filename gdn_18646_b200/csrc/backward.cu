@@ -394,15 +394,20 @@ __global__ void __launch_bounds__(128) bwd_finish_kernel(const BwdArgs a) {
 }
 
 // dA_log[h] = sum dlogg * log g, ddt_bias[h] = sum da over (b, t), in order.  One CTA per head.
+// A cluster of kHeadSplit CTAs per head, each summing every kHeadSplit-th token
+// block of the head's B*T tokens; rank 0 adds the CTAs' sums in rank order (the
+// peers' shared memory, read after a cluster barrier), so the result does not
+// depend on scheduling.
+constexpr int kHeadSplit = 8;
 __global__ void __launch_bounds__(256) bwd_head_kernel(const BwdArgs a) {
-    const int h = blockIdx.x, tid = threadIdx.x;
+    const int h = blockIdx.x / kHeadSplit, rank = blockIdx.x % kHeadSplit, tid = threadIdx.x;
     __shared__ float r0[256], r1[256];
     const float dtb = a.dt_bias_vec ? a.dt_bias_vec[h] : a.dt_bias;
     const float Aneg = -expf(a.A_log[h]);
     float s0 = 0.f, s1 = 0.f;
     for (int bi = 0; bi < a.B; ++bi) {
         const long base = (static_cast<long>(bi) * a.H + h) * a.T;
-        for (int t = tid; t < a.T; t += 256) {
+        for (int t = rank * 256 + tid; t < a.T; t += 256 * kHeadSplit) {
             const float logg = Aneg * softplus_f(load_gate(a.a, base + t, a.gate_dtype) + dtb);
             s0 = fmaf(a.dlogg[base + t], logg, s0);
             s1 += a.da[base + t];
@@ -418,10 +423,43 @@ __global__ void __launch_bounds__(256) bwd_head_kernel(const BwdArgs a) {
         }
         __syncthreads();
     }
-    if (tid == 0) {
-        a.dA_log[h] = r0[0];
-        a.ddt_bias[h] = r1[0];
+    asm volatile("barrier.cluster.arrive.release.aligned;" ::: "memory");
+    asm volatile("barrier.cluster.wait.acquire.aligned;" ::: "memory");
+    if (rank == 0 && tid == 0) {
+        float t0 = 0.f, t1 = 0.f;
+        for (int q = 0; q < kHeadSplit; ++q) {
+            uint32_t p0, p1;
+            float v0, v1;
+            asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(p0) : "r"(smem_u32(&r0[0])), "r"(q));
+            asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(p1) : "r"(smem_u32(&r1[0])), "r"(q));
+            asm volatile("ld.shared::cluster.f32 %0, [%1];" : "=f"(v0) : "r"(p0) : "memory");
+            asm volatile("ld.shared::cluster.f32 %0, [%1];" : "=f"(v1) : "r"(p1) : "memory");
+            t0 += v0;
+            t1 += v1;
+        }
+        a.dA_log[h] = t0;
+        a.ddt_bias[h] = t1;
     }
+    // no CTA leaves (and releases its shared memory) before rank 0 has read it
+    asm volatile("barrier.cluster.arrive.release.aligned;" ::: "memory");
+    asm volatile("barrier.cluster.wait.acquire.aligned;" ::: "memory");
+}
+
+int launch_head(const BwdArgs& a, cudaStream_t st) {
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3(a.H * kHeadSplit);
+    cfg.blockDim = dim3(256);
+    cfg.stream = st;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeClusterDimension;
+    attr[0].val.clusterDim.x = kHeadSplit;
+    attr[0].val.clusterDim.y = 1;
+    attr[0].val.clusterDim.z = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    const cudaError_t e = cudaLaunchKernelEx(&cfg, bwd_head_kernel, a);
+    if (e != cudaSuccess) return fail(GDN_ERR_CUDA, "gdn_prefill_bwd (heads): launch failed: %s", cudaGetErrorString(e));
+    return launch_status("gdn_prefill_bwd (heads)");
 }
 
 // The backward runs window by window, last window first, so that only one window's
@@ -464,8 +502,7 @@ int launch_bwd(BwdArgs a, int W, float* ckpt, float* carry, cudaStream_t st) {
         bwd_finish_kernel<DK, DV><<<static_cast<unsigned>(static_cast<long>(a.B) * a.H * (a.t1 - a.t0)), 128, 0, st>>>(a);
         if ((s = launch_status("gdn_prefill_bwd (finish)")) != GDN_OK) return s;
     }
-    bwd_head_kernel<<<a.H, 256, 0, st>>>(a);
-    return launch_status("gdn_prefill_bwd (heads)");
+    return launch_head(a, st);
 }
 
 }  // namespace
@@ -475,9 +512,9 @@ namespace gdn {
 
 // The head sums for the chunked backward (backward_chunked.cu), which leaves dlogg and da in
 // the same layouts.
-void launch_bwd_head_sums(const float* A_log, const void* a, int gate_dtype, float dt_bias, const float* dt_bias_vec,
-                          const float* dlogg, const float* da, float* dA_log, float* ddt_bias, int B, int T, int H,
-                          cudaStream_t st) {
+int launch_bwd_head_sums(const float* A_log, const void* a, int gate_dtype, float dt_bias, const float* dt_bias_vec,
+                         const float* dlogg, const float* da, float* dA_log, float* ddt_bias, int B, int T, int H,
+                         cudaStream_t st) {
     BwdArgs ar{};
     ar.A_log = A_log;
     ar.a = a;
@@ -491,7 +528,7 @@ void launch_bwd_head_sums(const float* A_log, const void* a, int gate_dtype, flo
     ar.B = B;
     ar.T = T;
     ar.H = H;
-    bwd_head_kernel<<<H, 256, 0, st>>>(ar);
+    return launch_head(ar, st);
 }
 
 size_t prefill_bwd_chunked_workspace(int B, int T, int H, int dk, int dv);

@@ -49,10 +49,10 @@
 
 namespace gdn {
 
-// the head sums (backward.cu): dA_log[h] = sum dlogg log g, ddt_bias[h] = sum da
-void launch_bwd_head_sums(const float* A_log, const void* a, int gate_dtype, float dt_bias, const float* dt_bias_vec,
-                          const float* dlogg, const float* da, float* dA_log, float* ddt_bias, int B, int T, int H,
-                          cudaStream_t st);
+// the head sums (backward.cu): dA_log[h] = sum dlogg log g, ddt_bias[h] = sum da; a status
+int launch_bwd_head_sums(const float* A_log, const void* a, int gate_dtype, float dt_bias, const float* dt_bias_vec,
+                         const float* dlogg, const float* da, float* dA_log, float* ddt_bias, int B, int T, int H,
+                         cudaStream_t st);
 
 namespace {
 
@@ -1343,8 +1343,8 @@ int prefill_bwd_chunked(const void* q, const void* k, const void* v, const float
     else if (dkd == 64 && dvd == 128) s = launch_cb<64, 128>(ar, st);
     else s = launch_cb<64, 64>(ar, st);
     if (s != GDN_OK) return s;
-    launch_bwd_head_sums(A_log, a, gate_dtype, dt_bias, dt_bias_vec, ar.dlogg, da, dA_log, ddt_bias, B, T, H, st);
-    return launch_status("gdn_prefill_bwd (heads)");
+    return launch_bwd_head_sums(A_log, a, gate_dtype, dt_bias, dt_bias_vec, ar.dlogg, da, dA_log, ddt_bias, B, T, H,
+                                st);
 }
 
 }  // namespace gdn
