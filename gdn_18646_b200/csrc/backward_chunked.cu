@@ -141,7 +141,7 @@ struct CRec {
 };
 
 // ---------------------------------------------------------------------------
-// Per chunk (one CTA of 128 threads): the gate vectors (Lambda, b, m) and the
+// Per chunk (one CTA of 256 threads): the gate vectors (Lambda, b, m) and the
 // chunk's record.  [Q; K] K^T runs on the tensor cores (bf16 q, k, fp32
 // accumulate: TMEM lane r < 64 holds row r of Q K^T, lane 64 + t row t of K K^T);
 // P = scale (Q K^T) * [G_t/G_s, s <= t]; A = (I + diag(b) M)^-1 with
