@@ -1,5 +1,5 @@
-"""Multi-rank host logic on CPU (gloo, world_size 2): the head-shard plan, the
-all-gather of o, a head-sharded prefill (oracle as the per-rank compute, the
+"""Multi-rank host logic on CPU (gloo, world_size 2, and 4 for the gather): the
+head-shard plan, the all-gather of o, a head-sharded prefill (oracle as the per-rank compute, the
 CUDA kernel is covered by the GPU tests) equal to the unsharded result, and
 failure detection when a rank dies before the collective."""
 import datetime
@@ -71,17 +71,18 @@ def _gather_worker(rank, world, port, q):
         dist.destroy_process_group()
 
 
-def test_gather_heads_gloo():
+@pytest.mark.parametrize("world", [2, 4])
+def test_gather_heads_gloo(world):
     ctx = mp.get_context("spawn")
     q = ctx.Queue()
     port = _free_port()
-    procs = [ctx.Process(target=_gather_worker, args=(r, 2, port, q)) for r in range(2)]
+    procs = [ctx.Process(target=_gather_worker, args=(r, world, port, q)) for r in range(world)]
     for p in procs:
         p.start()
     res = dict(q.get(timeout=120) for _ in procs)
     for p in procs:
         p.join(60)
-    assert res == {0: True, 1: True}
+    assert res == {r: True for r in range(world)}
 
 
 def _sharded_oracle_worker(rank, world, port, q):
