@@ -855,31 +855,8 @@ __global__ void __launch_bounds__(256, 1) cb_grads_tc_kernel(const CbArgs a, int
     const uint8_t* rec = a.rec + static_cast<long>(cid) * CRec<DK, DV>::BYTES;
     const int next = cid + static_cast<int>(gridDim.x);   // this CTA's next chunk
     if (tid == kIssuer && next + static_cast<int>(gridDim.x) < nchunks) prefetch(next + gridDim.x);
-    if (tid < kCC) {
-        const float* gv = a.gv + static_cast<long>(cid) * 3 * kCC;
-        // the gate chain-rule factors of the chunk's tokens, loaded with the gate vectors so
-        // that the token sums at the end of the chunk read no global memory
-        float xg = 0.f, xb = 0.f;
-        if (tid < nt) {
-            const long tok = tokbase + tid;
-            xg = load_gate(a.a, tok, a.gate_dtype) + (a.dt_bias_vec ? a.dt_bias_vec[h] : a.dt_bias);
-            xb = load_gate(a.b, tok, a.gate_dtype);
-        }
-        const float g0 = gv[tid], m0 = gv[2 * kCC + tid];
-        lam[tid] = g0;
-        lam2[tid] = g0 * 1.4426950408889634f;
-        Gs[tid] = expf(g0);
-        bms[tid] = gv[kCC + tid];
-        ms[tid] = m0;
-        dfac[tid] = -expf(a.A_log[h]) * (xg > 20.f ? 1.f : sigmoid_f(xg));
-        const float sb = sigmoid_f(xb);
-        dbfac[tid] = m0 * sb * (1.f - sb);
-    }
-    __syncthreads();
-
-    // ---- phase A: the images of this chunk (issued during the previous one) land on bars[3], bars[4]
-    fence_async_smem();
-    __syncthreads();
+    // ---- phase A: the images of this chunk (issued during the previous one) land on bars[3],
+    //      bars[4]; T1, T3, T5 go to the tensor pipe before the chunk's gate loads
     const uint32_t rh = sbase + L::OFF_RH, rl = sbase + L::OFF_RL, sh = sbase + L::OFF_SH, sl = sbase + L::OFF_SL;
     if (tid == kIssuer) {
         if (!mbar_wait(&bars[4], ph, a.err) || !mbar_wait(&bars[3], ph, a.err)) *dead = 1;
@@ -911,6 +888,28 @@ __global__ void __launch_bounds__(256, 1) cb_grads_tc_kernel(const CbArgs a, int
         }
         umma_commit(&bars[0]);
     }
+
+    if (tid < kCC) {
+        const float* gv = a.gv + static_cast<long>(cid) * 3 * kCC;
+        // the gate chain-rule factors of the chunk's tokens, loaded with the gate vectors so
+        // that the token sums at the end of the chunk read no global memory
+        float xg = 0.f, xb = 0.f;
+        if (tid < nt) {
+            const long tok = tokbase + tid;
+            xg = load_gate(a.a, tok, a.gate_dtype) + (a.dt_bias_vec ? a.dt_bias_vec[h] : a.dt_bias);
+            xb = load_gate(a.b, tok, a.gate_dtype);
+        }
+        const float g0 = gv[tid], m0 = gv[2 * kCC + tid];
+        lam[tid] = g0;
+        lam2[tid] = g0 * 1.4426950408889634f;
+        Gs[tid] = expf(g0);
+        bms[tid] = gv[kCC + tid];
+        ms[tid] = m0;
+        dfac[tid] = -expf(a.A_log[h]) * (xg > 20.f ? 1.f : sigmoid_f(xg));
+        const float sb = sigmoid_f(xb);
+        dbfac[tid] = m0 * sb * (1.f - sb);
+    }
+    __syncthreads();
 
     // ---- phase B: dd . v while T1, T3, T5 run (the T image has landed), then the Sb^T image
     //      over the S image once T1 has read it, <S, Sb>, then T2
