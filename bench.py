@@ -792,15 +792,17 @@ def run_only(args):
     from gdn_18646_b200 import ops
     dev = torch.device("cuda", 0)
     torch.cuda.set_device(dev)
-    if args.only == "prefill":
+    if args.only in ("prefill", "prefill_single"):
+        # "prefill_single": the SINGLE schedule, whose prep runs as its own launch
         c = C1
         inp = gen_prefill(c["B"], c["T"], c["H"], c["dk"], c["dv"], 1234, dev)
         out = torch.empty_like(inp["v"])
         s_out = torch.empty_like(inp["state_in"])
+        sched = "single" if args.only == "prefill_single" else None
 
         def step():
             ops.prefill(inp["q"], inp["k"], inp["v"], inp["A_log"], inp["a"], inp["b"], state_in=inp["state_in"],
-                        scale=c["dk"] ** -0.5, out=out, state_out=s_out)
+                        scale=c["dk"] ** -0.5, out=out, state_out=s_out, schedule=sched)
     elif args.only == "layer_decode":
         from gdn_18646_b200.layer import GDNConfig, GDNLayer, make_weights
         cfg = GDNConfig()
@@ -899,8 +901,8 @@ def main(argv=None):
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--workload", choices=["prefill", "long"], default="prefill")
     ap.add_argument("--no-cpu-baseline", action="store_true")
-    ap.add_argument("--only", choices=["prefill", "decode", "proj", "layer_decode", "layer_prefill", "backward", "backward_config1",
-                             "outproj", "norm"], default=None,
+    ap.add_argument("--only", choices=["prefill", "prefill_single", "decode", "proj", "layer_decode", "layer_prefill",
+                                       "backward", "backward_config1", "outproj", "norm"], default=None,
                     help="run just one kernel's workload (for profiling); prints a short JSON line")
     args = ap.parse_args(argv)
     if args.only:
